@@ -1,0 +1,394 @@
+"""Batch-1 W4A8 Qwen3 decode throughput on B200 (tok/s), with its HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload qwen3-8b-p4096-g256]
+
+Workload (random-init, seeded; there is no network for checkpoints): Qwen3-8B geometry
+(hidden 4096, ffn 12288, 36 layers, 32/8 heads of 128, vocab 151936, untied head),
+per-32 int4 weights with f32 scales (5.00 bits/weight), a 4096-token random prompt
+prefilled into an fp32 KV cache, then greedy decode at batch 1. A step is one decode
+token: the whole forward, the LM head and the greedy argmax -- one fused kernel launch.
+Decode positions run 4096..4351 (the workload's 256 generated tokens); a longer timed
+run rewinds the position to 4096 every 256 steps so every step has the same shape.
+
+value    : decode tok/s, device-timed (CUDA events, inputs resident), max over ranks.
+e2e      : the same through the public API (Engine.stream with host_tokens): every step
+           copies its token + position host->device from pinned memory and the produced
+           token device->host.
+roofline : algorithmic bytes per step (int4 weights + f32 scales of every GEMV and the
+           LM head, plus the fp32 KV read) / average step time, against the measured HBM
+           copy bandwidth in MEASURED_PEAKS.json.
+cpu_baseline : the oracle (a C + numpy restatement of the reference's engine/reference.py)
+           on the host cores, a bounded sample of decode steps at the same context.
+
+--gpus N > 1 (under torchrun): N independent replicas, one per GPU, each decoding its own
+stream (weak scaling); value = total tok/s over all ranks.
+--impl reference: the reference's CPU algorithm (oracle port, all host threads) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "hive-limited_b200"))
+sys.path.insert(0, str(REPO / "oracle"))
+
+import synth  # noqa: E402
+import w4format  # noqa: E402
+
+F32 = np.float32
+METRIC = "batch-1 decode tok/s (Qwen3-8B W4A8); GEMV HBM GB/s vs B200 peak"
+UNIT = "tok/s"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (torch.distributed over gloo for host-side barrier and max)
+# ---------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+        self.t_on = self.t_off = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self._th = threading.Thread(target=self._read, daemon=True)
+        self._th.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.perf_counter(), line.strip()))
+
+    def mark(self, on: bool):
+        if on:
+            self.t_on = time.perf_counter()
+        else:
+            self.t_off = time.perf_counter()
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        lo, hi = (self.t_on or 0) - 0.06, (self.t_off or time.perf_counter()) + 0.06
+        sel = [r for t, r in self.rows if lo <= t <= hi] or [r for _, r in self.rows]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in sel:
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """dram bytes per launch of the fused step, from the committed ncu summary."""
+    p = REPO / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_step_full_workload:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def step_bytes(cfg, head_rows: int, pos: int) -> int:
+    """Algorithmic HBM bytes of one decode step at position `pos`: int4 weights + f32
+    scales of every GEMV (0.625 B per weight) plus the fp32 K and V rows 0..pos read."""
+    c = cfg
+    qd = c.head_dim
+    per_layer = ((c.n_head + 2 * c.n_kv) * qd * c.hidden + c.hidden * c.n_head * qd
+                 + 2 * c.ffn * c.hidden + c.hidden * c.ffn)
+    w = c.n_layer * per_layer + head_rows * c.hidden
+    kv = 2 * c.n_layer * c.n_kv * qd * 4 * (pos + 1)
+    return int(w * 5 // 8 + kv)
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle port of the reference's decode step
+# ---------------------------------------------------------------------------
+
+def cpu_decode_sample(cfg, seed, n_prompt, n_steps, budget_s=25.0):
+    """Time greedy decode steps of the oracle at positions n_prompt.. (bounded). The KV
+    rows 0..n_prompt-1 are filled with seeded N(0,1) values instead of running the
+    prompt (a 4096-token CPU prefill would take days); a step's cost does not depend on
+    the values. Returns (tok/s, steps, seconds, threads)."""
+    import hv_oracle as O
+    t0 = time.perf_counter()
+    w = O.quantize_model_c(cfg, synth.iter_tensors(cfg, seed))
+    cap = n_prompt + n_steps + 1
+    m = O.FastOracleModel(cfg, w, cap)
+    g = np.random.default_rng(seed)
+    for l in range(cfg.n_layer):
+        m.KC[l][:, :n_prompt] = g.standard_normal((cfg.n_kv, n_prompt, cfg.head_dim), F32)
+        m.VC[l][:, :n_prompt] = g.standard_normal((cfg.n_kv, n_prompt, cfg.head_dim), F32)
+    setup = time.perf_counter() - t0
+    tok = synth.prompt_ids(cfg, seed, 1)[0]
+    done, t1 = 0, time.perf_counter()
+    for i in range(n_steps):
+        logits = m.step(tok, n_prompt + i)
+        tok = O.argmax(logits)
+        done += 1
+        if time.perf_counter() - t1 > budget_s:
+            break
+    dt = time.perf_counter() - t1
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return done / dt, done, dt, threads, setup
+
+
+# ---------------------------------------------------------------------------
+# the arms
+# ---------------------------------------------------------------------------
+
+def run_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return 0
+    arch, seed, n_prompt, n_new = synth.WORKLOADS[args.workload]
+    cfg = w4format.Config(synth.ARCH[arch])
+    per_step = []
+    total_steps, total_s = 0, 0.0
+    rate, done, dt, threads, setup = cpu_decode_sample(cfg, seed, n_prompt,
+                                                       max(args.warmup + args.steps, 2),
+                                                       budget_s=args.cpu_budget)
+    total_steps, total_s = done, dt
+    value = total_steps / total_s
+    sample = (f"{done} oracle decode steps of {arch} at positions {n_prompt}..; "
+              f"KV rows of the prompt filled with seeded values; setup {setup:.0f} s")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": dist.world, "steps": done, "warmup": 0, "ms_per_step": 1e3 * dt / done,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded random-init weights and prompt)",
+        "config": {"workload": args.workload, "batch": 1, "prompt": n_prompt,
+                   "generated": n_new, "kv": "f32", "weights": "int4 + f32 scale per 32"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    del per_step
+    return 0
+
+
+def run_ours(args, dist: Dist):
+    import hvdrv
+    import limited
+    arch, seed, n_prompt, n_new = synth.WORKLOADS[args.workload]
+    cfg = w4format.Config(synth.ARCH[arch])
+    cap = n_prompt + n_new
+    t0 = time.perf_counter()
+    eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
+                         max_context=cap, device=dist.local, fused=True)
+    t_load = time.perf_counter() - t0
+    prompt = synth.prompt_ids(cfg, seed, n_prompt)
+    window = cap - n_prompt              # decode positions available before a rewind
+
+    # prefill (the last prompt token's launch takes the first argmax)
+    t0 = time.perf_counter()
+    eng._prefill(prompt)
+    hvdrv.synchronize()
+    eng._check_status()
+    t_prefill = time.perf_counter() - t0
+
+    pin = hvdrv.host_alloc(16)
+    pbuf = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_int32 * 4).from_address(pin))
+    pbuf[:] = [n_prompt, 0, 0, 0]
+    done = [0]
+
+    def decode(k):
+        for _ in range(k):
+            if done[0] and done[0] % window == 0:          # rewind to the first position
+                hvdrv.upload_async(eng.d_pos, pin, 4)
+                hvdrv.upload_async(eng.d_step, pin + 4, 4)
+            eng._decode_one()
+            done[0] += 1
+
+    decode(args.warmup)
+    hvdrv.synchronize()
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = hvdrv.event_create(), hvdrv.event_create()
+    dist.barrier()
+    hvdrv.synchronize()
+    clocks.mark(True)
+    hvdrv.event_record(e0, 0)
+    first_step = done[0]
+    decode(args.steps)
+    hvdrv.event_record(e1, 0)
+    hvdrv.synchronize()
+    clocks.mark(False)
+    dist.barrier()
+    ms = hvdrv.event_elapsed_ms(e0, e1)
+    clk = clocks.stop()
+    eng._check_status()
+    ms_max = dist.max(ms)
+    ms_per_step = ms_max / args.steps
+    value = dist.world * args.steps / (ms_max / 1e3)
+
+    # algorithmic bytes over the timed steps (position of each step)
+    positions = [n_prompt + ((first_step + i) % window) for i in range(args.steps)]
+    bytes_mean = float(np.mean([step_bytes(cfg, eng.n_head_rows, p) for p in positions]))
+    peak, peak_kind = measured_peak()
+    achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
+    traffic = profiled_traffic("k_step_qwen3-8b_decode.md")
+
+    # end to end through the public API: Engine.stream with host-fed tokens
+    n_e2e = min(args.e2e_steps, window)
+    ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True))
+    times = [e[2] for e in ev if e[0] == "tok"]
+    e2e = (len(times) - 1) / (times[-1] - times[0]) if len(times) > 1 else None
+    e2e_all = dist.sum(e2e or 0.0) if dist.world > 1 else e2e
+
+    line = None
+    if dist.rank == 0:
+        cpu = None
+        if dist.world == 1 and not args.no_cpu:
+            rate, n_cpu, dt, threads, setup = cpu_decode_sample(
+                cfg, seed, n_prompt, 64, budget_s=args.cpu_budget)
+            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{n_cpu} oracle decode steps of {arch} at positions "
+                             f"{n_prompt}.. in {dt:.1f} s (KV rows of the prompt filled "
+                             f"with seeded values)"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded random-init weights and prompt)",
+            "config": {"workload": args.workload, "model": arch, "batch": 1,
+                       "prompt": n_prompt, "generated": n_new, "kv": "f32",
+                       "weights": "int4 + f32 scale per 32 (5.00 bits/weight)",
+                       "parallelism": "replicas" if dist.world > 1 else "single",
+                       "l2": "inputs larger than L2 (5.9 GB read per step)",
+                       "positions": f"{min(positions)}..{max(positions)}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_kind": peak_kind, "kernel": "k_step",
+                         "bytes_per_step": bytes_mean},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_all, "unit": UNIT, "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": args.steps,
+            "clocks": clk,
+            "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
+        }
+        print(json.dumps(line), flush=True)
+    hvdrv.host_free(pin)
+    eng.free()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="qwen3-8b-p4096-g256", choices=list(synth.WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            return run_reference(args, dist)
+        return run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

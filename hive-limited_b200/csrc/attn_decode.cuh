@@ -1,0 +1,207 @@
+// Split-sequence (flash-decoding) causal attention for batch-1 decode, head_dim 128.
+//
+// The reference (fda_warp_pos, engine/limited.py:401-404; engine/reference.py:104-118)
+// runs one warp per query head and so reads every KV row `group` times with only
+// n_head warps in flight. Here one CTA serves one (kv head, chunk of positions) work
+// item for the WHOLE query group: each K/V row is read from HBM once, and the
+// positions of every kv head are split into enough chunks to fill the SMs. A chunk
+// leaves its softmax state (running max m, sum l, unnormalised V-sum) in scratch; the
+// last CTA to finish a kv head (atomic ticket) merges the chunks into ctx.
+//
+// Numerics: logits = (k . q) * scale, softmax by exp(x - max), weighted V sum -- the
+// reference's math in another summation order (and CUDA's expf), so the result matches
+// engine/reference.py to within float rounding, not bit for bit.
+#pragma once
+
+#include "hv_common.cuh"
+
+namespace hv {
+
+constexpr int kHd = 128;
+constexpr int kAttnChunkMax = 1024;   // positions one work item may hold
+constexpr int kPartStride = 132;      // per q head: m, l, 2 pad, acc[128]
+
+HV_DEV void chunk_bounds(int npos, int nch, int c, int* t0, int* t1) {
+  *t0 = (int)(((long long)c * npos) / nch);
+  *t1 = (int)(((long long)(c + 1) * npos) / nch);
+}
+
+HV_DEV float4 ldg_f4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Sum V values held in every lane across the 32 lanes by recursive halving: after it,
+// lane l holds the total of value index `*idx`; lanes whose low (log2(32/V)) bits are
+// zero are the representatives of their index.
+template <int V>
+HV_DEV float halving_reduce(float (&v)[V], int lane, int* idx) {
+  int id = 0;
+#pragma unroll
+  for (int L = 0; L < 5; ++L) {
+    const int o = 16 >> L;
+    const int cur = (V >> L) > 0 ? (V >> L) : 1;
+    if (cur >= 2) {
+      const int half = cur / 2;
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int k = 0; k < half; ++k) {
+        const float send = up ? v[k] : v[k + half];
+        const float keep = up ? v[k + half] : v[k];
+        v[k] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+      }
+      if (up) id += half;
+    } else {
+      v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], o);
+    }
+  }
+  *idx = id;
+  return v[0];
+}
+
+// Shared memory a work item needs (bytes), for `nwarps` warps.
+template <int GS>
+constexpr size_t attn_smem_bytes(int nwarps) {
+  return sizeof(float) * ((size_t)GS * kHd                 // q
+                          + (size_t)kAttnChunkMax * GS      // logits / probabilities
+                          + (size_t)nwarps * GS * kHd       // cross-warp V sums
+                          + 2 * GS + 2 * kHd);              // stats, k/v row at pos
+}
+
+// One work item: positions [t0, t1) of one kv head for its GS query heads.
+//   q_s    smem [GS][128]  query heads, already normed and rotated
+//   K, V   global [cap][128] rows of this kv head
+//   pos, kpos_s/vpos_s: if kpos_s is set, row `pos` is taken from it instead of K/V
+//   part   global [GS][kPartStride] partial state written by this item
+// Block-cooperative; all threads call it.
+template <int GS>
+HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
+                       const float* __restrict__ V, int t0, int t1, float scale, int pos,
+                       const float* kpos_s, const float* vpos_s, float* lg_s, float* red_s,
+                       float* stat_s, float* __restrict__ part) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int n = t1 - t0;
+
+  // ---- scores: each warp takes 4 positions at a time; lane l owns dims 4l..4l+3
+  float4 qv[GS];
+#pragma unroll
+  for (int i = 0; i < GS; ++i) qv[i] = reinterpret_cast<const float4*>(q_s + i * kHd)[lane];
+  for (int tb = t0 + warp * 4; tb < t1; tb += nw * 4) {
+    float4 kv[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int t = tb + p;
+      if (t < t1) {
+        kv[p] = (kpos_s && t == pos) ? reinterpret_cast<const float4*>(kpos_s)[lane]
+                                     : ldg_f4(K + (size_t)t * kHd + lane * 4);
+      } else {
+        kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float v[4 * GS];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int i = 0; i < GS; ++i) {
+        float s = qv[i].x * kv[p].x;
+        s = fmaf(qv[i].y, kv[p].y, s);
+        s = fmaf(qv[i].z, kv[p].z, s);
+        s = fmaf(qv[i].w, kv[p].w, s);
+        v[p * GS + i] = s;
+      }
+    int idx;
+    const float tot = halving_reduce<4 * GS>(v, lane, &idx);
+    constexpr int dup = 32 / (4 * GS);
+    if ((lane & (dup - 1)) == 0) {
+      const int p = idx / GS, i = idx % GS;
+      const int t = tb + p;
+      if (t < t1) lg_s[(t - t0) * GS + i] = tot * scale;
+    }
+  }
+  __syncthreads();
+
+  // ---- per-head max and exp: warp i handles head i
+  for (int i = warp; i < GS; i += nw) {
+    float m = -INFINITY;
+    for (int t = lane; t < n; t += 32) m = fmaxf(m, lg_s[t * GS + i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    float l = 0.f;
+    for (int t = lane; t < n; t += 32) {
+      const float e = (n > 0) ? expf(lg_s[t * GS + i] - m) : 0.f;
+      lg_s[t * GS + i] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    if (lane == 0) { stat_s[2 * i] = m; stat_s[2 * i + 1] = l; }
+  }
+  __syncthreads();
+
+  // ---- probability-weighted V sum: warps split positions, lane owns 4 dims
+  float4 acc[GS];
+#pragma unroll
+  for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int tb = t0 + warp * 4; tb < t1; tb += nw * 4) {
+    float4 vv[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int t = tb + p;
+      if (t < t1) {
+        vv[p] = (vpos_s && t == pos) ? reinterpret_cast<const float4*>(vpos_s)[lane]
+                                     : ldg_f4(V + (size_t)t * kHd + lane * 4);
+      } else {
+        vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int t = tb + p;
+      if (t < t1) {
+#pragma unroll
+        for (int i = 0; i < GS; ++i) {
+          const float w = lg_s[(t - t0) * GS + i];
+          acc[i].x = fmaf(w, vv[p].x, acc[i].x);
+          acc[i].y = fmaf(w, vv[p].y, acc[i].y);
+          acc[i].z = fmaf(w, vv[p].z, acc[i].z);
+          acc[i].w = fmaf(w, vv[p].w, acc[i].w);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < GS; ++i)
+    reinterpret_cast<float4*>(red_s + ((size_t)warp * GS + i) * kHd)[lane] = acc[i];
+  __syncthreads();
+  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red_s[(size_t)w * GS * kHd + e];
+    const int i = e / kHd, d = e % kHd;
+    part[i * kPartStride + 4 + d] = s;
+  }
+  if (threadIdx.x < GS) {
+    part[threadIdx.x * kPartStride + 0] = (n > 0) ? stat_s[2 * threadIdx.x] : -INFINITY;
+    part[threadIdx.x * kPartStride + 1] = (n > 0) ? stat_s[2 * threadIdx.x + 1] : 0.f;
+  }
+}
+
+// Merge the nch chunk states of one kv head into ctx rows [GS][128]. Reads the
+// partials through L2 (they were written by other CTAs).
+template <int GS>
+HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx) {
+  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) {
+    const int i = e / kHd, d = e % kHd;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c)
+      M = fmaxf(M, __ldcg(part_head + ((size_t)c * GS + i) * kPartStride));
+    float L = 0.f, o = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      const float* pc = part_head + ((size_t)c * GS + i) * kPartStride;
+      const float w = expf(__ldcg(pc) - M);
+      L = fmaf(w, __ldcg(pc + 1), L);
+      o = fmaf(w, __ldcg(pc + 4 + d), o);
+    }
+    ctx[i * kHd + d] = o / L;
+  }
+}
+
+}  // namespace hv

@@ -1,0 +1,507 @@
+// Standalone kernels: one per HIVE Limited PTX entry point (engine/limited.py:173-181),
+// with the reference's argument meaning. The decode engine's fast path fuses these into
+// one persistent kernel (k_step.cu); these serve the eager path, the C ABI and the
+// parity tests.
+#include <mutex>
+
+#include <cuda_fp16.h>
+
+#include "attn_decode.cuh"
+#include "gemv_w4a8.cuh"
+#include "hv_internal.h"
+
+namespace hv {
+
+// ---------------------------------------------------------------------------
+// quant_a8s: one warp per 32-block
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_qa8s(const float* __restrict__ src,
+                                              int8_t* __restrict__ a8,
+                                              float* __restrict__ sa, int nb) {
+  const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= nb) return;
+  int8_t q;
+  float s;
+  int bs;
+  quant_block_warp(src[b * kBlock + lane], lane, &q, &s, &bs);
+  a8[b * kBlock + lane] = q;
+  if (lane == 0) {
+    sa[b] = s;
+    sa[nb + b] = __int_as_float(bs);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// gemv_wpo_a4: a grid of warps, four rows per warp per pass
+// ---------------------------------------------------------------------------
+template <bool kIdot>
+__global__ void __launch_bounds__(256) k_a4gv(const int8_t* __restrict__ a8,
+                                              const float* __restrict__ sa,
+                                              const uint32_t* __restrict__ b4,
+                                              const float* __restrict__ sw,
+                                              float* __restrict__ dst,
+                                              int32_t* __restrict__ idot, int nb, int n) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint4* q_s = reinterpret_cast<uint4*>(smem);
+  int2* sb_s = reinterpret_cast<int2*>(smem + (size_t)nb * 32);
+  GvPlan* plan = reinterpret_cast<GvPlan*>(smem + (size_t)nb * 40);
+  load_act_smem(a8, sa, nb, q_s, sb_s);
+  if (threadIdx.x == 0) gv_make_plan(nb, plan);
+  __syncthreads();
+  const ActView act{q_s, sb_s};
+  const int lane = threadIdx.x & 31;
+  const int nquads = (n + 3) / 4;
+  const int wpb = blockDim.x >> 5;
+  for (int q = blockIdx.x * wpb + (threadIdx.x >> 5); q < nquads; q += gridDim.x * wpb) {
+    const int row = q * 4 + (lane >> 3);
+    const bool ok = row < n;
+    const float y = gemv_rows4<8, kIdot>(b4, sw, row, ok, act, *plan, idot);
+    if (ok && (lane & 7) == 0) dst[row] = y;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// rmsnorm_bp: one CTA per row
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ src,
+                                                 float* __restrict__ dst,
+                                                 const float* __restrict__ w, int cols,
+                                                 float eps) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  PwPlan* plan = reinterpret_cast<PwPlan*>(smem);
+  float* leafval = reinterpret_cast<float*>(smem + sizeof(PwPlan));
+  float* red = leafval + kPwMaxLeaf;
+  float* x = red + 4;
+  float* sq = x + cols;
+  const float* row = src + (size_t)blockIdx.x * cols;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = row[i];
+    x[i] = v;
+    sq[i] = __fmul_rn(v, v);
+  }
+  if (threadIdx.x == 0) pw_make_plan(cols, plan);
+  __syncthreads();
+  const float ss = block_pw_sum(sq, plan, leafval, red);
+  const float ms = __fdiv_rn(ss, (float)cols);
+  const float d = __fsqrt_rn(__fadd_rn(ms, eps));
+  float* out = dst + (size_t)blockIdx.x * cols;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x)
+    out[i] = __fmul_rn(w[i], __fdiv_rn(x[i], d));
+}
+
+// ---------------------------------------------------------------------------
+// rope_pos / kvapp_pos / gpu_silu_mul / vec_add / gather_emb
+// ---------------------------------------------------------------------------
+__global__ void k_rope(float* __restrict__ vec, const float* __restrict__ cos_t,
+                       const float* __restrict__ sin_t, const int32_t* __restrict__ pos,
+                       int half) {
+  const int p = *pos;
+  float* v = vec + (size_t)blockIdx.x * 2 * half;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float c = cos_t[(size_t)p * half + i], s = sin_t[(size_t)p * half + i];
+    const float lo = v[i], hi = v[half + i];
+    v[i] = __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
+    v[half + i] = __fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s));
+  }
+}
+
+__global__ void k_kvapp(const float* __restrict__ k, const float* __restrict__ v,
+                        float* __restrict__ kc, float* __restrict__ vc,
+                        const int32_t* __restrict__ pos, int hd, int cap) {
+  const int p = *pos;
+  const int h = blockIdx.x;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    kc[((size_t)h * cap + p) * hd + d] = k[h * hd + d];
+    vc[((size_t)h * cap + p) * hd + d] = v[h * hd + d];
+  }
+}
+
+__global__ void k_silu(const float* __restrict__ g, const float* __restrict__ u,
+                       float* __restrict__ act, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) act[i] = silu_mul1(g[i], u[i]);
+}
+
+__global__ void k_vadd(const float* __restrict__ a, const float* __restrict__ b,
+                       float* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void k_gather(const __half* __restrict__ emb, const int32_t* __restrict__ tok,
+                         float* __restrict__ h, int hid) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < hid) h[i] = __half2float(emb[(size_t)(*tok) * hid + i]);
+}
+
+// ---------------------------------------------------------------------------
+// argmax_p / argmax_f: first maximal index
+// ---------------------------------------------------------------------------
+HV_DEV bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+HV_DEV void block_argmax(float* v, int* i, float* sv, int* si) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, *v, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, *i, o);
+    if (better(ov, oi, *v, *i)) { *v = ov; *i = oi; }
+  }
+  if (lane == 0) { sv[warp] = *v; si[warp] = *i; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], sv[0], si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
+  }
+  __syncthreads();
+  *v = sv[0];
+  *i = si[0];
+}
+
+__global__ void __launch_bounds__(256) k_argmax_p(const float* __restrict__ logits,
+                                                  float* __restrict__ pv,
+                                                  int32_t* __restrict__ pi, int n, int parts) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int lo = (int)(((long long)blockIdx.x * n) / parts);
+  const int hi = (int)(((long long)(blockIdx.x + 1) * n) / parts);
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
+    const float v = logits[j];
+    if (better(v, j, bv, bi)) { bv = v; bi = j; }
+  }
+  block_argmax(&bv, &bi, sv, si);
+  if (threadIdx.x == 0) { pv[blockIdx.x] = bv; pi[blockIdx.x] = bi; }
+}
+
+__global__ void __launch_bounds__(128) k_argmax_f(const float* __restrict__ pv,
+                                                  const int32_t* __restrict__ pi,
+                                                  int32_t* tok, int32_t* gen, int32_t* step,
+                                                  int32_t* pos, int parts) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int j = threadIdx.x; j < parts; j += blockDim.x)
+    if (better(pv[j], pi[j], bv, bi)) { bv = pv[j]; bi = pi[j]; }
+  block_argmax(&bv, &bi, sv, si);
+  if (threadIdx.x == 0) {
+    *tok = bi;
+    gen[*step] = bi;
+    *step += 1;
+    *pos += 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// quantize_w4 on the device: one thread per 32-block
+// ---------------------------------------------------------------------------
+__global__ void k_quantize_w4(const float* __restrict__ w, uint32_t* __restrict__ packed,
+                              float* __restrict__ scale, long long nblocks) {
+  const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblocks) return;
+  const float4* src = reinterpret_cast<const float4*>(w + b * kBlock);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = src[i];
+    v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+  }
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  float s = __fdiv_rn(mx, 7.0f);
+  if (s == 0.0f) s = 1.0f;
+  uint32_t words[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float r = rintf(__fdiv_rn(v[i], s));
+    r = fminf(fmaxf(r, -7.0f), 7.0f);
+    const uint32_t nib = (uint32_t)((int)r) & 15u;
+    const int word = i / 8, j = i % 8;
+    const int shift = (j < 4) ? (8 * j) : (8 * (j - 4) + 4);
+    words[word] |= nib << shift;
+  }
+  reinterpret_cast<uint4*>(packed)[b] = make_uint4(words[0], words[1], words[2], words[3]);
+  scale[b] = s;
+}
+
+// ---------------------------------------------------------------------------
+// split-sequence attention (standalone): one CTA per (kv head, chunk)
+// ---------------------------------------------------------------------------
+constexpr int kAttnThreads = 256;
+
+template <int GS>
+__global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q,
+                                                       const float* __restrict__ kc,
+                                                       const float* __restrict__ vc,
+                                                       float* __restrict__ ctx,
+                                                       const float* __restrict__ scale_p,
+                                                       const int32_t* __restrict__ pos_p,
+                                                       int cap, int nch,
+                                                       float* __restrict__ part,
+                                                       int* __restrict__ ticket) {
+  extern __shared__ __align__(16) float fsm[];
+  const int nw = blockDim.x >> 5;
+  float* q_s = fsm;
+  float* lg_s = q_s + GS * kHd;
+  float* red_s = lg_s + kAttnChunkMax * GS;
+  float* stat_s = red_s + nw * GS * kHd;
+  __shared__ int last;
+  const int g = blockIdx.x / nch, c = blockIdx.x % nch;
+  const int pos = *pos_p;
+  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) q_s[e] = q[(size_t)g * GS * kHd + e];
+  __syncthreads();
+  int t0, t1;
+  chunk_bounds(pos + 1, nch, c, &t0, &t1);
+  float* mypart = part + ((size_t)g * nch + c) * GS * kPartStride;
+  attn_chunk<GS>(q_s, kc + (size_t)g * cap * kHd, vc + (size_t)g * cap * kHd, t0, t1,
+                 *scale_p, pos, nullptr, nullptr, lg_s, red_s, stat_s, mypart);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(ticket + g, 1) == nch - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  attn_merge<GS>(part + (size_t)g * nch * GS * kPartStride, nch, ctx + (size_t)g * GS * kHd);
+  if (threadIdx.x == 0) ticket[g] = 0;
+}
+
+// per-device attention scratch, grown on demand
+struct AttnScratch {
+  float* part = nullptr;
+  int* ticket = nullptr;
+  size_t part_floats = 0;
+  int tickets = 0;
+};
+static std::mutex g_attn_mu;
+static AttnScratch g_attn[64];
+
+static int attn_nch(int nkv, int cap, int* out) {
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  int nch = (sms + nkv - 1) / nkv;
+  const int need = (cap + kAttnChunkMax - 1) / kAttnChunkMax;
+  *out = nch > need ? nch : need;
+  return HV_OK;
+}
+
+static int attn_scratch(int nkv, int group, int cap, void* stream, AttnScratch** out) {
+  int dev = 0;
+  HV_CUDA(cudaGetDevice(&dev));
+  HV_REQUIRE(dev >= 0 && dev < 64, HV_E_UNSUPPORTED, "device index %d out of range", dev);
+  int nch = 0;
+  int rc = attn_nch(nkv, cap, &nch);
+  if (rc) return rc;
+  const size_t need = (size_t)nkv * nch * group * kPartStride;
+  std::lock_guard<std::mutex> lk(g_attn_mu);
+  AttnScratch& s = g_attn[dev];
+  if (s.part_floats < need || s.tickets < nkv) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (stream) HV_CUDA(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
+    HV_REQUIRE(cs == cudaStreamCaptureStatusNone, HV_E_CAPTURE,
+               "attention scratch must grow during stream capture; call hv_attn_reserve first");
+    if (s.part) cudaFree(s.part);
+    if (s.ticket) cudaFree(s.ticket);
+    s.part = nullptr;
+    s.ticket = nullptr;
+    const size_t nf = need > s.part_floats ? need : s.part_floats;
+    const int nt = nkv > s.tickets ? nkv : s.tickets;
+    HV_CUDA(cudaMalloc(&s.part, nf * sizeof(float)));
+    HV_CUDA(cudaMalloc(&s.ticket, (size_t)nt * sizeof(int)));
+    HV_CUDA(cudaMemset(s.ticket, 0, (size_t)nt * sizeof(int)));
+    s.part_floats = nf;
+    s.tickets = nt;
+  }
+  *out = &s;
+  return HV_OK;
+}
+
+template <int GS>
+static int launch_attn(const float* q, const float* kc, const float* vc, float* ctx,
+                       const float* scale, const int32_t* pos, int nkv, int cap, int nch,
+                       AttnScratch* s, cudaStream_t st) {
+  const size_t smem = attn_smem_bytes<GS>(kAttnThreads / 32);
+  HV_CUDA(cudaFuncSetAttribute(k_attn<GS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  k_attn<GS><<<nkv * nch, kAttnThreads, smem, st>>>(q, kc, vc, ctx, scale, pos, cap, nch,
+                                                    s->part, s->ticket);
+  HV_LAUNCHED("k_attn");
+}
+
+}  // namespace hv
+
+using namespace hv;
+
+extern "C" {
+
+int hv_kernel_list(char* buf, size_t len) {
+  static const char* names =
+      "k_qa8s,k_a4gv,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
+      "k_argmax_p,k_argmax_f,k_quantize_w4,k_step";
+  HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
+  strncpy(buf, names, len - 1);
+  buf[len - 1] = 0;
+  return HV_OK;
+}
+
+int hv_qa8s(const float* src, int8_t* a8, float* sa, int nb, void* stream) {
+  HV_REQUIRE(src && a8 && sa && nb > 0, HV_E_INVALID, "hv_qa8s: bad arguments");
+  k_qa8s<<<(nb + 7) / 8, 256, 0, (cudaStream_t)stream>>>(src, a8, sa, nb);
+  HV_LAUNCHED("k_qa8s");
+}
+
+static int a4gv_launch(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
+                       float* dst, int32_t* idot, int k8, int n, void* stream) {
+  HV_REQUIRE(a8 && sa && b4 && sw && dst && k8 > 0 && n > 0, HV_E_INVALID,
+             "hv_a4gv: bad arguments");
+  HV_REQUIRE(k8 % 4 == 0, HV_E_INVALID, "hv_a4gv: K = %d is not a multiple of 32", k8 * 8);
+  HV_REQUIRE(((uintptr_t)a8 & 15) == 0 && ((uintptr_t)b4 & 15) == 0, HV_E_INVALID,
+             "hv_a4gv: a8 and b4 must be 16-byte aligned");
+  const int nb = k8 / 4;
+  HV_REQUIRE(nb <= 4096, HV_E_UNSUPPORTED, "hv_a4gv: K = %d exceeds 131072", k8 * 8);
+  const size_t smem = (size_t)nb * 40 + sizeof(GvPlan);
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  const int nquads = (n + 3) / 4;
+  int grid = (nquads + 7) / 8;
+  if (grid > sms * 8) grid = sms * 8;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (idot) {
+    HV_CUDA(cudaFuncSetAttribute(k_a4gv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    k_a4gv<true><<<grid, 256, smem, st>>>(a8, sa, b4, sw, dst, idot, nb, n);
+  } else {
+    HV_CUDA(cudaFuncSetAttribute(k_a4gv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    k_a4gv<false><<<grid, 256, smem, st>>>(a8, sa, b4, sw, dst, nullptr, nb, n);
+  }
+  HV_LAUNCHED("k_a4gv");
+}
+
+int hv_a4gv(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
+            float* dst, int k8, int n, void* stream) {
+  return a4gv_launch(a8, sa, b4, sw, dst, nullptr, k8, n, stream);
+}
+
+int hv_a4gv_idot(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
+                 float* dst, int32_t* idot, int k8, int n, void* stream) {
+  HV_REQUIRE(idot, HV_E_INVALID, "hv_a4gv_idot: null idot");
+  return a4gv_launch(a8, sa, b4, sw, dst, idot, k8, n, stream);
+}
+
+int hv_rmsnorm(const float* src, float* dst, const float* w, int rows, int cols, float eps,
+               void* stream) {
+  HV_REQUIRE(src && dst && w && rows > 0 && cols > 0, HV_E_INVALID, "hv_rmsnorm: bad arguments");
+  // +8 floats: the idle lane groups of the leaf pass read x[0..8) even when cols < 8
+  const size_t smem = sizeof(PwPlan) + sizeof(float) * (kPwMaxLeaf + 4 + 2 * (size_t)cols + 8);
+  HV_REQUIRE(smem <= 220 * 1024, HV_E_UNSUPPORTED, "hv_rmsnorm: %d columns is too wide", cols);
+  HV_CUDA(cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  k_rmsnorm<<<rows, 256, smem, (cudaStream_t)stream>>>(src, dst, w, cols, eps);
+  HV_LAUNCHED("k_rmsnorm");
+}
+
+int hv_rope(float* vec, const float* cos_t, const float* sin_t, const int32_t* pos, int heads,
+            int half, void* stream) {
+  HV_REQUIRE(vec && cos_t && sin_t && pos && heads > 0 && half > 0, HV_E_INVALID,
+             "hv_rope: bad arguments");
+  k_rope<<<heads, 64, 0, (cudaStream_t)stream>>>(vec, cos_t, sin_t, pos, half);
+  HV_LAUNCHED("k_rope");
+}
+
+int hv_kv_append(const float* k, const float* v, float* kc, float* vc, const int32_t* pos,
+                 int nkv, int hd, int cap, void* stream) {
+  HV_REQUIRE(k && v && kc && vc && pos && nkv > 0 && hd > 0 && cap > 0, HV_E_INVALID,
+             "hv_kv_append: bad arguments");
+  k_kvapp<<<nkv, 128, 0, (cudaStream_t)stream>>>(k, v, kc, vc, pos, hd, cap);
+  HV_LAUNCHED("k_kvapp");
+}
+
+int hv_attn_reserve(int nkv, int group, int cap) {
+  HV_REQUIRE(nkv > 0 && group > 0 && cap > 0, HV_E_INVALID, "hv_attn_reserve: bad arguments");
+  AttnScratch* s = nullptr;
+  return attn_scratch(nkv, group, cap, nullptr, &s);
+}
+
+int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
+                   const float* scale, const int32_t* pos, int nq, int hd, int group,
+                   int kvstride, void* stream) {
+  HV_REQUIRE(q && kc && vc && ctx && scale && pos && nq > 0 && group > 0, HV_E_INVALID,
+             "hv_attn_decode: bad arguments");
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_attn_decode: head_dim %d (only 128)", hd);
+  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
+             "hv_attn_decode: nq %% group or kvstride %% hd is not zero");
+  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
+             "hv_attn_decode: group size %d (1, 2, 4 or 8)", group);
+  const int nkv = nq / group, cap = kvstride / hd;
+  AttnScratch* s = nullptr;
+  int rc = attn_scratch(nkv, group, cap, stream, &s);
+  if (rc) return rc;
+  int nch = 0;
+  rc = attn_nch(nkv, cap, &nch);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (group) {
+    case 1: return launch_attn<1>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    case 2: return launch_attn<2>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    case 4: return launch_attn<4>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    default: return launch_attn<8>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+  }
+}
+
+int hv_silu_mul(const float* gate, const float* up, float* act, int n, void* stream) {
+  HV_REQUIRE(gate && up && act && n > 0, HV_E_INVALID, "hv_silu_mul: bad arguments");
+  k_silu<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(gate, up, act, n);
+  HV_LAUNCHED("k_silu");
+}
+
+int hv_vadd(const float* a, const float* b, float* out, int n, void* stream) {
+  HV_REQUIRE(a && b && out && n > 0, HV_E_INVALID, "hv_vadd: bad arguments");
+  k_vadd<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(a, b, out, n);
+  HV_LAUNCHED("k_vadd");
+}
+
+int hv_gather_emb(const uint16_t* emb16, const int32_t* tok, float* h, int hid, void* stream) {
+  HV_REQUIRE(emb16 && tok && h && hid > 0, HV_E_INVALID, "hv_gather_emb: bad arguments");
+  k_gather<<<(hid + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __half*>(emb16), tok, h, hid);
+  HV_LAUNCHED("k_gather");
+}
+
+int hv_argmax_partial(const float* logits, float* pv, int32_t* pi, int n, int parts,
+                      void* stream) {
+  HV_REQUIRE(logits && pv && pi && n > 0 && parts > 0, HV_E_INVALID,
+             "hv_argmax_partial: bad arguments");
+  k_argmax_p<<<parts, 256, 0, (cudaStream_t)stream>>>(logits, pv, pi, n, parts);
+  HV_LAUNCHED("k_argmax_p");
+}
+
+int hv_argmax_final(const float* pv, const int32_t* pi, int32_t* tok, int32_t* gen,
+                    int32_t* step, int32_t* pos, int parts, void* stream) {
+  HV_REQUIRE(pv && pi && tok && gen && step && pos && parts > 0, HV_E_INVALID,
+             "hv_argmax_final: bad arguments");
+  k_argmax_f<<<1, 128, 0, (cudaStream_t)stream>>>(pv, pi, tok, gen, step, pos, parts);
+  HV_LAUNCHED("k_argmax_f");
+}
+
+int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,
+                   void* stream) {
+  HV_REQUIRE(w && packed && scale && n > 0 && k > 0, HV_E_INVALID,
+             "hv_quantize_w4: bad arguments");
+  HV_REQUIRE(k % kBlock == 0, HV_E_INVALID, "hv_quantize_w4: K=%d is not a multiple of 32", k);
+  HV_REQUIRE(((uintptr_t)w & 15) == 0 && ((uintptr_t)packed & 15) == 0, HV_E_INVALID,
+             "hv_quantize_w4: w and packed must be 16-byte aligned");
+  const long long nblocks = (long long)n * (k / kBlock);
+  k_quantize_w4<<<(unsigned)((nblocks + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      w, packed, scale, nblocks);
+  HV_LAUNCHED("k_quantize_w4");
+}
+
+}  // extern "C"

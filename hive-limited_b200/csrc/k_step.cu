@@ -1,0 +1,464 @@
+// The fused decode step: HIVE Limited's Engine._step() + LM head + greedy argmax
+// (engine/limited.py:374-428) as ONE persistent cooperative kernel.
+//
+// Why one kernel: at batch 1 the step is ~20 dependent launches per layer (the
+// reference issues 538 for 28 layers). Each launch boundary drains the GPU; here the
+// dependencies become grid barriers inside one launch, and every CTA recomputes the
+// small vector work it needs (RMSNorm + per-32 quantisation of a 4-20 KB vector, the
+// q/k norms and RoPE of its own heads) instead of waiting on a separate kernel.
+//
+// Per layer, five phases separated by grid barriers:
+//   P1 qkv  : act <- quant(rmsnorm(h, an)); rows of W_qkv        -> qkv
+//   P2 attn : per (kv head, chunk): q/k norm + RoPE, KV append at pos, split softmax;
+//             last CTA of each kv head merges                     -> ctx
+//   P3 o    : act <- quant(ctx);   rows of W_o, h[row] += y        -> h
+//   P4 gu   : act <- quant(rmsnorm(h, fn)); gate/up row pairs, SiLU -> act
+//   P5 down : act <- quant(act);   rows of W_down, h[row] += y     -> h
+// then the head: act <- quant(rmsnorm(h, onorm)); rows of the LM head -> logits and a
+// per-CTA argmax; the last CTA picks the token and advances tok/gen/step/pos.
+//
+// Rows of every matrix are split evenly over the CTAs; the o and down splits are the
+// same (N = hidden), so the CTA that adds into h[row] is always the one that last
+// wrote it. Data produced by other CTAs is read through L2 (ld.global.cg): L1 is not
+// coherent across SMs.
+#include <cuda_fp16.h>
+
+#include "attn_decode.cuh"
+#include "gemv_w4a8.cuh"
+#include "hv_internal.h"
+
+namespace hv {
+
+constexpr int kStepThreads = 512;
+constexpr int kStepWarps = kStepThreads / 32;
+constexpr unsigned long long kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
+
+struct StepShared {
+  PwPlan pw_hid;
+  GvPlan gv_hid, gv_o, gv_ffn;
+  float leafval[kPwMaxLeaf];
+  float red[4];
+  float sv[32];
+  int si[32];
+  int flag;
+  int ok;
+};
+
+HV_DEV unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+HV_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Grid-wide barrier over a self-resetting counter: CTA 0 adds 2^31 - (grid - 1), the
+// others add 1, so the top bit flips exactly when all have arrived and the low bits
+// return to zero. The wait is bounded: after kWaitNs (or once another CTA has reported
+// a failure) it records HV_E_TIMEOUT in *status and returns false.
+HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
+    __threadfence();
+    const unsigned old = atomicAdd(bar, add);
+    const unsigned long long t0 = global_ns();
+    int ok = 1;
+    while (((ld_acquire(bar) ^ old) & 0x80000000u) == 0) {
+      if (*(volatile int*)status != 0) { ok = 0; break; }
+      if (global_ns() - t0 > kWaitNs) {
+        atomicExch(status, HV_E_TIMEOUT);
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+    S.ok = ok;
+  }
+  __syncthreads();
+  return S.ok != 0;
+}
+
+HV_DEV void row_range(int n, int* r0, int* r1) {
+  *r0 = (int)(((long long)blockIdx.x * n) / gridDim.x);
+  *r1 = (int)(((long long)(blockIdx.x + 1) * n) / gridDim.x);
+}
+
+// ---- prologues: build the quantised activation in shared memory ---------------------
+
+// act <- quant(rmsnorm(src, w)) over n = hidden values; src from global (through L2) or,
+// for layer 0, the f16 embedding row.
+__device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row, const float* __restrict__ w,
+                           int n, float eps, StepShared& S, float* x, float* sq, uint4* q_s,
+                           int2* sb_s) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = src ? __ldcg(src + i) : __half2float(emb_row[i]);
+    x[i] = v;
+    sq[i] = __fmul_rn(v, v);
+  }
+  __syncthreads();
+  const float ss = block_pw_sum(sq, &S.pw_hid, S.leafval, S.red);
+  const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__ldg(w + i), __fdiv_rn(x[i], d));
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  int8_t* q8 = reinterpret_cast<int8_t*>(q_s);
+  for (int b = threadIdx.x >> 5; b < n / kBlock; b += kStepWarps) {
+    int8_t q;
+    float s;
+    int bs;
+    quant_block_warp(x[b * kBlock + lane], lane, &q, &s, &bs);
+    q8[b * kBlock + lane] = q;
+    if (lane == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+  }
+  __syncthreads();
+}
+
+// act <- quant(src) over n values produced by other CTAs
+__device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2* sb_s) {
+  const int lane = threadIdx.x & 31;
+  int8_t* q8 = reinterpret_cast<int8_t*>(q_s);
+  for (int b = threadIdx.x >> 5; b < n / kBlock; b += kStepWarps) {
+    int8_t q;
+    float s;
+    int bs;
+    quant_block_warp(__ldcg(src + b * kBlock + lane), lane, &q, &s, &bs);
+    q8[b * kBlock + lane] = q;
+    if (lane == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+  }
+  __syncthreads();
+}
+
+// ---- GEMV phases -----------------------------------------------------------------------
+
+enum { kStore = 0, kResidual = 1, kSiluPair = 2, kHead = 3 };
+
+// MODE kStore/kResidual/kHead: rows [r0, r1) of b4/sw. kSiluPair: gate/up pairs [r0, r1)
+// of a [gate | up] matrix with `ffn` rows per half, writing act[p] = silu(gate) * up.
+template <int MODE>
+__device__ __noinline__ void gemv_phase(const uint32_t* __restrict__ b4, const float* __restrict__ sw,
+                       const GvPlan& P, const ActView act, int r0, int r1, int ffn,
+                       float* __restrict__ out, float* best_v, int* best_i) {
+  const int lane = threadIdx.x & 31;
+  const int grp = lane >> 3;
+  const int per_quad = (MODE == kSiluPair) ? 2 : 4;
+  const int nq = (r1 - r0 + per_quad - 1) / per_quad;
+  for (int q = threadIdx.x >> 5; q < nq; q += kStepWarps) {
+    int row;
+    bool ok;
+    if (MODE == kSiluPair) {
+      const int p = r0 + q * 2 + (grp & 1);
+      ok = p < r1;
+      row = (grp < 2) ? p : ffn + p;
+    } else {
+      row = r0 + q * 4 + grp;
+      ok = row < r1;
+    }
+    const float y = gemv_rows4<8, false>(b4, sw, row, ok, act, P, nullptr);
+    if (MODE == kSiluPair) {
+      const float up = __shfl_down_sync(0xFFFFFFFFu, y, 16);
+      if (grp < 2 && (lane & 7) == 0 && ok) out[row] = silu_mul1(y, up);
+    } else if ((lane & 7) == 0 && ok) {
+      if (MODE == kStore) {
+        out[row] = y;
+      } else if (MODE == kResidual) {
+        out[row] = __fadd_rn(__ldcg(out + row), y);
+      } else {
+        out[row] = y;
+        if (y > *best_v || (y == *best_v && row < *best_i)) { *best_v = y; *best_i = row; }
+      }
+    }
+  }
+}
+
+// ---- attention -------------------------------------------------------------------------
+
+// One warp: rmsnorm(raw[0..128), gain) then rotate-half RoPE with this position's tables,
+// bit-identical to k_rmsnorm (cols = 128) followed by k_rope.
+HV_DEV void warp_norm_rope(const float* raw, const float* __restrict__ gain,
+                           const float* __restrict__ cs, const float* __restrict__ sn,
+                           float eps, float* tmp, float* dst) {
+  const int lane = threadIdx.x & 31;
+  const float4 x = __ldcg(reinterpret_cast<const float4*>(raw) + lane);
+  tmp[4 * lane + 0] = __fmul_rn(x.x, x.x);
+  tmp[4 * lane + 1] = __fmul_rn(x.y, x.y);
+  tmp[4 * lane + 2] = __fmul_rn(x.z, x.z);
+  tmp[4 * lane + 3] = __fmul_rn(x.w, x.w);
+  __syncwarp();
+  const float ss = __fadd_rn(0.0f, pw_leaf8(tmp, kHd, lane & 7));
+  const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHd), eps));
+  __syncwarp();
+  tmp[4 * lane + 0] = __fmul_rn(__ldg(gain + 4 * lane + 0), __fdiv_rn(x.x, d));
+  tmp[4 * lane + 1] = __fmul_rn(__ldg(gain + 4 * lane + 1), __fdiv_rn(x.y, d));
+  tmp[4 * lane + 2] = __fmul_rn(__ldg(gain + 4 * lane + 2), __fdiv_rn(x.z, d));
+  tmp[4 * lane + 3] = __fmul_rn(__ldg(gain + 4 * lane + 3), __fdiv_rn(x.w, d));
+  __syncwarp();
+  for (int i = lane; i < kHd / 2; i += 32) {
+    const float c = __ldg(cs + i), s = __ldg(sn + i);
+    const float lo = tmp[i], hi = tmp[kHd / 2 + i];
+    dst[i] = __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
+    dst[kHd / 2 + i] = __fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s));
+  }
+  __syncwarp();
+}
+
+template <typename T>
+HV_DEV T* ldg_ptr(T* const* p) {
+  return reinterpret_cast<T*>(__ldg(reinterpret_cast<const unsigned long long*>(p)));
+}
+
+template <int GS>
+__device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w* L, int pos, StepShared& S,
+                       float* area) {
+  const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
+  const int chunk_max = (cap + nch - 1) / nch;
+  float* q_s = area;
+  float* kpos_s = q_s + GS * kHd;
+  float* vpos_s = kpos_s + kHd;
+  float* tmp_s = vpos_s + kHd;                       // (GS + 1) x 128
+  float* stat_s = tmp_s + (GS + 1) * kHd;            // 2 GS (+pad)
+  float* lg_s = stat_s + 4 * GS;
+  float* red_s = lg_s + chunk_max * GS;
+  const int warp = threadIdx.x >> 5;
+  const float* cs = D.cos_t + (size_t)pos * (kHd / 2);
+  const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
+  for (int wi = blockIdx.x; wi < nkv * nch; wi += gridDim.x) {
+    const int g = wi / nch, c = wi % nch;
+    if (warp < GS) {
+      warp_norm_rope(D.qkv + (size_t)(g * GS + warp) * kHd, ldg_ptr(&L->qn), cs, sn, D.eps,
+                     tmp_s + warp * kHd, q_s + warp * kHd);
+    } else if (warp == GS) {
+      warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, ldg_ptr(&L->kn), cs, sn, D.eps,
+                     tmp_s + GS * kHd, kpos_s);
+    } else if (warp == GS + 1) {
+      const int lane = threadIdx.x & 31;
+      reinterpret_cast<float4*>(vpos_s)[lane] =
+          __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
+    }
+    __syncthreads();
+    float* kc = ldg_ptr(&L->kc) + (size_t)g * cap * kHd;
+    float* vc = ldg_ptr(&L->vc) + (size_t)g * cap * kHd;
+    if (c == nch - 1 && threadIdx.x < kHd) {         // the chunk holding pos appends
+      kc[(size_t)pos * kHd + threadIdx.x] = kpos_s[threadIdx.x];
+      vc[(size_t)pos * kHd + threadIdx.x] = vpos_s[threadIdx.x];
+    }
+    int t0, t1;
+    chunk_bounds(pos + 1, nch, c, &t0, &t1);
+    float* part = D.part + ((size_t)g * nch + c) * GS * kPartStride;
+    attn_chunk<GS>(q_s, kc, vc, t0, t1, D.attn_scale, pos, kpos_s, vpos_s, lg_s, red_s,
+                   stat_s, part);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) S.flag = (atomicAdd(D.ticket + g, 1) == nch - 1);
+    __syncthreads();
+    if (S.flag) {
+      __threadfence();
+      attn_merge<GS>(D.part + (size_t)g * nch * GS * kPartStride, nch,
+                     D.ctx + (size_t)g * GS * kHd);
+      if (threadIdx.x == 0) D.ticket[g] = 0;
+    }
+    __syncthreads();
+  }
+}
+
+// ---- the kernel ------------------------------------------------------------------------
+
+template <int GS>
+__global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  StepShared& S = *reinterpret_cast<StepShared*>(smem);
+  float* area = reinterpret_cast<float*>(smem + ((sizeof(StepShared) + 15) & ~size_t(15)));
+  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
+  const int kmax = max(max(hid, qdim), ffn);
+  uint4* q_s = reinterpret_cast<uint4*>(area);
+  int2* sb_s = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(area) + kmax);
+  float* x_s = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sb_s) + (kmax / kBlock) * 8);
+  float* sq_s = x_s + hid;
+  const ActView act{q_s, sb_s};
+
+  if (threadIdx.x == 0) {
+    pw_make_plan(hid, &S.pw_hid);
+    gv_make_plan(hid / kBlock, &S.gv_hid);
+    gv_make_plan(qdim / kBlock, &S.gv_o);
+    gv_make_plan(ffn / kBlock, &S.gv_ffn);
+  }
+  const int pos = *D.pos;
+  const int tok = *D.tok;
+  __syncthreads();
+  if (pos < 0 || pos >= D.cap || tok < 0 || tok >= D.vocab) {
+    // every CTA reads the same values, so all leave here, before the first barrier
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(D.status, HV_E_INVALID);
+    return;
+  }
+
+  int hr0, hr1;                       // this CTA's rows of the residual (o and down)
+  row_range(hid, &hr0, &hr1);
+  const __half* emb_row = reinterpret_cast<const __half*>(D.emb16) + (size_t)tok * hid;
+  for (int i = hr0 + threadIdx.x; i < hr1; i += blockDim.x) D.h[i] = __half2float(emb_row[i]);
+
+  for (int l = 0; l < D.n_layer; ++l) {
+    const hv_layer_w* L = D.layers + l;
+    int r0, r1;
+    // P1: qkv
+    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, ldg_ptr(&L->an), hid, D.eps, S, x_s, sq_s,
+                   q_s, sb_s);
+    row_range((D.n_head + 2 * D.n_kv) * kHd, &r0, &r1);
+    gemv_phase<kStore>(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), S.gv_hid, act, r0, r1, 0,
+                       D.qkv, nullptr, nullptr);
+    if (!grid_sync(D.barrier, D.status, S)) return;
+    // P2: attention
+    attn_phase<GS>(D, L, pos, S, area);
+    if (!grid_sync(D.barrier, D.status, S)) return;
+    // P3: o projection + residual
+    pro_quant(D.ctx, qdim, q_s, sb_s);
+    gemv_phase<kResidual>(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), S.gv_o, act, hr0, hr1, 0, D.h,
+                          nullptr, nullptr);
+    if (!grid_sync(D.barrier, D.status, S)) return;
+    // P4: gate/up + SiLU
+    pro_norm_quant(D.h, nullptr, ldg_ptr(&L->fn), hid, D.eps, S, x_s, sq_s, q_s, sb_s);
+    row_range(ffn, &r0, &r1);
+    gemv_phase<kSiluPair>(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), S.gv_hid, act, r0, r1, ffn,
+                          D.act, nullptr, nullptr);
+    if (!grid_sync(D.barrier, D.status, S)) return;
+    // P5: down + residual
+    pro_quant(D.act, ffn, q_s, sb_s);
+    gemv_phase<kResidual>(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), S.gv_ffn, act, hr0, hr1, 0,
+                          D.h, nullptr, nullptr);
+    if (!grid_sync(D.barrier, D.status, S)) return;
+  }
+
+  if (!(flags & HV_STEP_HEAD)) return;
+  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, x_s, sq_s, q_s, sb_s);
+  int r0, r1;
+  row_range(D.head_rows, &r0, &r1);
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  gemv_phase<kHead>(D.head_b4, D.head_sw, S.gv_hid, act, r0, r1, 0, D.logits, &bv, &bi);
+  if (!(flags & HV_STEP_ARGMAX)) return;
+
+  // per-CTA argmax, then the last CTA to finish picks the token
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { S.sv[warp] = bv; S.si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < kStepWarps; ++w)
+        if (S.sv[w] > S.sv[0] || (S.sv[w] == S.sv[0] && S.si[w] < S.si[0])) {
+          S.sv[0] = S.sv[w];
+          S.si[0] = S.si[w];
+        }
+      D.amax_v[blockIdx.x] = S.sv[0];
+      D.amax_i[blockIdx.x] = S.si[0];
+      __threadfence();
+      S.flag = (atomicAdd(D.ticket + D.n_kv, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (S.flag && threadIdx.x == 0) {
+      __threadfence();
+      float v = -INFINITY;
+      int idx = 0x7FFFFFFF;
+      for (int c = 0; c < (int)gridDim.x; ++c) {
+        const float cv = __ldcg(D.amax_v + c);
+        const int ci = __ldcg(D.amax_i + c);
+        if (cv > v || (cv == v && ci < idx)) { v = cv; idx = ci; }
+      }
+      *D.tok = idx;
+      const int s = *D.step;
+      if (s >= 0 && s <= D.cap) D.gen[s] = idx;      // gen holds cap + 1 entries
+      *D.step = s + 1;
+      *D.pos = pos + 1;
+      D.ticket[D.n_kv] = 0;
+    }
+  }
+}
+
+template <int GS>
+static size_t step_smem(int hid, int qdim, int ffn, int cap, int nch) {
+  const int kmax = std::max(std::max(hid, qdim), ffn);
+  const size_t gemv = (size_t)kmax + (size_t)(kmax / kBlock) * 8 + 2 * (size_t)hid * 4;
+  const int chunk_max = (cap + nch - 1) / nch;
+  const size_t attn = sizeof(float) * ((size_t)GS * kHd + 2 * kHd + (GS + 1) * kHd + 4 * GS +
+                                       (size_t)chunk_max * GS + (size_t)kStepWarps * GS * kHd);
+  return ((sizeof(StepShared) + 15) & ~size_t(15)) + std::max(gemv, attn);
+}
+
+static size_t step_smem_any(int gs, int hid, int qdim, int ffn, int cap, int nch) {
+  switch (gs) {
+    case 1: return step_smem<1>(hid, qdim, ffn, cap, nch);
+    case 2: return step_smem<2>(hid, qdim, ffn, cap, nch);
+    case 4: return step_smem<4>(hid, qdim, ffn, cap, nch);
+    default: return step_smem<8>(hid, qdim, ffn, cap, nch);
+  }
+}
+
+static void* step_fn(int gs) {
+  switch (gs) {
+    case 1: return (void*)k_step<1>;
+    case 2: return (void*)k_step<2>;
+    case 4: return (void*)k_step<4>;
+    default: return (void*)k_step<8>;
+  }
+}
+
+}  // namespace hv
+
+using namespace hv;
+
+extern "C" {
+
+int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t* smem,
+                   int* chunks, size_t* part_floats) {
+  HV_REQUIRE(n_kv > 0 && cap > 0 && grid && threads && chunks && part_floats, HV_E_INVALID,
+             "hv_step_config: bad arguments");
+  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
+             "hv_step_config: group size %d (1, 2, 4 or 8)", group);
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  *grid = sms;
+  *threads = kStepThreads;
+  int nch = sms / n_kv;
+  if (nch < 1) nch = 1;
+  const int need = (cap + 511) / 512;
+  if (nch < need) nch = need;
+  *chunks = nch;
+  *part_floats = (size_t)n_kv * nch * group * kPartStride;
+  if (smem) *smem = 0;
+  return HV_OK;
+}
+
+int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
+  HV_REQUIRE(desc, HV_E_INVALID, "hv_step_launch: null descriptor");
+  hv_step_desc h = *desc;
+  HV_REQUIRE(h.head_dim == kHd, HV_E_UNSUPPORTED, "hv_step_launch: head_dim %d", h.head_dim);
+  HV_REQUIRE(h.hidden % kBlock == 0 && h.ffn % kBlock == 0, HV_E_UNSUPPORTED,
+             "hv_step_launch: hidden/ffn not multiples of 32");
+  const int gs = h.n_head / h.n_kv;
+  HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
+             "hv_step_launch: group size %d", gs);
+  HV_REQUIRE(gs + 2 <= kStepWarps, HV_E_UNSUPPORTED, "hv_step_launch: group too large");
+  const size_t smem = step_smem_any(gs, h.hidden, h.n_head * kHd, h.ffn, h.cap, h.attn_chunks);
+  HV_REQUIRE(smem <= 227 * 1024, HV_E_UNSUPPORTED, "hv_step_launch: needs %zu B of smem", smem);
+  void* fn = step_fn(gs);
+  HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  void* args[] = {(void*)&h, (void*)&flags};
+  HV_CUDA(cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kStepThreads), args, smem,
+                                      (cudaStream_t)stream));
+  return HV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,400 @@
+"""ctypes binding to libhive_b200.so — the replacement for HIVE Limited's engine/cudrv.py.
+
+Same surface as the reference's driver binding (init, device, device_name,
+driver_version, device_attribute, compute_capability, retain_primary_context,
+set_current, synchronize, mem_info, alloc, free, upload, download, memset8,
+stream_create, stream_synchronize, capture_begin, capture_end, graph_instantiate,
+graph_launch, graph_destroy, CudaError), plus one function per kernel. Device pointers
+are Python ints; every native call returns a status and a failure raises CudaError
+carrying the library's message.
+
+There is no CPU fallback: if the library cannot be loaded or no GPU is present, the
+first call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+import json
+import os
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_NAME = "libhive_b200.so"
+ABI_VERSION = 1
+
+_L = None
+_lib_path = None
+
+
+class CudaError(RuntimeError):
+    """A library call failed. Carries the call name, the status and the message."""
+
+    def __init__(self, fn: str, code: int, msg: str = ""):
+        super().__init__(f"{fn} failed ({code}): {msg}")
+        self.fn, self.code, self.msg = fn, code, msg
+
+
+_VP, _I, _SZ, _F = C.c_void_p, C.c_int, C.c_size_t, C.c_float
+_PI = C.POINTER(C.c_int)
+
+# name -> argtypes (all functions return int)
+_SIGS = {
+    "hv_version": [],
+    "hv_kernel_list": [C.c_char_p, _SZ],
+    "hv_last_error": [C.c_char_p, _SZ],
+    "hv_init": [],
+    "hv_device_count": [_PI],
+    "hv_set_device": [_I],
+    "hv_get_device": [_PI],
+    "hv_device_name": [_I, C.c_char_p, _I],
+    "hv_compute_capability": [_I, _PI, _PI],
+    "hv_device_attribute": [_I, _I, _PI],
+    "hv_driver_version": [_PI],
+    "hv_mem_info": [C.POINTER(_SZ), C.POINTER(_SZ)],
+    "hv_synchronize": [],
+    "hv_alloc": [C.POINTER(_VP), _SZ],
+    "hv_free": [_VP],
+    "hv_upload": [_VP, _VP, _SZ],
+    "hv_download": [_VP, _VP, _SZ],
+    "hv_memset": [_VP, _I, _SZ],
+    "hv_host_alloc": [C.POINTER(_VP), _SZ],
+    "hv_host_free": [_VP],
+    "hv_upload_async": [_VP, _VP, _SZ, _VP],
+    "hv_download_async": [_VP, _VP, _SZ, _VP],
+    "hv_copy_async": [_VP, _VP, _SZ, _VP],
+    "hv_stream_create": [C.POINTER(_VP)],
+    "hv_stream_destroy": [_VP],
+    "hv_stream_synchronize": [_VP],
+    "hv_capture_begin": [_VP],
+    "hv_capture_end": [_VP, C.POINTER(_VP)],
+    "hv_graph_instantiate": [_VP, C.POINTER(_VP)],
+    "hv_graph_launch": [_VP, _VP],
+    "hv_graph_destroy": [_VP, _VP],
+    "hv_event_create": [C.POINTER(_VP)],
+    "hv_event_destroy": [_VP],
+    "hv_event_record": [_VP, _VP],
+    "hv_event_elapsed_ms": [_VP, _VP, C.POINTER(_F)],
+    "hv_qa8s": [_VP, _VP, _VP, _I, _VP],
+    "hv_a4gv": [_VP, _VP, _VP, _VP, _VP, _I, _I, _VP],
+    "hv_a4gv_idot": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _VP],
+    "hv_rmsnorm": [_VP, _VP, _VP, _I, _I, _F, _VP],
+    "hv_rope": [_VP, _VP, _VP, _VP, _I, _I, _VP],
+    "hv_kv_append": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
+    "hv_attn_decode": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
+    "hv_attn_reserve": [_I, _I, _I],
+    "hv_silu_mul": [_VP, _VP, _VP, _I, _VP],
+    "hv_vadd": [_VP, _VP, _VP, _I, _VP],
+    "hv_gather_emb": [_VP, _VP, _VP, _I, _VP],
+    "hv_argmax_partial": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_argmax_final": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _VP],
+    "hv_quantize_w4": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
+    "hv_step_launch": [_VP, _I, _VP],
+}
+
+
+def library_path(kernels_dir=None) -> Path:
+    d = Path(kernels_dir) if kernels_dir else Path(os.environ.get("HIVE_B200_LIB_DIR", HERE))
+    return d / LIB_NAME
+
+
+def load(kernels_dir=None, verify: bool = True):
+    """Load the library once. With `verify`, its sha256 must match MANIFEST.json (the
+    equivalent of the reference's PTX manifest check, engine/limited.py:218-235) and its
+    ABI version must be the one this binding speaks."""
+    global _L, _lib_path
+    path = library_path(kernels_dir)
+    if _L is not None:
+        if path.resolve() != _lib_path.resolve():
+            raise RuntimeError(f"{LIB_NAME} already loaded from {_lib_path}")
+        return _L
+    if not path.exists():
+        raise RuntimeError(
+            f"{path} not found: build it with `python hive-limited_b200/build.py` "
+            "(there is no CPU fallback)")
+    if verify:
+        man = path.parent / "MANIFEST.json"
+        if man.exists():
+            want = json.loads(man.read_text()).get("sha256")
+            got = hashlib.sha256(path.read_bytes()).hexdigest()
+            if want != got:
+                raise RuntimeError(f"{path.name}: sha256 mismatch.\n  manifest {want}\n"
+                                   f"  on disk  {got}\nRefusing to run a library that is "
+                                   "not the one built.")
+    lib = C.CDLL(str(path))
+    for name, args in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = C.c_int
+    if lib.hv_version() != ABI_VERSION:
+        raise RuntimeError(f"{path.name}: ABI version {lib.hv_version()} != {ABI_VERSION}")
+    _L, _lib_path = lib, path
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    load().hv_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def _call(name: str, *args) -> None:
+    rc = getattr(load(), name)(*args)
+    if rc != 0:
+        raise CudaError(name, rc, last_error())
+
+
+def kernel_list() -> list[str]:
+    buf = C.create_string_buffer(1024)
+    _call("hv_kernel_list", buf, len(buf))
+    return buf.value.decode().split(",")
+
+
+# ---- context (engine/cudrv.py:73-143) ---------------------------------------
+
+def init() -> None:
+    _call("hv_init")
+
+
+def device_count() -> int:
+    n = C.c_int()
+    _call("hv_device_count", C.byref(n))
+    return n.value
+
+
+def device(index: int = 0) -> int:
+    return int(index)
+
+
+def device_name(dev: int) -> str:
+    buf = C.create_string_buffer(128)
+    _call("hv_device_name", dev, buf, 128)
+    return buf.value.decode(errors="replace")
+
+
+def driver_version() -> str:
+    v = C.c_int()
+    _call("hv_driver_version", C.byref(v))
+    return f"{v.value // 1000}.{(v.value % 1000) // 10}"
+
+
+def device_attribute(dev: int, attr: int) -> int:
+    v = C.c_int()
+    _call("hv_device_attribute", dev, attr, C.byref(v))
+    return v.value
+
+
+def compute_capability(dev: int) -> tuple[int, int]:
+    a, b = C.c_int(), C.c_int()
+    _call("hv_compute_capability", dev, C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def retain_primary_context(dev: int) -> int:
+    """Binds the device's primary context to this thread; the returned handle is what
+    set_current() takes."""
+    _call("hv_set_device", dev)
+    return int(dev)
+
+
+def set_current(ctx: int) -> None:
+    _call("hv_set_device", int(ctx))
+
+
+def synchronize() -> None:
+    _call("hv_synchronize")
+
+
+def mem_info() -> tuple[int, int]:
+    f, t = C.c_size_t(), C.c_size_t()
+    _call("hv_mem_info", C.byref(f), C.byref(t))
+    return f.value, t.value
+
+
+# ---- memory -------------------------------------------------------------------
+
+def alloc(nbytes: int) -> int:
+    p = C.c_void_p()
+    _call("hv_alloc", C.byref(p), int(nbytes))
+    return p.value or 0
+
+
+def free(ptr: int) -> None:
+    _call("hv_free", C.c_void_p(ptr))
+
+
+def upload(dst: int, host_ptr: int, nbytes: int) -> None:
+    _call("hv_upload", C.c_void_p(dst), C.c_void_p(host_ptr), int(nbytes))
+
+
+def download(host_ptr: int, src: int, nbytes: int) -> None:
+    _call("hv_download", C.c_void_p(host_ptr), C.c_void_p(src), int(nbytes))
+
+
+def memset8(ptr: int, value: int, nbytes: int) -> None:
+    _call("hv_memset", C.c_void_p(ptr), int(value), int(nbytes))
+
+
+def host_alloc(nbytes: int) -> int:
+    p = C.c_void_p()
+    _call("hv_host_alloc", C.byref(p), int(nbytes))
+    return p.value or 0
+
+
+def host_free(ptr: int) -> None:
+    _call("hv_host_free", C.c_void_p(ptr))
+
+
+def upload_async(dst, host_ptr, nbytes, stream=0):
+    _call("hv_upload_async", C.c_void_p(dst), C.c_void_p(host_ptr), int(nbytes),
+          C.c_void_p(stream))
+
+
+def download_async(host_ptr, src, nbytes, stream=0):
+    _call("hv_download_async", C.c_void_p(host_ptr), C.c_void_p(src), int(nbytes),
+          C.c_void_p(stream))
+
+
+def copy_async(dst, src, nbytes, stream=0):
+    _call("hv_copy_async", C.c_void_p(dst), C.c_void_p(src), int(nbytes), C.c_void_p(stream))
+
+
+# ---- streams, graphs, events ------------------------------------------------------
+
+def stream_create() -> int:
+    s = C.c_void_p()
+    _call("hv_stream_create", C.byref(s))
+    return s.value or 0
+
+
+def stream_destroy(stream: int) -> None:
+    _call("hv_stream_destroy", C.c_void_p(stream))
+
+
+def stream_synchronize(stream: int) -> None:
+    _call("hv_stream_synchronize", C.c_void_p(stream))
+
+
+def capture_begin(stream: int) -> None:
+    _call("hv_capture_begin", C.c_void_p(stream))
+
+
+def capture_end(stream: int) -> int:
+    g = C.c_void_p()
+    _call("hv_capture_end", C.c_void_p(stream), C.byref(g))
+    return g.value or 0
+
+
+def graph_instantiate(graph: int) -> int:
+    e = C.c_void_p()
+    _call("hv_graph_instantiate", C.c_void_p(graph), C.byref(e))
+    return e.value or 0
+
+
+def graph_launch(exec_: int, stream: int) -> None:
+    _call("hv_graph_launch", C.c_void_p(exec_), C.c_void_p(stream))
+
+
+def graph_destroy(graph: int, exec_: int) -> None:
+    try:
+        _call("hv_graph_destroy", C.c_void_p(graph), C.c_void_p(exec_))
+    except CudaError:
+        pass
+
+
+def event_create() -> int:
+    e = C.c_void_p()
+    _call("hv_event_create", C.byref(e))
+    return e.value or 0
+
+
+def event_destroy(e: int) -> None:
+    _call("hv_event_destroy", C.c_void_p(e))
+
+
+def event_record(e: int, stream: int = 0) -> None:
+    _call("hv_event_record", C.c_void_p(e), C.c_void_p(stream))
+
+
+def event_elapsed_ms(e0: int, e1: int) -> float:
+    ms = C.c_float()
+    _call("hv_event_elapsed_ms", C.c_void_p(e0), C.c_void_p(e1), C.byref(ms))
+    return ms.value
+
+
+# ---- kernels ------------------------------------------------------------------------
+
+def _p(x):
+    return C.c_void_p(int(x))
+
+
+def qa8s(src, a8, sa, nb, stream=0):
+    _call("hv_qa8s", _p(src), _p(a8), _p(sa), nb, _p(stream))
+
+
+def a4gv(a8, sa, b4, sw, dst, k8, n, stream=0):
+    _call("hv_a4gv", _p(a8), _p(sa), _p(b4), _p(sw), _p(dst), k8, n, _p(stream))
+
+
+def a4gv_idot(a8, sa, b4, sw, dst, idot, k8, n, stream=0):
+    _call("hv_a4gv_idot", _p(a8), _p(sa), _p(b4), _p(sw), _p(dst), _p(idot), k8, n, _p(stream))
+
+
+def rmsnorm(src, dst, w, rows, cols, eps=1e-5, stream=0):
+    _call("hv_rmsnorm", _p(src), _p(dst), _p(w), rows, cols, C.c_float(eps), _p(stream))
+
+
+def rope(vec, cos_t, sin_t, pos, heads, half, stream=0):
+    _call("hv_rope", _p(vec), _p(cos_t), _p(sin_t), _p(pos), heads, half, _p(stream))
+
+
+def kv_append(k, v, kc, vc, pos, nkv, hd, cap, stream=0):
+    _call("hv_kv_append", _p(k), _p(v), _p(kc), _p(vc), _p(pos), nkv, hd, cap, _p(stream))
+
+
+def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
+    _call("hv_attn_decode", _p(q), _p(kc), _p(vc), _p(ctx), _p(scale), _p(pos), nq, hd,
+          group, kvstride, _p(stream))
+
+
+def attn_reserve(nkv, group, cap):
+    _call("hv_attn_reserve", nkv, group, cap)
+
+
+def silu_mul(gate, up, act, n, stream=0):
+    _call("hv_silu_mul", _p(gate), _p(up), _p(act), n, _p(stream))
+
+
+def vadd(a, b, out, n, stream=0):
+    _call("hv_vadd", _p(a), _p(b), _p(out), n, _p(stream))
+
+
+def gather_emb(emb16, tok, h, hid, stream=0):
+    _call("hv_gather_emb", _p(emb16), _p(tok), _p(h), hid, _p(stream))
+
+
+def argmax_partial(logits, pv, pi, n, parts, stream=0):
+    _call("hv_argmax_partial", _p(logits), _p(pv), _p(pi), n, parts, _p(stream))
+
+
+def argmax_final(pv, pi, tok, gen, step, pos, parts, stream=0):
+    _call("hv_argmax_final", _p(pv), _p(pi), _p(tok), _p(gen), _p(step), _p(pos), parts,
+          _p(stream))
+
+
+def quantize_w4(w, packed, scale, n, k, stream=0):
+    _call("hv_quantize_w4", _p(w), _p(packed), _p(scale), n, k, _p(stream))
+
+
+class Scalar:
+    """Kept for source compatibility with engine/cudrv.py:272-278."""
+
+    __slots__ = ("value",)
+
+    def __init__(self, value: int):
+        self.value = int(value)

@@ -1,0 +1,592 @@
+"""HIVE Limited's batch-1 decode engine, B200-native.
+
+Same public API as engine/limited.py of the reference (Engine, generate, stream,
+logits, verify_graph, bits_per_weight, weight_bytes, bind_thread, free, cfg,
+device_name, kv_bytes, _graph_ok; quantize_w4 / dequantize_w4 / Config / SafeTensors /
+load_model_tensors / BLOCK), with the driver layer replaced: kernels come from
+libhive_b200.so (hand-written CUDA for sm_100a) through ctypes (hvdrv.py). No PyTorch,
+no CPU fallback.
+
+Two step implementations, both bit-identical by construction:
+  * the eager step issues the reference's sequence of kernels one by one
+    (engine/limited.py:374-419), each a standalone hv_* entry point;
+  * the fused step (default) runs the whole token -- every layer, the LM head and the
+    greedy argmax -- as ONE persistent kernel launch (hv_step_launch).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+from pathlib import Path
+
+import numpy as np
+
+import hvdrv
+from w4format import (BLOCK, Config, SafeTensors, dequantize_w4, load_model_tensors,  # noqa: F401
+                      quantize_w4)
+
+F32 = np.float32
+RMS_EPS = 1e-5          # the shipped rmsnorm kernel's epsilon (engine/reference.py:34)
+GVBD = 256              # kept for source compatibility (engine/limited.py:183)
+ARGMAX_PARTS = 128      # argmax_p partial count (engine/limited.py:423-425)
+
+
+class _LayerW(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "qkv_b4", "qkv_sw", "o_b4", "o_sw", "gu_b4", "gu_sw", "dn_b4", "dn_sw",
+        "an", "fn", "qn", "kn", "kc", "vc")]
+
+
+class _StepDesc(C.Structure):
+    _fields_ = ([(n, C.c_int) for n in ("n_layer", "hidden", "ffn", "n_head", "n_kv",
+                                          "head_dim", "head_rows", "cap")]
+                + [("eps", C.c_float), ("attn_scale", C.c_float),
+                   ("attn_chunks", C.c_int), ("vocab", C.c_int)]
+                + [(n, C.c_void_p) for n in (
+                    "layers", "emb16", "onorm", "head_b4", "head_sw", "cos_t", "sin_t",
+                    "tok", "pos", "step", "gen", "h", "qkv", "ctx", "act", "logits",
+                    "part", "ticket", "amax_v", "amax_i", "barrier", "status")])
+
+
+STEP_HEAD = 1
+STEP_ARGMAX = 2
+
+
+class _TensorSource:
+    """name -> float array, from a dict or from an iterator of (name, array) pairs drawn
+    lazily (so a streamed synthetic model is never fully resident on the host)."""
+
+    def __init__(self, src):
+        if isinstance(src, dict):
+            self._d, self._it = dict(src), None
+        else:
+            self._d, self._it = {}, iter(src)
+
+    def take(self, name) -> np.ndarray:
+        while name not in self._d:
+            if self._it is None:
+                raise KeyError(f"missing tensor {name!r} -- is this a Qwen3 model?")
+            try:
+                k, v = next(self._it)
+            except StopIteration:
+                self._it = None
+                continue
+            self._d[k] = v
+        return self._d.pop(name)
+
+
+class Engine:
+    """Batch-1 resident decode (engine/limited.py:186-659).
+
+    Extra keyword arguments beyond the reference's:
+      config / tensors  -- build from a geometry dict and a name -> array source instead
+                           of a model directory (synthetic workloads);
+      max_context       -- KV capacity (the reference fixes 4096);
+      device            -- CUDA device index;
+      fused             -- use the one-launch fused step (default) or the eager sequence;
+      quantize_on       -- "device" (hv_quantize_w4, bit-identical) or "host" (numpy).
+    """
+
+    def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
+                 config=None, tensors=None, max_context=None, device=0, fused=True,
+                 quantize_on="device"):
+        if config is None:
+            self.cfg = Config.load(model_dir)
+        else:
+            self.cfg = config if isinstance(config, Config) else Config(config)
+        if max_context is not None:
+            self.cfg.max_context = int(max_context)
+        self.quiet = quiet
+        self.fused = bool(fused)
+        self._buffers: list[int] = []
+        hvdrv.load(kernels_dir, verify=verify_kernels)
+        hvdrv.init()
+        self.dev = hvdrv.device(device)
+        major, minor = hvdrv.compute_capability(self.dev)
+        if (major, minor) != (10, 0):
+            raise RuntimeError(f"libhive_b200 is built for sm_100a (B200); this device is "
+                               f"{major}.{minor}")
+        self.ctx = hvdrv.retain_primary_context(self.dev)
+        self.device_name = hvdrv.device_name(self.dev)
+        self._graph = self._graph_exec = 0
+        self._graph_ok = None
+        self._stream = 0
+        self._stream_cur = 0
+        src = _TensorSource(tensors if tensors is not None
+                            else load_model_tensors(model_dir))
+        self._upload_weights(src, quantize_on)
+        del src
+        self._alloc_state()
+
+    # -- setup ----------------------------------------------------------------------
+
+    def _log(self, msg):
+        if not self.quiet:
+            print(msg, flush=True)
+
+    def _alloc(self, nbytes: int) -> int:
+        p = hvdrv.alloc(max(int(nbytes), 16))
+        self._buffers.append(p)
+        return p
+
+    def _up(self, arr: np.ndarray) -> int:
+        arr = np.ascontiguousarray(arr)
+        p = self._alloc(arr.nbytes)
+        hvdrv.upload(p, arr.ctypes.data, arr.nbytes)
+        return p
+
+    def _up_w4(self, parts: list[np.ndarray]):
+        """Quantise rows [part0 | part1 | ...] to the per-32 int4 form and upload.
+        -> (b4, sw, K, N)"""
+        k = parts[0].shape[1]
+        n = sum(p.shape[0] for p in parts)
+        if self._quantize_on == "host":
+            w = np.concatenate([p.astype(F32, copy=False) for p in parts], 0)
+            packed, scale = quantize_w4(w)
+            return self._up(packed), self._up(scale), k, n
+        b4 = self._alloc(n * k // 2)
+        sw = self._alloc(n * k // BLOCK * 4)
+        off = 0
+        for p in parts:
+            p = np.ascontiguousarray(p, dtype=F32)
+            hvdrv.upload(self._stage + off, p.ctypes.data, p.nbytes)
+            off += p.nbytes
+        hvdrv.quantize_w4(self._stage, b4, sw, n, k)
+        hvdrv.synchronize()
+        return b4, sw, k, n
+
+    def _upload_weights(self, src: _TensorSource, quantize_on: str):
+        c = self.cfg
+        qd, nq, nkv = c.head_dim, c.n_head, c.n_kv
+        self._quantize_on = quantize_on
+        self._stage = 0
+        if quantize_on == "device":
+            elems = max((nq + 2 * nkv) * qd * c.hidden, 2 * c.ffn * c.hidden,
+                        c.hidden * nq * qd, c.hidden * c.ffn, c.vocab * c.hidden)
+            self._stage = hvdrv.alloc(elems * 4)
+        try:
+            self._log(f"quantizing {c.n_layer} layers to per-32 int4 ...")
+            emb = src.take("model.embed_tokens.weight")
+            emb16 = emb.astype(np.float16)
+            del emb
+            self.d_emb16 = self._up(emb16)
+            if c.tied:                        # the reference quantises the f16 copy
+                self.head = self._up_w4([emb16.astype(F32)])
+            del emb16
+            self.layers = []
+            for l in range(c.n_layer):
+                p = f"model.layers.{l}."
+                t = lambda n: src.take(p + n)  # noqa: E731
+                qkv = self._up_w4([t("self_attn.q_proj.weight"), t("self_attn.k_proj.weight"),
+                                   t("self_attn.v_proj.weight")])
+                o = self._up_w4([t("self_attn.o_proj.weight")])
+                gu = self._up_w4([t("mlp.gate_proj.weight"), t("mlp.up_proj.weight")])
+                down = self._up_w4([t("mlp.down_proj.weight")])
+                self.layers.append({
+                    "an": self._up(t("input_layernorm.weight").astype(F32)),
+                    "fn": self._up(t("post_attention_layernorm.weight").astype(F32)),
+                    "qn": self._up(t("self_attn.q_norm.weight").astype(F32)),
+                    "kn": self._up(t("self_attn.k_norm.weight").astype(F32)),
+                    "qkv": qkv, "o": o, "gu": gu, "down": down,
+                })
+                if (l + 1) % 7 == 0:
+                    self._log(f"  {l + 1}/{c.n_layer}")
+            self.d_onorm = self._up(src.take("model.norm.weight").astype(F32))
+            if not c.tied:
+                self.head = self._up_w4([src.take("lm_head.weight")])
+            self.n_head_rows = self.head[3]
+        finally:
+            if self._stage:
+                hvdrv.free(self._stage)
+                self._stage = 0
+
+    def _alloc_state(self):
+        c = self.cfg
+        hid, ffn, qd = c.hidden, c.ffn, c.head_dim
+        nq, nkv, cap = c.n_head, c.n_kv, c.max_context
+        qkv_rows = (nq + 2 * nkv) * qd
+        wide = max(hid, ffn, nq * qd)
+        self.d_h = self._alloc(hid * 4)
+        self.d_hn = self._alloc(hid * 4)
+        self.d_qkv = self._alloc(qkv_rows * 4)
+        self.d_ctx = self._alloc(nq * qd * 4)
+        self.d_o = self._alloc(hid * 4)
+        self.d_gu = self._alloc(2 * ffn * 4)
+        self.d_act = self._alloc(ffn * 4)
+        self.d_logits = self._alloc(self.n_head_rows * 4)
+        self.d_a8 = self._alloc(wide)
+        self.d_sa = self._alloc(2 * (wide // BLOCK) * 4)
+        # KV cache: f32, one allocation, [layer][k|v][n_kv][cap][hd]
+        self.kv_bytes = 2 * c.n_layer * nkv * cap * qd * 4
+        self.d_kv = self._alloc(self.kv_bytes)
+        per = nkv * cap * qd * 4
+        self.KC = [self.d_kv + (2 * l) * per for l in range(c.n_layer)]
+        self.VC = [self.d_kv + (2 * l + 1) * per for l in range(c.n_layer)]
+        hvdrv.memset8(self.d_kv, 0, self.kv_bytes)
+        half = qd // 2
+        pos = np.arange(cap, dtype=np.float64)[:, None]
+        inv = 1.0 / (c.rope_theta ** (np.arange(half, dtype=np.float64) * 2.0 / qd))
+        ang = pos * inv[None, :]
+        self.d_cos = self._up(np.cos(ang).astype(F32))
+        self.d_sin = self._up(np.sin(ang).astype(F32))
+        self.attn_scale = F32(1.0 / np.sqrt(qd))
+        self.d_scale = self._up(np.array([self.attn_scale], F32))
+        self.d_tok = self._alloc(4)
+        self.d_pos = self._alloc(4)
+        self.d_step = self._alloc(4)
+        self.d_pv = self._alloc(ARGMAX_PARTS * 4)
+        self.d_pi = self._alloc(ARGMAX_PARTS * 4)
+        self.d_gen = self._alloc((cap + 1) * 4)
+        hvdrv.attn_reserve(nkv, c.group, cap)
+        self._build_desc()
+
+    def _build_desc(self):
+        """The fused step's descriptor and its scratch (engine/limited.py has no
+        equivalent: the reference issues each kernel separately)."""
+        c = self.cfg
+        grid, threads = C.c_int(), C.c_int()
+        smem, chunks, part = C.c_size_t(), C.c_int(), C.c_size_t()
+        hvdrv._call("hv_step_config", c.n_kv, c.group, c.max_context, C.byref(grid),
+                    C.byref(threads), C.byref(smem), C.byref(chunks), C.byref(part))
+        self.step_grid = grid.value
+        lw = (_LayerW * c.n_layer)()
+        for l, w in enumerate(self.layers):
+            lw[l] = _LayerW(w["qkv"][0], w["qkv"][1], w["o"][0], w["o"][1], w["gu"][0],
+                            w["gu"][1], w["down"][0], w["down"][1], w["an"], w["fn"],
+                            w["qn"], w["kn"], self.KC[l], self.VC[l])
+        self.d_layers = self._alloc(C.sizeof(lw))
+        hvdrv.upload(self.d_layers, C.addressof(lw), C.sizeof(lw))
+        self.d_part = self._alloc(part.value * 4)
+        self.d_ticket = self._alloc((c.n_kv + 1) * 4)
+        hvdrv.memset8(self.d_ticket, 0, (c.n_kv + 1) * 4)
+        self.d_amax_v = self._alloc(grid.value * 4)
+        self.d_amax_i = self._alloc(grid.value * 4)
+        self.d_barrier = self._alloc(4)
+        self.d_status = self._alloc(4)
+        hvdrv.memset8(self.d_barrier, 0, 4)
+        hvdrv.memset8(self.d_status, 0, 4)
+        hb4, hsw, _, hn = self.head
+        self._desc = _StepDesc(
+            c.n_layer, c.hidden, c.ffn, c.n_head, c.n_kv, c.head_dim, hn, c.max_context,
+            RMS_EPS, float(self.attn_scale), chunks.value, c.vocab,
+            self.d_layers, self.d_emb16, self.d_onorm, hb4, hsw, self.d_cos, self.d_sin,
+            self.d_tok, self.d_pos, self.d_step, self.d_gen, self.d_h, self.d_qkv,
+            self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
+            self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status)
+
+    def _set_i32(self, ptr: int, value: int):
+        hvdrv.upload(ptr, np.array([value], np.int32).ctypes.data, 4)
+
+    def _get_i32(self, ptr: int) -> int:
+        out = np.zeros(1, np.int32)
+        hvdrv.download(out.ctypes.data, ptr, 4)
+        return int(out[0])
+
+    # -- the decode step ------------------------------------------------------------------
+
+    def _gemv(self, src, w4, dst):
+        """quantize activations to per-32 int8, then the exact-int32 int4 GEMV."""
+        b4, sw, k, n = w4
+        s = self._stream_cur
+        hvdrv.qa8s(src, self.d_a8, self.d_sa, k // BLOCK, s)
+        hvdrv.a4gv(self.d_a8, self.d_sa, b4, sw, dst, k // 8, n, s)
+
+    def _step_eager(self):
+        """One transformer step at d_pos, kernel by kernel (engine/limited.py:374-419)."""
+        c = self.cfg
+        hid, ffn, qd = c.hidden, c.ffn, c.head_dim
+        nq, nkv, cap = c.n_head, c.n_kv, c.max_context
+        s = self._stream_cur
+        dq = self.d_qkv
+        dk = self.d_qkv + nq * qd * 4
+        dv = self.d_qkv + (nq + nkv) * qd * 4
+        hvdrv.gather_emb(self.d_emb16, self.d_tok, self.d_h, hid, s)
+        for l, w in enumerate(self.layers):
+            hvdrv.rmsnorm(self.d_h, self.d_hn, w["an"], 1, hid, RMS_EPS, s)
+            self._gemv(self.d_hn, w["qkv"], self.d_qkv)
+            hvdrv.rmsnorm(dq, dq, w["qn"], nq, qd, RMS_EPS, s)
+            hvdrv.rmsnorm(dk, dk, w["kn"], nkv, qd, RMS_EPS, s)
+            hvdrv.rope(dq, self.d_cos, self.d_sin, self.d_pos, nq, qd // 2, s)
+            hvdrv.rope(dk, self.d_cos, self.d_sin, self.d_pos, nkv, qd // 2, s)
+            hvdrv.kv_append(dk, dv, self.KC[l], self.VC[l], self.d_pos, nkv, qd, cap, s)
+            hvdrv.attn_decode(dq, self.KC[l], self.VC[l], self.d_ctx, self.d_scale,
+                              self.d_pos, nq, qd, c.group, cap * qd, s)
+            self._gemv(self.d_ctx, w["o"], self.d_o)
+            hvdrv.vadd(self.d_h, self.d_o, self.d_h, hid, s)
+            hvdrv.rmsnorm(self.d_h, self.d_hn, w["fn"], 1, hid, RMS_EPS, s)
+            self._gemv(self.d_hn, w["gu"], self.d_gu)
+            hvdrv.silu_mul(self.d_gu, self.d_gu + ffn * 4, self.d_act, ffn, s)
+            self._gemv(self.d_act, w["down"], self.d_o)
+            hvdrv.vadd(self.d_h, self.d_o, self.d_h, hid, s)
+        hvdrv.rmsnorm(self.d_h, self.d_hn, self.d_onorm, 1, hid, RMS_EPS, s)
+        self._gemv(self.d_hn, self.head, self.d_logits)
+
+    def _argmax_into_next(self):
+        """Pick the next token and advance tok/pos/step on device (limited.py:421-428)."""
+        s = self._stream_cur
+        hvdrv.argmax_partial(self.d_logits, self.d_pv, self.d_pi, self.n_head_rows,
+                             ARGMAX_PARTS, s)
+        hvdrv.argmax_final(self.d_pv, self.d_pi, self.d_tok, self.d_gen, self.d_step,
+                           self.d_pos, ARGMAX_PARTS, s)
+
+    def _step_fused(self, flags: int):
+        hvdrv._call("hv_step_launch", C.byref(self._desc), int(flags),
+                    C.c_void_p(self._stream_cur))
+
+    def step_status(self) -> int:
+        """Nonzero if a bounded wait inside the fused step ran out (HV_E_TIMEOUT)."""
+        return self._get_i32(self.d_status)
+
+    def reset_step_state(self):
+        """Clear the fused step's barrier/ticket/status words after a failed launch."""
+        hvdrv.synchronize()
+        hvdrv.memset8(self.d_barrier, 0, 4)
+        hvdrv.memset8(self.d_status, 0, 4)
+        hvdrv.memset8(self.d_ticket, 0, (self.cfg.n_kv + 1) * 4)
+
+    def _check_status(self):
+        st = self.step_status()
+        if st:
+            self.reset_step_state()
+            raise hvdrv.CudaError("hv_step_launch", st,
+                                  "a bounded device-side wait ran out; state was reset")
+
+    def _prefill_token(self, tok: int, pos: int, last_flags):
+        """Step one prompt token. `last_flags` is None for every prompt token but the last;
+        for the last it is the fused step's flags (the eager step always runs the head)."""
+        self._set_i32(self.d_tok, int(tok))
+        self._set_i32(self.d_pos, pos)
+        if self.fused:
+            self._step_fused(0 if last_flags is None else last_flags)
+        else:
+            self._step_eager()
+
+    def _decode_one(self):
+        """One decode iteration (engine/limited.py:479-484).
+
+        Eager: argmax of the current logits -> tok/gen/step/pos, then the step at the new
+        position. Fused: the same work in the other order inside one launch -- the step
+        at the current tok/pos, its LM head, then argmax -> tok/gen/step/pos -- because
+        the fused prefill's last launch already took the first argmax. Either way an
+        iteration is one full step, and token i sits in gen[i] once iteration i is done.
+        """
+        if self.fused:
+            self._step_fused(STEP_HEAD | STEP_ARGMAX)
+        else:
+            self._argmax_into_next()
+            self._step_eager()
+
+    def bind_thread(self):
+        """Bind this engine's device to the calling thread (engine/limited.py:430-436)."""
+        hvdrv.set_current(self.ctx)
+
+    # -- public API -------------------------------------------------------------------
+
+    def _check_len(self, prompt_ids, max_new):
+        c = self.cfg
+        if not prompt_ids:
+            raise ValueError("prompt_ids is empty")
+        if len(prompt_ids) + max_new > c.max_context:
+            raise ValueError(
+                f"{len(prompt_ids)} prompt + {max_new} new exceeds the {c.max_context}-token "
+                "context of this engine")
+
+    def _prefill(self, prompt_ids, last_flags=STEP_HEAD | STEP_ARGMAX):
+        self._set_i32(self.d_step, 0)
+        hvdrv.memset8(self.d_gen, 0, (self.cfg.max_context + 1) * 4)
+        n = len(prompt_ids)
+        for i, tok in enumerate(prompt_ids):
+            self._prefill_token(tok, i, last_flags if i == n - 1 else None)
+
+    def _token(self, i: int) -> int:
+        """Token i of the current generation, once decode iteration i has run."""
+        return self._get_i32(self.d_gen + 4 * i)
+
+    def generate(self, prompt_ids, max_new=64, stop_on_eos=True, use_graph=None):
+        """Greedy generation. Returns (tokens, prefill_seconds, decode_seconds)."""
+        c = self.cfg
+        self._check_len(prompt_ids, max_new)
+        hvdrv.synchronize()
+        t0 = time.perf_counter()
+        self._prefill(prompt_ids)
+        hvdrv.synchronize()
+        t1 = time.perf_counter()
+        graph = self._graph_ok if use_graph is None else use_graph
+        if graph:
+            try:
+                self._build_graph()
+            except Exception:
+                graph = False
+        out = []
+        for i in range(max_new):
+            if graph:
+                self._step_graph()
+            else:
+                self._decode_one()
+            if stop_on_eos:
+                hvdrv.synchronize()
+                tok = self._token(i)
+                out.append(tok)
+                if c.eos is not None and tok == c.eos:
+                    break
+            else:
+                out.append(None)
+        hvdrv.synchronize()
+        t2 = time.perf_counter()
+        if self.fused:
+            self._check_status()
+        if out and out[0] is None:
+            got = np.zeros(c.max_context + 1, np.int32)
+            hvdrv.download(got.ctypes.data, self.d_gen, got.nbytes)
+            out = [int(x) for x in got[:len(out)]]
+        return out, t1 - t0, t2 - t1
+
+    # ---- graph-replayed decode (engine/limited.py:502-539) ------------------------------
+
+    def _build_graph(self):
+        if self._graph_exec:
+            return
+        if not self._stream:
+            self._stream = hvdrv.stream_create()
+        hvdrv.synchronize()
+        hvdrv.capture_begin(self._stream)
+        self._stream_cur = self._stream
+        try:
+            self._decode_one()
+            graph = hvdrv.capture_end(self._stream)
+        except Exception:
+            try:
+                hvdrv.capture_end(self._stream)
+            except Exception:
+                pass
+            raise
+        finally:
+            self._stream_cur = 0
+        self._graph = graph
+        self._graph_exec = hvdrv.graph_instantiate(graph)
+
+    def _step_graph(self):
+        hvdrv.graph_launch(self._graph_exec, self._stream)
+
+    def verify_graph(self, prompt_ids, n=24) -> bool:
+        """The graph must produce the same tokens as issuing the launches directly."""
+        eager, _, _ = self.generate(prompt_ids, max_new=n, use_graph=False)
+        fast, _, _ = self.generate(prompt_ids, max_new=n, use_graph=True)
+        return eager == fast
+
+    def stream(self, prompt_ids, max_new=64, stop_evt=None, host_tokens=False):
+        """Yields ("prefill", seconds) once, then ("tok", id, seconds_since_first_token).
+
+        With host_tokens (fused step only), every decode step is driven from the host:
+        the token and position are copied host->device from pinned memory, the step is
+        launched, and the token it produces is copied back device->host before the next
+        step -- the loop a host-side sampler or detokeniser would run."""
+        c = self.cfg
+        self._check_len(prompt_ids, max_new)
+        if host_tokens and not self.fused:
+            raise ValueError("host_tokens needs the fused step")
+        hvdrv.synchronize()
+        t0 = time.perf_counter()
+        self._prefill(prompt_ids)
+        hvdrv.synchronize()
+        yield ("prefill", time.perf_counter() - t0)
+        if host_tokens:
+            yield from self._stream_host_fed(len(prompt_ids), max_new, stop_evt)
+            return
+        graph = bool(self._graph_ok)
+        if graph:
+            try:
+                self._build_graph()
+            except Exception:
+                graph = False
+        first = None
+        for i in range(max_new):
+            if stop_evt is not None and stop_evt.is_set():
+                return
+            if graph:
+                self._step_graph()
+            else:
+                self._decode_one()
+            hvdrv.synchronize()
+            now = time.perf_counter()
+            if first is None:
+                first = now
+            tok = self._token(i)
+            yield ("tok", tok, now - first)
+            if c.eos is not None and tok == c.eos:
+                return
+
+    def _stream_host_fed(self, n_prompt, max_new, stop_evt):
+        c = self.cfg
+        pin = hvdrv.host_alloc(16)
+        buf = (C.c_int32 * 4).from_address(pin)
+        try:
+            tok = self._get_i32(self.d_tok)        # token 0, from the prefill's argmax
+            first = None
+            for i in range(max_new):
+                if stop_evt is not None and stop_evt.is_set():
+                    return
+                buf[0], buf[1] = tok, n_prompt + i
+                hvdrv.upload_async(self.d_tok, pin, 4)
+                hvdrv.upload_async(self.d_pos, pin + 4, 4)
+                self._step_fused(STEP_HEAD | STEP_ARGMAX)
+                hvdrv.download_async(pin + 8, self.d_tok, 4)
+                hvdrv.synchronize()
+                now = time.perf_counter()
+                if first is None:
+                    first = now
+                yield ("tok", tok, now - first)
+                if c.eos is not None and tok == c.eos:
+                    return
+                tok = int(buf[2])
+        finally:
+            hvdrv.host_free(pin)
+
+    def logits(self, prompt_ids) -> np.ndarray:
+        """Run the prompt and return the final f32 logits."""
+        n = len(prompt_ids)
+        for i, tok in enumerate(prompt_ids):
+            self._prefill_token(tok, i, STEP_HEAD if i == n - 1 else None)
+        hvdrv.synchronize()
+        if self.fused:
+            self._check_status()
+        return self.download_logits()
+
+    def download_logits(self) -> np.ndarray:
+        out = np.zeros(self.n_head_rows, F32)
+        hvdrv.download(out.ctypes.data, self.d_logits, out.nbytes)
+        return out
+
+    def _weight_bits(self) -> tuple[int, int]:
+        bits = elems = 0
+        mats = [w[key] for w in self.layers for key in ("qkv", "o", "gu", "down")]
+        for b4, sw, k, n in mats + [self.head]:
+            bits += n * (k // 8) * 32 + n * (k // BLOCK) * 32
+            elems += n * k
+        return bits, elems
+
+    def bits_per_weight(self) -> float:
+        bits, elems = self._weight_bits()
+        return bits / elems
+
+    def weight_bytes(self) -> int:
+        """Weight bytes a batch-1 step reads per token (packed int4 + f32 scales)."""
+        bits, _ = self._weight_bits()
+        return bits // 8
+
+    def free(self):
+        if getattr(self, "_graph_exec", 0) or getattr(self, "_graph", 0):
+            hvdrv.graph_destroy(self._graph, self._graph_exec)
+            self._graph = self._graph_exec = 0
+        if getattr(self, "_stream", 0):
+            try:
+                hvdrv.stream_destroy(self._stream)
+            except Exception:
+                pass
+            self._stream = 0
+        for p in self._buffers:
+            try:
+                hvdrv.free(p)
+            except Exception:
+                pass
+        self._buffers.clear()

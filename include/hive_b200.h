@@ -1,0 +1,231 @@
+/* hive_b200 — C ABI of the B200-native batch-1 W4A8 Qwen3 decode library.
+ *
+ * Drop-in for HIVE Limited's driver layer: engine/cudrv.py (ctypes over libcuda plus the
+ * PTX loader) and the eleven PTX entry points engine/limited.py launches through it.
+ * Each declaration names the reference interface it replaces.
+ *
+ * Conventions
+ *   - Every function returns an int status: HV_OK (0) on success, a CUDA runtime error
+ *     code (1..999) when a CUDA call failed, or an HV_E_* code (>= 1000). The message of
+ *     the most recent failure on the calling thread is read with hv_last_error(). The
+ *     library never calls exit() or abort().
+ *   - Device pointers are plain pointers into memory from hv_alloc() (or any CUDA
+ *     allocation on the current device); sizes are element or byte counts as named.
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy default stream
+ *     (the stream the reference launches on outside graph capture).
+ *   - Threads: calls act on the device current on the calling thread; a thread that did
+ *     not create the engine binds it first with hv_set_device() (engine/limited.py:430-436
+ *     bind_thread, engine/cudrv.py:124-132 set_current).
+ *   - Device-resident scalars (token, position, step) are int32 device pointers, as in
+ *     the reference (engine/limited.py:336-343).
+ */
+#ifndef HIVE_B200_H
+#define HIVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HV_ABI_VERSION 1
+
+#define HV_OK 0
+#define HV_E_INVALID 1001      /* bad argument (null pointer, size, alignment) */
+#define HV_E_UNSUPPORTED 1002  /* shape outside what the kernels implement */
+#define HV_E_NODEVICE 1003     /* no CUDA device */
+#define HV_E_TIMEOUT 1004      /* a bounded device-side wait ran out (see hv_step_status) */
+#define HV_E_CAPTURE 1005      /* operation not allowed while the stream is being captured */
+#define HV_E_COMM 1006         /* collective / peer setup failed */
+
+/* ---- library ------------------------------------------------------------------- */
+
+/* ABI version of the loaded library (HV_ABI_VERSION). Replaces the kernel manifest
+ * check of engine/limited.py:218-235 together with hv_kernel_list(). */
+int hv_version(void);
+/* Comma-separated names of the device entry points compiled into this library. */
+int hv_kernel_list(char* buf, size_t len);
+/* Copies the calling thread's most recent error message (NUL-terminated). */
+int hv_last_error(char* buf, size_t len);
+
+/* ---- device and context (engine/cudrv.py:73-135) -------------------------------- */
+
+int hv_init(void);                                            /* cudrv.init          :73-74  */
+int hv_device_count(int* n);
+int hv_set_device(int dev);                                   /* cudrv.set_current   :124-132 */
+int hv_get_device(int* dev);                                  /* cudrv.device        :77-80  */
+int hv_device_name(int dev, char* buf, int len);              /* cudrv.device_name   :83-86  */
+int hv_compute_capability(int dev, int* major, int* minor);   /* cudrv.compute_capability :106-114 */
+int hv_device_attribute(int dev, int attr, int* value);       /* cudrv.device_attribute :99-103 (CUdevice_attribute numbering) */
+int hv_driver_version(int* version);                          /* cudrv.driver_version :89-96 */
+int hv_mem_info(size_t* free_bytes, size_t* total_bytes);     /* cudrv.mem_info      :139-143 */
+int hv_synchronize(void);                                     /* cudrv.synchronize   :135-136 */
+
+/* ---- memory (engine/cudrv.py:148-172) -------------------------------------------- */
+
+/* Sizes are rounded up to 256 bytes, so bulk prefetches that round a range outwards to
+ * 16 bytes stay inside the allocation. */
+int hv_alloc(void** ptr, size_t nbytes);                      /* cudrv.alloc   :148-151 */
+int hv_free(void* ptr);                                       /* cudrv.free    :154-155 */
+int hv_upload(void* dst, const void* host_src, size_t nbytes);    /* cudrv.upload  :158-161 */
+int hv_download(void* host_dst, const void* src, size_t nbytes);  /* cudrv.download :164-167 */
+int hv_memset(void* ptr, int value, size_t nbytes);           /* cudrv.memset8 :170-173 */
+int hv_host_alloc(void** ptr, size_t nbytes);                 /* pinned host memory */
+int hv_host_free(void* ptr);
+int hv_upload_async(void* dst, const void* host_src, size_t nbytes, void* stream);
+int hv_download_async(void* host_dst, const void* src, size_t nbytes, void* stream);
+int hv_copy_async(void* dst, const void* src, size_t nbytes, void* stream);
+
+/* ---- streams, graphs, events (engine/cudrv.py:226-266) --------------------------- */
+
+int hv_stream_create(void** stream);                          /* cudrv.stream_create :226-230 */
+int hv_stream_destroy(void* stream);
+int hv_stream_synchronize(void* stream);                      /* cudrv.stream_synchronize :233-234 */
+int hv_capture_begin(void* stream);                           /* cudrv.capture_begin :237-240 */
+int hv_capture_end(void* stream, void** graph);               /* cudrv.capture_end   :243-247 */
+int hv_graph_instantiate(void* graph, void** exec);           /* cudrv.graph_instantiate :250-256 */
+int hv_graph_launch(void* exec, void* stream);                /* cudrv.graph_launch :259-261 */
+int hv_graph_destroy(void* graph, void* exec);                /* cudrv.graph_destroy :264-270 */
+int hv_event_create(void** event);
+int hv_event_destroy(void* event);
+int hv_event_record(void* event, void* stream);
+int hv_event_elapsed_ms(void* start, void* end, float* ms);
+
+/* ---- kernels: one per reference PTX entry point (engine/limited.py:173-181) ------ */
+
+/* quant_a8s (k_qa8s.ptx; launch engine/limited.py:368-369). Per-32 int8 activation
+ * quantisation of src[nb*32]: a8[nb*32] int8; sa[0..nb) f32 scales and sa[nb..2nb) the
+ * int32 block sums stored bit-for-bit in the same f32 array. */
+int hv_qa8s(const float* src, int8_t* a8, float* sa, int nb, void* stream);
+
+/* gemv_wpo_a4 (k_a4gv.ptx; launch engine/limited.py:370-372). dst[n] f32 for an
+ * int4 [n, k8*8] weight b4 (u32 [n][k8], byte-sliced nibbles) with f32 per-32 scales
+ * sw [n][k8/4], times the quantised activation (a8, sa). Bit-exact with
+ * engine/reference.py gemv_w4, including numpy's pairwise combine order. */
+int hv_a4gv(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
+            float* dst, int k8, int n, void* stream);
+
+/* The same GEMV, also writing the exact int32 block dots idot [n][k8/4]
+ * (engine/reference.py:66-69). For parity checking. */
+int hv_a4gv_idot(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
+                 float* dst, int32_t* idot, int k8, int n, void* stream);
+
+/* rmsnorm_bp (k_rmsbp.ptx; launch engine/limited.py:361-362): row-wise
+ * dst = w * (src / sqrt(mean(src^2) + eps)); rows x cols; in place allowed. The
+ * reference kernel hard-wires eps = 1e-5 (engine/reference.py:34). */
+int hv_rmsnorm(const float* src, float* dst, const float* w, int rows, int cols, float eps,
+               void* stream);
+
+/* rope_pos (k_devgen.ptx; engine/limited.py:394-397): rotate-half RoPE in place on
+ * vec [heads][2*half] at the device position *pos, tables cos/sin [cap][half]. */
+int hv_rope(float* vec, const float* cos_t, const float* sin_t, const int32_t* pos, int heads,
+            int half, void* stream);
+
+/* kvapp_pos (k_devgen.ptx; engine/limited.py:398-400): KC/VC [nkv][cap][hd] <- k, v at
+ * the device position *pos. */
+int hv_kv_append(const float* k, const float* v, float* kc, float* vc, const int32_t* pos,
+                 int nkv, int hd, int cap, void* stream);
+
+/* fda_warp_pos (k_devgen.ptx; engine/limited.py:401-404): causal decode attention of
+ * nq query heads over cache positions 0..*pos, kv head = h / group, logits scaled by
+ * *scale. Split-sequence: the library keeps a per-device scratch buffer for the partial
+ * softmax state (allocated on first use; grow it with hv_attn_reserve before a stream
+ * capture). hd must be 128. */
+int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
+                   const float* scale, const int32_t* pos, int nq, int hd, int group,
+                   int kvstride, void* stream);
+/* Makes sure the attention scratch can serve nkv heads at a cache of `cap` positions. */
+int hv_attn_reserve(int nkv, int group, int cap);
+
+/* gpu_silu_mul (k_silu.ptx; engine/limited.py:412-413): act = g * sigma(g) * up. */
+int hv_silu_mul(const float* gate, const float* up, float* act, int n, void* stream);
+
+/* vec_add (k_vadd.ptx; engine/limited.py:407-408): out = a + b. */
+int hv_vadd(const float* a, const float* b, float* out, int n, void* stream);
+
+/* gather_emb (k_devgen.ptx; engine/limited.py:384-385): h = f32(emb16[*tok]). */
+int hv_gather_emb(const uint16_t* emb16, const int32_t* tok, float* h, int hid, void* stream);
+
+/* argmax_p (k_devgen.ptx; engine/limited.py:423-425): per-part max of logits[n] into
+ * pv/pi [parts], ties to the lowest index. */
+int hv_argmax_partial(const float* logits, float* pv, int32_t* pi, int n, int parts,
+                      void* stream);
+/* argmax_f (k_devgen.ptx; engine/limited.py:426-428): final max over the parts; writes
+ * *tok, gen[*step] = tok, then ++*step and ++*pos, all on the device. */
+int hv_argmax_final(const float* pv, const int32_t* pi, int32_t* tok, int32_t* gen,
+                    int32_t* step, int32_t* pos, int parts, void* stream);
+
+/* quantize_w4 (engine/limited.py:40-58) on the device: f32 w [n][k] -> packed u32
+ * [n][k/8] and scales f32 [n][k/32], bit-exact with the host rule. */
+int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,
+                   void* stream);
+
+/* ---- the fused decode step ---------------------------------------------------------
+ *
+ * One cooperative launch performs the whole of engine/limited.py Engine._step()
+ * (:374-419) and, with HV_STEP_HEAD|HV_STEP_ARGMAX, the LM head and
+ * _argmax_into_next() (:421-428): every layer's RMSNorm, quantisation, GEMVs, q/k norm,
+ * RoPE, KV append, attention, SiLU and residual adds, then greedy argmax that advances
+ * tok/pos/step on the device. One CTA per SM; phases are separated by grid barriers
+ * whose waits are bounded (HV_E_TIMEOUT, with *status set, instead of a hang). A
+ * launch whose *pos is outside [0, cap) or *tok outside [0, vocab) does nothing but set
+ * *status = HV_E_INVALID. The host reads *status after synchronising; after a nonzero
+ * status, zero `barrier`, `ticket` and `status` before the next launch.
+ *
+ * Every pointer in these structs is a device pointer; the caller owns all buffers. The
+ * hv_step_desc itself is a host struct passed by value into the launch (capturable in a
+ * CUDA graph); its `layers` table lives in device memory. */
+
+typedef struct hv_layer_w {
+  const uint32_t* qkv_b4; const float* qkv_sw;   /* rows [q | k | v], K = hidden   */
+  const uint32_t* o_b4;   const float* o_sw;     /* hidden rows, K = n_head*hd     */
+  const uint32_t* gu_b4;  const float* gu_sw;    /* rows [gate | up], K = hidden   */
+  const uint32_t* dn_b4;  const float* dn_sw;    /* hidden rows, K = ffn           */
+  const float* an; const float* fn;              /* input / post-attention norms   */
+  const float* qn; const float* kn;              /* per-head q / k norms [hd]      */
+  float* kc; float* vc;                          /* KV cache [n_kv][cap][hd] f32   */
+} hv_layer_w;
+
+typedef struct hv_step_desc {
+  int n_layer, hidden, ffn, n_head, n_kv, head_dim, head_rows, cap;
+  float eps, attn_scale;
+  int attn_chunks;              /* chunks per kv head (hv_step_config)            */
+  int vocab;                    /* embedding rows: *tok must lie in [0, vocab)     */
+  const hv_layer_w* layers;     /* [n_layer]                                       */
+  const uint16_t* emb16;        /* [vocab][hidden] f16                             */
+  const float* onorm;           /* final norm [hidden]                             */
+  const uint32_t* head_b4; const float* head_sw;   /* LM head [head_rows][hidden] */
+  const float* cos_t; const float* sin_t;          /* RoPE tables [cap][hd/2]      */
+  int32_t* tok; int32_t* pos; int32_t* step;      /* device scalars                  */
+  int32_t* gen;                 /* generated tokens [cap + 1]                      */
+  float* h;                     /* residual [hidden]                               */
+  float* qkv;                   /* [(n_head + 2 n_kv) hd]                          */
+  float* ctx;                   /* [n_head hd]                                     */
+  float* act;                   /* SiLU output [ffn]                               */
+  float* logits;                /* [head_rows]                                     */
+  float* part;                  /* attention partials (hv_step_config)             */
+  int32_t* ticket;              /* [n_kv + 1] zeroed once                          */
+  float* amax_v; int32_t* amax_i;                  /* [grid] argmax partials       */
+  uint32_t* barrier;            /* one word, zeroed once                           */
+  int32_t* status;              /* 0 = ok; nonzero after a bounded wait ran out    */
+} hv_step_desc;
+
+#define HV_STEP_HEAD 1     /* compute the LM head into logits                          */
+#define HV_STEP_ARGMAX 2   /* then greedy argmax: tok = argmax, gen[step] = tok,
+                              ++step, ++pos (engine/limited.py:421-428)               */
+
+/* Launch geometry of the fused step on the current device, and the sizes of the
+ * scratch it needs: `part_floats` floats for hv_step_desc.part, `chunks` for
+ * attn_chunks, `grid` entries for amax_v / amax_i. */
+int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t* smem,
+                   int* chunks, size_t* part_floats);
+
+/* One fused decode step. `desc` is a host pointer to a filled hv_step_desc. */
+int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIVE_B200_H */

@@ -1,0 +1,112 @@
+"""CPU-side checks of the native library and the host logic (no GPU calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "hive_b200.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\bint\s+(hv_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build
+    path = build.build()
+    return ctypes.CDLL(str(path))
+
+
+def test_library_exports_every_header_symbol(lib):
+    syms = header_symbols()
+    assert len(syms) > 40
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    import hvdrv
+    assert set(header_symbols()) == set(hvdrv.exported_symbols())
+
+
+def test_library_version_and_kernels(lib):
+    import hvdrv
+    hvdrv.load()
+    assert hvdrv.load().hv_version() == hvdrv.ABI_VERSION
+    ks = hvdrv.kernel_list()
+    for k in ("k_a4gv", "k_qa8s", "k_rmsnorm", "k_attn", "k_step", "k_argmax_p"):
+        assert k in ks
+
+
+def test_errors_are_reported_not_fatal(lib):
+    """Argument checks fail with a status and a message; nothing aborts the process."""
+    import hvdrv
+    with pytest.raises(hvdrv.CudaError) as e:
+        hvdrv.a4gv(0, 0, 0, 0, 0, 8, 16)
+    assert "bad arguments" in str(e.value)
+    with pytest.raises(hvdrv.CudaError) as e:
+        hvdrv.rmsnorm(0, 0, 0, 1, 128)
+    assert e.value.code == 1001
+
+
+def test_manifest_matches_library():
+    import hashlib
+    import json
+
+    import build
+    build.build()
+    man = json.loads(build.MANIFEST.read_text())
+    assert man["sha256"] == hashlib.sha256(build.LIB.read_bytes()).hexdigest()
+    assert man["arch"] == "sm_100a"
+
+
+def test_step_desc_layout_matches_header():
+    """The ctypes mirror of hv_step_desc / hv_layer_w has the C layout."""
+    import limited
+    assert ctypes.sizeof(limited._LayerW) == 14 * 8
+    # 8 ints + 2 floats + 2 ints = 48 bytes, then 22 pointers
+    assert limited._StepDesc.layers.offset == 48
+    assert ctypes.sizeof(limited._StepDesc) == 48 + 22 * 8
+
+
+def test_gpu_only_paths_fail_loudly_without_gpu():
+    """No CPU fallback: constructing an engine needs the GPU."""
+    import hvdrv
+    try:
+        n = hvdrv.device_count()
+    except hvdrv.CudaError:
+        n = 0
+    if n:
+        pytest.skip("a GPU is visible")
+    import limited
+    import synth
+    with pytest.raises((hvdrv.CudaError, RuntimeError)):
+        limited.Engine(config=synth.tiny_arch(), tensors={})
+
+
+def test_host_quantizer_matches_oracle():
+    import hv_oracle
+    import w4format
+    w = (np.random.default_rng(0).standard_normal((33, 96)) * 0.02).astype(np.float32)
+    a = w4format.quantize_w4(w)
+    b = hv_oracle.quantize_w4(w)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    back = w4format.dequantize_w4(a[0], a[1], 96)
+    assert np.abs(back - w).max() <= np.abs(w).max() / 7 / 2 * 1.0001
+
+
+def test_synthetic_draw_is_deterministic_and_thread_independent():
+    import synth
+    import w4format
+    cfg = w4format.Config(synth.tiny_arch())
+    a = dict(synth.iter_tensors(cfg, 5, threads=1))
+    b = dict(synth.iter_tensors(cfg, 5, threads=4))
+    assert list(a) == [n for n, _, _ in synth.tensor_plan(cfg)]
+    for k in a:
+        assert np.array_equal(a[k], b[k])

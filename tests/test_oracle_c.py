@@ -1,0 +1,77 @@
+"""Pin the C restatement of the GEMV to the numpy oracle and the reference's goldens."""
+import numpy as np
+import pytest
+
+import hv_oracle as O
+
+F32 = np.float32
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_c_gemv_matches_reference_golden(golden, i):
+    g = golden("ops.npz")
+    a, p, sc = g[f"gv{i}_a"], g[f"gv{i}_packed"], g[f"gv{i}_scale"]
+    qa, sa, _ = O.quantize_act(a)
+    idot, y = O.gemv_q_c(qa, sa, p, sc, a.size, want_idot=True)
+    assert np.array_equal(idot, g[f"gv{i}_idot"])
+    assert np.array_equal(y.view(np.uint32), g[f"gv{i}_y"].view(np.uint32))
+
+
+@pytest.mark.parametrize("n,k", [(37, 32), (5, 224), (16, 2048), (9, 5120), (4, 12288),
+                                 (3, 25600), (7, 32 * 1000)])
+def test_c_gemv_matches_numpy_oracle(n, k):
+    g = np.random.default_rng(n * 7 + k)
+    p, sc = O.quantize_w4((g.standard_normal((n, k)) * 0.02).astype(F32))
+    a = g.standard_normal(k).astype(F32) * F32(3.0)
+    qa, sa, _ = O.quantize_act(a)
+    i1, y1 = O.gemv_q(qa, sa, p, sc, k)
+    i2, y2 = O.gemv_q_c(qa, sa, p, sc, k, want_idot=True)
+    assert np.array_equal(i1, i2)
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+
+
+def test_c_pairwise_sum_is_numpys():
+    import ctypes
+    lib = O._clib()
+    for n in (1, 7, 8, 100, 129, 800, 4096, 5120, 25600):
+        x = (np.random.default_rng(n).standard_normal(n) * 10).astype(F32)
+        got = lib.hvo_pairwise_sum(x.ctypes.data, n)
+        assert np.float32(got).view(np.uint32) == x.sum().view(np.uint32)
+
+
+def test_fast_oracle_model_matches_reference_decode(golden):
+    import synth
+    import w4format
+    g = golden("decode_tiny.npz")
+    cfg = w4format.Config(synth.tiny_arch())
+    w = O.quantize_model(cfg, synth.model_tensors(cfg, 7))
+    m = O.FastOracleModel(cfg, w, 5 + 12 + 2)
+    toks, logits = m.generate(g["prompt"].tolist(), 12)
+    assert toks == g["tokens"].tolist()
+    assert np.array_equal(np.stack(logits).view(np.uint32), g["logits"].view(np.uint32))
+
+
+def test_c_quantizer_matches_reference(golden):
+    g = golden("ops.npz")
+    p, s = O.quantize_w4_c(g["qw_in"])
+    assert np.array_equal(p, g["qw_packed"])
+    assert np.array_equal(s.view(np.uint32), g["qw_scale"].view(np.uint32))
+    w = (np.random.default_rng(9).standard_normal((70, 4096)) * 0.02).astype(F32)
+    p1, s1 = O.quantize_w4(w)
+    p2, s2 = O.quantize_w4_c(w)
+    assert np.array_equal(p1, p2) and np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
+
+
+def test_quantize_model_c_matches_numpy():
+    import synth
+    import w4format
+    for arch in (synth.tiny_arch(), synth.tiny_arch(tied=True)):
+        cfg = w4format.Config(arch)
+        a = O.quantize_model(cfg, synth.model_tensors(cfg, 3))
+        b = O.quantize_model_c(cfg, synth.iter_tensors(cfg, 3))
+        assert sorted(a) == sorted(b)
+        for key in a:
+            if isinstance(a[key], tuple):
+                assert all(np.array_equal(x, y) for x, y in zip(a[key], b[key])), key
+            else:
+                assert np.array_equal(a[key], b[key]), key
