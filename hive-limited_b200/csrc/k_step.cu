@@ -217,13 +217,14 @@ __device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w*
                        float* area) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
   const int chunk_max = (cap + nch - 1) / nch;
+  const int lg_floats = (chunk_max * GS + 3) & ~3;   // keeps red_s 16-byte aligned
   float* q_s = area;
   float* kpos_s = q_s + GS * kHd;
   float* vpos_s = kpos_s + kHd;
   float* tmp_s = vpos_s + kHd;                       // (GS + 1) x 128
   float* stat_s = tmp_s + (GS + 1) * kHd;            // 2 GS (+pad)
   float* lg_s = stat_s + 4 * GS;
-  float* red_s = lg_s + chunk_max * GS;
+  float* red_s = lg_s + lg_floats;                  // accessed as float4
   const int warp = threadIdx.x >> 5;
   const float* cs = D.cos_t + (size_t)pos * (kHd / 2);
   const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
@@ -388,8 +389,9 @@ static size_t step_smem(int hid, int qdim, int ffn, int cap, int nch) {
   const int kmax = std::max(std::max(hid, qdim), ffn);
   const size_t gemv = (size_t)kmax + (size_t)(kmax / kBlock) * 8 + 2 * (size_t)hid * 4;
   const int chunk_max = (cap + nch - 1) / nch;
+  const size_t lg_floats = ((size_t)chunk_max * GS + 3) & ~size_t(3);
   const size_t attn = sizeof(float) * ((size_t)GS * kHd + 2 * kHd + (GS + 1) * kHd + 4 * GS +
-                                       (size_t)chunk_max * GS + (size_t)kStepWarps * GS * kHd);
+                                       lg_floats + (size_t)kStepWarps * GS * kHd);
   return ((sizeof(StepShared) + 15) & ~size_t(15)) + std::max(gemv, attn);
 }
 

@@ -127,6 +127,14 @@ def test_qwen3_1p7b_shape_matches_reference(hv, golden):
         eng.free()
 
 
+# Logits of a full decode can only be compared to the reference within the model's own
+# sensitivity: in the oracle, perturbing np.exp by one ulp in 10% of its calls moves the
+# 8B-shape step-0 logits by 2.9e-2 of their scale (an int8 activation rounding flips and
+# the change propagates through 36 layers). Tokens must agree exactly; logits within
+# 0.1 of the logit scale; op-level bit-exactness is checked layer by layer below.
+LARGE_LOGIT_TOL = 0.1
+
+
 @pytest.mark.parametrize("arch_name,seed", [
     ("qwen3-8b", 2),
     pytest.param("qwen3-32b", 3, marks=pytest.mark.skipif(
@@ -134,7 +142,8 @@ def test_qwen3_1p7b_shape_matches_reference(hv, golden):
 ])
 def test_large_shapes_match_oracle(hv, arch_name, seed):
     """8B/32B geometry, 4-token prompt + 3 greedy tokens, against the C oracle run on the
-    engine's own quantised weights (the quantiser is checked bit-exact separately)."""
+    engine's own quantised weights (the quantiser is checked bit-exact separately); and
+    the fused one-launch step bit-identical to the eager kernel sequence at full size."""
     import hvdrv
     arch = synth.ARCH[arch_name]
     eng = make_engine(arch, seed, 16)
@@ -149,7 +158,97 @@ def test_large_shapes_match_oracle(hv, arch_name, seed):
         err = rel_err(lg, want_logits[0])
         print(f"{arch_name}: tokens {toks} vs {want_toks}; step-0 logits rel err {err:.2e}")
         assert toks == want_toks
-        assert err < 1e-4
+        assert err < LARGE_LOGIT_TOL
+        eng.fused = False
+        lg_eager = eng.logits(prompt)
+        eng.fused = True
+        assert np.array_equal(bits(lg), bits(lg_eager))
+    finally:
+        eng.free()
+
+
+def test_layer_ops_bit_exact_at_8b_shape(hv):
+    """One decoder layer of the 8B-shape model (layers 0, 17 and 35) at position 77, with
+    a seeded KV history. Each op is fed the oracle's input, so every op that the
+    reference fixes bit for bit is compared bit for bit at the real shapes: RMSNorm +
+    quant + qkv GEMV, q/k norm, RoPE, KV append, o GEMV, residual, gate/up GEMV, down
+    GEMV; attention and SiLU (exp) are held to tolerances."""
+    import hvdrv
+    from gpu_util import Dev
+    arch = synth.ARCH["qwen3-8b"]
+    eng = make_engine(arch, 2, 128)
+    c = eng.cfg
+    qd, nq, nkv, hid, ffn = c.head_dim, c.n_head, c.n_kv, c.hidden, c.ffn
+    pos = 77
+    try:
+        w = download_weights(eng, hvdrv)
+        cos_t, sin_t = O.rope_tables(128, qd, c.rope_theta)
+        g = np.random.default_rng(123)
+        dpos = Dev(np.array([pos], np.int32))
+        scale = Dev(np.array([1.0 / np.sqrt(qd)], F32))
+
+        def run_gemv(name, x):
+            packed, sc, k = w[name]
+            b4, sw, _, n = eng.layers[L][name.split(".")[1]] if name != "head" else eng.head
+            xd = Dev(x)
+            y = Dev(nbytes=n * 4)
+            hvdrv.qa8s(xd, eng.d_a8, eng.d_sa, k // 32)
+            hvdrv.a4gv(eng.d_a8, eng.d_sa, b4, sw, y, k // 8, n)
+            return y.get(F32)
+
+        for L in (0, 17, 35):
+            h = (g.standard_normal(hid) * 3).astype(F32)
+            kc = g.standard_normal((nkv, 128, qd)).astype(F32)
+            vc = g.standard_normal((nkv, 128, qd)).astype(F32)
+            hvdrv.upload(eng.KC[L], kc.ctypes.data, kc.nbytes)
+            hvdrv.upload(eng.VC[L], vc.ctypes.data, vc.nbytes)
+            # oracle
+            hn = O.rmsnorm(h, w[f"{L}.an"])
+            qkv = O.gemv_w4_c(hn, *w[f"{L}.qkv"])
+            q = O.rope(O.rmsnorm(qkv[:nq * qd].reshape(nq, qd), w[f"{L}.qn"]), pos, cos_t, sin_t)
+            k = O.rope(O.rmsnorm(qkv[nq * qd:(nq + nkv) * qd].reshape(nkv, qd), w[f"{L}.kn"]),
+                       pos, cos_t, sin_t)
+            v = qkv[(nq + nkv) * qd:].reshape(nkv, qd)
+            kc[:, pos], vc[:, pos] = k, v
+            ctx = O.attention(q, kc, vc, pos, c.group, 1.0 / np.sqrt(qd)).reshape(-1)
+            h2 = (h + O.gemv_w4_c(ctx, *w[f"{L}.o"])).astype(F32)
+            gu = O.gemv_w4_c(O.rmsnorm(h2, w[f"{L}.fn"]), *w[f"{L}.gu"])
+            act = O.silu_mul(gu[:ffn], gu[ffn:])
+            h3 = (h2 + O.gemv_w4_c(act, *w[f"{L}.down"])).astype(F32)
+            # GPU, op by op
+            hd_ = Dev(h)
+            hn_d = Dev(nbytes=hid * 4)
+            hvdrv.rmsnorm(hd_, hn_d, eng.layers[L]["an"], 1, hid, 1e-5)
+            assert np.array_equal(bits(hn_d.get(F32)), bits(hn))
+            qkv_g = run_gemv(f"{L}.qkv", hn)
+            assert np.array_equal(bits(qkv_g), bits(qkv)), L
+            qkv_d = Dev(qkv)
+            dq, dk = qkv_d.ptr, qkv_d.ptr + nq * qd * 4
+            dv = qkv_d.ptr + (nq + nkv) * qd * 4
+            hvdrv.rmsnorm(dq, dq, eng.layers[L]["qn"], nq, qd, 1e-5)
+            hvdrv.rmsnorm(dk, dk, eng.layers[L]["kn"], nkv, qd, 1e-5)
+            hvdrv.rope(dq, eng.d_cos, eng.d_sin, dpos, nq, qd // 2)
+            hvdrv.rope(dk, eng.d_cos, eng.d_sin, dpos, nkv, qd // 2)
+            got = qkv_d.get(F32)
+            assert np.array_equal(bits(got[:nq * qd]), bits(q.reshape(-1)))
+            assert np.array_equal(bits(got[nq * qd:(nq + nkv) * qd]), bits(k.reshape(-1)))
+            hvdrv.kv_append(dk, dv, eng.KC[L], eng.VC[L], dpos, nkv, qd, c.max_context)
+            ctx_d = Dev(nbytes=nq * qd * 4)
+            hvdrv.attn_decode(dq, eng.KC[L], eng.VC[L], ctx_d, scale, dpos, nq, qd, c.group,
+                              c.max_context * qd)
+            np.testing.assert_allclose(ctx_d.get(F32), ctx, rtol=1e-4, atol=1e-6)
+            o_g = run_gemv(f"{L}.o", ctx)
+            assert np.array_equal(bits((h + o_g).astype(F32)), bits(h2))
+            gu_g = run_gemv(f"{L}.gu", O.rmsnorm(h2, w[f"{L}.fn"]))
+            assert np.array_equal(bits(gu_g), bits(gu))
+            act_d = Dev(nbytes=ffn * 4)
+            gud = Dev(gu_g)
+            hvdrv.silu_mul(gud.ptr, gud.ptr + ffn * 4, act_d, ffn)
+            sc = np.abs(gu[:ffn].astype(np.float64) * gu[ffn:])
+            assert np.all(np.abs(act_d.get(F32) - act) <= 2.0 ** -21 * sc + 1e-37)
+            dn_g = run_gemv(f"{L}.down", act)
+            assert np.array_equal(bits((h2 + dn_g).astype(F32)), bits(h3))
+            print(f"layer {L}: every restatable op bit-exact at the 8B shape")
     finally:
         eng.free()
 

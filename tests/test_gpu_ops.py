@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import hv_oracle as O
-from gpu_util import Dev, bits, quantize_on_device, ulp_diff
+from gpu_util import Dev, bits, quantize_on_device
 
 pytestmark = pytest.mark.gpu
 F32 = np.float32
@@ -102,17 +102,22 @@ def test_rope_bit_exact(hv, golden, i):
     assert np.array_equal(bits(vec.get(F32, v.shape)), bits(g[f"rp{i}_y"]))
 
 
-def test_silu_within_4_ulp(hv, golden):
-    """np.exp and CUDA's expf differ in the last bit now and then; the SiLU built on them
-    stays within 4 ulp of the reference (measured max printed)."""
+def test_silu_within_exp_rounding(hv, golden):
+    """np.exp and CUDA's expf differ in the last bit now and then. In the reference's
+    sign-split form sigma = 0.5 (1 + (1 - e) / (1 + e)), one ulp of e moves sigma by at
+    most ~2^-24 absolute (1 - e cancels near g = 0, so ulps of the output are the wrong
+    yardstick). Bound: |got - want| <= 2^-21 |g u| + 1e-37."""
     g = golden("ops.npz")
     gt, up, want = g["silu_g"], g["silu_u"], g["silu_y"]
     out = Dev(nbytes=gt.nbytes)
     hv.silu_mul(Dev(gt), Dev(up), out, gt.size)
     got = out.get(F32)
-    d = ulp_diff(got, want)
-    print(f"silu max ulp diff vs reference: {d}")
-    assert d <= 4
+    scale = np.abs(gt.astype(np.float64) * up)
+    err = np.abs(got.astype(np.float64) - want)
+    worst = float((err / np.maximum(scale, 1e-30)).max())
+    print(f"silu: max |diff| / |g u| = {worst:.2e}; exact in "
+          f"{np.mean(got.view(np.uint32) == want.view(np.uint32)):.1%} of values")
+    assert np.all(err <= 2.0 ** -21 * scale + 1e-37)
 
 
 def test_vadd_gather_kvapp_exact(hv):
