@@ -185,22 +185,46 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
 }
 
 // Merge the nch chunk states of one kv head into ctx rows [GS][128]. Reads the
-// partials through L2 (they were written by other CTAs).
+// partials through L2 (they were written by other CTAs): first every chunk's (m, l) in
+// parallel, then per head the global max and weights, then each output element sums
+// its chunks with all loads of a batch in flight. `w_s` is shared scratch of
+// 2 * nch * GS + GS floats. Block-cooperative.
 template <int GS>
-HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx) {
+HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx, float* w_s) {
+  float* l_s = w_s + nch * GS;                    // l of (c, i)
+  float* inv_s = l_s + nch * GS;                  // 1 / L per head
+  for (int e = threadIdx.x; e < nch * GS; e += blockDim.x) {
+    w_s[e] = __ldcg(part_head + (size_t)e * kPartStride);          // m of (c, i)
+    l_s[e] = __ldcg(part_head + (size_t)e * kPartStride + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < GS) {
+    const int i = threadIdx.x;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, w_s[c * GS + i]);
+    float L = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      const float w = expf(w_s[c * GS + i] - M);
+      L = fmaf(w, l_s[c * GS + i], L);
+      w_s[c * GS + i] = w;
+    }
+    inv_s[i] = 1.0f / L;
+  }
+  __syncthreads();
   for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) {
     const int i = e / kHd, d = e % kHd;
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c)
-      M = fmaxf(M, __ldcg(part_head + ((size_t)c * GS + i) * kPartStride));
-    float L = 0.f, o = 0.f;
-    for (int c = 0; c < nch; ++c) {
-      const float* pc = part_head + ((size_t)c * GS + i) * kPartStride;
-      const float w = expf(__ldcg(pc) - M);
-      L = fmaf(w, __ldcg(pc + 1), L);
-      o = fmaf(w, __ldcg(pc + 4 + d), o);
+    float o = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+      float a[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        a[k] = (c0 + k < nch)
+                   ? __ldcg(part_head + ((size_t)(c0 + k) * GS + i) * kPartStride + 4 + d) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (c0 + k < nch) o = fmaf(w_s[(c0 + k) * GS + i], a[k], o);
     }
-    ctx[i * kHd + d] = o / L;
+    ctx[i * kHd + d] = o * inv_s[i];
   }
 }
 

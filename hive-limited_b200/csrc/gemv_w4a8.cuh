@@ -30,8 +30,9 @@ struct GvPlan {
   unsigned char pops[kGvMaxLeaf];   // '+' of the recursion closing after leaf L
 };
 
-// numpy's pairwise recursion over nb block terms, as iteration boundaries (one thread).
-HV_DEV bool gv_make_plan(int nb, GvPlan* g) {
+// numpy's pairwise recursion over nb block terms, as iteration boundaries. Runs on the
+// host so kernels receive a finished plan.
+HV_HD bool gv_make_plan(int nb, GvPlan* g) {
   int sk[64], ss[64], sm[64];
   int sp = 1, nl = 0;
   sk[0] = 0; ss[0] = 0; sm[0] = nb;

@@ -23,9 +23,15 @@ int cuda_fail(const char* what, cudaError_t e) {
 }
 
 int sm_count(int* out) {
+  static int cache[64];
   int dev = 0;
   HV_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *out = cache[dev];
+    return HV_OK;
+  }
   HV_CUDA(cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev));
+  if (dev >= 0 && dev < 64) cache[dev] = *out;
   return HV_OK;
 }
 

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #define HV_DEV __device__ __forceinline__
+#define HV_HD __host__ __device__ inline
 
 namespace hv {
 
@@ -35,8 +36,9 @@ struct PwPlan {
   unsigned char pops[kPwMaxLeaf];
 };
 
-// Builds the plan for n values (one thread). Returns false if it does not fit.
-HV_DEV bool pw_make_plan(int n, PwPlan* p) {
+// Builds the plan for n values. Returns false if it does not fit. Runs on the host so
+// kernels receive a finished plan.
+HV_HD bool pw_make_plan(int n, PwPlan* p) {
   // explicit DFS stack: kind 0 = node (s, m), kind 1 = '+'
   int sk[64], ss[64], sm[64];
   int sp = 0, nl = 0;
@@ -215,6 +217,37 @@ HV_DEV void prefetch_l2(const void* p, size_t bytes) {
     a0 += chunk;
     n -= chunk;
   }
+}
+
+// Per-32 quantisation with 8 lanes per block: lane (b = lane / 8, sub = lane % 8) holds
+// v = values 4 sub .. 4 sub + 3 of block b. Same arithmetic as quant_block_warp (the
+// max and the block sum are exact, so the grouping does not change any bit). Returns the
+// four int8 values packed little-endian; lanes with sub == 0 receive the scale and sum.
+HV_DEV unsigned quant_block_8lanes(float4 v, float* s_out, int* bsum_out) {
+  const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+  float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  mx = fmaxf(mx, __shfl_xor_sync(gmask, mx, 1, 8));
+  mx = fmaxf(mx, __shfl_xor_sync(gmask, mx, 2, 8));
+  mx = fmaxf(mx, __shfl_xor_sync(gmask, mx, 4, 8));
+  float s = __fdiv_rn(mx, 127.0f);
+  if (s == 0.0f) s = 1.0f;
+  const float a[4] = {v.x, v.y, v.z, v.w};
+  unsigned packed = 0;
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float half = (a[i] < 0.0f) ? -0.5f : 0.5f;
+    int q = (int)truncf(__fadd_rn(__fdiv_rn(a[i], s), half));
+    q = q > 127 ? 127 : (q < -127 ? -127 : q);
+    sum += q;
+    packed |= ((unsigned)q & 0xFFu) << (8 * i);
+  }
+  sum += __shfl_xor_sync(gmask, sum, 1, 8);
+  sum += __shfl_xor_sync(gmask, sum, 2, 8);
+  sum += __shfl_xor_sync(gmask, sum, 4, 8);
+  *s_out = s;
+  *bsum_out = sum;
+  return packed;
 }
 
 // ---------------------------------------------------------------------------

@@ -7,10 +7,30 @@
 #include <cuda_fp16.h>
 
 #include "attn_decode.cuh"
-#include "gemv_w4a8.cuh"
+#include "gemv_mma.cuh"
 #include "hv_internal.h"
 
 namespace hv {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
+static std::mutex g_attr_mu;
+static int smem_attr(const void* fn, size_t bytes) {
+  static const void* fns[64];
+  static size_t done[64][16];
+  int dev = 0;
+  HV_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  int slot = -1;
+  for (int i = 0; i < 64; ++i) {
+    if (fns[i] == fn) { slot = i; break; }
+    if (!fns[i]) { fns[i] = fn; slot = i; break; }
+  }
+  if (slot < 0 || dev >= 16 || done[slot][dev] < bytes) {
+    HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    if (slot >= 0 && dev < 16) done[slot][dev] = bytes;
+  }
+  return HV_OK;
+}
 
 // ---------------------------------------------------------------------------
 // quant_a8s: one warp per 32-block
@@ -41,13 +61,13 @@ __global__ void __launch_bounds__(256) k_a4gv(const int8_t* __restrict__ a8,
                                               const uint32_t* __restrict__ b4,
                                               const float* __restrict__ sw,
                                               float* __restrict__ dst,
-                                              int32_t* __restrict__ idot, int nb, int n) {
+                                              int32_t* __restrict__ idot, int n,
+                                              const __grid_constant__ GvPlan plan) {
   extern __shared__ __align__(16) unsigned char smem[];
+  const int nb = plan.nb;
   uint4* q_s = reinterpret_cast<uint4*>(smem);
   int2* sb_s = reinterpret_cast<int2*>(smem + (size_t)nb * 32);
-  GvPlan* plan = reinterpret_cast<GvPlan*>(smem + (size_t)nb * 40);
   load_act_smem(a8, sa, nb, q_s, sb_s);
-  if (threadIdx.x == 0) gv_make_plan(nb, plan);
   __syncthreads();
   const ActView act{q_s, sb_s};
   const int lane = threadIdx.x & 31;
@@ -56,8 +76,109 @@ __global__ void __launch_bounds__(256) k_a4gv(const int8_t* __restrict__ a8,
   for (int q = blockIdx.x * wpb + (threadIdx.x >> 5); q < nquads; q += gridDim.x * wpb) {
     const int row = q * 4 + (lane >> 3);
     const bool ok = row < n;
-    const float y = gemv_rows4<8, kIdot>(b4, sw, row, ok, act, *plan, idot);
+    const float y = gemv_rows4<8, kIdot>(b4, sw, row, ok, act, plan, idot);
     if (ok && (lane & 7) == 0) dst[row] = y;
+  }
+}
+
+// gemv_wpo_a4 on the tensor pipe: one warp per 8-row tile
+__global__ void __launch_bounds__(256) k_a4gv_mma(const int8_t* __restrict__ a8,
+                                                  const float* __restrict__ sa,
+                                                  const uint32_t* __restrict__ b4,
+                                                  const float* __restrict__ sw,
+                                                  float* __restrict__ dst, int n,
+                                                  const __grid_constant__ GvPlan plan) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int nb = plan.nb;
+  uint4* q_s = reinterpret_cast<uint4*>(smem);
+  int2* sb_s = reinterpret_cast<int2*>(smem + (size_t)nb * 32);
+  load_act_smem(a8, sa, nb, q_s, sb_s);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int ntile = (n + 7) / 8;
+  const int wpb = blockDim.x >> 5;
+  for (int tile = blockIdx.x * wpb + (threadIdx.x >> 5); tile < ntile; tile += gridDim.x * wpb) {
+    const int row = tile * 8 + g;
+    const bool ok = row < n;
+    const int lr = ok ? row : 0;
+    float y;
+    gemv_tile8<6, true>(b4 + (size_t)lr * nb * 4, sw + (size_t)lr * nb,
+                        reinterpret_cast<const unsigned*>(q_s), sb_s, plan, 0, plan.nleaf, &y,
+                        nullptr);
+    if (t == 0 && ok) dst[row] = y;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tile-interleaved weight layout (see gemv_mma.cuh) and the GEMV over it
+// ---------------------------------------------------------------------------
+
+// Row of the reference matrix behind quad g of `tile`: plain 8-row tiles, or (pair_ffn
+// > 0) 4 gate rows p and their 4 up rows ffn + p of a [gate | up] matrix.
+HV_DEV int pp_row(int tile, int g, int rows, int pair_ffn, bool* ok) {
+  if (pair_ffn > 0) {
+    const int p = tile * 4 + (g & 3);
+    *ok = p < pair_ffn;
+    return (g < 4) ? p : pair_ffn + p;
+  }
+  const int row = tile * 8 + g;
+  *ok = row < rows;
+  return row;
+}
+
+// one thread per (tile, iteration, lane): 8 nibble words and 2 scales
+__global__ void k_w4_prepack(const uint32_t* __restrict__ b4, const float* __restrict__ sw,
+                             int rows, int nb, int pair_ffn, int ntile, int niter,
+                             uint32_t* __restrict__ pb4, float* __restrict__ psw) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)ntile * niter * 32) return;
+  const int lane = (int)(idx & 31);
+  const long long rest = idx >> 5;
+  const int it = (int)(rest % niter), tile = (int)(rest / niter);
+  const int g = lane >> 2, t = lane & 3;
+  bool ok;
+  const int row = pp_row(tile, g, rows, pair_ffn, &ok);
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int blk = it * 8 + j;
+    w[j] = (ok && blk < nb) ? b4[((size_t)row * nb + blk) * 4 + t] : 0u;
+  }
+  uint32_t* dn = pb4 + ((size_t)tile * niter + it) * kPpNibWords;
+  reinterpret_cast<uint4*>(dn)[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(dn + 128)[lane] = make_uint4(w[4], w[5], w[6], w[7]);
+  const int b0 = it * 8 + 2 * t;
+  float* ds = psw + ((size_t)tile * niter + it) * kPpScales;
+  ds[2 * lane] = (ok && b0 < nb) ? sw[(size_t)row * nb + b0] : 0.f;
+  ds[2 * lane + 1] = (ok && b0 + 1 < nb) ? sw[(size_t)row * nb + b0 + 1] : 0.f;
+}
+
+// GEMV over the tile-interleaved layout, one warp per tile; with pair_ffn > 0 the output
+// keeps the reference order [gate | up].
+__global__ void __launch_bounds__(256) k_a4gv_pp(const int8_t* __restrict__ a8,
+                                                 const float* __restrict__ sa,
+                                                 const uint32_t* __restrict__ pb4,
+                                                 const float* __restrict__ psw,
+                                                 float* __restrict__ dst, int rows, int pair_ffn,
+                                                 const __grid_constant__ GvPlan plan) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int nb = plan.nb;
+  uint4* q_s = reinterpret_cast<uint4*>(smem);
+  int2* sb_s = reinterpret_cast<int2*>(smem + (size_t)nb * 32);
+  load_act_smem(a8, sa, nb, q_s, sb_s);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int ntile = pp_tiles(rows, pair_ffn), niter = pp_iters(nb);
+  const int wpb = blockDim.x >> 5;
+  for (int tile = blockIdx.x * wpb + (threadIdx.x >> 5); tile < ntile; tile += gridDim.x * wpb) {
+    bool ok;
+    const int row = pp_row(tile, g, rows, pair_ffn, &ok);
+    float y;
+    gemv_tile8<8, true, true>(pb4 + (size_t)tile * niter * kPpNibWords,
+                              psw + (size_t)tile * niter * kPpScales,
+                              reinterpret_cast<const unsigned*>(q_s), sb_s, plan, 0, plan.nleaf,
+                              &y, nullptr);
+    if (t == 0 && ok) dst[row] = y;
   }
 }
 
@@ -67,10 +188,9 @@ __global__ void __launch_bounds__(256) k_a4gv(const int8_t* __restrict__ a8,
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ src,
                                                  float* __restrict__ dst,
                                                  const float* __restrict__ w, int cols,
-                                                 float eps) {
+                                                 float eps, const __grid_constant__ PwPlan plan) {
   extern __shared__ __align__(16) unsigned char smem[];
-  PwPlan* plan = reinterpret_cast<PwPlan*>(smem);
-  float* leafval = reinterpret_cast<float*>(smem + sizeof(PwPlan));
+  float* leafval = reinterpret_cast<float*>(smem);
   float* red = leafval + kPwMaxLeaf;
   float* x = red + 4;
   float* sq = x + cols;
@@ -80,9 +200,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ src,
     x[i] = v;
     sq[i] = __fmul_rn(v, v);
   }
-  if (threadIdx.x == 0) pw_make_plan(cols, plan);
   __syncthreads();
-  const float ss = block_pw_sum(sq, plan, leafval, red);
+  const float ss = block_pw_sum(sq, &plan, leafval, red);
   const float ms = __fdiv_rn(ss, (float)cols);
   const float d = __fsqrt_rn(__fadd_rn(ms, eps));
   float* out = dst + (size_t)blockIdx.x * cols;
@@ -267,7 +386,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
   __syncthreads();
   if (!last) return;
   __threadfence();
-  attn_merge<GS>(part + (size_t)g * nch * GS * kPartStride, nch, ctx + (size_t)g * GS * kHd);
+  attn_merge<GS>(part + (size_t)g * nch * GS * kPartStride, nch, ctx + (size_t)g * GS * kHd,
+                 red_s);
   if (threadIdx.x == 0) ticket[g] = 0;
 }
 
@@ -327,8 +447,8 @@ static int launch_attn(const float* q, const float* kc, const float* vc, float* 
                        const float* scale, const int32_t* pos, int nkv, int cap, int nch,
                        AttnScratch* s, cudaStream_t st) {
   const size_t smem = attn_smem_bytes<GS>(kAttnThreads / 32);
-  HV_CUDA(cudaFuncSetAttribute(k_attn<GS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
+  const int rc = smem_attr((const void*)k_attn<GS>, smem);
+  if (rc) return rc;
   k_attn<GS><<<nkv * nch, kAttnThreads, smem, st>>>(q, kc, vc, ctx, scale, pos, cap, nch,
                                                     s->part, s->ticket);
   HV_LAUNCHED("k_attn");
@@ -342,7 +462,7 @@ extern "C" {
 
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
-      "k_qa8s,k_a4gv,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
+      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
       "k_argmax_p,k_argmax_f,k_quantize_w4,k_step";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
@@ -365,7 +485,9 @@ static int a4gv_launch(const int8_t* a8, const float* sa, const uint32_t* b4, co
              "hv_a4gv: a8 and b4 must be 16-byte aligned");
   const int nb = k8 / 4;
   HV_REQUIRE(nb <= 4096, HV_E_UNSUPPORTED, "hv_a4gv: K = %d exceeds 131072", k8 * 8);
-  const size_t smem = (size_t)nb * 40 + sizeof(GvPlan);
+  const size_t smem = (size_t)nb * 40;
+  GvPlan plan;
+  HV_REQUIRE(gv_make_plan(nb, &plan), HV_E_UNSUPPORTED, "hv_a4gv: no reduction plan for K");
   int sms = 0;
   int rc = sm_count(&sms);
   if (rc) return rc;
@@ -374,13 +496,16 @@ static int a4gv_launch(const int8_t* a8, const float* sa, const uint32_t* b4, co
   if (grid > sms * 8) grid = sms * 8;
   cudaStream_t st = (cudaStream_t)stream;
   if (idot) {
-    HV_CUDA(cudaFuncSetAttribute(k_a4gv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    k_a4gv<true><<<grid, 256, smem, st>>>(a8, sa, b4, sw, dst, idot, nb, n);
+    rc = smem_attr((const void*)k_a4gv<true>, smem);
+    if (rc) return rc;
+    k_a4gv<true><<<grid, 256, smem, st>>>(a8, sa, b4, sw, dst, idot, n, plan);
   } else {
-    HV_CUDA(cudaFuncSetAttribute(k_a4gv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    k_a4gv<false><<<grid, 256, smem, st>>>(a8, sa, b4, sw, dst, nullptr, nb, n);
+    const int ntile = (n + 7) / 8;
+    int grid8 = (ntile + 7) / 8;
+    if (grid8 > sms * 4) grid8 = sms * 4;
+    rc = smem_attr((const void*)k_a4gv_mma, smem);
+    if (rc) return rc;
+    k_a4gv_mma<<<grid8, 256, smem, st>>>(a8, sa, b4, sw, dst, n, plan);
   }
   HV_LAUNCHED("k_a4gv");
 }
@@ -396,15 +521,71 @@ int hv_a4gv_idot(const int8_t* a8, const float* sa, const uint32_t* b4, const fl
   return a4gv_launch(a8, sa, b4, sw, dst, idot, k8, n, stream);
 }
 
+int hv_w4_prepacked_size(int rows, int k, int pair_ffn, size_t* nib_bytes, size_t* scale_bytes) {
+  HV_REQUIRE(rows > 0 && k > 0 && k % kBlock == 0 && nib_bytes && scale_bytes, HV_E_INVALID,
+             "hv_w4_prepacked_size: bad arguments");
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_w4_prepacked_size: a paired matrix has 2 * pair_ffn rows");
+  const size_t tiles = (size_t)pp_tiles(rows, pair_ffn), iters = (size_t)pp_iters(k / kBlock);
+  *nib_bytes = tiles * iters * kPpNibWords * 4;
+  *scale_bytes = tiles * iters * kPpScales * 4;
+  return HV_OK;
+}
+
+int hv_w4_prepack(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
+                  uint32_t* pb4, float* psw, void* stream) {
+  HV_REQUIRE(b4 && sw && pb4 && psw && rows > 0 && k > 0 && k % kBlock == 0, HV_E_INVALID,
+             "hv_w4_prepack: bad arguments");
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_w4_prepack: a paired matrix has 2 * pair_ffn rows");
+  HV_REQUIRE(((uintptr_t)pb4 & 15) == 0 && ((uintptr_t)psw & 15) == 0, HV_E_INVALID,
+             "hv_w4_prepack: outputs must be 16-byte aligned");
+  const int nb = k / kBlock;
+  const int ntile = pp_tiles(rows, pair_ffn), niter = pp_iters(nb);
+  const long long threads = (long long)ntile * niter * 32;
+  k_w4_prepack<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      b4, sw, rows, nb, pair_ffn, ntile, niter, pb4, psw);
+  HV_LAUNCHED("k_w4_prepack");
+}
+
+int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+               float* dst, int k8, int rows, int pair_ffn, void* stream) {
+  HV_REQUIRE(a8 && sa && pb4 && psw && dst && k8 > 0 && rows > 0, HV_E_INVALID,
+             "hv_a4gv_pp: bad arguments");
+  HV_REQUIRE(k8 % 4 == 0, HV_E_INVALID, "hv_a4gv_pp: K = %d is not a multiple of 32", k8 * 8);
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_a4gv_pp: a paired matrix has 2 * pair_ffn rows");
+  HV_REQUIRE(((uintptr_t)a8 & 15) == 0 && ((uintptr_t)pb4 & 15) == 0 &&
+                 ((uintptr_t)psw & 15) == 0, HV_E_INVALID, "hv_a4gv_pp: unaligned pointer");
+  const int nb = k8 / 4;
+  HV_REQUIRE(nb <= 4096, HV_E_UNSUPPORTED, "hv_a4gv_pp: K = %d exceeds 131072", k8 * 8);
+  GvPlan plan;
+  HV_REQUIRE(gv_make_plan(nb, &plan), HV_E_UNSUPPORTED, "hv_a4gv_pp: no reduction plan for K");
+  const size_t smem = (size_t)nb * 40;
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  const int ntile = pp_tiles(rows, pair_ffn);
+  int grid = (ntile + 7) / 8;
+  if (grid > sms * 4) grid = sms * 4;
+  rc = smem_attr((const void*)k_a4gv_pp, smem);
+  if (rc) return rc;
+  k_a4gv_pp<<<grid, 256, smem, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, rows, pair_ffn,
+                                                       plan);
+  HV_LAUNCHED("k_a4gv_pp");
+}
+
 int hv_rmsnorm(const float* src, float* dst, const float* w, int rows, int cols, float eps,
                void* stream) {
   HV_REQUIRE(src && dst && w && rows > 0 && cols > 0, HV_E_INVALID, "hv_rmsnorm: bad arguments");
   // +8 floats: the idle lane groups of the leaf pass read x[0..8) even when cols < 8
-  const size_t smem = sizeof(PwPlan) + sizeof(float) * (kPwMaxLeaf + 4 + 2 * (size_t)cols + 8);
+  const size_t smem = sizeof(float) * (kPwMaxLeaf + 4 + 2 * (size_t)cols + 8);
   HV_REQUIRE(smem <= 220 * 1024, HV_E_UNSUPPORTED, "hv_rmsnorm: %d columns is too wide", cols);
-  HV_CUDA(cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
-  k_rmsnorm<<<rows, 256, smem, (cudaStream_t)stream>>>(src, dst, w, cols, eps);
+  PwPlan plan;
+  HV_REQUIRE(pw_make_plan(cols, &plan), HV_E_UNSUPPORTED, "hv_rmsnorm: no plan for %d", cols);
+  int rc = smem_attr((const void*)k_rmsnorm, smem);
+  if (rc) return rc;
+  k_rmsnorm<<<rows, 256, smem, (cudaStream_t)stream>>>(src, dst, w, cols, eps, plan);
   HV_LAUNCHED("k_rmsnorm");
 }
 

@@ -21,21 +21,32 @@
 // same (N = hidden), so the CTA that adds into h[row] is always the one that last
 // wrote it. Data produced by other CTAs is read through L2 (ld.global.cg): L1 is not
 // coherent across SMs.
+#include <mutex>
+
 #include <cuda_fp16.h>
 
 #include "attn_decode.cuh"
-#include "gemv_w4a8.cuh"
+#include "gemv_mma.cuh"
 #include "hv_internal.h"
 
 namespace hv {
 
 constexpr int kStepThreads = 512;
 constexpr int kStepWarps = kStepThreads / 32;
+constexpr int kStepU = 4;                 // GEMV load pipeline depth (iterations in flight)
+constexpr int kLeafScratch = 2048;        // floats of leaf values when leaves are split
+constexpr int kMaxHidden = 8192;          // pro_norm_quant holds 4 float4 per thread
 constexpr unsigned long long kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
 
+// Reduction plans of the step, built on the host (hv_step_plans) and copied into shared
+// memory at the start of every launch.
+struct StepPlans {
+  PwPlan pw_hid;                 // RMSNorm over the hidden vector
+  GvPlan gv_hid, gv_o, gv_ffn;   // GEMV rows with K = hidden, n_head * 128, ffn
+};
+
 struct StepShared {
-  PwPlan pw_hid;
-  GvPlan gv_hid, gv_o, gv_ffn;
+  StepPlans P;
   float leafval[kPwMaxLeaf];
   float red[4];
   float sv[32];
@@ -84,6 +95,11 @@ HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
   return S.ok != 0;
 }
 
+HV_DEV void trace_mark(const hv_step_desc& D, int idx) {
+  if (D.trace != nullptr && threadIdx.x == 0)
+    D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + idx] = global_ns();
+}
+
 HV_DEV void row_range(int n, int* r0, int* r1) {
   *r0 = (int)(((long long)blockIdx.x * n) / gridDim.x);
   *r1 = (int)(((long long)(blockIdx.x + 1) * n) / gridDim.x);
@@ -91,79 +107,184 @@ HV_DEV void row_range(int n, int* r0, int* r1) {
 
 // ---- prologues: build the quantised activation in shared memory ---------------------
 
-// act <- quant(rmsnorm(src, w)) over n = hidden values; src from global (through L2) or,
-// for layer 0, the f16 embedding row.
-__device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row, const float* __restrict__ w,
-                           int n, float eps, StepShared& S, float* x, float* sq, uint4* q_s,
-                           int2* sb_s) {
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = src ? __ldcg(src + i) : __half2float(emb_row[i]);
-    x[i] = v;
-    sq[i] = __fmul_rn(v, v);
+// act <- quant(rmsnorm(src, w)) over n = hidden values (n % 32 == 0, n <= kMaxHidden);
+// src from global (through L2) or, for layer 0, the f16 embedding row. Every load of
+// the vector and of the gain is issued before any is used.
+__device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row,
+                                            const float* __restrict__ w, int n, float eps,
+                                            StepShared& S, float* x, float* sq, uint4* q_s,
+                                            int2* sb_s) {
+  const int n4 = n / 4;
+  const int t = threadIdx.x;
+  float4 xv[4], wv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i4 = t + k * kStepThreads;
+    if (i4 < n4) {
+      if (src) {
+        xv[k] = __ldcg(reinterpret_cast<const float4*>(src) + i4);
+      } else {
+        const __half2* e = reinterpret_cast<const __half2*>(emb_row) + 2 * i4;
+        const float2 a = __half22float2(e[0]), b = __half22float2(e[1]);
+        xv[k] = make_float4(a.x, a.y, b.x, b.y);
+      }
+      wv[k] = __ldg(reinterpret_cast<const float4*>(w) + i4);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i4 = t + k * kStepThreads;
+    if (i4 < n4)
+      reinterpret_cast<float4*>(sq)[i4] =
+          make_float4(__fmul_rn(xv[k].x, xv[k].x), __fmul_rn(xv[k].y, xv[k].y),
+                      __fmul_rn(xv[k].z, xv[k].z), __fmul_rn(xv[k].w, xv[k].w));
   }
   __syncthreads();
-  const float ss = block_pw_sum(sq, &S.pw_hid, S.leafval, S.red);
+  const float ss = block_pw_sum(sq, &S.P.pw_hid, S.leafval, S.red);
   const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__ldg(w + i), __fdiv_rn(x[i], d));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i4 = t + k * kStepThreads;
+    if (i4 < n4)
+      reinterpret_cast<float4*>(x)[i4] = make_float4(
+          __fmul_rn(wv[k].x, __fdiv_rn(xv[k].x, d)), __fmul_rn(wv[k].y, __fdiv_rn(xv[k].y, d)),
+          __fmul_rn(wv[k].z, __fdiv_rn(xv[k].z, d)), __fmul_rn(wv[k].w, __fdiv_rn(xv[k].w, d)));
+  }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  int8_t* q8 = reinterpret_cast<int8_t*>(q_s);
-  for (int b = threadIdx.x >> 5; b < n / kBlock; b += kStepWarps) {
-    int8_t q;
-    float s;
-    int bs;
-    quant_block_warp(x[b * kBlock + lane], lane, &q, &s, &bs);
-    q8[b * kBlock + lane] = q;
-    if (lane == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+  // quantise: 8 lanes per 32-block, 4 blocks per warp pass
+  const int lane = t & 31, sub = lane & 7;
+  unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
+  const int nb = n / kBlock;
+  for (int b0 = (t >> 5) * 4; b0 < nb; b0 += kStepWarps * 4) {
+    const int b = b0 + (lane >> 3);
+    if (b < nb) {
+      float s;
+      int bs;
+      const float4 v = reinterpret_cast<const float4*>(x)[b * 8 + sub];
+      q32[b * 8 + sub] = quant_block_8lanes(v, &s, &bs);
+      if (sub == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+    }
   }
   __syncthreads();
 }
 
-// act <- quant(src) over n values produced by other CTAs
+// act <- quant(src) over n values produced by other CTAs (n % 32 == 0); 8 lanes per
+// 32-block, the loads of up to 8 passes in flight together.
 __device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2* sb_s) {
-  const int lane = threadIdx.x & 31;
-  int8_t* q8 = reinterpret_cast<int8_t*>(q_s);
-  for (int b = threadIdx.x >> 5; b < n / kBlock; b += kStepWarps) {
-    int8_t q;
-    float s;
-    int bs;
-    quant_block_warp(__ldcg(src + b * kBlock + lane), lane, &q, &s, &bs);
-    q8[b * kBlock + lane] = q;
-    if (lane == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+  constexpr int kBatch = 8;
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
+  const int nb = n / kBlock;
+  const int step = kStepWarps * 4;
+  for (int base = (threadIdx.x >> 5) * 4; base < nb; base += step * kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int b = base + k * step + (lane >> 3);
+      v[k] = (b < nb) ? __ldcg(reinterpret_cast<const float4*>(src) + b * 8 + sub)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int b = base + k * step + (lane >> 3);
+      if (b < nb) {
+        float s;
+        int bs;
+        q32[b * 8 + sub] = quant_block_8lanes(v[k], &s, &bs);
+        if (sub == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+      }
+    }
   }
   __syncthreads();
+}
+
+// L2 prefetch (one thread) of tiles [t0, t1) of a prepacked matrix with K columns: the
+// tiles' nibbles and scales are each one contiguous range.
+HV_DEV void prefetch_tiles(const uint32_t* pb4, const float* psw, int k, int t0, int t1) {
+  if (threadIdx.x != 0 || t1 <= t0) return;
+  const size_t it = (size_t)pp_iters(k / kBlock);
+  prefetch_l2(pb4 + (size_t)t0 * it * kPpNibWords, (size_t)(t1 - t0) * it * kPpNibWords * 4);
+  prefetch_l2(psw + (size_t)t0 * it * kPpScales, (size_t)(t1 - t0) * it * kPpScales * 4);
 }
 
 // ---- GEMV phases -----------------------------------------------------------------------
 
 enum { kStore = 0, kResidual = 1, kSiluPair = 2, kHead = 3 };
 
-// MODE kStore/kResidual/kHead: rows [r0, r1) of b4/sw. kSiluPair: gate/up pairs [r0, r1)
-// of a [gate | up] matrix with `ffn` rows per half, writing act[p] = silu(gate) * up.
+HV_DEV int pp_row_of(int tile, int g, int rows, int pair_ffn, bool* ok) {
+  if (pair_ffn > 0) {
+    const int p = tile * 4 + (g & 3);
+    *ok = p < pair_ffn;
+    return (g < 4) ? p : pair_ffn + p;
+  }
+  const int row = tile * 8 + g;
+  *ok = row < rows;
+  return row;
+}
+
+// (tile, leaf) tasks spread over the warps; leaf values meet in shared memory and a last
+// pass folds each row in numpy's order (kStore / kResidual only).
 template <int MODE>
-__device__ __noinline__ void gemv_phase(const uint32_t* __restrict__ b4, const float* __restrict__ sw,
-                       const GvPlan& P, const ActView act, int r0, int r1, int ffn,
-                       float* __restrict__ out, float* best_v, int* best_i) {
-  const int lane = threadIdx.x & 31;
-  const int grp = lane >> 3;
-  const int per_quad = (MODE == kSiluPair) ? 2 : 4;
-  const int nq = (r1 - r0 + per_quad - 1) / per_quad;
-  for (int q = threadIdx.x >> 5; q < nq; q += kStepWarps) {
-    int row;
-    bool ok;
-    if (MODE == kSiluPair) {
-      const int p = r0 + q * 2 + (grp & 1);
-      ok = p < r1;
-      row = (grp < 2) ? p : ffn + p;
-    } else {
-      row = r0 + q * 4 + grp;
-      ok = row < r1;
+__device__ __noinline__ void gemv_phase_split(const uint32_t* __restrict__ pb4,
+                                              const float* __restrict__ psw, const GvPlan& P,
+                                              const ActView act, int t0, int t1, int rows,
+                                              float* __restrict__ out, float* leaf_s) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
+  const int warp = threadIdx.x >> 5;
+  const int nl = P.nleaf, niter = pp_iters(P.nb);
+  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
+  for (int task = warp; task < (t1 - t0) * nl; task += kStepWarps) {
+    const int lt = task / nl, leaf = task % nl;
+    const int tile = t0 + lt;
+    gemv_tile8<kStepU, false, true>(pb4 + (size_t)tile * niter * kPpNibWords,
+                                    psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P,
+                                    leaf, leaf + 1, nullptr, leaf_s + (size_t)(lt * 8 + g) * nl);
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < (t1 - t0) * 8; s += blockDim.x) {
+    const int row = t0 * 8 + s;
+    if (row >= rows) continue;
+    const float y = fold_leaves(P, leaf_s + (size_t)s * nl);
+    if (MODE == kStore) out[row] = y;
+    else out[row] = __fadd_rn(__ldcg(out + row), y);
+  }
+  __syncthreads();
+}
+
+// GEMV over this CTA's tiles [t0, t1) of a matrix in the tile-interleaved layout, one
+// warp per tile. MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair:
+// tiles of 4 gate rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up]
+// matrix with pair_ffn rows per half; SiLU(gate) * up is formed in the lane that holds
+// the gate row and written to act[p]. When a CTA has few tiles but the rows have several
+// pairwise leaves, the leaves are spread over the warps.
+template <int MODE>
+__device__ __noinline__ void gemv_phase(const uint32_t* __restrict__ pb4,
+                                        const float* __restrict__ psw, const GvPlan& P,
+                                        const ActView act, int t0, int t1, int rows,
+                                        int pair_ffn, float* __restrict__ out, float* best_v,
+                                        int* best_i, float* leaf_s) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int warp = threadIdx.x >> 5;
+  const int ntile = t1 - t0;
+  const int niter = pp_iters(P.nb);
+  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
+  if constexpr (MODE == kStore || MODE == kResidual) {
+    if (P.nleaf > 1 && ntile * 2 <= kStepWarps && ntile * 8 * P.nleaf <= kLeafScratch) {
+      gemv_phase_split<MODE>(pb4, psw, P, act, t0, t1, rows, out, leaf_s);
+      return;
     }
-    const float y = gemv_rows4<8, false>(b4, sw, row, ok, act, P, nullptr);
+  }
+  for (int tile = t0 + warp; tile < t1; tile += kStepWarps) {
+    bool ok;
+    const int row = pp_row_of(tile, g, rows, pair_ffn, &ok);
+    float y;
+    gemv_tile8<kStepU, true, true>(pb4 + (size_t)tile * niter * kPpNibWords,
+                                   psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P, 0,
+                                   P.nleaf, &y, nullptr);
     if (MODE == kSiluPair) {
       const float up = __shfl_down_sync(0xFFFFFFFFu, y, 16);
-      if (grp < 2 && (lane & 7) == 0 && ok) out[row] = silu_mul1(y, up);
-    } else if ((lane & 7) == 0 && ok) {
+      if (g < 4 && t == 0 && ok) out[row] = silu_mul1(y, up);
+    } else if (t == 0 && ok) {
       if (MODE == kStore) {
         out[row] = y;
       } else if (MODE == kResidual) {
@@ -260,10 +381,27 @@ __device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w*
     if (S.flag) {
       __threadfence();
       attn_merge<GS>(D.part + (size_t)g * nch * GS * kPartStride, nch,
-                     D.ctx + (size_t)g * GS * kHd);
+                     D.ctx + (size_t)g * GS * kHd, red_s);
       if (threadIdx.x == 0) D.ticket[g] = 0;
     }
     __syncthreads();
+  }
+}
+
+// L2 prefetch (one thread) of the K and V rows this CTA's attention work items read.
+HV_DEV void prefetch_kv(const hv_step_desc& D, const hv_layer_w* L, int pos) {
+  if (threadIdx.x != 0) return;
+  const int nch = D.attn_chunks;
+  const float* kc = ldg_ptr(&L->kc);
+  const float* vc = ldg_ptr(&L->vc);
+  for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
+    const int g = wi / nch, c = wi % nch;
+    int t0, t1;
+    chunk_bounds(pos + 1, nch, c, &t0, &t1);
+    if (t1 <= t0) continue;
+    const size_t off = ((size_t)g * D.cap + t0) * kHd;
+    prefetch_l2(kc + off, (size_t)(t1 - t0) * kHd * 4);
+    prefetch_l2(vc + off, (size_t)(t1 - t0) * kHd * 4);
   }
 }
 
@@ -278,15 +416,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   const int kmax = max(max(hid, qdim), ffn);
   uint4* q_s = reinterpret_cast<uint4*>(area);
   int2* sb_s = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(area) + kmax);
-  float* x_s = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sb_s) + (kmax / kBlock) * 8);
+  // every region starts on a 16-byte boundary (float4 / int4 accesses)
+  float* x_s = reinterpret_cast<float*>(
+      reinterpret_cast<unsigned char*>(area) + (((size_t)kmax + (kmax / kBlock) * 8 + 15) & ~size_t(15)));
   float* sq_s = x_s + hid;
+  float* leaf_s = sq_s + hid;
   const ActView act{q_s, sb_s};
 
-  if (threadIdx.x == 0) {
-    pw_make_plan(hid, &S.pw_hid);
-    gv_make_plan(hid / kBlock, &S.gv_hid);
-    gv_make_plan(qdim / kBlock, &S.gv_o);
-    gv_make_plan(ffn / kBlock, &S.gv_ffn);
+  trace_mark(D, 0);
+  {
+    const int* src = reinterpret_cast<const int*>(D.plans);
+    int* dst = reinterpret_cast<int*>(&S.P);
+    for (int i = threadIdx.x; i < (int)(sizeof(StepPlans) / 4); i += blockDim.x) dst[i] = __ldg(src + i);
   }
   const int pos = *D.pos;
   const int tok = *D.tok;
@@ -297,49 +438,85 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     return;
   }
 
-  int hr0, hr1;                       // this CTA's rows of the residual (o and down)
-  row_range(hid, &hr0, &hr1);
+  // this CTA's tiles of every matrix; o and down share N = hidden, so the CTA that adds
+  // into h[row] is always the one that last wrote it
+  const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
+  int qt0, qt1, ht0, ht1, gt0, gt1;
+  row_range(pp_tiles(nqkv, 0), &qt0, &qt1);
+  row_range(pp_tiles(hid, 0), &ht0, &ht1);
+  row_range(pp_tiles(2 * ffn, ffn), &gt0, &gt1);
+  const int hr0 = ht0 * 8, hr1 = min(ht1 * 8, hid);
   const __half* emb_row = reinterpret_cast<const __half*>(D.emb16) + (size_t)tok * hid;
   for (int i = hr0 + threadIdx.x; i < hr1; i += blockDim.x) D.h[i] = __half2float(emb_row[i]);
 
+  prefetch_tiles(ldg_ptr(&D.layers[0].qkv_b4), ldg_ptr(&D.layers[0].qkv_sw), hid, qt0, qt1);
+  trace_mark(D, 1);
   for (int l = 0; l < D.n_layer; ++l) {
     const hv_layer_w* L = D.layers + l;
-    int r0, r1;
+    const int tb = 2 + 14 * l;
     // P1: qkv
     pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, ldg_ptr(&L->an), hid, D.eps, S, x_s, sq_s,
                    q_s, sb_s);
-    row_range((D.n_head + 2 * D.n_kv) * kHd, &r0, &r1);
-    gemv_phase<kStore>(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), S.gv_hid, act, r0, r1, 0,
-                       D.qkv, nullptr, nullptr);
+    trace_mark(D, tb + 0);
+    gemv_phase<kStore>(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), S.P.gv_hid, act, qt0, qt1, nqkv,
+                       0, D.qkv, nullptr, nullptr, leaf_s);
+    trace_mark(D, tb + 1);
+    prefetch_kv(D, L, pos);
     if (!grid_sync(D.barrier, D.status, S)) return;
+    trace_mark(D, tb + 2);
     // P2: attention
     attn_phase<GS>(D, L, pos, S, area);
+    trace_mark(D, tb + 3);
+    prefetch_tiles(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), qdim, ht0, ht1);
     if (!grid_sync(D.barrier, D.status, S)) return;
+    trace_mark(D, tb + 4);
     // P3: o projection + residual
     pro_quant(D.ctx, qdim, q_s, sb_s);
-    gemv_phase<kResidual>(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), S.gv_o, act, hr0, hr1, 0, D.h,
-                          nullptr, nullptr);
+    trace_mark(D, tb + 5);
+    gemv_phase<kResidual>(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), S.P.gv_o, act, ht0, ht1, hid, 0,
+                          D.h, nullptr, nullptr, leaf_s);
+    trace_mark(D, tb + 6);
+    prefetch_tiles(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), hid, gt0, gt1);
     if (!grid_sync(D.barrier, D.status, S)) return;
+    trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
     pro_norm_quant(D.h, nullptr, ldg_ptr(&L->fn), hid, D.eps, S, x_s, sq_s, q_s, sb_s);
-    row_range(ffn, &r0, &r1);
-    gemv_phase<kSiluPair>(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), S.gv_hid, act, r0, r1, ffn,
-                          D.act, nullptr, nullptr);
+    trace_mark(D, tb + 8);
+    gemv_phase<kSiluPair>(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), S.P.gv_hid, act, gt0, gt1,
+                          2 * ffn, ffn, D.act, nullptr, nullptr, leaf_s);
+    trace_mark(D, tb + 9);
+    prefetch_tiles(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), ffn, ht0, ht1);
     if (!grid_sync(D.barrier, D.status, S)) return;
+    trace_mark(D, tb + 10);
     // P5: down + residual
     pro_quant(D.act, ffn, q_s, sb_s);
-    gemv_phase<kResidual>(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), S.gv_ffn, act, hr0, hr1, 0,
-                          D.h, nullptr, nullptr);
+    trace_mark(D, tb + 11);
+    gemv_phase<kResidual>(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), S.P.gv_ffn, act, ht0, ht1, hid,
+                          0, D.h, nullptr, nullptr, leaf_s);
+    trace_mark(D, tb + 12);
+    if (l + 1 < D.n_layer) {
+      prefetch_tiles(ldg_ptr(&D.layers[l + 1].qkv_b4), ldg_ptr(&D.layers[l + 1].qkv_sw), hid,
+                     qt0, qt1);
+    } else if (flags & HV_STEP_HEAD) {
+      int a0, a1;
+      row_range(pp_tiles(D.head_rows, 0), &a0, &a1);
+      prefetch_tiles(D.head_b4, D.head_sw, hid, a0, min(a1, a0 + 8));
+    }
     if (!grid_sync(D.barrier, D.status, S)) return;
+    trace_mark(D, tb + 13);
   }
 
   if (!(flags & HV_STEP_HEAD)) return;
+  const int th = 2 + 14 * D.n_layer;
   pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, x_s, sq_s, q_s, sb_s);
-  int r0, r1;
-  row_range(D.head_rows, &r0, &r1);
+  trace_mark(D, th + 0);
+  int a0, a1;
+  row_range(pp_tiles(D.head_rows, 0), &a0, &a1);
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
-  gemv_phase<kHead>(D.head_b4, D.head_sw, S.gv_hid, act, r0, r1, 0, D.logits, &bv, &bi);
+  gemv_phase<kHead>(D.head_b4, D.head_sw, S.P.gv_hid, act, a0, a1, D.head_rows, 0, D.logits, &bv,
+                    &bi, leaf_s);
+  trace_mark(D, th + 1);
   if (!(flags & HV_STEP_ARGMAX)) return;
 
   // per-CTA argmax, then the last CTA to finish picks the token
@@ -382,12 +559,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       D.ticket[D.n_kv] = 0;
     }
   }
+  trace_mark(D, th + 2);
 }
 
 template <int GS>
 static size_t step_smem(int hid, int qdim, int ffn, int cap, int nch) {
   const int kmax = std::max(std::max(hid, qdim), ffn);
-  const size_t gemv = (size_t)kmax + (size_t)(kmax / kBlock) * 8 + 2 * (size_t)hid * 4;
+  const size_t gemv = (((size_t)kmax + (size_t)(kmax / kBlock) * 8 + 15) & ~size_t(15)) +
+                      2 * (size_t)hid * 4 + (size_t)kLeafScratch * 4;
   const int chunk_max = (cap + nch - 1) / nch;
   const size_t lg_floats = ((size_t)chunk_max * GS + 3) & ~size_t(3);
   const size_t attn = sizeof(float) * ((size_t)GS * kHd + 2 * kHd + (GS + 1) * kHd + 4 * GS +
@@ -440,12 +619,34 @@ int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t
   return HV_OK;
 }
 
+int hv_step_plans(int hidden, int qdim, int ffn, void* host_buf, size_t len) {
+  HV_REQUIRE(host_buf && len >= sizeof(StepPlans), HV_E_INVALID,
+             "hv_step_plans: buffer of %zu bytes needed", sizeof(StepPlans));
+  HV_REQUIRE(hidden > 0 && qdim > 0 && ffn > 0 && hidden % kBlock == 0 && qdim % kBlock == 0 &&
+                 ffn % kBlock == 0, HV_E_INVALID, "hv_step_plans: bad geometry");
+  StepPlans* P = static_cast<StepPlans*>(host_buf);
+  memset(P, 0, sizeof(StepPlans));
+  const bool ok = pw_make_plan(hidden, &P->pw_hid) && gv_make_plan(hidden / kBlock, &P->gv_hid) &&
+                  gv_make_plan(qdim / kBlock, &P->gv_o) && gv_make_plan(ffn / kBlock, &P->gv_ffn);
+  HV_REQUIRE(ok, HV_E_UNSUPPORTED, "hv_step_plans: reduction plan does not fit");
+  return HV_OK;
+}
+
+int hv_step_plans_bytes(size_t* bytes) {
+  HV_REQUIRE(bytes, HV_E_INVALID, "hv_step_plans_bytes: null pointer");
+  *bytes = sizeof(StepPlans);
+  return HV_OK;
+}
+
 int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(desc, HV_E_INVALID, "hv_step_launch: null descriptor");
   hv_step_desc h = *desc;
   HV_REQUIRE(h.head_dim == kHd, HV_E_UNSUPPORTED, "hv_step_launch: head_dim %d", h.head_dim);
   HV_REQUIRE(h.hidden % kBlock == 0 && h.ffn % kBlock == 0, HV_E_UNSUPPORTED,
              "hv_step_launch: hidden/ffn not multiples of 32");
+  HV_REQUIRE(h.hidden <= kMaxHidden, HV_E_UNSUPPORTED, "hv_step_launch: hidden %d > %d",
+             h.hidden, kMaxHidden);
+  HV_REQUIRE(h.plans != nullptr, HV_E_INVALID, "hv_step_launch: plans not set (hv_step_plans)");
   const int gs = h.n_head / h.n_kv;
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
@@ -453,7 +654,19 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const size_t smem = step_smem_any(gs, h.hidden, h.n_head * kHd, h.ffn, h.cap, h.attn_chunks);
   HV_REQUIRE(smem <= 227 * 1024, HV_E_UNSUPPORTED, "hv_step_launch: needs %zu B of smem", smem);
   void* fn = step_fn(gs);
-  HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  {
+    // set the function's shared-memory limit once per (group size, device, size)
+    static std::mutex mu;
+    static size_t done[4][64];
+    int dev = 0;
+    HV_CUDA(cudaGetDevice(&dev));
+    const int gi = gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || done[gi][dev] < smem) {
+      HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      if (dev >= 0 && dev < 64) done[gi][dev] = smem;
+    }
+  }
   int sms = 0;
   int rc = sm_count(&sms);
   if (rc) return rc;

@@ -89,8 +89,13 @@ _SIGS = {
     "hv_argmax_partial": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_argmax_final": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _VP],
     "hv_quantize_w4": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_w4_prepacked_size": [_I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
+    "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
+    "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
+    "hv_step_plans_bytes": [C.POINTER(_SZ)],
+    "hv_step_plans": [_I, _I, _I, _VP, _SZ],
 }
 
 
@@ -104,6 +109,8 @@ def load(kernels_dir=None, verify: bool = True):
     equivalent of the reference's PTX manifest check, engine/limited.py:218-235) and its
     ABI version must be the one this binding speaks."""
     global _L, _lib_path
+    if _L is not None and kernels_dir is None:
+        return _L                     # the per-call fast path: no filesystem access
     path = library_path(kernels_dir)
     if _L is not None:
         if path.resolve() != _lib_path.resolve():
@@ -144,7 +151,7 @@ def last_error() -> str:
 
 
 def _call(name: str, *args) -> None:
-    rc = getattr(load(), name)(*args)
+    rc = getattr(_L if _L is not None else load(), name)(*args)
     if rc != 0:
         raise CudaError(name, rc, last_error())
 
@@ -384,6 +391,21 @@ def argmax_partial(logits, pv, pi, n, parts, stream=0):
 
 def argmax_final(pv, pi, tok, gen, step, pos, parts, stream=0):
     _call("hv_argmax_final", _p(pv), _p(pi), _p(tok), _p(gen), _p(step), _p(pos), parts,
+          _p(stream))
+
+
+def w4_prepacked_size(rows, k, pair_ffn=0):
+    a, b = C.c_size_t(), C.c_size_t()
+    _call("hv_w4_prepacked_size", rows, k, pair_ffn, C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def w4_prepack(b4, sw, rows, k, pair_ffn, pb4, psw, stream=0):
+    _call("hv_w4_prepack", _p(b4), _p(sw), rows, k, pair_ffn, _p(pb4), _p(psw), _p(stream))
+
+
+def a4gv_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn=0, stream=0):
+    _call("hv_a4gv_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
           _p(stream))
 
 

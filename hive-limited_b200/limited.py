@@ -45,7 +45,8 @@ class _StepDesc(C.Structure):
                 + [(n, C.c_void_p) for n in (
                     "layers", "emb16", "onorm", "head_b4", "head_sw", "cos_t", "sin_t",
                     "tok", "pos", "step", "gen", "h", "qkv", "ctx", "act", "logits",
-                    "part", "ticket", "amax_v", "amax_i", "barrier", "status")])
+                    "part", "ticket", "amax_v", "amax_i", "barrier", "status", "trace",
+                    "plans")])
 
 
 STEP_HEAD = 1
@@ -135,25 +136,35 @@ class Engine:
         hvdrv.upload(p, arr.ctypes.data, arr.nbytes)
         return p
 
-    def _up_w4(self, parts: list[np.ndarray]):
-        """Quantise rows [part0 | part1 | ...] to the per-32 int4 form and upload.
-        -> (b4, sw, K, N)"""
+    def _up_w4(self, parts: list[np.ndarray], pair_ffn: int = 0):
+        """Quantise rows [part0 | part1 | ...] to the per-32 int4 form, upload, and reorder
+        into the GEMV's tile-interleaved layout (hv_w4_prepack; pair_ffn > 0 pairs gate
+        and up rows). -> (pb4, psw, K, N, pair_ffn)"""
         k = parts[0].shape[1]
         n = sum(p.shape[0] for p in parts)
         if self._quantize_on == "host":
             w = np.concatenate([p.astype(F32, copy=False) for p in parts], 0)
             packed, scale = quantize_w4(w)
-            return self._up(packed), self._up(scale), k, n
-        b4 = self._alloc(n * k // 2)
-        sw = self._alloc(n * k // BLOCK * 4)
-        off = 0
-        for p in parts:
-            p = np.ascontiguousarray(p, dtype=F32)
-            hvdrv.upload(self._stage + off, p.ctypes.data, p.nbytes)
-            off += p.nbytes
-        hvdrv.quantize_w4(self._stage, b4, sw, n, k)
+            b4 = hvdrv.alloc(packed.nbytes)
+            sw = hvdrv.alloc(scale.nbytes)
+            hvdrv.upload(b4, packed.ctypes.data, packed.nbytes)
+            hvdrv.upload(sw, scale.ctypes.data, scale.nbytes)
+        else:
+            b4 = hvdrv.alloc(n * k // 2)
+            sw = hvdrv.alloc(n * k // BLOCK * 4)
+            off = 0
+            for p in parts:
+                p = np.ascontiguousarray(p, dtype=F32)
+                hvdrv.upload(self._stage + off, p.ctypes.data, p.nbytes)
+                off += p.nbytes
+            hvdrv.quantize_w4(self._stage, b4, sw, n, k)
+        nib_bytes, sc_bytes = hvdrv.w4_prepacked_size(n, k, pair_ffn)
+        pb4, psw = self._alloc(nib_bytes), self._alloc(sc_bytes)
+        hvdrv.w4_prepack(b4, sw, n, k, pair_ffn, pb4, psw)
         hvdrv.synchronize()
-        return b4, sw, k, n
+        hvdrv.free(b4)
+        hvdrv.free(sw)
+        return pb4, psw, k, n, pair_ffn
 
     def _upload_weights(self, src: _TensorSource, quantize_on: str):
         c = self.cfg
@@ -180,7 +191,8 @@ class Engine:
                 qkv = self._up_w4([t("self_attn.q_proj.weight"), t("self_attn.k_proj.weight"),
                                    t("self_attn.v_proj.weight")])
                 o = self._up_w4([t("self_attn.o_proj.weight")])
-                gu = self._up_w4([t("mlp.gate_proj.weight"), t("mlp.up_proj.weight")])
+                gu = self._up_w4([t("mlp.gate_proj.weight"), t("mlp.up_proj.weight")],
+                                 pair_ffn=c.ffn)
                 down = self._up_w4([t("mlp.down_proj.weight")])
                 self.layers.append({
                     "an": self._up(t("input_layernorm.weight").astype(F32)),
@@ -265,14 +277,21 @@ class Engine:
         self.d_status = self._alloc(4)
         hvdrv.memset8(self.d_barrier, 0, 4)
         hvdrv.memset8(self.d_status, 0, 4)
-        hb4, hsw, _, hn = self.head
+        nbytes = C.c_size_t()
+        hvdrv._call("hv_step_plans_bytes", C.byref(nbytes))
+        plans = C.create_string_buffer(nbytes.value)
+        hvdrv._call("hv_step_plans", c.hidden, c.n_head * c.head_dim, c.ffn, plans,
+                    nbytes.value)
+        self.d_plans = self._alloc(nbytes.value)
+        hvdrv.upload(self.d_plans, C.addressof(plans), nbytes.value)
+        hb4, hsw, _, hn, _ = self.head
         self._desc = _StepDesc(
             c.n_layer, c.hidden, c.ffn, c.n_head, c.n_kv, c.head_dim, hn, c.max_context,
             RMS_EPS, float(self.attn_scale), chunks.value, c.vocab,
             self.d_layers, self.d_emb16, self.d_onorm, hb4, hsw, self.d_cos, self.d_sin,
             self.d_tok, self.d_pos, self.d_step, self.d_gen, self.d_h, self.d_qkv,
             self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
-            self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status)
+            self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans)
 
     def _set_i32(self, ptr: int, value: int):
         hvdrv.upload(ptr, np.array([value], np.int32).ctypes.data, 4)
@@ -286,10 +305,10 @@ class Engine:
 
     def _gemv(self, src, w4, dst):
         """quantize activations to per-32 int8, then the exact-int32 int4 GEMV."""
-        b4, sw, k, n = w4
+        pb4, psw, k, n, pair = w4
         s = self._stream_cur
         hvdrv.qa8s(src, self.d_a8, self.d_sa, k // BLOCK, s)
-        hvdrv.a4gv(self.d_a8, self.d_sa, b4, sw, dst, k // 8, n, s)
+        hvdrv.a4gv_pp(self.d_a8, self.d_sa, pb4, psw, dst, k // 8, n, pair, s)
 
     def _step_eager(self):
         """One transformer step at d_pos, kernel by kernel (engine/limited.py:374-419)."""
@@ -332,6 +351,48 @@ class Engine:
     def _step_fused(self, flags: int):
         hvdrv._call("hv_step_launch", C.byref(self._desc), int(flags),
                     C.c_void_p(self._stream_cur))
+
+    TRACE_PHASES = ("qkv_prologue", "qkv_gemv", "barrier1", "attention", "barrier2",
+                    "o_prologue", "o_gemv", "barrier3", "gu_prologue", "gu_gemv", "barrier4",
+                    "down_prologue", "down_gemv", "barrier5")
+
+    def profile_step(self, flags: int = STEP_HEAD | STEP_ARGMAX) -> dict:
+        """Run one fused step at the current tok/pos with the per-phase trace on.
+
+        Returns {"total_us", "phases": {name: {"median_us", "max_us"}}, "raw": ns array
+        [grid, stride]} where each phase's duration is taken per CTA and summed over the
+        layers (median and max over CTAs)."""
+        c = self.cfg
+        stride = 5 + 14 * c.n_layer
+        n = self.step_grid * stride
+        buf = hvdrv.alloc(n * 8)
+        try:
+            hvdrv.memset8(buf, 0, n * 8)
+            self._desc.trace = buf
+            self._step_fused(flags)
+            hvdrv.synchronize()
+            self._check_status()
+            raw = np.zeros((self.step_grid, stride), np.uint64)
+            hvdrv.download(raw.ctypes.data, buf, raw.nbytes)
+        finally:
+            self._desc.trace = None
+            hvdrv.free(buf)
+        t = raw.astype(np.int64)
+        t = t - t[:, :1]
+        out = {}
+        for k, name in enumerate(self.TRACE_PHASES):
+            idx = np.array([2 + 14 * l + k for l in range(c.n_layer)])
+            d = t[:, idx] - t[:, idx - 1]
+            out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
+                         "max_us": float(d.max(axis=0).sum() / 1e3)}
+        th = 2 + 14 * c.n_layer
+        for k, name in enumerate(("head_prologue", "head_gemv", "argmax")):
+            d = t[:, th + k] - t[:, th + k - 1]
+            out[name] = {"median_us": float(np.median(d) / 1e3), "max_us": float(d.max() / 1e3)}
+        out["setup"] = {"median_us": float(np.median(t[:, 1]) / 1e3),
+                        "max_us": float(t[:, 1].max() / 1e3)}
+        last = flags & STEP_ARGMAX and th + 2 or (flags & STEP_HEAD and th + 1 or th - 1)
+        return {"total_us": float(t[:, last].max() / 1e3), "phases": out, "raw": raw}
 
     def step_status(self) -> int:
         """Nonzero if a bounded wait inside the fused step ran out (HV_E_TIMEOUT)."""
@@ -560,7 +621,7 @@ class Engine:
     def _weight_bits(self) -> tuple[int, int]:
         bits = elems = 0
         mats = [w[key] for w in self.layers for key in ("qkv", "o", "gu", "down")]
-        for b4, sw, k, n in mats + [self.head]:
+        for b4, sw, k, n, _ in mats + [self.head]:
             bits += n * (k // 8) * 32 + n * (k // BLOCK) * 32
             elems += n * k
         return bits, elems

@@ -111,6 +111,18 @@ int hv_a4gv(const int8_t* a8, const float* sa, const uint32_t* b4, const float* 
 int hv_a4gv_idot(const int8_t* a8, const float* sa, const uint32_t* b4, const float* sw,
                  float* dst, int32_t* idot, int k8, int n, void* stream);
 
+/* The engine's weight layout: the same int4 values and scales reordered into 8-row
+ * tiles (pair_ffn > 0: 4 gate rows and their 4 up rows of a [gate | up] matrix with
+ * 2 * pair_ffn rows), 8 blocks per iteration, so that every warp-wide load of the GEMV
+ * reads 512 contiguous bytes. Nothing in the reference corresponds: its GEMV reads the
+ * row-major packed form (engine/limited.py:40-58) directly. */
+int hv_w4_prepacked_size(int rows, int k, int pair_ffn, size_t* nib_bytes, size_t* scale_bytes);
+int hv_w4_prepack(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
+                  uint32_t* pb4, float* psw, void* stream);
+/* gemv_wpo_a4 over the prepacked layout; dst keeps the reference row order. */
+int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+               float* dst, int k8, int rows, int pair_ffn, void* stream);
+
 /* rmsnorm_bp (k_rmsbp.ptx; launch engine/limited.py:361-362): row-wise
  * dst = w * (src / sqrt(mean(src^2) + eps)); rows x cols; in place allowed. The
  * reference kernel hard-wires eps = 1e-5 (engine/reference.py:34). */
@@ -209,7 +221,17 @@ typedef struct hv_step_desc {
   float* amax_v; int32_t* amax_i;                  /* [grid] argmax partials       */
   uint32_t* barrier;            /* one word, zeroed once                           */
   int32_t* status;              /* 0 = ok; nonzero after a bounded wait ran out    */
+  uint64_t* trace;              /* NULL, or [grid][HV_STEP_TRACE_STRIDE(n_layer)]:
+                                   %globaltimer (ns) at each phase boundary, per CTA */
+  const void* plans;            /* hv_step_plans() output, uploaded to the device  */
 } hv_step_desc;
+
+/* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 14 l:
+ * +0 qkv prologue, +1 qkv GEMV, +2 barrier, +3 attention, +4 barrier, +5 o prologue,
+ * +6 o GEMV, +7 barrier, +8 gate/up prologue, +9 gate/up GEMV, +10 barrier,
+ * +11 down prologue, +12 down GEMV, +13 barrier; then the head prologue, head GEMV and
+ * argmax at 2 + 14 n_layer + {0, 1, 2}. */
+#define HV_STEP_TRACE_STRIDE(n_layer) (5 + 14 * (n_layer))
 
 #define HV_STEP_HEAD 1     /* compute the LM head into logits                          */
 #define HV_STEP_ARGMAX 2   /* then greedy argmax: tok = argmax, gen[step] = tok,
@@ -220,6 +242,12 @@ typedef struct hv_step_desc {
  * attn_chunks, `grid` entries for amax_v / amax_i. */
 int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t* smem,
                    int* chunks, size_t* part_floats);
+
+/* The step's reduction plans (numpy's pairwise order for RMSNorm over `hidden` and for
+ * GEMV rows of K = hidden, qdim, ffn) into a host buffer of hv_step_plans_bytes() bytes;
+ * the caller uploads it and points hv_step_desc.plans at the device copy. */
+int hv_step_plans_bytes(size_t* bytes);
+int hv_step_plans(int hidden, int qdim, int ffn, void* host_buf, size_t len);
 
 /* One fused decode step. `desc` is a host pointer to a filled hv_step_desc. */
 int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);

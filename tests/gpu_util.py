@@ -68,3 +68,30 @@ def quantize_on_device(a):
     sa = Dev(nbytes=nb * 8)
     hvdrv.qa8s(src, a8, sa, nb)
     return a8, sa
+
+
+def unprepack(pb4, psw, rows, k, pair_ffn=0):
+    """The tile-interleaved layout (hv_w4_prepack) back to the reference layout:
+    (packed u32 [rows, k/8], scales f32 [rows, k/32])."""
+    nb = k // 32
+    niter = (nb + 7) // 8
+    ntile = (pair_ffn + 3) // 4 if pair_ffn else (rows + 7) // 8
+    # nibbles: [tile][iter][half][g][t][jj] = word t of block 8 iter + 4 half + jj of row(g)
+    w = np.asarray(pb4, np.uint32).reshape(ntile, niter, 2, 8, 4, 4)
+    w = w.transpose(0, 3, 1, 2, 5, 4).reshape(ntile * 8, niter * 8, 4)
+    # scales: [tile][iter][g][t][e] = scale of block 8 iter + 2t + e of row(g)
+    sc = np.asarray(psw, np.float32).reshape(ntile, niter, 8, 4, 2)
+    sc = sc.transpose(0, 2, 1, 3, 4).reshape(ntile * 8, niter * 8)
+    if pair_ffn:
+        tiles = np.arange(ntile * 8) // 8
+        g = np.arange(ntile * 8) % 8
+        p = tiles * 4 + (g % 4)
+        row = np.where(g < 4, p, pair_ffn + p)
+        keep = p < pair_ffn
+        packed = np.zeros((rows, nb * 4), np.uint32)
+        scale = np.zeros((rows, nb), np.float32)
+        packed[row[keep]] = w[keep, :nb].reshape(-1, nb * 4)
+        scale[row[keep]] = sc[keep, :nb]
+        return packed.reshape(rows, k // 8), scale
+    return (np.ascontiguousarray(w[:rows, :nb].reshape(rows, k // 8)),
+            np.ascontiguousarray(sc[:rows, :nb]))

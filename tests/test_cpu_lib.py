@@ -70,9 +70,9 @@ def test_step_desc_layout_matches_header():
     """The ctypes mirror of hv_step_desc / hv_layer_w has the C layout."""
     import limited
     assert ctypes.sizeof(limited._LayerW) == 14 * 8
-    # 8 ints + 2 floats + 2 ints = 48 bytes, then 22 pointers
+    # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers
     assert limited._StepDesc.layers.offset == 48
-    assert ctypes.sizeof(limited._StepDesc) == 48 + 22 * 8
+    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8
 
 
 def test_gpu_only_paths_fail_loudly_without_gpu():

@@ -188,12 +188,11 @@ def test_layer_ops_bit_exact_at_8b_shape(hv):
         scale = Dev(np.array([1.0 / np.sqrt(qd)], F32))
 
         def run_gemv(name, x):
-            packed, sc, k = w[name]
-            b4, sw, _, n = eng.layers[L][name.split(".")[1]] if name != "head" else eng.head
+            pb4, psw, k, n, pair = eng.layers[L][name.split(".")[1]]
             xd = Dev(x)
             y = Dev(nbytes=n * 4)
             hvdrv.qa8s(xd, eng.d_a8, eng.d_sa, k // 32)
-            hvdrv.a4gv(eng.d_a8, eng.d_sa, b4, sw, y, k // 8, n)
+            hvdrv.a4gv_pp(eng.d_a8, eng.d_sa, pb4, psw, y, k // 8, n, pair)
             return y.get(F32)
 
         for L in (0, 17, 35):
@@ -263,8 +262,12 @@ def download_weights(eng, hvdrv):
         return out
 
     def mat(t):
-        b4, sw, k, n = t
-        return get(b4, np.uint32, (n, k // 8)), get(sw, F32, (n, k // 32)), k
+        from gpu_util import unprepack
+        pb4, psw, k, n, pair = t
+        nib, sc = hvdrv.w4_prepacked_size(n, k, pair)
+        packed, scale = unprepack(get(pb4, np.uint32, (nib // 4,)), get(psw, F32, (sc // 4,)),
+                                  n, k, pair)
+        return packed, scale, k
 
     w = {"emb16": get(eng.d_emb16, np.float16, (c.vocab, c.hidden))}
     for l, L in enumerate(eng.layers):

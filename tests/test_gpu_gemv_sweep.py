@@ -49,3 +49,10 @@ def test_sweep_shape_bit_exact(hv, golden, j):
     y2 = Dev(nbytes=n * 4)
     hv.a4gv(a8, sa, b4, sw, y2, k // 8, n)
     assert sha(y2.get(F32)) == str(g[f"s{j}_y_sha"])
+    # the engine's tile-interleaved layout gives the same bits
+    nib, scb = hv.w4_prepacked_size(n, k, 0)
+    pb4, psw = Dev(nbytes=nib), Dev(nbytes=scb)
+    hv.w4_prepack(b4, sw, n, k, 0, pb4, psw)
+    y3 = Dev(nbytes=n * 4)
+    hv.a4gv_pp(a8, sa, pb4, psw, y3, k // 8, n, 0)
+    assert sha(y3.get(F32)) == str(g[f"s{j}_y_sha"])

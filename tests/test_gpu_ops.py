@@ -180,3 +180,27 @@ def test_argmax_ties_lowest_and_device_state(hv):
     assert tok.get(np.int32)[0] == 500 == O.argmax(logits)
     assert gen.get(np.int32)[3] == 500
     assert step.get(np.int32)[0] == 4 and pos.get(np.int32)[0] == 42
+
+
+@pytest.mark.parametrize("n,k,pair", [(5, 32, 0), (13, 416, 0), (777, 4096, 0), (64, 12288, 0),
+                                      (21, 25600, 0), (26, 2048, 13), (24576, 4096, 12288),
+                                      (10, 160, 5)])
+def test_prepack_roundtrip_and_gemv_pp_bit_exact(hv, n, k, pair):
+    """hv_w4_prepack only reorders (download + inverse gives the reference layout back);
+    the GEMV over the reordered layout is bit-exact with the oracle, rows in reference
+    order (for a paired [gate | up] matrix too)."""
+    from gpu_util import unprepack
+    g = np.random.default_rng(n * 31 + k)
+    p, sc = O.quantize_w4((g.standard_normal((n, k)) * 0.02).astype(F32))
+    nib, scb = hv.w4_prepacked_size(n, k, pair)
+    pb4, psw = Dev(nbytes=nib), Dev(nbytes=scb)
+    hv.w4_prepack(Dev(p), Dev(sc), n, k, pair, pb4, psw)
+    p2, s2 = unprepack(pb4.get(np.uint32), psw.get(F32), n, k, pair)
+    assert np.array_equal(p2, p) and np.array_equal(bits(s2), bits(sc))
+    a = (g.standard_normal(k) * 2).astype(F32)
+    qa, sa_h, _ = O.quantize_act(a)
+    _, want = O.gemv_q_c(qa, sa_h, p, sc, k)
+    a8, sa = quantize_on_device(a)
+    y = Dev(nbytes=n * 4)
+    hv.a4gv_pp(a8, sa, pb4, psw, y, k // 8, n, pair)
+    assert np.array_equal(bits(y.get(F32)), bits(want))
