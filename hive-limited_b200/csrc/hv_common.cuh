@@ -31,6 +31,7 @@ constexpr int kPwMaxLeaf = 512; // leaves a plan may hold (n <= 65536)
 // ---------------------------------------------------------------------------
 struct PwPlan {
   int nleaf;
+  int balanced;   // every split halves exactly and nleaf is a power of two <= 64
   int start[kPwMaxLeaf];
   short len[kPwMaxLeaf];
   unsigned char pops[kPwMaxLeaf];
@@ -60,6 +61,11 @@ HV_HD bool pw_make_plan(int n, PwPlan* p) {
     }
   }
   p->nleaf = nl;
+  // balanced: all leaves equal, a power-of-two count, each split exactly in half -- then
+  // the recursion's '+' is the xor-butterfly over leaf indices
+  bool bal = nl <= 64 && (nl & (nl - 1)) == 0;
+  for (int i = 0; bal && i < nl; ++i) bal = p->len[i] == p->len[0] && p->start[i] == i * p->len[0];
+  p->balanced = bal ? 1 : 0;
   return true;
 }
 
@@ -115,7 +121,24 @@ HV_DEV float block_pw_sum(const float* x, const PwPlan* plan, float* leafval,
     if (live && sub == 0) leafval[leaf] = v;
   }
   __syncthreads();
-  if (threadIdx.x == 0) *result = pw_fold(plan, leafval);
+  if (plan->balanced) {
+    // one warp folds: leaf i -> lane i % 32 (two per lane when 64), then the butterfly
+    if (threadIdx.x < 32) {
+      const int n = plan->nleaf;
+      const int lane = threadIdx.x;
+      float v;
+      if (n == 64) {
+        v = __fadd_rn(leafval[2 * lane], leafval[2 * lane + 1]);
+      } else {
+        v = (lane < n) ? leafval[lane] : 0.0f;
+      }
+      const int m = n == 64 ? 32 : n;
+      for (int o = 1; o < m; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+      if (lane == 0) *result = __fadd_rn(0.0f, v);
+    }
+  } else if (threadIdx.x == 0) {
+    *result = pw_fold(plan, leafval);
+  }
   __syncthreads();
   return *result;
 }

