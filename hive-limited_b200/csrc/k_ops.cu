@@ -463,7 +463,7 @@ extern "C" {
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
       "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_quantize_w4,k_step";
+      "k_argmax_p,k_argmax_f,k_quantize_w4,k_step,k_attn_na";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;

@@ -83,6 +83,7 @@ _SIGS = {
     "hv_kv_append": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_attn_decode": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_attn_reserve": [_I, _I, _I],
+    "hv_attn_decode_noalloc": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_silu_mul": [_VP, _VP, _VP, _I, _VP],
     "hv_vadd": [_VP, _VP, _VP, _I, _VP],
     "hv_gather_emb": [_VP, _VP, _VP, _I, _VP],
@@ -371,6 +372,13 @@ def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
 
 def attn_reserve(nkv, group, cap):
     _call("hv_attn_reserve", nkv, group, cap)
+
+
+def attn_decode_noalloc(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
+    """attn_decode over the library's fixed static scratch: never allocates (see
+    hv_attn_decode_noalloc in include/hive_b200.h for its limits)."""
+    _call("hv_attn_decode_noalloc", _p(q), _p(kc), _p(vc), _p(ctx), _p(scale), _p(pos), nq,
+          hd, group, kvstride, _p(stream))
 
 
 def silu_mul(gate, up, act, n, stream=0):

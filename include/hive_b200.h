@@ -150,6 +150,19 @@ int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
 /* Makes sure the attention scratch can serve nkv heads at a cache of `cap` positions. */
 int hv_attn_reserve(int nkv, int group, int cap);
 
+/* No counterpart in the reference. hv_attn_decode for callers that cannot let the
+ * library allocate (a process that gives all of HBM to its own pool, or a loop that
+ * cannot take the device-wide synchronisation of cudaMalloc/cudaFree): same arguments
+ * and results, but its scratch is a fixed 2 MiB static device array, so it calls no
+ * cudaMalloc or cudaFree. Limits: at most 64 kv heads and nkv x chunks x group x 528
+ * bytes of partial state (chunks = max(ceil(SMs / nkv), ceil(cap / 1024))) within
+ * 2 MiB - 256 B; larger problems return HV_E_INVALID. The first call on a device does
+ * a one-time set-up (symbol address, kernel attributes): make it before any stream
+ * capture. All calls on a device share the array; calls that overlap on the GPU race. */
+int hv_attn_decode_noalloc(const float* q, const float* kc, const float* vc, float* ctx,
+                           const float* scale, const int32_t* pos, int nq, int hd, int group,
+                           int kvstride, void* stream);
+
 /* gpu_silu_mul (k_silu.ptx; engine/limited.py:412-413): act = g * sigma(g) * up. */
 int hv_silu_mul(const float* gate, const float* up, float* act, int n, void* stream);
 
