@@ -188,16 +188,17 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
 // partials through L2 (they were written by other CTAs): first every chunk's (m, l) in
 // parallel, then per head the global max and weights, then each output element sums
 // its chunks with all loads of a batch in flight. `w_s` is shared scratch of
-// 2 * nch * GS + GS floats. Block-cooperative.
-template <int GS>
+// 2 * nch * GS + GS floats. Cooperative over the threads of Sync.
+template <int GS, class Sync = SyncBlock>
 HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx, float* w_s) {
   float* l_s = w_s + nch * GS;                    // l of (c, i)
   float* inv_s = l_s + nch * GS;                  // 1 / L per head
-  for (int e = threadIdx.x; e < nch * GS; e += blockDim.x) {
+  const int nt = Sync::threads();
+  for (int e = threadIdx.x; e < nch * GS; e += nt) {
     w_s[e] = __ldcg(part_head + (size_t)e * kPartStride);          // m of (c, i)
     l_s[e] = __ldcg(part_head + (size_t)e * kPartStride + 1);
   }
-  __syncthreads();
+  Sync::sync();
   if (threadIdx.x < GS) {
     const int i = threadIdx.x;
     float M = -INFINITY;
@@ -210,8 +211,8 @@ HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx,
     }
     inv_s[i] = 1.0f / L;
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) {
+  Sync::sync();
+  for (int e = threadIdx.x; e < GS * kHd; e += nt) {
     const int i = e / kHd, d = e % kHd;
     float o = 0.f;
     for (int c0 = 0; c0 < nch; c0 += 8) {

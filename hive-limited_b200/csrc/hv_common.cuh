@@ -104,12 +104,27 @@ HV_DEV float pw_leaf8(const float* x, int len, int sub) {
   return r;
 }
 
+// The threads that run a block-cooperative routine and how they synchronise: the whole
+// block (__syncthreads), or the first N threads on named barrier ID (warp-specialised
+// kernels whose other warps never join).
+struct SyncBlock {
+  HV_DEV static void sync() { __syncthreads(); }
+  HV_DEV static int threads() { return blockDim.x; }
+};
+template <int N, int ID>
+struct SyncNamed {
+  static_assert(N % 32 == 0 && ID > 0 && ID < 16, "named barrier of whole warps");
+  HV_DEV static void sync() { asm volatile("bar.sync %0, %1;" :: "n"(ID), "n"(N) : "memory"); }
+  HV_DEV static int threads() { return N; }
+};
+
 // Block-cooperative numpy sum of x[0..n) in shared memory. `plan` and `leafval`
 // (kPwMaxLeaf floats) are shared scratch; the plan must already be built for n.
-// All threads of the block must call it; the result is returned to every thread.
+// All threads of Sync must call it; the result is returned to every thread.
+template <class Sync = SyncBlock>
 HV_DEV float block_pw_sum(const float* x, const PwPlan* plan, float* leafval,
                           float* result) {
-  const int nthreads = blockDim.x;
+  const int nthreads = Sync::threads();
   const int groups = nthreads / 8;
   const int g = threadIdx.x / 8, sub = threadIdx.x % 8;
   for (int leaf = g; leaf < ((plan->nleaf + groups - 1) / groups) * groups; leaf += groups) {
@@ -120,7 +135,7 @@ HV_DEV float block_pw_sum(const float* x, const PwPlan* plan, float* leafval,
     const float v = pw_leaf8(x + s, len, sub);
     if (live && sub == 0) leafval[leaf] = v;
   }
-  __syncthreads();
+  Sync::sync();
   if (plan->balanced) {
     // one warp folds: leaf i -> lane i % 32 (two per lane when 64), then the butterfly
     if (threadIdx.x < 32) {
@@ -139,7 +154,7 @@ HV_DEV float block_pw_sum(const float* x, const PwPlan* plan, float* leafval,
   } else if (threadIdx.x == 0) {
     *result = pw_fold(plan, leafval);
   }
-  __syncthreads();
+  Sync::sync();
   return *result;
 }
 

@@ -7,6 +7,19 @@
 // small vector work it needs (RMSNorm + per-32 quantisation of a 4-20 KB vector, the
 // q/k norms and RoPE of its own heads) instead of waiting on a separate kernel.
 //
+// Why warp-specialised: the step reads ~6 GB (8B shape at a 4k context) and computes
+// little, so its speed is how continuously HBM is kept busy. Each CTA (one per SM) has a
+// PRODUCER warp that walks the CTA's share of every byte the step streams -- its weight
+// tiles of every GEMV, the K and V rows of its attention chunks, its rows of the LM head
+// -- in the order they are consumed, and copies them with the bulk-copy engine
+// (cp.async.bulk, completion on an mbarrier) into a ring of 10 KB shared-memory slots.
+// Eight CONSUMER warps wait for slots, compute, and release them. Only the consumers
+// take part in the grid barriers between phases, so while they wait for the rest of the
+// GPU, or build the next activation vector, the producer is already loading the next
+// phase's weights (as far as the ring reaches). Nothing the producer streams depends on
+// this step's results: weights are constant and the KV rows it reads (positions < pos)
+// were written by earlier launches; row `pos` itself comes from this step's qkv output.
+//
 // Per layer, five phases separated by grid barriers:
 //   P1 qkv  : act <- quant(rmsnorm(h, an)); rows of W_qkv        -> qkv
 //   P2 attn : per (kv head, chunk): q/k norm + RoPE, KV append at pos, split softmax;
@@ -17,10 +30,9 @@
 // then the head: act <- quant(rmsnorm(h, onorm)); rows of the LM head -> logits and a
 // per-CTA argmax; the last CTA picks the token and advances tok/gen/step/pos.
 //
-// Rows of every matrix are split evenly over the CTAs; the o and down splits are the
-// same (N = hidden), so the CTA that adds into h[row] is always the one that last
-// wrote it. Data produced by other CTAs is read through L2 (ld.global.cg): L1 is not
-// coherent across SMs.
+// GEMV tiles split evenly over the CTAs; the CTAs that take the remainder's extra tile
+// rotate from phase to phase. Data produced by other CTAs is read through L2
+// (ld.global.cg) after a grid barrier: L1 is not coherent across SMs.
 #include <mutex>
 
 #include <cuda_fp16.h>
@@ -31,12 +43,24 @@
 
 namespace hv {
 
-constexpr int kStepThreads = 512;        // 16 warps, up to 128 registers each
-constexpr int kStepWarps = kStepThreads / 32;
-constexpr int kStepU = 4;                 // GEMV load pipeline depth (iterations in flight)
-constexpr int kCBufFloats = 12288;        // block terms of split GEMV phases (48 KB)
-constexpr int kMaxHidden = 8192;          // pro_norm_quant holds 4 float4 per thread
-constexpr unsigned long long kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
+constexpr int kConsWarps = 8;                          // consumer warps
+constexpr int kConsThreads = kConsWarps * 32;
+constexpr int kStepThreads = kConsThreads + 32;        // + the producer warp
+constexpr int kSlotBytes = 10240;                      // one ring slot
+constexpr int kSlotIters = 8;                          // GEMV iterations per slot
+constexpr int kSlotScaleOff = kSlotIters * kPpNibWords * 4;   // nibbles, then scales
+constexpr int kSlotRows = kSlotBytes / (kHd * 4);      // KV rows per slot (20)
+constexpr int kMaxSlots = 32;
+constexpr int kMaxHidden = 8192;                       // pro_norm_quant's registers
+constexpr int kSmemLimit = 227 * 1024;
+constexpr unsigned long long kWaitNs = 2000000000ull;          // consumer waits: 2 s
+constexpr unsigned long long kProducerWaitNs = 4000000000ull;  // producer waits: 4 s
+
+static_assert(kSlotScaleOff + kSlotIters * kPpScales * 4 == kSlotBytes, "slot layout");
+static_assert(kSlotRows % 4 == 0, "attention groups of 4 rows never straddle slots");
+
+using CSync = SyncNamed<kConsThreads, 1>;
+HV_DEV void csync() { CSync::sync(); }
 
 // Reduction plans of the step, built on the host (hv_step_plans) and copied into shared
 // memory at the start of every launch.
@@ -53,7 +77,68 @@ struct StepShared {
   int si[32];
   int flag;
   int ok;
+  int abort;                     // set by any warp of this CTA whose wait gave up
 };
+
+// Byte offsets of the dynamic shared memory regions (host and device agree).
+struct StepLayout {
+  size_t bars, act_q, act_sb, work, ring, total;
+};
+
+HV_HD size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
+  const size_t chunk_max = ((size_t)cap + nch - 1) / nch;
+  const size_t lg = ((size_t)chunk_max * gs + 3) & ~size_t(3);
+  return (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 4 * (size_t)gs + lg +
+         (size_t)kConsWarps * gs * kHd;
+}
+
+HV_HD StepLayout step_layout(int gs, int hid, int qdim, int ffn, int cap, int nch, int nslots) {
+  const int kmax = hid > qdim ? (hid > ffn ? hid : ffn) : (qdim > ffn ? qdim : ffn);
+  StepLayout L;
+  L.bars = align_up(sizeof(StepShared), 16);
+  L.act_q = L.bars + 2 * kMaxSlots * sizeof(uint64_t);
+  L.act_sb = L.act_q + align_up((size_t)kmax, 16);
+  L.work = L.act_sb + align_up((size_t)(kmax / kBlock) * 8, 16);
+  const size_t attn = attn_area_floats(gs, cap, nch) * 4;
+  const size_t norm = (size_t)hid * 4;
+  L.ring = align_up(L.work + (attn > norm ? attn : norm), 128);
+  L.total = L.ring + (size_t)nslots * kSlotBytes;
+  return L;
+}
+
+// ---- mbarriers and bulk copies -----------------------------------------------------------
+
+HV_DEV unsigned sm_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+HV_DEV void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(sm_addr(b)), "r"(count) : "memory");
+}
+HV_DEV void mbar_arrive_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\t"
+               "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               :: "r"(sm_addr(b)), "r"(bytes) : "memory");
+}
+HV_DEV void mbar_arrive_n(uint64_t* b, unsigned n) {
+  asm volatile("{\n\t.reg .b64 st;\n\t"
+               "mbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}"
+               :: "r"(sm_addr(b)), "r"(n) : "memory");
+}
+HV_DEV bool mbar_test(uint64_t* b, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(sm_addr(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// global -> this CTA's shared memory, `bytes` (multiple of 16, both addresses 16-byte
+// aligned), completion counted on mbarrier `bar`
+HV_DEV void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(sm_addr(dst)), "l"(src), "r"(bytes), "r"(sm_addr(bar)) : "memory");
+}
 
 HV_DEV unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -67,31 +152,75 @@ HV_DEV unsigned long long global_ns() {
   return t;
 }
 
-// Grid-wide barrier over a self-resetting counter: CTA 0 adds 2^31 - (grid - 1), the
-// others add 1, so the top bit flips exactly when all have arrived and the low bits
-// return to zero. The wait is bounded: after kWaitNs (or once another CTA has reported
-// a failure) it records HV_E_TIMEOUT in *status and returns false.
-HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
-    __threadfence();
-    const unsigned old = atomicAdd(bar, add);
-    const unsigned long long t0 = global_ns();
-    int ok = 1;
-    while (((ld_acquire(bar) ^ old) & 0x80000000u) == 0) {
-      if (*(volatile int*)status != 0) { ok = 0; break; }
-      if (global_ns() - t0 > kWaitNs) {
-        atomicExch(status, HV_E_TIMEOUT);
-        ok = 0;
-        break;
-      }
-      __nanosleep(32);
+// Bounded wait for the completion of phase `parity` of mbarrier b. Gives up (false) when
+// this CTA has aborted, when any CTA reported a failure in *status, or after `limit` ns
+// (then records HV_E_TIMEOUT). Every caller that gives up sets S.abort.
+HV_DEV bool mbar_wait(uint64_t* b, unsigned parity, StepShared& S, int* status,
+                      unsigned long long limit) {
+  if (mbar_test(b, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned n = 0;; ++n) {
+    if (mbar_test(b, parity)) return true;
+    if (*(volatile int*)&S.abort) return false;
+    if ((n & 63) == 63 && *(volatile int*)status != 0) break;
+    if (global_ns() - t0 > limit) {
+      atomicCAS(status, 0, HV_E_TIMEOUT);
+      break;
     }
-    __threadfence();
+  }
+  *(volatile int*)&S.abort = 1;
+  return false;
+}
+
+// A warp's wait: every lane waits; the warp goes on only if all lanes saw the phase.
+HV_DEV bool warp_wait(uint64_t* b, unsigned parity, StepShared& S, int* status) {
+  const bool ok = mbar_wait(b, parity, S, status, kWaitNs);
+  return __all_sync(0xFFFFFFFFu, ok);
+}
+
+// The slot ring. Sequence number q (counted identically by producer and consumers) maps
+// to slot q % ns; its full barrier completes phase q / ns when the data has landed, its
+// empty barrier (kConsWarps arrivals) when the consumers are done with it.
+struct Ring {
+  unsigned char* slots;
+  uint64_t* full;
+  uint64_t* empty;
+  int ns;
+  HV_DEV unsigned char* slot(unsigned q) const { return slots + (size_t)(q % ns) * kSlotBytes; }
+  HV_DEV uint64_t* full_of(unsigned q) const { return full + q % ns; }
+  HV_DEV uint64_t* empty_of(unsigned q) const { return empty + q % ns; }
+  HV_DEV unsigned parity(unsigned q) const { return (q / ns) & 1u; }
+};
+
+// Grid-wide barrier of the consumer threads over a self-resetting counter: CTA 0 adds
+// 2^31 - (grid - 1), the others add 1, so the top bit flips exactly when all have arrived
+// and the low bits return to zero. The wait is bounded: after kWaitNs (or once another
+// CTA has reported a failure, or this CTA aborted) it records the failure and returns
+// false in every consumer thread.
+HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
+  csync();
+  if (threadIdx.x == 0) {
+    int ok = *(volatile int*)&S.abort == 0;
+    if (ok) {
+      const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
+      __threadfence();
+      const unsigned old = atomicAdd(bar, add);
+      const unsigned long long t0 = global_ns();
+      while (((ld_acquire(bar) ^ old) & 0x80000000u) == 0) {
+        if (*(volatile int*)status != 0) { ok = 0; break; }
+        if (global_ns() - t0 > kWaitNs) {
+          atomicCAS(status, 0, HV_E_TIMEOUT);
+          ok = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+      __threadfence();
+    }
+    if (!ok) *(volatile int*)&S.abort = 1;
     S.ok = ok;
   }
-  __syncthreads();
+  csync();
   return S.ok != 0;
 }
 
@@ -100,27 +229,148 @@ HV_DEV void trace_mark(const hv_step_desc& D, int idx) {
     D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + idx] = global_ns();
 }
 
-HV_DEV void row_range(int n, int* r0, int* r1) {
-  *r0 = (int)(((long long)blockIdx.x * n) / gridDim.x);
-  *r1 = (int)(((long long)(blockIdx.x + 1) * n) / gridDim.x);
+// ---- the schedule (walked identically by the producer and the consumers) --------------
+
+// Tiles [t0, t1) of a GEMV phase for this CTA: ntiles / grid each, and one more for the
+// `extra` CTAs starting at *off (cyclically). *off advances by extra, so the remainder
+// moves on to other CTAs in the next phase.
+HV_DEV void phase_tiles(int ntiles, int* off, int* t0, int* t1) {
+  const int G = gridDim.x, s = blockIdx.x;
+  const int base = ntiles / G, extra = ntiles % G, o = *off;
+  const int e1 = min(o + extra, G), wrap = max(0, o + extra - G);
+  const int b0 = max(0, min(s, e1) - o) + min(s, wrap);
+  const int b1 = max(0, min(s + 1, e1) - o) + min(s + 1, wrap);
+  *t0 = s * base + b0;
+  *t1 = (s + 1) * base + b1;
+  *off = (o + extra) % G;
+}
+
+// Positions [t0, t1) of attention chunk c, and te: rows [t0, te) come from the cache,
+// row pos (if in the chunk) from this step's qkv.
+HV_DEV void attn_rows(int pos, int nch, int c, int* t0, int* t1, int* te) {
+  chunk_bounds(pos + 1, nch, c, t0, t1);
+  *te = max(*t0, min(*t1, pos));
+}
+
+HV_DEV int slots_per_tile(int niter) { return (niter + kSlotIters - 1) / kSlotIters; }
+
+template <typename T>
+HV_DEV T* ldg_ptr(T* const* p) {
+  return reinterpret_cast<T*>(__ldg(reinterpret_cast<const unsigned long long*>(p)));
+}
+
+// ---- the producer ----------------------------------------------------------------------
+
+struct Producer {
+  const Ring& R;
+  StepShared& S;
+  int* status;
+  unsigned q = 0;
+  bool live = true;
+
+  HV_DEV Producer(const Ring& r, StepShared& s, int* st) : R(r), S(s), status(st) {}
+
+  // Claims the next slot (waiting until its previous contents were released) and
+  // starts up to two copies into it.
+  HV_DEV void issue(const void* a, unsigned na, const void* b, unsigned nb_, unsigned b_off) {
+    if (!live) return;
+    if (q >= (unsigned)R.ns &&
+        !mbar_wait(R.empty_of(q), R.parity(q) ^ 1u, S, status, kProducerWaitNs)) {
+      live = false;
+      return;
+    }
+    unsigned char* dst = R.slot(q);
+    uint64_t* full = R.full_of(q);
+    mbar_arrive_tx(full, na + nb_);
+    bulk_load(dst, a, na, full);
+    if (nb_) bulk_load(dst + b_off, b, nb_, full);
+    ++q;
+  }
+
+  // This CTA's tiles [t0, t1) of a prepacked matrix with niter iterations per tile.
+  HV_DEV void gemv(const uint32_t* pb4, const float* psw, int niter, int t0, int t1) {
+    const int spt = slots_per_tile(niter);
+    for (int tile = t0; tile < t1 && live; ++tile) {
+      for (int j = 0; j < spt; ++j) {
+        const int it0 = j * kSlotIters;
+        const unsigned n = (unsigned)min(kSlotIters, niter - it0);
+        const size_t first = (size_t)tile * niter + it0;
+        issue(pb4 + first * kPpNibWords, n * kPpNibWords * 4, psw + first * kPpScales,
+              n * kPpScales * 4, kSlotScaleOff);
+      }
+    }
+  }
+
+  // K rows then V rows [t0, te) of kv head g for one attention work item.
+  HV_DEV void kv(const float* kc, const float* vc, int g, int cap, int t0, int te) {
+    for (int pass = 0; pass < 2; ++pass) {
+      const float* base = (pass == 0 ? kc : vc) + (size_t)g * cap * kHd;
+      for (int r = t0; r < te && live; r += kSlotRows) {
+        const unsigned n = (unsigned)min(kSlotRows, te - r);
+        issue(base + (size_t)r * kHd, n * kHd * 4, nullptr, 0, 0);
+      }
+    }
+  }
+};
+
+// Wait (bounded) until every copy this producer started has landed, so no bulk copy is
+// still writing into shared memory when the CTA exits (on an abort the consumers may
+// leave without waiting for their slots).
+HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
+  const unsigned first = q > (unsigned)R.ns ? q - R.ns : 0u;
+  const unsigned long long t0 = global_ns();
+  for (unsigned k = first; k < q; ++k)
+    while (!mbar_test(R.full_of(k), R.parity(k)) && global_ns() - t0 < kWaitNs) {
+    }
+}
+
+HV_DEV void produce(const hv_step_desc& D, int flags, int pos, const Ring& R, StepShared& S) {
+  Producer P(R, S, D.status);
+  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
+  const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
+  const int nch = D.attn_chunks;
+  const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
+            it_ffn = pp_iters(ffn / kBlock);
+  int off = 0, t0, t1;
+  for (int l = 0; l < D.n_layer && P.live; ++l) {
+    const hv_layer_w* L = D.layers + l;
+    phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
+    P.gemv(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), it_hid, t0, t1);
+    for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
+      int a0, a1, ae;
+      attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
+      P.kv(ldg_ptr(&L->kc), ldg_ptr(&L->vc), wi / nch, D.cap, a0, ae);
+    }
+    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    P.gemv(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), it_q, t0, t1);
+    phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
+    P.gemv(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), it_hid, t0, t1);
+    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    P.gemv(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), it_ffn, t0, t1);
+  }
+  if ((flags & HV_STEP_HEAD) && P.live) {
+    phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
+    P.gemv(D.head_b4, D.head_sw, it_hid, t0, t1);
+  }
+  producer_drain(R, P.q, S);
 }
 
 // ---- prologues: build the quantised activation in shared memory ---------------------
 
 // act <- quant(rmsnorm(src, w)) over n = hidden values (n % 32 == 0, n <= kMaxHidden);
-// src from global (through L2) or, for layer 0, the f16 embedding row. Every load of
-// the vector and of the gain is issued before any is used.
+// src from global (through L2) or, for layer 0, the f16 embedding row. Thread t holds
+// float4 i4 = t + 256 k, so the 8 lanes of a lane group hold one 32-block and quantise
+// it from registers.
 __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row,
                                             const float* __restrict__ w, int n, float eps,
-                                            StepShared& S, float* x, float* sq, uint4* q_s,
-                                            int2* sb_s) {
-  constexpr int kV = kMaxHidden / 4 / kStepThreads;   // float4 per thread
+                                            StepShared& S, float* sq, uint4* q_s, int2* sb_s) {
+  constexpr int kV = kMaxHidden / 4 / kConsThreads;   // float4 per thread
   const int n4 = n / 4;
   const int t = threadIdx.x;
   float4 xv[kV], wv[kV];
 #pragma unroll
   for (int k = 0; k < kV; ++k) {
-    const int i4 = t + k * kStepThreads;
+    const int i4 = t + k * kConsThreads;
     if (i4 < n4) {
       if (src) {
         xv[k] = __ldcg(reinterpret_cast<const float4*>(src) + i4);
@@ -134,39 +384,30 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
   }
 #pragma unroll
   for (int k = 0; k < kV; ++k) {
-    const int i4 = t + k * kStepThreads;
+    const int i4 = t + k * kConsThreads;
     if (i4 < n4)
       reinterpret_cast<float4*>(sq)[i4] =
           make_float4(__fmul_rn(xv[k].x, xv[k].x), __fmul_rn(xv[k].y, xv[k].y),
                       __fmul_rn(xv[k].z, xv[k].z), __fmul_rn(xv[k].w, xv[k].w));
   }
-  __syncthreads();
-  const float ss = block_pw_sum(sq, &S.P.pw_hid, S.leafval, S.red);
+  csync();
+  const float ss = block_pw_sum<CSync>(sq, &S.P.pw_hid, S.leafval, S.red);
   const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+  unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
 #pragma unroll
   for (int k = 0; k < kV; ++k) {
-    const int i4 = t + k * kStepThreads;
-    if (i4 < n4)
-      reinterpret_cast<float4*>(x)[i4] = make_float4(
+    const int i4 = t + k * kConsThreads;
+    if (i4 < n4) {                      // uniform over each 8-lane group (n4 % 8 == 0)
+      const float4 x = make_float4(
           __fmul_rn(wv[k].x, __fdiv_rn(xv[k].x, d)), __fmul_rn(wv[k].y, __fdiv_rn(xv[k].y, d)),
           __fmul_rn(wv[k].z, __fdiv_rn(xv[k].z, d)), __fmul_rn(wv[k].w, __fdiv_rn(xv[k].w, d)));
-  }
-  __syncthreads();
-  // quantise: 8 lanes per 32-block, 4 blocks per warp pass
-  const int lane = t & 31, sub = lane & 7;
-  unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
-  const int nb = n / kBlock;
-  for (int b0 = (t >> 5) * 4; b0 < nb; b0 += kStepWarps * 4) {
-    const int b = b0 + (lane >> 3);
-    if (b < nb) {
       float s;
       int bs;
-      const float4 v = reinterpret_cast<const float4*>(x)[b * 8 + sub];
-      q32[b * 8 + sub] = quant_block_8lanes(v, &s, &bs);
-      if (sub == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
+      q32[i4] = quant_block_8lanes(x, &s, &bs);
+      if ((i4 & 7) == 0) sb_s[i4 >> 3] = make_int2(__float_as_int(s), bs);
     }
   }
-  __syncthreads();
+  csync();
 }
 
 // act <- quant(src) over n values produced by other CTAs (n % 32 == 0); 8 lanes per
@@ -176,7 +417,7 @@ __device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2
   const int lane = threadIdx.x & 31, sub = lane & 7;
   unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
   const int nb = n / kBlock;
-  const int step = kStepWarps * 4;
+  const int step = kConsWarps * 4;
   for (int base = (threadIdx.x >> 5) * 4; base < nb; base += step * kBatch) {
     float4 v[kBatch];
 #pragma unroll
@@ -196,19 +437,10 @@ __device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2
       }
     }
   }
-  __syncthreads();
+  csync();
 }
 
-// L2 prefetch (one thread) of tiles [t0, t1) of a prepacked matrix with K columns: the
-// tiles' nibbles and scales are each one contiguous range.
-HV_DEV void prefetch_tiles(const uint32_t* pb4, const float* psw, int k, int t0, int t1) {
-  if (threadIdx.x != 0 || t1 <= t0) return;
-  const size_t it = (size_t)pp_iters(k / kBlock);
-  prefetch_l2(pb4 + (size_t)t0 * it * kPpNibWords, (size_t)(t1 - t0) * it * kPpNibWords * 4);
-  prefetch_l2(psw + (size_t)t0 * it * kPpScales, (size_t)(t1 - t0) * it * kPpScales * 4);
-}
-
-// ---- GEMV phases -----------------------------------------------------------------------
+// ---- GEMV phases from the ring ----------------------------------------------------------
 
 enum { kStore = 0, kResidual = 1, kSiluPair = 2, kHead = 3 };
 
@@ -223,15 +455,6 @@ HV_DEV int pp_row_of(int tile, int g, int rows, int pair_ffn, bool* ok) {
   return row;
 }
 
-// GEMV over this CTA's tiles [t0, t1) of a matrix in the tile-interleaved layout.
-// MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate
-// rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
-// rows per half; SiLU(gate) * up is formed in the lane that holds the gate row.
-//
-// With fewer tiles than warps, each tile's iterations are cut into chunks so every warp
-// has work: (tile, chunk) items write their block terms to shared memory (cbuf), then
-// one warp per tile walks numpy's chains over them in order. Otherwise a warp takes a
-// whole tile and keeps the chains in registers. Both give the same bits.
 template <int MODE>
 HV_DEV void gemv_epilogue(float y, int row, bool ok, float* __restrict__ out, float* best_v,
                           int* best_i) {
@@ -251,74 +474,102 @@ HV_DEV void gemv_epilogue(float y, int row, bool ok, float* __restrict__ out, fl
   }
 }
 
-template <int MODE>
-__device__ __noinline__ void gemv_split(const uint32_t* __restrict__ pb4,
-                                        const float* __restrict__ psw, const GvPlan& P,
-                                        const ActView act, int t0, int t1, int rows,
-                                        int pair_ffn, int chunks, float* __restrict__ out,
-                                        float* best_v, int* best_i, float* cbuf) {
-  const int lane = threadIdx.x & 31, g = lane >> 2;
-  const int warp = threadIdx.x >> 5;
-  const int ntile = t1 - t0;
-  const int niter = pp_iters(P.nb);
-  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
-  float2* cb = reinterpret_cast<float2*>(cbuf);
-  for (int item = warp; item < ntile * chunks; item += kStepWarps) {
-    const int lt = item / chunks, c = item % chunks;
-    const int tile = t0 + lt;
-    tile_terms_pp<kStepU>(pb4 + (size_t)tile * niter * kPpNibWords,
-                          psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P,
-                          (c * niter) / chunks, ((c + 1) * niter) / chunks,
-                          cb + (size_t)lt * niter * 32);
+// numpy's pairwise chains of one row, walked iteration by iteration (the order of
+// chains_fold in gemv_mma.cuh): leaves of eight strided accumulators, the lane's two
+// accumulators 2t, 2t+1 folded across the quad at each leaf end, the recursion's '+'
+// in postfix order, the n % 8 tail in order at the very end.
+struct Chain {
+  float st[8];
+  int sp, leaf, leaf_begin;
+  float ae, ao;
+};
+
+HV_DEV void chain_step(Chain& c, const GvPlan& P, int it, float2 v) {
+  if (it == c.leaf_begin) {
+    c.ae = v.x;
+    c.ao = v.y;
+  } else {
+    c.ae = __fadd_rn(c.ae, v.x);
+    c.ao = __fadd_rn(c.ao, v.y);
   }
-  __syncthreads();
-  for (int lt = warp; lt < ntile; lt += kStepWarps) {
+  if (it + 1 == P.it_end[c.leaf] && c.leaf + 1 < P.nleaf) {
+    c.st[c.sp++] = quad_fold(c.ae, c.ao);
+    for (int k = 0; k < P.pops[c.leaf]; ++k) {
+      --c.sp;
+      c.st[c.sp - 1] = __fadd_rn(c.st[c.sp - 1], c.st[c.sp]);
+    }
+    c.leaf_begin = P.it_end[c.leaf];
+    ++c.leaf;
+  }
+}
+
+HV_DEV float chain_finish(Chain& c, const GvPlan& P, float2 tail) {
+  const int lane = threadIdx.x & 31;
+  float v = (P.nfull > c.leaf_begin) ? quad_fold(c.ae, c.ao) : 0.f;
+  for (int j = 0; j < P.ntail; ++j) {
+    const float x = __shfl_sync(0xFFFFFFFFu, (j & 1) ? tail.y : tail.x, (lane & ~3) | (j >> 1));
+    v = __fadd_rn(v, x);
+  }
+  c.st[c.sp++] = v;
+  for (int k = 0; k < P.pops[P.nleaf - 1]; ++k) {
+    --c.sp;
+    c.st[c.sp - 1] = __fadd_rn(c.st[c.sp - 1], c.st[c.sp]);
+  }
+  return __fadd_rn(0.0f, c.st[0]);
+}
+
+// The CTA's tiles [t0, t1) of one GEMV phase, their slots starting at sequence number
+// q0: warp w takes tiles w, w + 8, ... and walks each tile's slots in order. MODE
+// kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate rows
+// (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
+// rows per half; SiLU(gate) * up is formed in the lane that holds the gate row.
+template <int MODE>
+__device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan& P,
+                                       const ActView act, int t0, int t1, int rows,
+                                       int pair_ffn, float* __restrict__ out, float* best_v,
+                                       int* best_i, StepShared& S, int* status) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int warp = threadIdx.x >> 5;
+  const int niter = pp_iters(P.nb);
+  const int spt = slots_per_tile(niter);
+  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
+  for (int lt = warp; lt < t1 - t0; lt += kConsWarps) {
+    Chain c;
+    c.sp = 0;
+    c.leaf = 0;
+    c.leaf_begin = 0;
+    c.ae = c.ao = 0.f;
+    float2 tail = make_float2(0.f, 0.f);
+    for (int j = 0; j < spt; ++j) {
+      const unsigned q = q0 + (unsigned)(lt * spt + j);
+      if (!warp_wait(R.full_of(q), R.parity(q), S, status)) return;
+      const unsigned char* sl = R.slot(q);
+      const uint32_t* nw = reinterpret_cast<const uint32_t*>(sl);
+      const float* sw = reinterpret_cast<const float*>(sl + kSlotScaleOff);
+      const int it0 = j * kSlotIters;
+      const int n = min(kSlotIters, niter - it0);
+#pragma unroll 4
+      for (int u = 0; u < n; ++u) {
+        MmaLoads L;
+        const uint4 a = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 4 * lane);
+        const uint4 b = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 128 + 4 * lane);
+        L.w[0] = a.x; L.w[1] = a.y; L.w[2] = a.z; L.w[3] = a.w;
+        L.w[4] = b.x; L.w[5] = b.y; L.w[6] = b.z; L.w[7] = b.w;
+        L.s = *reinterpret_cast<const float2*>(sw + u * kPpScales + 2 * lane);
+        const int it = it0 + u;
+        if (it < P.nfull) {
+          chain_step(c, P, it, iter_terms(L, act_w, act.sb, it, g, t, 8));
+        } else {
+          tail = iter_terms(L, act_w, act.sb, it, g, t, P.ntail);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_n(R.empty_of(q), kConsWarps);
+    }
     bool ok;
     const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
-    const float y = chains_fold(P, cb + (size_t)lt * niter * 32);
-    gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
+    gemv_epilogue<MODE>(chain_finish(c, P, tail), row, ok, out, best_v, best_i);
   }
-  __syncthreads();
-}
-
-template <int MODE>
-__device__ __noinline__ void gemv_direct(const uint32_t* __restrict__ pb4,
-                                         const float* __restrict__ psw, const GvPlan& P,
-                                         const ActView act, int t0, int t1, int rows,
-                                         int pair_ffn, float* __restrict__ out, float* best_v,
-                                         int* best_i) {
-  const int lane = threadIdx.x & 31, g = lane >> 2;
-  const int warp = threadIdx.x >> 5;
-  const int niter = pp_iters(P.nb);
-  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
-  for (int tile = t0 + warp; tile < t1; tile += kStepWarps) {
-    bool ok;
-    const int row = pp_row_of(tile, g, rows, pair_ffn, &ok);
-    float y;
-    gemv_tile8<kStepU, true, true>(pb4 + (size_t)tile * niter * kPpNibWords,
-                                   psw + (size_t)tile * niter * kPpScales, act_w, act.sb, P, 0,
-                                   P.nleaf, &y, nullptr);
-    gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
-  }
-}
-
-template <int MODE>
-HV_DEV void gemv_phase(const uint32_t* __restrict__ pb4, const float* __restrict__ psw,
-                       const GvPlan& P, const ActView act, int t0, int t1, int rows,
-                       int pair_ffn, float* __restrict__ out, float* best_v, int* best_i,
-                       float* cbuf) {
-  const int ntile = t1 - t0;
-  const int niter = pp_iters(P.nb);
-  int chunks = 1;
-  if (ntile > 0 && ntile < kStepWarps) {
-    chunks = (kStepWarps + ntile - 1) / ntile;
-    if (chunks > niter) chunks = niter;
-    if ((size_t)ntile * niter * 64 > (size_t)kCBufFloats) chunks = 1;
-  }
-  if (chunks > 1)
-    gemv_split<MODE>(pb4, psw, P, act, t0, t1, rows, pair_ffn, chunks, out, best_v, best_i, cbuf);
-  else
-    gemv_direct<MODE>(pb4, psw, P, act, t0, t1, rows, pair_ffn, out, best_v, best_i);
 }
 
 // ---- attention -------------------------------------------------------------------------
@@ -352,14 +603,80 @@ HV_DEV void warp_norm_rope(const float* raw, const float* __restrict__ gain,
   __syncwarp();
 }
 
-template <typename T>
-HV_DEV T* ldg_ptr(T* const* p) {
-  return reinterpret_cast<T*>(__ldg(reinterpret_cast<const unsigned long long*>(p)));
+// Scores of one group of 4 positions tb..tb+3 for the GS heads (the arithmetic of
+// attn_chunk in attn_decode.cuh): rows below te from the slot whose first row is r0,
+// row pos from kpos_s, rows from t1 on are zero.
+template <int GS>
+HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int t0, int t1, int te, int pos,
+                         const float* slot, int r0, const float* kpos_s, float scale,
+                         float* lg_s) {
+  const int lane = threadIdx.x & 31;
+  float4 kv[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int t = tb + p;
+    if (t < te) kv[p] = reinterpret_cast<const float4*>(slot + (size_t)(t - r0) * kHd)[lane];
+    else if (t < t1 && t == pos) kv[p] = reinterpret_cast<const float4*>(kpos_s)[lane];
+    else kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float v[4 * GS];
+#pragma unroll
+  for (int p = 0; p < 4; ++p)
+#pragma unroll
+    for (int i = 0; i < GS; ++i) {
+      float s = qv[i].x * kv[p].x;
+      s = fmaf(qv[i].y, kv[p].y, s);
+      s = fmaf(qv[i].z, kv[p].z, s);
+      s = fmaf(qv[i].w, kv[p].w, s);
+      v[p * GS + i] = s;
+    }
+  int idx;
+  const float tot = halving_reduce<4 * GS>(v, lane, &idx);
+  constexpr int dup = 32 / (4 * GS);
+  if ((lane & (dup - 1)) == 0) {
+    const int p = idx / GS, i = idx % GS;
+    const int t = tb + p;
+    if (t < t1) lg_s[(t - t0) * GS + i] = tot * scale;
+  }
 }
 
+// Probability-weighted V rows of one group into acc (the order of attn_chunk).
 template <int GS>
-__device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w* L, int pos, StepShared& S,
-                       float* area) {
+HV_DEV void group_values(float4 (&acc)[GS], int tb, int t0, int t1, int te, int pos,
+                         const float* slot, int r0, const float* vpos_s, const float* lg_s) {
+  const int lane = threadIdx.x & 31;
+  float4 vv[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int t = tb + p;
+    if (t < te) vv[p] = reinterpret_cast<const float4*>(slot + (size_t)(t - r0) * kHd)[lane];
+    else if (t < t1 && t == pos) vv[p] = reinterpret_cast<const float4*>(vpos_s)[lane];
+    else vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int t = tb + p;
+    if (t < t1) {
+#pragma unroll
+      for (int i = 0; i < GS; ++i) {
+        const float w = lg_s[(t - t0) * GS + i];
+        acc[i].x = fmaf(w, vv[p].x, acc[i].x);
+        acc[i].y = fmaf(w, vv[p].y, acc[i].y);
+        acc[i].z = fmaf(w, vv[p].z, acc[i].z);
+        acc[i].w = fmaf(w, vv[p].w, acc[i].w);
+      }
+    }
+  }
+}
+
+// The attention phase: this CTA's (kv head, chunk) work items, K and V rows streamed
+// through the ring (sequence numbers from *q). Same arithmetic, in the same order, as
+// attn_chunk with eight warps (k_attn): groups of 4 positions go to warp (group % 8)
+// for the scores and the weighted V sum; warp i takes head i for the max and exp.
+template <int GS>
+__device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
+                                       const Ring& R, unsigned* qp, StepShared& S,
+                                       float* area) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
   const int chunk_max = (cap + nch - 1) / nch;
   const int lg_floats = (chunk_max * GS + 3) & ~3;   // keeps red_s 16-byte aligned
@@ -369,14 +686,21 @@ __device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w*
   float* tmp_s = vpos_s + kHd;                       // (GS + 1) x 128
   float* stat_s = tmp_s + (GS + 1) * kHd;            // 2 GS (+pad)
   float* lg_s = stat_s + 4 * GS;
-  float* red_s = lg_s + lg_floats;                  // accessed as float4
-  const int warp = threadIdx.x >> 5;
+  float* red_s = lg_s + lg_floats;                   // accessed as float4
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* cs = D.cos_t + (size_t)pos * (kHd / 2);
   const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
+  const float scale = D.attn_scale;
   for (int wi = blockIdx.x; wi < nkv * nch; wi += gridDim.x) {
     const int g = wi / nch, c = wi % nch;
+    int t0, t1, te;
+    attn_rows(pos, nch, c, &t0, &t1, &te);
+    const int n = t1 - t0;
+    const int nk = (te - t0 + kSlotRows - 1) / kSlotRows;
+    const unsigned qk = *qp, qv0 = *qp + (unsigned)nk;
+    *qp += 2u * (unsigned)nk;
     // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
-    for (int h = warp; h < GS + 2; h += kStepWarps) {
+    for (int h = warp; h < GS + 2; h += kConsWarps) {
       if (h < GS) {
         warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, ldg_ptr(&L->qn), cs, sn, D.eps,
                        tmp_s + h * kHd, q_s + h * kHd);
@@ -384,73 +708,135 @@ __device__ __noinline__ void attn_phase(const hv_step_desc& D, const hv_layer_w*
         warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, ldg_ptr(&L->kn), cs, sn, D.eps,
                        tmp_s + GS * kHd, kpos_s);
       } else {
-        const int lane = threadIdx.x & 31;
         reinterpret_cast<float4*>(vpos_s)[lane] =
             __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
       }
     }
-    __syncthreads();
-    float* kc = ldg_ptr(&L->kc) + (size_t)g * cap * kHd;
-    float* vc = ldg_ptr(&L->vc) + (size_t)g * cap * kHd;
+    csync();
     if (c == nch - 1 && threadIdx.x < kHd) {         // the chunk holding pos appends
+      float* kc = ldg_ptr(&L->kc) + (size_t)g * cap * kHd;
+      float* vc = ldg_ptr(&L->vc) + (size_t)g * cap * kHd;
       kc[(size_t)pos * kHd + threadIdx.x] = kpos_s[threadIdx.x];
       vc[(size_t)pos * kHd + threadIdx.x] = vpos_s[threadIdx.x];
     }
-    int t0, t1;
-    chunk_bounds(pos + 1, nch, c, &t0, &t1);
+
+    // ---- scores: K rows from the ring, group gi = (t - t0) / 4 to warp gi % 8
+    float4 qv[GS];
+#pragma unroll
+    for (int i = 0; i < GS; ++i) qv[i] = reinterpret_cast<const float4*>(q_s + i * kHd)[lane];
+    bool ok = true;
+    for (int m = 0; m < nk; ++m) {
+      const unsigned q = qk + (unsigned)m;
+      ok = ok && warp_wait(R.full_of(q), R.parity(q), S, D.status);
+      if (ok) {
+        const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, te);
+        const float* slot = reinterpret_cast<const float*>(R.slot(q));
+        const int g0 = m * (kSlotRows / 4), g1 = (r1 - t0 + 3) / 4;
+        for (int gi = g0 + ((warp - g0) % kConsWarps + kConsWarps) % kConsWarps; gi < g1;
+             gi += kConsWarps)
+          group_scores<GS>(qv, t0 + 4 * gi, t0, t1, te, pos, slot, r0, kpos_s, scale, lg_s);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(R.empty_of(q), 1);
+      }
+    }
+    // a group that starts at pos (no cached row in it)
+    const bool pos_group = te < t1 && ((te - t0) & 3) == 0;
+    if (pos_group && ((te - t0) / 4) % kConsWarps == warp)
+      group_scores<GS>(qv, te, t0, t1, te, pos, nullptr, te, kpos_s, scale, lg_s);
+    csync();
+
+    // ---- per-head max and exp: warp i handles head i
+    for (int i = warp; i < GS; i += kConsWarps) {
+      float mx = -INFINITY;
+      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, lg_s[t * GS + i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      float l = 0.f;
+      for (int t = lane; t < n; t += 32) {
+        const float e = (n > 0) ? expf(lg_s[t * GS + i] - mx) : 0.f;
+        lg_s[t * GS + i] = e;
+        l += e;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+      if (lane == 0) { stat_s[2 * i] = mx; stat_s[2 * i + 1] = l; }
+    }
+    csync();
+
+    // ---- probability-weighted V sum: V rows from the ring, same group -> warp map
+    float4 acc[GS];
+#pragma unroll
+    for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int m = 0; m < nk; ++m) {
+      const unsigned q = qv0 + (unsigned)m;
+      ok = ok && warp_wait(R.full_of(q), R.parity(q), S, D.status);
+      if (ok) {
+        const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, te);
+        const float* slot = reinterpret_cast<const float*>(R.slot(q));
+        const int g0 = m * (kSlotRows / 4), g1 = (r1 - t0 + 3) / 4;
+        for (int gi = g0 + ((warp - g0) % kConsWarps + kConsWarps) % kConsWarps; gi < g1;
+             gi += kConsWarps)
+          group_values<GS>(acc, t0 + 4 * gi, t0, t1, te, pos, slot, r0, vpos_s, lg_s);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(R.empty_of(q), 1);
+      }
+    }
+    if (pos_group && ((te - t0) / 4) % kConsWarps == warp)
+      group_values<GS>(acc, te, t0, t1, te, pos, nullptr, te, vpos_s, lg_s);
+#pragma unroll
+    for (int i = 0; i < GS; ++i)
+      reinterpret_cast<float4*>(red_s + ((size_t)warp * GS + i) * kHd)[lane] = acc[i];
+    csync();
     float* part = D.part + ((size_t)g * nch + c) * GS * kPartStride;
-    attn_chunk<GS>(q_s, kc, vc, t0, t1, D.attn_scale, pos, kpos_s, vpos_s, lg_s, red_s,
-                   stat_s, part);
+    for (int e = threadIdx.x; e < GS * kHd; e += kConsThreads) {
+      float s = 0.f;
+      for (int w = 0; w < kConsWarps; ++w) s += red_s[(size_t)w * GS * kHd + e];
+      const int i = e / kHd, d = e % kHd;
+      part[i * kPartStride + 4 + d] = s;
+    }
+    if (threadIdx.x < GS) {
+      part[threadIdx.x * kPartStride + 0] = (n > 0) ? stat_s[2 * threadIdx.x] : -INFINITY;
+      part[threadIdx.x * kPartStride + 1] = (n > 0) ? stat_s[2 * threadIdx.x + 1] : 0.f;
+    }
     __threadfence();
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) S.flag = (atomicAdd(D.ticket + g, 1) == nch - 1);
-    __syncthreads();
+    csync();
     if (S.flag) {
       __threadfence();
-      attn_merge<GS>(D.part + (size_t)g * nch * GS * kPartStride, nch,
-                     D.ctx + (size_t)g * GS * kHd, red_s);
+      attn_merge<GS, CSync>(D.part + (size_t)g * nch * GS * kPartStride, nch,
+                            D.ctx + (size_t)g * GS * kHd, red_s);
       if (threadIdx.x == 0) D.ticket[g] = 0;
     }
-    __syncthreads();
-  }
-}
-
-// L2 prefetch (one thread) of the K and V rows this CTA's attention work items read.
-HV_DEV void prefetch_kv(const hv_step_desc& D, const hv_layer_w* L, int pos) {
-  if (threadIdx.x != 0) return;
-  const int nch = D.attn_chunks;
-  const float* kc = ldg_ptr(&L->kc);
-  const float* vc = ldg_ptr(&L->vc);
-  for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
-    const int g = wi / nch, c = wi % nch;
-    int t0, t1;
-    chunk_bounds(pos + 1, nch, c, &t0, &t1);
-    if (t1 <= t0) continue;
-    const size_t off = ((size_t)g * D.cap + t0) * kHd;
-    prefetch_l2(kc + off, (size_t)(t1 - t0) * kHd * 4);
-    prefetch_l2(vc + off, (size_t)(t1 - t0) * kHd * 4);
+    csync();
   }
 }
 
 // ---- the kernel ------------------------------------------------------------------------
 
 template <int GS>
-__global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  StepShared& S = *reinterpret_cast<StepShared*>(smem);
-  float* area = reinterpret_cast<float*>(smem + ((sizeof(StepShared) + 15) & ~size_t(15)));
+__global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
+                                                          int nslots) {
+  extern __shared__ __align__(128) unsigned char smem[];
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
-  const int kmax = max(max(hid, qdim), ffn);
-  uint4* q_s = reinterpret_cast<uint4*>(area);
-  int2* sb_s = reinterpret_cast<int2*>(reinterpret_cast<unsigned char*>(area) + kmax);
-  // every region starts on a 16-byte boundary (float4 / int4 accesses)
-  float* x_s = reinterpret_cast<float*>(
-      reinterpret_cast<unsigned char*>(area) + (((size_t)kmax + (kmax / kBlock) * 8 + 15) & ~size_t(15)));
-  float* sq_s = x_s + hid;
-  float* leaf_s = sq_s + hid;             // block terms of split GEMV phases
+  const StepLayout Lo = step_layout(GS, hid, qdim, ffn, D.cap, D.attn_chunks, nslots);
+  StepShared& S = *reinterpret_cast<StepShared*>(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lo.bars);
+  uint4* q_s = reinterpret_cast<uint4*>(smem + Lo.act_q);
+  int2* sb_s = reinterpret_cast<int2*>(smem + Lo.act_sb);
+  float* work = reinterpret_cast<float*>(smem + Lo.work);
+  const Ring R{smem + Lo.ring, bars, bars + kMaxSlots, nslots};
   const ActView act{q_s, sb_s};
 
   trace_mark(D, 0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nslots; ++i) {
+      mbar_init(R.full + i, 1);
+      mbar_init(R.empty + i, kConsWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    S.abort = 0;
+  }
   {
     const int* src = reinterpret_cast<const int*>(D.plans);
     int* dst = reinterpret_cast<int*>(&S.P);
@@ -460,89 +846,88 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   const int tok = *D.tok;
   __syncthreads();
   if (pos < 0 || pos >= D.cap || tok < 0 || tok >= D.vocab) {
-    // every CTA reads the same values, so all leave here, before the first barrier
+    // every CTA reads the same values, so all leave here, before any copy or barrier
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(D.status, HV_E_INVALID);
     return;
   }
+  if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
+    if (threadIdx.x == kConsThreads) produce(D, flags, pos, R, S);
+    return;
+  }
 
-  // this CTA's tiles of every matrix; o and down share N = hidden, so the CTA that adds
-  // into h[row] is always the one that last wrote it
+  // ---- consumers
   const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
-  int qt0, qt1, ht0, ht1, gt0, gt1;
-  row_range(pp_tiles(nqkv, 0), &qt0, &qt1);
-  row_range(pp_tiles(hid, 0), &ht0, &ht1);
-  row_range(pp_tiles(2 * ffn, ffn), &gt0, &gt1);
-  const int hr0 = ht0 * 8, hr1 = min(ht1 * 8, hid);
   const __half* emb_row = reinterpret_cast<const __half*>(D.emb16) + (size_t)tok * hid;
-  for (int i = hr0 + threadIdx.x; i < hr1; i += blockDim.x) D.h[i] = __half2float(emb_row[i]);
-
-  prefetch_tiles(ldg_ptr(&D.layers[0].qkv_b4), ldg_ptr(&D.layers[0].qkv_sw), hid, qt0, qt1);
+  {
+    const int r0 = (int)(((long long)blockIdx.x * hid) / gridDim.x);
+    const int r1 = (int)(((long long)(blockIdx.x + 1) * hid) / gridDim.x);
+    for (int i = r0 + threadIdx.x; i < r1; i += kConsThreads) D.h[i] = __half2float(emb_row[i]);
+  }
+  const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
+            it_ffn = pp_iters(ffn / kBlock);
+  unsigned q = 0;
+  int off = 0, t0, t1;
   trace_mark(D, 1);
   for (int l = 0; l < D.n_layer; ++l) {
     const hv_layer_w* L = D.layers + l;
     const int tb = 2 + 14 * l;
     // P1: qkv
-    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, ldg_ptr(&L->an), hid, D.eps, S, x_s, sq_s,
-                   q_s, sb_s);
+    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, ldg_ptr(&L->an), hid, D.eps, S, work, q_s,
+                   sb_s);
     trace_mark(D, tb + 0);
-    gemv_phase<kStore>(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), S.P.gv_hid, act, qt0, qt1, nqkv,
-                       0, D.qkv, nullptr, nullptr, leaf_s);
+    phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
+    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, D.qkv, nullptr, nullptr, S,
+                      D.status);
+    q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
-    prefetch_kv(D, L, pos);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 2);
     // P2: attention
-    attn_phase<GS>(D, L, pos, S, area);
+    attn_ring<GS>(D, L, pos, R, &q, S, work);
     trace_mark(D, tb + 3);
-    prefetch_tiles(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), qdim, ht0, ht1);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 4);
     // P3: o projection + residual
     pro_quant(D.ctx, qdim, q_s, sb_s);
     trace_mark(D, tb + 5);
-    gemv_phase<kResidual>(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), S.P.gv_o, act, ht0, ht1, hid, 0,
-                          D.h, nullptr, nullptr, leaf_s);
+    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hid, 0, D.h, nullptr, nullptr, S,
+                         D.status);
+    q += (unsigned)((t1 - t0) * slots_per_tile(it_q));
     trace_mark(D, tb + 6);
-    prefetch_tiles(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), hid, gt0, gt1);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
-    pro_norm_quant(D.h, nullptr, ldg_ptr(&L->fn), hid, D.eps, S, x_s, sq_s, q_s, sb_s);
+    pro_norm_quant(D.h, nullptr, ldg_ptr(&L->fn), hid, D.eps, S, work, q_s, sb_s);
     trace_mark(D, tb + 8);
-    gemv_phase<kSiluPair>(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), S.P.gv_hid, act, gt0, gt1,
-                          2 * ffn, ffn, D.act, nullptr, nullptr, leaf_s);
+    phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
+    gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, D.act, nullptr, nullptr,
+                         S, D.status);
+    q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 9);
-    prefetch_tiles(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), ffn, ht0, ht1);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 10);
     // P5: down + residual
     pro_quant(D.act, ffn, q_s, sb_s);
     trace_mark(D, tb + 11);
-    gemv_phase<kResidual>(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), S.P.gv_ffn, act, ht0, ht1, hid,
-                          0, D.h, nullptr, nullptr, leaf_s);
+    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hid, 0, D.h, nullptr, nullptr, S,
+                         D.status);
+    q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
-    if (l + 1 < D.n_layer) {
-      prefetch_tiles(ldg_ptr(&D.layers[l + 1].qkv_b4), ldg_ptr(&D.layers[l + 1].qkv_sw), hid,
-                     qt0, qt1);
-    } else if (flags & HV_STEP_HEAD) {
-      int a0, a1;
-      row_range(pp_tiles(D.head_rows, 0), &a0, &a1);
-      prefetch_tiles(D.head_b4, D.head_sw, hid, a0, min(a1, a0 + 8));
-    }
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 13);
   }
 
   if (!(flags & HV_STEP_HEAD)) return;
   const int th = 2 + 14 * D.n_layer;
-  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, x_s, sq_s, q_s, sb_s);
+  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s);
   trace_mark(D, th + 0);
-  int a0, a1;
-  row_range(pp_tiles(D.head_rows, 0), &a0, &a1);
+  phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
-  gemv_phase<kHead>(D.head_b4, D.head_sw, S.P.gv_hid, act, a0, a1, D.head_rows, 0, D.logits, &bv,
-                    &bi, leaf_s);
+  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, D.logits, &bv, &bi, S,
+                   D.status);
   trace_mark(D, th + 1);
   if (!(flags & HV_STEP_ARGMAX)) return;
 
@@ -556,9 +941,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if (lane == 0) { S.sv[warp] = bv; S.si[warp] = bi; }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
-      for (int w = 1; w < kStepWarps; ++w)
+      for (int w = 1; w < kConsWarps; ++w)
         if (S.sv[w] > S.sv[0] || (S.sv[w] == S.sv[0] && S.si[w] < S.si[0])) {
           S.sv[0] = S.sv[w];
           S.si[0] = S.si[w];
@@ -568,7 +953,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       __threadfence();
       S.flag = (atomicAdd(D.ticket + D.n_kv, 1) == (int)gridDim.x - 1);
     }
-    __syncthreads();
+    csync();
     if (S.flag && threadIdx.x == 0) {
       __threadfence();
       float v = -INFINITY;
@@ -589,27 +974,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   trace_mark(D, th + 2);
 }
 
-template <int GS>
-static size_t step_smem(int hid, int qdim, int ffn, int cap, int nch) {
-  const int kmax = std::max(std::max(hid, qdim), ffn);
-  const size_t gemv = (((size_t)kmax + (size_t)(kmax / kBlock) * 8 + 15) & ~size_t(15)) +
-                      2 * (size_t)hid * 4 + (size_t)kCBufFloats * 4;
-  const int chunk_max = (cap + nch - 1) / nch;
-  const size_t lg_floats = ((size_t)chunk_max * GS + 3) & ~size_t(3);
-  const size_t attn = sizeof(float) * ((size_t)GS * kHd + 2 * kHd + (GS + 1) * kHd + 4 * GS +
-                                       lg_floats + (size_t)kStepWarps * GS * kHd);
-  return ((sizeof(StepShared) + 15) & ~size_t(15)) + std::max(gemv, attn);
-}
-
-static size_t step_smem_any(int gs, int hid, int qdim, int ffn, int cap, int nch) {
-  switch (gs) {
-    case 1: return step_smem<1>(hid, qdim, ffn, cap, nch);
-    case 2: return step_smem<2>(hid, qdim, ffn, cap, nch);
-    case 4: return step_smem<4>(hid, qdim, ffn, cap, nch);
-    default: return step_smem<8>(hid, qdim, ffn, cap, nch);
-  }
-}
-
 static void* step_fn(int gs) {
   switch (gs) {
     case 1: return (void*)k_step<1>;
@@ -617,6 +981,14 @@ static void* step_fn(int gs) {
     case 4: return (void*)k_step<4>;
     default: return (void*)k_step<8>;
   }
+}
+
+// Ring slots that fit next to the fixed regions (0 if the fixed regions alone do not).
+static int step_slots(int gs, int hid, int qdim, int ffn, int cap, int nch) {
+  const StepLayout L = step_layout(gs, hid, qdim, ffn, cap, nch, 0);
+  if (L.ring >= (size_t)kSmemLimit) return 0;
+  const int n = (int)(((size_t)kSmemLimit - L.ring) / kSlotBytes);
+  return n > kMaxSlots ? kMaxSlots : n;
 }
 
 }  // namespace hv
@@ -674,11 +1046,17 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(h.hidden <= kMaxHidden, HV_E_UNSUPPORTED, "hv_step_launch: hidden %d > %d",
              h.hidden, kMaxHidden);
   HV_REQUIRE(h.plans != nullptr, HV_E_INVALID, "hv_step_launch: plans not set (hv_step_plans)");
+  HV_REQUIRE(h.attn_chunks > 0 && 2 * h.attn_chunks + 1 <= kConsWarps * kHd, HV_E_INVALID,
+             "hv_step_launch: attn_chunks %d outside [1, %d]", h.attn_chunks,
+             (kConsWarps * kHd - 1) / 2);
   const int gs = h.n_head / h.n_kv;
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
-  const size_t smem = step_smem_any(gs, h.hidden, h.n_head * kHd, h.ffn, h.cap, h.attn_chunks);
-  HV_REQUIRE(smem <= 227 * 1024, HV_E_UNSUPPORTED, "hv_step_launch: needs %zu B of smem", smem);
+  const int qdim = h.n_head * kHd;
+  const int nslots = step_slots(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks);
+  HV_REQUIRE(nslots >= 4, HV_E_UNSUPPORTED,
+             "hv_step_launch: shared memory leaves %d ring slots (need 4)", nslots);
+  const size_t smem = step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots).total;
   void* fn = step_fn(gs);
   {
     // set the function's shared-memory limit once per (group size, device, size)
@@ -696,7 +1074,7 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   int sms = 0;
   int rc = sm_count(&sms);
   if (rc) return rc;
-  void* args[] = {(void*)&h, (void*)&flags};
+  void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots};
   HV_CUDA(cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kStepThreads), args, smem,
                                       (cudaStream_t)stream));
   return HV_OK;

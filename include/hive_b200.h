@@ -192,8 +192,10 @@ int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,
  * (:374-419) and, with HV_STEP_HEAD|HV_STEP_ARGMAX, the LM head and
  * _argmax_into_next() (:421-428): every layer's RMSNorm, quantisation, GEMVs, q/k norm,
  * RoPE, KV append, attention, SiLU and residual adds, then greedy argmax that advances
- * tok/pos/step on the device. One CTA per SM; phases are separated by grid barriers
- * whose waits are bounded (HV_E_TIMEOUT, with *status set, instead of a hang). A
+ * tok/pos/step on the device. One CTA per SM: a producer warp streams the CTA's weight
+ * tiles and KV rows into a shared-memory ring with bulk copies while eight consumer
+ * warps compute; phases are separated by grid barriers. Every wait (barrier or ring
+ * slot) is bounded (HV_E_TIMEOUT, with *status set, instead of a hang). A
  * launch whose *pos is outside [0, cap) or *tok outside [0, vocab) does nothing but set
  * *status = HV_E_INVALID. The host reads *status after synchronising; after a nonzero
  * status, zero `barrier`, `ticket` and `status` before the next launch.
