@@ -59,6 +59,12 @@ constexpr unsigned long long kProducerWaitNs = 4000000000ull;  // producer waits
 static_assert(kSlotScaleOff + kSlotIters * kPpScales * 4 == kSlotBytes, "slot layout");
 static_assert(kSlotRows % 4 == 0, "attention groups of 4 rows never straddle slots");
 
+// Run-time tunables (hv_step_set_option): bulk copies a producer keeps in flight, and
+// whether streamed bytes are marked evict-first in L2. Copies beyond what saturates HBM
+// only queue in front of the consumers' own (latency-critical) loads.
+static int g_opt_inflight = 6;
+static int g_opt_evict_first = 1;
+
 using CSync = SyncNamed<kConsThreads, 1>;
 HV_DEV void csync() { CSync::sync(); }
 
@@ -133,11 +139,34 @@ HV_DEV bool mbar_test(uint64_t* b, unsigned parity) {
                : "=r"(ok) : "r"(sm_addr(b)), "r"(parity) : "memory");
   return ok != 0;
 }
+// The same test, but a thread whose phase has not completed is suspended (up to
+// hint_ns) until it does, instead of spinning on the issue slots other warps need.
+HV_DEV bool mbar_test_sleep(uint64_t* b, unsigned parity, unsigned hint_ns) {
+  unsigned ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(sm_addr(b)), "r"(parity), "r"(hint_ns) : "memory");
+  return ok != 0;
+}
 // global -> this CTA's shared memory, `bytes` (multiple of 16, both addresses 16-byte
 // aligned), completion counted on mbarrier `bar`
 HV_DEV void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                :: "r"(sm_addr(dst)), "l"(src), "r"(bytes), "r"(sm_addr(bar)) : "memory");
+}
+// the same with an L2 cache policy (createpolicy)
+HV_DEV void bulk_load_hint(void* dst, const void* src, unsigned bytes, uint64_t* bar,
+                           unsigned long long policy) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+               " [%0], [%1], %2, [%3], %4;"
+               :: "r"(sm_addr(dst)), "l"(src), "r"(bytes), "r"(sm_addr(bar)), "l"(policy)
+               : "memory");
+}
+HV_DEV unsigned long long policy_evict_first() {
+  unsigned long long p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 HV_DEV unsigned ld_acquire(const unsigned* p) {
@@ -160,9 +189,9 @@ HV_DEV bool mbar_wait(uint64_t* b, unsigned parity, StepShared& S, int* status,
   if (mbar_test(b, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (unsigned n = 0;; ++n) {
-    if (mbar_test(b, parity)) return true;
+    if (mbar_test_sleep(b, parity, 20000u)) return true;
     if (*(volatile int*)&S.abort) return false;
-    if ((n & 63) == 63 && *(volatile int*)status != 0) break;
+    if ((n & 7) == 7 && *(volatile int*)status != 0) break;
     if (global_ns() - t0 > limit) {
       atomicCAS(status, 0, HV_E_TIMEOUT);
       break;
@@ -259,19 +288,42 @@ HV_DEV T* ldg_ptr(T* const* p) {
   return reinterpret_cast<T*>(__ldg(reinterpret_cast<const unsigned long long*>(p)));
 }
 
+// L2 prefetch (one thread) of a layer's small vectors a phase before they are needed:
+// the input norm and the q/k norms (attn) or the post-attention norm. The weights and
+// KV rows go through the ring; these few KB would otherwise be demand misses on the
+// critical path.
+HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
+  if (attn) {
+    prefetch_l2(ldg_ptr(&L->an), (size_t)hid * 4);
+    prefetch_l2(ldg_ptr(&L->qn), kHd * 4);
+    prefetch_l2(ldg_ptr(&L->kn), kHd * 4);
+  } else {
+    prefetch_l2(ldg_ptr(&L->fn), (size_t)hid * 4);
+  }
+}
+
 // ---- the producer ----------------------------------------------------------------------
 
 struct Producer {
   const Ring& R;
   StepShared& S;
   int* status;
+  unsigned inflight;             // copies allowed in flight (<= ring slots)
+  bool hint;
+  unsigned long long policy;
   unsigned q = 0;
   bool live = true;
 
-  HV_DEV Producer(const Ring& r, StepShared& s, int* st) : R(r), S(s), status(st) {}
+  HV_DEV Producer(const Ring& r, StepShared& s, int* st, int infl, int evict_first)
+      : R(r), S(s), status(st) {
+    inflight = (unsigned)max(1, min(infl, r.ns));
+    hint = evict_first != 0;
+    policy = hint ? policy_evict_first() : 0ull;
+  }
 
-  // Claims the next slot (waiting until its previous contents were released) and
-  // starts up to two copies into it.
+  // Claims the next slot (waiting until its previous contents were released and until
+  // fewer than `inflight` earlier copies are still in flight) and starts up to two
+  // copies into it.
   HV_DEV void issue(const void* a, unsigned na, const void* b, unsigned nb_, unsigned b_off) {
     if (!live) return;
     if (q >= (unsigned)R.ns &&
@@ -279,11 +331,23 @@ struct Producer {
       live = false;
       return;
     }
+    if (q >= inflight) {
+      const unsigned p = q - inflight;
+      if (!mbar_wait(R.full_of(p), R.parity(p), S, status, kProducerWaitNs)) {
+        live = false;
+        return;
+      }
+    }
     unsigned char* dst = R.slot(q);
     uint64_t* full = R.full_of(q);
     mbar_arrive_tx(full, na + nb_);
-    bulk_load(dst, a, na, full);
-    if (nb_) bulk_load(dst + b_off, b, nb_, full);
+    if (hint) {
+      bulk_load_hint(dst, a, na, full, policy);
+      if (nb_) bulk_load_hint(dst + b_off, b, nb_, full, policy);
+    } else {
+      bulk_load(dst, a, na, full);
+      if (nb_) bulk_load(dst + b_off, b, nb_, full);
+    }
     ++q;
   }
 
@@ -324,8 +388,9 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
     }
 }
 
-HV_DEV void produce(const hv_step_desc& D, int flags, int pos, const Ring& R, StepShared& S) {
-  Producer P(R, S, D.status);
+HV_DEV void produce(const hv_step_desc& D, int flags, int pos, const Ring& R, StepShared& S,
+                    int inflight, int evict_first) {
+  Producer P(R, S, D.status, inflight, evict_first);
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
   const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
   const int nch = D.attn_chunks;
@@ -474,101 +539,107 @@ HV_DEV void gemv_epilogue(float y, int row, bool ok, float* __restrict__ out, fl
   }
 }
 
-// numpy's pairwise chains of one row, walked iteration by iteration (the order of
-// chains_fold in gemv_mma.cuh): leaves of eight strided accumulators, the lane's two
-// accumulators 2t, 2t+1 folded across the quad at each leaf end, the recursion's '+'
-// in postfix order, the n % 8 tail in order at the very end.
-struct Chain {
-  float st[8];
-  int sp, leaf, leaf_begin;
-  float ae, ao;
-};
-
-HV_DEV void chain_step(Chain& c, const GvPlan& P, int it, float2 v) {
-  if (it == c.leaf_begin) {
-    c.ae = v.x;
-    c.ao = v.y;
-  } else {
-    c.ae = __fadd_rn(c.ae, v.x);
-    c.ao = __fadd_rn(c.ao, v.y);
-  }
-  if (it + 1 == P.it_end[c.leaf] && c.leaf + 1 < P.nleaf) {
-    c.st[c.sp++] = quad_fold(c.ae, c.ao);
-    for (int k = 0; k < P.pops[c.leaf]; ++k) {
-      --c.sp;
-      c.st[c.sp - 1] = __fadd_rn(c.st[c.sp - 1], c.st[c.sp]);
-    }
-    c.leaf_begin = P.it_end[c.leaf];
-    ++c.leaf;
-  }
+// Block terms of iteration u of a ring slot for the lane's row g: blocks 2t (x) and
+// 2t+1 (y) of logical iteration `it`; nvalid < 8 only for the tail iteration.
+HV_DEV float2 slot_terms(const unsigned char* sl, int u, const unsigned* __restrict__ act_w,
+                         const int2* __restrict__ sb, int it, int g, int t, int lane,
+                         int nvalid) {
+  const uint32_t* nw = reinterpret_cast<const uint32_t*>(sl);
+  const float* sw = reinterpret_cast<const float*>(sl + kSlotScaleOff);
+  MmaLoads L;
+  const uint4 a = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 4 * lane);
+  const uint4 b = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 128 + 4 * lane);
+  L.w[0] = a.x; L.w[1] = a.y; L.w[2] = a.z; L.w[3] = a.w;
+  L.w[4] = b.x; L.w[5] = b.y; L.w[6] = b.z; L.w[7] = b.w;
+  L.s = *reinterpret_cast<const float2*>(sw + u * kPpScales + 2 * lane);
+  return iter_terms(L, act_w, sb, it, g, t, nvalid);
 }
 
-HV_DEV float chain_finish(Chain& c, const GvPlan& P, float2 tail) {
-  const int lane = threadIdx.x & 31;
-  float v = (P.nfull > c.leaf_begin) ? quad_fold(c.ae, c.ao) : 0.f;
-  for (int j = 0; j < P.ntail; ++j) {
-    const float x = __shfl_sync(0xFFFFFFFFu, (j & 1) ? tail.y : tail.x, (lane & ~3) | (j >> 1));
-    v = __fadd_rn(v, x);
-  }
-  c.st[c.sp++] = v;
-  for (int k = 0; k < P.pops[P.nleaf - 1]; ++k) {
-    --c.sp;
-    c.st[c.sp - 1] = __fadd_rn(c.st[c.sp - 1], c.st[c.sp]);
-  }
-  return __fadd_rn(0.0f, c.st[0]);
-}
-
-// The CTA's tiles [t0, t1) of one GEMV phase, their slots starting at sequence number
-// q0: warp w takes tiles w, w + 8, ... and walks each tile's slots in order. MODE
-// kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate rows
-// (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
+// The CTA's tiles [t0, t1) of one GEMV phase, their slots starting at sequence number q0.
+// Work items are (tile, leaf of numpy's pairwise recursion), tile-major like the ring;
+// item k goes to warp k % 8, so every warp has work even when the CTA has few tiles
+// (leaves are independent chains). An item walks its leaf's eight strided accumulators
+// (the lane's 2t, 2t+1) with no branch per iteration, folds them across the quad
+// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) and, in the last leaf, adds the n % 8 tail in order.
+// Single-leaf rows finish in the item; otherwise leaf values meet in `leafbuf` and one
+// warp per tile folds them with the recursion's '+' (fold_leaves). A slot shared by two
+// items (a leaf boundary inside it) gets half the release count from each.
+// MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate
+// rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
 // rows per half; SiLU(gate) * up is formed in the lane that holds the gate row.
 template <int MODE>
 __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan& P,
                                        const ActView act, int t0, int t1, int rows,
                                        int pair_ffn, float* __restrict__ out, float* best_v,
-                                       int* best_i, StepShared& S, int* status) {
+                                       int* best_i, float* leafbuf, StepShared& S,
+                                       int* status) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int warp = threadIdx.x >> 5;
   const int niter = pp_iters(P.nb);
   const int spt = slots_per_tile(niter);
+  const int nleaf = P.nleaf, nfull = P.nfull, ntail = P.ntail;
+  const int nitems = (t1 - t0) * nleaf;
   const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
-  for (int lt = warp; lt < t1 - t0; lt += kConsWarps) {
-    Chain c;
-    c.sp = 0;
-    c.leaf = 0;
-    c.leaf_begin = 0;
-    c.ae = c.ao = 0.f;
+  bool failed = false;
+  for (int k = warp; k < nitems && !failed; k += kConsWarps) {
+    const int lt = k / nleaf, lf = k - lt * nleaf;
+    const int ia = lf == 0 ? 0 : P.it_end[lf - 1];
+    const int ib = lf == nleaf - 1 ? niter : P.it_end[lf];   // the last leaf owns the tail
+    const int ifull = min(ib, nfull);
+    float ae = 0.f, ao = 0.f;
     float2 tail = make_float2(0.f, 0.f);
-    for (int j = 0; j < spt; ++j) {
-      const unsigned q = q0 + (unsigned)(lt * spt + j);
-      if (!warp_wait(R.full_of(q), R.parity(q), S, status)) return;
-      const unsigned char* sl = R.slot(q);
-      const uint32_t* nw = reinterpret_cast<const uint32_t*>(sl);
-      const float* sw = reinterpret_cast<const float*>(sl + kSlotScaleOff);
-      const int it0 = j * kSlotIters;
-      const int n = min(kSlotIters, niter - it0);
-#pragma unroll 4
-      for (int u = 0; u < n; ++u) {
-        MmaLoads L;
-        const uint4 a = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 4 * lane);
-        const uint4 b = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 128 + 4 * lane);
-        L.w[0] = a.x; L.w[1] = a.y; L.w[2] = a.z; L.w[3] = a.w;
-        L.w[4] = b.x; L.w[5] = b.y; L.w[6] = b.z; L.w[7] = b.w;
-        L.s = *reinterpret_cast<const float2*>(sw + u * kPpScales + 2 * lane);
-        const int it = it0 + u;
-        if (it < P.nfull) {
-          chain_step(c, P, it, iter_terms(L, act_w, act.sb, it, g, t, 8));
-        } else {
-          tail = iter_terms(L, act_w, act.sb, it, g, t, P.ntail);
-        }
+    for (int s0 = ia - ia % kSlotIters; s0 < ib; s0 += kSlotIters) {
+      const int s1 = min(s0 + kSlotIters, niter);
+      const unsigned q = q0 + (unsigned)(lt * spt + s0 / kSlotIters);
+      if (!warp_wait(R.full_of(q), R.parity(q), S, status)) {
+        failed = true;
+        break;
       }
+      const unsigned char* sl = R.slot(q);
+      const int a = max(ia, s0), bb = min(ib, s1), bf = min(bb, ifull);
+      int it = a;
+      if (it == ia && it < bf) {                     // a leaf starts with an assignment
+        const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
+        ae = v.x;
+        ao = v.y;
+        ++it;
+      }
+#pragma unroll 4
+      for (; it < bf; ++it) {
+        const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
+        ae = __fadd_rn(ae, v.x);
+        ao = __fadd_rn(ao, v.y);
+      }
+      if (bb > bf) tail = slot_terms(sl, bf - s0, act_w, act.sb, bf, g, t, lane, ntail);
       __syncwarp();
-      if (lane == 0) mbar_arrive_n(R.empty_of(q), kConsWarps);
+      const bool shared = ia > s0 || ib < s1;
+      if (lane == 0) mbar_arrive_n(R.empty_of(q), shared ? kConsWarps / 2 : kConsWarps);
     }
-    bool ok;
-    const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
-    gemv_epilogue<MODE>(chain_finish(c, P, tail), row, ok, out, best_v, best_i);
+    if (failed) break;
+    float v = (ifull > ia) ? quad_fold(ae, ao) : 0.f;
+    if (lf == nleaf - 1) {
+      for (int j = 0; j < ntail; ++j) {
+        const float x =
+            __shfl_sync(0xFFFFFFFFu, (j & 1) ? tail.y : tail.x, (lane & ~3) | (j >> 1));
+        v = __fadd_rn(v, x);
+      }
+    }
+    if (nleaf == 1) {
+      bool ok;
+      const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      gemv_epilogue<MODE>(__fadd_rn(0.0f, v), row, ok, out, best_v, best_i);
+    } else if (t == 0) {
+      leafbuf[((size_t)lt * 8 + g) * nleaf + lf] = v;
+    }
+  }
+  if (nleaf > 1) {
+    csync();
+    for (int lt = warp; lt < t1 - t0 && !failed; lt += kConsWarps) {
+      bool ok;
+      const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      const float y = fold_leaves(P, leafbuf + ((size_t)lt * 8 + g) * nleaf);
+      gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
+    }
   }
 }
 
@@ -816,7 +887,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
 
 template <int GS>
 __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
-                                                          int nslots) {
+                                                          int nslots, int inflight,
+                                                          int evict_first) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
   const StepLayout Lo = step_layout(GS, hid, qdim, ffn, D.cap, D.attn_chunks, nslots);
@@ -851,7 +923,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     return;
   }
   if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
-    if (threadIdx.x == kConsThreads) produce(D, flags, pos, R, S);
+    if (threadIdx.x == kConsThreads) produce(D, flags, pos, R, S, inflight, evict_first);
     return;
   }
 
@@ -867,6 +939,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
             it_ffn = pp_iters(ffn / kBlock);
   unsigned q = 0;
   int off = 0, t0, t1;
+  if (threadIdx.x == 0) prefetch_vectors(D.layers, hid, true);
   trace_mark(D, 1);
   for (int l = 0; l < D.n_layer; ++l) {
     const hv_layer_w* L = D.layers + l;
@@ -876,8 +949,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
                    sb_s);
     trace_mark(D, tb + 0);
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
-    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, D.qkv, nullptr, nullptr, S,
-                      D.status);
+    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, D.qkv, nullptr, nullptr, work,
+                      S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
     if (!grid_sync(D.barrier, D.status, S)) return;
@@ -887,12 +960,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 3);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 4);
+    if (threadIdx.x == 0) prefetch_vectors(L, hid, false);
     // P3: o projection + residual
     pro_quant(D.ctx, qdim, q_s, sb_s);
     trace_mark(D, tb + 5);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hid, 0, D.h, nullptr, nullptr, S,
-                         D.status);
+    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
+                         S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_q));
     trace_mark(D, tb + 6);
     if (!grid_sync(D.barrier, D.status, S)) return;
@@ -902,17 +976,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 8);
     phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
     gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, D.act, nullptr, nullptr,
-                         S, D.status);
+                         work, S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 9);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 10);
+    if (threadIdx.x == 0) {
+      if (l + 1 < D.n_layer) prefetch_vectors(L + 1, hid, true);
+      else prefetch_l2(D.onorm, (size_t)hid * 4);
+    }
     // P5: down + residual
     pro_quant(D.act, ffn, q_s, sb_s);
     trace_mark(D, tb + 11);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hid, 0, D.h, nullptr, nullptr, S,
-                         D.status);
+    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
+                         S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
     if (!grid_sync(D.barrier, D.status, S)) return;
@@ -926,8 +1004,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
-  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, D.logits, &bv, &bi, S,
-                   D.status);
+  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, D.logits, &bv, &bi, work,
+                   S, D.status);
   trace_mark(D, th + 1);
   if (!(flags & HV_STEP_ARGMAX)) return;
 
@@ -1037,6 +1115,21 @@ int hv_step_plans_bytes(size_t* bytes) {
   return HV_OK;
 }
 
+int hv_step_set_option(int option, int value) {
+  switch (option) {
+    case HV_STEP_OPT_INFLIGHT:
+      HV_REQUIRE(value >= 1 && value <= kMaxSlots, HV_E_INVALID,
+                 "hv_step_set_option: in-flight copies %d outside [1, %d]", value, kMaxSlots);
+      g_opt_inflight = value;
+      return HV_OK;
+    case HV_STEP_OPT_EVICT_FIRST:
+      g_opt_evict_first = value != 0;
+      return HV_OK;
+    default:
+      HV_REQUIRE(false, HV_E_INVALID, "hv_step_set_option: unknown option %d", option);
+  }
+}
+
 int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(desc, HV_E_INVALID, "hv_step_launch: null descriptor");
   hv_step_desc h = *desc;
@@ -1056,7 +1149,26 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const int nslots = step_slots(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks);
   HV_REQUIRE(nslots >= 4, HV_E_UNSUPPORTED,
              "hv_step_launch: shared memory leaves %d ring slots (need 4)", nslots);
-  const size_t smem = step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots).total;
+  const StepLayout lay = step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots);
+  const size_t smem = lay.total;
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  {
+    // multi-leaf GEMV rows meet in the work area: tiles per CTA x 8 rows x leaves
+    const int nqkv = (h.n_head + 2 * h.n_kv) * kHd;
+    const int tiles[5] = {pp_tiles(nqkv, 0), pp_tiles(h.hidden, 0), pp_tiles(2 * h.ffn, h.ffn),
+                          pp_tiles(h.hidden, 0), pp_tiles(h.head_rows, 0)};
+    const int ks[5] = {h.hidden, qdim, h.hidden, h.ffn, h.hidden};
+    for (int i = 0; i < 5; ++i) {
+      GvPlan gp;
+      HV_REQUIRE(gv_make_plan(ks[i] / kBlock, &gp), HV_E_UNSUPPORTED,
+                 "hv_step_launch: K = %d has too many pairwise leaves", ks[i]);
+      const size_t need = (size_t)((tiles[i] + sms - 1) / sms) * 8 * gp.nleaf * 4;
+      HV_REQUIRE(gp.nleaf == 1 || need <= lay.ring - lay.work, HV_E_UNSUPPORTED,
+                 "hv_step_launch: %zu B of leaf values exceed the work area", need);
+    }
+  }
   void* fn = step_fn(gs);
   {
     // set the function's shared-memory limit once per (group size, device, size)
@@ -1071,10 +1183,9 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
       if (dev >= 0 && dev < 64) done[gi][dev] = smem;
     }
   }
-  int sms = 0;
-  int rc = sm_count(&sms);
-  if (rc) return rc;
-  void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots};
+  int inflight = g_opt_inflight, evict_first = g_opt_evict_first;
+  void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots, (void*)&inflight,
+                  (void*)&evict_first};
   HV_CUDA(cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kStepThreads), args, smem,
                                       (cudaStream_t)stream));
   return HV_OK;

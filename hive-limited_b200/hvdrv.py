@@ -95,6 +95,7 @@ _SIGS = {
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
+    "hv_step_set_option": [_I, _I],
     "hv_step_plans_bytes": [C.POINTER(_SZ)],
     "hv_step_plans": [_I, _I, _I, _VP, _SZ],
 }
@@ -372,6 +373,16 @@ def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
 
 def attn_reserve(nkv, group, cap):
     _call("hv_attn_reserve", nkv, group, cap)
+
+
+STEP_OPT_INFLIGHT = 1
+STEP_OPT_EVICT_FIRST = 2
+
+
+def step_set_option(option, value):
+    """Tuning of the fused step (bulk copies in flight per SM, L2 evict-first streaming);
+    results do not change."""
+    _call("hv_step_set_option", int(option), int(value))
 
 
 def attn_decode_noalloc(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
