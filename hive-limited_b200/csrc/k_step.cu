@@ -57,6 +57,7 @@ constexpr unsigned long long kWaitNs = 2000000000ull;          // consumer waits
 constexpr unsigned long long kProducerWaitNs = 4000000000ull;  // producer waits: 4 s
 
 static_assert(kSlotScaleOff + kSlotIters * kPpScales * 4 == kSlotBytes, "slot layout");
+static_assert(sizeof(hv_layer_w) % 8 == 0, "layer table copied as 8-byte words");
 static_assert(kSlotRows % 4 == 0, "attention groups of 4 rows never straddle slots");
 
 // Run-time tunables (hv_step_set_option): bulk copies a producer keeps in flight, and
@@ -84,11 +85,13 @@ struct StepShared {
   int flag;
   int ok;
   int abort;                     // set by any warp of this CTA whose wait gave up
+  unsigned phase;                // top bit of the grid barrier counter to wait for next
+  unsigned long long wait[kConsWarps];   // ns each consumer warp waited for ring slots
 };
 
 // Byte offsets of the dynamic shared memory regions (host and device agree).
 struct StepLayout {
-  size_t bars, act_q, act_sb, work, ring, total;
+  size_t layers, bars, act_q, act_sb, work, ring, total;
 };
 
 HV_HD size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -100,10 +103,12 @@ HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
          (size_t)kConsWarps * gs * kHd;
 }
 
-HV_HD StepLayout step_layout(int gs, int hid, int qdim, int ffn, int cap, int nch, int nslots) {
+HV_HD StepLayout step_layout(int gs, int hid, int qdim, int ffn, int cap, int nch, int nslots,
+                             int n_layer) {
   const int kmax = hid > qdim ? (hid > ffn ? hid : ffn) : (qdim > ffn ? qdim : ffn);
   StepLayout L;
-  L.bars = align_up(sizeof(StepShared), 16);
+  L.layers = align_up(sizeof(StepShared), 16);
+  L.bars = L.layers + align_up((size_t)n_layer * sizeof(hv_layer_w), 16);
   L.act_q = L.bars + 2 * kMaxSlots * sizeof(uint64_t);
   L.act_sb = L.act_q + align_up((size_t)kmax, 16);
   L.work = L.act_sb + align_up((size_t)(kmax / kBlock) * 8, 16);
@@ -135,6 +140,15 @@ HV_DEV bool mbar_test(uint64_t* b, unsigned parity) {
   unsigned ok;
   asm volatile("{\n\t.reg .pred p;\n\t"
                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(sm_addr(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Non-blocking test (try_wait may suspend the thread for a while before failing).
+HV_DEV bool mbar_probe(uint64_t* b, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                "selp.u32 %0, 1, 0, p;\n\t}"
                : "=r"(ok) : "r"(sm_addr(b)), "r"(parity) : "memory");
   return ok != 0;
@@ -202,8 +216,12 @@ HV_DEV bool mbar_wait(uint64_t* b, unsigned parity, StepShared& S, int* status,
 }
 
 // A warp's wait: every lane waits; the warp goes on only if all lanes saw the phase.
+// The time a warp spends waiting for slots is added to S.wait[warp] (for the trace).
 HV_DEV bool warp_wait(uint64_t* b, unsigned parity, StepShared& S, int* status) {
+  if (__all_sync(0xFFFFFFFFu, mbar_probe(b, parity))) return true;
+  const unsigned long long t0 = global_ns();
   const bool ok = mbar_wait(b, parity, S, status, kWaitNs);
+  if ((threadIdx.x & 31) == 0) S.wait[threadIdx.x >> 5] += global_ns() - t0;
   return __all_sync(0xFFFFFFFFu, ok);
 }
 
@@ -223,34 +241,47 @@ struct Ring {
 
 // Grid-wide barrier of the consumer threads over a self-resetting counter: CTA 0 adds
 // 2^31 - (grid - 1), the others add 1, so the top bit flips exactly when all have arrived
-// and the low bits return to zero. The wait is bounded: after kWaitNs (or once another
-// CTA has reported a failure, or this CTA aborted) it records the failure and returns
-// false in every consumer thread.
+// and the low bits return to zero. Each CTA knows which top bit to wait for (S.phase,
+// read once per launch and flipped at every barrier), so arriving is a fire-and-forget
+// release add and waiting is one acquire load per poll. The wait is bounded: after
+// kWaitNs (or once another CTA has reported a failure, or this CTA aborted) it records
+// the failure and returns false in every consumer thread.
 HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
   csync();
   if (threadIdx.x == 0) {
     int ok = *(volatile int*)&S.abort == 0;
     if (ok) {
       const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
-      __threadfence();
-      const unsigned old = atomicAdd(bar, add);
+      const unsigned want = S.phase ^ 0x80000000u;
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(bar), "r"(add) : "memory");
       const unsigned long long t0 = global_ns();
-      while (((ld_acquire(bar) ^ old) & 0x80000000u) == 0) {
-        if (*(volatile int*)status != 0) { ok = 0; break; }
-        if (global_ns() - t0 > kWaitNs) {
-          atomicCAS(status, 0, HV_E_TIMEOUT);
-          ok = 0;
-          break;
+      for (unsigned n = 1;; ++n) {
+        if ((ld_acquire(bar) & 0x80000000u) == want) break;
+        if ((n & 31) == 0) {
+          if (*(volatile int*)status != 0) { ok = 0; break; }
+          if (global_ns() - t0 > kWaitNs) {
+            atomicCAS(status, 0, HV_E_TIMEOUT);
+            ok = 0;
+            break;
+          }
         }
-        __nanosleep(32);
       }
-      __threadfence();
+      S.phase = want;
     }
     if (!ok) *(volatile int*)&S.abort = 1;
     S.ok = ok;
   }
   csync();
   return S.ok != 0;
+}
+
+// Trace entry idx <- the ns warp 0 waited for slots since the last call; restarts the count.
+HV_DEV void trace_wait(const hv_step_desc& D, StepShared& S, int idx) {
+  if (threadIdx.x == 0) {
+    if (D.trace != nullptr)
+      D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + idx] = S.wait[0];
+    S.wait[0] = 0;
+  }
 }
 
 HV_DEV void trace_mark(const hv_step_desc& D, int idx) {
@@ -283,22 +314,17 @@ HV_DEV void attn_rows(int pos, int nch, int c, int* t0, int* t1, int* te) {
 
 HV_DEV int slots_per_tile(int niter) { return (niter + kSlotIters - 1) / kSlotIters; }
 
-template <typename T>
-HV_DEV T* ldg_ptr(T* const* p) {
-  return reinterpret_cast<T*>(__ldg(reinterpret_cast<const unsigned long long*>(p)));
-}
-
 // L2 prefetch (one thread) of a layer's small vectors a phase before they are needed:
 // the input norm and the q/k norms (attn) or the post-attention norm. The weights and
 // KV rows go through the ring; these few KB would otherwise be demand misses on the
 // critical path.
 HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
   if (attn) {
-    prefetch_l2(ldg_ptr(&L->an), (size_t)hid * 4);
-    prefetch_l2(ldg_ptr(&L->qn), kHd * 4);
-    prefetch_l2(ldg_ptr(&L->kn), kHd * 4);
+    prefetch_l2(L->an, (size_t)hid * 4);
+    prefetch_l2(L->qn, kHd * 4);
+    prefetch_l2(L->kn, kHd * 4);
   } else {
-    prefetch_l2(ldg_ptr(&L->fn), (size_t)hid * 4);
+    prefetch_l2(L->fn, (size_t)hid * 4);
   }
 }
 
@@ -313,6 +339,7 @@ struct Producer {
   unsigned long long policy;
   unsigned q = 0;
   bool live = true;
+  unsigned long long t_empty = 0, t_flight = 0;   // ns blocked on free slots / on copies
 
   HV_DEV Producer(const Ring& r, StepShared& s, int* st, int infl, int evict_first)
       : R(r), S(s), status(st) {
@@ -326,16 +353,23 @@ struct Producer {
   // copies into it.
   HV_DEV void issue(const void* a, unsigned na, const void* b, unsigned nb_, unsigned b_off) {
     if (!live) return;
-    if (q >= (unsigned)R.ns &&
-        !mbar_wait(R.empty_of(q), R.parity(q) ^ 1u, S, status, kProducerWaitNs)) {
-      live = false;
-      return;
+    if (q >= (unsigned)R.ns && !mbar_probe(R.empty_of(q), R.parity(q) ^ 1u)) {
+      const unsigned long long t0 = global_ns();
+      if (!mbar_wait(R.empty_of(q), R.parity(q) ^ 1u, S, status, kProducerWaitNs)) {
+        live = false;
+        return;
+      }
+      t_empty += global_ns() - t0;
     }
     if (q >= inflight) {
       const unsigned p = q - inflight;
-      if (!mbar_wait(R.full_of(p), R.parity(p), S, status, kProducerWaitNs)) {
-        live = false;
-        return;
+      if (!mbar_probe(R.full_of(p), R.parity(p))) {
+        const unsigned long long t0 = global_ns();
+        if (!mbar_wait(R.full_of(p), R.parity(p), S, status, kProducerWaitNs)) {
+          live = false;
+          return;
+        }
+        t_flight += global_ns() - t0;
       }
     }
     unsigned char* dst = R.slot(q);
@@ -388,8 +422,8 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
     }
 }
 
-HV_DEV void produce(const hv_step_desc& D, int flags, int pos, const Ring& R, StepShared& S,
-                    int inflight, int evict_first) {
+HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int pos,
+                    const Ring& R, StepShared& S, int inflight, int evict_first) {
   Producer P(R, S, D.status, inflight, evict_first);
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
   const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
@@ -398,29 +432,52 @@ HV_DEV void produce(const hv_step_desc& D, int flags, int pos, const Ring& R, St
             it_ffn = pp_iters(ffn / kBlock);
   int off = 0, t0, t1;
   for (int l = 0; l < D.n_layer && P.live; ++l) {
-    const hv_layer_w* L = D.layers + l;
+    const hv_layer_w* L = Ls + l;
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
-    P.gemv(ldg_ptr(&L->qkv_b4), ldg_ptr(&L->qkv_sw), it_hid, t0, t1);
+    P.gemv(L->qkv_b4, L->qkv_sw, it_hid, t0, t1);
     for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
       int a0, a1, ae;
       attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
-      P.kv(ldg_ptr(&L->kc), ldg_ptr(&L->vc), wi / nch, D.cap, a0, ae);
+      P.kv(L->kc, L->vc, wi / nch, D.cap, a0, ae);
     }
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    P.gemv(ldg_ptr(&L->o_b4), ldg_ptr(&L->o_sw), it_q, t0, t1);
+    P.gemv(L->o_b4, L->o_sw, it_q, t0, t1);
     phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
-    P.gemv(ldg_ptr(&L->gu_b4), ldg_ptr(&L->gu_sw), it_hid, t0, t1);
+    P.gemv(L->gu_b4, L->gu_sw, it_hid, t0, t1);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    P.gemv(ldg_ptr(&L->dn_b4), ldg_ptr(&L->dn_sw), it_ffn, t0, t1);
+    P.gemv(L->dn_b4, L->dn_sw, it_ffn, t0, t1);
   }
   if ((flags & HV_STEP_HEAD) && P.live) {
     phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
     P.gemv(D.head_b4, D.head_sw, it_hid, t0, t1);
   }
   producer_drain(R, P.q, S);
+  if (D.trace != nullptr) {
+    uint64_t* tr = D.trace + (size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + 2 +
+                   26 * D.n_layer;
+    tr[3] = P.t_empty;
+    tr[4] = P.t_flight;
+    tr[5] = P.q;
+  }
 }
 
 // ---- prologues: build the quantised activation in shared memory ---------------------
+
+// One float4 of a vector, quantised by its 8-lane group (one 32-block): optionally
+// normalised first (w * (x / d)). Out of line so that the division-heavy code exists
+// once, not once per unrolled load: the prologues run once per phase, with an
+// instruction cache that the phase in between has refilled.
+__device__ __noinline__ unsigned quant4(float4 x, float4 w, float d, bool norm, int b,
+                                        bool lead, int2* sb_s) {
+  if (norm)
+    x = make_float4(__fmul_rn(w.x, __fdiv_rn(x.x, d)), __fmul_rn(w.y, __fdiv_rn(x.y, d)),
+                    __fmul_rn(w.z, __fdiv_rn(x.z, d)), __fmul_rn(w.w, __fdiv_rn(x.w, d)));
+  float s;
+  int bs;
+  const unsigned q = quant_block_8lanes(x, &s, &bs);
+  if (lead) sb_s[b] = make_int2(__float_as_int(s), bs);
+  return q;
+}
 
 // act <- quant(rmsnorm(src, w)) over n = hidden values (n % 32 == 0, n <= kMaxHidden);
 // src from global (through L2) or, for layer 0, the f16 embedding row. Thread t holds
@@ -462,15 +519,8 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
 #pragma unroll
   for (int k = 0; k < kV; ++k) {
     const int i4 = t + k * kConsThreads;
-    if (i4 < n4) {                      // uniform over each 8-lane group (n4 % 8 == 0)
-      const float4 x = make_float4(
-          __fmul_rn(wv[k].x, __fdiv_rn(xv[k].x, d)), __fmul_rn(wv[k].y, __fdiv_rn(xv[k].y, d)),
-          __fmul_rn(wv[k].z, __fdiv_rn(xv[k].z, d)), __fmul_rn(wv[k].w, __fdiv_rn(xv[k].w, d)));
-      float s;
-      int bs;
-      q32[i4] = quant_block_8lanes(x, &s, &bs);
-      if ((i4 & 7) == 0) sb_s[i4 >> 3] = make_int2(__float_as_int(s), bs);
-    }
+    if (i4 < n4)                        // uniform over each 8-lane group (n4 % 8 == 0)
+      q32[i4] = quant4(xv[k], wv[k], d, true, i4 >> 3, (i4 & 7) == 0, sb_s);
   }
   csync();
 }
@@ -494,12 +544,7 @@ __device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int b = base + k * step + (lane >> 3);
-      if (b < nb) {
-        float s;
-        int bs;
-        q32[b * 8 + sub] = quant_block_8lanes(v[k], &s, &bs);
-        if (sub == 0) sb_s[b] = make_int2(__float_as_int(s), bs);
-      }
+      if (b < nb) q32[b * 8 + sub] = quant4(v[k], v[k], 1.0f, false, b, sub == 0, sb_s);
     }
   }
   csync();
@@ -747,7 +792,7 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int t0, int t1, int te, int 
 template <int GS>
 __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
                                        const Ring& R, unsigned* qp, StepShared& S,
-                                       float* area) {
+                                       float* area, int tb) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
   const int chunk_max = (cap + nch - 1) / nch;
   const int lg_floats = (chunk_max * GS + 3) & ~3;   // keeps red_s 16-byte aligned
@@ -773,10 +818,10 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
     for (int h = warp; h < GS + 2; h += kConsWarps) {
       if (h < GS) {
-        warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, ldg_ptr(&L->qn), cs, sn, D.eps,
+        warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, L->qn, cs, sn, D.eps,
                        tmp_s + h * kHd, q_s + h * kHd);
       } else if (h == GS) {
-        warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, ldg_ptr(&L->kn), cs, sn, D.eps,
+        warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, L->kn, cs, sn, D.eps,
                        tmp_s + GS * kHd, kpos_s);
       } else {
         reinterpret_cast<float4*>(vpos_s)[lane] =
@@ -784,9 +829,11 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       }
     }
     csync();
+    trace_mark(D, tb + 14);
+    trace_wait(D, S, tb + 20);
     if (c == nch - 1 && threadIdx.x < kHd) {         // the chunk holding pos appends
-      float* kc = ldg_ptr(&L->kc) + (size_t)g * cap * kHd;
-      float* vc = ldg_ptr(&L->vc) + (size_t)g * cap * kHd;
+      float* kc = L->kc + (size_t)g * cap * kHd;
+      float* vc = L->vc + (size_t)g * cap * kHd;
       kc[(size_t)pos * kHd + threadIdx.x] = kpos_s[threadIdx.x];
       vc[(size_t)pos * kHd + threadIdx.x] = vpos_s[threadIdx.x];
     }
@@ -815,6 +862,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     if (pos_group && ((te - t0) / 4) % kConsWarps == warp)
       group_scores<GS>(qv, te, t0, t1, te, pos, nullptr, te, kpos_s, scale, lg_s);
     csync();
+    trace_mark(D, tb + 15);
+    trace_wait(D, S, tb + 21);
 
     // ---- per-head max and exp: warp i handles head i
     for (int i = warp; i < GS; i += kConsWarps) {
@@ -833,6 +882,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       if (lane == 0) { stat_s[2 * i] = mx; stat_s[2 * i + 1] = l; }
     }
     csync();
+    trace_mark(D, tb + 16);
+    trace_wait(D, S, tb + 20);
 
     // ---- probability-weighted V sum: V rows from the ring, same group -> warp map
     float4 acc[GS];
@@ -871,8 +922,11 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     }
     __threadfence();
     csync();
+    trace_mark(D, tb + 17);
+    trace_wait(D, S, tb + 22);
     if (threadIdx.x == 0) S.flag = (atomicAdd(D.ticket + g, 1) == nch - 1);
     csync();
+    trace_mark(D, tb + 18);
     if (S.flag) {
       __threadfence();
       attn_merge<GS, CSync>(D.part + (size_t)g * nch * GS * kPartStride, nch,
@@ -880,6 +934,7 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       if (threadIdx.x == 0) D.ticket[g] = 0;
     }
     csync();
+    trace_mark(D, tb + 19);
   }
 }
 
@@ -891,13 +946,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
                                                           int evict_first) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
-  const StepLayout Lo = step_layout(GS, hid, qdim, ffn, D.cap, D.attn_chunks, nslots);
+  const StepLayout Lo = step_layout(GS, hid, qdim, ffn, D.cap, D.attn_chunks, nslots, D.n_layer);
   StepShared& S = *reinterpret_cast<StepShared*>(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint4* q_s = reinterpret_cast<uint4*>(smem + Lo.act_q);
   int2* sb_s = reinterpret_cast<int2*>(smem + Lo.act_sb);
   float* work = reinterpret_cast<float*>(smem + Lo.work);
   const Ring R{smem + Lo.ring, bars, bars + kMaxSlots, nslots};
+  hv_layer_w* Ls = reinterpret_cast<hv_layer_w*>(smem + Lo.layers);
   const ActView act{q_s, sb_s};
 
   trace_mark(D, 0);
@@ -908,11 +964,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     S.abort = 0;
+    // no barrier of this launch can complete before this CTA arrives, so the counter's
+    // top bit is still the one the previous launch left
+    S.phase = ld_acquire(D.barrier) & 0x80000000u;
+    for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0;
   }
   {
     const int* src = reinterpret_cast<const int*>(D.plans);
     int* dst = reinterpret_cast<int*>(&S.P);
     for (int i = threadIdx.x; i < (int)(sizeof(StepPlans) / 4); i += blockDim.x) dst[i] = __ldg(src + i);
+    // the layer table, so no phase starts with a pointer load from global memory
+    const unsigned long long* ls = reinterpret_cast<const unsigned long long*>(D.layers);
+    unsigned long long* ld = reinterpret_cast<unsigned long long*>(Ls);
+    const int nw = D.n_layer * (int)(sizeof(hv_layer_w) / 8);
+    for (int i = threadIdx.x; i < nw; i += blockDim.x) ld[i] = __ldg(ls + i);
   }
   const int pos = *D.pos;
   const int tok = *D.tok;
@@ -923,7 +988,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     return;
   }
   if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
-    if (threadIdx.x == kConsThreads) produce(D, flags, pos, R, S, inflight, evict_first);
+    if (threadIdx.x == kConsThreads) produce(D, Ls, flags, pos, R, S, inflight, evict_first);
     return;
   }
 
@@ -939,24 +1004,26 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
             it_ffn = pp_iters(ffn / kBlock);
   unsigned q = 0;
   int off = 0, t0, t1;
-  if (threadIdx.x == 0) prefetch_vectors(D.layers, hid, true);
+  if (threadIdx.x == 0) prefetch_vectors(Ls, hid, true);
   trace_mark(D, 1);
   for (int l = 0; l < D.n_layer; ++l) {
-    const hv_layer_w* L = D.layers + l;
-    const int tb = 2 + 14 * l;
+    const hv_layer_w* L = Ls + l;
+    const int tb = 2 + 26 * l;
     // P1: qkv
-    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, ldg_ptr(&L->an), hid, D.eps, S, work, q_s,
+    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, L->an, hid, D.eps, S, work, q_s,
                    sb_s);
     trace_mark(D, tb + 0);
+    trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
     gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, D.qkv, nullptr, nullptr, work,
                       S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
+    trace_wait(D, S, tb + 23);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 2);
     // P2: attention
-    attn_ring<GS>(D, L, pos, R, &q, S, work);
+    attn_ring<GS>(D, L, pos, R, &q, S, work, tb);
     trace_mark(D, tb + 3);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 4);
@@ -972,13 +1039,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
-    pro_norm_quant(D.h, nullptr, ldg_ptr(&L->fn), hid, D.eps, S, work, q_s, sb_s);
+    pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s);
     trace_mark(D, tb + 8);
+    trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
     gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, D.act, nullptr, nullptr,
                          work, S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 9);
+    trace_wait(D, S, tb + 24);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 10);
     if (threadIdx.x == 0) {
@@ -988,17 +1057,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     // P5: down + residual
     pro_quant(D.act, ffn, q_s, sb_s);
     trace_mark(D, tb + 11);
+    trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
     gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
+    trace_wait(D, S, tb + 25);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 13);
   }
 
   if (!(flags & HV_STEP_HEAD)) return;
-  const int th = 2 + 14 * D.n_layer;
+  const int th = 2 + 26 * D.n_layer;
   pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s);
   trace_mark(D, th + 0);
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
@@ -1062,8 +1133,8 @@ static void* step_fn(int gs) {
 }
 
 // Ring slots that fit next to the fixed regions (0 if the fixed regions alone do not).
-static int step_slots(int gs, int hid, int qdim, int ffn, int cap, int nch) {
-  const StepLayout L = step_layout(gs, hid, qdim, ffn, cap, nch, 0);
+static int step_slots(int gs, int hid, int qdim, int ffn, int cap, int nch, int n_layer) {
+  const StepLayout L = step_layout(gs, hid, qdim, ffn, cap, nch, 0, n_layer);
   if (L.ring >= (size_t)kSmemLimit) return 0;
   const int n = (int)(((size_t)kSmemLimit - L.ring) / kSlotBytes);
   return n > kMaxSlots ? kMaxSlots : n;
@@ -1139,6 +1210,8 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(h.hidden <= kMaxHidden, HV_E_UNSUPPORTED, "hv_step_launch: hidden %d > %d",
              h.hidden, kMaxHidden);
   HV_REQUIRE(h.plans != nullptr, HV_E_INVALID, "hv_step_launch: plans not set (hv_step_plans)");
+  HV_REQUIRE(h.n_layer > 0 && h.layers != nullptr, HV_E_INVALID,
+             "hv_step_launch: no layer table");
   HV_REQUIRE(h.attn_chunks > 0 && 2 * h.attn_chunks + 1 <= kConsWarps * kHd, HV_E_INVALID,
              "hv_step_launch: attn_chunks %d outside [1, %d]", h.attn_chunks,
              (kConsWarps * kHd - 1) / 2);
@@ -1146,10 +1219,11 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
   const int qdim = h.n_head * kHd;
-  const int nslots = step_slots(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks);
+  const int nslots = step_slots(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, h.n_layer);
   HV_REQUIRE(nslots >= 4, HV_E_UNSUPPORTED,
              "hv_step_launch: shared memory leaves %d ring slots (need 4)", nslots);
-  const StepLayout lay = step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots);
+  const StepLayout lay =
+      step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots, h.n_layer);
   const size_t smem = lay.total;
   int sms = 0;
   int rc = sm_count(&sms);

@@ -355,6 +355,10 @@ class Engine:
     TRACE_PHASES = ("qkv_prologue", "qkv_gemv", "barrier1", "attention", "barrier2",
                     "o_prologue", "o_gemv", "barrier3", "gu_prologue", "gu_gemv", "barrier4",
                     "down_prologue", "down_gemv", "barrier5")
+    TRACE_WAITS = ("wait_attn_scores", "wait_attn_values", "wait_qkv_gemv", "wait_gu_gemv",
+                   "wait_down_gemv")
+    TRACE_ATTN = ("attn_heads", "attn_scores", "attn_softmax", "attn_values", "attn_ticket",
+                  "attn_merge")
 
     def profile_step(self, flags: int = STEP_HEAD | STEP_ARGMAX) -> dict:
         """Run one fused step at the current tok/pos with the per-phase trace on.
@@ -363,7 +367,7 @@ class Engine:
         [grid, stride]} where each phase's duration is taken per CTA and summed over the
         layers (median and max over CTAs)."""
         c = self.cfg
-        stride = 5 + 14 * c.n_layer
+        stride = 8 + 26 * c.n_layer
         n = self.step_grid * stride
         buf = hvdrv.alloc(n * 8)
         try:
@@ -380,17 +384,42 @@ class Engine:
         t = raw.astype(np.int64)
         t = t - t[:, :1]
         out = {}
+        def prev_mark(l, k):      # the mark that ends the phase before (layer l, mark k)
+            if k > 0:
+                return 2 + 26 * l + k - 1
+            return 1 if l == 0 else 2 + 26 * (l - 1) + 13
+
         for k, name in enumerate(self.TRACE_PHASES):
-            idx = np.array([2 + 14 * l + k for l in range(c.n_layer)])
-            d = t[:, idx] - t[:, idx - 1]
+            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            pidx = np.array([prev_mark(l, k) for l in range(c.n_layer)])
+            d = t[:, idx] - t[:, pidx]
             out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
                          "max_us": float(d.max(axis=0).sum() / 1e3)}
-        th = 2 + 14 * c.n_layer
+        # inside the attention, CTAs that had a work item (the marks stay 0 otherwise)
+        busy = raw[:, 2 + 14] != 0
+        prev = 2
+        for k, name in zip(range(14, 20), self.TRACE_ATTN):
+            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            d = (t[:, idx] - t[:, idx - k + prev])[busy]
+            prev = k
+            if d.size:
+                out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
+                             "max_us": float(d.max(axis=0).sum() / 1e3)}
+        for k, name in zip(range(21, 26), self.TRACE_WAITS):
+            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            d = raw[:, idx].astype(np.int64)
+            out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
+                         "max_us": float(d.max(axis=0).sum() / 1e3)}
+        th = 2 + 26 * c.n_layer
         for k, name in enumerate(("head_prologue", "head_gemv", "argmax")):
-            d = t[:, th + k] - t[:, th + k - 1]
+            d = t[:, th + k] - t[:, th + k - 1 if k else prev_mark(c.n_layer, 0)]
             out[name] = {"median_us": float(np.median(d) / 1e3), "max_us": float(d.max() / 1e3)}
         out["setup"] = {"median_us": float(np.median(t[:, 1]) / 1e3),
                         "max_us": float(t[:, 1].max() / 1e3)}
+        for k, name in zip(range(3, 6), ("producer_wait_slot_us", "producer_wait_flight_us",
+                                          "producer_slots")):
+            v = raw[:, th + k].astype(np.float64) / (1e3 if k < 5 else 1.0)
+            out[name] = {"median_us": float(np.median(v)), "max_us": float(v.max())}
         last = flags & STEP_ARGMAX and th + 2 or (flags & STEP_HEAD and th + 1 or th - 1)
         return {"total_us": float(t[:, last].max() / 1e3), "phases": out, "raw": raw}
 

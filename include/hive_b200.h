@@ -241,12 +241,18 @@ typedef struct hv_step_desc {
   const void* plans;            /* hv_step_plans() output, uploaded to the device  */
 } hv_step_desc;
 
-/* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 14 l:
+/* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 26 l:
  * +0 qkv prologue, +1 qkv GEMV, +2 barrier, +3 attention, +4 barrier, +5 o prologue,
  * +6 o GEMV, +7 barrier, +8 gate/up prologue, +9 gate/up GEMV, +10 barrier,
- * +11 down prologue, +12 down GEMV, +13 barrier; then the head prologue, head GEMV and
- * argmax at 2 + 14 n_layer + {0, 1, 2}. */
-#define HV_STEP_TRACE_STRIDE(n_layer) (5 + 14 * (n_layer))
+ * +11 down prologue, +12 down GEMV, +13 barrier; inside the attention (last work item
+ * of the CTA): +14 q/k norms and RoPE, +15 scores, +16 softmax, +17 weighted V sum and
+ * partials, +18 ticket, +19 merge (all %globaltimer ns). Durations (ns) that consumer
+ * warp 0 spent waiting for its shared-memory ring slots: +21 attention scores, +22
+ * attention V sum, +23 qkv GEMV, +24 gate/up GEMV, +25 down GEMV (+20 is scratch). Then
+ * the head prologue, head GEMV and argmax at 2 + 26 n_layer + {0, 1, 2}; then, for the
+ * producer warp: ns blocked on a ring slot still in use (+3), ns blocked on the copies in
+ * flight (+4), slots copied (+5). */
+#define HV_STEP_TRACE_STRIDE(n_layer) (8 + 26 * (n_layer))
 
 #define HV_STEP_HEAD 1     /* compute the LM head into logits                          */
 #define HV_STEP_ARGMAX 2   /* then greedy argmax: tok = argmax, gen[step] = tok,
