@@ -20,6 +20,7 @@ namespace hv {
 constexpr int kHd = 128;
 constexpr int kAttnChunkMax = 1024;   // positions one work item may hold
 constexpr int kPartStride = 132;      // per q head: m, l, 2 pad, acc[128]
+constexpr int kAttnBlock = 20;        // positions per block: block b of a chunk -> warp b % nw
 
 HV_DEV void chunk_bounds(int npos, int nch, int c, int* t0, int* t1) {
   *t0 = (int)(((long long)c * npos) / nch);
@@ -81,40 +82,44 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
   const int nw = blockDim.x >> 5;
   const int n = t1 - t0;
 
-  // ---- scores: each warp takes 4 positions at a time; lane l owns dims 4l..4l+3
+  // ---- scores: blocks of kAttnBlock positions, block b to warp b % nw, 4 positions at a
+  // time; lane l owns dims 4l..4l+3
   float4 qv[GS];
 #pragma unroll
   for (int i = 0; i < GS; ++i) qv[i] = reinterpret_cast<const float4*>(q_s + i * kHd)[lane];
-  for (int tb = t0 + warp * 4; tb < t1; tb += nw * 4) {
-    float4 kv[4];
+  for (int b0 = t0 + warp * kAttnBlock; b0 < t1; b0 += nw * kAttnBlock) {
+    const int b1 = min(b0 + kAttnBlock, t1);
+    for (int tb = b0; tb < b1; tb += 4) {
+      float4 kv[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int t = tb + p;
-      if (t < t1) {
-        kv[p] = (kpos_s && t == pos) ? reinterpret_cast<const float4*>(kpos_s)[lane]
-                                     : ldg_f4(K + (size_t)t * kHd + lane * 4);
-      } else {
-        kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < 4; ++p) {
+        const int t = tb + p;
+        if (t < t1) {
+          kv[p] = (kpos_s && t == pos) ? reinterpret_cast<const float4*>(kpos_s)[lane]
+                                       : ldg_f4(K + (size_t)t * kHd + lane * 4);
+        } else {
+          kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-    }
-    float v[4 * GS];
+      float v[4 * GS];
 #pragma unroll
-    for (int p = 0; p < 4; ++p)
+      for (int p = 0; p < 4; ++p)
 #pragma unroll
-      for (int i = 0; i < GS; ++i) {
-        float s = qv[i].x * kv[p].x;
-        s = fmaf(qv[i].y, kv[p].y, s);
-        s = fmaf(qv[i].z, kv[p].z, s);
-        s = fmaf(qv[i].w, kv[p].w, s);
-        v[p * GS + i] = s;
+        for (int i = 0; i < GS; ++i) {
+          float sc = qv[i].x * kv[p].x;
+          sc = fmaf(qv[i].y, kv[p].y, sc);
+          sc = fmaf(qv[i].z, kv[p].z, sc);
+          sc = fmaf(qv[i].w, kv[p].w, sc);
+          v[p * GS + i] = sc;
+        }
+      int idx;
+      const float tot = halving_reduce<4 * GS>(v, lane, &idx);
+      constexpr int dup = 32 / (4 * GS);
+      if ((lane & (dup - 1)) == 0) {
+        const int p = idx / GS, i = idx % GS;
+        const int t = tb + p;
+        if (t < t1) lg_s[(t - t0) * GS + i] = tot * scale;
       }
-    int idx;
-    const float tot = halving_reduce<4 * GS>(v, lane, &idx);
-    constexpr int dup = 32 / (4 * GS);
-    if ((lane & (dup - 1)) == 0) {
-      const int p = idx / GS, i = idx % GS;
-      const int t = tb + p;
-      if (t < t1) lg_s[(t - t0) * GS + i] = tot * scale;
     }
   }
   __syncthreads();
@@ -137,33 +142,37 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
   }
   __syncthreads();
 
-  // ---- probability-weighted V sum: warps split positions, lane owns 4 dims
+  // ---- probability-weighted V sum: the same blocks to the same warps, positions in
+  // order within a block; lane owns 4 dims
   float4 acc[GS];
 #pragma unroll
   for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int tb = t0 + warp * 4; tb < t1; tb += nw * 4) {
-    float4 vv[4];
+  for (int b0 = t0 + warp * kAttnBlock; b0 < t1; b0 += nw * kAttnBlock) {
+    const int b1 = min(b0 + kAttnBlock, t1);
+    for (int tb = b0; tb < b1; tb += 4) {
+      float4 vv[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int t = tb + p;
-      if (t < t1) {
-        vv[p] = (vpos_s && t == pos) ? reinterpret_cast<const float4*>(vpos_s)[lane]
-                                     : ldg_f4(V + (size_t)t * kHd + lane * 4);
-      } else {
-        vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < 4; ++p) {
+        const int t = tb + p;
+        if (t < t1) {
+          vv[p] = (vpos_s && t == pos) ? reinterpret_cast<const float4*>(vpos_s)[lane]
+                                       : ldg_f4(V + (size_t)t * kHd + lane * 4);
+        } else {
+          vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-    }
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int t = tb + p;
-      if (t < t1) {
+      for (int p = 0; p < 4; ++p) {
+        const int t = tb + p;
+        if (t < t1) {
 #pragma unroll
-        for (int i = 0; i < GS; ++i) {
-          const float w = lg_s[(t - t0) * GS + i];
-          acc[i].x = fmaf(w, vv[p].x, acc[i].x);
-          acc[i].y = fmaf(w, vv[p].y, acc[i].y);
-          acc[i].z = fmaf(w, vv[p].z, acc[i].z);
-          acc[i].w = fmaf(w, vv[p].w, acc[i].w);
+          for (int i = 0; i < GS; ++i) {
+            const float w = lg_s[(t - t0) * GS + i];
+            acc[i].x = fmaf(w, vv[p].x, acc[i].x);
+            acc[i].y = fmaf(w, vv[p].y, acc[i].y);
+            acc[i].z = fmaf(w, vv[p].z, acc[i].z);
+            acc[i].w = fmaf(w, vv[p].w, acc[i].w);
+          }
         }
       }
     }
@@ -188,9 +197,13 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
 // partials through L2 (they were written by other CTAs): first every chunk's (m, l) in
 // parallel, then per head the global max and weights, then each output element sums
 // its chunks with all loads of a batch in flight. `w_s` is shared scratch of
-// 2 * nch * GS + GS floats. Cooperative over the threads of Sync.
-template <int GS, class Sync = SyncBlock>
-HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx, float* w_s) {
+// 2 * nch * GS + GS floats. Cooperative over the threads of Sync. With kQuant the rows
+// are not stored as floats but quantised per 32 values (quant_a8s, one warp per block):
+// int8 into q_out[i * 128 + d], (scale bits, block sum) into sb_out[(i * 128 + d) / 32]
+// (Sync's thread count must then be a multiple of 32).
+template <int GS, class Sync = SyncBlock, bool kQuant = false>
+HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx, float* w_s,
+                       int8_t* __restrict__ q_out = nullptr, int2* __restrict__ sb_out = nullptr) {
   float* l_s = w_s + nch * GS;                    // l of (c, i)
   float* inv_s = l_s + nch * GS;                  // 1 / L per head
   const int nt = Sync::threads();
@@ -225,7 +238,17 @@ HV_DEV void attn_merge(const float* part_head, int nch, float* __restrict__ ctx,
       for (int k = 0; k < 8; ++k)
         if (c0 + k < nch) o = fmaf(w_s[(c0 + k) * GS + i], a[k], o);
     }
-    ctx[i * kHd + d] = o * inv_s[i];
+    const float val = o * inv_s[i];
+    if constexpr (kQuant) {
+      int8_t q8;
+      float sc;
+      int bs;
+      quant_block_warp(val, threadIdx.x & 31, &q8, &sc, &bs);
+      q_out[e] = q8;
+      if ((threadIdx.x & 31) == 0) sb_out[e / 32] = make_int2(__float_as_int(sc), bs);
+    } else {
+      ctx[i * kHd + d] = val;
+    }
   }
 }
 

@@ -59,6 +59,7 @@ constexpr unsigned long long kProducerWaitNs = 4000000000ull;  // producer waits
 static_assert(kSlotScaleOff + kSlotIters * kPpScales * 4 == kSlotBytes, "slot layout");
 static_assert(sizeof(hv_layer_w) % 8 == 0, "layer table copied as 8-byte words");
 static_assert(kSlotRows % 4 == 0, "attention groups of 4 rows never straddle slots");
+static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention block");
 
 // Run-time tunables (hv_step_set_option): bulk copies a producer keeps in flight, and
 // whether streamed bytes are marked evict-first in L2. Copies beyond what saturates HBM
@@ -87,6 +88,7 @@ struct StepShared {
   int abort;                     // set by any warp of this CTA whose wait gave up
   unsigned phase;                // top bit of the grid barrier counter to wait for next
   unsigned long long wait[kConsWarps];   // ns each consumer warp waited for ring slots
+  long long busy[kConsWarps];            // cycles spent computing attention scores
 };
 
 // Byte offsets of the dynamic shared memory regions (host and device agree).
@@ -305,6 +307,16 @@ HV_DEV void phase_tiles(int ntiles, int* off, int* t0, int* t1) {
   *off = (o + extra) % G;
 }
 
+// Tiles [t0, t1) of the gate/up phase: whole units of 8 tiles (= 32 SiLU outputs, one
+// quantisation block), so each CTA quantises the blocks it produced.
+HV_DEV void gu_tiles(int ffn, int* off, int* t0, int* t1) {
+  const int ntiles = pp_tiles(2 * ffn, ffn);
+  int u0, u1;
+  phase_tiles((ntiles + 7) / 8, off, &u0, &u1);
+  *t0 = min(u0 * 8, ntiles);
+  *t1 = min(u1 * 8, ntiles);
+}
+
 // Positions [t0, t1) of attention chunk c, and te: rows [t0, te) come from the cache,
 // row pos (if in the chunk) from this step's qkv.
 HV_DEV void attn_rows(int pos, int nch, int c, int* t0, int* t1, int* te) {
@@ -313,6 +325,17 @@ HV_DEV void attn_rows(int pos, int nch, int c, int* t0, int* t1, int* te) {
 }
 
 HV_DEV int slots_per_tile(int niter) { return (niter + kSlotIters - 1) / kSlotIters; }
+
+// Ring sequence number (relative to the phase's first) of slot j of local tile lt. Rows
+// of one pairwise leaf (one work item per tile, tile i to warp i % 8) are filled in
+// waves: slot 0 of tiles 8R .. 8R+7, then their slot 1, ..., the order the eight warps
+// consume them, so free slots go to real prefetch instead of to each warp's later slots.
+// Rows of several leaves (items share slots) keep tile-major order.
+HV_DEV unsigned slot_seq(int lt, int j, int ntile, int spt, bool wave) {
+  if (!wave) return (unsigned)(lt * spt + j);
+  const int r = lt / kConsWarps, nr = min(kConsWarps, ntile - r * kConsWarps);
+  return (unsigned)(r * kConsWarps * spt + j * nr + (lt - r * kConsWarps));
+}
 
 // L2 prefetch (one thread) of a layer's small vectors a phase before they are needed:
 // the input norm and the q/k norms (attn) or the post-attention norm. The weights and
@@ -386,16 +409,27 @@ struct Producer {
   }
 
   // This CTA's tiles [t0, t1) of a prepacked matrix with niter iterations per tile.
-  HV_DEV void gemv(const uint32_t* pb4, const float* psw, int niter, int t0, int t1) {
-    const int spt = slots_per_tile(niter);
-    for (int tile = t0; tile < t1 && live; ++tile) {
-      for (int j = 0; j < spt; ++j) {
-        const int it0 = j * kSlotIters;
-        const unsigned n = (unsigned)min(kSlotIters, niter - it0);
-        const size_t first = (size_t)tile * niter + it0;
-        issue(pb4 + first * kPpNibWords, n * kPpNibWords * 4, psw + first * kPpScales,
-              n * kPpScales * 4, kSlotScaleOff);
-      }
+  HV_DEV void gemv_slot(const uint32_t* pb4, const float* psw, int niter, int tile, int j) {
+    const int it0 = j * kSlotIters;
+    const unsigned n = (unsigned)min(kSlotIters, niter - it0);
+    const size_t first = (size_t)tile * niter + it0;
+    issue(pb4 + first * kPpNibWords, n * kPpNibWords * 4, psw + first * kPpScales,
+          n * kPpScales * 4, kSlotScaleOff);
+  }
+
+  // This CTA's tiles [t0, t1) of a prepacked matrix with niter iterations per tile, in the
+  // order of slot_seq.
+  HV_DEV void gemv(const uint32_t* pb4, const float* psw, int niter, int t0, int t1, int nleaf) {
+    const int spt = slots_per_tile(niter), ntile = t1 - t0;
+    if (nleaf > 1) {
+      for (int lt = 0; lt < ntile && live; ++lt)
+        for (int j = 0; j < spt; ++j) gemv_slot(pb4, psw, niter, t0 + lt, j);
+      return;
+    }
+    for (int r0 = 0; r0 < ntile && live; r0 += kConsWarps) {
+      const int nr = min(kConsWarps, ntile - r0);
+      for (int j = 0; j < spt; ++j)
+        for (int i = 0; i < nr; ++i) gemv_slot(pb4, psw, niter, t0 + r0 + i, j);
     }
   }
 
@@ -434,22 +468,22 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
   for (int l = 0; l < D.n_layer && P.live; ++l) {
     const hv_layer_w* L = Ls + l;
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
-    P.gemv(L->qkv_b4, L->qkv_sw, it_hid, t0, t1);
+    P.gemv(L->qkv_b4, L->qkv_sw, it_hid, t0, t1, S.P.gv_hid.nleaf);
     for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
       int a0, a1, ae;
       attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
       P.kv(L->kc, L->vc, wi / nch, D.cap, a0, ae);
     }
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    P.gemv(L->o_b4, L->o_sw, it_q, t0, t1);
-    phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
-    P.gemv(L->gu_b4, L->gu_sw, it_hid, t0, t1);
+    P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
+    gu_tiles(ffn, &off, &t0, &t1);
+    P.gemv(L->gu_b4, L->gu_sw, it_hid, t0, t1, S.P.gv_hid.nleaf);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    P.gemv(L->dn_b4, L->dn_sw, it_ffn, t0, t1);
+    P.gemv(L->dn_b4, L->dn_sw, it_ffn, t0, t1, S.P.gv_ffn.nleaf);
   }
   if ((flags & HV_STEP_HEAD) && P.live) {
     phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
-    P.gemv(D.head_b4, D.head_sw, it_hid, t0, t1);
+    P.gemv(D.head_b4, D.head_sw, it_hid, t0, t1, S.P.gv_hid.nleaf);
   }
   producer_drain(R, P.q, S);
   if (D.trace != nullptr) {
@@ -550,6 +584,34 @@ __device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2
   csync();
 }
 
+// act <- a vector other CTAs already quantised: int8 [n] at q, then (scale, sum) pairs
+// for its n / 32 blocks at sb (read through L2).
+__device__ __noinline__ void pro_load_quant(const void* q, const int2* sb, int n, uint4* q_s,
+                                            int2* sb_s) {
+  const uint4* q4 = reinterpret_cast<const uint4*>(q);
+  for (int i = threadIdx.x; i < n / 16; i += kConsThreads) q_s[i] = __ldcg(q4 + i);
+  for (int i = threadIdx.x; i < n / kBlock; i += kConsThreads) sb_s[i] = __ldcg(sb + i);
+  csync();
+}
+
+// The CTA's SiLU outputs, staged in shared memory (nval values starting at element
+// first, first % 32 == 0, nval % 32 == 0), quantised per 32 (8 lanes per block) into
+// int8 q[first ..] and (scale, sum) sb[first / 32 ..] in global memory.
+__device__ __noinline__ void quant_staged(const float* vals, int nval, int first, int8_t* q,
+                                          int2* sb) {
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int nb = nval / kBlock;
+  for (int base = (threadIdx.x >> 5) * 4; base < nb; base += kConsWarps * 4) {
+    const int b = base + (lane >> 3);
+    if (b < nb) {                      // uniform over each 8-lane group
+      const float4 v = reinterpret_cast<const float4*>(vals)[b * 8 + sub];
+      const unsigned w = quant4(v, v, 1.0f, false, first / kBlock + b, sub == 0, sb);
+      reinterpret_cast<unsigned*>(q + first)[b * 8 + sub] = w;
+    }
+  }
+}
+
+
 // ---- GEMV phases from the ring ----------------------------------------------------------
 
 enum { kStore = 0, kResidual = 1, kSiluPair = 2, kHead = 3 };
@@ -611,7 +673,8 @@ HV_DEV float2 slot_terms(const unsigned char* sl, int u, const unsigned* __restr
 // items (a leaf boundary inside it) gets half the release count from each.
 // MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate
 // rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
-// rows per half; SiLU(gate) * up is formed in the lane that holds the gate row.
+// rows per half; SiLU(gate) * up is formed in the lane that holds the gate row and stored
+// at out[p - 4 t0] for pair p (a shared-memory staging buffer).
 template <int MODE>
 __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan& P,
                                        const ActView act, int t0, int t1, int rows,
@@ -631,29 +694,33 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
     const int ia = lf == 0 ? 0 : P.it_end[lf - 1];
     const int ib = lf == nleaf - 1 ? niter : P.it_end[lf];   // the last leaf owns the tail
     const int ifull = min(ib, nfull);
-    float ae = 0.f, ao = 0.f;
+    // numpy assigns a leaf's first term and adds the rest; starting from -0.0 and adding
+    // every term gives the same bits ((-0) + x == x for every x, -0 and +0 included), so
+    // the loop needs no peeled first iteration
+    float ae = -0.0f, ao = -0.0f;
     float2 tail = make_float2(0.f, 0.f);
     for (int s0 = ia - ia % kSlotIters; s0 < ib; s0 += kSlotIters) {
       const int s1 = min(s0 + kSlotIters, niter);
-      const unsigned q = q0 + (unsigned)(lt * spt + s0 / kSlotIters);
+      const unsigned q = q0 + slot_seq(lt, s0 / kSlotIters, t1 - t0, spt, nleaf == 1);
       if (!warp_wait(R.full_of(q), R.parity(q), S, status)) {
         failed = true;
         break;
       }
       const unsigned char* sl = R.slot(q);
       const int a = max(ia, s0), bb = min(ib, s1), bf = min(bb, ifull);
-      int it = a;
-      if (it == ia && it < bf) {                     // a leaf starts with an assignment
-        const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
-        ae = v.x;
-        ao = v.y;
-        ++it;
-      }
-#pragma unroll 4
-      for (; it < bf; ++it) {
-        const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
-        ae = __fadd_rn(ae, v.x);
-        ao = __fadd_rn(ao, v.y);
+      if (a == s0 && bf == s0 + kSlotIters) {       // the whole slot: fixed trip count
+#pragma unroll
+        for (int u = 0; u < kSlotIters; ++u) {
+          const float2 v = slot_terms(sl, u, act_w, act.sb, s0 + u, g, t, lane, 8);
+          ae = __fadd_rn(ae, v.x);
+          ao = __fadd_rn(ao, v.y);
+        }
+      } else {
+        for (int it = a; it < bf; ++it) {
+          const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
+          ae = __fadd_rn(ae, v.x);
+          ao = __fadd_rn(ao, v.y);
+        }
       }
       if (bb > bf) tail = slot_terms(sl, bf - s0, act_w, act.sb, bf, g, t, lane, ntail);
       __syncwarp();
@@ -671,7 +738,8 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
     }
     if (nleaf == 1) {
       bool ok;
-      const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      if (MODE == kSiluPair) row -= 4 * t0;            // staged in shared memory
       gemv_epilogue<MODE>(__fadd_rn(0.0f, v), row, ok, out, best_v, best_i);
     } else if (t == 0) {
       leafbuf[((size_t)lt * 8 + g) * nleaf + lf] = v;
@@ -681,7 +749,8 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
     csync();
     for (int lt = warp; lt < t1 - t0 && !failed; lt += kConsWarps) {
       bool ok;
-      const int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
+      if (MODE == kSiluPair) row -= 4 * t0;
       const float y = fold_leaves(P, leafbuf + ((size_t)lt * 8 + g) * nleaf);
       gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
     }
@@ -719,25 +788,47 @@ HV_DEV void warp_norm_rope(const float* raw, const float* __restrict__ gain,
   __syncwarp();
 }
 
-// Scores of one group of 4 positions tb..tb+3 for the GS heads (the arithmetic of
-// attn_chunk in attn_decode.cuh): rows below te from the slot whose first row is r0,
-// row pos from kpos_s, rows from t1 on are zero.
+// Rows per score group: enough that one butterfly reduces 32 values (4 rows for GS = 8).
+// Each score is the lane-partial dot (x*x, then three fma) summed over the 32 lanes with
+// the xor-16, 8, 4, 2, 1 tree whatever the group size, so the grouping changes no bit.
 template <int GS>
-HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int t0, int t1, int te, int pos,
+constexpr int kScoreRows = GS >= 8 ? 4 : 8;
+
+// Rows tb .. tb + RW - 1 of a block whose cached rows [r0, te) sit in `slot` (null for a
+// block that holds only pos): one shared-memory load per cached row (index clamped inside
+// the slot, so no branch precedes it), the pos row loaded once if this group holds it,
+// rows from `tend` on (not this block's) and stale slot rows selected to zero.
+template <int RW>
+HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, const float* slot,
+                       int r0, const float* pos_s, int lane) {
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < RW; ++p) {
+    const int r = min(tb + p - r0, kSlotRows - 1);
+    kv[p] = slot ? reinterpret_cast<const float4*>(slot + (size_t)r * kHd)[lane] : zero;
+  }
+  const bool has_pos = pos >= tb && pos < tb + RW && pos < tend && pos >= te;
+  const float4 pv = has_pos ? reinterpret_cast<const float4*>(pos_s)[lane] : zero;
+#pragma unroll
+  for (int p = 0; p < RW; ++p) {
+    const int t = tb + p;
+    kv[p] = (t < te && t < tend) ? kv[p] : ((has_pos && t == pos) ? pv : zero);
+  }
+}
+
+// Scores of positions tb .. tb + kScoreRows - 1 (those below tend) for the GS heads, the
+// arithmetic of attn_chunk in attn_decode.cuh.
+template <int GS>
+HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int te, int pos,
                          const float* slot, int r0, const float* kpos_s, float scale,
                          float* lg_s) {
+  constexpr int RW = kScoreRows<GS>;
   const int lane = threadIdx.x & 31;
-  float4 kv[4];
+  float4 kv[RW];
+  block_rows<RW>(kv, tb, tend, te, pos, slot, r0, kpos_s, lane);
+  float v[RW * GS];
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int t = tb + p;
-    if (t < te) kv[p] = reinterpret_cast<const float4*>(slot + (size_t)(t - r0) * kHd)[lane];
-    else if (t < t1 && t == pos) kv[p] = reinterpret_cast<const float4*>(kpos_s)[lane];
-    else kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  float v[4 * GS];
-#pragma unroll
-  for (int p = 0; p < 4; ++p)
+  for (int p = 0; p < RW; ++p)
 #pragma unroll
     for (int i = 0; i < GS; ++i) {
       float s = qv[i].x * kv[p].x;
@@ -747,39 +838,38 @@ HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int t0, int t1, int te,
       v[p * GS + i] = s;
     }
   int idx;
-  const float tot = halving_reduce<4 * GS>(v, lane, &idx);
-  constexpr int dup = 32 / (4 * GS);
+  const float tot = halving_reduce<RW * GS>(v, lane, &idx);
+  constexpr int dup = 32 / (RW * GS) > 0 ? 32 / (RW * GS) : 1;
   if ((lane & (dup - 1)) == 0) {
     const int p = idx / GS, i = idx % GS;
     const int t = tb + p;
-    if (t < t1) lg_s[(t - t0) * GS + i] = tot * scale;
+    if (t < tend) lg_s[(t - t0) * GS + i] = tot * scale;
   }
 }
 
-// Probability-weighted V rows of one group into acc (the order of attn_chunk).
+// Probability-weighted V rows [tb, tb + 8) (those below tend) into acc, rows in order
+// (the order of attn_chunk); all loads are issued before the first multiply-add.
 template <int GS>
-HV_DEV void group_values(float4 (&acc)[GS], int tb, int t0, int t1, int te, int pos,
+HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, int pos,
                          const float* slot, int r0, const float* vpos_s, const float* lg_s) {
+  constexpr int RW = 8;
   const int lane = threadIdx.x & 31;
-  float4 vv[4];
+  float4 vv[RW];
+  float w[RW][GS];
+  block_rows<RW>(vv, tb, tend, te, pos, slot, r0, vpos_s, lane);
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int t = tb + p;
-    if (t < te) vv[p] = reinterpret_cast<const float4*>(slot + (size_t)(t - r0) * kHd)[lane];
-    else if (t < t1 && t == pos) vv[p] = reinterpret_cast<const float4*>(vpos_s)[lane];
-    else vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int p = 0; p < RW; ++p)
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int t = tb + p;
-    if (t < t1) {
+    for (int i = 0; i < GS; ++i) w[p][i] = (tb + p < tend) ? lg_s[(tb + p - t0) * GS + i] : 0.f;
+#pragma unroll
+  for (int p = 0; p < RW; ++p) {
+    if (tb + p < tend) {
 #pragma unroll
       for (int i = 0; i < GS; ++i) {
-        const float w = lg_s[(t - t0) * GS + i];
-        acc[i].x = fmaf(w, vv[p].x, acc[i].x);
-        acc[i].y = fmaf(w, vv[p].y, acc[i].y);
-        acc[i].z = fmaf(w, vv[p].z, acc[i].z);
-        acc[i].w = fmaf(w, vv[p].w, acc[i].w);
+        acc[i].x = fmaf(w[p][i], vv[p].x, acc[i].x);
+        acc[i].y = fmaf(w[p][i], vv[p].y, acc[i].y);
+        acc[i].z = fmaf(w[p][i], vv[p].z, acc[i].z);
+        acc[i].w = fmaf(w[p][i], vv[p].w, acc[i].w);
       }
     }
   }
@@ -787,7 +877,7 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int t0, int t1, int te, int 
 
 // The attention phase: this CTA's (kv head, chunk) work items, K and V rows streamed
 // through the ring (sequence numbers from *q). Same arithmetic, in the same order, as
-// attn_chunk with eight warps (k_attn): groups of 4 positions go to warp (group % 8)
+// attn_chunk with eight warps (k_attn): blocks of 20 positions go to warp (block % 8)
 // for the scores and the weighted V sum; warp i takes head i for the max and exp.
 template <int GS>
 __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
@@ -838,32 +928,39 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       vc[(size_t)pos * kHd + threadIdx.x] = vpos_s[threadIdx.x];
     }
 
-    // ---- scores: K rows from the ring, group gi = (t - t0) / 4 to warp gi % 8
+    // ---- scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows, row
+    // pos from kpos_s) to warp m % 8, so each slot has a single consumer warp; the block
+    // after the last slot holds only pos when pos starts a block
     float4 qv[GS];
 #pragma unroll
     for (int i = 0; i < GS; ++i) qv[i] = reinterpret_cast<const float4*>(q_s + i * kHd)[lane];
     bool ok = true;
-    for (int m = 0; m < nk; ++m) {
-      const unsigned q = qk + (unsigned)m;
-      ok = ok && warp_wait(R.full_of(q), R.parity(q), S, D.status);
-      if (ok) {
-        const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, te);
-        const float* slot = reinterpret_cast<const float*>(R.slot(q));
-        const int g0 = m * (kSlotRows / 4), g1 = (r1 - t0 + 3) / 4;
-        for (int gi = g0 + ((warp - g0) % kConsWarps + kConsWarps) % kConsWarps; gi < g1;
-             gi += kConsWarps)
-          group_scores<GS>(qv, t0 + 4 * gi, t0, t1, te, pos, slot, r0, kpos_s, scale, lg_s);
+    const int nblk = (n + kSlotRows - 1) / kSlotRows;
+    for (int m = warp; m < nblk && ok; m += kConsWarps) {
+      const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
+      const float* slot = nullptr;
+      if (m < nk) {
+        const unsigned q = qk + (unsigned)m;
+        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+        if (!ok) break;
+        slot = reinterpret_cast<const float*>(R.slot(q));
+      }
+      const long long c0 = clock64();
+      for (int tg = r0; tg < r1; tg += kScoreRows<GS>)
+        group_scores<GS>(qv, tg, r1, t0, te, pos, slot, r0, kpos_s, scale, lg_s);
+      if (lane == 0) S.busy[warp] += clock64() - c0;
+      if (m < nk) {
         __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(q), 1);
+        if (lane == 0) mbar_arrive_n(R.empty_of(qk + (unsigned)m), kConsWarps);
       }
     }
-    // a group that starts at pos (no cached row in it)
-    const bool pos_group = te < t1 && ((te - t0) & 3) == 0;
-    if (pos_group && ((te - t0) / 4) % kConsWarps == warp)
-      group_scores<GS>(qv, te, t0, t1, te, pos, nullptr, te, kpos_s, scale, lg_s);
     csync();
     trace_mark(D, tb + 15);
     trace_wait(D, S, tb + 21);
+    if (threadIdx.x == 0 && D.trace != nullptr) {
+      D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + tb + 25] = S.busy[0];
+      S.busy[0] = 0;
+    }
 
     // ---- per-head max and exp: warp i handles head i
     for (int i = warp; i < GS; i += kConsWarps) {
@@ -885,26 +982,27 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     trace_mark(D, tb + 16);
     trace_wait(D, S, tb + 20);
 
-    // ---- probability-weighted V sum: V rows from the ring, same group -> warp map
+    // ---- probability-weighted V sum: V rows from the ring, the same block -> warp map,
+    // positions in order within a block
     float4 acc[GS];
 #pragma unroll
     for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int m = 0; m < nk; ++m) {
-      const unsigned q = qv0 + (unsigned)m;
-      ok = ok && warp_wait(R.full_of(q), R.parity(q), S, D.status);
-      if (ok) {
-        const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, te);
-        const float* slot = reinterpret_cast<const float*>(R.slot(q));
-        const int g0 = m * (kSlotRows / 4), g1 = (r1 - t0 + 3) / 4;
-        for (int gi = g0 + ((warp - g0) % kConsWarps + kConsWarps) % kConsWarps; gi < g1;
-             gi += kConsWarps)
-          group_values<GS>(acc, t0 + 4 * gi, t0, t1, te, pos, slot, r0, vpos_s, lg_s);
+    for (int m = warp; m < nblk && ok; m += kConsWarps) {
+      const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
+      const float* slot = nullptr;
+      if (m < nk) {
+        const unsigned q = qv0 + (unsigned)m;
+        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+        if (!ok) break;
+        slot = reinterpret_cast<const float*>(R.slot(q));
+      }
+      for (int tg = r0; tg < r1; tg += 8)
+        group_values<GS>(acc, tg, r1, t0, te, pos, slot, r0, vpos_s, lg_s);
+      if (m < nk) {
         __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(q), 1);
+        if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)m), kConsWarps);
       }
     }
-    if (pos_group && ((te - t0) / 4) % kConsWarps == warp)
-      group_values<GS>(acc, te, t0, t1, te, pos, nullptr, te, vpos_s, lg_s);
 #pragma unroll
     for (int i = 0; i < GS; ++i)
       reinterpret_cast<float4*>(red_s + ((size_t)warp * GS + i) * kHd)[lane] = acc[i];
@@ -929,8 +1027,12 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     trace_mark(D, tb + 18);
     if (S.flag) {
       __threadfence();
-      attn_merge<GS, CSync>(D.part + (size_t)g * nch * GS * kPartStride, nch,
-                            D.ctx + (size_t)g * GS * kHd, red_s);
+      // the o projection's input, quantised here: int8 [qdim] then (scale, sum) pairs
+      int8_t* cq = reinterpret_cast<int8_t*>(D.ctx);
+      int2* csb = reinterpret_cast<int2*>(cq + (size_t)nq * kHd);
+      attn_merge<GS, CSync, true>(D.part + (size_t)g * nch * GS * kPartStride, nch, nullptr,
+                                  red_s, cq + (size_t)g * GS * kHd,
+                                  csb + (size_t)g * GS * kHd / kBlock);
       if (threadIdx.x == 0) D.ticket[g] = 0;
     }
     csync();
@@ -967,7 +1069,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     // no barrier of this launch can complete before this CTA arrives, so the counter's
     // top bit is still the one the previous launch left
     S.phase = ld_acquire(D.barrier) & 0x80000000u;
-    for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0;
+    for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0, S.busy[w] = 0;
   }
   {
     const int* src = reinterpret_cast<const int*>(D.plans);
@@ -1029,7 +1131,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 4);
     if (threadIdx.x == 0) prefetch_vectors(L, hid, false);
     // P3: o projection + residual
-    pro_quant(D.ctx, qdim, q_s, sb_s);
+    pro_load_quant(D.ctx, reinterpret_cast<const int2*>(reinterpret_cast<const int8_t*>(D.ctx) + qdim),
+                   qdim, q_s, sb_s);
     trace_mark(D, tb + 5);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
     gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
@@ -1042,9 +1145,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s);
     trace_mark(D, tb + 8);
     trace_wait(D, S, tb + 20);
-    phase_tiles(pp_tiles(2 * ffn, ffn), &off, &t0, &t1);
-    gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, D.act, nullptr, nullptr,
-                         work, S, D.status);
+    gu_tiles(ffn, &off, &t0, &t1);
+    {
+      // SiLU outputs staged after the leaf values, then quantised by the CTA that made them
+      const int nl = S.P.gv_hid.nleaf;
+      float* act_s = work + (nl > 1 ? (size_t)(t1 - t0) * 8 * nl : 0);
+      int8_t* aq = reinterpret_cast<int8_t*>(D.act);
+      gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, act_s, nullptr, nullptr,
+                           work, S, D.status);
+      csync();
+      quant_staged(act_s, (t1 - t0) * 4, t0 * 4, aq, reinterpret_cast<int2*>(aq + ffn));
+    }
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 9);
     trace_wait(D, S, tb + 24);
@@ -1055,7 +1166,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       else prefetch_l2(D.onorm, (size_t)hid * 4);
     }
     // P5: down + residual
-    pro_quant(D.act, ffn, q_s, sb_s);
+    pro_load_quant(D.act, reinterpret_cast<const int2*>(reinterpret_cast<const int8_t*>(D.act) + ffn),
+                   ffn, q_s, sb_s);
     trace_mark(D, tb + 11);
     trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
@@ -1063,7 +1175,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
-    trace_wait(D, S, tb + 25);
+    trace_wait(D, S, tb + 20);
     if (!grid_sync(D.barrier, D.status, S)) return;
     trace_mark(D, tb + 13);
   }
@@ -1238,8 +1350,10 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
       GvPlan gp;
       HV_REQUIRE(gv_make_plan(ks[i] / kBlock, &gp), HV_E_UNSUPPORTED,
                  "hv_step_launch: K = %d has too many pairwise leaves", ks[i]);
-      const size_t need = (size_t)((tiles[i] + sms - 1) / sms) * 8 * gp.nleaf * 4;
-      HV_REQUIRE(gp.nleaf == 1 || need <= lay.ring - lay.work, HV_E_UNSUPPORTED,
+      // gate/up: whole units of 8 tiles per CTA, plus 4 staged SiLU outputs per tile
+      const int per = i == 2 ? ((tiles[i] + 7) / 8 + sms - 1) / sms * 8 : (tiles[i] + sms - 1) / sms;
+      const size_t need = (size_t)per * (8 * (gp.nleaf > 1 ? gp.nleaf : 0) + (i == 2 ? 4 : 0)) * 4;
+      HV_REQUIRE(need <= lay.ring - lay.work, HV_E_UNSUPPORTED,
                  "hv_step_launch: %zu B of leaf values exceed the work area", need);
     }
   }

@@ -356,7 +356,7 @@ class Engine:
                     "o_prologue", "o_gemv", "barrier3", "gu_prologue", "gu_gemv", "barrier4",
                     "down_prologue", "down_gemv", "barrier5")
     TRACE_WAITS = ("wait_attn_scores", "wait_attn_values", "wait_qkv_gemv", "wait_gu_gemv",
-                   "wait_down_gemv")
+                   "attn_scores_busy_kcycles")
     TRACE_ATTN = ("attn_heads", "attn_scores", "attn_softmax", "attn_values", "attn_ticket",
                   "attn_merge")
 

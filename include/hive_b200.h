@@ -248,7 +248,8 @@ typedef struct hv_step_desc {
  * of the CTA): +14 q/k norms and RoPE, +15 scores, +16 softmax, +17 weighted V sum and
  * partials, +18 ticket, +19 merge (all %globaltimer ns). Durations (ns) that consumer
  * warp 0 spent waiting for its shared-memory ring slots: +21 attention scores, +22
- * attention V sum, +23 qkv GEMV, +24 gate/up GEMV, +25 down GEMV (+20 is scratch). Then
+ * attention V sum, +23 qkv GEMV, +24 gate/up GEMV (+20 is scratch); +25 = SM cycles
+ * warp 0 spent computing attention scores. Then
  * the head prologue, head GEMV and argmax at 2 + 26 n_layer + {0, 1, 2}; then, for the
  * producer warp: ns blocked on a ring slot still in use (+3), ns blocked on the copies in
  * flight (+4), slots copied (+5). */
