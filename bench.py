@@ -21,8 +21,11 @@ roofline : algorithmic bytes per step (int4 weights + f32 scales of every GEMV a
 cpu_baseline : the oracle (a C + numpy restatement of the reference's engine/reference.py)
            on the host cores, a bounded sample of decode steps at the same context.
 
---gpus N > 1 (under torchrun): N independent replicas, one per GPU, each decoding its own
-stream (weak scaling); value = total tok/s over all ranks.
+--gpus N > 1 (under torchrun): by default (--mode sharded) the N GPUs decode ONE stream
+together, every projection column-sharded across them with the all-gathers done inside
+the fused step as NVLink peer stores (strong scaling; value = that stream's tok/s, the
+roofline against N x the HBM peak); --mode replicas runs N independent streams (weak
+scaling; value = total tok/s).
 --impl reference: the reference's CPU algorithm (oracle port, all host threads) on rank 0.
 """
 from __future__ import annotations
@@ -87,6 +90,15 @@ class Dist:
         t = torch.tensor([x], dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
+
+    def allgather_bytes(self, blob: bytes) -> list[bytes]:
+        """All-gather of one bytes object per rank (host plumbing: the sharded engine's
+        one swap of CUDA IPC handles)."""
+        if not self.pg:
+            return [blob]
+        out = [None] * self.world
+        self.pg.all_gather_object(out, blob)
+        return out
 
     def close(self):
         if self.pg:
@@ -267,8 +279,11 @@ def run_ours(args, dist: Dist):
     cfg = w4format.Config(synth.ARCH[arch])
     cap = n_prompt + n_new
     t0 = time.perf_counter()
+    sharded = dist.world > 1 and args.mode == "sharded"
     eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
-                         max_context=cap, device=dist.local, fused=True)
+                         max_context=cap, device=dist.local, fused=True,
+                         world=dist.world if sharded else 1, rank=dist.rank if sharded else 0,
+                         exchange=dist.allgather_bytes if sharded else None)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
     window = cap - n_prompt              # decode positions available before a rewind
@@ -314,21 +329,25 @@ def run_ours(args, dist: Dist):
     eng._check_status()
     ms_max = dist.max(ms)
     ms_per_step = ms_max / args.steps
-    value = dist.world * args.steps / (ms_max / 1e3)
+    # replicas: every GPU decodes its own stream (weak scaling, tokens add up); sharded:
+    # the GPUs decode ONE stream together (strong scaling)
+    value = (1 if sharded else dist.world) * args.steps / (ms_max / 1e3)
 
     # algorithmic bytes over the timed steps (position of each step)
     positions = [n_prompt + ((first_step + i) % window) for i in range(args.steps)]
-    bytes_mean = float(np.mean([step_bytes(cfg, eng.n_head_rows, p) for p in positions]))
+    head_rows = eng.n_head_rows * (dist.world if sharded else 1)
+    n_peak = dist.world if sharded else 1        # the HBM of every GPU the stream uses
+    bytes_mean = float(np.mean([step_bytes(cfg, head_rows, p) for p in positions]))
     peak, peak_kind = measured_peak()
     achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
-    traffic = profiled_traffic("k_step_qwen3-8b_decode.md")
+    traffic = None if sharded else profiled_traffic("k_step_qwen3-8b_decode.md")
 
     # end to end through the public API: Engine.stream with host-fed tokens
     n_e2e = min(args.e2e_steps, window)
     ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True))
     times = [e[2] for e in ev if e[0] == "tok"]
     e2e = (len(times) - 1) / (times[-1] - times[0]) if len(times) > 1 else None
-    e2e_all = dist.sum(e2e or 0.0) if dist.world > 1 else e2e
+    e2e_all = dist.sum(e2e or 0.0) if dist.world > 1 and not sharded else e2e
 
     line = None
     if dist.rank == 0:
@@ -343,16 +362,19 @@ def run_ours(args, dist: Dist):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+            "vs_baseline": None,
             "dtype": "int8", "data": "synthetic (seeded random-init weights and prompt)",
             "config": {"workload": args.workload, "model": arch, "batch": 1,
                        "prompt": n_prompt, "generated": n_new, "kv": "f32",
                        "weights": "int4 + f32 scale per 32 (5.00 bits/weight)",
-                       "parallelism": "replicas" if dist.world > 1 else "single",
+                       "parallelism": (f"column-sharded x{dist.world} (NVLink peer stores "
+                                       "inside the fused step)" if sharded else
+                                       "replicas" if dist.world > 1 else "single"),
                        "l2": "inputs larger than L2 (5.9 GB read per step)",
                        "positions": f"{min(positions)}..{max(positions)}"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
-                         "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * n_peak,
+                         "unit": "GB/s", "frac": achieved / (peak * n_peak), "traffic": traffic,
                          "peak_kind": peak_kind, "kernel": "k_step",
                          "bytes_per_step": bytes_mean},
             "cpu_baseline": cpu,
@@ -378,6 +400,9 @@ def main(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
+                    help="with more than one GPU: shard one stream across them (column "
+                         "parallel) or run one independent stream per GPU")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -168,6 +168,29 @@ int hv_copy_async(void* dst, const void* src, size_t nbytes, void* stream) {
   return HV_OK;
 }
 
+int hv_ipc_handle(const void* dev_ptr, void* handle_out) {
+  HV_REQUIRE(dev_ptr && handle_out, HV_E_INVALID, "hv_ipc_handle: null pointer");
+  static_assert(sizeof(cudaIpcMemHandle_t) == HV_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  HV_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  memcpy(handle_out, &h, sizeof(h));
+  return HV_OK;
+}
+
+int hv_ipc_open(const void* handle, void** dev_ptr) {
+  HV_REQUIRE(handle && dev_ptr, HV_E_INVALID, "hv_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  HV_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return HV_OK;
+}
+
+int hv_ipc_close(void* dev_ptr) {
+  HV_REQUIRE(dev_ptr, HV_E_INVALID, "hv_ipc_close: null pointer");
+  HV_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return HV_OK;
+}
+
 int hv_stream_create(void** stream) {
   HV_REQUIRE(stream, HV_E_INVALID, "hv_stream_create: null pointer");
   cudaStream_t s;

@@ -241,28 +241,48 @@ struct Ring {
   HV_DEV unsigned parity(unsigned q) const { return (q / ns) & 1u; }
 };
 
-// Grid-wide barrier of the consumer threads over a self-resetting counter: CTA 0 adds
-// 2^31 - (grid - 1), the others add 1, so the top bit flips exactly when all have arrived
-// and the low bits return to zero. Each CTA knows which top bit to wait for (S.phase,
-// read once per launch and flipped at every barrier), so arriving is a fire-and-forget
-// release add and waiting is one acquire load per poll. The wait is bounded: after
-// kWaitNs (or once another CTA has reported a failure, or this CTA aborted) it records
-// the failure and returns false in every consumer thread.
-HV_DEV bool grid_sync(unsigned* bar, int* status, StepShared& S) {
+HV_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier of the consumer threads (of every rank's grid when the step is
+// sharded) over a self-resetting counter: the first CTA of rank 0 adds
+// 2^31 - (world * grid - 1), every other CTA adds 1, so the top bit flips exactly when all
+// have arrived and the low bits return to zero. Each rank keeps its own counter and every
+// arrival goes to all of them (NVLink atomics), so a CTA polls only local memory. Each
+// CTA knows which top bit to wait for (S.phase, read once per launch and flipped at every
+// barrier), so arriving is a fire-and-forget release add and waiting is one acquire load
+// per poll. The wait is bounded: after kWaitNs (or once this rank reported a failure, or
+// this CTA aborted) it records the failure and returns false in every consumer thread.
+HV_DEV bool grid_sync(const hv_step_desc& D, StepShared& S) {
   csync();
   if (threadIdx.x == 0) {
     int ok = *(volatile int*)&S.abort == 0;
     if (ok) {
-      const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
+      const bool sharded = D.world > 1;
+      const unsigned total = gridDim.x * (sharded ? (unsigned)D.world : 1u);
+      const bool first = blockIdx.x == 0 && (!sharded || D.rank == 0);
+      const unsigned add = first ? (0x80000000u - (total - 1)) : 1u;
       const unsigned want = S.phase ^ 0x80000000u;
-      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(bar), "r"(add) : "memory");
+      if (sharded) {
+        __threadfence_system();     // this CTA's peer stores before its arrival
+        for (int k = 0; k < D.world; ++k)
+          asm volatile("red.release.sys.global.add.u32 [%0], %1;"
+                       :: "l"(D.peers->barrier[k]), "r"(add) : "memory");
+      } else {
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(D.barrier), "r"(add)
+                     : "memory");
+      }
       const unsigned long long t0 = global_ns();
       for (unsigned n = 1;; ++n) {
-        if ((ld_acquire(bar) & 0x80000000u) == want) break;
+        const unsigned v = sharded ? ld_acquire_sys(D.barrier) : ld_acquire(D.barrier);
+        if ((v & 0x80000000u) == want) break;
         if ((n & 31) == 0) {
-          if (*(volatile int*)status != 0) { ok = 0; break; }
+          if (*(volatile int*)D.status != 0) { ok = 0; break; }
           if (global_ns() - t0 > kWaitNs) {
-            atomicCAS(status, 0, HV_E_TIMEOUT);
+            atomicCAS(D.status, 0, HV_E_TIMEOUT);
             ok = 0;
             break;
           }
@@ -459,11 +479,12 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
 HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int pos,
                     const Ring& R, StepShared& S, int inflight, int evict_first) {
   Producer P(R, S, D.status, inflight, evict_first);
-  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
+  const int world = D.world > 1 ? D.world : 1;
+  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd * world, hrows = hid / world;
   const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
   const int nch = D.attn_chunks;
   const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
-            it_ffn = pp_iters(ffn / kBlock);
+            it_ffn = pp_iters(ffn * world / kBlock);
   int off = 0, t0, t1;
   for (int l = 0; l < D.n_layer && P.live; ++l) {
     const hv_layer_w* L = Ls + l;
@@ -474,11 +495,11 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
       attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
       P.kv(L->kc, L->vc, wi / nch, D.cap, a0, ae);
     }
-    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
     gu_tiles(ffn, &off, &t0, &t1);
     P.gemv(L->gu_b4, L->gu_sw, it_hid, t0, t1, S.P.gv_hid.nleaf);
-    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
+    phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->dn_b4, L->dn_sw, it_ffn, t0, t1, S.P.gv_ffn.nleaf);
   }
   if ((flags & HV_STEP_HEAD) && P.live) {
@@ -612,9 +633,74 @@ __device__ __noinline__ void quant_staged(const float* vals, int nval, int first
 }
 
 
+// Sharded head: every rank's winner (value, global index) goes into every rank's
+// exchange row [rank]; once all `world` rows carry this launch's sequence number, the
+// overall winner (lowest index on ties, as np.argmax) is the same on every rank. The
+// sequence number is a launch counter kept in row HV_MAX_WORLD of the local exchange
+// array (every rank makes the same launches, so the counters agree). One thread; the
+// wait is bounded (false and HV_E_TIMEOUT when it runs out).
+HV_DEV bool exchange_argmax(const hv_step_desc& D, int rank, int world, float* v, int* idx) {
+  int32_t* mine = D.peers->xchg[rank];
+  const int seq = mine[HV_MAX_WORLD * 4] + 1;
+  mine[HV_MAX_WORLD * 4] = seq;
+  for (int k = 0; k < world; ++k) {
+    int32_t* row = D.peers->xchg[k] + rank * 4;
+    row[0] = __float_as_int(*v);
+    row[1] = *idx;
+  }
+  __threadfence_system();
+  for (int k = 0; k < world; ++k)
+    asm volatile("st.release.sys.global.s32 [%0], %1;" :: "l"(D.peers->xchg[k] + rank * 4 + 2),
+                 "r"(seq) : "memory");
+  const unsigned long long t0 = global_ns();
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int j = 0; j < world; ++j) {
+    const unsigned* flag = reinterpret_cast<const unsigned*>(mine + j * 4 + 2);
+    while ((int)ld_acquire_sys(flag) != seq) {
+      if (global_ns() - t0 > kWaitNs) {
+        atomicCAS(D.status, 0, HV_E_TIMEOUT);
+        return false;
+      }
+    }
+    const float cv = __int_as_float(__ldcv(mine + j * 4));
+    const int ci = __ldcv(mine + j * 4 + 1);
+    if (cv > bv || (cv == bv && ci < bi)) { bv = cv; bi = ci; }
+  }
+  *v = bv;
+  *idx = bi;
+  return true;
+}
+
+// Copies n quantised values starting at element `first` (first, n multiples of 32) of a
+// quantised vector of `len` elements (int8 [len], then (scale, sum) per 32) from this
+// rank's buffer `mine` into every other rank's copy. Cooperative over the consumers.
+__device__ __noinline__ void share_bytes(void* const* peers, int rank, int world,
+                                         const int8_t* mine, int first, int n, int len) {
+  const uint4* q = reinterpret_cast<const uint4*>(mine + first);
+  const int2* sb = reinterpret_cast<const int2*>(mine + len) + first / kBlock;
+  for (int k = 0; k < world; ++k) {
+    if (k == rank) continue;
+    int8_t* dst = reinterpret_cast<int8_t*>(peers[k]);
+    uint4* dq = reinterpret_cast<uint4*>(dst + first);
+    int2* dsb = reinterpret_cast<int2*>(dst + len) + first / kBlock;
+    for (int i = threadIdx.x; i < n / 16; i += kConsThreads) dq[i] = q[i];
+    for (int i = threadIdx.x; i < n / kBlock; i += kConsThreads) dsb[i] = sb[i];
+  }
+}
+
 // ---- GEMV phases from the ring ----------------------------------------------------------
 
 enum { kStore = 0, kResidual = 1, kSiluPair = 2, kHead = 3 };
+
+// Where a GEMV phase's rows go. Row r of the CTA's matrix is global row row0 + r; with a
+// sharded step (world > 1) the residual rows are also stored into every other rank's h.
+struct OutCtx {
+  float* out;
+  int row0;
+  int world, rank;
+  const hv_step_peers* peers;
+};
 
 HV_DEV int pp_row_of(int tile, int g, int rows, int pair_ffn, bool* ok) {
   if (pair_ffn > 0) {
@@ -628,20 +714,25 @@ HV_DEV int pp_row_of(int tile, int g, int rows, int pair_ffn, bool* ok) {
 }
 
 template <int MODE>
-HV_DEV void gemv_epilogue(float y, int row, bool ok, float* __restrict__ out, float* best_v,
+HV_DEV void gemv_epilogue(float y, int row, bool ok, const OutCtx& O, float* best_v,
                           int* best_i) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (MODE == kSiluPair) {
     const float up = __shfl_down_sync(0xFFFFFFFFu, y, 16);
-    if (g < 4 && t == 0 && ok) out[row] = silu_mul1(y, up);
+    if (g < 4 && t == 0 && ok) O.out[row] = silu_mul1(y, up);
   } else if (t == 0 && ok) {
     if (MODE == kStore) {
-      out[row] = y;
+      O.out[row] = y;
     } else if (MODE == kResidual) {
-      out[row] = __fadd_rn(__ldcg(out + row), y);
+      const int gr = O.row0 + row;
+      const float v = __fadd_rn(__ldcg(O.out + gr), y);
+      O.out[gr] = v;
+      for (int k = 0; k < O.world; ++k)
+        if (k != O.rank) O.peers->h[k][gr] = v;
     } else {
-      out[row] = y;
-      if (y > *best_v || (y == *best_v && row < *best_i)) { *best_v = y; *best_i = row; }
+      O.out[row] = y;
+      const int gr = O.row0 + row;                      // global vocab index
+      if (y > *best_v || (y == *best_v && gr < *best_i)) { *best_v = y; *best_i = gr; }
     }
   }
 }
@@ -678,7 +769,7 @@ HV_DEV float2 slot_terms(const unsigned char* sl, int u, const unsigned* __restr
 template <int MODE>
 __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan& P,
                                        const ActView act, int t0, int t1, int rows,
-                                       int pair_ffn, float* __restrict__ out, float* best_v,
+                                       int pair_ffn, const OutCtx O, float* best_v,
                                        int* best_i, float* leafbuf, StepShared& S,
                                        int* status) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -740,7 +831,7 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
       bool ok;
       int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
       if (MODE == kSiluPair) row -= 4 * t0;            // staged in shared memory
-      gemv_epilogue<MODE>(__fadd_rn(0.0f, v), row, ok, out, best_v, best_i);
+      gemv_epilogue<MODE>(__fadd_rn(0.0f, v), row, ok, O, best_v, best_i);
     } else if (t == 0) {
       leafbuf[((size_t)lt * 8 + g) * nleaf + lf] = v;
     }
@@ -752,7 +843,7 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
       int row = pp_row_of(t0 + lt, g, rows, pair_ffn, &ok);
       if (MODE == kSiluPair) row -= 4 * t0;
       const float y = fold_leaves(P, leafbuf + ((size_t)lt * 8 + g) * nleaf);
-      gemv_epilogue<MODE>(y, row, ok, out, best_v, best_i);
+      gemv_epilogue<MODE>(y, row, ok, O, best_v, best_i);
     }
   }
 }
@@ -1027,13 +1118,19 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     trace_mark(D, tb + 18);
     if (S.flag) {
       __threadfence();
-      // the o projection's input, quantised here: int8 [qdim] then (scale, sum) pairs
+      // the o projection's input, quantised here: int8 [qdim] then (scale, sum) pairs;
+      // this rank's heads start at head rank * n_head of the whole vector
+      const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
+      const int qall = nq * kHd * world, first = (rank * nq + g * GS) * kHd;
       int8_t* cq = reinterpret_cast<int8_t*>(D.ctx);
-      int2* csb = reinterpret_cast<int2*>(cq + (size_t)nq * kHd);
+      int2* csb = reinterpret_cast<int2*>(cq + qall);
       attn_merge<GS, CSync, true>(D.part + (size_t)g * nch * GS * kPartStride, nch, nullptr,
-                                  red_s, cq + (size_t)g * GS * kHd,
-                                  csb + (size_t)g * GS * kHd / kBlock);
+                                  red_s, cq + first, csb + first / kBlock);
       if (threadIdx.x == 0) D.ticket[g] = 0;
+      if (world > 1) {
+        csync();
+        share_bytes(D.peers->ctx, rank, world, cq, first, GS * kHd, qall);
+      }
     }
     csync();
     trace_mark(D, tb + 19);
@@ -1047,8 +1144,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
                                                           int nslots, int inflight,
                                                           int evict_first) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd;
-  const StepLayout Lo = step_layout(GS, hid, qdim, ffn, D.cap, D.attn_chunks, nslots, D.n_layer);
+  // sharded: n_head, n_kv, ffn and head_rows are this rank's; hidden, the o projection's
+  // input (qdim) and the down projection's input (ffn_all) are whole
+  const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
+  const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd * world, ffn_all = ffn * world;
+  const int hrows = hid / world;
+  const StepLayout Lo =
+      step_layout(GS, hid, qdim, ffn_all, D.cap, D.attn_chunks, nslots, D.n_layer);
   StepShared& S = *reinterpret_cast<StepShared*>(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint4* q_s = reinterpret_cast<uint4*>(smem + Lo.act_q);
@@ -1103,7 +1205,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     for (int i = r0 + threadIdx.x; i < r1; i += kConsThreads) D.h[i] = __half2float(emb_row[i]);
   }
   const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
-            it_ffn = pp_iters(ffn / kBlock);
+            it_ffn = pp_iters(ffn_all / kBlock);
+  const OutCtx o_qkv{D.qkv, 0, 1, 0, nullptr};
+  const OutCtx o_h{D.h, rank * hrows, world, rank, D.peers};
+  const OutCtx o_head{D.logits, rank * D.head_rows, 1, 0, nullptr};
+  int8_t* const cq = reinterpret_cast<int8_t*>(D.ctx);     // int8 [qdim], then (s, sum)
+  int8_t* const aq = reinterpret_cast<int8_t*>(D.act);     // int8 [ffn_all], then (s, sum)
   unsigned q = 0;
   int off = 0, t0, t1;
   if (threadIdx.x == 0) prefetch_vectors(Ls, hid, true);
@@ -1117,29 +1224,28 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 0);
     trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
-    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, D.qkv, nullptr, nullptr, work,
+    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, o_qkv, nullptr, nullptr, work,
                       S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
     trace_wait(D, S, tb + 23);
-    if (!grid_sync(D.barrier, D.status, S)) return;
+    if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 2);
     // P2: attention
     attn_ring<GS>(D, L, pos, R, &q, S, work, tb);
     trace_mark(D, tb + 3);
-    if (!grid_sync(D.barrier, D.status, S)) return;
+    if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 4);
     if (threadIdx.x == 0) prefetch_vectors(L, hid, false);
     // P3: o projection + residual
-    pro_load_quant(D.ctx, reinterpret_cast<const int2*>(reinterpret_cast<const int8_t*>(D.ctx) + qdim),
-                   qdim, q_s, sb_s);
+    pro_load_quant(cq, reinterpret_cast<const int2*>(cq + qdim), qdim, q_s, sb_s);
     trace_mark(D, tb + 5);
-    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
+    phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
+    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_q));
     trace_mark(D, tb + 6);
-    if (!grid_sync(D.barrier, D.status, S)) return;
+    if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
     pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s);
@@ -1150,33 +1256,37 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       // SiLU outputs staged after the leaf values, then quantised by the CTA that made them
       const int nl = S.P.gv_hid.nleaf;
       float* act_s = work + (nl > 1 ? (size_t)(t1 - t0) * 8 * nl : 0);
-      int8_t* aq = reinterpret_cast<int8_t*>(D.act);
-      gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, act_s, nullptr, nullptr,
-                           work, S, D.status);
+      const OutCtx o_act{act_s, 0, 1, 0, nullptr};
+      gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, o_act, nullptr,
+                           nullptr, work, S, D.status);
       csync();
-      quant_staged(act_s, (t1 - t0) * 4, t0 * 4, aq, reinterpret_cast<int2*>(aq + ffn));
+      const int first = rank * ffn + t0 * 4;               // this CTA's outputs, whole blocks
+      quant_staged(act_s, (t1 - t0) * 4, first, aq, reinterpret_cast<int2*>(aq + ffn_all));
+      if (world > 1) {
+        csync();
+        share_bytes(D.peers->act, rank, world, aq, first, (t1 - t0) * 4, ffn_all);
+      }
     }
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 9);
     trace_wait(D, S, tb + 24);
-    if (!grid_sync(D.barrier, D.status, S)) return;
+    if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 10);
     if (threadIdx.x == 0) {
       if (l + 1 < D.n_layer) prefetch_vectors(L + 1, hid, true);
       else prefetch_l2(D.onorm, (size_t)hid * 4);
     }
     // P5: down + residual
-    pro_load_quant(D.act, reinterpret_cast<const int2*>(reinterpret_cast<const int8_t*>(D.act) + ffn),
-                   ffn, q_s, sb_s);
+    pro_load_quant(aq, reinterpret_cast<const int2*>(aq + ffn_all), ffn_all, q_s, sb_s);
     trace_mark(D, tb + 11);
     trace_wait(D, S, tb + 20);
-    phase_tiles(pp_tiles(hid, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hid, 0, D.h, nullptr, nullptr, work,
+    phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
+    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
     trace_wait(D, S, tb + 20);
-    if (!grid_sync(D.barrier, D.status, S)) return;
+    if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 13);
   }
 
@@ -1187,7 +1297,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
-  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, D.logits, &bv, &bi, work,
+  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, o_head, &bv, &bi, work,
                    S, D.status);
   trace_mark(D, th + 1);
   if (!(flags & HV_STEP_ARGMAX)) return;
@@ -1224,6 +1334,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
         const int ci = __ldcg(D.amax_i + c);
         if (cv > v || (cv == v && ci < idx)) { v = cv; idx = ci; }
       }
+      if (world > 1 && !exchange_argmax(D, rank, world, &v, &idx)) return;
       *D.tok = idx;
       const int s = *D.step;
       if (s >= 0 && s <= D.cap) D.gen[s] = idx;      // gen holds cap + 1 entries
@@ -1330,12 +1441,21 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const int gs = h.n_head / h.n_kv;
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
-  const int qdim = h.n_head * kHd;
-  const int nslots = step_slots(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, h.n_layer);
+  HV_REQUIRE(h.world >= 1 && h.world <= HV_MAX_WORLD && h.rank >= 0 && h.rank < h.world,
+             HV_E_INVALID, "hv_step_launch: rank %d of world %d", h.rank, h.world);
+  HV_REQUIRE(h.world == 1 || h.peers != nullptr, HV_E_INVALID,
+             "hv_step_launch: a sharded step needs the peer table");
+  HV_REQUIRE(h.hidden % (8 * h.world) == 0, HV_E_UNSUPPORTED,
+             "hv_step_launch: hidden %d does not split into 8-row tiles over %d ranks",
+             h.hidden, h.world);
+  const int world = h.world;
+  const int qdim = h.n_head * kHd * world, ffn_all = h.ffn * world;
+  const int nslots =
+      step_slots(gs, h.hidden, qdim, ffn_all, h.cap, h.attn_chunks, h.n_layer);
   HV_REQUIRE(nslots >= 4, HV_E_UNSUPPORTED,
              "hv_step_launch: shared memory leaves %d ring slots (need 4)", nslots);
   const StepLayout lay =
-      step_layout(gs, h.hidden, qdim, h.ffn, h.cap, h.attn_chunks, nslots, h.n_layer);
+      step_layout(gs, h.hidden, qdim, ffn_all, h.cap, h.attn_chunks, nslots, h.n_layer);
   const size_t smem = lay.total;
   int sms = 0;
   int rc = sm_count(&sms);
@@ -1343,9 +1463,10 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   {
     // multi-leaf GEMV rows meet in the work area: tiles per CTA x 8 rows x leaves
     const int nqkv = (h.n_head + 2 * h.n_kv) * kHd;
-    const int tiles[5] = {pp_tiles(nqkv, 0), pp_tiles(h.hidden, 0), pp_tiles(2 * h.ffn, h.ffn),
-                          pp_tiles(h.hidden, 0), pp_tiles(h.head_rows, 0)};
-    const int ks[5] = {h.hidden, qdim, h.hidden, h.ffn, h.hidden};
+    const int hrows = h.hidden / world;
+    const int tiles[5] = {pp_tiles(nqkv, 0), pp_tiles(hrows, 0), pp_tiles(2 * h.ffn, h.ffn),
+                          pp_tiles(hrows, 0), pp_tiles(h.head_rows, 0)};
+    const int ks[5] = {h.hidden, qdim, h.hidden, ffn_all, h.hidden};
     for (int i = 0; i < 5; ++i) {
       GvPlan gp;
       HV_REQUIRE(gv_make_plan(ks[i] / kBlock, &gp), HV_E_UNSUPPORTED,

@@ -21,7 +21,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 LIB_NAME = "libhive_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _L = None
 _lib_path = None
@@ -96,6 +96,9 @@ _SIGS = {
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
     "hv_step_set_option": [_I, _I],
+    "hv_ipc_handle": [_VP, _VP],
+    "hv_ipc_open": [_VP, C.POINTER(_VP)],
+    "hv_ipc_close": [_VP],
     "hv_step_plans_bytes": [C.POINTER(_SZ)],
     "hv_step_plans": [_I, _I, _I, _VP, _SZ],
 }
@@ -373,6 +376,29 @@ def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
 
 def attn_reserve(nkv, group, cap):
     _call("hv_attn_reserve", nkv, group, cap)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_handle(ptr) -> bytes:
+    """64-byte CUDA IPC handle of a device allocation made by this process."""
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    _call("hv_ipc_handle", _p(ptr), buf)
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's allocation (its ipc_handle) into this process."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("an IPC handle is 64 bytes")
+    out = _VP()
+    _call("hv_ipc_open", C.create_string_buffer(handle, IPC_HANDLE_BYTES), C.byref(out))
+    return int(out.value)
+
+
+def ipc_close(ptr):
+    _call("hv_ipc_close", _p(ptr))
 
 
 STEP_OPT_INFLIGHT = 1

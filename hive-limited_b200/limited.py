@@ -46,11 +46,43 @@ class _StepDesc(C.Structure):
                     "layers", "emb16", "onorm", "head_b4", "head_sw", "cos_t", "sin_t",
                     "tok", "pos", "step", "gen", "h", "qkv", "ctx", "act", "logits",
                     "part", "ticket", "amax_v", "amax_i", "barrier", "status", "trace",
-                    "plans")])
+                    "plans")]
+                + [("world", C.c_int), ("rank", C.c_int), ("peers", C.c_void_p)])
+
+
+MAX_WORLD = 8
+
+
+class _StepPeers(C.Structure):
+    _fields_ = [(n, C.c_void_p * MAX_WORLD) for n in ("h", "ctx", "act", "barrier", "xchg")]
 
 
 STEP_HEAD = 1
 STEP_ARGMAX = 2
+
+
+def shard_plan(cfg, world: int, rank: int) -> dict:
+    """Rows of every projection held by `rank` of `world` (column-parallel sharding: each
+    output element is computed whole on one GPU, so results match one GPU bit for bit).
+    -> {"q": (r0, r1) q-proj rows, "kv": (r0, r1) rows of k-proj and of v-proj,
+        "hid": (r0, r1) rows of o-proj and down-proj, "ffn": (r0, r1) rows of gate and of
+        up, "vocab": (r0, r1) LM-head rows, "n_head", "n_kv", "ffn_n", "vocab_n"}"""
+    if not 1 <= world <= MAX_WORLD or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world} (1..{MAX_WORLD} ranks)")
+    qd = cfg.head_dim
+    for name, n, unit in (("n_head", cfg.n_head, 1), ("n_kv", cfg.n_kv, 1),
+                          ("hidden", cfg.hidden, 8), ("ffn", cfg.ffn, 32),
+                          ("vocab", cfg.vocab, 1)):
+        if n % (world * unit):
+            raise ValueError(f"{name} = {n} does not split into {world} shards of whole "
+                             f"{unit}-row units")
+    nh, nk = cfg.n_head // world, cfg.n_kv // world
+    hs, fs, vs = cfg.hidden // world, cfg.ffn // world, cfg.vocab // world
+    return {"q": (rank * nh * qd, (rank + 1) * nh * qd),
+            "kv": (rank * nk * qd, (rank + 1) * nk * qd),
+            "hid": (rank * hs, (rank + 1) * hs), "ffn": (rank * fs, (rank + 1) * fs),
+            "vocab": (rank * vs, (rank + 1) * vs),
+            "n_head": nh, "n_kv": nk, "ffn_n": fs, "vocab_n": vs}
 
 
 class _TensorSource:
@@ -85,12 +117,18 @@ class Engine:
       max_context       -- KV capacity (the reference fixes 4096);
       device            -- CUDA device index;
       fused             -- use the one-launch fused step (default) or the eager sequence;
-      quantize_on       -- "device" (hv_quantize_w4, bit-identical) or "host" (numpy).
+      quantize_on       -- "device" (hv_quantize_w4, bit-identical) or "host" (numpy);
+      world / rank / exchange
+                        -- column-parallel sharding over `world` GPUs, one process per GPU:
+                           this engine holds rank `rank`'s rows of every projection and its
+                           heads; `exchange(bytes) -> list[bytes]` is an all-gather over the
+                           ranks (any transport) used once, to swap the CUDA IPC handles of
+                           the buffers the fused step writes into on every rank.
     """
 
     def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
                  config=None, tensors=None, max_context=None, device=0, fused=True,
-                 quantize_on="device"):
+                 quantize_on="device", world=1, rank=0, exchange=None):
         if config is None:
             self.cfg = Config.load(model_dir)
         else:
@@ -100,6 +138,13 @@ class Engine:
         self.quiet = quiet
         self.fused = bool(fused)
         self._buffers: list[int] = []
+        self._opened: list[int] = []
+        self.world, self.rank = int(world), int(rank)
+        self.shard = shard_plan(self.cfg, self.world, self.rank)
+        if self.world > 1 and (not self.fused or exchange is None):
+            raise ValueError("a sharded engine runs the fused step and needs `exchange`")
+        self._exchange = exchange
+        self.d_peers = None
         hvdrv.load(kernels_dir, verify=verify_kernels)
         hvdrv.init()
         self.dev = hvdrv.device(device)
@@ -181,19 +226,24 @@ class Engine:
             emb16 = emb.astype(np.float16)
             del emb
             self.d_emb16 = self._up(emb16)
+            sh = self.shard
+            v0, v1 = sh["vocab"]
             if c.tied:                        # the reference quantises the f16 copy
-                self.head = self._up_w4([emb16.astype(F32)])
+                self.head = self._up_w4([emb16[v0:v1].astype(F32)])
             del emb16
             self.layers = []
             for l in range(c.n_layer):
                 p = f"model.layers.{l}."
                 t = lambda n: src.take(p + n)  # noqa: E731
-                qkv = self._up_w4([t("self_attn.q_proj.weight"), t("self_attn.k_proj.weight"),
-                                   t("self_attn.v_proj.weight")])
-                o = self._up_w4([t("self_attn.o_proj.weight")])
-                gu = self._up_w4([t("mlp.gate_proj.weight"), t("mlp.up_proj.weight")],
-                                 pair_ffn=c.ffn)
-                down = self._up_w4([t("mlp.down_proj.weight")])
+                (q0, q1), (k0, k1) = sh["q"], sh["kv"]
+                (h0, h1), (f0, f1) = sh["hid"], sh["ffn"]
+                qkv = self._up_w4([t("self_attn.q_proj.weight")[q0:q1],
+                                   t("self_attn.k_proj.weight")[k0:k1],
+                                   t("self_attn.v_proj.weight")[k0:k1]])
+                o = self._up_w4([t("self_attn.o_proj.weight")[h0:h1]])
+                gu = self._up_w4([t("mlp.gate_proj.weight")[f0:f1],
+                                  t("mlp.up_proj.weight")[f0:f1]], pair_ffn=f1 - f0)
+                down = self._up_w4([t("mlp.down_proj.weight")[h0:h1]])
                 self.layers.append({
                     "an": self._up(t("input_layernorm.weight").astype(F32)),
                     "fn": self._up(t("post_attention_layernorm.weight").astype(F32)),
@@ -205,7 +255,7 @@ class Engine:
                     self._log(f"  {l + 1}/{c.n_layer}")
             self.d_onorm = self._up(src.take("model.norm.weight").astype(F32))
             if not c.tied:
-                self.head = self._up_w4([src.take("lm_head.weight")])
+                self.head = self._up_w4([src.take("lm_head.weight")[v0:v1]])
             self.n_head_rows = self.head[3]
         finally:
             if self._stage:
@@ -215,8 +265,9 @@ class Engine:
     def _alloc_state(self):
         c = self.cfg
         hid, ffn, qd = c.hidden, c.ffn, c.head_dim
-        nq, nkv, cap = c.n_head, c.n_kv, c.max_context
-        qkv_rows = (nq + 2 * nkv) * qd
+        nq, cap = c.n_head, c.max_context
+        nkv = self.shard["n_kv"]                     # this rank's kv heads (all, unsharded)
+        qkv_rows = (self.shard["n_head"] + 2 * nkv) * qd
         wide = max(hid, ffn, nq * qd)
         self.d_h = self._alloc(hid * 4)
         self.d_hn = self._alloc(hid * 4)
@@ -256,9 +307,10 @@ class Engine:
         """The fused step's descriptor and its scratch (engine/limited.py has no
         equivalent: the reference issues each kernel separately)."""
         c = self.cfg
+        sh = self.shard
         grid, threads = C.c_int(), C.c_int()
         smem, chunks, part = C.c_size_t(), C.c_int(), C.c_size_t()
-        hvdrv._call("hv_step_config", c.n_kv, c.group, c.max_context, C.byref(grid),
+        hvdrv._call("hv_step_config", sh["n_kv"], c.group, c.max_context, C.byref(grid),
                     C.byref(threads), C.byref(smem), C.byref(chunks), C.byref(part))
         self.step_grid = grid.value
         lw = (_LayerW * c.n_layer)()
@@ -269,8 +321,8 @@ class Engine:
         self.d_layers = self._alloc(C.sizeof(lw))
         hvdrv.upload(self.d_layers, C.addressof(lw), C.sizeof(lw))
         self.d_part = self._alloc(part.value * 4)
-        self.d_ticket = self._alloc((c.n_kv + 1) * 4)
-        hvdrv.memset8(self.d_ticket, 0, (c.n_kv + 1) * 4)
+        self.d_ticket = self._alloc((sh["n_kv"] + 1) * 4)
+        hvdrv.memset8(self.d_ticket, 0, (sh["n_kv"] + 1) * 4)
         self.d_amax_v = self._alloc(grid.value * 4)
         self.d_amax_i = self._alloc(grid.value * 4)
         self.d_barrier = self._alloc(4)
@@ -285,13 +337,43 @@ class Engine:
         self.d_plans = self._alloc(nbytes.value)
         hvdrv.upload(self.d_plans, C.addressof(plans), nbytes.value)
         hb4, hsw, _, hn, _ = self.head
+        if self.world > 1:
+            self._connect_peers()
         self._desc = _StepDesc(
-            c.n_layer, c.hidden, c.ffn, c.n_head, c.n_kv, c.head_dim, hn, c.max_context,
+            c.n_layer, c.hidden, sh["ffn_n"], sh["n_head"], sh["n_kv"], c.head_dim, hn,
+            c.max_context,
             RMS_EPS, float(self.attn_scale), chunks.value, c.vocab,
             self.d_layers, self.d_emb16, self.d_onorm, hb4, hsw, self.d_cos, self.d_sin,
             self.d_tok, self.d_pos, self.d_step, self.d_gen, self.d_h, self.d_qkv,
             self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
-            self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans)
+            self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans,
+            self.world, self.rank, self.d_peers)
+
+    def _connect_peers(self):
+        """Swap CUDA IPC handles of the buffers every rank's step writes into (residual,
+        quantised attention output and SiLU output, barrier word, argmax exchange) and
+        upload the peer table. The barrier and exchange words are zeroed before the swap,
+        so no rank's first launch can meet a stale word."""
+        self.d_xchg = self._alloc((MAX_WORLD + 1) * 4 * 4)
+        hvdrv.memset8(self.d_xchg, 0, (MAX_WORLD + 1) * 4 * 4)
+        hvdrv.synchronize()
+        mine = [self.d_h, self.d_ctx, self.d_act, self.d_barrier, self.d_xchg]
+        blob = b"".join(hvdrv.ipc_handle(p) for p in mine)
+        blobs = self._exchange(blob)
+        if len(blobs) != self.world:
+            raise RuntimeError(f"exchange returned {len(blobs)} entries for {self.world} ranks")
+        peers = _StepPeers()
+        n = hvdrv.IPC_HANDLE_BYTES
+        for k, b in enumerate(blobs):
+            for j, name in enumerate(("h", "ctx", "act", "barrier", "xchg")):
+                if k == self.rank:
+                    ptr = mine[j]
+                else:
+                    ptr = hvdrv.ipc_open(bytes(b[j * n:(j + 1) * n]))
+                    self._opened.append(ptr)
+                getattr(peers, name)[k] = ptr
+        self.d_peers = self._alloc(C.sizeof(peers))
+        hvdrv.upload(self.d_peers, C.addressof(peers), C.sizeof(peers))
 
     def _set_i32(self, ptr: int, value: int):
         hvdrv.upload(ptr, np.array([value], np.int32).ctypes.data, 4)
@@ -432,7 +514,7 @@ class Engine:
         hvdrv.synchronize()
         hvdrv.memset8(self.d_barrier, 0, 4)
         hvdrv.memset8(self.d_status, 0, 4)
-        hvdrv.memset8(self.d_ticket, 0, (self.cfg.n_kv + 1) * 4)
+        hvdrv.memset8(self.d_ticket, 0, (self.shard["n_kv"] + 1) * 4)
 
     def _check_status(self):
         st = self.step_status()
@@ -674,6 +756,12 @@ class Engine:
             except Exception:
                 pass
             self._stream = 0
+        for p in getattr(self, "_opened", []):
+            try:
+                hvdrv.ipc_close(p)
+            except Exception:
+                pass
+        self._opened = []
         for p in self._buffers:
             try:
                 hvdrv.free(p)

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define HV_ABI_VERSION 1
+#define HV_ABI_VERSION 2
 
 #define HV_OK 0
 #define HV_E_INVALID 1001      /* bad argument (null pointer, size, alignment) */
@@ -76,6 +76,15 @@ int hv_host_free(void* ptr);
 int hv_upload_async(void* dst, const void* host_src, size_t nbytes, void* stream);
 int hv_download_async(void* host_dst, const void* src, size_t nbytes, void* stream);
 int hv_copy_async(void* dst, const void* src, size_t nbytes, void* stream);
+
+/* Cross-process device memory (CUDA IPC) for the sharded step's peer buffers: a
+ * 64-byte handle of an allocation made by this process, and the mapping of another
+ * process's handle into this one (peer access over NVLink enabled on first use). No
+ * counterpart in the reference (it has no multi-GPU path). */
+#define HV_IPC_HANDLE_BYTES 64
+int hv_ipc_handle(const void* dev_ptr, void* handle_out);
+int hv_ipc_open(const void* handle, void** dev_ptr);
+int hv_ipc_close(void* dev_ptr);
 
 /* ---- streams, graphs, events (engine/cudrv.py:226-266) --------------------------- */
 
@@ -239,7 +248,27 @@ typedef struct hv_step_desc {
   uint64_t* trace;              /* NULL, or [grid][HV_STEP_TRACE_STRIDE(n_layer)]:
                                    %globaltimer (ns) at each phase boundary, per CTA */
   const void* plans;            /* hv_step_plans() output, uploaded to the device  */
+  /* Column-parallel sharding over `world` GPUs (world 1 = one GPU, `peers` unused).
+   * Rank r holds q heads [r nq, (r+1) nq) and kv heads [r nkv, (r+1) nkv) with nq =
+   * n_head and nkv = n_kv (per-rank counts), rows [r hidden/world, ...) of W_o and
+   * W_down, gate/up rows [r ffn, (r+1) ffn) with ffn per rank, and LM-head rows
+   * [r head_rows, ...); every output element is still computed whole on one GPU. The
+   * step writes each produced slice into every rank's copy (NVLink peer stores) and its
+   * grid barrier spans all ranks' CTAs, so the all-gathers are part of the kernel. */
+  int world, rank;
+  const struct hv_step_peers* peers;   /* device pointer (world > 1) */
 } hv_step_desc;
+
+#define HV_MAX_WORLD 8
+/* Every rank's copies of the exchanged buffers (device pointers valid on this rank:
+ * its own allocations and the other ranks' opened with hv_ipc_open). */
+typedef struct hv_step_peers {
+  float* h[HV_MAX_WORLD];          /* residual [hidden]                              */
+  void* ctx[HV_MAX_WORLD];         /* quantised attention output (desc.ctx buffers)  */
+  void* act[HV_MAX_WORLD];         /* quantised SiLU output (desc.act buffers)       */
+  uint32_t* barrier[HV_MAX_WORLD]; /* grid barrier words                             */
+  int32_t* xchg[HV_MAX_WORLD];     /* argmax exchange [HV_MAX_WORLD + 1][4], zeroed once */
+} hv_step_peers;
 
 /* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 26 l:
  * +0 qkv prologue, +1 qkv GEMV, +2 barrier, +3 attention, +4 barrier, +5 o prologue,

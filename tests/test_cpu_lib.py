@@ -72,7 +72,10 @@ def test_step_desc_layout_matches_header():
     assert ctypes.sizeof(limited._LayerW) == 14 * 8
     # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers
     assert limited._StepDesc.layers.offset == 48
-    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8
+    assert limited._StepDesc.world.offset == 48 + 24 * 8
+    assert limited._StepDesc.peers.offset == 48 + 24 * 8 + 8
+    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 16
+    assert ctypes.sizeof(limited._StepPeers) == 5 * 8 * 8
 
 
 def test_gpu_only_paths_fail_loudly_without_gpu():
