@@ -509,7 +509,7 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
   producer_drain(R, P.q, S);
   if (D.trace != nullptr) {
     uint64_t* tr = D.trace + (size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + 2 +
-                   26 * D.n_layer;
+                   28 * D.n_layer;
     tr[3] = P.t_empty;
     tr[4] = P.t_flight;
     tr[5] = P.q;
@@ -540,7 +540,8 @@ __device__ __noinline__ unsigned quant4(float4 x, float4 w, float d, bool norm, 
 // it from registers.
 __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row,
                                             const float* __restrict__ w, int n, float eps,
-                                            StepShared& S, float* sq, uint4* q_s, int2* sb_s) {
+                                            StepShared& S, float* sq, uint4* q_s, int2* sb_s,
+                                            const hv_step_desc& D, int mark) {
   constexpr int kV = kMaxHidden / 4 / kConsThreads;   // float4 per thread
   const int n4 = n / 4;
   const int t = threadIdx.x;
@@ -568,7 +569,9 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
                       __fmul_rn(xv[k].z, xv[k].z), __fmul_rn(xv[k].w, xv[k].w));
   }
   csync();
+  if (mark >= 0) trace_mark(D, mark);
   const float ss = block_pw_sum<CSync>(sq, &S.P.pw_hid, S.leafval, S.red);
+  if (mark >= 0) trace_mark(D, mark + 1);
   const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
   unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
 #pragma unroll
@@ -1217,10 +1220,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   trace_mark(D, 1);
   for (int l = 0; l < D.n_layer; ++l) {
     const hv_layer_w* L = Ls + l;
-    const int tb = 2 + 26 * l;
+    const int tb = 2 + 28 * l;
     // P1: qkv
-    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, L->an, hid, D.eps, S, work, q_s,
-                   sb_s);
+    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, L->an, hid, D.eps, S, work, q_s, sb_s, D,
+                   tb + 26);
     trace_mark(D, tb + 0);
     trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
@@ -1248,7 +1251,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
-    pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s);
+    pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s, D, -1);
     trace_mark(D, tb + 8);
     trace_wait(D, S, tb + 20);
     gu_tiles(ffn, &off, &t0, &t1);
@@ -1291,8 +1294,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   }
 
   if (!(flags & HV_STEP_HEAD)) return;
-  const int th = 2 + 26 * D.n_layer;
-  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s);
+  const int th = 2 + 28 * D.n_layer;
+  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s, D, -1);
   trace_mark(D, th + 0);
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;

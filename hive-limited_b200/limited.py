@@ -449,7 +449,7 @@ class Engine:
         [grid, stride]} where each phase's duration is taken per CTA and summed over the
         layers (median and max over CTAs)."""
         c = self.cfg
-        stride = 8 + 26 * c.n_layer
+        stride = 8 + 28 * c.n_layer
         n = self.step_grid * stride
         buf = hvdrv.alloc(n * 8)
         try:
@@ -468,11 +468,11 @@ class Engine:
         out = {}
         def prev_mark(l, k):      # the mark that ends the phase before (layer l, mark k)
             if k > 0:
-                return 2 + 26 * l + k - 1
-            return 1 if l == 0 else 2 + 26 * (l - 1) + 13
+                return 2 + 28 * l + k - 1
+            return 1 if l == 0 else 2 + 28 * (l - 1) + 13
 
         for k, name in enumerate(self.TRACE_PHASES):
-            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            idx = np.array([2 + 28 * l + k for l in range(c.n_layer)])
             pidx = np.array([prev_mark(l, k) for l in range(c.n_layer)])
             d = t[:, idx] - t[:, pidx]
             out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
@@ -481,18 +481,26 @@ class Engine:
         busy = raw[:, 2 + 14] != 0
         prev = 2
         for k, name in zip(range(14, 20), self.TRACE_ATTN):
-            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            idx = np.array([2 + 28 * l + k for l in range(c.n_layer)])
             d = (t[:, idx] - t[:, idx - k + prev])[busy]
             prev = k
             if d.size:
                 out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
                              "max_us": float(d.max(axis=0).sum() / 1e3)}
         for k, name in zip(range(21, 26), self.TRACE_WAITS):
-            idx = np.array([2 + 26 * l + k for l in range(c.n_layer)])
+            idx = np.array([2 + 28 * l + k for l in range(c.n_layer)])
             d = raw[:, idx].astype(np.int64)
             out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
                          "max_us": float(d.max(axis=0).sum() / 1e3)}
-        th = 2 + 26 * c.n_layer
+        for name, k0, k1 in (("qkv_pro_load", None, 26), ("qkv_pro_sumsq", 26, 27),
+                             ("qkv_pro_quant", 27, 0)):
+            idx1 = np.array([2 + 28 * l + k1 for l in range(c.n_layer)])
+            idx0 = (np.array([prev_mark(l, 0) for l in range(c.n_layer)]) if k0 is None
+                    else np.array([2 + 28 * l + k0 for l in range(c.n_layer)]))
+            d = t[:, idx1] - t[:, idx0]
+            out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
+                         "max_us": float(d.max(axis=0).sum() / 1e3)}
+        th = 2 + 28 * c.n_layer
         for k, name in enumerate(("head_prologue", "head_gemv", "argmax")):
             d = t[:, th + k] - t[:, th + k - 1 if k else prev_mark(c.n_layer, 0)]
             out[name] = {"median_us": float(np.median(d) / 1e3), "max_us": float(d.max() / 1e3)}

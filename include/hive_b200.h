@@ -237,8 +237,11 @@ typedef struct hv_step_desc {
   int32_t* gen;                 /* generated tokens [cap + 1]                      */
   float* h;                     /* residual [hidden]                               */
   float* qkv;                   /* [(n_head + 2 n_kv) hd]                          */
-  float* ctx;                   /* [n_head hd]                                     */
-  float* act;                   /* SiLU output [ffn]                               */
+  float* ctx;                   /* room for [n_head hd] floats (whole, all ranks); the
+                                   step keeps the attention output there quantised:
+                                   int8 [n_head hd] then (scale, sum) per 32 values  */
+  float* act;                   /* room for [ffn] floats (whole); holds the SiLU output
+                                   quantised the same way                           */
   float* logits;                /* [head_rows]                                     */
   float* part;                  /* attention partials (hv_step_config)             */
   int32_t* ticket;              /* [n_kv + 1] zeroed once                          */
@@ -270,7 +273,7 @@ typedef struct hv_step_peers {
   int32_t* xchg[HV_MAX_WORLD];     /* argmax exchange [HV_MAX_WORLD + 1][4], zeroed once */
 } hv_step_peers;
 
-/* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 26 l:
+/* Trace layout: entry 0 = kernel start, 1 = set-up done; layer l at 2 + 28 l:
  * +0 qkv prologue, +1 qkv GEMV, +2 barrier, +3 attention, +4 barrier, +5 o prologue,
  * +6 o GEMV, +7 barrier, +8 gate/up prologue, +9 gate/up GEMV, +10 barrier,
  * +11 down prologue, +12 down GEMV, +13 barrier; inside the attention (last work item
@@ -278,11 +281,12 @@ typedef struct hv_step_peers {
  * partials, +18 ticket, +19 merge (all %globaltimer ns). Durations (ns) that consumer
  * warp 0 spent waiting for its shared-memory ring slots: +21 attention scores, +22
  * attention V sum, +23 qkv GEMV, +24 gate/up GEMV (+20 is scratch); +25 = SM cycles
- * warp 0 spent computing attention scores. Then
- * the head prologue, head GEMV and argmax at 2 + 26 n_layer + {0, 1, 2}; then, for the
+ * warp 0 spent computing attention scores; +26 / +27: inside the qkv prologue, vector
+ * loaded and squared / sum of squares done. Then
+ * the head prologue, head GEMV and argmax at 2 + 28 n_layer + {0, 1, 2}; then, for the
  * producer warp: ns blocked on a ring slot still in use (+3), ns blocked on the copies in
  * flight (+4), slots copied (+5). */
-#define HV_STEP_TRACE_STRIDE(n_layer) (8 + 26 * (n_layer))
+#define HV_STEP_TRACE_STRIDE(n_layer) (8 + 28 * (n_layer))
 
 #define HV_STEP_HEAD 1     /* compute the LM head into logits                          */
 #define HV_STEP_ARGMAX 2   /* then greedy argmax: tok = argmax, gen[step] = tok,
