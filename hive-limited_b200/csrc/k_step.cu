@@ -534,20 +534,22 @@ __device__ __noinline__ unsigned quant4(float4 x, float4 w, float d, bool norm, 
   return q;
 }
 
-// act <- quant(rmsnorm(src, w)) over n = hidden values (n % 32 == 0, n <= kMaxHidden);
-// src from global (through L2) or, for layer 0, the f16 embedding row. Thread t holds
-// float4 i4 = t + 256 k, so the 8 lanes of a lane group hold one 32-block and quantise
-// it from registers.
+// act <- quant(rmsnorm(src, w)) over n = hidden values (n % 32 == 0,
+// n <= KV * 4 * kConsThreads); src from global (through L2) or, for layer 0, the f16
+// embedding row. Thread t holds float4 i4 = t + 256 k, so the 8 lanes of a lane group
+// hold one 32-block and quantise it from registers. KV (float4 per thread) is a template
+// argument so the normalise/quantise chains of a thread's blocks are inline and
+// interleave, with code for exactly the blocks a hidden size needs.
+template <int KV>
 __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_row,
                                             const float* __restrict__ w, int n, float eps,
                                             StepShared& S, float* sq, uint4* q_s, int2* sb_s,
                                             const hv_step_desc& D, int mark) {
-  constexpr int kV = kMaxHidden / 4 / kConsThreads;   // float4 per thread
   const int n4 = n / 4;
   const int t = threadIdx.x;
-  float4 xv[kV], wv[kV];
+  float4 xv[KV], wv[KV];
 #pragma unroll
-  for (int k = 0; k < kV; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int i4 = t + k * kConsThreads;
     if (i4 < n4) {
       if (src) {
@@ -558,10 +560,12 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
         xv[k] = make_float4(a.x, a.y, b.x, b.y);
       }
       wv[k] = __ldg(reinterpret_cast<const float4*>(w) + i4);
+    } else {
+      xv[k] = wv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 #pragma unroll
-  for (int k = 0; k < kV; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int i4 = t + k * kConsThreads;
     if (i4 < n4)
       reinterpret_cast<float4*>(sq)[i4] =
@@ -573,39 +577,34 @@ __device__ __noinline__ void pro_norm_quant(const float* src, const __half* emb_
   const float ss = block_pw_sum<CSync>(sq, &S.P.pw_hid, S.leafval, S.red);
   if (mark >= 0) trace_mark(D, mark + 1);
   const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+#pragma unroll
+  for (int k = 0; k < KV; ++k)
+    xv[k] = make_float4(
+        __fmul_rn(wv[k].x, __fdiv_rn(xv[k].x, d)), __fmul_rn(wv[k].y, __fdiv_rn(xv[k].y, d)),
+        __fmul_rn(wv[k].z, __fdiv_rn(xv[k].z, d)), __fmul_rn(wv[k].w, __fdiv_rn(xv[k].w, d)));
   unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
 #pragma unroll
-  for (int k = 0; k < kV; ++k) {
+  for (int k = 0; k < KV; ++k) {
     const int i4 = t + k * kConsThreads;
-    if (i4 < n4)                        // uniform over each 8-lane group (n4 % 8 == 0)
-      q32[i4] = quant4(xv[k], wv[k], d, true, i4 >> 3, (i4 & 7) == 0, sb_s);
+    if (i4 < n4) {                      // uniform over each 8-lane group (n4 % 8 == 0)
+      float sc;
+      int bs;
+      q32[i4] = quant_block_8lanes(xv[k], &sc, &bs);
+      if ((i4 & 7) == 0) sb_s[i4 >> 3] = make_int2(__float_as_int(sc), bs);
+    }
   }
   csync();
 }
 
-// act <- quant(src) over n values produced by other CTAs (n % 32 == 0); 8 lanes per
-// 32-block, the loads of up to 8 passes in flight together.
-__device__ __noinline__ void pro_quant(const float* src, int n, uint4* q_s, int2* sb_s) {
-  constexpr int kBatch = 8;
-  const int lane = threadIdx.x & 31, sub = lane & 7;
-  unsigned* q32 = reinterpret_cast<unsigned*>(q_s);
-  const int nb = n / kBlock;
-  const int step = kConsWarps * 4;
-  for (int base = (threadIdx.x >> 5) * 4; base < nb; base += step * kBatch) {
-    float4 v[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int b = base + k * step + (lane >> 3);
-      v[k] = (b < nb) ? __ldcg(reinterpret_cast<const float4*>(src) + b * 8 + sub)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int b = base + k * step + (lane >> 3);
-      if (b < nb) q32[b * 8 + sub] = quant4(v[k], v[k], 1.0f, false, b, sub == 0, sb_s);
-    }
-  }
-  csync();
+// The hidden-size dispatch of pro_norm_quant (n <= kMaxHidden).
+HV_DEV void norm_quant(const float* src, const __half* emb_row, const float* w, int n,
+                       float eps, StepShared& S, float* sq, uint4* q_s, int2* sb_s,
+                       const hv_step_desc& D, int mark) {
+  const int kv = (n / 4 + kConsThreads - 1) / kConsThreads;
+  if (kv <= 2) pro_norm_quant<2>(src, emb_row, w, n, eps, S, sq, q_s, sb_s, D, mark);
+  else if (kv <= 4) pro_norm_quant<4>(src, emb_row, w, n, eps, S, sq, q_s, sb_s, D, mark);
+  else if (kv <= 5) pro_norm_quant<5>(src, emb_row, w, n, eps, S, sq, q_s, sb_s, D, mark);
+  else pro_norm_quant<kMaxHidden / 4 / kConsThreads>(src, emb_row, w, n, eps, S, sq, q_s, sb_s, D, mark);
 }
 
 // act <- a vector other CTAs already quantised: int8 [n] at q, then (scale, sum) pairs
@@ -1222,7 +1221,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     const hv_layer_w* L = Ls + l;
     const int tb = 2 + 28 * l;
     // P1: qkv
-    pro_norm_quant(l == 0 ? nullptr : D.h, emb_row, L->an, hid, D.eps, S, work, q_s, sb_s, D,
+    norm_quant(l == 0 ? nullptr : D.h, emb_row, L->an, hid, D.eps, S, work, q_s, sb_s, D,
                    tb + 26);
     trace_mark(D, tb + 0);
     trace_wait(D, S, tb + 20);
@@ -1251,7 +1250,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 7);
     // P4: gate/up + SiLU
-    pro_norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s, D, -1);
+    norm_quant(D.h, nullptr, L->fn, hid, D.eps, S, work, q_s, sb_s, D, -1);
     trace_mark(D, tb + 8);
     trace_wait(D, S, tb + 20);
     gu_tiles(ffn, &off, &t0, &t1);
@@ -1295,7 +1294,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
 
   if (!(flags & HV_STEP_HEAD)) return;
   const int th = 2 + 28 * D.n_layer;
-  pro_norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s, D, -1);
+  norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s, D, -1);
   trace_mark(D, th + 0);
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;
