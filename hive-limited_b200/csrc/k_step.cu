@@ -739,21 +739,62 @@ HV_DEV void gemv_epilogue(float y, int row, bool ok, const OutCtx& O, float* bes
   }
 }
 
+// Explicit shared-memory loads from 32-bit shared addresses. The phase functions are out
+// of line and receive generic pointers, through which the compiler would emit generic
+// loads (about twice the cost in the GEMV loop); these keep the hot loops on ld.shared.
+HV_DEV unsigned sh_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+HV_DEV uint4 lds_u4(unsigned a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+HV_DEV uint2 lds_u2(unsigned a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+HV_DEV float4 lds_f4(unsigned a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+HV_DEV float2 lds_f2(unsigned a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+HV_DEV float lds_f1(unsigned a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+
 // Block terms of iteration u of a ring slot for the lane's row g: blocks 2t (x) and
-// 2t+1 (y) of logical iteration `it`; nvalid < 8 only for the tail iteration.
-HV_DEV float2 slot_terms(const unsigned char* sl, int u, const unsigned* __restrict__ act_w,
-                         const int2* __restrict__ sb, int it, int g, int t, int lane,
-                         int nvalid) {
-  const uint32_t* nw = reinterpret_cast<const uint32_t*>(sl);
-  const float* sw = reinterpret_cast<const float*>(sl + kSlotScaleOff);
+// 2t+1 (y) of logical iteration `it` (the arithmetic of iter_terms in gemv_mma.cuh).
+// sl, act_w and sb are shared addresses of the slot, the int8 activation words and the
+// (scale, sum) pairs.
+HV_DEV float2 slot_terms_sh(unsigned sl, int u, unsigned act_w, unsigned sb, int it, int g,
+                            int t, int lane, int nvalid) {
   MmaLoads L;
-  const uint4 a = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 4 * lane);
-  const uint4 b = *reinterpret_cast<const uint4*>(nw + u * kPpNibWords + 128 + 4 * lane);
+  const uint4 a = lds_u4(sl + u * kPpNibWords * 4 + 16 * lane);
+  const uint4 b = lds_u4(sl + u * kPpNibWords * 4 + 512 + 16 * lane);
   L.w[0] = a.x; L.w[1] = a.y; L.w[2] = a.z; L.w[3] = a.w;
   L.w[4] = b.x; L.w[5] = b.y; L.w[6] = b.z; L.w[7] = b.w;
-  L.s = *reinterpret_cast<const float2*>(sw + u * kPpScales + 2 * lane);
-  return iter_terms(L, act_w, sb, it, g, t, nvalid);
+  L.s = lds_f2(sl + kSlotScaleOff + u * kPpScales * 4 + 8 * lane);
+  const uint2 bw = (g < nvalid) ? lds_u2(act_w + ((it * 8 + g) * 4 + t) * 8) : make_uint2(0u, 0u);
+  int e, o;
+  mma_iter(L.w, bw, t, nvalid, e, o);
+  const uint4 sbp = lds_u4(sb + (it * 8 + 2 * t) * 8);   // blocks 2t and 2t+1: (s, sum) x 2
+  float ce = 0.f, co = 0.f;
+  if (2 * t < nvalid)
+    ce = __fmul_rn(__fmul_rn(L.s.x, __int_as_float((int)sbp.x)), i2f_exact(e - 8 * (int)sbp.y));
+  if (2 * t + 1 < nvalid)
+    co = __fmul_rn(__fmul_rn(L.s.y, __int_as_float((int)sbp.z)), i2f_exact(o - 8 * (int)sbp.w));
+  return make_float2(ce, co);
 }
+
 
 // The CTA's tiles [t0, t1) of one GEMV phase, their slots starting at sequence number q0.
 // Work items are (tile, leaf of numpy's pairwise recursion), tile-major like the ring;
@@ -780,7 +821,7 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
   const int spt = slots_per_tile(niter);
   const int nleaf = P.nleaf, nfull = P.nfull, ntail = P.ntail;
   const int nitems = (t1 - t0) * nleaf;
-  const unsigned* act_w = reinterpret_cast<const unsigned*>(act.q);
+  const unsigned act_w = sh_addr(act.q), sbs = sh_addr(act.sb);
   bool failed = false;
   for (int k = warp; k < nitems && !failed; k += kConsWarps) {
     const int lt = k / nleaf, lf = k - lt * nleaf;
@@ -799,23 +840,23 @@ __device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan&
         failed = true;
         break;
       }
-      const unsigned char* sl = R.slot(q);
+      const unsigned sl = sh_addr(R.slot(q));
       const int a = max(ia, s0), bb = min(ib, s1), bf = min(bb, ifull);
       if (a == s0 && bf == s0 + kSlotIters) {       // the whole slot: fixed trip count
 #pragma unroll
         for (int u = 0; u < kSlotIters; ++u) {
-          const float2 v = slot_terms(sl, u, act_w, act.sb, s0 + u, g, t, lane, 8);
+          const float2 v = slot_terms_sh(sl, u, act_w, sbs, s0 + u, g, t, lane, 8);
           ae = __fadd_rn(ae, v.x);
           ao = __fadd_rn(ao, v.y);
         }
       } else {
         for (int it = a; it < bf; ++it) {
-          const float2 v = slot_terms(sl, it - s0, act_w, act.sb, it, g, t, lane, 8);
+          const float2 v = slot_terms_sh(sl, it - s0, act_w, sbs, it, g, t, lane, 8);
           ae = __fadd_rn(ae, v.x);
           ao = __fadd_rn(ao, v.y);
         }
       }
-      if (bb > bf) tail = slot_terms(sl, bf - s0, act_w, act.sb, bf, g, t, lane, ntail);
+      if (bb > bf) tail = slot_terms_sh(sl, bf - s0, act_w, sbs, bf, g, t, lane, ntail);
       __syncwarp();
       const bool shared = ia > s0 || ib < s1;
       if (lane == 0) mbar_arrive_n(R.empty_of(q), shared ? kConsWarps / 2 : kConsWarps);
@@ -892,16 +933,16 @@ constexpr int kScoreRows = GS >= 8 ? 4 : 8;
 // the slot, so no branch precedes it), the pos row loaded once if this group holds it,
 // rows from `tend` on (not this block's) and stale slot rows selected to zero.
 template <int RW>
-HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, const float* slot,
-                       int r0, const float* pos_s, int lane) {
+HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, unsigned slot,
+                       int r0, unsigned pos_s, int lane) {
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int p = 0; p < RW; ++p) {
     const int r = min(tb + p - r0, kSlotRows - 1);
-    kv[p] = slot ? reinterpret_cast<const float4*>(slot + (size_t)r * kHd)[lane] : zero;
+    kv[p] = slot ? lds_f4(slot + (unsigned)(r * kHd + 4 * lane) * 4) : zero;
   }
   const bool has_pos = pos >= tb && pos < tb + RW && pos < tend && pos >= te;
-  const float4 pv = has_pos ? reinterpret_cast<const float4*>(pos_s)[lane] : zero;
+  const float4 pv = has_pos ? lds_f4(pos_s + 16 * lane) : zero;
 #pragma unroll
   for (int p = 0; p < RW; ++p) {
     const int t = tb + p;
@@ -910,11 +951,11 @@ HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, cons
 }
 
 // Scores of positions tb .. tb + kScoreRows - 1 (those below tend) for the GS heads, the
-// arithmetic of attn_chunk in attn_decode.cuh.
+// arithmetic of attn_chunk in attn_decode.cuh. slot (0: none), kpos_s and lg_s are shared
+// addresses.
 template <int GS>
 HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int te, int pos,
-                         const float* slot, int r0, const float* kpos_s, float scale,
-                         float* lg_s) {
+                         unsigned slot, int r0, unsigned kpos_s, float scale, unsigned lg_s) {
   constexpr int RW = kScoreRows<GS>;
   const int lane = threadIdx.x & 31;
   float4 kv[RW];
@@ -936,7 +977,11 @@ HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int t
   if ((lane & (dup - 1)) == 0) {
     const int p = idx / GS, i = idx % GS;
     const int t = tb + p;
-    if (t < tend) lg_s[(t - t0) * GS + i] = tot * scale;
+    if (t < tend) {
+      const float val = tot * scale;
+      asm volatile("st.shared.f32 [%0], %1;" :: "r"(lg_s + (unsigned)((t - t0) * GS + i) * 4),
+                   "f"(val) : "memory");
+    }
   }
 }
 
@@ -944,7 +989,7 @@ HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int t
 // (the order of attn_chunk); all loads are issued before the first multiply-add.
 template <int GS>
 HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, int pos,
-                         const float* slot, int r0, const float* vpos_s, const float* lg_s) {
+                         unsigned slot, int r0, unsigned vpos_s, unsigned lg_s) {
   constexpr int RW = 8;
   const int lane = threadIdx.x & 31;
   float4 vv[RW];
@@ -953,7 +998,8 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, in
 #pragma unroll
   for (int p = 0; p < RW; ++p)
 #pragma unroll
-    for (int i = 0; i < GS; ++i) w[p][i] = (tb + p < tend) ? lg_s[(tb + p - t0) * GS + i] : 0.f;
+    for (int i = 0; i < GS; ++i)
+      w[p][i] = (tb + p < tend) ? lds_f1(lg_s + (unsigned)((tb + p - t0) * GS + i) * 4) : 0.f;
 #pragma unroll
   for (int p = 0; p < RW; ++p) {
     if (tb + p < tend) {
@@ -1031,16 +1077,17 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     const int nblk = (n + kSlotRows - 1) / kSlotRows;
     for (int m = warp; m < nblk && ok; m += kConsWarps) {
       const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
-      const float* slot = nullptr;
+      unsigned slot = 0;
       if (m < nk) {
         const unsigned q = qk + (unsigned)m;
         ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
         if (!ok) break;
-        slot = reinterpret_cast<const float*>(R.slot(q));
+        slot = sh_addr(R.slot(q));
       }
       const long long c0 = clock64();
       for (int tg = r0; tg < r1; tg += kScoreRows<GS>)
-        group_scores<GS>(qv, tg, r1, t0, te, pos, slot, r0, kpos_s, scale, lg_s);
+        group_scores<GS>(qv, tg, r1, t0, te, pos, slot, r0, sh_addr(kpos_s), scale,
+                         sh_addr(lg_s));
       if (lane == 0) S.busy[warp] += clock64() - c0;
       if (m < nk) {
         __syncwarp();
@@ -1082,15 +1129,15 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int m = warp; m < nblk && ok; m += kConsWarps) {
       const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
-      const float* slot = nullptr;
+      unsigned slot = 0;
       if (m < nk) {
         const unsigned q = qv0 + (unsigned)m;
         ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
         if (!ok) break;
-        slot = reinterpret_cast<const float*>(R.slot(q));
+        slot = sh_addr(R.slot(q));
       }
       for (int tg = r0; tg < r1; tg += 8)
-        group_values<GS>(acc, tg, r1, t0, te, pos, slot, r0, vpos_s, lg_s);
+        group_values<GS>(acc, tg, r1, t0, te, pos, slot, r0, sh_addr(vpos_s), sh_addr(lg_s));
       if (m < nk) {
         __syncwarp();
         if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)m), kConsWarps);
