@@ -87,6 +87,8 @@ struct StepShared {
   int ok;
   int abort;                     // set by any warp of this CTA whose wait gave up
   unsigned phase;                // top bit of the grid barrier counter to wait for next
+  unsigned xphase;               // sharded: top bit of the cross-rank counter (CTA 0)
+  unsigned gen;                  // sharded: generation of the local release word
   unsigned long long wait[kConsWarps];   // ns each consumer warp waited for ring slots
   long long busy[kConsWarps];            // cycles spent computing attention scores
 };
@@ -247,46 +249,71 @@ HV_DEV unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
-// Grid-wide barrier of the consumer threads (of every rank's grid when the step is
-// sharded) over a self-resetting counter: the first CTA of rank 0 adds
-// 2^31 - (world * grid - 1), every other CTA adds 1, so the top bit flips exactly when all
-// have arrived and the low bits return to zero. Each rank keeps its own counter and every
-// arrival goes to all of them (NVLink atomics), so a CTA polls only local memory. Each
-// CTA knows which top bit to wait for (S.phase, read once per launch and flipped at every
-// barrier), so arriving is a fire-and-forget release add and waiting is one acquire load
-// per poll. The wait is bounded: after kWaitNs (or once this rank reported a failure, or
-// this CTA aborted) it records the failure and returns false in every consumer thread.
+// Bounded poll of a barrier word until (value & mask) == want; false (HV_E_TIMEOUT, or
+// another failure already reported on this rank) when it gives up.
+template <bool kSys>
+HV_DEV bool poll_word(const unsigned* w, unsigned mask, unsigned want, int* status) {
+  const unsigned long long t0 = global_ns();
+  for (unsigned n = 1;; ++n) {
+    const unsigned v = kSys ? ld_acquire_sys(w) : ld_acquire(w);
+    if ((v & mask) == want) return true;
+    if ((n & 31) == 0) {
+      if (*(volatile int*)status != 0) return false;
+      if (global_ns() - t0 > kWaitNs) {
+        atomicCAS(status, 0, HV_E_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Grid-wide barrier of the consumer threads over self-resetting counters: the first
+// arrival adds 2^31 - (n - 1), the n - 1 others add 1, so the top bit flips exactly when
+// all n have arrived and the low bits return to zero. Each CTA knows which top bit to
+// wait for (read once per launch, flipped at every barrier), so arriving is a
+// fire-and-forget release add and waiting is one acquire load per poll.
+// Sharded step (world > 1), two levels: the rank's CTAs meet on its local counter
+// (barrier[0]); the rank's CTA 0 then meets the other ranks' CTA 0 on the cross-rank
+// counter (barrier[1] of every rank, NVLink atomics: `world` per barrier, not one per
+// CTA), and releases its CTAs by advancing the generation word barrier[2]. Every CTA
+// fences its peer stores at system scope before it arrives. Waits are bounded (kWaitNs,
+// or until a failure is reported on this rank, or this CTA aborted): the failure is
+// recorded and every consumer thread gets false.
 HV_DEV bool grid_sync(const hv_step_desc& D, StepShared& S) {
   csync();
   if (threadIdx.x == 0) {
     int ok = *(volatile int*)&S.abort == 0;
     if (ok) {
-      const bool sharded = D.world > 1;
-      const unsigned total = gridDim.x * (sharded ? (unsigned)D.world : 1u);
-      const bool first = blockIdx.x == 0 && (!sharded || D.rank == 0);
-      const unsigned add = first ? (0x80000000u - (total - 1)) : 1u;
+      const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
       const unsigned want = S.phase ^ 0x80000000u;
-      if (sharded) {
-        __threadfence_system();     // this CTA's peer stores before its arrival
-        for (int k = 0; k < D.world; ++k)
-          asm volatile("red.release.sys.global.add.u32 [%0], %1;"
-                       :: "l"(D.peers->barrier[k]), "r"(add) : "memory");
-      } else {
+      if (D.world <= 1) {
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(D.barrier), "r"(add)
                      : "memory");
-      }
-      const unsigned long long t0 = global_ns();
-      for (unsigned n = 1;; ++n) {
-        const unsigned v = sharded ? ld_acquire_sys(D.barrier) : ld_acquire(D.barrier);
-        if ((v & 0x80000000u) == want) break;
-        if ((n & 31) == 0) {
-          if (*(volatile int*)D.status != 0) { ok = 0; break; }
-          if (global_ns() - t0 > kWaitNs) {
-            atomicCAS(D.status, 0, HV_E_TIMEOUT);
-            ok = 0;
-            break;
+        ok = poll_word<false>(D.barrier, 0x80000000u, want, D.status);
+      } else {
+        __threadfence_system();     // this CTA's peer stores before its arrival
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(D.barrier), "r"(add)
+                     : "memory");
+        const unsigned gen = S.gen + 1;
+        if (blockIdx.x == 0) {
+          ok = poll_word<false>(D.barrier, 0x80000000u, want, D.status);
+          if (ok) {
+            const unsigned xadd = D.rank == 0 ? 0x80000000u - (D.world - 1) : 1u;
+            const unsigned xwant = S.xphase ^ 0x80000000u;
+            __threadfence_system();
+            for (int k = 0; k < D.world; ++k)
+              asm volatile("red.release.sys.global.add.u32 [%0], %1;"
+                           :: "l"(D.peers->barrier[k] + 1), "r"(xadd) : "memory");
+            ok = poll_word<true>(D.barrier + 1, 0x80000000u, xwant, D.status);
+            S.xphase = xwant;
+            if (ok)
+              asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(D.barrier + 2), "r"(gen)
+                           : "memory");
           }
+        } else {
+          ok = poll_word<false>(D.barrier + 2, 0xFFFFFFFFu, gen, D.status);
         }
+        S.gen = gen;
       }
       S.phase = want;
     }
@@ -810,7 +837,7 @@ HV_DEV float2 slot_terms_sh(unsigned sl, int u, unsigned act_w, unsigned sb, int
 // rows per half; SiLU(gate) * up is formed in the lane that holds the gate row and stored
 // at out[p - 4 t0] for pair p (a shared-memory staging buffer).
 template <int MODE>
-__device__ __noinline__ void gemv_ring(const Ring& R, unsigned q0, const GvPlan& P,
+__device__ __noinline__ void gemv_ring(const Ring R, unsigned q0, const GvPlan& P,
                                        const ActView act, int t0, int t1, int rows,
                                        int pair_ffn, const OutCtx O, float* best_v,
                                        int* best_i, float* leafbuf, StepShared& S,
@@ -1020,7 +1047,7 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, in
 // for the scores and the weighted V sum; warp i takes head i for the max and exp.
 template <int GS>
 __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
-                                       const Ring& R, unsigned* qp, StepShared& S,
+                                       const Ring R, unsigned* qp, StepShared& S,
                                        float* area, int tb) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
   const int chunk_max = (cap + nch - 1) / nch;
@@ -1220,6 +1247,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     // no barrier of this launch can complete before this CTA arrives, so the counter's
     // top bit is still the one the previous launch left
     S.phase = ld_acquire(D.barrier) & 0x80000000u;
+    // sharded: neither word can move before this CTA has arrived (the cross-rank counter
+    // flips only when this rank's CTA 0 arrives, which waits for this CTA)
+    S.xphase = D.world > 1 ? ld_acquire_sys(D.barrier + 1) & 0x80000000u : 0u;
+    S.gen = D.world > 1 ? ld_acquire(D.barrier + 2) : 0u;
     for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0, S.busy[w] = 0;
   }
   {

@@ -325,9 +325,9 @@ class Engine:
         hvdrv.memset8(self.d_ticket, 0, (sh["n_kv"] + 1) * 4)
         self.d_amax_v = self._alloc(grid.value * 4)
         self.d_amax_i = self._alloc(grid.value * 4)
-        self.d_barrier = self._alloc(4)
+        self.d_barrier = self._alloc(16)
         self.d_status = self._alloc(4)
-        hvdrv.memset8(self.d_barrier, 0, 4)
+        hvdrv.memset8(self.d_barrier, 0, 16)
         hvdrv.memset8(self.d_status, 0, 4)
         nbytes = C.c_size_t()
         hvdrv._call("hv_step_plans_bytes", C.byref(nbytes))
@@ -520,7 +520,7 @@ class Engine:
     def reset_step_state(self):
         """Clear the fused step's barrier/ticket/status words after a failed launch."""
         hvdrv.synchronize()
-        hvdrv.memset8(self.d_barrier, 0, 4)
+        hvdrv.memset8(self.d_barrier, 0, 16)
         hvdrv.memset8(self.d_status, 0, 4)
         hvdrv.memset8(self.d_ticket, 0, (self.shard["n_kv"] + 1) * 4)
 

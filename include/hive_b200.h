@@ -246,7 +246,7 @@ typedef struct hv_step_desc {
   float* part;                  /* attention partials (hv_step_config)             */
   int32_t* ticket;              /* [n_kv + 1] zeroed once                          */
   float* amax_v; int32_t* amax_i;                  /* [grid] argmax partials       */
-  uint32_t* barrier;            /* one word, zeroed once                           */
+  uint32_t* barrier;            /* four words, zeroed once                         */
   int32_t* status;              /* 0 = ok; nonzero after a bounded wait ran out    */
   uint64_t* trace;              /* NULL, or [grid][HV_STEP_TRACE_STRIDE(n_layer)]:
                                    %globaltimer (ns) at each phase boundary, per CTA */
@@ -269,7 +269,7 @@ typedef struct hv_step_peers {
   float* h[HV_MAX_WORLD];          /* residual [hidden]                              */
   void* ctx[HV_MAX_WORLD];         /* quantised attention output (desc.ctx buffers)  */
   void* act[HV_MAX_WORLD];         /* quantised SiLU output (desc.act buffers)       */
-  uint32_t* barrier[HV_MAX_WORLD]; /* grid barrier words                             */
+  uint32_t* barrier[HV_MAX_WORLD]; /* every rank's desc.barrier (four words)         */
   int32_t* xchg[HV_MAX_WORLD];     /* argmax exchange [HV_MAX_WORLD + 1][4], zeroed once */
 } hv_step_peers;
 
