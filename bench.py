@@ -342,6 +342,21 @@ def run_ours(args, dist: Dist):
     achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
     traffic = None if sharded else profiled_traffic("k_step_qwen3-8b_decode.md")
 
+    if args.profile and dist.rank == 0:
+        # one extra step with the per-phase device trace, at the next decode position
+        # (after the timed region, so it perturbs nothing that is measured)
+        if done[0] and done[0] % window == 0:      # at the cache's end: rewind first
+            hvdrv.upload_async(eng.d_pos, pin, 4)
+            hvdrv.upload_async(eng.d_step, pin + 4, 4)
+        prof = eng.profile_step()
+        print(f"per-phase trace of one step at position {n_prompt + done[0] % window} "
+              f"(us, summed over {cfg.n_layer} layers; median and max over CTAs):",
+              file=sys.stderr)
+        for name, v in prof["phases"].items():
+            print(f"  {name:26s} {v['median_us']:10.1f} {v['max_us']:10.1f}", file=sys.stderr)
+        print(f"  total {prof['total_us']:.1f} us", file=sys.stderr, flush=True)
+        eng._check_status()
+
     # end to end through the public API: Engine.stream with host-fed tokens
     n_e2e = min(args.e2e_steps, window)
     ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True))
@@ -400,6 +415,8 @@ def main(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="also print the fused step's per-phase device trace (stderr)")
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
