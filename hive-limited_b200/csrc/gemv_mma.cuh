@@ -250,90 +250,6 @@ HV_DEV void gemv_tile8(const uint32_t* __restrict__ r, const float* __restrict__
   }
 }
 
-// ---- split form: terms to shared memory, chains walked afterwards ------------------
-
-// The block terms c of one iteration for the lane's row: blocks 2t (x) and 2t+1 (y).
-// nvalid < 8 only for the tail iteration; missing blocks give 0.
-HV_DEV float2 iter_terms(const MmaLoads& L, const unsigned* __restrict__ act_w,
-                         const int2* __restrict__ sb, int it, int g, int t, int nvalid) {
-  const uint2 bw = (g < nvalid) ? reinterpret_cast<const uint2*>(act_w)[(it * 8 + g) * 4 + t]
-                                : make_uint2(0u, 0u);
-  int e, o;
-  mma_iter(L.w, bw, t, nvalid, e, o);
-  float ce = 0.f, co = 0.f;
-  if (2 * t < nvalid) {
-    const int2 s = sb[it * 8 + 2 * t];
-    ce = __fmul_rn(__fmul_rn(L.s.x, __int_as_float(s.x)), i2f_exact(e - 8 * s.y));
-  }
-  if (2 * t + 1 < nvalid) {
-    const int2 s = sb[it * 8 + 2 * t + 1];
-    co = __fmul_rn(__fmul_rn(L.s.y, __int_as_float(s.x)), i2f_exact(o - 8 * s.y));
-  }
-  return make_float2(ce, co);
-}
-
-// Terms of iterations [it_a, it_b) of one prepacked tile into cout[it * 32 + lane]
-// (float2: blocks 2t, 2t+1 of row g). Iteration P.nfull is the tail group.
-template <int U>
-HV_DEV void tile_terms_pp(const uint32_t* __restrict__ tn, const float* __restrict__ ts,
-                          const unsigned* __restrict__ act_w, const int2* __restrict__ sb,
-                          const GvPlan& P, int it_a, int it_b, float2* cout) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  MmaLoads L[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u)
-    if (it_a + u < it_b) mma_load_pp(L[u], tn, ts, it_a + u, lane);
-  for (int it0 = it_a; it0 < it_b; it0 += U) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + u;
-      if (it < it_b) {
-        const int nvalid = (it < P.nfull) ? 8 : P.ntail;
-        cout[it * 32 + lane] = iter_terms(L[u], act_w, sb, it, g, t, nvalid);
-        if (it + U < it_b) mma_load_pp(L[u], tn, ts, it + U, lane);
-      }
-    }
-  }
-}
-
-// Walks numpy's pairwise chains over terms cin[it * 32 + lane] (leaves, their 8
-// accumulators, the tail in order, the recursion's '+'): y of the lane's row in all
-// four lanes of its quad.
-HV_DEV float chains_fold(const GvPlan& P, const float2* cin) {
-  const int lane = threadIdx.x & 31;
-  float st[8];
-  int sp = 0, leaf = 0, leaf_begin = 0;
-  float ae = 0.f, ao = 0.f;
-  for (int it = 0; it < P.nfull; ++it) {
-    const float2 c = cin[it * 32 + lane];
-    if (it == leaf_begin) { ae = c.x; ao = c.y; }
-    else { ae = __fadd_rn(ae, c.x); ao = __fadd_rn(ao, c.y); }
-    if (it + 1 == P.it_end[leaf] && leaf + 1 < P.nleaf) {
-      st[sp++] = quad_fold(ae, ao);
-      for (int k = 0; k < P.pops[leaf]; ++k) {
-        --sp;
-        st[sp - 1] = __fadd_rn(st[sp - 1], st[sp]);
-      }
-      leaf_begin = P.it_end[leaf];
-      ++leaf;
-    }
-  }
-  float v = (P.nfull > leaf_begin) ? quad_fold(ae, ao) : 0.f;
-  if (P.ntail > 0) {
-    const float2 c = cin[P.nfull * 32 + lane];
-    for (int j = 0; j < P.ntail; ++j) {
-      const float x = __shfl_sync(0xFFFFFFFFu, (j & 1) ? c.y : c.x, (lane & ~3) | (j >> 1));
-      v = __fadd_rn(v, x);
-    }
-  }
-  st[sp++] = v;
-  for (int k = 0; k < P.pops[P.nleaf - 1]; ++k) {
-    --sp;
-    st[sp - 1] = __fadd_rn(st[sp - 1], st[sp]);
-  }
-  return __fadd_rn(0.0f, st[0]);
-}
-
 // Folds a row's leaf values leafv[0 .. nleaf) with the plan's postfix '+'.
 HV_DEV float fold_leaves(const GvPlan& P, const float* leafv) {
   float st[8];

@@ -799,7 +799,7 @@ HV_DEV float lds_f1(unsigned a) {
 }
 
 // Block terms of iteration u of a ring slot for the lane's row g: blocks 2t (x) and
-// 2t+1 (y) of logical iteration `it` (the arithmetic of iter_terms in gemv_mma.cuh).
+// 2t+1 (y) of logical iteration `it` (the combine of gemv_tile8 in gemv_mma.cuh).
 // sl, act_w and sb are shared addresses of the slot, the int8 activation words and the
 // (scale, sum) pairs.
 HV_DEV float2 slot_terms_sh(unsigned sl, int u, unsigned act_w, unsigned sb, int it, int g,

@@ -34,3 +34,12 @@ def test_indivisible_shapes_are_refused():
         limited.shard_plan(cfg, 2, 2)                 # rank outside the world
     with pytest.raises(ValueError):
         limited.shard_plan(cfg, 16, 0)                # more ranks than the step supports
+
+
+def test_sharded_engine_arguments_are_checked_before_any_device_work():
+    cfg = Config(synth.tiny_arch())
+    with pytest.raises(ValueError):       # the sharded step exists only in the fused form
+        limited.Engine(config=cfg, tensors={}, world=2, rank=0, fused=False,
+                       exchange=lambda b: [b, b])
+    with pytest.raises(ValueError):       # the IPC handle swap needs a transport
+        limited.Engine(config=cfg, tensors={}, world=2, rank=1)
