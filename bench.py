@@ -405,6 +405,94 @@ def run_ours(args, dist: Dist):
     return 0
 
 
+def run_gemv_sweep(args, dist: Dist):
+    """The isolated W4A8 GEMV sweep (batch 1): the six sweep shapes (weights N(0,0.02)
+    from seed 1, activation N(0,1)) and the 151936 x 5120 LM head (seed 4), through the
+    C ABI: hv_a4gv_pp over the engine's tile-interleaved layout and hv_a4gv over the
+    reference's row-major layout. One JSON line per (shape, kernel): device time per
+    launch (CUDA events over `--gemv-reps` launches) and achieved GB/s of the algorithmic
+    0.625 B per weight. Weight copies rotate so every launch reads bytes that are not in
+    L2 (126 MB): at least `--gemv-rotate-mb` MB of copies per shape, or one copy with
+    `--gemv-rotate-mb 0`."""
+    if dist.rank != 0:
+        return 0
+    import hvdrv
+    hvdrv.init()
+    peak, peak_kind = measured_peak()
+    e0, e1 = hvdrv.event_create(), hvdrv.event_create()
+    cases = [(j, n, k) for j, (n, k) in enumerate(synth.GEMV_SHAPES)] + [(None, *synth.HEAD_SHAPE)]
+    for j, n, k in cases:
+        if j is None:
+            w, h = synth.head_case(1)
+            a = h[0]
+        else:
+            w, a = synth.gemv_case(j, n, k)
+        nb = k // 32
+        alg = n * k * 5 // 8
+        bufs = []
+
+        def dev(nbytes):
+            p = hvdrv.alloc(nbytes)
+            bufs.append(p)
+            return p
+
+        wd = hvdrv.alloc(w.nbytes)
+        hvdrv.upload(wd, w.ctypes.data, w.nbytes)
+        b4, sw = dev(n * k // 2), dev(n * nb * 4)
+        hvdrv.quantize_w4(wd, b4, sw, n, k)
+        hvdrv.synchronize()
+        hvdrv.free(wd)
+        del w
+        nib, scb = hvdrv.w4_prepacked_size(n, k, 0)
+        pb4, psw = dev(nib), dev(scb)
+        hvdrv.w4_prepack(b4, sw, n, k, 0, pb4, psw)
+        ad, a8, sa, y = dev(k * 4), dev(k), dev(nb * 8), dev(n * 4)
+        hvdrv.upload(ad, a.ctypes.data, a.nbytes)
+        hvdrv.qa8s(ad, a8, sa, nb)
+        copies = max(1, -(-(args.gemv_rotate_mb << 20) // alg)) if args.gemv_rotate_mb else 1
+        rot_pp, rot_ref = [(pb4, psw)], [(b4, sw)]
+        for _ in range(copies - 1):
+            p, s = dev(nib), dev(scb)
+            hvdrv.copy_async(p, pb4, nib)
+            hvdrv.copy_async(s, psw, scb)
+            rot_pp.append((p, s))
+            p, s = dev(n * k // 2), dev(n * nb * 4)
+            hvdrv.copy_async(p, b4, n * k // 2)
+            hvdrv.copy_async(s, sw, n * nb * 4)
+            rot_ref.append((p, s))
+        hvdrv.synchronize()
+
+        def pp(c):
+            hvdrv.a4gv_pp(a8, sa, rot_pp[c][0], rot_pp[c][1], y, k // 8, n, 0)
+
+        def ref(c):
+            hvdrv.a4gv(a8, sa, rot_ref[c][0], rot_ref[c][1], y, k // 8, n)
+
+        for kernel, layout, launch in (("k_a4gv_pp", "tile-interleaved (engine)", pp),
+                                       ("k_a4gv_mma", "row-major (reference)", ref)):
+            for i in range(max(3, copies)):
+                launch(i % copies)
+            hvdrv.synchronize()
+            hvdrv.event_record(e0, 0)
+            for i in range(args.gemv_reps):
+                launch(i % copies)
+            hvdrv.event_record(e1, 0)
+            hvdrv.synchronize()
+            us = hvdrv.event_elapsed_ms(e0, e1) * 1e3 / args.gemv_reps
+            gbs = alg / (us * 1e-6) / 1e9
+            print(json.dumps({
+                "metric": "W4A8 GEMV HBM GB/s (batch 1)", "workload": "gemv-sweep",
+                "shape": [n, k], "kernel": kernel, "layout": layout, "value": gbs,
+                "unit": "GB/s", "us_per_launch": us, "bytes_per_launch": alg,
+                "frac": gbs / peak, "peak": peak, "peak_kind": peak_kind,
+                "launches": args.gemv_reps,
+                "l2": f"{copies} rotating weight copies ({copies * alg / 2**20:.0f} MB)"}),
+                flush=True)
+        for p in bufs:
+            hvdrv.free(p)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,11 +508,18 @@ def main(argv=None):
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
+    ap.add_argument("--gemv-sweep", action="store_true",
+                    help="instead of the decode step: the isolated GEMV sweep, one JSON line "
+                         "per shape and kernel")
+    ap.add_argument("--gemv-reps", type=int, default=300)
+    ap.add_argument("--gemv-rotate-mb", type=int, default=320)
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()
     try:
+        if args.gemv_sweep:
+            return run_gemv_sweep(args, dist)
         if args.impl == "reference":
             return run_reference(args, dist)
         return run_ours(args, dist)

@@ -317,6 +317,61 @@ __global__ void __launch_bounds__(128) k_argmax_f(const float* __restrict__ pv,
 }
 
 // ---------------------------------------------------------------------------
+// Vocabulary-sharded argmax. Each candidate becomes a 64-bit key whose unsigned order
+// is np.argmax's order: high word = the f32 bits mapped to an unsigned total order,
+// low word = ~(global id), so equal values rank the lower id higher. -0 counts as +0
+// (np compares them equal) and every NaN ranks above +inf (np.argmax returns the first
+// NaN). A real key is never 0 (that would need the mapped NaN 0xFFFFFFFF), so 0 is the
+// empty key and the cross-shard reduce is a plain unsigned max.
+// ---------------------------------------------------------------------------
+HV_DEV unsigned long long argmax_key(float v, int id) {
+  unsigned u = __float_as_uint(v);
+  if (v != v) u = 0x7FC00000u;
+  else if (v == 0.f) u = 0u;
+  const unsigned ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(~(unsigned)id);
+}
+
+HV_DEV unsigned long long umax64(unsigned long long a, unsigned long long b) {
+  return a > b ? a : b;
+}
+
+__global__ void __launch_bounds__(256) k_argmax_key(const float* __restrict__ logits, int n,
+                                                    int base, unsigned long long* key) {
+  __shared__ unsigned long long s[8];
+  unsigned long long best = 0;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+    best = umax64(best, argmax_key(logits[j], base + j));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = umax64(best, s[w]);
+    atomicMax(key, best);
+  }
+}
+
+// One warp: max over the shards' keys, then the device generation state advances as in
+// k_argmax_f; the keys are cleared for the next token (each lane clears what it read).
+__global__ void __launch_bounds__(32) k_argmax_keyf(unsigned long long* keys, int nkeys,
+                                                    int32_t* tok, int32_t* gen,
+                                                    int32_t* step, int32_t* pos) {
+  unsigned long long best = 0;
+  for (int j = threadIdx.x; j < nkeys; j += 32) best = umax64(best, keys[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
+  for (int j = threadIdx.x; j < nkeys; j += 32) keys[j] = 0ull;
+  if (threadIdx.x == 0) {
+    const int t = best ? (int)(~(unsigned)(best & 0xFFFFFFFFull)) : -1;
+    *tok = t;
+    gen[*step] = t;
+    *step += 1;
+    *pos += 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // quantize_w4 on the device: one thread per 32-block
 // ---------------------------------------------------------------------------
 __global__ void k_quantize_w4(const float* __restrict__ w, uint32_t* __restrict__ packed,
@@ -463,7 +518,7 @@ extern "C" {
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
       "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_quantize_w4,k_step,k_attn_na";
+      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;
@@ -670,6 +725,28 @@ int hv_argmax_final(const float* pv, const int32_t* pi, int32_t* tok, int32_t* g
              "hv_argmax_final: bad arguments");
   k_argmax_f<<<1, 128, 0, (cudaStream_t)stream>>>(pv, pi, tok, gen, step, pos, parts);
   HV_LAUNCHED("k_argmax_f");
+}
+
+int hv_argmax_key(const float* logits, int n, int base, uint64_t* key, void* stream) {
+  HV_REQUIRE(logits && key && n > 0 && base >= 0 && (long long)base + n <= 0x7FFFFFFFll,
+             HV_E_INVALID, "hv_argmax_key: bad arguments");
+  HV_REQUIRE(((uintptr_t)key & 7) == 0, HV_E_INVALID, "hv_argmax_key: key not 8-byte aligned");
+  int grid = (n + 1023) / 1024;
+  if (grid > 512) grid = 512;
+  k_argmax_key<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      logits, n, base, reinterpret_cast<unsigned long long*>(key));
+  HV_LAUNCHED("k_argmax_key");
+}
+
+int hv_argmax_key_final(uint64_t* keys, int nkeys, int32_t* tok, int32_t* gen, int32_t* step,
+                        int32_t* pos, void* stream) {
+  HV_REQUIRE(keys && tok && gen && step && pos && nkeys > 0, HV_E_INVALID,
+             "hv_argmax_key_final: bad arguments");
+  HV_REQUIRE(((uintptr_t)keys & 7) == 0, HV_E_INVALID,
+             "hv_argmax_key_final: keys not 8-byte aligned");
+  k_argmax_keyf<<<1, 32, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<unsigned long long*>(keys), nkeys, tok, gen, step, pos);
+  HV_LAUNCHED("k_argmax_keyf");
 }
 
 int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,

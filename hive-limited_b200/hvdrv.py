@@ -89,6 +89,8 @@ _SIGS = {
     "hv_gather_emb": [_VP, _VP, _VP, _I, _VP],
     "hv_argmax_partial": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_argmax_final": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _VP],
+    "hv_argmax_key": [_VP, _I, _I, _VP, _VP],
+    "hv_argmax_key_final": [_VP, _I, _VP, _VP, _VP, _VP, _VP],
     "hv_quantize_w4": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_w4_prepacked_size": [_I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
     "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
@@ -437,6 +439,23 @@ def argmax_partial(logits, pv, pi, n, parts, stream=0):
 def argmax_final(pv, pi, tok, gen, step, pos, parts, stream=0):
     _call("hv_argmax_final", _p(pv), _p(pi), _p(tok), _p(gen), _p(step), _p(pos), parts,
           _p(stream))
+
+
+def argmax_key(logits, n, base, key, stream=0):
+    """Fold one vocabulary shard (global ids base..base+n-1) into its 64-bit argmax key."""
+    _call("hv_argmax_key", _p(logits), n, base, _p(key), _p(stream))
+
+
+def argmax_key_final(keys, nkeys, tok, gen, step, pos, stream=0):
+    """Token = the best of `nkeys` shard keys; advances tok/gen/step/pos like argmax_f and
+    clears the keys."""
+    _call("hv_argmax_key_final", _p(keys), nkeys, _p(tok), _p(gen), _p(step), _p(pos),
+          _p(stream))
+
+
+def token_of_key(key: int) -> int:
+    """Global token id carried by a 64-bit argmax key (-1 for the empty key 0)."""
+    return (~key) & 0xFFFFFFFF if key else -1
 
 
 def w4_prepacked_size(rows, k, pair_ffn=0):

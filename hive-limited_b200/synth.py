@@ -157,8 +157,21 @@ def gemv_case(index: int, n: int, k: int, seed: int = GEMV_SEED):
     return w, a
 
 
-def head_case(n_states: int, seed: int = HEAD_SEED, shape=HEAD_SHAPE):
-    """LM-head workload: weights [151936, 5120] and `n_states` N(0,1) hidden states."""
-    w = rng_for(seed, 0).standard_normal(shape, dtype=F32) * F32(0.02)
-    h = rng_for(seed, 1).standard_normal((n_states, shape[1]), dtype=F32)
+def head_case(n_states: int, seed: int = HEAD_SEED, shape=HEAD_SHAPE, threads: int | None = None):
+    """LM-head workload: weights [151936, 5120] N(0,0.02) and `n_states` N(0,1) hidden
+    states (stream (seed, 1)). The weight rows are drawn in 8 row blocks, block b from
+    stream (seed, 0, b), on a thread pool; the draw does not depend on the thread count."""
+    n, k = shape
+    w = np.empty(shape, F32)
+    nblk = 8
+    edges = [n * b // nblk for b in range(nblk + 1)]
+
+    def fill(b):
+        part = w[edges[b]:edges[b + 1]]
+        rng_for(seed, 0, b).standard_normal(part.shape, dtype=F32, out=part)
+        part *= F32(0.02)
+
+    with cf.ThreadPoolExecutor(threads or min(nblk, os.cpu_count() or 1)) as ex:
+        list(ex.map(fill, range(nblk)))
+    h = rng_for(seed, 1).standard_normal((n_states, k), dtype=F32)
     return w, h

@@ -190,6 +190,19 @@ int hv_argmax_partial(const float* logits, float* pv, int32_t* pi, int n, int pa
 int hv_argmax_final(const float* pv, const int32_t* pi, int32_t* tok, int32_t* gen,
                     int32_t* step, int32_t* pos, int parts, void* stream);
 
+/* Vocabulary-sharded greedy argmax: argmax_p/argmax_f (engine/limited.py:421-428) split
+ * at shard boundaries, for an LM head whose rows are spread over several GPUs. The
+ * result is np.argmax over the whole vocabulary (engine/reference.py:219: first maximal
+ * id; -0 equals +0; a NaN wins, the first one).
+ * hv_argmax_key folds logits[0..n) of one shard, whose first row is global id `base`,
+ * into *key (atomic max of an order-preserving 64-bit key: value, then lower id).
+ * *key must be 0 before the shard's first fold; hv_argmax_key_final leaves it 0. */
+int hv_argmax_key(const float* logits, int n, int base, uint64_t* key, void* stream);
+/* Max over nkeys shard keys (one per shard, e.g. gathered from every rank), then as
+ * argmax_f: *tok, gen[*step] = tok, ++*step, ++*pos; every keys[i] is reset to 0. */
+int hv_argmax_key_final(uint64_t* keys, int nkeys, int32_t* tok, int32_t* gen,
+                        int32_t* step, int32_t* pos, void* stream);
+
 /* quantize_w4 (engine/limited.py:40-58) on the device: f32 w [n][k] -> packed u32
  * [n][k/8] and scales f32 [n][k/32], bit-exact with the host rule. */
 int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,
