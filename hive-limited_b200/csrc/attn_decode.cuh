@@ -20,6 +20,8 @@ namespace hv {
 constexpr int kHd = 128;
 constexpr int kAttnChunkMax = 1024;   // positions one work item may hold
 constexpr int kPartStride = 132;      // per q head: m, l, 2 pad, acc[128]
+constexpr int kAttnMaxChunks = 480;   // chunks per kv head: the merge scratch (2 nch GS + GS
+                                      // floats) lies within the 8 x GS x 128 V-sum area
 constexpr int kAttnBlock = 20;        // positions per block: block b of a chunk -> warp b % nw
 
 HV_DEV void chunk_bounds(int npos, int nch, int c, int* t0, int* t1) {

@@ -147,6 +147,8 @@ extern "C" int hv_attn_decode_noalloc(const float* q, const float* kc, const flo
              "hv_attn_decode_noalloc: %zu bytes of partial softmax state (%d kv heads x %d "
              "chunks x group %d) exceed the fixed scratch of %zu bytes",
              part_bytes, nkv, nch, group, kNaScratchBytes - kNaTicketBytes);
+  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
+             "hv_attn_decode_noalloc: %d chunks per kv head (at most %d)", nch, kAttnMaxChunks);
 
   int dev = 0;
   HV_CUDA(cudaGetDevice(&dev));

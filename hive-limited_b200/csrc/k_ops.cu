@@ -463,6 +463,9 @@ static int attn_nch(int nkv, int cap, int* out) {
   int nch = (sms + nkv - 1) / nkv;
   const int need = (cap + kAttnChunkMax - 1) / kAttnChunkMax;
   *out = nch > need ? nch : need;
+  HV_REQUIRE(*out <= kAttnMaxChunks, HV_E_UNSUPPORTED,
+             "hv_attn_decode: %d chunks per kv head (at most %d; the cache is too long)", *out,
+             kAttnMaxChunks);
   return HV_OK;
 }
 

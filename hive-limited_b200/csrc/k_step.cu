@@ -1464,6 +1464,9 @@ int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t
   if (nch < 1) nch = 1;
   const int need = (cap + 511) / 512;
   if (nch < need) nch = need;
+  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
+             "hv_step_config: %d attention chunks per kv head (at most %d; cap %d is too long)",
+             nch, kAttnMaxChunks, cap);
   *chunks = nch;
   *part_floats = (size_t)n_kv * nch * group * kPartStride;
   if (smem) *smem = 0;
