@@ -58,7 +58,7 @@ UNIT = "tok/s"
 # ---------------------------------------------------------------------------
 
 class Dist:
-    def __init__(self):
+    def __init__(self, timeout_s: float = 600.0):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -68,7 +68,7 @@ class Dist:
 
             import torch.distributed as dist
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=timeout_s))
             self.pg = dist
 
     def barrier(self):
