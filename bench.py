@@ -283,7 +283,9 @@ def run_ours(args, dist: Dist):
     eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
                          max_context=cap, device=dist.local, fused=True,
                          world=dist.world if sharded else 1, rank=dist.rank if sharded else 0,
-                         exchange=dist.allgather_bytes if sharded else None)
+                         exchange=dist.allgather_bytes if sharded else None,
+                         weight_cache=args.weight_cache,
+                         cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
     window = cap - n_prompt              # decode positions available before a rewind
@@ -398,6 +400,7 @@ def run_ours(args, dist: Dist):
             "gpu_launches": args.steps,
             "clocks": clk,
             "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
+            "weight_cache": {None: None, True: "hit", False: "miss"}[eng.cache_hit],
         }
         print(json.dumps(line), flush=True)
     hvdrv.host_free(pin)
@@ -508,6 +511,9 @@ def main(argv=None):
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
+    ap.add_argument("--weight-cache", default=None, metavar="DIR",
+                    help="load device-ready weights from DIR when present, else quantise "
+                         "and write them there (the timed steps are the same either way)")
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="instead of the decode step: the isolated GEMV sweep, one JSON line "
                          "per shape and kernel")

@@ -22,6 +22,7 @@ from pathlib import Path
 import numpy as np
 
 import hvdrv
+import wcache
 from w4format import (BLOCK, Config, SafeTensors, dequantize_w4, load_model_tensors,  # noqa: F401
                       quantize_w4)
 
@@ -123,12 +124,20 @@ class Engine:
                            this engine holds rank `rank`'s rows of every projection and its
                            heads; `exchange(bytes) -> list[bytes]` is an all-gather over the
                            ranks (any transport) used once, to swap the CUDA IPC handles of
-                           the buffers the fused step writes into on every rank.
+                           the buffers the fused step writes into on every rank;
+      weight_cache / cache_tag
+                        -- a directory of device-ready weights (wcache.py): on a hit the
+                           engine uploads the cached prepacked int4 weights, embedding and
+                           norms and reads no checkpoint; on a miss it loads as usual and
+                           then writes the entry. The entry is keyed by the model
+                           directory's files, or by `cache_tag` for `tensors=` sources.
+                           `cache_hit` tells which happened (None without a cache).
     """
 
     def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
                  config=None, tensors=None, max_context=None, device=0, fused=True,
-                 quantize_on="device", world=1, rank=0, exchange=None):
+                 quantize_on="device", world=1, rank=0, exchange=None, weight_cache=None,
+                 cache_tag=None):
         if config is None:
             self.cfg = Config.load(model_dir)
         else:
@@ -145,6 +154,12 @@ class Engine:
             raise ValueError("a sharded engine runs the fused step and needs `exchange`")
         self._exchange = exchange
         self.d_peers = None
+        self.cache_hit = None
+        key = ident = None
+        if weight_cache is not None:          # argument errors before any device work
+            key, ident = wcache.entry_key(self.cfg, self.world, self.rank,
+                                          model_dir=None if cache_tag is not None else model_dir,
+                                          tag=cache_tag)
         hvdrv.load(kernels_dir, verify=verify_kernels)
         hvdrv.init()
         self.dev = hvdrv.device(device)
@@ -158,10 +173,18 @@ class Engine:
         self._graph_ok = None
         self._stream = 0
         self._stream_cur = 0
-        src = _TensorSource(tensors if tensors is not None
-                            else load_model_tensors(model_dir))
-        self._upload_weights(src, quantize_on)
-        del src
+        entry = wcache.open_entry(weight_cache, key) if weight_cache is not None else None
+        if entry is not None:
+            self._upload_cached(entry)
+            self.cache_hit = True
+        else:
+            src = _TensorSource(tensors if tensors is not None
+                                else load_model_tensors(model_dir))
+            self._upload_weights(src, quantize_on)
+            del src
+            if weight_cache is not None:
+                self._save_cache(weight_cache, key, ident)
+                self.cache_hit = False
         self._alloc_state()
 
     # -- setup ----------------------------------------------------------------------
@@ -261,6 +284,76 @@ class Engine:
             if self._stage:
                 hvdrv.free(self._stage)
                 self._stage = 0
+
+    # -- the weight cache (wcache.py) -------------------------------------------------
+
+    def _download(self, ptr: int, shape, dtype) -> np.ndarray:
+        out = np.empty(shape, dtype)
+        hvdrv.download(out.ctypes.data, ptr, out.nbytes)
+        return out
+
+    def _cache_items(self):
+        """(name, kind, device object, shape, dtype) of every uploaded weight."""
+        c = self.cfg
+        yield "emb16", "array", self.d_emb16, (c.vocab, c.hidden), np.float16
+        for l, L in enumerate(self.layers):
+            for nm, n in (("an", c.hidden), ("fn", c.hidden), ("qn", c.head_dim),
+                          ("kn", c.head_dim)):
+                yield f"{l}.{nm}", "array", L[nm], (n,), F32
+            for nm in ("qkv", "o", "gu", "down"):
+                yield f"{l}.{nm}", "w4", L[nm], None, None
+        yield "onorm", "array", self.d_onorm, (c.hidden,), F32
+        yield "head", "w4", self.head, None, None
+
+    def _save_cache(self, root, key: str, ident: dict):
+        w = wcache.EntryWriter(root, key, ident)
+        try:
+            for name, kind, obj, shape, dtype in self._cache_items():
+                if kind == "array":
+                    w.add_array(name, self._download(obj, shape, dtype))
+                else:
+                    pb4, psw, k, n, pair = obj
+                    nib, scb = hvdrv.w4_prepacked_size(n, k, pair)
+                    w.add_w4(name, self._download(pb4, (nib,), np.uint8),
+                             self._download(psw, (scb,), np.uint8), k, n, pair)
+            path = w.commit()
+        except BaseException:
+            w.abort()
+            raise
+        self._log(f"weight cache written: {path}")
+
+    def _upload_cached(self, e):
+        """Upload a cache entry (the bytes _save_cache downloaded, unchanged)."""
+        c = self.cfg
+        sh = self.shard
+        qd = c.head_dim
+        want_rows = {"qkv": (sh["n_head"] + 2 * sh["n_kv"]) * qd,
+                     "o": sh["hid"][1] - sh["hid"][0], "gu": 2 * sh["ffn_n"],
+                     "down": sh["hid"][1] - sh["hid"][0]}
+        want_k = {"qkv": c.hidden, "o": c.n_head * qd, "gu": c.hidden, "down": c.ffn}
+
+        def up_w4(name, rows=None, k=None):
+            nib, sc, kk, n, pair = e.w4(name)
+            if (rows is not None and n != rows) or (k is not None and kk != k):
+                raise ValueError(f"weight cache {e.path}: {name} is {n}x{kk}, "
+                                 f"expected {rows}x{k}")
+            if (nib.nbytes, sc.nbytes) != hvdrv.w4_prepacked_size(n, kk, pair):
+                raise ValueError(f"weight cache {e.path}: {name} has the wrong byte count")
+            return self._up(nib), self._up(sc), kk, n, pair
+
+        self._quantize_on = "cache"
+        self._log(f"loading device-ready weights from {e.path} ...")
+        self.d_emb16 = self._up(e.array("emb16"))
+        self.layers = []
+        for l in range(c.n_layer):
+            d = {nm: self._up(e.array(f"{l}.{nm}")) for nm in ("an", "fn", "qn", "kn")}
+            for nm in ("qkv", "o", "gu", "down"):
+                d[nm] = up_w4(f"{l}.{nm}", want_rows[nm], want_k[nm])
+            self.layers.append(d)
+        self.d_onorm = self._up(e.array("onorm"))
+        self.head = up_w4("head", sh["vocab_n"], c.hidden)
+        self.n_head_rows = self.head[3]
+        hvdrv.synchronize()
 
     def _alloc_state(self):
         c = self.cfg
