@@ -424,6 +424,8 @@ def run_gemv_sweep(args, dist: Dist):
     peak, peak_kind = measured_peak()
     e0, e1 = hvdrv.event_create(), hvdrv.event_create()
     cases = [(j, n, k) for j, (n, k) in enumerate(synth.GEMV_SHAPES)] + [(None, *synth.HEAD_SHAPE)]
+    if args.gemv_max_rows:
+        cases = [c for c in cases if c[1] <= args.gemv_max_rows]
     for j, n, k in cases:
         if j is None:
             w, h = synth.head_case(1)
@@ -518,6 +520,8 @@ def main(argv=None):
                     help="instead of the decode step: the isolated GEMV sweep, one JSON line "
                          "per shape and kernel")
     ap.add_argument("--gemv-reps", type=int, default=300)
+    ap.add_argument("--gemv-max-rows", type=int, default=0,
+                    help="sweep only the shapes with at most this many rows (0: all)")
     ap.add_argument("--gemv-rotate-mb", type=int, default=320)
     args = ap.parse_args(argv)
     if args.warmup < 3:

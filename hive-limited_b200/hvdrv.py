@@ -95,6 +95,7 @@ _SIGS = {
     "hv_w4_prepacked_size": [_I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
     "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
+    "hv_gemv_set_split": [_I],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
     "hv_step_set_option": [_I, _I],
@@ -471,6 +472,12 @@ def w4_prepack(b4, sw, rows, k, pair_ffn, pb4, psw, stream=0):
 def a4gv_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn=0, stream=0):
     _call("hv_a4gv_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
           _p(stream))
+
+
+def gemv_set_split(enable: bool) -> None:
+    """Whether hv_a4gv_pp may run small matrices on the iteration-split kernel (default
+    on; the results are identical either way)."""
+    _call("hv_gemv_set_split", 1 if enable else 0)
 
 
 def quantize_w4(w, packed, scale, n, k, stream=0):

@@ -128,9 +128,15 @@ int hv_a4gv_idot(const int8_t* a8, const float* sa, const uint32_t* b4, const fl
 int hv_w4_prepacked_size(int rows, int k, int pair_ffn, size_t* nib_bytes, size_t* scale_bytes);
 int hv_w4_prepack(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
                   uint32_t* pb4, float* psw, void* stream);
-/* gemv_wpo_a4 over the prepacked layout; dst keeps the reference row order. */
+/* gemv_wpo_a4 over the prepacked layout; dst keeps the reference row order. Matrices of
+ * few tiles (under 16 per SM, 4096 <= K <= 16384, K a multiple of 256) run on an
+ * iteration-split kernel whose warps share each tile's K; the result is the same bit for
+ * bit. */
 int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
                float* dst, int k8, int rows, int pair_ffn, void* stream);
+/* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split
+ * kernel, 0 runs every matrix on the one-warp-per-tile kernel. Process-wide. */
+int hv_gemv_set_split(int enable);
 
 /* rmsnorm_bp (k_rmsbp.ptx; launch engine/limited.py:361-362): row-wise
  * dst = w * (src / sqrt(mean(src^2) + eps)); rows x cols; in place allowed. The

@@ -204,3 +204,32 @@ def test_prepack_roundtrip_and_gemv_pp_bit_exact(hv, n, k, pair):
     y = Dev(nbytes=n * 4)
     hv.a4gv_pp(a8, sa, pb4, psw, y, k // 8, n, pair)
     assert np.array_equal(bits(y.get(F32)), bits(want))
+
+
+@pytest.mark.parametrize("n,k,pair", [(8, 256, 0), (40, 16384, 0), (100, 12288, 0),
+                                      (2048, 6144, 0), (24, 2048, 12), (3000, 4096, 0),
+                                      (8, 4096, 0), (24, 4096, 12)])
+def test_gemv_split_kernel_bit_identical(hv, n, k, pair):
+    """hv_a4gv_pp on the iteration-split kernel (few tiles and K >= 4096, the default)
+    and on the one-warp-per-tile kernel give the same bits, and both the oracle's
+    (multi-leaf plans, gate/up pairs and the 64-iteration limit included)."""
+    g = np.random.default_rng(n + 7 * k)
+    p, sc = O.quantize_w4((g.standard_normal((n, k)) * 0.02).astype(F32))
+    nib, scb = hv.w4_prepacked_size(n, k, pair)
+    pb4, psw = Dev(nbytes=nib), Dev(nbytes=scb)
+    hv.w4_prepack(Dev(p), Dev(sc), n, k, pair, pb4, psw)
+    a = (g.standard_normal(k) * 2).astype(F32)
+    qa, sa_h, _ = O.quantize_act(a)
+    _, want = O.gemv_q_c(qa, sa_h, p, sc, k)
+    a8, sa = quantize_on_device(a)
+    out = []
+    try:
+        for split in (True, False):
+            hv.gemv_set_split(split)
+            y = Dev(nbytes=n * 4)
+            hv.a4gv_pp(a8, sa, pb4, psw, y, k // 8, n, pair)
+            out.append(y.get(F32))
+    finally:
+        hv.gemv_set_split(True)
+    assert np.array_equal(bits(out[0]), bits(out[1]))
+    assert np.array_equal(bits(out[0]), bits(want))
