@@ -9,6 +9,7 @@
 #include "attn_decode.cuh"
 #include "gemv_mma.cuh"
 #include "hv_internal.h"
+#include "hv_wait.cuh"
 
 namespace hv {
 
@@ -461,6 +462,13 @@ __global__ void __launch_bounds__(32) k_argmax_keyf(unsigned long long* keys, in
   }
 }
 
+// One thread: the bounded poll every wait of the fused step uses, on a caller's word.
+__global__ void k_wait_probe(const unsigned* word, unsigned mask, unsigned want,
+                             unsigned long long limit_ns, int* status) {
+  if (threadIdx.x == 0 && blockIdx.x == 0)
+    poll_word_until<false>(word, mask, want, status, limit_ns);
+}
+
 // ---------------------------------------------------------------------------
 // quantize_w4 on the device: one thread per 32-block
 // ---------------------------------------------------------------------------
@@ -611,7 +619,7 @@ extern "C" {
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
       "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na";
+      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;
@@ -854,6 +862,18 @@ int hv_argmax_key_final(uint64_t* keys, int nkeys, int32_t* tok, int32_t* gen, i
   k_argmax_keyf<<<1, 32, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<unsigned long long*>(keys), nkeys, tok, gen, step, pos);
   HV_LAUNCHED("k_argmax_keyf");
+}
+
+int hv_wait_probe(const uint32_t* word, uint32_t mask, uint32_t want, long long limit_ns,
+                  int32_t* status, void* stream) {
+  HV_REQUIRE(word && status && ((uintptr_t)word & 3) == 0 && ((uintptr_t)status & 3) == 0,
+             HV_E_INVALID, "hv_wait_probe: bad arguments");
+  HV_REQUIRE(limit_ns > 0 && limit_ns <= 10000000000ll, HV_E_INVALID,
+             "hv_wait_probe: limit %lld ns outside (0, 10 s]", limit_ns);
+  k_wait_probe<<<1, 32, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const unsigned*>(word), mask, want, (unsigned long long)limit_ns,
+      reinterpret_cast<int*>(status));
+  HV_LAUNCHED("k_wait_probe");
 }
 
 int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,

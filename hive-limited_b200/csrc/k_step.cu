@@ -40,6 +40,7 @@
 #include "attn_decode.cuh"
 #include "gemv_mma.cuh"
 #include "hv_internal.h"
+#include "hv_wait.cuh"
 
 namespace hv {
 
@@ -187,17 +188,6 @@ HV_DEV unsigned long long policy_evict_first() {
   return p;
 }
 
-HV_DEV unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-HV_DEV unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 
 // Bounded wait for the completion of phase `parity` of mbarrier b. Gives up (false) when
 // this CTA has aborted, when any CTA reported a failure in *status, or after `limit` ns
@@ -243,28 +233,11 @@ struct Ring {
   HV_DEV unsigned parity(unsigned q) const { return (q / ns) & 1u; }
 };
 
-HV_DEV unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Bounded poll of a barrier word until (value & mask) == want; false (HV_E_TIMEOUT, or
 // another failure already reported on this rank) when it gives up.
 template <bool kSys>
 HV_DEV bool poll_word(const unsigned* w, unsigned mask, unsigned want, int* status) {
-  const unsigned long long t0 = global_ns();
-  for (unsigned n = 1;; ++n) {
-    const unsigned v = kSys ? ld_acquire_sys(w) : ld_acquire(w);
-    if ((v & mask) == want) return true;
-    if ((n & 31) == 0) {
-      if (*(volatile int*)status != 0) return false;
-      if (global_ns() - t0 > kWaitNs) {
-        atomicCAS(status, 0, HV_E_TIMEOUT);
-        return false;
-      }
-    }
-  }
+  return poll_word_until<kSys>(w, mask, want, status, kWaitNs);
 }
 
 // Grid-wide barrier of the consumer threads over self-resetting counters: the first

@@ -92,6 +92,7 @@ _SIGS = {
     "hv_argmax_key": [_VP, _I, _I, _VP, _VP],
     "hv_argmax_key_final": [_VP, _I, _VP, _VP, _VP, _VP, _VP],
     "hv_quantize_w4": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_wait_probe": [_VP, C.c_uint32, C.c_uint32, C.c_longlong, _VP, _VP],
     "hv_w4_prepacked_size": [_I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
     "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
@@ -471,6 +472,13 @@ def w4_prepack(b4, sw, rows, k, pair_ffn, pb4, psw, stream=0):
 
 def a4gv_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn=0, stream=0):
     _call("hv_a4gv_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
+          _p(stream))
+
+
+def wait_probe(word, mask, want, limit_ns, status, stream=0):
+    """The fused step's bounded wait on a caller's device word (see hv_wait_probe):
+    *status becomes HV_E_TIMEOUT (1004) if (*word & mask) != want for limit_ns."""
+    _call("hv_wait_probe", _p(word), int(mask), int(want), int(limit_ns), _p(status),
           _p(stream))
 
 

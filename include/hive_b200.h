@@ -209,6 +209,16 @@ int hv_argmax_key(const float* logits, int n, int base, uint64_t* key, void* str
 int hv_argmax_key_final(uint64_t* keys, int nkeys, int32_t* tok, int32_t* gen,
                         int32_t* step, int32_t* pos, void* stream);
 
+/* The bounded device-side wait that every cross-CTA and cross-rank wait of the fused
+ * step is built on (no counterpart in the reference, whose kernels never wait on each
+ * other): one thread polls *word until (*word & mask) == want, for at most limit_ns
+ * (0 < limit_ns <= 10 s). If the limit passes it sets *status = HV_E_TIMEOUT (unless
+ * *status already holds a failure, which also ends the wait early) and the kernel
+ * returns; the context stays usable. Asynchronous: read *status after synchronising.
+ * Lets the timeout path be exercised on a word that nothing sets, without a hung GPU. */
+int hv_wait_probe(const uint32_t* word, uint32_t mask, uint32_t want, long long limit_ns,
+                  int32_t* status, void* stream);
+
 /* quantize_w4 (engine/limited.py:40-58) on the device: f32 w [n][k] -> packed u32
  * [n][k/8] and scales f32 [n][k/32], bit-exact with the host rule. */
 int hv_quantize_w4(const float* w, uint32_t* packed, float* scale, int n, int k,
