@@ -271,4 +271,17 @@ HV_HD int pp_tiles(int rows, int pair_ffn) {
 }
 HV_HD int pp_iters(int nb) { return (nb + 7) / 8; }
 
+// Row of the reference matrix behind quad g of `tile`: plain 8-row tiles, or (pair_ffn
+// > 0) 4 gate rows p and their 4 up rows ffn + p of a [gate | up] matrix.
+HV_DEV int pp_row(int tile, int g, int rows, int pair_ffn, bool* ok) {
+  if (pair_ffn > 0) {
+    const int p = tile * 4 + (g & 3);
+    *ok = p < pair_ffn;
+    return (g < 4) ? p : pair_ffn + p;
+  }
+  const int row = tile * 8 + g;
+  *ok = row < rows;
+  return row;
+}
+
 }  // namespace hv

@@ -118,18 +118,6 @@ __global__ void __launch_bounds__(256) k_a4gv_mma(const int8_t* __restrict__ a8,
 // tile-interleaved weight layout (see gemv_mma.cuh) and the GEMV over it
 // ---------------------------------------------------------------------------
 
-// Row of the reference matrix behind quad g of `tile`: plain 8-row tiles, or (pair_ffn
-// > 0) 4 gate rows p and their 4 up rows ffn + p of a [gate | up] matrix.
-HV_DEV int pp_row(int tile, int g, int rows, int pair_ffn, bool* ok) {
-  if (pair_ffn > 0) {
-    const int p = tile * 4 + (g & 3);
-    *ok = p < pair_ffn;
-    return (g < 4) ? p : pair_ffn + p;
-  }
-  const int row = tile * 8 + g;
-  *ok = row < rows;
-  return row;
-}
 
 // one thread per (tile, iteration, lane): 8 nibble words and 2 scales
 __global__ void k_w4_prepack(const uint32_t* __restrict__ b4, const float* __restrict__ sw,
@@ -619,7 +607,7 @@ extern "C" {
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
       "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe";
+      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;

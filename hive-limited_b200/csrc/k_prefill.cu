@@ -1,0 +1,175 @@
+// Prompt prefill: the W4A8 projections of many tokens at once.
+//
+// The reference prefills a prompt by running its decode step once per token
+// (engine/limited.py:455-462), so every weight byte is read once per prompt token. Here
+// the projections of T tokens are one GEMM over the engine's tile-interleaved weights.
+// Each token's output is bit-identical to hv_a4gv_pp on that token alone: the same exact
+// int32 block dots, the same f32 combine f32(f32(sw * sa) * f32(idot)), the same numpy
+// pairwise order (eight strided accumulators per leaf, the ((r0+r1)+(r2+r3))+((r4+r5)+
+// (r6+r7)) fold, the recursion's postfix '+', then (+0) + ...).
+//
+// Mapping onto mma.sync.m16n8k32 (u8 x s8 -> s32), lane = 4 g + t:
+//   * A (16 x 32): rows 0..7 are the 8 rows of weight tile 2p at block b, rows 8..15 the
+//     8 rows of tile 2p + 1 at the same block. k is permuted as in the decode GEMV, so
+//     lane (g, t)'s A registers are the low / high nibbles of packed word t of block b of
+//     row g of each tile -- exactly the words the tile-interleaved layout gives lane L.
+//   * B (32 x 8): column n is token 8 q + n's int8 activation block b (lane (g, t) holds
+//     bytes 8t .. 8t+7 of token 8 q + g's block).
+//   * D: lane (g, t) gets the dots of rows g of both tiles with tokens 8 q + 2t and
+//     8 q + 2t + 1 -- four (row, token) pairs, whose eight pairwise accumulators per leaf
+//     it keeps in registers, so a leaf folds without shuffles.
+// Every block's dot is its own MMA (a block's idot must stay separate for the per-block
+// scale), so the f32 combine, not the MMA, is the cost: 4 combines per lane per MMA.
+//
+// A CTA is 8 warps: 2 tile pairs (32 weight rows) x 4 token groups (32 tokens). No CTA
+// barrier: warps of the same tile pair share the weights through L1.
+#include "gemv_mma.cuh"
+#include "hv_internal.h"
+
+namespace hv {
+namespace {
+
+constexpr int kPfMaxBlocks = 1024;   // K <= 32768
+
+HV_DEV float pf_fold8(const float (&r)[8]) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                   __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+}
+
+HV_DEV float pf_term(float sw, float sa, int d, int bsum) {
+  return __fmul_rn(__fmul_rn(sw, sa), i2f_exact(d - 8 * bsum));
+}
+
+__global__ void __launch_bounds__(256) k_a4gemm_pp(const int8_t* __restrict__ a8,
+                                                   const float* __restrict__ sa,
+                                                   const uint32_t* __restrict__ pb4,
+                                                   const float* __restrict__ psw,
+                                                   float* __restrict__ dst, int ntok,
+                                                   int rows, int pair_ffn,
+                                                   const __grid_constant__ GvPlan plan) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+  const int nb = plan.nb, niter = plan.nfull, k = nb * kBlock;
+  const int ntile = pp_tiles(rows, pair_ffn);
+  const int tile_a = 2 * (blockIdx.x * 2 + (warp & 1));
+  const int tq = blockIdx.y * 4 + (warp >> 1);          // tokens 8 tq .. 8 tq + 7
+  if (tile_a >= ntile || tq * 8 >= ntok) return;      // whole warps; no CTA barrier below
+  const bool has_b = tile_a + 1 < ntile;
+  const int tile_b = has_b ? tile_a + 1 : tile_a;       // a missing tile is computed, not stored
+  const int tok_col = min(tq * 8 + g, ntok - 1);         // B column of this lane
+  const int n0 = tq * 8 + 2 * t, n1 = n0 + 1;           // D columns of this lane
+  const int8_t* act = a8 + (size_t)tok_col * k + 8 * t;
+  const float* sa0 = sa + (size_t)min(n0, ntok - 1) * 2 * nb;
+  const float* sa1 = sa + (size_t)min(n1, ntok - 1) * 2 * nb;
+  const uint32_t* wa = pb4 + (size_t)tile_a * niter * kPpNibWords + 4 * lane;
+  const uint32_t* wb = pb4 + (size_t)tile_b * niter * kPpNibWords + 4 * lane;
+  const float* sca = psw + (size_t)tile_a * niter * kPpScales + 8 * g;
+  const float* scb = psw + (size_t)tile_b * niter * kPpScales + 8 * g;
+
+  float r[4][8];        // accumulators of (row A, n0), (A, n1), (B, n0), (B, n1)
+  float st[4][8];       // fold stacks (postfix '+' of numpy's recursion)
+  int sp = 0, leaf = 0, leaf_begin = 0;
+  for (int it = 0; it < niter; ++it) {
+    const size_t wo = (size_t)it * kPpNibWords, so = (size_t)it * kPpScales;
+    const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + wo));
+    const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wa + wo + 128));
+    const uint4 b_lo = __ldg(reinterpret_cast<const uint4*>(wb + wo));
+    const uint4 b_hi = __ldg(reinterpret_cast<const uint4*>(wb + wo + 128));
+    const unsigned wA[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+    const unsigned wB[8] = {b_lo.x, b_lo.y, b_lo.z, b_lo.w, b_hi.x, b_hi.y, b_hi.z, b_hi.w};
+    const float4 sA0 = __ldg(reinterpret_cast<const float4*>(sca + so));
+    const float4 sA1 = __ldg(reinterpret_cast<const float4*>(sca + so + 4));
+    const float4 sB0 = __ldg(reinterpret_cast<const float4*>(scb + so));
+    const float4 sB1 = __ldg(reinterpret_cast<const float4*>(scb + so + 4));
+    const float swA[8] = {sA0.x, sA0.y, sA0.z, sA0.w, sA1.x, sA1.y, sA1.z, sA1.w};
+    const float swB[8] = {sB0.x, sB0.y, sB0.z, sB0.w, sB1.x, sB1.y, sB1.z, sB1.w};
+    const float4 x00 = __ldg(reinterpret_cast<const float4*>(sa0 + 8 * it));
+    const float4 x01 = __ldg(reinterpret_cast<const float4*>(sa0 + 8 * it + 4));
+    const int4 y00 = __ldg(reinterpret_cast<const int4*>(sa0 + nb + 8 * it));
+    const int4 y01 = __ldg(reinterpret_cast<const int4*>(sa0 + nb + 8 * it + 4));
+    const float4 x10 = __ldg(reinterpret_cast<const float4*>(sa1 + 8 * it));
+    const float4 x11 = __ldg(reinterpret_cast<const float4*>(sa1 + 8 * it + 4));
+    const int4 y10 = __ldg(reinterpret_cast<const int4*>(sa1 + nb + 8 * it));
+    const int4 y11 = __ldg(reinterpret_cast<const int4*>(sa1 + nb + 8 * it + 4));
+    const float s0[8] = {x00.x, x00.y, x00.z, x00.w, x01.x, x01.y, x01.z, x01.w};
+    const int q0[8] = {y00.x, y00.y, y00.z, y00.w, y01.x, y01.y, y01.z, y01.w};
+    const float s1[8] = {x10.x, x10.y, x10.z, x10.w, x11.x, x11.y, x11.z, x11.w};
+    const int q1[8] = {y10.x, y10.y, y10.z, y10.w, y11.x, y11.y, y11.z, y11.w};
+    uint2 bw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      bw[j] = __ldg(reinterpret_cast<const uint2*>(act + (size_t)(it * 8 + j) * kBlock));
+    const bool first = it == leaf_begin;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int d0, d1, d2, d3;
+      mma_u8s8(nib_lo(wA[j]), nib_lo(wB[j]), nib_hi(wA[j]), nib_hi(wB[j]), bw[j].x, bw[j].y,
+               d0, d1, d2, d3);
+      const float c[4] = {pf_term(swA[j], s0[j], d0, q0[j]), pf_term(swA[j], s1[j], d1, q1[j]),
+                          pf_term(swB[j], s0[j], d2, q0[j]), pf_term(swB[j], s1[j], d3, q1[j])};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) r[p][j] = first ? c[p] : __fadd_rn(r[p][j], c[p]);
+    }
+    if (it + 1 == plan.it_end[leaf]) {                // a leaf ends: fold, push, close
+#pragma unroll
+      for (int p = 0; p < 4; ++p) st[p][sp] = pf_fold8(r[p]);
+      ++sp;
+      for (int c = 0; c < plan.pops[leaf]; ++c) {
+        --sp;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) st[p][sp - 1] = __fadd_rn(st[p][sp - 1], st[p][sp]);
+      }
+      ++leaf;
+      leaf_begin = it + 1;
+    }
+  }
+  bool ok_a, ok_b;
+  const int row_a = pp_row(tile_a, g, rows, pair_ffn, &ok_a);
+  const int row_b = pp_row(tile_b, g, rows, pair_ffn, &ok_b);
+  ok_b = ok_b && has_b;
+  if (n0 < ntok) {
+    if (ok_a) dst[(size_t)n0 * rows + row_a] = __fadd_rn(0.0f, st[0][0]);
+    if (ok_b) dst[(size_t)n0 * rows + row_b] = __fadd_rn(0.0f, st[2][0]);
+  }
+  if (n1 < ntok) {
+    if (ok_a) dst[(size_t)n1 * rows + row_a] = __fadd_rn(0.0f, st[1][0]);
+    if (ok_b) dst[(size_t)n1 * rows + row_b] = __fadd_rn(0.0f, st[3][0]);
+  }
+}
+
+}  // namespace
+}  // namespace hv
+
+using namespace hv;
+
+extern "C" int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4,
+                            const float* psw, float* dst, int k8, int rows, int pair_ffn,
+                            int ntok, void* stream) {
+  HV_REQUIRE(a8 && sa && pb4 && psw && dst && k8 > 0 && rows > 0 && ntok > 0, HV_E_INVALID,
+             "hv_a4gemm_pp: bad arguments");
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_a4gemm_pp: a paired matrix has 2 * pair_ffn rows");
+  HV_REQUIRE(k8 % 32 == 0, HV_E_UNSUPPORTED,
+             "hv_a4gemm_pp: K = %d is not a multiple of 256 (whole 8-block iterations)", k8 * 8);
+  const int nb = k8 / 4;
+  HV_REQUIRE(nb <= kPfMaxBlocks, HV_E_UNSUPPORTED, "hv_a4gemm_pp: K = %d exceeds %d", k8 * 8,
+             kPfMaxBlocks * kBlock);
+  HV_REQUIRE(((uintptr_t)a8 & 15) == 0 && ((uintptr_t)sa & 15) == 0 &&
+                 ((uintptr_t)pb4 & 15) == 0 && ((uintptr_t)psw & 15) == 0,
+             HV_E_INVALID, "hv_a4gemm_pp: unaligned pointer");
+  GvPlan plan;
+  HV_REQUIRE(gv_make_plan(nb, &plan) && plan.ntail == 0, HV_E_UNSUPPORTED,
+             "hv_a4gemm_pp: no reduction plan for K");
+  int depth = 0, maxd = 0;
+  for (int l = 0; l < plan.nleaf; ++l) {
+    ++depth;
+    maxd = depth > maxd ? depth : maxd;
+    depth -= plan.pops[l];
+  }
+  HV_REQUIRE(maxd <= 8, HV_E_UNSUPPORTED, "hv_a4gemm_pp: reduction stack deeper than 8");
+  const int ntile = pp_tiles(rows, pair_ffn);
+  const dim3 grid((unsigned)((ntile + 3) / 4), (unsigned)((ntok + 31) / 32));
+  HV_REQUIRE(grid.y <= 65535u, HV_E_UNSUPPORTED, "hv_a4gemm_pp: %d tokens at once", ntok);
+  k_a4gemm_pp<<<grid, 256, 0, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, ntok, rows,
+                                                      pair_ffn, plan);
+  HV_LAUNCHED("k_a4gemm_pp");
+}

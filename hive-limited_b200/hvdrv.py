@@ -97,6 +97,7 @@ _SIGS = {
     "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_gemv_set_split": [_I],
+    "hv_a4gemm_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
     "hv_step_set_option": [_I, _I],
@@ -480,6 +481,12 @@ def wait_probe(word, mask, want, limit_ns, status, stream=0):
     *status becomes HV_E_TIMEOUT (1004) if (*word & mask) != want for limit_ns."""
     _call("hv_wait_probe", _p(word), int(mask), int(want), int(limit_ns), _p(status),
           _p(stream))
+
+
+def a4gemm_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok, stream=0):
+    """a4gv_pp for ntok tokens at once (prompt prefill); rows of dst are tokens."""
+    _call("hv_a4gemm_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
+          ntok, _p(stream))
 
 
 def gemv_set_split(enable: bool) -> None:

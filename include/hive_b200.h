@@ -134,6 +134,14 @@ int hv_w4_prepack(const uint32_t* b4, const float* sw, int rows, int k, int pair
  * bit. */
 int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
                float* dst, int k8, int rows, int pair_ffn, void* stream);
+/* Prompt prefill: the same GEMV for ntok tokens at once, dst [ntok][rows] (row order as
+ * hv_a4gv_pp, [gate | up] for a paired matrix). a8 [ntok][K] int8 and sa [ntok][2 K/32]
+ * hold each token's quant_a8s output (scales, then block sums), one row per token. Each
+ * token's row is bit-identical to hv_a4gv_pp on that token. K a multiple of 256, at most
+ * 32768. The reference has no batched path: it prefills through its decode step one
+ * token at a time (engine/limited.py:455-462). */
+int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+                 float* dst, int k8, int rows, int pair_ffn, int ntok, void* stream);
 /* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split
  * kernel, 0 runs every matrix on the one-warp-per-tile kernel. Process-wide. */
 int hv_gemv_set_split(int enable);

@@ -1,0 +1,51 @@
+"""The prefill GEMM (hv_a4gemm_pp) on a B200: every token's output row is bit-identical to
+hv_a4gv_pp on that token alone, and to the oracle's gemv_w4, for plain and gate/up-paired
+matrices, partial token groups and multi-leaf K."""
+import os
+
+import numpy as np
+import pytest
+
+import hv_oracle as O
+from gpu_util import Dev, bits
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(
+    not os.environ.get("HV_PREFILL_GPU_TESTS"),
+    reason="prefill kernels: set HV_PREFILL_GPU_TESTS=1 (not yet part of the default run)")]
+F32 = np.float32
+
+
+def quantize_rows(hv, x):
+    """quant_a8s per token: a8 [T][K], sa [T][2 K/32] (scales, then block sums)."""
+    t, k = x.shape
+    nb = k // 32
+    xd = Dev(x)
+    a8, sa = Dev(nbytes=t * k), Dev(nbytes=t * nb * 8)
+    for n in range(t):
+        hv.qa8s(xd.ptr + 4 * n * k, a8.ptr + n * k, sa.ptr + 8 * n * nb, nb)
+    return a8, sa
+
+
+@pytest.mark.parametrize("rows,k,pair,ntok", [(24, 512, 0, 11), (24, 256, 12, 8),
+                                              (2048, 6144, 0, 37), (6144, 4096, 0, 64),
+                                              (2 * 1536, 4096, 1536, 40), (100, 12288, 0, 5)])
+def test_prefill_gemm_rows_equal_per_token_gemv(hv, rows, k, pair, ntok):
+    g = np.random.default_rng(rows + k + ntok)
+    packed, scale = O.quantize_w4((g.standard_normal((rows, k)) * 0.02).astype(F32))
+    nib, scb = hv.w4_prepacked_size(rows, k, pair)
+    pb4, psw = Dev(nbytes=nib), Dev(nbytes=scb)
+    hv.w4_prepack(Dev(packed), Dev(scale), rows, k, pair, pb4, psw)
+    x = (g.standard_normal((ntok, k)) * 2).astype(F32)
+    a8, sa = quantize_rows(hv, x)
+    y = Dev(nbytes=ntok * rows * 4)
+    hv.a4gemm_pp(a8, sa, pb4, psw, y, k // 8, rows, pair, ntok)
+    got = y.get(F32, (ntok, rows))
+    one = Dev(nbytes=rows * 4)
+    nb = k // 32
+    for n in range(ntok):
+        hv.a4gv_pp(a8.ptr + n * k, sa.ptr + 8 * n * nb, pb4, psw, one, k // 8, rows, pair)
+        assert np.array_equal(bits(got[n]), bits(one.get(F32))), n
+    for n in (0, ntok - 1):
+        q, s, _ = O.quantize_act(x[n])
+        _, want = O.gemv_q_c(q, s, packed, scale, k)
+        assert np.array_equal(bits(got[n]), bits(want)), n
