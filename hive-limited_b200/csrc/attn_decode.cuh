@@ -59,6 +59,35 @@ HV_DEV float halving_reduce(float (&v)[V], int lane, int* idx) {
   return v[0];
 }
 
+// One warp: rmsnorm(raw[0..128), gain) then rotate-half RoPE with this position's tables,
+// bit-identical to k_rmsnorm (cols = 128) followed by k_rope.
+HV_DEV void warp_norm_rope(const float* raw, const float* __restrict__ gain,
+                           const float* __restrict__ cs, const float* __restrict__ sn,
+                           float eps, float* tmp, float* dst) {
+  const int lane = threadIdx.x & 31;
+  const float4 x = __ldcg(reinterpret_cast<const float4*>(raw) + lane);
+  tmp[4 * lane + 0] = __fmul_rn(x.x, x.x);
+  tmp[4 * lane + 1] = __fmul_rn(x.y, x.y);
+  tmp[4 * lane + 2] = __fmul_rn(x.z, x.z);
+  tmp[4 * lane + 3] = __fmul_rn(x.w, x.w);
+  __syncwarp();
+  const float ss = __fadd_rn(0.0f, pw_leaf8(tmp, kHd, lane & 7));
+  const float d = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHd), eps));
+  __syncwarp();
+  tmp[4 * lane + 0] = __fmul_rn(__ldg(gain + 4 * lane + 0), __fdiv_rn(x.x, d));
+  tmp[4 * lane + 1] = __fmul_rn(__ldg(gain + 4 * lane + 1), __fdiv_rn(x.y, d));
+  tmp[4 * lane + 2] = __fmul_rn(__ldg(gain + 4 * lane + 2), __fdiv_rn(x.z, d));
+  tmp[4 * lane + 3] = __fmul_rn(__ldg(gain + 4 * lane + 3), __fdiv_rn(x.w, d));
+  __syncwarp();
+  for (int i = lane; i < kHd / 2; i += 32) {
+    const float c = __ldg(cs + i), s = __ldg(sn + i);
+    const float lo = tmp[i], hi = tmp[kHd / 2 + i];
+    dst[i] = __fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s));
+    dst[kHd / 2 + i] = __fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s));
+  }
+  __syncwarp();
+}
+
 // Shared memory a work item needs (bytes), for `nwarps` warps.
 template <int GS>
 constexpr size_t attn_smem_bytes(int nwarps) {

@@ -607,7 +607,7 @@ extern "C" {
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
       "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp";
+      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp,k_gather_rows,k_qa8s_rows,k_qk_rows,k_attn_rows,k_silu_rows";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;

@@ -23,6 +23,9 @@
 //
 // A CTA is 8 warps: 2 tile pairs (32 weight rows) x 4 token groups (32 tokens). No CTA
 // barrier: warps of the same tile pair share the weights through L1.
+#include <cuda_fp16.h>
+
+#include "attn_decode.cuh"
 #include "gemv_mma.cuh"
 #include "hv_internal.h"
 
@@ -136,10 +139,245 @@ __global__ void __launch_bounds__(256) k_a4gemm_pp(const int8_t* __restrict__ a8
   }
 }
 
+// ---- the per-token steps around the GEMMs, for a run of prompt tokens ----------------
+//
+// Each kernel applies to every row (token) exactly the arithmetic of the one-token kernel
+// the eager step uses, so a batched prefill reproduces the eager per-token prefill bit
+// for bit.
+
+// h[t] = f32(emb16[tok[t]]) (gather_emb per token).
+__global__ void k_gather_rows(const __half* __restrict__ emb, const int32_t* __restrict__ tok,
+                              float* __restrict__ h, int hid) {
+  const int t = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < hid) h[(size_t)t * hid + i] = __half2float(emb[(size_t)tok[t] * hid + i]);
+}
+
+// quant_a8s per row: one warp per (row, 32-block); row t's scales and block sums go to
+// sa[t][0 .. nb) and sa[t][nb .. 2 nb).
+__global__ void __launch_bounds__(256) k_qa8s_rows(const float* __restrict__ src,
+                                                   int8_t* __restrict__ a8,
+                                                   float* __restrict__ sa, int nb, int ntok) {
+  const long long wi = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wi >= (long long)ntok * nb) return;                 // whole warps
+  const int t = (int)(wi / nb), b = (int)(wi % nb);
+  const size_t e = ((size_t)t * nb + b) * kBlock + lane;
+  int8_t q;
+  float s;
+  int bs;
+  quant_block_warp(src[e], lane, &q, &s, &bs);
+  a8[e] = q;
+  if (lane == 0) {
+    sa[(size_t)t * 2 * nb + b] = s;
+    sa[(size_t)t * 2 * nb + nb + b] = __int_as_float(bs);
+  }
+}
+
+// q/k RMSNorm and RoPE at position pos0 + t, K and V rows appended to the cache: one warp
+// per (token, head) over the nq query heads and the nkv key heads (whose warp also
+// copies the head's V row). qkv rows are [q | k | v] as the qkv projection writes them.
+__global__ void __launch_bounds__(256) k_qk_rows(const float* __restrict__ qkv,
+                                                 const float* __restrict__ qn,
+                                                 const float* __restrict__ kn,
+                                                 const float* __restrict__ cos_t,
+                                                 const float* __restrict__ sin_t, int pos0,
+                                                 float* __restrict__ q_out, float* kc,
+                                                 float* vc, int nq, int nkv, int cap,
+                                                 float eps, int ntok) {
+  __shared__ __align__(16) float tmp[8][kHd];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = nq + nkv;
+  const long long wi = (long long)blockIdx.x * 8 + warp;
+  if (wi >= (long long)ntok * heads) return;              // whole warps
+  const int t = (int)(wi / heads), h = (int)(wi % heads);
+  const int pos = pos0 + t;
+  const float* row = qkv + (size_t)t * (nq + 2 * nkv) * kHd;
+  const float* cs = cos_t + (size_t)pos * (kHd / 2);
+  const float* sn = sin_t + (size_t)pos * (kHd / 2);
+  if (h < nq) {
+    warp_norm_rope(row + (size_t)h * kHd, qn, cs, sn, eps, tmp[warp],
+                   q_out + ((size_t)t * nq + h) * kHd);
+  } else {
+    const int g = h - nq;
+    warp_norm_rope(row + (size_t)(nq + g) * kHd, kn, cs, sn, eps, tmp[warp],
+                   kc + ((size_t)g * cap + pos) * kHd);
+    reinterpret_cast<float4*>(vc + ((size_t)g * cap + pos) * kHd)[lane] =
+        reinterpret_cast<const float4*>(row + (size_t)(nq + nkv + g) * kHd)[lane];
+  }
+}
+
+// The eager step's split-sequence attention (k_attn) for a run of query tokens: token t
+// attends positions 0 .. pos0 + t with the same chunking (nch) and merge, so its ctx row
+// is what hv_attn_decode gives at that position. Grid (nkv * nch, ntok); per-token
+// partials and tickets in caller scratch (tickets zero; each merge re-zeroes its own).
+template <int GS>
+__global__ void __launch_bounds__(256) k_attn_rows(const float* __restrict__ q,
+                                                   const float* __restrict__ kc,
+                                                   const float* __restrict__ vc,
+                                                   float* __restrict__ ctx,
+                                                   const float* __restrict__ scale_p, int pos0,
+                                                   int cap, int nch, int nq,
+                                                   float* __restrict__ part,
+                                                   int* __restrict__ ticket) {
+  extern __shared__ __align__(16) float fsm[];
+  const int nw = blockDim.x >> 5;
+  float* q_s = fsm;
+  float* lg_s = q_s + GS * kHd;
+  float* red_s = lg_s + kAttnChunkMax * GS;
+  float* stat_s = red_s + nw * GS * kHd;
+  __shared__ int last;
+  const int nkv = nq / GS;
+  const int t = blockIdx.y;
+  const int g = blockIdx.x / nch, c = blockIdx.x % nch;
+  const int pos = pos0 + t;
+  const float* qt = q + (size_t)t * nq * kHd + (size_t)g * GS * kHd;
+  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) q_s[e] = qt[e];
+  __syncthreads();
+  int t0, t1;
+  chunk_bounds(pos + 1, nch, c, &t0, &t1);
+  float* part_t = part + (size_t)t * nkv * nch * GS * kPartStride;
+  attn_chunk<GS>(q_s, kc + (size_t)g * cap * kHd, vc + (size_t)g * cap * kHd, t0, t1,
+                 *scale_p, pos, nullptr, nullptr, lg_s, red_s, stat_s,
+                 part_t + ((size_t)g * nch + c) * GS * kPartStride);
+  __threadfence();
+  __syncthreads();
+  int* tk = ticket + (size_t)t * nkv + g;
+  if (threadIdx.x == 0) last = (atomicAdd(tk, 1) == nch - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  attn_merge<GS>(part_t + (size_t)g * nch * GS * kPartStride, nch,
+                 ctx + (size_t)t * nq * kHd + (size_t)g * GS * kHd, red_s);
+  if (threadIdx.x == 0) *tk = 0;
+}
+
+// act[t] = silu(gate[t]) * up[t] for rows [gate | up] of 2 ffn values (gpu_silu_mul).
+__global__ void k_silu_rows(const float* __restrict__ gu, float* __restrict__ act, int ffn) {
+  const int t = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < ffn)
+    act[(size_t)t * ffn + i] = silu_mul1(gu[(size_t)t * 2 * ffn + i],
+                                         gu[(size_t)t * 2 * ffn + ffn + i]);
+}
+
+// The chunk count hv_attn_decode uses for (nkv, cap), so both split alike.
+int rows_attn_chunks(int nkv, int cap, int* out) {
+  int sms = 0;
+  const int rc = sm_count(&sms);
+  if (rc) return rc;
+  const int nch = (sms + nkv - 1) / nkv;
+  const int need = (cap + kAttnChunkMax - 1) / kAttnChunkMax;
+  *out = nch > need ? nch : need;
+  return HV_OK;
+}
+
+template <int GS>
+int launch_attn_rows(const float* q, const float* kc, const float* vc, float* ctx,
+                     const float* scale, int pos0, int cap, int nch, int nq, int ntok,
+                     float* part, int* ticket, cudaStream_t st) {
+  const size_t smem = attn_smem_bytes<GS>(8);
+  HV_CUDA(cudaFuncSetAttribute((const void*)k_attn_rows<GS>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const dim3 grid((unsigned)(nq / GS * nch), (unsigned)ntok);
+  k_attn_rows<GS><<<grid, 256, smem, st>>>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, part,
+                                           ticket);
+  HV_LAUNCHED("k_attn_rows");
+}
+
 }  // namespace
 }  // namespace hv
 
 using namespace hv;
+
+extern "C" int hv_gather_rows(const uint16_t* emb16, const int32_t* tok, float* h, int hid,
+                              int ntok, void* stream) {
+  HV_REQUIRE(emb16 && tok && h && hid > 0 && ntok > 0 && ntok <= 65535, HV_E_INVALID,
+             "hv_gather_rows: bad arguments");
+  k_gather_rows<<<dim3((unsigned)((hid + 255) / 256), (unsigned)ntok), 256, 0,
+                  (cudaStream_t)stream>>>(reinterpret_cast<const __half*>(emb16), tok, h, hid);
+  HV_LAUNCHED("k_gather_rows");
+}
+
+extern "C" int hv_qa8s_rows(const float* src, int8_t* a8, float* sa, int nb, int ntok,
+                            void* stream) {
+  HV_REQUIRE(src && a8 && sa && nb > 0 && ntok > 0, HV_E_INVALID, "hv_qa8s_rows: bad arguments");
+  const long long warps = (long long)nb * ntok;
+  HV_REQUIRE((warps + 7) / 8 <= 0x7FFFFFFFll, HV_E_UNSUPPORTED, "hv_qa8s_rows: too many rows");
+  k_qa8s_rows<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(src, a8, sa, nb,
+                                                                              ntok);
+  HV_LAUNCHED("k_qa8s_rows");
+}
+
+extern "C" int hv_qk_rows(const float* qkv, const float* qn, const float* kn,
+                          const float* cos_t, const float* sin_t, int pos0, float* q_out,
+                          float* kc, float* vc, int nq, int nkv, int hd, int cap, float eps,
+                          int ntok, void* stream) {
+  HV_REQUIRE(qkv && qn && kn && cos_t && sin_t && q_out && kc && vc && nq > 0 && nkv > 0 &&
+                 ntok > 0 && pos0 >= 0,
+             HV_E_INVALID, "hv_qk_rows: bad arguments");
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_qk_rows: head_dim %d (only 128)", hd);
+  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
+             "hv_qk_rows: positions %d .. %d outside the cache of %d", pos0, pos0 + ntok - 1, cap);
+  HV_REQUIRE(((uintptr_t)qkv & 15) == 0 && ((uintptr_t)kc & 15) == 0 &&
+                 ((uintptr_t)vc & 15) == 0,
+             HV_E_INVALID, "hv_qk_rows: unaligned pointer");
+  const long long warps = (long long)(nq + nkv) * ntok;
+  k_qk_rows<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, cap, eps, ntok);
+  HV_LAUNCHED("k_qk_rows");
+}
+
+extern "C" int hv_attn_rows_scratch(int nq, int group, int cap, int ntok, size_t* part_bytes,
+                                    size_t* ticket_bytes) {
+  HV_REQUIRE(nq > 0 && group > 0 && nq % group == 0 && cap > 0 && ntok > 0 && part_bytes &&
+                 ticket_bytes,
+             HV_E_INVALID, "hv_attn_rows_scratch: bad arguments");
+  int nch = 0;
+  const int rc = rows_attn_chunks(nq / group, cap, &nch);
+  if (rc) return rc;
+  *part_bytes = (size_t)ntok * nq * nch * kPartStride * sizeof(float);
+  *ticket_bytes = (size_t)ntok * (nq / group) * sizeof(int);
+  return HV_OK;
+}
+
+extern "C" int hv_attn_rows(const float* q, const float* kc, const float* vc, float* ctx,
+                            const float* scale, int pos0, int nq, int hd, int group,
+                            int kvstride, int ntok, float* part, int32_t* ticket,
+                            void* stream) {
+  HV_REQUIRE(q && kc && vc && ctx && scale && part && ticket && nq > 0 && group > 0 &&
+                 ntok > 0 && ntok <= 65535 && pos0 >= 0,
+             HV_E_INVALID, "hv_attn_rows: bad arguments");
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_attn_rows: head_dim %d (only 128)", hd);
+  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
+             "hv_attn_rows: nq %% group or kvstride %% hd is not zero");
+  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
+             "hv_attn_rows: group size %d (1, 2, 4 or 8)", group);
+  const int cap = kvstride / hd;
+  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
+             "hv_attn_rows: positions %d .. %d outside the cache of %d", pos0, pos0 + ntok - 1, cap);
+  int nch = 0;
+  const int rc = rows_attn_chunks(nq / group, cap, &nch);
+  if (rc) return rc;
+  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
+             "hv_attn_rows: %d chunks per kv head (at most %d)", nch, kAttnMaxChunks);
+  cudaStream_t st = (cudaStream_t)stream;
+  int* tk = reinterpret_cast<int*>(ticket);
+  switch (group) {
+    case 1: return launch_attn_rows<1>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    case 2: return launch_attn_rows<2>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    case 4: return launch_attn_rows<4>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    default: return launch_attn_rows<8>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+  }
+}
+
+extern "C" int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void* stream) {
+  HV_REQUIRE(gu && act && ffn > 0 && ntok > 0 && ntok <= 65535, HV_E_INVALID,
+             "hv_silu_rows: bad arguments");
+  k_silu_rows<<<dim3((unsigned)((ffn + 255) / 256), (unsigned)ntok), 256, 0,
+                (cudaStream_t)stream>>>(gu, act, ffn);
+  HV_LAUNCHED("k_silu_rows");
+}
 
 extern "C" int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4,
                             const float* psw, float* dst, int k8, int rows, int pair_ffn,

@@ -98,6 +98,12 @@ _SIGS = {
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_gemv_set_split": [_I],
     "hv_a4gemm_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
+    "hv_gather_rows": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_qa8s_rows": [_VP, _VP, _VP, _I, _I, _VP],
+    "hv_qk_rows": [_VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP],
+    "hv_attn_rows_scratch": [_I, _I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
+    "hv_attn_rows": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP, _VP],
+    "hv_silu_rows": [_VP, _VP, _I, _I, _VP],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
     "hv_step_set_option": [_I, _I],
@@ -487,6 +493,36 @@ def a4gemm_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok, stream=0):
     """a4gv_pp for ntok tokens at once (prompt prefill); rows of dst are tokens."""
     _call("hv_a4gemm_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
           ntok, _p(stream))
+
+
+def gather_rows(emb16, tok, h, hid, ntok, stream=0):
+    _call("hv_gather_rows", _p(emb16), _p(tok), _p(h), hid, ntok, _p(stream))
+
+
+def qa8s_rows(src, a8, sa, nb, ntok, stream=0):
+    _call("hv_qa8s_rows", _p(src), _p(a8), _p(sa), nb, ntok, _p(stream))
+
+
+def qk_rows(qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, hd, cap, eps, ntok,
+            stream=0):
+    _call("hv_qk_rows", _p(qkv), _p(qn), _p(kn), _p(cos_t), _p(sin_t), int(pos0), _p(q_out),
+          _p(kc), _p(vc), nq, nkv, hd, cap, C.c_float(eps), ntok, _p(stream))
+
+
+def attn_rows_scratch(nq, group, cap, ntok) -> tuple[int, int]:
+    a, b = C.c_size_t(), C.c_size_t()
+    _call("hv_attn_rows_scratch", nq, group, cap, ntok, C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def attn_rows(q, kc, vc, ctx, scale, pos0, nq, hd, group, kvstride, ntok, part, ticket,
+              stream=0):
+    _call("hv_attn_rows", _p(q), _p(kc), _p(vc), _p(ctx), _p(scale), int(pos0), nq, hd, group,
+          kvstride, ntok, _p(part), _p(ticket), _p(stream))
+
+
+def silu_rows(gu, act, ffn, ntok, stream=0):
+    _call("hv_silu_rows", _p(gu), _p(act), ffn, ntok, _p(stream))
 
 
 def gemv_set_split(enable: bool) -> None:

@@ -142,6 +142,34 @@ int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const flo
  * token at a time (engine/limited.py:455-462). */
 int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
                  float* dst, int k8, int rows, int pair_ffn, int ntok, void* stream);
+/* The per-token steps of a batched prompt prefill, for ntok tokens (rows) at once. Each
+ * applies to every row the arithmetic of the one-token kernel the eager step uses
+ * (engine/limited.py:374-419), so a prefill built from them equals the token-by-token
+ * prefill bit for bit:
+ *   hv_gather_rows  h[t] = f32(emb16[tok[t]])                          (gather_emb)
+ *   hv_qa8s_rows    quant_a8s of each row of src [ntok][nb*32]; sa row t = (scales,
+ *                   block sums) [2 nb]                                   (quant_a8s)
+ *   hv_qk_rows      q/k RMSNorm (eps) + RoPE at position pos0 + t of the qkv rows
+ *                   [ntok][(nq + 2 nkv) hd]; q heads to q_out [ntok][nq][hd], k and v
+ *                   rows appended at pos0 + t of the f32 cache [nkv][cap][hd]
+ *                                                     (rmsnorm_bp, rope_pos, kvapp_pos)
+ *   hv_attn_rows    attention of query row t over positions 0 .. pos0 + t, with the
+ *                   chunking and merge of hv_attn_decode at that position; part/ticket
+ *                   are caller scratch of hv_attn_rows_scratch's sizes (tickets zeroed
+ *                   once; every call leaves them zero)                (fda_warp_pos)
+ *   hv_silu_rows    act[t] = silu(gate[t]) * up[t] from [gate | up] rows (gpu_silu_mul) */
+int hv_gather_rows(const uint16_t* emb16, const int32_t* tok, float* h, int hid, int ntok,
+                   void* stream);
+int hv_qa8s_rows(const float* src, int8_t* a8, float* sa, int nb, int ntok, void* stream);
+int hv_qk_rows(const float* qkv, const float* qn, const float* kn, const float* cos_t,
+               const float* sin_t, int pos0, float* q_out, float* kc, float* vc, int nq,
+               int nkv, int hd, int cap, float eps, int ntok, void* stream);
+int hv_attn_rows_scratch(int nq, int group, int cap, int ntok, size_t* part_bytes,
+                         size_t* ticket_bytes);
+int hv_attn_rows(const float* q, const float* kc, const float* vc, float* ctx,
+                 const float* scale, int pos0, int nq, int hd, int group, int kvstride,
+                 int ntok, float* part, int32_t* ticket, void* stream);
+int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void* stream);
 /* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split
  * kernel, 0 runs every matrix on the one-warp-per-tile kernel. Process-wide. */
 int hv_gemv_set_split(int enable);
