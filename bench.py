@@ -284,7 +284,7 @@ def run_ours(args, dist: Dist):
                          max_context=cap, device=dist.local, fused=True,
                          world=dist.world if sharded else 1, rank=dist.rank if sharded else 0,
                          exchange=dist.allgather_bytes if sharded else None,
-                         weight_cache=args.weight_cache,
+                         weight_cache=args.weight_cache, prefill=args.prefill,
                          cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
@@ -400,6 +400,7 @@ def run_ours(args, dist: Dist):
             "gpu_launches": args.steps,
             "clocks": clk,
             "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
+            "prefill": args.prefill,
             "weight_cache": {None: None, True: "hit", False: "miss"}[eng.cache_hit],
         }
         print(json.dumps(line), flush=True)
@@ -513,6 +514,9 @@ def main(argv=None):
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
+    ap.add_argument("--prefill", default="steps", choices=["steps", "batched"],
+                    help="how the prompt is prefilled before the timed decode: through the "
+                         "decode step token by token (as the reference), or in batches")
     ap.add_argument("--weight-cache", default=None, metavar="DIR",
                     help="load device-ready weights from DIR when present, else quantise "
                          "and write them there (the timed steps are the same either way)")

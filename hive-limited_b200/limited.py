@@ -125,6 +125,11 @@ class Engine:
                            heads; `exchange(bytes) -> list[bytes]` is an all-gather over the
                            ranks (any transport) used once, to swap the CUDA IPC handles of
                            the buffers the fused step writes into on every rank;
+      prefill           -- "steps" (default): the prompt runs through the decode step one
+                           token at a time, as the reference does; "batched": runs of
+                           PREFILL_BATCH tokens go through each layer at once (GEMMs over
+                           the prepacked weights, hv_*_rows kernels), with results
+                           bit-identical to the eager token-by-token prefill (one GPU);
       weight_cache / cache_tag
                         -- a directory of device-ready weights (wcache.py): on a hit the
                            engine uploads the cached prepacked int4 weights, embedding and
@@ -137,7 +142,7 @@ class Engine:
     def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
                  config=None, tensors=None, max_context=None, device=0, fused=True,
                  quantize_on="device", world=1, rank=0, exchange=None, weight_cache=None,
-                 cache_tag=None):
+                 cache_tag=None, prefill="steps"):
         if config is None:
             self.cfg = Config.load(model_dir)
         else:
@@ -149,6 +154,12 @@ class Engine:
         self._buffers: list[int] = []
         self._opened: list[int] = []
         self.world, self.rank = int(world), int(rank)
+        if prefill not in ("steps", "batched"):
+            raise ValueError(f"prefill={prefill!r}: 'steps' or 'batched'")
+        if prefill == "batched" and self.world > 1:
+            raise ValueError("the batched prefill runs on one GPU (world = 1)")
+        self.prefill_mode = prefill
+        self._pf = None
         self.shard = shard_plan(self.cfg, self.world, self.rank)
         if self.world > 1 and (not self.fused or exchange is None):
             raise ValueError("a sharded engine runs the fused step and needs `exchange`")
@@ -665,11 +676,92 @@ class Engine:
                 "context of this engine")
 
     def _prefill(self, prompt_ids, last_flags=STEP_HEAD | STEP_ARGMAX):
+        if self.prefill_mode == "batched":
+            self._prefill_batched(prompt_ids, argmax=bool(last_flags & STEP_ARGMAX))
+            return
         self._set_i32(self.d_step, 0)
         hvdrv.memset8(self.d_gen, 0, (self.cfg.max_context + 1) * 4)
         n = len(prompt_ids)
         for i, tok in enumerate(prompt_ids):
             self._prefill_token(tok, i, last_flags if i == n - 1 else None)
+
+    # ---- batched prefill --------------------------------------------------------------
+
+    PREFILL_BATCH = 256      # prompt tokens that go through a layer together
+
+    def _prefill_buffers(self) -> dict:
+        """Device buffers of one run of PREFILL_BATCH tokens (allocated on first use)."""
+        if self._pf is not None:
+            return self._pf
+        c = self.cfg
+        b, hid, ffn, qd, nq, nkv = (self.PREFILL_BATCH, c.hidden, c.ffn, c.head_dim, c.n_head,
+                                    c.n_kv)
+        wide = max(hid, ffn, nq * qd)
+        part_b, ticket_b = hvdrv.attn_rows_scratch(nq, c.group, c.max_context, b)
+        pf = {"n": b, "tok": self._alloc(b * 4), "h": self._alloc(b * hid * 4),
+              "hn": self._alloc(b * hid * 4), "a8": self._alloc(b * wide),
+              "sa": self._alloc(b * 2 * (wide // BLOCK) * 4),
+              "qkv": self._alloc(b * (nq + 2 * nkv) * qd * 4), "q": self._alloc(b * nq * qd * 4),
+              "ctx": self._alloc(b * nq * qd * 4), "o": self._alloc(b * hid * 4),
+              "gu": self._alloc(b * 2 * ffn * 4), "act": self._alloc(b * ffn * 4),
+              "part": self._alloc(part_b), "ticket": self._alloc(ticket_b)}
+        hvdrv.memset8(pf["ticket"], 0, ticket_b)
+        self._pf = pf
+        return pf
+
+    def _gemm(self, src, w4, dst, m: int):
+        """quant_a8s per row, then the W4A8 GEMM of m tokens (rows of src and dst)."""
+        pb4, psw, k, n, pair = w4
+        s, pf = self._stream_cur, self._pf
+        hvdrv.qa8s_rows(src, pf["a8"], pf["sa"], k // BLOCK, m, s)
+        hvdrv.a4gemm_pp(pf["a8"], pf["sa"], pb4, psw, dst, k // 8, n, pair, m, s)
+
+    def _prefill_batched(self, prompt_ids, argmax: bool):
+        """The prompt through every layer PREFILL_BATCH tokens at a time: per token the
+        arithmetic of the eager step (engine/limited.py:374-419), so the KV cache and the
+        last token's logits equal the token-by-token prefill's bit for bit. Leaves the
+        state the token-by-token prefill leaves: logits of the last prompt token, tok and
+        pos at it, step 0 -- then, with `argmax`, the first greedy token taken as the
+        fused step's last prompt launch does (gen[0], step 1, pos = prompt length)."""
+        c = self.cfg
+        hid, ffn, qd, nq, nkv, cap = (c.hidden, c.ffn, c.head_dim, c.n_head, c.n_kv,
+                                      c.max_context)
+        toks = np.ascontiguousarray(prompt_ids, np.int32)
+        n = toks.size
+        if n == 0 or n > cap:
+            raise ValueError(f"{n} prompt tokens for a {cap}-token context")
+        pf = self._prefill_buffers()
+        s = self._stream_cur
+        self._set_i32(self.d_step, 0)
+        hvdrv.memset8(self.d_gen, 0, (cap + 1) * 4)
+        m = 0
+        for b0 in range(0, n, pf["n"]):
+            m = min(pf["n"], n - b0)
+            hvdrv.synchronize()                 # the host copy below reuses pf["tok"]
+            hvdrv.upload(pf["tok"], toks[b0:b0 + m].ctypes.data, 4 * m)
+            hvdrv.gather_rows(self.d_emb16, pf["tok"], pf["h"], hid, m, s)
+            for l, w in enumerate(self.layers):
+                hvdrv.rmsnorm(pf["h"], pf["hn"], w["an"], m, hid, RMS_EPS, s)
+                self._gemm(pf["hn"], w["qkv"], pf["qkv"], m)
+                hvdrv.qk_rows(pf["qkv"], w["qn"], w["kn"], self.d_cos, self.d_sin, b0, pf["q"],
+                              self.KC[l], self.VC[l], nq, nkv, qd, cap, RMS_EPS, m, s)
+                hvdrv.attn_rows(pf["q"], self.KC[l], self.VC[l], pf["ctx"], self.d_scale, b0,
+                                nq, qd, c.group, cap * qd, m, pf["part"], pf["ticket"], s)
+                self._gemm(pf["ctx"], w["o"], pf["o"], m)
+                hvdrv.vadd(pf["h"], pf["o"], pf["h"], m * hid, s)
+                hvdrv.rmsnorm(pf["h"], pf["hn"], w["fn"], m, hid, RMS_EPS, s)
+                self._gemm(pf["hn"], w["gu"], pf["gu"], m)
+                hvdrv.silu_rows(pf["gu"], pf["act"], ffn, m, s)
+                self._gemm(pf["act"], w["down"], pf["o"], m)
+                hvdrv.vadd(pf["h"], pf["o"], pf["h"], m * hid, s)
+        # the last prompt token: final norm and LM head, as the eager step ends
+        hvdrv.copy_async(self.d_h, pf["h"] + (m - 1) * hid * 4, hid * 4, s)
+        hvdrv.rmsnorm(self.d_h, self.d_hn, self.d_onorm, 1, hid, RMS_EPS, s)
+        self._gemv(self.d_hn, self.head, self.d_logits)
+        self._set_i32(self.d_tok, int(toks[-1]))
+        self._set_i32(self.d_pos, n - 1)
+        if argmax and self.fused:
+            self._argmax_into_next()
 
     def _token(self, i: int) -> int:
         """Token i of the current generation, once decode iteration i has run."""
@@ -818,8 +910,11 @@ class Engine:
     def logits(self, prompt_ids) -> np.ndarray:
         """Run the prompt and return the final f32 logits."""
         n = len(prompt_ids)
-        for i, tok in enumerate(prompt_ids):
-            self._prefill_token(tok, i, STEP_HEAD if i == n - 1 else None)
+        if self.prefill_mode == "batched":
+            self._prefill_batched(prompt_ids, argmax=False)
+        else:
+            for i, tok in enumerate(prompt_ids):
+                self._prefill_token(tok, i, STEP_HEAD if i == n - 1 else None)
         hvdrv.synchronize()
         if self.fused:
             self._check_status()

@@ -49,3 +49,34 @@ def test_prefill_gemm_rows_equal_per_token_gemv(hv, rows, k, pair, ntok):
         q, s, _ = O.quantize_act(x[n])
         _, want = O.gemv_q_c(q, s, packed, scale, k)
         assert np.array_equal(bits(got[n]), bits(want)), n
+
+
+TINY = dict(n_layer=2, hidden=512, ffn=1024, n_head=8, n_kv=2, vocab=4096)
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_batched_prefill_equals_token_by_token(hv, fused):
+    """A 300-token prompt (two runs of the 256-token batch) prefilled in batches leaves the
+    same KV cache and last-token logits as the token-by-token prefill, and greedy decoding
+    from it gives the same tokens."""
+    import limited
+    import synth
+    from w4format import Config
+    cfg = Config(synth.tiny_arch(**TINY))
+    prompt = synth.prompt_ids(cfg, 11, 300)
+    out = {}
+    for mode in ("steps", "batched"):
+        eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, 11), quiet=True,
+                             max_context=512, fused=fused, prefill=mode)
+        try:
+            lg = eng.logits(prompt)
+            kv = np.empty(eng.kv_bytes // 4, F32)
+            hv.download(kv.ctypes.data, eng.d_kv, kv.nbytes)
+            toks, _, _ = eng.generate(prompt, max_new=8)
+            out[mode] = (lg, kv[kv != 0].copy(), toks)
+        finally:
+            eng.free()
+    (lg0, kv0, t0), (lg1, kv1, t1) = out["steps"], out["batched"]
+    assert np.array_equal(bits(kv0), bits(kv1))
+    assert np.array_equal(bits(lg0), bits(lg1))
+    assert t0 == t1

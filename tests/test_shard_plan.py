@@ -43,3 +43,12 @@ def test_sharded_engine_arguments_are_checked_before_any_device_work():
                        exchange=lambda b: [b, b])
     with pytest.raises(ValueError):       # the IPC handle swap needs a transport
         limited.Engine(config=cfg, tensors={}, world=2, rank=1)
+
+
+def test_prefill_mode_is_checked_before_any_device_work():
+    cfg = Config(synth.tiny_arch())
+    with pytest.raises(ValueError, match="prefill"):
+        limited.Engine(config=cfg, tensors={}, prefill="bulk")
+    with pytest.raises(ValueError, match="one GPU"):
+        limited.Engine(config=cfg, tensors={}, world=2, rank=0, exchange=lambda b: [b, b],
+                       prefill="batched")
