@@ -499,6 +499,65 @@ def run_gemv_sweep(args, dist: Dist):
     return 0
 
 
+def run_prefill_sweep(args, dist: Dist):
+    """The prefill GEMM (hv_a4gemm_pp) on the 8B layer shapes for a run of
+    `--prefill-tokens` tokens: device time per GEMM (CUDA events over `--gemv-reps`
+    launches), prompt tokens per second through that matrix, the int8 MMA rate it
+    sustains (2 * N * K * T ops per launch) and the weight bytes it reads per token.
+    One JSON line per shape."""
+    if dist.rank != 0:
+        return 0
+    import hvdrv
+    hvdrv.init()
+    e0, e1 = hvdrv.event_create(), hvdrv.event_create()
+    ntok = args.prefill_tokens
+    cfg = w4format.Config(synth.ARCH["qwen3-8b"])
+    hid, ffn, qd = cfg.hidden, cfg.ffn, cfg.head_dim
+    shapes = [("qkv", (cfg.n_head + 2 * cfg.n_kv) * qd, hid, 0),
+              ("o", hid, cfg.n_head * qd, 0), ("gate_up", 2 * ffn, hid, ffn),
+              ("down", hid, ffn, 0)]
+    g = np.random.default_rng(9)
+    for name, n, k, pair in shapes:
+        bufs = []
+
+        def dev(nbytes):
+            ptr = hvdrv.alloc(nbytes)
+            bufs.append(ptr)
+            return ptr
+
+        packed = g.integers(0, 2**32, (n, k // 8), dtype=np.uint32)
+        scale = (g.random((n, k // 32), dtype=np.float32) * 0.01 + 1e-3).astype(F32)
+        b4, sw = dev(packed.nbytes), dev(scale.nbytes)
+        hvdrv.upload(b4, packed.ctypes.data, packed.nbytes)
+        hvdrv.upload(sw, scale.ctypes.data, scale.nbytes)
+        nib, scb = hvdrv.w4_prepacked_size(n, k, pair)
+        pb4, psw = dev(nib), dev(scb)
+        hvdrv.w4_prepack(b4, sw, n, k, pair, pb4, psw)
+        x = g.standard_normal((ntok, k), dtype=np.float32)
+        xd, a8, sa, y = dev(x.nbytes), dev(ntok * k), dev(ntok * (k // 32) * 8), dev(ntok * n * 4)
+        hvdrv.upload(xd, x.ctypes.data, x.nbytes)
+        hvdrv.qa8s_rows(xd, a8, sa, k // 32, ntok)
+        for _ in range(3):
+            hvdrv.a4gemm_pp(a8, sa, pb4, psw, y, k // 8, n, pair, ntok)
+        hvdrv.synchronize()
+        hvdrv.event_record(e0, 0)
+        for _ in range(args.gemv_reps):
+            hvdrv.a4gemm_pp(a8, sa, pb4, psw, y, k // 8, n, pair, ntok)
+        hvdrv.event_record(e1, 0)
+        hvdrv.synchronize()
+        us = hvdrv.event_elapsed_ms(e0, e1) * 1e3 / args.gemv_reps
+        print(json.dumps({
+            "metric": "W4A8 prefill GEMM", "workload": "prefill-gemm",
+            "matrix": name, "shape": [n, k], "tokens": ntok, "kernel": "k_a4gemm_pp",
+            "us_per_launch": us, "tokens_per_s": ntok / (us * 1e-6),
+            "int8_tops": 2.0 * n * k * ntok / (us * 1e-6) / 1e12,
+            "weight_bytes_per_token": n * k * 5 / 8 / ntok, "launches": args.gemv_reps}),
+            flush=True)
+        for ptr in bufs:
+            hvdrv.free(ptr)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -523,6 +582,10 @@ def main(argv=None):
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="instead of the decode step: the isolated GEMV sweep, one JSON line "
                          "per shape and kernel")
+    ap.add_argument("--prefill-sweep", action="store_true",
+                    help="instead of the decode step: the prefill GEMM on the 8B layer "
+                         "shapes, one JSON line per matrix")
+    ap.add_argument("--prefill-tokens", type=int, default=256)
     ap.add_argument("--gemv-reps", type=int, default=300)
     ap.add_argument("--gemv-max-rows", type=int, default=0,
                     help="sweep only the shapes with at most this many rows (0: all)")
@@ -534,6 +597,8 @@ def main(argv=None):
     try:
         if args.gemv_sweep:
             return run_gemv_sweep(args, dist)
+        if args.prefill_sweep:
+            return run_prefill_sweep(args, dist)
         if args.impl == "reference":
             return run_reference(args, dist)
         return run_ours(args, dist)
