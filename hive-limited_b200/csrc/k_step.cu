@@ -67,6 +67,10 @@ static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention 
 // only queue in front of the consumers' own (latency-critical) loads.
 static int g_opt_inflight = 6;
 static int g_opt_evict_first = 1;
+static int g_opt_local_qkv_barrier = 0;
+// Launch flag set by the library (not by callers): the barrier after the qkv projection
+// of a sharded step stays among the rank's own CTAs.
+constexpr int kFlagLocalQkvBarrier = 1 << 8;
 
 using CSync = SyncNamed<kConsThreads, 1>;
 HV_DEV void csync() { CSync::sync(); }
@@ -252,14 +256,17 @@ HV_DEV bool poll_word(const unsigned* w, unsigned mask, unsigned want, int* stat
 // fences its peer stores at system scope before it arrives. Waits are bounded (kWaitNs,
 // or until a failure is reported on this rank, or this CTA aborted): the failure is
 // recorded and every consumer thread gets false.
-HV_DEV bool grid_sync(const hv_step_desc& D, StepShared& S) {
+// `cross` false: a sharded step's barrier among this rank's CTAs only, for a phase whose
+// consumers read nothing the other ranks wrote (attention after the qkv projection: each
+// rank owns its heads).
+HV_DEV bool grid_sync(const hv_step_desc& D, StepShared& S, bool cross = true) {
   csync();
   if (threadIdx.x == 0) {
     int ok = *(volatile int*)&S.abort == 0;
     if (ok) {
       const unsigned add = (blockIdx.x == 0) ? (0x80000000u - (gridDim.x - 1)) : 1u;
       const unsigned want = S.phase ^ 0x80000000u;
-      if (D.world <= 1) {
+      if (D.world <= 1 || !cross) {
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(D.barrier), "r"(add)
                      : "memory");
         ok = poll_word<false>(D.barrier, 0x80000000u, want, D.status);
@@ -1253,7 +1260,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
     trace_wait(D, S, tb + 23);
-    if (!grid_sync(D, S)) return;
+    if (!grid_sync(D, S, (flags & kFlagLocalQkvBarrier) == 0)) return;
     trace_mark(D, tb + 2);
     // P2: attention
     attn_ring<GS>(D, L, pos, R, &q, S, work, tb);
@@ -1446,6 +1453,9 @@ int hv_step_set_option(int option, int value) {
     case HV_STEP_OPT_EVICT_FIRST:
       g_opt_evict_first = value != 0;
       return HV_OK;
+    case HV_STEP_OPT_LOCAL_QKV_BARRIER:
+      g_opt_local_qkv_barrier = value != 0;
+      return HV_OK;
     default:
       HV_REQUIRE(false, HV_E_INVALID, "hv_step_set_option: unknown option %d", option);
   }
@@ -1519,6 +1529,9 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
       if (dev >= 0 && dev < 64) done[gi][dev] = smem;
     }
   }
+  HV_REQUIRE((flags & ~(HV_STEP_HEAD | HV_STEP_ARGMAX)) == 0, HV_E_INVALID,
+             "hv_step_launch: unknown flags 0x%x", flags);
+  if (g_opt_local_qkv_barrier && world > 1) flags |= kFlagLocalQkvBarrier;
   int inflight = g_opt_inflight, evict_first = g_opt_evict_first;
   void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots, (void*)&inflight,
                   (void*)&evict_first};

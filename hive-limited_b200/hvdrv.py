@@ -414,6 +414,7 @@ def ipc_close(ptr):
 
 STEP_OPT_INFLIGHT = 1
 STEP_OPT_EVICT_FIRST = 2
+STEP_OPT_LOCAL_QKV_BARRIER = 3
 
 
 def step_set_option(option, value):

@@ -374,10 +374,13 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);
 
 /* Tuning of later hv_step_launch calls (process-wide): HV_STEP_OPT_INFLIGHT = bulk copies
  * each CTA's producer keeps in flight (1..32, default 6); HV_STEP_OPT_EVICT_FIRST = mark
- * the streamed weights and KV rows evict-first in L2 (0/1, default 1). Neither changes
+ * the streamed weights and KV rows evict-first in L2 (0/1, default 1);
+ * HV_STEP_OPT_LOCAL_QKV_BARRIER = in a sharded step, meet only the rank's own CTAs after
+ * the qkv projection (attention reads no other rank's data; 0/1, default 0). None changes
  * any result. No counterpart in the reference (its kernels have no such knobs). */
 #define HV_STEP_OPT_INFLIGHT 1
 #define HV_STEP_OPT_EVICT_FIRST 2
+#define HV_STEP_OPT_LOCAL_QKV_BARRIER 3
 int hv_step_set_option(int option, int value);
 
 #ifdef __cplusplus
