@@ -272,9 +272,15 @@ def run_reference(args, dist: Dist):
     return 0
 
 
+STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3}
+
+
 def run_ours(args, dist: Dist):
     import hvdrv
     import limited
+    for opt in args.step_opt:
+        name, _, value = opt.partition("=")
+        hvdrv.step_set_option(STEP_OPTS[name], int(value))
     arch, seed, n_prompt, n_new = synth.WORKLOADS[args.workload]
     cfg = w4format.Config(synth.ARCH[arch])
     cap = n_prompt + n_new
@@ -400,7 +406,7 @@ def run_ours(args, dist: Dist):
             "gpu_launches": args.steps,
             "clocks": clk,
             "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
-            "prefill": args.prefill,
+            "prefill": args.prefill, "step_options": args.step_opt,
             "weight_cache": {None: None, True: "hit", False: "miss"}[eng.cache_hit],
         }
         print(json.dumps(line), flush=True)
@@ -573,6 +579,9 @@ def main(argv=None):
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
+    ap.add_argument("--step-opt", action="append", default=[], metavar="NAME=VALUE",
+                    help="fused-step tuning option (results unchanged): "
+                         + ", ".join(STEP_OPTS))
     ap.add_argument("--prefill", default="steps", choices=["steps", "batched"],
                     help="how the prompt is prefilled before the timed decode: through the "
                          "decode step token by token (as the reference), or in batches")
@@ -591,6 +600,9 @@ def main(argv=None):
                     help="sweep only the shapes with at most this many rows (0: all)")
     ap.add_argument("--gemv-rotate-mb", type=int, default=320)
     args = ap.parse_args(argv)
+    for opt in args.step_opt:
+        if opt.partition("=")[0] not in STEP_OPTS or not opt.partition("=")[2].isdigit():
+            ap.error(f"--step-opt {opt!r}: NAME=VALUE with NAME in {', '.join(STEP_OPTS)}")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()
