@@ -5,7 +5,10 @@ geometry of a real Qwen3 size. The draw is fixed down to the RNG stream so that 
 engine, the oracle and the golden-vector script all see the same numbers:
 
 * tensor i of a model (in the order of `tensor_plan`) is drawn from
-  ``np.random.default_rng(np.random.SeedSequence(seed, spawn_key=(i,)))``;
+  ``np.random.default_rng(np.random.SeedSequence(seed, spawn_key=(i,)))``; a tensor of
+  more than BIG_DRAW elements (the 8B and 32B embeddings and LM heads) is drawn as
+  BIG_BLOCKS row blocks, block b from spawn key (i, b), in parallel -- a single stream
+  of 600M+ values would take ~20 s on one core;
 * projection matrices and the embedding: ``standard_normal(float32) * 0.02``;
 * RMSNorm gains: ``1 + standard_normal(float32) * 0.01``;
 * a tied model's embedding is stored as float16 (the reference gathers from an f16
@@ -98,9 +101,23 @@ def rng_for(seed: int, *key: int) -> np.random.Generator:
     return np.random.default_rng(np.random.SeedSequence(seed, spawn_key=tuple(key)))
 
 
+BIG_DRAW = 1 << 29      # elements above which a tensor is drawn in row blocks
+BIG_BLOCKS = 16
+
+
 def draw(seed: int, index: int, shape, kind: str) -> np.ndarray:
-    g = rng_for(seed, index)
-    x = g.standard_normal(shape, dtype=F32)
+    if int(np.prod(shape)) > BIG_DRAW:
+        x = np.empty(shape, F32)
+        edges = [shape[0] * b // BIG_BLOCKS for b in range(BIG_BLOCKS + 1)]
+
+        def fill(b):
+            part = x[edges[b]:edges[b + 1]]
+            rng_for(seed, index, b).standard_normal(part.shape, dtype=F32, out=part)
+
+        with cf.ThreadPoolExecutor(min(BIG_BLOCKS, os.cpu_count() or 1)) as ex:
+            list(ex.map(fill, range(BIG_BLOCKS)))
+    else:
+        x = rng_for(seed, index).standard_normal(shape, dtype=F32)
     if kind == "w":
         x *= F32(0.02)
     else:
@@ -116,7 +133,7 @@ def iter_tensors(cfg: Config, seed: int, threads: int | None = None, names=None)
     """
     plan = [(i, n, s, k) for i, (n, s, k) in enumerate(tensor_plan(cfg))
             if names is None or n in names]
-    threads = threads or min(8, os.cpu_count() or 1)
+    threads = threads or min(16, os.cpu_count() or 1)
 
     def make(item):
         i, n, s, k = item

@@ -104,6 +104,30 @@ def test_host_quantizer_matches_oracle():
     assert np.abs(back - w).max() <= np.abs(w).max() / 7 / 2 * 1.0001
 
 
+def test_big_tensors_are_drawn_in_row_blocks(monkeypatch):
+    """Above BIG_DRAW elements a tensor is BIG_BLOCKS row blocks, block b from stream
+    (seed, index, b); below it, one stream (seed, index). Either way the draw does not
+    depend on how many threads draw."""
+    import synth
+    monkeypatch.setattr(synth, "BIG_DRAW", 1000)
+    x = synth.draw(3, 7, (40, 64), "w")
+    edges = [40 * b // synth.BIG_BLOCKS for b in range(synth.BIG_BLOCKS + 1)]
+    for b in range(synth.BIG_BLOCKS):
+        want = synth.rng_for(3, 7, b).standard_normal((edges[b + 1] - edges[b], 64),
+                                                       dtype=np.float32) * np.float32(0.02)
+        assert np.array_equal(x[edges[b]:edges[b + 1]], want)
+    small = synth.draw(3, 7, (10, 64), "w")
+    assert np.array_equal(small, synth.rng_for(3, 7).standard_normal((10, 64),
+                                                                      dtype=np.float32)
+                          * np.float32(0.02))
+    import w4format
+    cfg = w4format.Config(synth.tiny_arch())
+    a = dict(synth.iter_tensors(cfg, 5, threads=1))
+    b = dict(synth.iter_tensors(cfg, 5, threads=6))
+    for k in a:
+        assert np.array_equal(a[k], b[k])
+
+
 def test_synthetic_draw_is_deterministic_and_thread_independent():
     import synth
     import w4format
