@@ -272,7 +272,7 @@ def run_reference(args, dist: Dist):
     return 0
 
 
-STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3}
+STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3, "split_merge": 4}
 
 
 def run_ours(args, dist: Dist):

@@ -68,6 +68,7 @@ static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention 
 static int g_opt_inflight = 6;
 static int g_opt_evict_first = 1;
 static int g_opt_local_qkv_barrier = 0;
+static int g_opt_split_merge = 0;
 // Launch flag set by the library (not by callers): the barrier after the qkv projection
 // of a sharded step stays among the rank's own CTAs.
 constexpr int kFlagLocalQkvBarrier = 1 << 8;
@@ -996,7 +997,7 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, in
 // through the ring (sequence numbers from *q). Same arithmetic, in the same order, as
 // attn_chunk with eight warps (k_attn): blocks of 20 positions go to warp (block % 8)
 // for the scores and the weighted V sum; warp i takes head i for the max and exp.
-template <int GS>
+template <int GS, bool kSplitMerge>
 __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
                                        const Ring R, unsigned* qp, StepShared& S,
                                        float* area, int tb) {
@@ -1136,10 +1137,11 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       part[threadIdx.x * kPartStride + 0] = (n > 0) ? stat_s[2 * threadIdx.x] : -INFINITY;
       part[threadIdx.x * kPartStride + 1] = (n > 0) ? stat_s[2 * threadIdx.x + 1] : 0.f;
     }
-    __threadfence();
+    if constexpr (!kSplitMerge) __threadfence();
     csync();
     trace_mark(D, tb + 17);
     trace_wait(D, S, tb + 22);
+    if constexpr (kSplitMerge) continue;             // merged after the grid barrier
     if (threadIdx.x == 0) S.flag = (atomicAdd(D.ticket + g, 1) == nch - 1);
     csync();
     trace_mark(D, tb + 18);
@@ -1164,9 +1166,62 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
   }
 }
 
+// The attention merge as its own phase (HV_STEP_OPT_SPLIT_MERGE, one GPU): after the
+// barrier that ends attention, each 32-value quantisation block of ctx is merged by one
+// warp (blocks spread over the CTAs), instead of each kv head's whole merge by the last
+// CTA of that head while every other CTA waits. Lane d of the warp does dim d of the
+// block; the arithmetic and its order are attn_merge's (M = max_c m_c, w_c = exp(m_c - M),
+// L = fma(w_c, l_c, L) and o = fma(w_c, acc_c, o) in chunk order, ctx = o * (1 / L), then
+// quant_a8s of the block), so the bits are the same. `area`: kConsWarps * nch floats.
+template <int GS>
+__device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = D.n_head, nch = D.attn_chunks;
+  constexpr int kPerHead = kHd / kBlock;
+  const int nblk = nq * kPerHead;
+  int8_t* cq = reinterpret_cast<int8_t*>(D.ctx);
+  int2* csb = reinterpret_cast<int2*>(cq + (size_t)nq * kHd);
+  float* wv = area + (size_t)warp * nch;
+  for (int qb = blockIdx.x + warp * gridDim.x; qb < nblk; qb += gridDim.x * kConsWarps) {
+    const int h = qb / kPerHead, d = (qb % kPerHead) * kBlock + lane;
+    const int g = h / GS, i = h % GS;
+    const float* ph = D.part + (size_t)g * nch * GS * kPartStride + (size_t)i * kPartStride;
+    constexpr size_t kChunk = (size_t)GS * kPartStride;
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(ph + c * kChunk));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    for (int c = lane; c < nch; c += 32) wv[c] = expf(__ldcg(ph + c * kChunk) - M);
+    __syncwarp();
+    float inv = 0.f;
+    if (lane == 0) {
+      float L = 0.f;
+      for (int c = 0; c < nch; ++c) L = fmaf(wv[c], __ldcg(ph + c * kChunk + 1), L);
+      inv = 1.0f / L;
+    }
+    inv = __shfl_sync(0xFFFFFFFFu, inv, 0);
+    float o = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+      float a[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = (c0 + k < nch) ? __ldcg(ph + (c0 + k) * kChunk + 4 + d) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (c0 + k < nch) o = fmaf(wv[c0 + k], a[k], o);
+    }
+    int8_t q8;
+    float sc;
+    int bs;
+    quant_block_warp(o * inv, lane, &q8, &sc, &bs);
+    cq[(size_t)h * kHd + d] = q8;
+    if (lane == 0) csb[qb] = make_int2(__float_as_int(sc), bs);
+    __syncwarp();                                   // wv is reused by the next block
+  }
+}
+
 // ---- the kernel ------------------------------------------------------------------------
 
-template <int GS>
+template <int GS, bool kSplitMerge>
 __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
                                                           int nslots, int inflight,
                                                           int evict_first) {
@@ -1263,9 +1318,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     if (!grid_sync(D, S, (flags & kFlagLocalQkvBarrier) == 0)) return;
     trace_mark(D, tb + 2);
     // P2: attention
-    attn_ring<GS>(D, L, pos, R, &q, S, work, tb);
+    attn_ring<GS, kSplitMerge>(D, L, pos, R, &q, S, work, tb);
     trace_mark(D, tb + 3);
     if (!grid_sync(D, S)) return;
+    if constexpr (kSplitMerge) {
+      merge_blocks<GS>(D, work);
+      if (!grid_sync(D, S)) return;
+    }
     trace_mark(D, tb + 4);
     if (threadIdx.x == 0) prefetch_vectors(L, hid, false);
     // P3: o projection + residual
@@ -1377,12 +1436,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   trace_mark(D, th + 2);
 }
 
-static void* step_fn(int gs) {
+static void* step_fn(int gs, bool split_merge) {
+  if (split_merge) {
+    switch (gs) {
+      case 1: return (void*)k_step<1, true>;
+      case 2: return (void*)k_step<2, true>;
+      case 4: return (void*)k_step<4, true>;
+      default: return (void*)k_step<8, true>;
+    }
+  }
   switch (gs) {
-    case 1: return (void*)k_step<1>;
-    case 2: return (void*)k_step<2>;
-    case 4: return (void*)k_step<4>;
-    default: return (void*)k_step<8>;
+    case 1: return (void*)k_step<1, false>;
+    case 2: return (void*)k_step<2, false>;
+    case 4: return (void*)k_step<4, false>;
+    default: return (void*)k_step<8, false>;
   }
 }
 
@@ -1456,6 +1523,9 @@ int hv_step_set_option(int option, int value) {
     case HV_STEP_OPT_LOCAL_QKV_BARRIER:
       g_opt_local_qkv_barrier = value != 0;
       return HV_OK;
+    case HV_STEP_OPT_SPLIT_MERGE:
+      g_opt_split_merge = value != 0;
+      return HV_OK;
     default:
       HV_REQUIRE(false, HV_E_INVALID, "hv_step_set_option: unknown option %d", option);
   }
@@ -1515,14 +1585,17 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
                  "hv_step_launch: %zu B of leaf values exceed the work area", need);
     }
   }
-  void* fn = step_fn(gs);
+  // the split merge (one GPU): its per-warp chunk weights live in the work area
+  const bool split_merge = g_opt_split_merge && world == 1 &&
+      (lay.ring - lay.work) / sizeof(float) >= (size_t)kConsWarps * h.attn_chunks;
+  void* fn = step_fn(gs, split_merge);
   {
-    // set the function's shared-memory limit once per (group size, device, size)
+    // set the function's shared-memory limit once per (kernel, device, size)
     static std::mutex mu;
-    static size_t done[4][64];
+    static size_t done[8][64];
     int dev = 0;
     HV_CUDA(cudaGetDevice(&dev));
-    const int gi = gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3;
+    const int gi = (gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3) + (split_merge ? 4 : 0);
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || done[gi][dev] < smem) {
       HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -1532,6 +1605,7 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE((flags & ~(HV_STEP_HEAD | HV_STEP_ARGMAX)) == 0, HV_E_INVALID,
              "hv_step_launch: unknown flags 0x%x", flags);
   if (g_opt_local_qkv_barrier && world > 1) flags |= kFlagLocalQkvBarrier;
+
   int inflight = g_opt_inflight, evict_first = g_opt_evict_first;
   void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots, (void*)&inflight,
                   (void*)&evict_first};

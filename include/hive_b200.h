@@ -381,6 +381,9 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);
 #define HV_STEP_OPT_INFLIGHT 1
 #define HV_STEP_OPT_EVICT_FIRST 2
 #define HV_STEP_OPT_LOCAL_QKV_BARRIER 3
+/* HV_STEP_OPT_SPLIT_MERGE: on one GPU, merge the attention partials as a phase of their
+ * own, one warp per 32-value block of ctx, after a grid barrier (0/1, default 0). */
+#define HV_STEP_OPT_SPLIT_MERGE 4
 int hv_step_set_option(int option, int value);
 
 #ifdef __cplusplus

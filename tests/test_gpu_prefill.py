@@ -10,8 +10,8 @@ import hv_oracle as O
 from gpu_util import Dev, bits
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(
-    not os.environ.get("HV_PREFILL_GPU_TESTS"),
-    reason="prefill kernels: set HV_PREFILL_GPU_TESTS=1 (not yet part of the default run)")]
+    not os.environ.get("HV_NEW_GPU_TESTS"),
+    reason="kernels not yet run on a B200: set HV_NEW_GPU_TESTS=1")]
 F32 = np.float32
 
 
