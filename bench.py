@@ -273,6 +273,70 @@ def run_reference(args, dist: Dist):
 
 
 STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3, "split_merge": 4}
+STEP_OPT_DEFAULTS = {"inflight": 6, "evict_first": 1, "local_qkv_barrier": 0, "split_merge": 0}
+
+
+def parse_opts(text: str) -> dict:
+    """'a=1,b=0' -> {'a': 1, 'b': 0} over STEP_OPTS names ('' -> {})."""
+    out = {}
+    for item in filter(None, (x.strip() for x in text.split(","))):
+        name, _, value = item.partition("=")
+        out[name] = int(value)
+    return out
+
+
+def run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv):
+    """Fused-step option sets against the baseline in this process (one load, one
+    prefill): `--ab-rounds` rounds, each timing every set for --steps steps in turn
+    (CUDA events, max over ranks), and each set's logits of one step at the first decode
+    position compared bit for bit with the baseline's. -> list of per-set results."""
+    sets = [{}] + [parse_opts(x) for x in args.ab]
+    base = dict(STEP_OPT_DEFAULTS, **parse_opts(",".join(args.step_opt)))
+
+    def apply(opts):
+        for name, value in dict(base, **opts).items():
+            hvdrv.step_set_option(STEP_OPTS[name], value)
+
+    def one_step_logits():
+        hvdrv.upload_async(eng.d_pos, pin, 4)              # position n_prompt, step 0
+        hvdrv.upload_async(eng.d_step, pin + 4, 4)
+        hvdrv.upload_async(eng.d_tok, pin + 8, 4)
+        eng._decode_one()
+        hvdrv.synchronize()
+        eng._check_status()
+        return eng.download_logits()
+
+    pbuf = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_int32 * 4).from_address(pin))
+    pbuf[2] = 17                                           # a fixed input token
+    ref = None
+    times = [[] for _ in sets]
+    same = [True for _ in sets]
+    e0, e1 = hvdrv.event_create(), hvdrv.event_create()
+    for _ in range(args.ab_rounds):
+        for i, opts in enumerate(sets):
+            apply(opts)
+            lg = one_step_logits()
+            if ref is None:
+                ref = lg
+            same[i] = same[i] and bool(np.array_equal(lg.view(np.uint32), ref.view(np.uint32)))
+            done[0] = 0
+            hvdrv.upload_async(eng.d_pos, pin, 4)
+            hvdrv.upload_async(eng.d_step, pin + 4, 4)
+            decode(3)
+            dist.barrier()
+            hvdrv.synchronize()
+            hvdrv.event_record(e0, 0)
+            decode(args.steps)
+            hvdrv.event_record(e1, 0)
+            hvdrv.synchronize()
+            times[i].append(dist.max(hvdrv.event_elapsed_ms(e0, e1)) / args.steps)
+    apply({})
+    out = []
+    for opts, t, ok in zip(sets, times, same):
+        ms = float(np.median(t))
+        out.append({"options": opts or "baseline", "ms_per_step": ms, "tok_s": 1e3 / ms,
+                    "runs_ms": [round(x, 4) for x in t], "logits_identical": ok})
+    return out
 
 
 def run_ours(args, dist: Dist):
@@ -365,6 +429,10 @@ def run_ours(args, dist: Dist):
         print(f"  total {prof['total_us']:.1f} us", file=sys.stderr, flush=True)
         eng._check_status()
 
+    ab = None
+    if args.ab:
+        ab = run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv)
+
     # end to end through the public API: Engine.stream with host-fed tokens
     n_e2e = min(args.e2e_steps, window)
     ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True))
@@ -407,6 +475,7 @@ def run_ours(args, dist: Dist):
             "clocks": clk,
             "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
             "prefill": args.prefill, "step_options": args.step_opt,
+            **({"ab": ab} if ab is not None else {}),
             "weight_cache": {None: None, True: "hit", False: "miss"}[eng.cache_hit],
         }
         print(json.dumps(line), flush=True)
@@ -579,6 +648,10 @@ def main(argv=None):
     ap.add_argument("--mode", default="sharded", choices=["sharded", "replicas"],
                     help="with more than one GPU: shard one stream across them (column "
                          "parallel) or run one independent stream per GPU")
+    ap.add_argument("--ab", action="append", default=[], metavar="NAME=VALUE[,...]",
+                    help="also time this fused-step option set against the baseline in "
+                         "the same process (repeatable); results under 'ab'")
+    ap.add_argument("--ab-rounds", type=int, default=3)
     ap.add_argument("--step-opt", action="append", default=[], metavar="NAME=VALUE",
                     help="fused-step tuning option (results unchanged): "
                          + ", ".join(STEP_OPTS))
@@ -600,9 +673,9 @@ def main(argv=None):
                     help="sweep only the shapes with at most this many rows (0: all)")
     ap.add_argument("--gemv-rotate-mb", type=int, default=320)
     args = ap.parse_args(argv)
-    for opt in args.step_opt:
+    for opt in args.step_opt + [x for a in args.ab for x in a.split(",") if x.strip()]:
         if opt.partition("=")[0] not in STEP_OPTS or not opt.partition("=")[2].isdigit():
-            ap.error(f"--step-opt {opt!r}: NAME=VALUE with NAME in {', '.join(STEP_OPTS)}")
+            ap.error(f"option {opt!r}: NAME=VALUE with NAME in {', '.join(STEP_OPTS)}")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()
