@@ -435,7 +435,7 @@ def run_ours(args, dist: Dist):
 
     # end to end through the public API: Engine.stream with host-fed tokens
     n_e2e = min(args.e2e_steps, window)
-    ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True))
+    ev = list(eng.stream(prompt, max_new=n_e2e, host_tokens=True)) if n_e2e > 0 else []
     times = [e[2] for e in ev if e[0] == "tok"]
     e2e = (len(times) - 1) / (times[-1] - times[0]) if len(times) > 1 else None
     e2e_all = dist.sum(e2e or 0.0) if dist.world > 1 and not sharded else e2e
@@ -640,7 +640,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qwen3-8b-p4096-g256", choices=list(synth.WORKLOADS))
-    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--e2e-steps", type=int, default=128,
+                    help="tokens of the end-to-end run (0 skips it, and its second prefill)")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true",
