@@ -80,3 +80,34 @@ def test_batched_prefill_equals_token_by_token(hv, fused):
     assert np.array_equal(bits(kv0), bits(kv1))
     assert np.array_equal(bits(lg0), bits(lg1))
     assert t0 == t1
+
+
+GOLDEN_TINY = [("decode_tiny.npz", dict(), 7),
+               ("decode_tiny_tied.npz", dict(n_layer=3, hidden=512, ffn=1024, n_head=8, n_kv=2,
+                                             vocab=2048, tied=True), 8)]
+
+
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("name,arch,seed", GOLDEN_TINY)
+def test_batched_prefill_matches_reference_decode(hv, golden, name, arch, seed, fused):
+    """The reference's own greedy decode of the tiny models (tests/golden, made by
+    engine/reference.py): with the batched prefill the tokens are the same and the
+    step-0 logits within the tolerance the token-by-token prefill meets (1e-5 of the
+    logit scale; exp-based ops are not bit-restatable)."""
+    import limited
+    import synth
+    from w4format import Config
+    g = golden(name)
+    prompt, want = g["prompt"].tolist(), g["tokens"].tolist()
+    cfg = Config(synth.tiny_arch(**arch))
+    eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
+                         max_context=64, fused=fused, prefill="batched")
+    try:
+        toks, _, _ = eng.generate(prompt, max_new=len(want))
+        assert toks == want
+        lg = eng.logits(prompt)
+        ref = g["logits"][0]
+        err = float(np.abs(lg.astype(np.float64) - ref).max() / np.abs(ref).max())
+        assert err < 1e-5, err
+    finally:
+        eng.free()
