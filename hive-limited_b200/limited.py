@@ -17,7 +17,6 @@ from __future__ import annotations
 
 import ctypes as C
 import time
-from pathlib import Path
 
 import numpy as np
 

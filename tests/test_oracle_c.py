@@ -31,7 +31,6 @@ def test_c_gemv_matches_numpy_oracle(n, k):
 
 
 def test_c_pairwise_sum_is_numpys():
-    import ctypes
     lib = O._clib()
     for n in (1, 7, 8, 100, 129, 800, 4096, 5120, 25600):
         x = (np.random.default_rng(n).standard_normal(n) * 10).astype(F32)
