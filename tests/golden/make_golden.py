@@ -6,6 +6,7 @@ Runs ONLY where the reference checkout exists (the build container); the resulti
     python tests/golden/make_golden.py ops         # op-level vectors (seconds)
     python tests/golden/make_golden.py gemv        # GEMV sweep digests (a minute)
     python tests/golden/make_golden.py tiny        # tiny-model greedy decode (seconds)
+    python tests/golden/make_golden.py long        # tiny model, 300- and 2000-token prompts
     python tests/golden/make_golden.py c1          # 1.7B-shape 32+64 decode (~1 hour)
 
 The reference's engine/limited.py dlopens libcuda at import; a stub `cudrv` module is
@@ -210,6 +211,11 @@ def main(argv):
         make_decode(HERE / "decode_tiny_tied.npz",
                     synth.tiny_arch(n_layer=3, hidden=512, ffn=1024, n_head=8, n_kv=2,
                                     vocab=2048, tied=True), 8, 9, 10, True)
+    elif what == "long":
+        # a prompt long enough that decode attention runs over several sequence chunks
+        make_decode(HERE / "decode_tiny_long.npz", synth.tiny_arch(), 9, 300, 8, True)
+        # over 20 positions per chunk on a 148-SM part: several position blocks per chunk
+        make_decode(HERE / "decode_tiny_2k.npz", synth.tiny_arch(), 10, 2000, 4, True)
     elif what == "c1":
         arch, seed, n_prompt, n_new = synth.WORKLOADS["qwen3-1.7b-p32-g64"]
         make_decode(HERE / "decode_qwen3_1p7b.npz", synth.ARCH[arch], seed, n_prompt,

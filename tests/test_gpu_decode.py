@@ -3,6 +3,8 @@
 * tiny Qwen3-shaped models: tokens identical to engine/reference.py's, logits within a
   stated tolerance (exp-based SiLU/softmax are the only non-bit-exact ops), and the
   eager kernel-by-kernel path bit-identical to the fused one-launch step;
+* the tiny model after 300- and 2000-token prompts, where decode attention runs over
+  every sequence chunk (several position blocks per chunk at 2000);
 * the 1.7B-shaped workload (32-token prompt, 64 greedy tokens) against the tokens and
   logits the reference produced in the build container;
 * 8B- and 32B-shaped models against the C oracle at short prompts.
@@ -80,6 +82,31 @@ def test_eager_and_fused_are_bit_identical(hv, golden, name, arch, seed):
     finally:
         a.free()
         b.free()
+
+
+LONG = [("decode_tiny_long.npz", 9, 300), ("decode_tiny_2k.npz", 10, 2000)]
+
+
+@pytest.mark.parametrize("name,seed,n_prompt", LONG)
+@pytest.mark.parametrize("fused", [True, False])
+def test_long_prompt_decode_matches_reference(hv, golden, name, seed, n_prompt, fused):
+    """Greedy tokens identical to the reference's after a long prompt; every generated
+    step's logits within the tiny-model tolerance. The fixtures' smallest top-2 margin is
+    2.8e-4 of the logit scale, far above that tolerance."""
+    g = golden(name)
+    arch = synth.tiny_arch()
+    prompt, want = g["prompt"].tolist(), g["tokens"].tolist()
+    assert prompt == synth.prompt_ids(w4format.Config(arch), seed, n_prompt)
+    eng = make_engine(arch, seed, n_prompt + len(want) + 2, fused=fused)
+    try:
+        toks, _, _ = eng.generate(prompt, max_new=len(want), stop_on_eos=False)
+        assert toks == want
+        errs = [rel_err(eng.logits(prompt + want[:i]), g["logits"][i])
+                for i in range(len(want) + 1)]
+        print(f"{name} fused={fused}: logits rel err max {max(errs):.2e}")
+        assert max(errs) < 1e-5
+    finally:
+        eng.free()
 
 
 def test_graph_replay_matches_direct(hv):

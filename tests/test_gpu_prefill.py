@@ -84,7 +84,10 @@ def test_batched_prefill_equals_token_by_token(hv, fused):
 
 GOLDEN_TINY = [("decode_tiny.npz", dict(), 7),
                ("decode_tiny_tied.npz", dict(n_layer=3, hidden=512, ffn=1024, n_head=8, n_kv=2,
-                                             vocab=2048, tied=True), 8)]
+                                             vocab=2048, tied=True), 8),
+               # several prefill batches, and decode attention over many positions per chunk
+               ("decode_tiny_long.npz", dict(), 9),
+               ("decode_tiny_2k.npz", dict(), 10)]
 
 
 @pytest.mark.parametrize("fused", [False, True])
@@ -101,7 +104,8 @@ def test_batched_prefill_matches_reference_decode(hv, golden, name, arch, seed, 
     prompt, want = g["prompt"].tolist(), g["tokens"].tolist()
     cfg = Config(synth.tiny_arch(**arch))
     eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
-                         max_context=64, fused=fused, prefill="batched")
+                         max_context=len(prompt) + len(want) + 2, fused=fused,
+                         prefill="batched")
     try:
         toks, _, _ = eng.generate(prompt, max_new=len(want))
         assert toks == want
