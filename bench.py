@@ -27,6 +27,8 @@ the fused step as NVLink peer stores (strong scaling; value = that stream's tok/
 roofline against N x the HBM peak); --mode replicas runs N independent streams (weak
 scaling; value = total tok/s).
 --impl reference: the reference's CPU algorithm (oracle port, all host threads) on rank 0.
+--kv-dtype f16: the compressed-KV lane (binary16 cache, half the KV bytes; results follow
+its own oracle, not the reference's fp32 cache). The default f32 is the headline.
 """
 from __future__ import annotations
 
@@ -193,15 +195,16 @@ def profiled_traffic(name: str):
     return None
 
 
-def step_bytes(cfg, head_rows: int, pos: int) -> int:
+def step_bytes(cfg, head_rows: int, pos: int, kv_elem: int = 4) -> int:
     """Algorithmic HBM bytes of one decode step at position `pos`: int4 weights + f32
-    scales of every GEMV (0.625 B per weight) plus the fp32 K and V rows 0..pos read."""
+    scales of every GEMV (0.625 B per weight) plus the K and V rows 0..pos read (fp32,
+    or kv_elem = 2 for the binary16 cache)."""
     c = cfg
     qd = c.head_dim
     per_layer = ((c.n_head + 2 * c.n_kv) * qd * c.hidden + c.hidden * c.n_head * qd
                  + 2 * c.ffn * c.hidden + c.hidden * c.ffn)
     w = c.n_layer * per_layer + head_rows * c.hidden
-    kv = 2 * c.n_layer * c.n_kv * qd * 4 * (pos + 1)
+    kv = 2 * c.n_layer * c.n_kv * qd * kv_elem * (pos + 1)
     return int(w * 5 // 8 + kv)
 
 
@@ -355,7 +358,8 @@ def run_ours(args, dist: Dist):
                          world=dist.world if sharded else 1, rank=dist.rank if sharded else 0,
                          exchange=dist.allgather_bytes if sharded else None,
                          weight_cache=args.weight_cache, prefill=args.prefill,
-                         cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None)
+                         cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None,
+                         kv_dtype=args.kv_dtype)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
     window = cap - n_prompt              # decode positions available before a rewind
@@ -409,10 +413,13 @@ def run_ours(args, dist: Dist):
     positions = [n_prompt + ((first_step + i) % window) for i in range(args.steps)]
     head_rows = eng.n_head_rows * (dist.world if sharded else 1)
     n_peak = dist.world if sharded else 1        # the HBM of every GPU the stream uses
-    bytes_mean = float(np.mean([step_bytes(cfg, head_rows, p) for p in positions]))
+    kv_elem = 2 if args.kv_dtype == "f16" else 4
+    bytes_mean = float(np.mean([step_bytes(cfg, head_rows, p, kv_elem) for p in positions]))
     peak, peak_kind = measured_peak()
     achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
-    traffic = None if sharded else profiled_traffic("k_step_qwen3-8b_decode.md")
+    # the committed ncu capture is of the f32-cache step
+    traffic = (None if sharded or args.kv_dtype != "f32"
+               else profiled_traffic("k_step_qwen3-8b_decode.md"))
 
     if args.profile and dist.rank == 0:
         # one extra step with the per-phase device trace, at the next decode position
@@ -457,12 +464,12 @@ def run_ours(args, dist: Dist):
             "vs_baseline": None,
             "dtype": "int8", "data": "synthetic (seeded random-init weights and prompt)",
             "config": {"workload": args.workload, "model": arch, "batch": 1,
-                       "prompt": n_prompt, "generated": n_new, "kv": "f32",
+                       "prompt": n_prompt, "generated": n_new, "kv": args.kv_dtype,
                        "weights": "int4 + f32 scale per 32 (5.00 bits/weight)",
                        "parallelism": (f"column-sharded x{dist.world} (NVLink peer stores "
                                        "inside the fused step)" if sharded else
                                        "replicas" if dist.world > 1 else "single"),
-                       "l2": "inputs larger than L2 (5.9 GB read per step)",
+                       "l2": f"inputs larger than L2 ({bytes_mean / 1e9:.1f} GB read per step)",
                        "positions": f"{min(positions)}..{max(positions)}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * n_peak,
                          "unit": "GB/s", "frac": achieved / (peak * n_peak), "traffic": traffic,
@@ -659,6 +666,9 @@ def main(argv=None):
     ap.add_argument("--prefill", default="steps", choices=["steps", "batched"],
                     help="how the prompt is prefilled before the timed decode: through the "
                          "decode step token by token (as the reference), or in batches")
+    ap.add_argument("--kv-dtype", default="f32", choices=["f32", "f16"],
+                    help="KV cache element type: f32 (the reference's cache) or f16 (the "
+                         "compressed-KV lane)")
     ap.add_argument("--weight-cache", default=None, metavar="DIR",
                     help="load device-ready weights from DIR when present, else quantise "
                          "and write them there (the timed steps are the same either way)")

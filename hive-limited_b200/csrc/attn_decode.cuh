@@ -13,6 +13,8 @@
 // engine/reference.py to within float rounding, not bit for bit.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "hv_common.cuh"
 
 namespace hv {
@@ -30,6 +32,39 @@ HV_DEV void chunk_bounds(int npos, int nch, int c, int* t0, int* t1) {
 }
 
 HV_DEV float4 ldg_f4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// The cache's element type: float, or __half for the compressed-KV lane.
+template <class KT>
+constexpr bool kKvHalf = false;
+template <>
+constexpr bool kKvHalf<__half> = true;
+
+// A float as stored in the cache (binary16: nearest, ties to even; overflow to infinity).
+template <class KT>
+HV_DEV KT to_kv(float x);
+template <>
+HV_DEV float to_kv<float>(float x) { return x; }
+template <>
+HV_DEV __half to_kv<__half>(float x) { return __float2half_rn(x); }
+
+// x rounded to binary16 and widened back: the value an f16 cache holds for x.
+HV_DEV float4 round_half4(float4 v) {
+  return make_float4(__half2float(__float2half_rn(v.x)), __half2float(__float2half_rn(v.y)),
+                     __half2float(__float2half_rn(v.z)), __half2float(__float2half_rn(v.w)));
+}
+
+// Dims 4 lane .. 4 lane + 3 of cache row t, as floats. The cache holds f32, or IEEE
+// binary16 (the compressed-KV lane); half -> float is exact, so everything after the load
+// is the same arithmetic on the same values either way.
+HV_DEV float4 kv_row4(const float* base, int t, int lane) {
+  return ldg_f4(base + (size_t)t * kHd + lane * 4);
+}
+HV_DEV float4 kv_row4(const __half* base, int t, int lane) {
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(base + (size_t)t * kHd + lane * 4));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
 
 // Sum V values held in every lane across the 32 lanes by recursive halving: after it,
 // lane l holds the total of value index `*idx`; lanes whose low (log2(32/V)) bits are
@@ -99,13 +134,13 @@ constexpr size_t attn_smem_bytes(int nwarps) {
 
 // One work item: positions [t0, t1) of one kv head for its GS query heads.
 //   q_s    smem [GS][128]  query heads, already normed and rotated
-//   K, V   global [cap][128] rows of this kv head
+//   K, V   global [cap][128] rows of this kv head (float, or __half for the f16 cache)
 //   pos, kpos_s/vpos_s: if kpos_s is set, row `pos` is taken from it instead of K/V
 //   part   global [GS][kPartStride] partial state written by this item
 // Block-cooperative; all threads call it.
-template <int GS>
-HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
-                       const float* __restrict__ V, int t0, int t1, float scale, int pos,
+template <int GS, class KT>
+HV_DEV void attn_chunk(const float* q_s, const KT* __restrict__ K,
+                       const KT* __restrict__ V, int t0, int t1, float scale, int pos,
                        const float* kpos_s, const float* vpos_s, float* lg_s, float* red_s,
                        float* stat_s, float* __restrict__ part) {
   const int lane = threadIdx.x & 31;
@@ -127,7 +162,7 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
         const int t = tb + p;
         if (t < t1) {
           kv[p] = (kpos_s && t == pos) ? reinterpret_cast<const float4*>(kpos_s)[lane]
-                                       : ldg_f4(K + (size_t)t * kHd + lane * 4);
+                                       : kv_row4(K, t, lane);
         } else {
           kv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -187,7 +222,7 @@ HV_DEV void attn_chunk(const float* q_s, const float* __restrict__ K,
         const int t = tb + p;
         if (t < t1) {
           vv[p] = (vpos_s && t == pos) ? reinterpret_cast<const float4*>(vpos_s)[lane]
-                                       : ldg_f4(V + (size_t)t * kHd + lane * 4);
+                                       : kv_row4(V, t, lane);
         } else {
           vv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
         }

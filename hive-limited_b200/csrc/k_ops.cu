@@ -315,6 +315,19 @@ __global__ void k_kvapp(const float* __restrict__ k, const float* __restrict__ v
   }
 }
 
+// The compressed-KV lane's append: each value rounded to the nearest binary16 (ties to
+// even, overflow to infinity), the conversion numpy's astype(float16) performs.
+__global__ void k_kvapp16(const float* __restrict__ k, const float* __restrict__ v,
+                          __half* __restrict__ kc, __half* __restrict__ vc,
+                          const int32_t* __restrict__ pos, int hd, int cap) {
+  const int p = *pos;
+  const int h = blockIdx.x;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    kc[((size_t)h * cap + p) * hd + d] = __float2half_rn(k[h * hd + d]);
+    vc[((size_t)h * cap + p) * hd + d] = __float2half_rn(v[h * hd + d]);
+  }
+}
+
 __global__ void k_silu(const float* __restrict__ g, const float* __restrict__ u,
                        float* __restrict__ act, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -495,10 +508,10 @@ __global__ void k_quantize_w4(const float* __restrict__ w, uint32_t* __restrict_
 // ---------------------------------------------------------------------------
 constexpr int kAttnThreads = 256;
 
-template <int GS>
+template <int GS, class KT>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q,
-                                                       const float* __restrict__ kc,
-                                                       const float* __restrict__ vc,
+                                                       const KT* __restrict__ kc,
+                                                       const KT* __restrict__ vc,
                                                        float* __restrict__ ctx,
                                                        const float* __restrict__ scale_p,
                                                        const int32_t* __restrict__ pos_p,
@@ -586,16 +599,44 @@ static int attn_scratch(int nkv, int group, int cap, void* stream, AttnScratch**
   return HV_OK;
 }
 
-template <int GS>
-static int launch_attn(const float* q, const float* kc, const float* vc, float* ctx,
+template <int GS, class KT>
+static int launch_attn(const float* q, const KT* kc, const KT* vc, float* ctx,
                        const float* scale, const int32_t* pos, int nkv, int cap, int nch,
                        AttnScratch* s, cudaStream_t st) {
   const size_t smem = attn_smem_bytes<GS>(kAttnThreads / 32);
-  const int rc = smem_attr((const void*)k_attn<GS>, smem);
+  const int rc = smem_attr((const void*)k_attn<GS, KT>, smem);
   if (rc) return rc;
-  k_attn<GS><<<nkv * nch, kAttnThreads, smem, st>>>(q, kc, vc, ctx, scale, pos, cap, nch,
-                                                    s->part, s->ticket);
+  k_attn<GS, KT><<<nkv * nch, kAttnThreads, smem, st>>>(q, kc, vc, ctx, scale, pos, cap, nch,
+                                                        s->part, s->ticket);
   HV_LAUNCHED("k_attn");
+}
+
+// hv_attn_decode and hv_attn_decode_f16: checks, scratch, chunk count, launch.
+template <class KT>
+static int attn_decode_any(const char* name, const float* q, const KT* kc, const KT* vc,
+                           float* ctx, const float* scale, const int32_t* pos, int nq, int hd,
+                           int group, int kvstride, void* stream) {
+  HV_REQUIRE(q && kc && vc && ctx && scale && pos && nq > 0 && group > 0, HV_E_INVALID,
+             "%s: bad arguments", name);
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, hd);
+  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
+             "%s: nq %% group or kvstride %% hd is not zero", name);
+  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
+             "%s: group size %d (1, 2, 4 or 8)", name, group);
+  const int nkv = nq / group, cap = kvstride / hd;
+  AttnScratch* s = nullptr;
+  int rc = attn_scratch(nkv, group, cap, stream, &s);
+  if (rc) return rc;
+  int nch = 0;
+  rc = attn_nch(nkv, cap, &nch);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (group) {
+    case 1: return launch_attn<1>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    case 2: return launch_attn<2>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    case 4: return launch_attn<4>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+    default: return launch_attn<8>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
+  }
 }
 
 }  // namespace hv
@@ -606,7 +647,7 @@ extern "C" {
 
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
-      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_attn,k_silu,k_vadd,k_gather,"
+      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_kvapp16,k_attn,k_silu,k_vadd,k_gather,"
       "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp,k_gather_rows,k_qa8s_rows,k_qk_rows,k_attn_rows,k_silu_rows";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
@@ -763,6 +804,15 @@ int hv_kv_append(const float* k, const float* v, float* kc, float* vc, const int
   HV_LAUNCHED("k_kvapp");
 }
 
+int hv_kv_append_f16(const float* k, const float* v, uint16_t* kc, uint16_t* vc,
+                     const int32_t* pos, int nkv, int hd, int cap, void* stream) {
+  HV_REQUIRE(k && v && kc && vc && pos && nkv > 0 && hd > 0 && cap > 0, HV_E_INVALID,
+             "hv_kv_append_f16: bad arguments");
+  k_kvapp16<<<nkv, 128, 0, (cudaStream_t)stream>>>(k, v, reinterpret_cast<__half*>(kc),
+                                                   reinterpret_cast<__half*>(vc), pos, hd, cap);
+  HV_LAUNCHED("k_kvapp16");
+}
+
 int hv_attn_reserve(int nkv, int group, int cap) {
   HV_REQUIRE(nkv > 0 && group > 0 && cap > 0, HV_E_INVALID, "hv_attn_reserve: bad arguments");
   AttnScratch* s = nullptr;
@@ -772,27 +822,16 @@ int hv_attn_reserve(int nkv, int group, int cap) {
 int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
                    const float* scale, const int32_t* pos, int nq, int hd, int group,
                    int kvstride, void* stream) {
-  HV_REQUIRE(q && kc && vc && ctx && scale && pos && nq > 0 && group > 0, HV_E_INVALID,
-             "hv_attn_decode: bad arguments");
-  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_attn_decode: head_dim %d (only 128)", hd);
-  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
-             "hv_attn_decode: nq %% group or kvstride %% hd is not zero");
-  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
-             "hv_attn_decode: group size %d (1, 2, 4 or 8)", group);
-  const int nkv = nq / group, cap = kvstride / hd;
-  AttnScratch* s = nullptr;
-  int rc = attn_scratch(nkv, group, cap, stream, &s);
-  if (rc) return rc;
-  int nch = 0;
-  rc = attn_nch(nkv, cap, &nch);
-  if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (group) {
-    case 1: return launch_attn<1>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    case 2: return launch_attn<2>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    case 4: return launch_attn<4>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    default: return launch_attn<8>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-  }
+  return attn_decode_any("hv_attn_decode", q, kc, vc, ctx, scale, pos, nq, hd, group,
+                         kvstride, stream);
+}
+
+int hv_attn_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, float* ctx,
+                       const float* scale, const int32_t* pos, int nq, int hd, int group,
+                       int kvstride, void* stream) {
+  return attn_decode_any("hv_attn_decode_f16", q, reinterpret_cast<const __half*>(kc),
+                         reinterpret_cast<const __half*>(vc), ctx, scale, pos, nq, hd, group,
+                         kvstride, stream);
 }
 
 int hv_silu_mul(const float* gate, const float* up, float* act, int n, void* stream) {

@@ -177,13 +177,16 @@ __global__ void __launch_bounds__(256) k_qa8s_rows(const float* __restrict__ src
 // q/k RMSNorm and RoPE at position pos0 + t, K and V rows appended to the cache: one warp
 // per (token, head) over the nq query heads and the nkv key heads (whose warp also
 // copies the head's V row). qkv rows are [q | k | v] as the qkv projection writes them.
+// KT: the cache's element type (float; __half for the compressed-KV lane, whose rows are
+// rounded as hv_kv_append_f16 rounds them).
+template <class KT>
 __global__ void __launch_bounds__(256) k_qk_rows(const float* __restrict__ qkv,
                                                  const float* __restrict__ qn,
                                                  const float* __restrict__ kn,
                                                  const float* __restrict__ cos_t,
                                                  const float* __restrict__ sin_t, int pos0,
-                                                 float* __restrict__ q_out, float* kc,
-                                                 float* vc, int nq, int nkv, int cap,
+                                                 float* __restrict__ q_out, KT* kc,
+                                                 KT* vc, int nq, int nkv, int cap,
                                                  float eps, int ntok) {
   __shared__ __align__(16) float tmp[8][kHd];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -198,12 +201,23 @@ __global__ void __launch_bounds__(256) k_qk_rows(const float* __restrict__ qkv,
   if (h < nq) {
     warp_norm_rope(row + (size_t)h * kHd, qn, cs, sn, eps, tmp[warp],
                    q_out + ((size_t)t * nq + h) * kHd);
-  } else {
+  } else if constexpr (!kKvHalf<KT>) {
     const int g = h - nq;
     warp_norm_rope(row + (size_t)(nq + g) * kHd, kn, cs, sn, eps, tmp[warp],
                    kc + ((size_t)g * cap + pos) * kHd);
     reinterpret_cast<float4*>(vc + ((size_t)g * cap + pos) * kHd)[lane] =
         reinterpret_cast<const float4*>(row + (size_t)(nq + nkv + g) * kHd)[lane];
+  } else {
+    __shared__ __align__(16) float krow[8][kHd];
+    const int g = h - nq;
+    warp_norm_rope(row + (size_t)(nq + g) * kHd, kn, cs, sn, eps, tmp[warp], krow[warp]);
+    const float4 k4 = reinterpret_cast<const float4*>(krow[warp])[lane];
+    const float4 v4 = reinterpret_cast<const float4*>(row + (size_t)(nq + nkv + g) * kHd)[lane];
+    const size_t at = ((size_t)g * cap + pos) * kHd + 4 * lane;
+    reinterpret_cast<__half2*>(kc + at)[0] = __floats2half2_rn(k4.x, k4.y);
+    reinterpret_cast<__half2*>(kc + at)[1] = __floats2half2_rn(k4.z, k4.w);
+    reinterpret_cast<__half2*>(vc + at)[0] = __floats2half2_rn(v4.x, v4.y);
+    reinterpret_cast<__half2*>(vc + at)[1] = __floats2half2_rn(v4.z, v4.w);
   }
 }
 
@@ -211,10 +225,10 @@ __global__ void __launch_bounds__(256) k_qk_rows(const float* __restrict__ qkv,
 // attends positions 0 .. pos0 + t with the same chunking (nch) and merge, so its ctx row
 // is what hv_attn_decode gives at that position. Grid (nkv * nch, ntok); per-token
 // partials and tickets in caller scratch (tickets zero; each merge re-zeroes its own).
-template <int GS>
+template <int GS, class KT>
 __global__ void __launch_bounds__(256) k_attn_rows(const float* __restrict__ q,
-                                                   const float* __restrict__ kc,
-                                                   const float* __restrict__ vc,
+                                                   const KT* __restrict__ kc,
+                                                   const KT* __restrict__ vc,
                                                    float* __restrict__ ctx,
                                                    const float* __restrict__ scale_p, int pos0,
                                                    int cap, int nch, int nq,
@@ -272,17 +286,68 @@ int rows_attn_chunks(int nkv, int cap, int* out) {
   return HV_OK;
 }
 
-template <int GS>
-int launch_attn_rows(const float* q, const float* kc, const float* vc, float* ctx,
+template <int GS, class KT>
+int launch_attn_rows(const float* q, const KT* kc, const KT* vc, float* ctx,
                      const float* scale, int pos0, int cap, int nch, int nq, int ntok,
                      float* part, int* ticket, cudaStream_t st) {
   const size_t smem = attn_smem_bytes<GS>(8);
-  HV_CUDA(cudaFuncSetAttribute((const void*)k_attn_rows<GS>,
+  HV_CUDA(cudaFuncSetAttribute((const void*)k_attn_rows<GS, KT>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const dim3 grid((unsigned)(nq / GS * nch), (unsigned)ntok);
-  k_attn_rows<GS><<<grid, 256, smem, st>>>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, part,
-                                           ticket);
+  k_attn_rows<GS, KT><<<grid, 256, smem, st>>>(q, kc, vc, ctx, scale, pos0, cap, nch, nq,
+                                               part, ticket);
   HV_LAUNCHED("k_attn_rows");
+}
+
+// hv_qk_rows and hv_qk_rows_f16.
+template <class KT>
+int qk_rows_any(const char* name, const float* qkv, const float* qn, const float* kn,
+                const float* cos_t, const float* sin_t, int pos0, float* q_out, KT* kc, KT* vc,
+                int nq, int nkv, int hd, int cap, float eps, int ntok, void* stream) {
+  HV_REQUIRE(qkv && qn && kn && cos_t && sin_t && q_out && kc && vc && nq > 0 && nkv > 0 &&
+                 ntok > 0 && pos0 >= 0,
+             HV_E_INVALID, "%s: bad arguments", name);
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, hd);
+  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
+             "%s: positions %d .. %d outside the cache of %d", name, pos0, pos0 + ntok - 1, cap);
+  HV_REQUIRE(((uintptr_t)qkv & 15) == 0 && ((uintptr_t)kc & 15) == 0 &&
+                 ((uintptr_t)vc & 15) == 0,
+             HV_E_INVALID, "%s: unaligned pointer", name);
+  const long long warps = (long long)(nq + nkv) * ntok;
+  k_qk_rows<KT><<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, cap, eps, ntok);
+  HV_LAUNCHED("k_qk_rows");
+}
+
+// hv_attn_rows and hv_attn_rows_f16.
+template <class KT>
+int attn_rows_any(const char* name, const float* q, const KT* kc, const KT* vc, float* ctx,
+                  const float* scale, int pos0, int nq, int hd, int group, int kvstride,
+                  int ntok, float* part, int32_t* ticket, void* stream) {
+  HV_REQUIRE(q && kc && vc && ctx && scale && part && ticket && nq > 0 && group > 0 &&
+                 ntok > 0 && ntok <= 65535 && pos0 >= 0,
+             HV_E_INVALID, "%s: bad arguments", name);
+  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, hd);
+  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
+             "%s: nq %% group or kvstride %% hd is not zero", name);
+  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
+             "%s: group size %d (1, 2, 4 or 8)", name, group);
+  const int cap = kvstride / hd;
+  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
+             "%s: positions %d .. %d outside the cache of %d", name, pos0, pos0 + ntok - 1, cap);
+  int nch = 0;
+  const int rc = rows_attn_chunks(nq / group, cap, &nch);
+  if (rc) return rc;
+  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
+             "%s: %d chunks per kv head (at most %d)", name, nch, kAttnMaxChunks);
+  cudaStream_t st = (cudaStream_t)stream;
+  int* tk = reinterpret_cast<int*>(ticket);
+  switch (group) {
+    case 1: return launch_attn_rows<1>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    case 2: return launch_attn_rows<2>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    case 4: return launch_attn_rows<4>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+    default: return launch_attn_rows<8>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
+  }
 }
 
 }  // namespace
@@ -313,19 +378,17 @@ extern "C" int hv_qk_rows(const float* qkv, const float* qn, const float* kn,
                           const float* cos_t, const float* sin_t, int pos0, float* q_out,
                           float* kc, float* vc, int nq, int nkv, int hd, int cap, float eps,
                           int ntok, void* stream) {
-  HV_REQUIRE(qkv && qn && kn && cos_t && sin_t && q_out && kc && vc && nq > 0 && nkv > 0 &&
-                 ntok > 0 && pos0 >= 0,
-             HV_E_INVALID, "hv_qk_rows: bad arguments");
-  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_qk_rows: head_dim %d (only 128)", hd);
-  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
-             "hv_qk_rows: positions %d .. %d outside the cache of %d", pos0, pos0 + ntok - 1, cap);
-  HV_REQUIRE(((uintptr_t)qkv & 15) == 0 && ((uintptr_t)kc & 15) == 0 &&
-                 ((uintptr_t)vc & 15) == 0,
-             HV_E_INVALID, "hv_qk_rows: unaligned pointer");
-  const long long warps = (long long)(nq + nkv) * ntok;
-  k_qk_rows<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-      qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, cap, eps, ntok);
-  HV_LAUNCHED("k_qk_rows");
+  return qk_rows_any("hv_qk_rows", qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, hd,
+                     cap, eps, ntok, stream);
+}
+
+extern "C" int hv_qk_rows_f16(const float* qkv, const float* qn, const float* kn,
+                              const float* cos_t, const float* sin_t, int pos0, float* q_out,
+                              uint16_t* kc, uint16_t* vc, int nq, int nkv, int hd, int cap,
+                              float eps, int ntok, void* stream) {
+  return qk_rows_any("hv_qk_rows_f16", qkv, qn, kn, cos_t, sin_t, pos0, q_out,
+                     reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), nq, nkv, hd,
+                     cap, eps, ntok, stream);
 }
 
 extern "C" int hv_attn_rows_scratch(int nq, int group, int cap, int ntok, size_t* part_bytes,
@@ -345,30 +408,17 @@ extern "C" int hv_attn_rows(const float* q, const float* kc, const float* vc, fl
                             const float* scale, int pos0, int nq, int hd, int group,
                             int kvstride, int ntok, float* part, int32_t* ticket,
                             void* stream) {
-  HV_REQUIRE(q && kc && vc && ctx && scale && part && ticket && nq > 0 && group > 0 &&
-                 ntok > 0 && ntok <= 65535 && pos0 >= 0,
-             HV_E_INVALID, "hv_attn_rows: bad arguments");
-  HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "hv_attn_rows: head_dim %d (only 128)", hd);
-  HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
-             "hv_attn_rows: nq %% group or kvstride %% hd is not zero");
-  HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
-             "hv_attn_rows: group size %d (1, 2, 4 or 8)", group);
-  const int cap = kvstride / hd;
-  HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
-             "hv_attn_rows: positions %d .. %d outside the cache of %d", pos0, pos0 + ntok - 1, cap);
-  int nch = 0;
-  const int rc = rows_attn_chunks(nq / group, cap, &nch);
-  if (rc) return rc;
-  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
-             "hv_attn_rows: %d chunks per kv head (at most %d)", nch, kAttnMaxChunks);
-  cudaStream_t st = (cudaStream_t)stream;
-  int* tk = reinterpret_cast<int*>(ticket);
-  switch (group) {
-    case 1: return launch_attn_rows<1>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    case 2: return launch_attn_rows<2>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    case 4: return launch_attn_rows<4>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    default: return launch_attn_rows<8>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-  }
+  return attn_rows_any("hv_attn_rows", q, kc, vc, ctx, scale, pos0, nq, hd, group, kvstride,
+                       ntok, part, ticket, stream);
+}
+
+extern "C" int hv_attn_rows_f16(const float* q, const uint16_t* kc, const uint16_t* vc,
+                                float* ctx, const float* scale, int pos0, int nq, int hd,
+                                int group, int kvstride, int ntok, float* part,
+                                int32_t* ticket, void* stream) {
+  return attn_rows_any("hv_attn_rows_f16", q, reinterpret_cast<const __half*>(kc),
+                       reinterpret_cast<const __half*>(vc), ctx, scale, pos0, nq, hd, group,
+                       kvstride, ntok, part, ticket, stream);
 }
 
 extern "C" int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void* stream) {

@@ -461,13 +461,15 @@ struct Producer {
     }
   }
 
-  // K rows then V rows [t0, te) of kv head g for one attention work item.
-  HV_DEV void kv(const float* kc, const float* vc, int g, int cap, int t0, int te) {
+  // K rows then V rows [t0, te) of kv head g for one attention work item (KT: the
+  // cache's element type, float or __half).
+  template <class KT>
+  HV_DEV void kv(const KT* kc, const KT* vc, int g, int cap, int t0, int te) {
     for (int pass = 0; pass < 2; ++pass) {
-      const float* base = (pass == 0 ? kc : vc) + (size_t)g * cap * kHd;
+      const KT* base = (pass == 0 ? kc : vc) + (size_t)g * cap * kHd;
       for (int r = t0; r < te && live; r += kSlotRows) {
         const unsigned n = (unsigned)min(kSlotRows, te - r);
-        issue(base + (size_t)r * kHd, n * kHd * 4, nullptr, 0, 0);
+        issue(base + (size_t)r * kHd, n * kHd * (unsigned)sizeof(KT), nullptr, 0, 0);
       }
     }
   }
@@ -484,6 +486,7 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
     }
 }
 
+template <class KT>
 HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int pos,
                     const Ring& R, StepShared& S, int inflight, int evict_first) {
   Producer P(R, S, D.status, inflight, evict_first);
@@ -501,7 +504,8 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
     for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
       int a0, a1, ae;
       attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
-      P.kv(L->kc, L->vc, wi / nch, D.cap, a0, ae);
+      P.kv(reinterpret_cast<const KT*>(L->kc), reinterpret_cast<const KT*>(L->vc), wi / nch,
+           D.cap, a0, ae);
     }
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
@@ -911,14 +915,26 @@ constexpr int kScoreRows = GS >= 8 ? 4 : 8;
 // block that holds only pos): one shared-memory load per cached row (index clamped inside
 // the slot, so no branch precedes it), the pos row loaded once if this group holds it,
 // rows from `tend` on (not this block's) and stale slot rows selected to zero.
-template <int RW>
+// Dims 4 lane .. 4 lane + 3 of row r of a ring slot of cache rows, as floats (half ->
+// float is exact).
+HV_DEV float4 slot_row4(const float*, unsigned slot, int r, int lane) {
+  return lds_f4(slot + (unsigned)(r * kHd + 4 * lane) * 4);
+}
+HV_DEV float4 slot_row4(const __half*, unsigned slot, int r, int lane) {
+  const uint2 w = lds_u2(slot + (unsigned)(r * kHd + 4 * lane) * 2);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <int RW, class KT>
 HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, unsigned slot,
                        int r0, unsigned pos_s, int lane) {
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int p = 0; p < RW; ++p) {
     const int r = min(tb + p - r0, kSlotRows - 1);
-    kv[p] = slot ? lds_f4(slot + (unsigned)(r * kHd + 4 * lane) * 4) : zero;
+    kv[p] = slot ? slot_row4(static_cast<const KT*>(nullptr), slot, r, lane) : zero;
   }
   const bool has_pos = pos >= tb && pos < tb + RW && pos < tend && pos >= te;
   const float4 pv = has_pos ? lds_f4(pos_s + 16 * lane) : zero;
@@ -932,13 +948,13 @@ HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, unsi
 // Scores of positions tb .. tb + kScoreRows - 1 (those below tend) for the GS heads, the
 // arithmetic of attn_chunk in attn_decode.cuh. slot (0: none), kpos_s and lg_s are shared
 // addresses.
-template <int GS>
+template <int GS, class KT>
 HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int te, int pos,
                          unsigned slot, int r0, unsigned kpos_s, float scale, unsigned lg_s) {
   constexpr int RW = kScoreRows<GS>;
   const int lane = threadIdx.x & 31;
   float4 kv[RW];
-  block_rows<RW>(kv, tb, tend, te, pos, slot, r0, kpos_s, lane);
+  block_rows<RW, KT>(kv, tb, tend, te, pos, slot, r0, kpos_s, lane);
   float v[RW * GS];
 #pragma unroll
   for (int p = 0; p < RW; ++p)
@@ -966,14 +982,14 @@ HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int t
 
 // Probability-weighted V rows [tb, tb + 8) (those below tend) into acc, rows in order
 // (the order of attn_chunk); all loads are issued before the first multiply-add.
-template <int GS>
+template <int GS, class KT>
 HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, int pos,
                          unsigned slot, int r0, unsigned vpos_s, unsigned lg_s) {
   constexpr int RW = 8;
   const int lane = threadIdx.x & 31;
   float4 vv[RW];
   float w[RW][GS];
-  block_rows<RW>(vv, tb, tend, te, pos, slot, r0, vpos_s, lane);
+  block_rows<RW, KT>(vv, tb, tend, te, pos, slot, r0, vpos_s, lane);
 #pragma unroll
   for (int p = 0; p < RW; ++p)
 #pragma unroll
@@ -997,7 +1013,10 @@ HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, in
 // through the ring (sequence numbers from *q). Same arithmetic, in the same order, as
 // attn_chunk with eight warps (k_attn): blocks of 20 positions go to warp (block % 8)
 // for the scores and the weighted V sum; warp i takes head i for the max and exp.
-template <int GS, bool kSplitMerge>
+// KT = __half: the compressed-KV lane. This step's k and v rows are rounded to binary16
+// before use, so row pos enters the scores and the V sum exactly as the appended cache
+// row does (hv_kv_append_f16 then hv_attn_decode_f16).
+template <int GS, bool kSplitMerge, class KT>
 __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
                                        const Ring R, unsigned* qp, StepShared& S,
                                        float* area, int tb) {
@@ -1031,19 +1050,25 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       } else if (h == GS) {
         warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, L->kn, cs, sn, D.eps,
                        tmp_s + GS * kHd, kpos_s);
+        if constexpr (kKvHalf<KT>) {
+          float4* k4 = reinterpret_cast<float4*>(kpos_s) + lane;
+          *k4 = round_half4(*k4);
+        }
       } else {
-        reinterpret_cast<float4*>(vpos_s)[lane] =
+        float4 v4 =
             __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
+        if constexpr (kKvHalf<KT>) v4 = round_half4(v4);
+        reinterpret_cast<float4*>(vpos_s)[lane] = v4;
       }
     }
     csync();
     trace_mark(D, tb + 14);
     trace_wait(D, S, tb + 20);
     if (c == nch - 1 && threadIdx.x < kHd) {         // the chunk holding pos appends
-      float* kc = L->kc + (size_t)g * cap * kHd;
-      float* vc = L->vc + (size_t)g * cap * kHd;
-      kc[(size_t)pos * kHd + threadIdx.x] = kpos_s[threadIdx.x];
-      vc[(size_t)pos * kHd + threadIdx.x] = vpos_s[threadIdx.x];
+      KT* kc = reinterpret_cast<KT*>(L->kc) + (size_t)g * cap * kHd;
+      KT* vc = reinterpret_cast<KT*>(L->vc) + (size_t)g * cap * kHd;
+      kc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(kpos_s[threadIdx.x]);
+      vc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(vpos_s[threadIdx.x]);
     }
 
     // ---- scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows, row
@@ -1065,8 +1090,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       }
       const long long c0 = clock64();
       for (int tg = r0; tg < r1; tg += kScoreRows<GS>)
-        group_scores<GS>(qv, tg, r1, t0, te, pos, slot, r0, sh_addr(kpos_s), scale,
-                         sh_addr(lg_s));
+        group_scores<GS, KT>(qv, tg, r1, t0, te, pos, slot, r0, sh_addr(kpos_s), scale,
+                             sh_addr(lg_s));
       if (lane == 0) S.busy[warp] += clock64() - c0;
       if (m < nk) {
         __syncwarp();
@@ -1116,7 +1141,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
         slot = sh_addr(R.slot(q));
       }
       for (int tg = r0; tg < r1; tg += 8)
-        group_values<GS>(acc, tg, r1, t0, te, pos, slot, r0, sh_addr(vpos_s), sh_addr(lg_s));
+        group_values<GS, KT>(acc, tg, r1, t0, te, pos, slot, r0, sh_addr(vpos_s),
+                             sh_addr(lg_s));
       if (m < nk) {
         __syncwarp();
         if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)m), kConsWarps);
@@ -1221,7 +1247,7 @@ __device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
 
 // ---- the kernel ------------------------------------------------------------------------
 
-template <int GS, bool kSplitMerge>
+template <int GS, bool kSplitMerge, class KT>
 __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
                                                           int nslots, int inflight,
                                                           int evict_first) {
@@ -1278,7 +1304,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     return;
   }
   if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
-    if (threadIdx.x == kConsThreads) produce(D, Ls, flags, pos, R, S, inflight, evict_first);
+    if (threadIdx.x == kConsThreads)
+      produce<KT>(D, Ls, flags, pos, R, S, inflight, evict_first);
     return;
   }
 
@@ -1318,7 +1345,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     if (!grid_sync(D, S, (flags & kFlagLocalQkvBarrier) == 0)) return;
     trace_mark(D, tb + 2);
     // P2: attention
-    attn_ring<GS, kSplitMerge>(D, L, pos, R, &q, S, work, tb);
+    attn_ring<GS, kSplitMerge, KT>(D, L, pos, R, &q, S, work, tb);
     trace_mark(D, tb + 3);
     if (!grid_sync(D, S)) return;
     if constexpr (kSplitMerge) {
@@ -1436,20 +1463,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   trace_mark(D, th + 2);
 }
 
-static void* step_fn(int gs, bool split_merge) {
-  if (split_merge) {
+// The step kernel for group size gs: variant 0 = f32 cache, 1 = f32 cache with the split
+// merge, 2 = binary16 cache.
+static void* step_fn(int gs, int variant) {
+  if (variant == 1) {
     switch (gs) {
-      case 1: return (void*)k_step<1, true>;
-      case 2: return (void*)k_step<2, true>;
-      case 4: return (void*)k_step<4, true>;
-      default: return (void*)k_step<8, true>;
+      case 1: return (void*)k_step<1, true, float>;
+      case 2: return (void*)k_step<2, true, float>;
+      case 4: return (void*)k_step<4, true, float>;
+      default: return (void*)k_step<8, true, float>;
+    }
+  }
+  if (variant == 2) {
+    switch (gs) {
+      case 1: return (void*)k_step<1, false, __half>;
+      case 2: return (void*)k_step<2, false, __half>;
+      case 4: return (void*)k_step<4, false, __half>;
+      default: return (void*)k_step<8, false, __half>;
     }
   }
   switch (gs) {
-    case 1: return (void*)k_step<1, false>;
-    case 2: return (void*)k_step<2, false>;
-    case 4: return (void*)k_step<4, false>;
-    default: return (void*)k_step<8, false>;
+    case 1: return (void*)k_step<1, false, float>;
+    case 2: return (void*)k_step<2, false, float>;
+    case 4: return (void*)k_step<4, false, float>;
+    default: return (void*)k_step<8, false, float>;
   }
 }
 
@@ -1585,17 +1622,20 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
                  "hv_step_launch: %zu B of leaf values exceed the work area", need);
     }
   }
-  // the split merge (one GPU): its per-warp chunk weights live in the work area
-  const bool split_merge = g_opt_split_merge && world == 1 &&
+  HV_REQUIRE(h.kv_dtype == HV_KV_F32 || h.kv_dtype == HV_KV_F16, HV_E_INVALID,
+             "hv_step_launch: kv_dtype %d (HV_KV_F32 or HV_KV_F16)", h.kv_dtype);
+  // the split merge (one GPU, f32 cache): its per-warp chunk weights live in the work area
+  const bool split_merge = g_opt_split_merge && world == 1 && h.kv_dtype == HV_KV_F32 &&
       (lay.ring - lay.work) / sizeof(float) >= (size_t)kConsWarps * h.attn_chunks;
-  void* fn = step_fn(gs, split_merge);
+  const int variant = h.kv_dtype == HV_KV_F16 ? 2 : split_merge ? 1 : 0;
+  void* fn = step_fn(gs, variant);
   {
     // set the function's shared-memory limit once per (kernel, device, size)
     static std::mutex mu;
-    static size_t done[8][64];
+    static size_t done[12][64];
     int dev = 0;
     HV_CUDA(cudaGetDevice(&dev));
-    const int gi = (gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3) + (split_merge ? 4 : 0);
+    const int gi = (gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3) + 4 * variant;
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || done[gi][dev] < smem) {
       HV_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

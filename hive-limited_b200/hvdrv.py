@@ -21,7 +21,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 LIB_NAME = "libhive_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _L = None
 _lib_path = None
@@ -82,6 +82,8 @@ _SIGS = {
     "hv_rope": [_VP, _VP, _VP, _VP, _I, _I, _VP],
     "hv_kv_append": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_attn_decode": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
+    "hv_kv_append_f16": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
+    "hv_attn_decode_f16": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_attn_reserve": [_I, _I, _I],
     "hv_attn_decode_noalloc": [_VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_silu_mul": [_VP, _VP, _VP, _I, _VP],
@@ -101,8 +103,10 @@ _SIGS = {
     "hv_gather_rows": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_qa8s_rows": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_qk_rows": [_VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP],
+    "hv_qk_rows_f16": [_VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP],
     "hv_attn_rows_scratch": [_I, _I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
     "hv_attn_rows": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP, _VP],
+    "hv_attn_rows_f16": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP, _VP],
     "hv_silu_rows": [_VP, _VP, _I, _I, _VP],
     "hv_step_config": [_I, _I, _I, _PI, _PI, C.POINTER(_SZ), _PI, C.POINTER(_SZ)],
     "hv_step_launch": [_VP, _I, _VP],
@@ -376,13 +380,16 @@ def rope(vec, cos_t, sin_t, pos, heads, half, stream=0):
     _call("hv_rope", _p(vec), _p(cos_t), _p(sin_t), _p(pos), heads, half, _p(stream))
 
 
-def kv_append(k, v, kc, vc, pos, nkv, hd, cap, stream=0):
-    _call("hv_kv_append", _p(k), _p(v), _p(kc), _p(vc), _p(pos), nkv, hd, cap, _p(stream))
+def kv_append(k, v, kc, vc, pos, nkv, hd, cap, stream=0, f16=False):
+    """f16=True: kc/vc are binary16 caches (hv_kv_append_f16, the compressed-KV lane)."""
+    _call("hv_kv_append_f16" if f16 else "hv_kv_append", _p(k), _p(v), _p(kc), _p(vc), _p(pos),
+          nkv, hd, cap, _p(stream))
 
 
-def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0):
-    _call("hv_attn_decode", _p(q), _p(kc), _p(vc), _p(ctx), _p(scale), _p(pos), nq, hd,
-          group, kvstride, _p(stream))
+def attn_decode(q, kc, vc, ctx, scale, pos, nq, hd, group, kvstride, stream=0, f16=False):
+    """f16=True: kc/vc are binary16 caches (hv_attn_decode_f16)."""
+    _call("hv_attn_decode_f16" if f16 else "hv_attn_decode", _p(q), _p(kc), _p(vc), _p(ctx),
+          _p(scale), _p(pos), nq, hd, group, kvstride, _p(stream))
 
 
 def attn_reserve(nkv, group, cap):
@@ -506,9 +513,10 @@ def qa8s_rows(src, a8, sa, nb, ntok, stream=0):
 
 
 def qk_rows(qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, hd, cap, eps, ntok,
-            stream=0):
-    _call("hv_qk_rows", _p(qkv), _p(qn), _p(kn), _p(cos_t), _p(sin_t), int(pos0), _p(q_out),
-          _p(kc), _p(vc), nq, nkv, hd, cap, C.c_float(eps), ntok, _p(stream))
+            stream=0, f16=False):
+    _call("hv_qk_rows_f16" if f16 else "hv_qk_rows", _p(qkv), _p(qn), _p(kn), _p(cos_t),
+          _p(sin_t), int(pos0), _p(q_out), _p(kc), _p(vc), nq, nkv, hd, cap, C.c_float(eps),
+          ntok, _p(stream))
 
 
 def attn_rows_scratch(nq, group, cap, ntok) -> tuple[int, int]:
@@ -518,9 +526,10 @@ def attn_rows_scratch(nq, group, cap, ntok) -> tuple[int, int]:
 
 
 def attn_rows(q, kc, vc, ctx, scale, pos0, nq, hd, group, kvstride, ntok, part, ticket,
-              stream=0):
-    _call("hv_attn_rows", _p(q), _p(kc), _p(vc), _p(ctx), _p(scale), int(pos0), nq, hd, group,
-          kvstride, ntok, _p(part), _p(ticket), _p(stream))
+              stream=0, f16=False):
+    _call("hv_attn_rows_f16" if f16 else "hv_attn_rows", _p(q), _p(kc), _p(vc), _p(ctx),
+          _p(scale), int(pos0), nq, hd, group, kvstride, ntok, _p(part), _p(ticket),
+          _p(stream))
 
 
 def silu_rows(gu, act, ffn, ntok, stream=0):

@@ -47,7 +47,8 @@ class _StepDesc(C.Structure):
                     "tok", "pos", "step", "gen", "h", "qkv", "ctx", "act", "logits",
                     "part", "ticket", "amax_v", "amax_i", "barrier", "status", "trace",
                     "plans")]
-                + [("world", C.c_int), ("rank", C.c_int), ("peers", C.c_void_p)])
+                + [("world", C.c_int), ("rank", C.c_int), ("peers", C.c_void_p),
+                   ("kv_dtype", C.c_int)])
 
 
 MAX_WORLD = 8
@@ -136,12 +137,18 @@ class Engine:
                            then writes the entry. The entry is keyed by the model
                            directory's files, or by `cache_tag` for `tensors=` sources.
                            `cache_hit` tells which happened (None without a cache).
+      kv_dtype          -- "f32" (default): the reference's fp32 KV cache; "f16": the
+                           compressed-KV lane, an IEEE binary16 cache (half the KV bytes
+                           per step). Each k/v row is rounded to nearest-even binary16 when
+                           appended and attention reads the widened values; the results
+                           then follow the oracle run with that rounding, not the
+                           reference's fp32 cache.
     """
 
     def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
                  config=None, tensors=None, max_context=None, device=0, fused=True,
                  quantize_on="device", world=1, rank=0, exchange=None, weight_cache=None,
-                 cache_tag=None, prefill="steps"):
+                 cache_tag=None, prefill="steps", kv_dtype="f32"):
         if config is None:
             self.cfg = Config.load(model_dir)
         else:
@@ -158,6 +165,10 @@ class Engine:
         if prefill == "batched" and self.world > 1:
             raise ValueError("the batched prefill runs on one GPU (world = 1)")
         self.prefill_mode = prefill
+        if kv_dtype not in ("f32", "f16"):
+            raise ValueError(f"kv_dtype={kv_dtype!r}: 'f32' or 'f16'")
+        self.kv_dtype = kv_dtype
+        self.kv_f16 = kv_dtype == "f16"
         self._pf = None
         self.shard = shard_plan(self.cfg, self.world, self.rank)
         if self.world > 1 and (not self.fused or exchange is None):
@@ -382,10 +393,11 @@ class Engine:
         self.d_logits = self._alloc(self.n_head_rows * 4)
         self.d_a8 = self._alloc(wide)
         self.d_sa = self._alloc(2 * (wide // BLOCK) * 4)
-        # KV cache: f32, one allocation, [layer][k|v][n_kv][cap][hd]
-        self.kv_bytes = 2 * c.n_layer * nkv * cap * qd * 4
+        # KV cache: f32 (or binary16), one allocation, [layer][k|v][n_kv][cap][hd]
+        esz = 2 if self.kv_f16 else 4
+        self.kv_bytes = 2 * c.n_layer * nkv * cap * qd * esz
         self.d_kv = self._alloc(self.kv_bytes)
-        per = nkv * cap * qd * 4
+        per = nkv * cap * qd * esz
         self.KC = [self.d_kv + (2 * l) * per for l in range(c.n_layer)]
         self.VC = [self.d_kv + (2 * l + 1) * per for l in range(c.n_layer)]
         hvdrv.memset8(self.d_kv, 0, self.kv_bytes)
@@ -450,7 +462,7 @@ class Engine:
             self.d_tok, self.d_pos, self.d_step, self.d_gen, self.d_h, self.d_qkv,
             self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
             self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans,
-            self.world, self.rank, self.d_peers)
+            self.world, self.rank, self.d_peers, 1 if self.kv_f16 else 0)
 
     def _connect_peers(self):
         """Swap CUDA IPC handles of the buffers every rank's step writes into (residual,
@@ -512,9 +524,10 @@ class Engine:
             hvdrv.rmsnorm(dk, dk, w["kn"], nkv, qd, RMS_EPS, s)
             hvdrv.rope(dq, self.d_cos, self.d_sin, self.d_pos, nq, qd // 2, s)
             hvdrv.rope(dk, self.d_cos, self.d_sin, self.d_pos, nkv, qd // 2, s)
-            hvdrv.kv_append(dk, dv, self.KC[l], self.VC[l], self.d_pos, nkv, qd, cap, s)
+            hvdrv.kv_append(dk, dv, self.KC[l], self.VC[l], self.d_pos, nkv, qd, cap, s,
+                            f16=self.kv_f16)
             hvdrv.attn_decode(dq, self.KC[l], self.VC[l], self.d_ctx, self.d_scale,
-                              self.d_pos, nq, qd, c.group, cap * qd, s)
+                              self.d_pos, nq, qd, c.group, cap * qd, s, f16=self.kv_f16)
             self._gemv(self.d_ctx, w["o"], self.d_o)
             hvdrv.vadd(self.d_h, self.d_o, self.d_h, hid, s)
             hvdrv.rmsnorm(self.d_h, self.d_hn, w["fn"], 1, hid, RMS_EPS, s)
@@ -743,9 +756,11 @@ class Engine:
                 hvdrv.rmsnorm(pf["h"], pf["hn"], w["an"], m, hid, RMS_EPS, s)
                 self._gemm(pf["hn"], w["qkv"], pf["qkv"], m)
                 hvdrv.qk_rows(pf["qkv"], w["qn"], w["kn"], self.d_cos, self.d_sin, b0, pf["q"],
-                              self.KC[l], self.VC[l], nq, nkv, qd, cap, RMS_EPS, m, s)
+                              self.KC[l], self.VC[l], nq, nkv, qd, cap, RMS_EPS, m, s,
+                              f16=self.kv_f16)
                 hvdrv.attn_rows(pf["q"], self.KC[l], self.VC[l], pf["ctx"], self.d_scale, b0,
-                                nq, qd, c.group, cap * qd, m, pf["part"], pf["ticket"], s)
+                                nq, qd, c.group, cap * qd, m, pf["part"], pf["ticket"], s,
+                                f16=self.kv_f16)
                 self._gemm(pf["ctx"], w["o"], pf["o"], m)
                 hvdrv.vadd(pf["h"], pf["o"], pf["h"], m * hid, s)
                 hvdrv.rmsnorm(pf["h"], pf["hn"], w["fn"], m, hid, RMS_EPS, s)

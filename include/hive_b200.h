@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define HV_ABI_VERSION 2
+#define HV_ABI_VERSION 3
 
 #define HV_OK 0
 #define HV_E_INVALID 1001      /* bad argument (null pointer, size, alignment) */
@@ -170,6 +170,15 @@ int hv_attn_rows(const float* q, const float* kc, const float* vc, float* ctx,
                  const float* scale, int pos0, int nq, int hd, int group, int kvstride,
                  int ntok, float* part, int32_t* ticket, void* stream);
 int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void* stream);
+/* hv_qk_rows and hv_attn_rows over a binary16 cache (the compressed-KV lane; see
+ * hv_kv_append_f16): K and V rows are stored rounded to nearest-even binary16, and
+ * attention reads the widened values. */
+int hv_qk_rows_f16(const float* qkv, const float* qn, const float* kn, const float* cos_t,
+                   const float* sin_t, int pos0, float* q_out, uint16_t* kc, uint16_t* vc,
+                   int nq, int nkv, int hd, int cap, float eps, int ntok, void* stream);
+int hv_attn_rows_f16(const float* q, const uint16_t* kc, const uint16_t* vc, float* ctx,
+                     const float* scale, int pos0, int nq, int hd, int group, int kvstride,
+                     int ntok, float* part, int32_t* ticket, void* stream);
 /* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split
  * kernel, 0 runs every matrix on the one-warp-per-tile kernel. Process-wide. */
 int hv_gemv_set_split(int enable);
@@ -198,6 +207,18 @@ int hv_kv_append(const float* k, const float* v, float* kc, float* vc, const int
 int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
                    const float* scale, const int32_t* pos, int nq, int hd, int group,
                    int kvstride, void* stream);
+/* The compressed-KV lane (no counterpart in the reference, which keeps an f32 cache;
+ * engine/limited.py:323-325 names the fp32 KV as the engine's sharpest limitation): the
+ * cache holds IEEE binary16 values [nkv][cap][hd] (half the bytes). hv_kv_append_f16
+ * stores f16(k), f16(v) rounded to nearest-even (numpy's astype(float16)); then
+ * hv_attn_decode_f16 computes exactly what hv_attn_decode computes over an f32 cache that
+ * holds those f16 values widened (same chunking, same arithmetic). */
+int hv_kv_append_f16(const float* k, const float* v, uint16_t* kc, uint16_t* vc,
+                     const int32_t* pos, int nkv, int hd, int cap, void* stream);
+int hv_attn_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, float* ctx,
+                       const float* scale, const int32_t* pos, int nq, int hd, int group,
+                       int kvstride, void* stream);
+
 /* Makes sure the attention scratch can serve nkv heads at a cache of `cap` positions. */
 int hv_attn_reserve(int nkv, int group, int cap);
 
@@ -285,7 +306,9 @@ typedef struct hv_layer_w {
   const uint32_t* dn_b4;  const float* dn_sw;    /* hidden rows, K = ffn           */
   const float* an; const float* fn;              /* input / post-attention norms   */
   const float* qn; const float* kn;              /* per-head q / k norms [hd]      */
-  float* kc; float* vc;                          /* KV cache [n_kv][cap][hd] f32   */
+  float* kc; float* vc;                          /* KV cache [n_kv][cap][hd]: f32, or
+                                                    binary16 when the step's kv_dtype
+                                                    is HV_KV_F16                     */
 } hv_layer_w;
 
 typedef struct hv_step_desc {
@@ -325,7 +348,15 @@ typedef struct hv_step_desc {
    * grid barrier spans all ranks' CTAs, so the all-gathers are part of the kernel. */
   int world, rank;
   const struct hv_step_peers* peers;   /* device pointer (world > 1) */
+  /* Element type of every layer's kc/vc: HV_KV_F32 (0, the reference's cache) or
+   * HV_KV_F16 (the compressed-KV lane: this step's k and v rows are rounded to binary16,
+   * appended as such, and attention reads every row as the widened binary16 value --
+   * the arithmetic of hv_kv_append_f16 followed by hv_attn_decode_f16). */
+  int kv_dtype;
 } hv_step_desc;
+
+#define HV_KV_F32 0
+#define HV_KV_F16 1
 
 #define HV_MAX_WORLD 8
 /* Every rank's copies of the exchanged buffers (device pointers valid on this rank:
@@ -381,8 +412,9 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);
 #define HV_STEP_OPT_INFLIGHT 1
 #define HV_STEP_OPT_EVICT_FIRST 2
 #define HV_STEP_OPT_LOCAL_QKV_BARRIER 3
-/* HV_STEP_OPT_SPLIT_MERGE: on one GPU, merge the attention partials as a phase of their
- * own, one warp per 32-value block of ctx, after a grid barrier (0/1, default 0). */
+/* HV_STEP_OPT_SPLIT_MERGE: on one GPU with the f32 cache, merge the attention partials as
+ * a phase of their own, one warp per 32-value block of ctx, after a grid barrier (0/1,
+ * default 0; steps over a binary16 cache ignore it). */
 #define HV_STEP_OPT_SPLIT_MERGE 4
 int hv_step_set_option(int option, int value);
 

@@ -13,6 +13,11 @@ the reference's own engine/reference.py in the build container
   residual add, the embedding gather and argmax;
 * exp-based ops (silu_mul, attention) call np.exp and a BLAS dot like the reference, so
   they match it bit for bit on the same host; the GPU is held to a tolerance there.
+
+The compressed-KV lane (kv_round, OracleModel(kv_dtype="f16")) has no counterpart in the
+reference: it is the reference's step with each appended k/v row rounded to binary16.
+Its rounding is numpy's float32 -> float16 conversion, checked against Python's own
+IEEE binary16 packing (struct format 'e') in tests/test_kv16.py.
 """
 from __future__ import annotations
 
@@ -230,15 +235,31 @@ def argmax(logits) -> int:
 # the model step (engine/reference.py:121-225)
 # ---------------------------------------------------------------------------
 
+def kv_round(x: np.ndarray, kv_dtype: str) -> np.ndarray:
+    """A k or v row as the cache holds it: unchanged for "f32"; for "f16" rounded to
+    binary16 (round to nearest, ties to even; overflow to infinity) and widened back."""
+    if kv_dtype == "f16":
+        return x.astype(np.float16).astype(F32)
+    return x
+
+
 class OracleModel:
     """CPU forward of the whole decode step over already-quantised weights.
 
     `w` maps: "emb16" f16 [V, hid]; per layer l: f"{l}.an|fn|qn|kn" f32 gains and
     f"{l}.qkv|o|gu|down" -> (packed, scale, K); "onorm"; "head" -> (packed, scale, K).
     qkv rows are [q | k | v] and gu rows are [gate | up], as the reference fuses them.
+
+    kv_dtype "f16" is the compressed-KV lane, which the reference does not have: each k
+    and v row is rounded to IEEE binary16 (nearest, ties to even: numpy's astype) when it
+    is appended, and attention (engine/reference.py:104-118, unchanged) reads the widened
+    values. The caches stay float32 arrays holding those values.
     """
 
-    def __init__(self, cfg, w: dict, max_context: int, eps=RMS_EPS):
+    def __init__(self, cfg, w: dict, max_context: int, eps=RMS_EPS, kv_dtype="f32"):
+        if kv_dtype not in ("f32", "f16"):
+            raise ValueError(f"kv_dtype={kv_dtype!r}")
+        self.kv_dtype = kv_dtype
         self.cfg, self.w, self.cap, self.eps = cfg, w, max_context, F32(eps)
         self.cos, self.sin = rope_tables(max_context, cfg.head_dim, cfg.rope_theta)
         self._qw = {}
@@ -269,8 +290,8 @@ class OracleModel:
             kk = rmsnorm(kk, self.w[f"{l}.kn"], self.eps)
             q = rope(q, pos, self.cos, self.sin)
             kk = rope(kk, pos, self.cos, self.sin)
-            self.KC[l][:, pos, :] = kk
-            self.VC[l][:, pos, :] = v
+            self.KC[l][:, pos, :] = kv_round(kk, self.kv_dtype)
+            self.VC[l][:, pos, :] = kv_round(v, self.kv_dtype)
             ctx = attention(q, self.KC[l], self.VC[l], pos, c.group,
                             1.0 / np.sqrt(qd)).reshape(-1)
             h = (h + self._gemv(f"{l}.o", ctx)).astype(F32)

@@ -66,16 +66,45 @@ def test_manifest_matches_library():
     assert man["arch"] == "sm_100a"
 
 
-def test_step_desc_layout_matches_header():
-    """The ctypes mirror of hv_step_desc / hv_layer_w has the C layout."""
+def test_step_desc_layout_matches_header(tmp_path):
+    """The ctypes mirror of hv_step_desc / hv_layer_w / hv_step_peers has the C layout:
+    every field's offset and each struct's size as the C compiler lays out the header."""
+    import shutil
+    import subprocess
     import limited
     assert ctypes.sizeof(limited._LayerW) == 14 * 8
-    # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers
+    # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers, world, rank, peers, kv_dtype
     assert limited._StepDesc.layers.offset == 48
     assert limited._StepDesc.world.offset == 48 + 24 * 8
     assert limited._StepDesc.peers.offset == 48 + 24 * 8 + 8
-    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 16
+    assert limited._StepDesc.kv_dtype.offset == 48 + 24 * 8 + 16
+    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 24
     assert ctypes.sizeof(limited._StepPeers) == 5 * 8 * 8
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler for the header's own layout")
+    structs = [("hv_step_desc", limited._StepDesc), ("hv_layer_w", limited._LayerW),
+               ("hv_step_peers", limited._StepPeers)]
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "hive_b200.h"',
+             'int main(void) {']
+    for cname, py in structs:
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ['  return 0;', '}']
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], capture_output=True, text=True,
+                             check=True).stdout.splitlines():
+        cname, field, val = ln.split()
+        got[(cname, field)] = int(val)
+    for cname, py in structs:
+        assert got[(cname, "sizeof")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, (cname, f)
 
 
 def test_gpu_only_paths_fail_loudly_without_gpu():

@@ -122,31 +122,33 @@ class FakeDevice:
         self._gemm(a8, sa, pb4, psw, dst, k8, rows, pair, 1)
 
     def qk_rows(self, qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, hd, cap, eps,
-                ntok, stream=0):
-        self.calls.append("qk_rows")
+                ntok, stream=0, f16=False):
+        self.calls.append("qk_rows_f16" if f16 else "qk_rows")
+        kt = np.float16 if f16 else F32
         rows = self.view(qkv, F32, ntok * (nq + 2 * nkv) * hd).reshape(ntok, -1)
         cs = self.view(cos_t, F32, cap * hd // 2).reshape(cap, hd // 2)
         sn = self.view(sin_t, F32, cap * hd // 2).reshape(cap, hd // 2)
         qo = self.view(q_out, F32, ntok * nq * hd).reshape(ntok, nq, hd)
-        K = self.view(kc, F32, nkv * cap * hd).reshape(nkv, cap, hd)
-        V = self.view(vc, F32, nkv * cap * hd).reshape(nkv, cap, hd)
+        K = self.view(kc, kt, nkv * cap * hd).reshape(nkv, cap, hd)
+        V = self.view(vc, kt, nkv * cap * hd).reshape(nkv, cap, hd)
         gq, gk = self.view(qn, F32, hd), self.view(kn, F32, hd)
         for t in range(ntok):
             pos = pos0 + t
             r = rows[t]
             qo[t] = O.rope(O.rmsnorm(r[:nq * hd].reshape(nq, hd), gq, F32(eps)), pos, cs, sn)
             K[:, pos] = O.rope(O.rmsnorm(r[nq * hd:(nq + nkv) * hd].reshape(nkv, hd), gk,
-                                         F32(eps)), pos, cs, sn)
-            V[:, pos] = r[(nq + nkv) * hd:].reshape(nkv, hd)
+                                         F32(eps)), pos, cs, sn).astype(kt)
+            V[:, pos] = r[(nq + nkv) * hd:].reshape(nkv, hd).astype(kt)
 
     def attn_rows(self, q, kc, vc, ctx, scale, pos0, nq, hd, group, kvstride, ntok, part,
-                  ticket, stream=0):
-        self.calls.append("attn_rows")
+                  ticket, stream=0, f16=False):
+        self.calls.append("attn_rows_f16" if f16 else "attn_rows")
+        kt = np.float16 if f16 else F32
         cap = kvstride // hd
         nkv = nq // group
         Q = self.view(q, F32, ntok * nq * hd).reshape(ntok, nq, hd)
-        K = self.view(kc, F32, nkv * cap * hd).reshape(nkv, cap, hd)
-        V = self.view(vc, F32, nkv * cap * hd).reshape(nkv, cap, hd)
+        K = self.view(kc, kt, nkv * cap * hd).reshape(nkv, cap, hd).astype(F32)
+        V = self.view(vc, kt, nkv * cap * hd).reshape(nkv, cap, hd).astype(F32)
         C = self.view(ctx, F32, ntok * nq * hd).reshape(ntok, nq, hd)
         sc = float(self.view(scale, F32, 1)[0])
         for t in range(ntok):
@@ -174,11 +176,12 @@ class FakeDevice:
         self.view(pos, np.int32, 1)[0] += 1
 
 
-def fake_engine(dev, cfg, w, cap, fused):
+def fake_engine(dev, cfg, w, cap, fused, kv_dtype="f32"):
     """An Engine whose device state lives on the fake device (constructor bypassed)."""
     c = cfg
     eng = object.__new__(limited.Engine)
     eng.cfg, eng.fused, eng.prefill_mode = c, fused, "batched"
+    eng.kv_dtype, eng.kv_f16 = kv_dtype, kv_dtype == "f16"
     eng.world, eng.rank, eng._pf, eng._buffers, eng._stream_cur = 1, 0, None, [], 0
     eng.quiet = True
 
@@ -212,7 +215,7 @@ def fake_engine(dev, cfg, w, cap, fused):
     eng.d_tok, eng.d_pos, eng.d_step = dev.alloc(4), dev.alloc(4), dev.alloc(4)
     eng.d_gen = dev.alloc((cap + 1) * 4)
     eng.d_pv, eng.d_pi = dev.alloc(512), dev.alloc(512)
-    per = c.n_kv * cap * qd * 4
+    per = c.n_kv * cap * qd * (2 if eng.kv_f16 else 4)
     eng.kv_bytes = 2 * c.n_layer * per
     eng.d_kv = dev.alloc(eng.kv_bytes)
     eng.KC = [eng.d_kv + 2 * l * per for l in range(c.n_layer)]
@@ -220,8 +223,10 @@ def fake_engine(dev, cfg, w, cap, fused):
     return eng
 
 
-@pytest.mark.parametrize("fused", [False, True])
-def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused):
+@pytest.mark.parametrize("fused,kv_dtype", [(False, "f32"), (True, "f32"), (True, "f16")])
+def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused, kv_dtype):
+    """kv_dtype "f16": the compressed-KV lane's prefill against the oracle run with the
+    same binary16 cache rounding."""
     arch = synth.tiny_arch(n_layer=2, hidden=256, ffn=512, n_head=4, n_kv=2, vocab=1000)
     cfg = Config(arch)
     cap = 320
@@ -230,20 +235,23 @@ def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused):
     prompt = synth.prompt_ids(cfg, 5, 300)
     dev = FakeDevice()
     monkeypatch.setattr(limited, "hvdrv", dev)
-    eng = fake_engine(dev, cfg, w, cap, fused)
+    eng = fake_engine(dev, cfg, w, cap, fused, kv_dtype)
     eng._prefill_batched(prompt, argmax=True)
     assert dev.calls.count("gather_rows") == 2               # 256 + 44 tokens
+    sfx = "_f16" if kv_dtype == "f16" else ""
+    assert dev.calls.count("qk_rows" + sfx) == dev.calls.count("attn_rows" + sfx) == 4
 
-    m = O.OracleModel(cfg, w, cap)
+    m = O.OracleModel(cfg, w, cap, kv_dtype=kv_dtype)
     logits = None
     for i, tok in enumerate(prompt):
         logits = m.step(tok, i, head=(i == len(prompt) - 1))
     got = dev.view(eng.d_logits, F32, cfg.vocab)
     assert np.array_equal(got.view(np.uint32), logits.view(np.uint32))
     per = cfg.n_kv * cap * cfg.head_dim
+    kt = np.float16 if kv_dtype == "f16" else F32
     for l in range(cfg.n_layer):
-        K = dev.view(eng.KC[l], F32, per).reshape(cfg.n_kv, cap, cfg.head_dim)
-        V = dev.view(eng.VC[l], F32, per).reshape(cfg.n_kv, cap, cfg.head_dim)
+        K = dev.view(eng.KC[l], kt, per).reshape(cfg.n_kv, cap, cfg.head_dim).astype(F32)
+        V = dev.view(eng.VC[l], kt, per).reshape(cfg.n_kv, cap, cfg.head_dim).astype(F32)
         assert np.array_equal(K.view(np.uint32), m.KC[l].view(np.uint32)), l
         assert np.array_equal(V.view(np.uint32), m.VC[l].view(np.uint32)), l
     tok, pos, step = (int(dev.view(p, np.int32, 1)[0]) for p in (eng.d_tok, eng.d_pos,
