@@ -534,16 +534,22 @@ def run_gemv_sweep(args, dist: Dist):
         nib, scb = hvdrv.w4_prepacked_size(n, k, 0)
         pb4, psw = dev(nib), dev(scb)
         hvdrv.w4_prepack(b4, sw, n, k, 0, pb4, psw)
+        qb4, qsw = dev(nib), dev(scb)
+        hvdrv.w4_prepack_dq(b4, sw, n, k, 0, qb4, qsw)
         ad, a8, sa, y = dev(k * 4), dev(k), dev(nb * 8), dev(n * 4)
         hvdrv.upload(ad, a.ctypes.data, a.nbytes)
         hvdrv.qa8s(ad, a8, sa, nb)
         copies = max(1, -(-(args.gemv_rotate_mb << 20) // alg)) if args.gemv_rotate_mb else 1
-        rot_pp, rot_ref = [(pb4, psw)], [(b4, sw)]
+        rot_pp, rot_ref, rot_dq = [(pb4, psw)], [(b4, sw)], [(qb4, qsw)]
         for _ in range(copies - 1):
             p, s = dev(nib), dev(scb)
             hvdrv.copy_async(p, pb4, nib)
             hvdrv.copy_async(s, psw, scb)
             rot_pp.append((p, s))
+            p, s = dev(nib), dev(scb)
+            hvdrv.copy_async(p, qb4, nib)
+            hvdrv.copy_async(s, qsw, scb)
+            rot_dq.append((p, s))
             p, s = dev(n * k // 2), dev(n * nb * 4)
             hvdrv.copy_async(p, b4, n * k // 2)
             hvdrv.copy_async(s, sw, n * nb * 4)
@@ -556,7 +562,21 @@ def run_gemv_sweep(args, dist: Dist):
         def ref(c):
             hvdrv.a4gv(a8, sa, rot_ref[c][0], rot_ref[c][1], y, k // 8, n)
 
+        def dq(c):
+            hvdrv.a4gv_dq(a8, sa, rot_dq[c][0], rot_dq[c][1], y, k // 8, n, 0)
+
+        # the dp4a kernel's output against the tensor-pipe kernel's, bit for bit
+        y_pp, y_dq = np.empty(n, np.float32), np.empty(n, np.float32)
+        pp(0)
+        hvdrv.synchronize()
+        hvdrv.download(y_pp.ctypes.data, y, y_pp.nbytes)
+        dq(0)
+        hvdrv.synchronize()
+        hvdrv.download(y_dq.ctypes.data, y, y_dq.nbytes)
+        same = bool(np.array_equal(y_pp.view(np.uint32), y_dq.view(np.uint32)))
+
         for kernel, layout, launch in (("k_a4gv_pp", "tile-interleaved (engine)", pp),
+                                       ("k_a4gv_dq", "dq tiles, dp4a block dots", dq),
                                        ("k_a4gv_mma", "row-major (reference)", ref)):
             for i in range(max(3, copies)):
                 launch(i % copies)
@@ -574,6 +594,7 @@ def run_gemv_sweep(args, dist: Dist):
                 "unit": "GB/s", "us_per_launch": us, "bytes_per_launch": alg,
                 "frac": gbs / peak, "peak": peak, "peak_kind": peak_kind,
                 "launches": args.gemv_reps,
+                **({"bit_identical_to_pp": same} if kernel == "k_a4gv_dq" else {}),
                 "l2": f"{copies} rotating weight copies ({copies * alg / 2**20:.0f} MB)"}),
                 flush=True)
         for p in bufs:

@@ -250,6 +250,116 @@ HV_DEV void gemv_tile8(const uint32_t* __restrict__ r, const float* __restrict__
   }
 }
 
+// ---- the dp4a form over the "dq" tile layout -------------------------------------------
+//
+// The same 8-row tiles and 8-block iterations as the tile-interleaved layout, with the
+// words of each iteration arranged so that lane L = 4g + t holds ALL four words of its own
+// two blocks: words 0..3 of block 2t of row g at 4L, of block 2t+1 at 128 + 4L (scales as
+// before: the pair at 2L). A lane then forms its two exact int32 block dots with dp4a
+// (block_dot), no tensor-pipe MMA and no selection among MMA outputs; the accumulators,
+// their order and the combine are those of gemv_tile8, so the fp32 results are
+// bit-identical to the tile-interleaved kernels.
+constexpr int kDqNibWords = kPpNibWords;   // per tile and iteration
+constexpr int kDqScales = kPpScales;
+
+struct DqLoads {
+  uint4 e, o;    // words 0..3 of blocks 2t and 2t+1
+  float2 s;      // their scales
+};
+
+HV_DEV void dq_load(DqLoads& L, const uint32_t* tn, const float* ts, int it, int lane) {
+  L.e = ldg_stream128(tn + (size_t)it * kDqNibWords + 4 * lane);
+  L.o = ldg_stream128(tn + (size_t)it * kDqNibWords + 128 + 4 * lane);
+  L.s = ldg_stream_f2(ts + (size_t)it * kDqScales + 2 * lane);
+}
+
+// Block terms of iteration `it` for lane (g, t): blocks 2t (x) and 2t+1 (y); blocks at or
+// beyond nvalid count zero. q: int8 activations, 2 x uint4 per block; sb: (scale bits,
+// block sum) per block.
+HV_DEV float2 dq_terms(const DqLoads& L, const uint4* __restrict__ q,
+                       const int2* __restrict__ sb, int it, int t, int nvalid) {
+  const int be = it * 8 + 2 * t;
+  float ce = 0.f, co = 0.f;
+  if (2 * t < nvalid) {
+    const int2 s2 = sb[be];
+    const int d = block_dot(L.e, q[2 * be], q[2 * be + 1], s2.y);
+    ce = __fmul_rn(__fmul_rn(L.s.x, __int_as_float(s2.x)), i2f_exact(d));
+  }
+  if (2 * t + 1 < nvalid) {
+    const int2 s2 = sb[be + 1];
+    const int d = block_dot(L.o, q[2 * be + 2], q[2 * be + 3], s2.y);
+    co = __fmul_rn(__fmul_rn(L.s.y, __int_as_float(s2.x)), i2f_exact(d));
+  }
+  return make_float2(ce, co);
+}
+
+// gemv_tile8<U, true, true> over the dq layout: the 8 rows of one tile, every leaf, the
+// quad's y = (+0) + pairwise over all blocks.
+template <int U>
+HV_DEV float gemv_tile8_dq(const uint32_t* __restrict__ tn, const float* __restrict__ ts,
+                           const uint4* __restrict__ q, const int2* __restrict__ sb,
+                           const GvPlan& P) {
+  const int lane = threadIdx.x & 31;
+  const int t = lane & 3;
+  const int it_hi = P.nfull;
+  DqLoads L[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    if (u < it_hi) dq_load(L[u], tn, ts, u, lane);
+
+  float st[8];               // fold stack (postfix '+' of numpy's recursion)
+  int sp = 0;
+  int leaf = 0;
+  int leaf_begin = 0;
+  int leaf_end = P.it_end[0];
+  float acc_e = 0.f, acc_o = 0.f;   // accumulators 2t, 2t+1
+
+  for (int it0 = 0; it0 < it_hi; it0 += U) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + u;
+      if (it < it_hi) {
+        const float2 c = dq_terms(L[u], q, sb, it, t, 8);
+        if (it == leaf_begin) {
+          acc_e = c.x;
+          acc_o = c.y;
+        } else {
+          acc_e = __fadd_rn(acc_e, c.x);
+          acc_o = __fadd_rn(acc_o, c.y);
+        }
+        const int itn = it + U;
+        if (itn < it_hi) dq_load(L[u], tn, ts, itn, lane);
+        if (it + 1 == leaf_end && leaf + 1 < P.nleaf) {
+          st[sp++] = quad_fold(acc_e, acc_o);        // a leaf that is not the last
+          for (int k = 0; k < P.pops[leaf]; ++k) {
+            --sp;
+            st[sp - 1] = __fadd_rn(st[sp - 1], st[sp]);
+          }
+          ++leaf;
+          leaf_begin = leaf_end;
+          leaf_end = P.it_end[leaf];
+        }
+      }
+    }
+  }
+  float v = (it_hi > leaf_begin) ? quad_fold(acc_e, acc_o) : 0.f;
+  if (P.ntail > 0) {                 // the n % 8 tail blocks, in order (last leaf only)
+    DqLoads T;
+    dq_load(T, tn, ts, P.nfull, lane);
+    const float2 c = dq_terms(T, q, sb, P.nfull, t, P.ntail);
+    for (int j = 0; j < P.ntail; ++j) {
+      const float x = __shfl_sync(0xFFFFFFFFu, (j & 1) ? c.y : c.x, (lane & ~3) | (j >> 1));
+      v = __fadd_rn(v, x);
+    }
+  }
+  st[sp++] = v;
+  for (int k = 0; k < P.pops[P.nleaf - 1]; ++k) {
+    --sp;
+    st[sp - 1] = __fadd_rn(st[sp - 1], st[sp]);
+  }
+  return __fadd_rn(0.0f, st[0]);
+}
+
 // Folds a row's leaf values leafv[0 .. nleaf) with the plan's postfix '+'.
 HV_DEV float fold_leaves(const GvPlan& P, const float* leafv) {
   float st[8];

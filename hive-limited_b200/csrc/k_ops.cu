@@ -146,6 +146,59 @@ __global__ void k_w4_prepack(const uint32_t* __restrict__ b4, const float* __res
   ds[2 * lane + 1] = (ok && b0 + 1 < nb) ? sw[(size_t)row * nb + b0 + 1] : 0.f;
 }
 
+// The dq arrangement of the same tiles (gemv_tile8_dq): lane L = 4g + t of iteration `it`
+// gets words 0..3 of blocks 8 it + 2t (at 4L) and 8 it + 2t + 1 (at 128 + 4L) of row g;
+// the scales as in k_w4_prepack. Blocks past nb are zero.
+__global__ void k_w4_prepack_dq(const uint32_t* __restrict__ b4, const float* __restrict__ sw,
+                                int rows, int nb, int pair_ffn, int ntile, int niter,
+                                uint32_t* __restrict__ pb4, float* __restrict__ psw) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)ntile * niter * 32) return;
+  const int lane = (int)(idx & 31);
+  const long long rest = idx >> 5;
+  const int it = (int)(rest % niter), tile = (int)(rest / niter);
+  const int g = lane >> 2, t = lane & 3;
+  bool ok;
+  const int row = pp_row(tile, g, rows, pair_ffn, &ok);
+  const int be = it * 8 + 2 * t;
+  const uint4* src = reinterpret_cast<const uint4*>(b4) + (size_t)row * nb;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  const uint4 e = (ok && be < nb) ? src[be] : zero;
+  const uint4 o = (ok && be + 1 < nb) ? src[be + 1] : zero;
+  uint32_t* dn = pb4 + ((size_t)tile * niter + it) * kDqNibWords;
+  reinterpret_cast<uint4*>(dn)[lane] = e;
+  reinterpret_cast<uint4*>(dn + 128)[lane] = o;
+  float* ds = psw + ((size_t)tile * niter + it) * kDqScales;
+  ds[2 * lane] = (ok && be < nb) ? sw[(size_t)row * nb + be] : 0.f;
+  ds[2 * lane + 1] = (ok && be + 1 < nb) ? sw[(size_t)row * nb + be + 1] : 0.f;
+}
+
+// GEMV over the dq layout with dp4a block dots, one warp per tile (k_a4gv_pp's schedule);
+// results bit-identical to k_a4gv_pp on the same matrix.
+__global__ void __launch_bounds__(256) k_a4gv_dq(const int8_t* __restrict__ a8,
+                                                 const float* __restrict__ sa,
+                                                 const uint32_t* __restrict__ pb4,
+                                                 const float* __restrict__ psw,
+                                                 float* __restrict__ dst, int rows, int pair_ffn,
+                                                 const __grid_constant__ GvPlan plan) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int nb = plan.nb;
+  uint4* q_s = reinterpret_cast<uint4*>(smem);
+  int2* sb_s = reinterpret_cast<int2*>(smem + (size_t)nb * 32);
+  load_act_smem(a8, sa, nb, q_s, sb_s);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int ntile = pp_tiles(rows, pair_ffn), niter = pp_iters(nb);
+  const int wpb = blockDim.x >> 5;
+  for (int tile = blockIdx.x * wpb + (threadIdx.x >> 5); tile < ntile; tile += gridDim.x * wpb) {
+    bool ok;
+    const int row = pp_row(tile, g, rows, pair_ffn, &ok);
+    const float y = gemv_tile8_dq<8>(pb4 + (size_t)tile * niter * kDqNibWords,
+                                     psw + (size_t)tile * niter * kDqScales, q_s, sb_s, plan);
+    if (t == 0 && ok) dst[row] = y;
+  }
+}
+
 // GEMV over the tile-interleaved layout, one warp per tile; with pair_ffn > 0 the output
 // keeps the reference order [gate | up].
 __global__ void __launch_bounds__(256) k_a4gv_pp(const int8_t* __restrict__ a8,
@@ -647,7 +700,7 @@ extern "C" {
 
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
-      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_w4_prepack,k_rmsnorm,k_rope,k_kvapp,k_kvapp16,k_attn,k_silu,k_vadd,k_gather,"
+      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_a4gv_dq,k_w4_prepack,k_w4_prepack_dq,k_rmsnorm,k_rope,k_kvapp,k_kvapp16,k_attn,k_silu,k_vadd,k_gather,"
       "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp,k_gather_rows,k_qa8s_rows,k_qk_rows,k_attn_rows,k_silu_rows";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
@@ -767,6 +820,50 @@ int hv_a4gv_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const flo
   k_a4gv_pp<<<grid, 256, smem, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, rows, pair_ffn,
                                                        plan);
   HV_LAUNCHED("k_a4gv_pp");
+}
+
+int hv_w4_prepack_dq(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
+                     uint32_t* pb4, float* psw, void* stream) {
+  HV_REQUIRE(b4 && sw && pb4 && psw && rows > 0 && k > 0 && k % kBlock == 0, HV_E_INVALID,
+             "hv_w4_prepack_dq: bad arguments");
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_w4_prepack_dq: a paired matrix has 2 * pair_ffn rows");
+  HV_REQUIRE(((uintptr_t)b4 & 15) == 0 && ((uintptr_t)pb4 & 15) == 0 &&
+                 ((uintptr_t)psw & 15) == 0,
+             HV_E_INVALID, "hv_w4_prepack_dq: pointers must be 16-byte aligned");
+  const int nb = k / kBlock;
+  const int ntile = pp_tiles(rows, pair_ffn), niter = pp_iters(nb);
+  const long long threads = (long long)ntile * niter * 32;
+  k_w4_prepack_dq<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      b4, sw, rows, nb, pair_ffn, ntile, niter, pb4, psw);
+  HV_LAUNCHED("k_w4_prepack_dq");
+}
+
+int hv_a4gv_dq(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+               float* dst, int k8, int rows, int pair_ffn, void* stream) {
+  HV_REQUIRE(a8 && sa && pb4 && psw && dst && k8 > 0 && rows > 0, HV_E_INVALID,
+             "hv_a4gv_dq: bad arguments");
+  HV_REQUIRE(k8 % 4 == 0, HV_E_INVALID, "hv_a4gv_dq: K = %d is not a multiple of 32", k8 * 8);
+  HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
+             "hv_a4gv_dq: a paired matrix has 2 * pair_ffn rows");
+  HV_REQUIRE(((uintptr_t)a8 & 15) == 0 && ((uintptr_t)pb4 & 15) == 0 &&
+                 ((uintptr_t)psw & 15) == 0, HV_E_INVALID, "hv_a4gv_dq: unaligned pointer");
+  const int nb = k8 / 4;
+  HV_REQUIRE(nb <= 4096, HV_E_UNSUPPORTED, "hv_a4gv_dq: K = %d exceeds 131072", k8 * 8);
+  GvPlan plan;
+  HV_REQUIRE(gv_make_plan(nb, &plan), HV_E_UNSUPPORTED, "hv_a4gv_dq: no reduction plan for K");
+  const size_t smem = (size_t)nb * 40;
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  const int ntile = pp_tiles(rows, pair_ffn);
+  int grid = (ntile + 7) / 8;
+  if (grid > sms * 4) grid = sms * 4;
+  rc = smem_attr((const void*)k_a4gv_dq, smem);
+  if (rc) return rc;
+  k_a4gv_dq<<<grid, 256, smem, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, rows, pair_ffn,
+                                                       plan);
+  HV_LAUNCHED("k_a4gv_dq");
 }
 
 int hv_gemv_set_split(int enable) {

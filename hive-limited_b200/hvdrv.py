@@ -98,6 +98,8 @@ _SIGS = {
     "hv_w4_prepacked_size": [_I, _I, _I, C.POINTER(_SZ), C.POINTER(_SZ)],
     "hv_w4_prepack": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
     "hv_a4gv_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
+    "hv_w4_prepack_dq": [_VP, _VP, _I, _I, _I, _VP, _VP, _VP],
+    "hv_a4gv_dq": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_gemv_set_split": [_I],
     "hv_a4gemm_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_gather_rows": [_VP, _VP, _VP, _I, _I, _VP],
@@ -488,6 +490,17 @@ def w4_prepack(b4, sw, rows, k, pair_ffn, pb4, psw, stream=0):
 
 def a4gv_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn=0, stream=0):
     _call("hv_a4gv_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
+          _p(stream))
+
+
+def w4_prepack_dq(b4, sw, rows, k, pair_ffn, pb4, psw, stream=0):
+    """The dq arrangement of the tiles (sizes as w4_prepacked_size) for a4gv_dq."""
+    _call("hv_w4_prepack_dq", _p(b4), _p(sw), rows, k, pair_ffn, _p(pb4), _p(psw), _p(stream))
+
+
+def a4gv_dq(a8, sa, pb4, psw, dst, k8, rows, pair_ffn=0, stream=0):
+    """a4gv_pp with dp4a block dots over the dq arrangement (bit-identical results)."""
+    _call("hv_a4gv_dq", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
           _p(stream))
 
 

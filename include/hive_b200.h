@@ -179,6 +179,15 @@ int hv_qk_rows_f16(const float* qkv, const float* qn, const float* kn, const flo
 int hv_attn_rows_f16(const float* q, const uint16_t* kc, const uint16_t* vc, float* ctx,
                      const float* scale, int pos0, int nq, int hd, int group, int kvstride,
                      int ntok, float* part, int32_t* ticket, void* stream);
+/* The same GEMV with dp4a block dots instead of tensor-pipe MMAs, over a "dq"
+ * arrangement of the same tiles (equal sizes: hv_w4_prepacked_size): in each 8-block
+ * iteration, lane 4g + t of the warp finds all four words of blocks 2t and 2t+1 of row g.
+ * hv_w4_prepack_dq writes it; hv_a4gv_dq gives results bit-identical to hv_a4gv_pp on
+ * the same matrix. No counterpart in the reference (its k_a4gv reads the row-major form). */
+int hv_w4_prepack_dq(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
+                     uint32_t* pb4, float* psw, void* stream);
+int hv_a4gv_dq(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+               float* dst, int k8, int rows, int pair_ffn, void* stream);
 /* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split
  * kernel, 0 runs every matrix on the one-warp-per-tile kernel. Process-wide. */
 int hv_gemv_set_split(int enable);

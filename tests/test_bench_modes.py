@@ -59,7 +59,9 @@ def test_gemv_sweep_lines(monkeypatch, capsys):
     monkeypatch.setitem(sys.modules, "hvdrv", FakeDriver())
     ns = types.SimpleNamespace(gemv_reps=4, gemv_rotate_mb=8, gemv_max_rows=2048)
     lines = run_lines(capsys, bench.run_gemv_sweep, ns, FakeDist())
-    assert len(lines) == 4                           # 2048x2048, 2048x6144; two kernels each
+    assert len(lines) == 6                  # 2048x2048, 2048x6144; three kernels each
+    assert [ln["kernel"] for ln in lines[:3]] == ["k_a4gv_pp", "k_a4gv_dq", "k_a4gv_mma"]
+    assert "bit_identical_to_pp" in lines[1] and "bit_identical_to_pp" not in lines[0]
     for ln in lines:
         assert ln["unit"] == "GB/s" and ln["us_per_launch"] == pytest.approx(250.0)
         assert ln["bytes_per_launch"] == ln["shape"][0] * ln["shape"][1] * 5 // 8

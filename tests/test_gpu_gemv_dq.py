@@ -1,0 +1,54 @@
+"""The dp4a GEMV over the dq tile layout on a B200 (hv_w4_prepack_dq + hv_a4gv_dq):
+bit-identical to hv_a4gv_pp (one warp per tile, tensor-pipe block dots) and to the
+oracle, for plain and gate/up-paired matrices, tails (nb % 8 != 0), multi-leaf K and the
+vocabulary-sized shapes of the GEMV sweep; the dq arrays are a rearrangement of the
+tile-interleaved ones (the lane-level CPU model checks the arithmetic,
+tests/test_gemv_dq_model.py)."""
+import os
+
+import numpy as np
+import pytest
+
+import hv_oracle as O
+from gpu_util import Dev, bits, quantize_on_device
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(
+    not os.environ.get("HV_NEW_GPU_TESTS"),
+    reason="kernels not yet run on a B200: set HV_NEW_GPU_TESTS=1")]
+F32 = np.float32
+
+
+@pytest.mark.parametrize("n,k,pair", [(5, 32, 0), (13, 416, 0), (777, 4096, 0), (64, 12288, 0),
+                                      (21, 25600, 0), (26, 2048, 13), (24576, 4096, 12288),
+                                      (10, 160, 5), (20, 800, 0), (12288, 4096, 0)])
+def test_gemv_dq_equals_pp_and_oracle(hv, n, k, pair):
+    g = np.random.default_rng(n * 13 + k)
+    p, sc = O.quantize_w4((g.standard_normal((n, k)) * 0.02).astype(F32))
+    nib, scb = hv.w4_prepacked_size(n, k, pair)
+    b4, sw = Dev(p), Dev(sc)
+    pp = (Dev(nbytes=nib), Dev(nbytes=scb))
+    dq = (Dev(nbytes=nib), Dev(nbytes=scb))
+    hv.w4_prepack(b4, sw, n, k, pair, *pp)
+    hv.w4_prepack_dq(b4, sw, n, k, pair, *dq)
+    # the same words per (tile, iteration), the same scales
+    per = 256
+    wp, wd = pp[0].get(np.uint32).reshape(-1, per), dq[0].get(np.uint32).reshape(-1, per)
+    assert np.array_equal(np.sort(wp, axis=1), np.sort(wd, axis=1))
+    assert np.array_equal(bits(pp[1].get(F32)), bits(dq[1].get(F32)))
+    a = (g.standard_normal(k) * 2).astype(F32)
+    a[:32] = 0.0                                       # an all-zero activation block
+    qa, sa_h, _ = O.quantize_act(a)
+    _, want = O.gemv_q_c(qa, sa_h, p, sc, k)
+    a8, sa = quantize_on_device(a)
+    y_pp, y_dq = Dev(nbytes=n * 4), Dev(nbytes=n * 4)
+    hv.a4gv_pp(a8, sa, *pp, y_pp, k // 8, n, pair)
+    hv.a4gv_dq(a8, sa, *dq, y_dq, k // 8, n, pair)
+    assert np.array_equal(bits(y_dq.get(F32)), bits(y_pp.get(F32)))
+    assert np.array_equal(bits(y_dq.get(F32)), bits(want))
+
+
+def test_gemv_dq_rejects_bad_arguments(hv):
+    with pytest.raises(hv.CudaError):
+        hv.a4gv_dq(16, 16, 16, 16, 16, 3, 8)           # K = 24: not a multiple of 32
+    with pytest.raises(hv.CudaError):
+        hv.w4_prepack_dq(16, 16, 10, 64, 4, 16, 16)    # a pair needs rows == 2 * pair
