@@ -359,7 +359,7 @@ def run_ours(args, dist: Dist):
                          exchange=dist.allgather_bytes if sharded else None,
                          weight_cache=args.weight_cache, prefill=args.prefill,
                          cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None,
-                         kv_dtype=args.kv_dtype)
+                         kv_dtype=args.kv_dtype, gemv_layout=args.gemv_layout)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
     window = cap - n_prompt              # decode positions available before a rewind
@@ -466,6 +466,7 @@ def run_ours(args, dist: Dist):
             "config": {"workload": args.workload, "model": arch, "batch": 1,
                        "prompt": n_prompt, "generated": n_new, "kv": args.kv_dtype,
                        "weights": "int4 + f32 scale per 32 (5.00 bits/weight)",
+                       "gemv_layout": args.gemv_layout,
                        "parallelism": (f"column-sharded x{dist.world} (NVLink peer stores "
                                        "inside the fused step)" if sharded else
                                        "replicas" if dist.world > 1 else "single"),
@@ -690,6 +691,9 @@ def main(argv=None):
     ap.add_argument("--kv-dtype", default="f32", choices=["f32", "f16"],
                     help="KV cache element type: f32 (the reference's cache) or f16 (the "
                          "compressed-KV lane)")
+    ap.add_argument("--gemv-layout", default="pp", choices=["pp", "dq"],
+                    help="weight tiles for tensor-pipe block dots (pp) or dp4a block dots "
+                         "(dq); results are bit-identical")
     ap.add_argument("--weight-cache", default=None, metavar="DIR",
                     help="load device-ready weights from DIR when present, else quantise "
                          "and write them there (the timed steps are the same either way)")
@@ -710,6 +714,8 @@ def main(argv=None):
             ap.error(f"option {opt!r}: NAME=VALUE with NAME in {', '.join(STEP_OPTS)}")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.gemv_layout == "dq" and (args.kv_dtype != "f32" or args.prefill != "steps"):
+        ap.error("--gemv-layout dq runs with --kv-dtype f32 and --prefill steps")
     dist = Dist()
     try:
         if args.gemv_sweep:

@@ -808,6 +808,40 @@ HV_DEV float2 slot_terms_sh(unsigned sl, int u, unsigned act_w, unsigned sb, int
 }
 
 
+// slot_terms_sh over a slot of dq words (hv_w4_prepack_dq): lane (g, t) finds all four
+// words of its blocks 2t and 2t+1 at the addresses where the tile-interleaved slot keeps
+// word t of blocks 0..3 and 4..7, and forms their exact int32 dots with dp4a (block_dot)
+// instead of the tensor-pipe MMAs; the terms are the same values. act_q: the int8
+// activations, 32 bytes per block.
+HV_DEV float2 slot_terms_dq(unsigned sl, int u, unsigned act_q, unsigned sb, int it, int t,
+                            int lane, int nvalid) {
+  const uint4 e = lds_u4(sl + u * kPpNibWords * 4 + 16 * lane);
+  const uint4 o = lds_u4(sl + u * kPpNibWords * 4 + 512 + 16 * lane);
+  const float2 s = lds_f2(sl + kSlotScaleOff + u * kPpScales * 4 + 8 * lane);
+  const int be = it * 8 + 2 * t;
+  const uint4 sbp = lds_u4(sb + be * 8);              // blocks 2t and 2t+1: (s, sum) x 2
+  float ce = 0.f, co = 0.f;
+  if (2 * t < nvalid) {
+    const int d = block_dot(e, lds_u4(act_q + be * 32), lds_u4(act_q + be * 32 + 16),
+                            (int)sbp.y);
+    ce = __fmul_rn(__fmul_rn(s.x, __int_as_float((int)sbp.x)), i2f_exact(d));
+  }
+  if (2 * t + 1 < nvalid) {
+    const int d = block_dot(o, lds_u4(act_q + be * 32 + 32), lds_u4(act_q + be * 32 + 48),
+                            (int)sbp.w);
+    co = __fmul_rn(__fmul_rn(s.y, __int_as_float((int)sbp.z)), i2f_exact(d));
+  }
+  return make_float2(ce, co);
+}
+
+// The block terms of one slot iteration in either weight arrangement.
+template <bool kDq>
+HV_DEV float2 slot_terms(unsigned sl, int u, unsigned act_w, unsigned sb, int it, int g, int t,
+                         int lane, int nvalid) {
+  if constexpr (kDq) return slot_terms_dq(sl, u, act_w, sb, it, t, lane, nvalid);
+  else return slot_terms_sh(sl, u, act_w, sb, it, g, t, lane, nvalid);
+}
+
 // The CTA's tiles [t0, t1) of one GEMV phase, their slots starting at sequence number q0.
 // Work items are (tile, leaf of numpy's pairwise recursion), tile-major like the ring;
 // item k goes to warp k % 8, so every warp has work even when the CTA has few tiles
@@ -820,8 +854,9 @@ HV_DEV float2 slot_terms_sh(unsigned sl, int u, unsigned act_w, unsigned sb, int
 // MODE kStore/kResidual/kHead: 8-row tiles of `rows` rows. kSiluPair: tiles of 4 gate
 // rows (quads 0-3) and their 4 up rows (quads 4-7) of a [gate | up] matrix with pair_ffn
 // rows per half; SiLU(gate) * up is formed in the lane that holds the gate row and stored
-// at out[p - 4 t0] for pair p (a shared-memory staging buffer).
-template <int MODE>
+// at out[p - 4 t0] for pair p (a shared-memory staging buffer). kDq: the slots hold the
+// dq arrangement of the words (slot_terms_dq).
+template <int MODE, bool kDq>
 __device__ __noinline__ void gemv_ring(const Ring R, unsigned q0, const GvPlan& P,
                                        const ActView act, int t0, int t1, int rows,
                                        int pair_ffn, const OutCtx O, float* best_v,
@@ -857,18 +892,18 @@ __device__ __noinline__ void gemv_ring(const Ring R, unsigned q0, const GvPlan& 
       if (a == s0 && bf == s0 + kSlotIters) {       // the whole slot: fixed trip count
 #pragma unroll
         for (int u = 0; u < kSlotIters; ++u) {
-          const float2 v = slot_terms_sh(sl, u, act_w, sbs, s0 + u, g, t, lane, 8);
+          const float2 v = slot_terms<kDq>(sl, u, act_w, sbs, s0 + u, g, t, lane, 8);
           ae = __fadd_rn(ae, v.x);
           ao = __fadd_rn(ao, v.y);
         }
       } else {
         for (int it = a; it < bf; ++it) {
-          const float2 v = slot_terms_sh(sl, it - s0, act_w, sbs, it, g, t, lane, 8);
+          const float2 v = slot_terms<kDq>(sl, it - s0, act_w, sbs, it, g, t, lane, 8);
           ae = __fadd_rn(ae, v.x);
           ao = __fadd_rn(ao, v.y);
         }
       }
-      if (bb > bf) tail = slot_terms_sh(sl, bf - s0, act_w, sbs, bf, g, t, lane, ntail);
+      if (bb > bf) tail = slot_terms<kDq>(sl, bf - s0, act_w, sbs, bf, g, t, lane, ntail);
       __syncwarp();
       const bool shared = ia > s0 || ib < s1;
       if (lane == 0) mbar_arrive_n(R.empty_of(q), shared ? kConsWarps / 2 : kConsWarps);
@@ -1247,7 +1282,7 @@ __device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
 
 // ---- the kernel ------------------------------------------------------------------------
 
-template <int GS, bool kSplitMerge, class KT>
+template <int GS, bool kSplitMerge, class KT, bool kDq>
 __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
                                                           int nslots, int inflight,
                                                           int evict_first) {
@@ -1337,7 +1372,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 0);
     trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
-    gemv_ring<kStore>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, o_qkv, nullptr, nullptr, work,
+    gemv_ring<kStore, kDq>(R, q, S.P.gv_hid, act, t0, t1, nqkv, 0, o_qkv, nullptr, nullptr, work,
                       S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_hid));
     trace_mark(D, tb + 1);
@@ -1358,7 +1393,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     pro_load_quant(cq, reinterpret_cast<const int2*>(cq + qdim), qdim, q_s, sb_s);
     trace_mark(D, tb + 5);
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_o, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
+    gemv_ring<kResidual, kDq>(R, q, S.P.gv_o, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_q));
     trace_mark(D, tb + 6);
@@ -1374,7 +1409,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
       const int nl = S.P.gv_hid.nleaf;
       float* act_s = work + (nl > 1 ? (size_t)(t1 - t0) * 8 * nl : 0);
       const OutCtx o_act{act_s, 0, 1, 0, nullptr};
-      gemv_ring<kSiluPair>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, o_act, nullptr,
+      gemv_ring<kSiluPair, kDq>(R, q, S.P.gv_hid, act, t0, t1, 2 * ffn, ffn, o_act, nullptr,
                            nullptr, work, S, D.status);
       csync();
       const int first = rank * ffn + t0 * 4;               // this CTA's outputs, whole blocks
@@ -1398,7 +1433,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 11);
     trace_wait(D, S, tb + 20);
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
-    gemv_ring<kResidual>(R, q, S.P.gv_ffn, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
+    gemv_ring<kResidual, kDq>(R, q, S.P.gv_ffn, act, t0, t1, hrows, 0, o_h, nullptr, nullptr, work,
                          S, D.status);
     q += (unsigned)((t1 - t0) * slots_per_tile(it_ffn));
     trace_mark(D, tb + 12);
@@ -1414,7 +1449,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   phase_tiles(pp_tiles(D.head_rows, 0), &off, &t0, &t1);
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
-  gemv_ring<kHead>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, o_head, &bv, &bi, work,
+  gemv_ring<kHead, kDq>(R, q, S.P.gv_hid, act, t0, t1, D.head_rows, 0, o_head, &bv, &bi, work,
                    S, D.status);
   trace_mark(D, th + 1);
   if (!(flags & HV_STEP_ARGMAX)) return;
@@ -1464,29 +1499,37 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
 }
 
 // The step kernel for group size gs: variant 0 = f32 cache, 1 = f32 cache with the split
-// merge, 2 = binary16 cache.
+// merge, 2 = binary16 cache, 3 = f32 cache over dq weight tiles.
 static void* step_fn(int gs, int variant) {
   if (variant == 1) {
     switch (gs) {
-      case 1: return (void*)k_step<1, true, float>;
-      case 2: return (void*)k_step<2, true, float>;
-      case 4: return (void*)k_step<4, true, float>;
-      default: return (void*)k_step<8, true, float>;
+      case 1: return (void*)k_step<1, true, float, false>;
+      case 2: return (void*)k_step<2, true, float, false>;
+      case 4: return (void*)k_step<4, true, float, false>;
+      default: return (void*)k_step<8, true, float, false>;
     }
   }
   if (variant == 2) {
     switch (gs) {
-      case 1: return (void*)k_step<1, false, __half>;
-      case 2: return (void*)k_step<2, false, __half>;
-      case 4: return (void*)k_step<4, false, __half>;
-      default: return (void*)k_step<8, false, __half>;
+      case 1: return (void*)k_step<1, false, __half, false>;
+      case 2: return (void*)k_step<2, false, __half, false>;
+      case 4: return (void*)k_step<4, false, __half, false>;
+      default: return (void*)k_step<8, false, __half, false>;
+    }
+  }
+  if (variant == 3) {
+    switch (gs) {
+      case 1: return (void*)k_step<1, false, float, true>;
+      case 2: return (void*)k_step<2, false, float, true>;
+      case 4: return (void*)k_step<4, false, float, true>;
+      default: return (void*)k_step<8, false, float, true>;
     }
   }
   switch (gs) {
-    case 1: return (void*)k_step<1, false, float>;
-    case 2: return (void*)k_step<2, false, float>;
-    case 4: return (void*)k_step<4, false, float>;
-    default: return (void*)k_step<8, false, float>;
+    case 1: return (void*)k_step<1, false, float, false>;
+    case 2: return (void*)k_step<2, false, float, false>;
+    case 4: return (void*)k_step<4, false, float, false>;
+    default: return (void*)k_step<8, false, float, false>;
   }
 }
 
@@ -1624,15 +1667,21 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   }
   HV_REQUIRE(h.kv_dtype == HV_KV_F32 || h.kv_dtype == HV_KV_F16, HV_E_INVALID,
              "hv_step_launch: kv_dtype %d (HV_KV_F32 or HV_KV_F16)", h.kv_dtype);
+  HV_REQUIRE(h.w4_layout == HV_W4_PP || h.w4_layout == HV_W4_DQ, HV_E_INVALID,
+             "hv_step_launch: w4_layout %d (HV_W4_PP or HV_W4_DQ)", h.w4_layout);
+  HV_REQUIRE(h.w4_layout == HV_W4_PP || h.kv_dtype == HV_KV_F32, HV_E_UNSUPPORTED,
+             "hv_step_launch: dq weight tiles run with the f32 cache");
   // the split merge (one GPU, f32 cache): its per-warp chunk weights live in the work area
   const bool split_merge = g_opt_split_merge && world == 1 && h.kv_dtype == HV_KV_F32 &&
+      h.w4_layout == HV_W4_PP &&
       (lay.ring - lay.work) / sizeof(float) >= (size_t)kConsWarps * h.attn_chunks;
-  const int variant = h.kv_dtype == HV_KV_F16 ? 2 : split_merge ? 1 : 0;
+  const int variant = h.w4_layout == HV_W4_DQ ? 3
+                      : h.kv_dtype == HV_KV_F16 ? 2 : split_merge ? 1 : 0;
   void* fn = step_fn(gs, variant);
   {
     // set the function's shared-memory limit once per (kernel, device, size)
     static std::mutex mu;
-    static size_t done[12][64];
+    static size_t done[16][64];
     int dev = 0;
     HV_CUDA(cudaGetDevice(&dev));
     const int gi = (gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3) + 4 * variant;

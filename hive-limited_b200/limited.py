@@ -48,7 +48,7 @@ class _StepDesc(C.Structure):
                     "part", "ticket", "amax_v", "amax_i", "barrier", "status", "trace",
                     "plans")]
                 + [("world", C.c_int), ("rank", C.c_int), ("peers", C.c_void_p),
-                   ("kv_dtype", C.c_int)])
+                   ("kv_dtype", C.c_int), ("w4_layout", C.c_int)])
 
 
 MAX_WORLD = 8
@@ -137,6 +137,11 @@ class Engine:
                            then writes the entry. The entry is keyed by the model
                            directory's files, or by `cache_tag` for `tensors=` sources.
                            `cache_hit` tells which happened (None without a cache).
+      gemv_layout       -- "pp" (default): weight tiles for tensor-pipe block dots
+                           (hv_w4_prepack); "dq": the same tiles arranged for dp4a block
+                           dots (hv_w4_prepack_dq, hv_a4gv_dq). Results are bit-identical;
+                           only the speed differs. "dq" runs with the f32 cache and the
+                           token-by-token prefill.
       kv_dtype          -- "f32" (default): the reference's fp32 KV cache; "f16": the
                            compressed-KV lane, an IEEE binary16 cache (half the KV bytes
                            per step). Each k/v row is rounded to nearest-even binary16 when
@@ -148,7 +153,7 @@ class Engine:
     def __init__(self, model_dir=None, kernels_dir=None, verify_kernels=True, quiet=False, *,
                  config=None, tensors=None, max_context=None, device=0, fused=True,
                  quantize_on="device", world=1, rank=0, exchange=None, weight_cache=None,
-                 cache_tag=None, prefill="steps", kv_dtype="f32"):
+                 cache_tag=None, prefill="steps", kv_dtype="f32", gemv_layout="pp"):
         if config is None:
             self.cfg = Config.load(model_dir)
         else:
@@ -169,6 +174,11 @@ class Engine:
             raise ValueError(f"kv_dtype={kv_dtype!r}: 'f32' or 'f16'")
         self.kv_dtype = kv_dtype
         self.kv_f16 = kv_dtype == "f16"
+        if gemv_layout not in ("pp", "dq"):
+            raise ValueError(f"gemv_layout={gemv_layout!r}: 'pp' or 'dq'")
+        if gemv_layout == "dq" and (self.kv_f16 or prefill == "batched"):
+            raise ValueError("gemv_layout='dq' runs with the f32 cache and the step prefill")
+        self.gemv_layout = gemv_layout
         self._pf = None
         self.shard = shard_plan(self.cfg, self.world, self.rank)
         if self.world > 1 and (not self.fused or exchange is None):
@@ -180,7 +190,7 @@ class Engine:
         if weight_cache is not None:          # argument errors before any device work
             key, ident = wcache.entry_key(self.cfg, self.world, self.rank,
                                           model_dir=None if cache_tag is not None else model_dir,
-                                          tag=cache_tag)
+                                          tag=cache_tag, w4_layout=gemv_layout)
         hvdrv.load(kernels_dir, verify=verify_kernels)
         hvdrv.init()
         self.dev = hvdrv.device(device)
@@ -249,7 +259,8 @@ class Engine:
             hvdrv.quantize_w4(self._stage, b4, sw, n, k)
         nib_bytes, sc_bytes = hvdrv.w4_prepacked_size(n, k, pair_ffn)
         pb4, psw = self._alloc(nib_bytes), self._alloc(sc_bytes)
-        hvdrv.w4_prepack(b4, sw, n, k, pair_ffn, pb4, psw)
+        prepack = hvdrv.w4_prepack_dq if self.gemv_layout == "dq" else hvdrv.w4_prepack
+        prepack(b4, sw, n, k, pair_ffn, pb4, psw)
         hvdrv.synchronize()
         hvdrv.free(b4)
         hvdrv.free(sw)
@@ -462,7 +473,8 @@ class Engine:
             self.d_tok, self.d_pos, self.d_step, self.d_gen, self.d_h, self.d_qkv,
             self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
             self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans,
-            self.world, self.rank, self.d_peers, 1 if self.kv_f16 else 0)
+            self.world, self.rank, self.d_peers, 1 if self.kv_f16 else 0,
+            1 if self.gemv_layout == "dq" else 0)
 
     def _connect_peers(self):
         """Swap CUDA IPC handles of the buffers every rank's step writes into (residual,
@@ -505,7 +517,8 @@ class Engine:
         pb4, psw, k, n, pair = w4
         s = self._stream_cur
         hvdrv.qa8s(src, self.d_a8, self.d_sa, k // BLOCK, s)
-        hvdrv.a4gv_pp(self.d_a8, self.d_sa, pb4, psw, dst, k // 8, n, pair, s)
+        gemv = hvdrv.a4gv_dq if self.gemv_layout == "dq" else hvdrv.a4gv_pp
+        gemv(self.d_a8, self.d_sa, pb4, psw, dst, k // 8, n, pair, s)
 
     def _step_eager(self):
         """One transformer step at d_pos, kernel by kernel (engine/limited.py:374-419)."""

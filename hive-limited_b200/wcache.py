@@ -36,14 +36,20 @@ ALIGN = 256
 GEOMETRY = ("n_layer", "hidden", "ffn", "n_head", "n_kv", "head_dim", "vocab", "tied")
 
 
-def entry_key(cfg, world: int, rank: int, model_dir=None, tag=None) -> tuple[str, dict]:
+def entry_key(cfg, world: int, rank: int, model_dir=None, tag=None,
+              w4_layout: str = "pp") -> tuple[str, dict]:
     """(key, identity) of the cache entry for this model source and shard. Exactly one
     of `model_dir` (a checkpoint directory) or `tag` (a caller-chosen name, e.g. for a
-    seeded synthetic model) identifies the source."""
+    seeded synthetic model) identifies the source. `w4_layout` is the arrangement of the
+    prepacked tiles ("pp" or "dq"), which the cached bytes are in."""
     if (model_dir is None) == (tag is None):
         raise ValueError("a weight-cache key needs exactly one of model_dir or tag")
+    if w4_layout not in ("pp", "dq"):
+        raise ValueError(f"w4_layout={w4_layout!r}")
     ident = {"layout": LAYOUT_VERSION, "world": int(world), "rank": int(rank),
              "geometry": {k: getattr(cfg, k) for k in GEOMETRY}}
+    if w4_layout != "pp":
+        ident["w4_layout"] = w4_layout
     if model_dir is not None:
         files = sorted(p for p in Path(model_dir).iterdir()
                        if p.is_file() and (p.suffix == ".safetensors" or p.name == "config.json"))

@@ -362,10 +362,16 @@ typedef struct hv_step_desc {
    * appended as such, and attention reads every row as the widened binary16 value --
    * the arithmetic of hv_kv_append_f16 followed by hv_attn_decode_f16). */
   int kv_dtype;
+  /* Arrangement of every prepacked weight tile: HV_W4_PP (0, hv_w4_prepack, block dots
+   * on the tensor pipe) or HV_W4_DQ (hv_w4_prepack_dq, dp4a block dots; same results;
+   * with the f32 cache only). */
+  int w4_layout;
 } hv_step_desc;
 
 #define HV_KV_F32 0
 #define HV_KV_F16 1
+#define HV_W4_PP 0
+#define HV_W4_DQ 1
 
 #define HV_MAX_WORLD 8
 /* Every rank's copies of the exchanged buffers (device pointers valid on this rank:

@@ -73,11 +73,13 @@ def test_step_desc_layout_matches_header(tmp_path):
     import subprocess
     import limited
     assert ctypes.sizeof(limited._LayerW) == 14 * 8
-    # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers, world, rank, peers, kv_dtype
+    # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers, world, rank, peers, kv_dtype,
+    # w4_layout
     assert limited._StepDesc.layers.offset == 48
     assert limited._StepDesc.world.offset == 48 + 24 * 8
     assert limited._StepDesc.peers.offset == 48 + 24 * 8 + 8
     assert limited._StepDesc.kv_dtype.offset == 48 + 24 * 8 + 16
+    assert limited._StepDesc.w4_layout.offset == 48 + 24 * 8 + 20
     assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 24
     assert ctypes.sizeof(limited._StepPeers) == 5 * 8 * 8
     cc = shutil.which("gcc") or shutil.which("cc")

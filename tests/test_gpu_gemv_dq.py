@@ -3,7 +3,8 @@ bit-identical to hv_a4gv_pp (one warp per tile, tensor-pipe block dots) and to t
 oracle, for plain and gate/up-paired matrices, tails (nb % 8 != 0), multi-leaf K and the
 vocabulary-sized shapes of the GEMV sweep; the dq arrays are a rearrangement of the
 tile-interleaved ones (the lane-level CPU model checks the arithmetic,
-tests/test_gemv_dq_model.py)."""
+tests/test_gemv_dq_model.py). An engine with dq tiles (fused step and eager sequence)
+gives the pp engine's logits bit for bit."""
 import os
 
 import numpy as np
@@ -52,3 +53,47 @@ def test_gemv_dq_rejects_bad_arguments(hv):
         hv.a4gv_dq(16, 16, 16, 16, 16, 3, 8)           # K = 24: not a multiple of 32
     with pytest.raises(hv.CudaError):
         hv.w4_prepack_dq(16, 16, 10, 64, 4, 16, 16)    # a pair needs rows == 2 * pair
+
+
+def _engine(arch, seed, cap, **kw):
+    import limited
+    import synth
+    import w4format
+    cfg = w4format.Config(arch)
+    return limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
+                          max_context=cap, **kw)
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_engine_dq_tiles_bit_identical_to_pp(hv, fused):
+    """The fused step (k_step over dq slots) and the eager sequence (hv_a4gv_dq) give the
+    pp engine's logits bit for bit, and the same greedy tokens."""
+    import synth
+    arch = synth.tiny_arch(n_layer=3, hidden=512, ffn=1024, n_head=8, n_kv=2, vocab=4096)
+    a = _engine(arch, 21, 64, fused=fused)
+    b = _engine(arch, 21, 64, fused=fused, gemv_layout="dq")
+    try:
+        prompt = synth.prompt_ids(a.cfg, 21, 9)
+        for n in (1, 5, 9):
+            assert np.array_equal(bits(a.logits(prompt[:n])), bits(b.logits(prompt[:n]))), n
+        assert a.generate(prompt, 12)[0] == b.generate(prompt, 12)[0]
+    finally:
+        a.free()
+        b.free()
+
+
+def test_engine_dq_tiles_8b_shape(hv):
+    """The 8B geometry (K = 4096 and 12288: one and four pairwise leaves per row)."""
+    import synth
+    arch = synth.ARCH["qwen3-8b"]
+    a = _engine(arch, 2, 16)
+    try:
+        prompt = synth.prompt_ids(a.cfg, 2, 4)
+        la = a.logits(prompt)
+    finally:
+        a.free()
+    b = _engine(arch, 2, 16, gemv_layout="dq")
+    try:
+        assert np.array_equal(bits(la), bits(b.logits(prompt)))
+    finally:
+        b.free()

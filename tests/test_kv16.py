@@ -127,3 +127,14 @@ def test_engine_rejects_unknown_kv_dtype():
     import limited
     with pytest.raises(ValueError, match="kv_dtype"):
         limited.Engine(config=synth.tiny_arch(), tensors={}, kv_dtype="bf16")
+
+
+def test_engine_rejects_bad_gemv_layout():
+    """Checked before any device work: an unknown arrangement, and dq tiles with the
+    binary16 cache or the batched prefill (neither has a dq form)."""
+    import limited
+    with pytest.raises(ValueError, match="gemv_layout"):
+        limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="rowmajor")
+    for kw in ({"kv_dtype": "f16"}, {"prefill": "batched"}):
+        with pytest.raises(ValueError, match="dq"):
+            limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="dq", **kw)

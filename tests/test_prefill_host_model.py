@@ -182,6 +182,7 @@ def fake_engine(dev, cfg, w, cap, fused, kv_dtype="f32"):
     eng = object.__new__(limited.Engine)
     eng.cfg, eng.fused, eng.prefill_mode = c, fused, "batched"
     eng.kv_dtype, eng.kv_f16 = kv_dtype, kv_dtype == "f16"
+    eng.gemv_layout = "pp"
     eng.world, eng.rank, eng._pf, eng._buffers, eng._stream_cur = 1, 0, None, [], 0
     eng.quiet = True
 

@@ -59,6 +59,8 @@ def test_key_follows_geometry_shard_and_source(tmp_path):
     assert wcache.entry_key(_cfg(), 2, 0, tag="a")[0] != base
     assert wcache.entry_key(_cfg(), 2, 1, tag="a")[0] != wcache.entry_key(_cfg(), 2, 0, tag="a")[0]
     assert wcache.entry_key(_cfg(), 1, 0, tag="b")[0] != base
+    assert wcache.entry_key(_cfg(), 1, 0, tag="a", w4_layout="dq")[0] != base
+    assert wcache.entry_key(_cfg(), 1, 0, tag="a", w4_layout="pp")[0] == base
     with pytest.raises(ValueError):
         wcache.entry_key(_cfg(), 1, 0)
     with pytest.raises(ValueError):
