@@ -277,6 +277,9 @@ def run_reference(args, dist: Dist):
 
 STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3, "split_merge": 4}
 STEP_OPT_DEFAULTS = {"inflight": 6, "evict_first": 1, "local_qkv_barrier": 0, "split_merge": 0}
+# A/B-only names that are not step options: layout_dq=1 times a second engine of the same
+# model whose weight tiles are in the dq arrangement (gemv_layout="dq")
+AB_ENGINE_OPTS = ("layout_dq",)
 
 
 def parse_opts(text: str) -> dict:
@@ -288,26 +291,37 @@ def parse_opts(text: str) -> dict:
     return out
 
 
-def run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv):
+def run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv, make_alt=None):
     """Fused-step option sets against the baseline in this process (one load, one
     prefill): `--ab-rounds` rounds, each timing every set for --steps steps in turn
     (CUDA events, max over ranks), and each set's logits of one step at the first decode
-    position compared bit for bit with the baseline's. -> list of per-set results."""
+    position compared bit for bit with the baseline's. A set with layout_dq=1 runs on a
+    second engine (make_alt() -> (engine, decode), built once, prefilled the same way).
+    -> list of per-set results."""
     sets = [{}] + [parse_opts(x) for x in args.ab]
     base = dict(STEP_OPT_DEFAULTS, **parse_opts(",".join(args.step_opt)))
+    alt = []
 
     def apply(opts):
         for name, value in dict(base, **opts).items():
-            hvdrv.step_set_option(STEP_OPTS[name], value)
+            if name not in AB_ENGINE_OPTS:
+                hvdrv.step_set_option(STEP_OPTS[name], value)
 
-    def one_step_logits():
-        hvdrv.upload_async(eng.d_pos, pin, 4)              # position n_prompt, step 0
-        hvdrv.upload_async(eng.d_step, pin + 4, 4)
-        hvdrv.upload_async(eng.d_tok, pin + 8, 4)
-        eng._decode_one()
+    def engine_of(opts):
+        if not opts.get("layout_dq"):
+            return eng, decode
+        if not alt:
+            alt.append(make_alt())
+        return alt[0]
+
+    def one_step_logits(e):
+        hvdrv.upload_async(e.d_pos, pin, 4)                # position n_prompt, step 0
+        hvdrv.upload_async(e.d_step, pin + 4, 4)
+        hvdrv.upload_async(e.d_tok, pin + 8, 4)
+        e._decode_one()
         hvdrv.synchronize()
-        eng._check_status()
-        return eng.download_logits()
+        e._check_status()
+        return e.download_logits()
 
     pbuf = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_int32 * 4).from_address(pin))
     pbuf[2] = 17                                           # a fixed input token
@@ -318,22 +332,25 @@ def run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv):
     for _ in range(args.ab_rounds):
         for i, opts in enumerate(sets):
             apply(opts)
-            lg = one_step_logits()
+            e, dec = engine_of(opts)
+            lg = one_step_logits(e)
             if ref is None:
                 ref = lg
             same[i] = same[i] and bool(np.array_equal(lg.view(np.uint32), ref.view(np.uint32)))
             done[0] = 0
-            hvdrv.upload_async(eng.d_pos, pin, 4)
-            hvdrv.upload_async(eng.d_step, pin + 4, 4)
-            decode(3)
+            hvdrv.upload_async(e.d_pos, pin, 4)
+            hvdrv.upload_async(e.d_step, pin + 4, 4)
+            dec(3)
             dist.barrier()
             hvdrv.synchronize()
             hvdrv.event_record(e0, 0)
-            decode(args.steps)
+            dec(args.steps)
             hvdrv.event_record(e1, 0)
             hvdrv.synchronize()
             times[i].append(dist.max(hvdrv.event_elapsed_ms(e0, e1)) / args.steps)
     apply({})
+    for e, _ in alt:
+        e.free()
     out = []
     for opts, t, ok in zip(sets, times, same):
         ms = float(np.median(t))
@@ -353,13 +370,18 @@ def run_ours(args, dist: Dist):
     cap = n_prompt + n_new
     t0 = time.perf_counter()
     sharded = dist.world > 1 and args.mode == "sharded"
-    eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True,
-                         max_context=cap, device=dist.local, fused=True,
-                         world=dist.world if sharded else 1, rank=dist.rank if sharded else 0,
-                         exchange=dist.allgather_bytes if sharded else None,
-                         weight_cache=args.weight_cache, prefill=args.prefill,
-                         cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None,
-                         kv_dtype=args.kv_dtype, gemv_layout=args.gemv_layout)
+
+    def make_engine(gemv_layout):
+        return limited.Engine(
+            config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True, max_context=cap,
+            device=dist.local, fused=True, world=dist.world if sharded else 1,
+            rank=dist.rank if sharded else 0,
+            exchange=dist.allgather_bytes if sharded else None,
+            weight_cache=args.weight_cache, prefill=args.prefill,
+            cache_tag=f"synthetic:{arch}:seed{seed}" if args.weight_cache else None,
+            kv_dtype=args.kv_dtype, gemv_layout=gemv_layout)
+
+    eng = make_engine(args.gemv_layout)
     t_load = time.perf_counter() - t0
     prompt = synth.prompt_ids(cfg, seed, n_prompt)
     window = cap - n_prompt              # decode positions available before a rewind
@@ -376,13 +398,25 @@ def run_ours(args, dist: Dist):
     pbuf[:] = [n_prompt, 0, 0, 0]
     done = [0]
 
-    def decode(k):
-        for _ in range(k):
-            if done[0] and done[0] % window == 0:          # rewind to the first position
-                hvdrv.upload_async(eng.d_pos, pin, 4)
-                hvdrv.upload_async(eng.d_step, pin + 4, 4)
-            eng._decode_one()
-            done[0] += 1
+    def decoder(e):
+        def decode(k):
+            for _ in range(k):
+                if done[0] and done[0] % window == 0:      # rewind to the first position
+                    hvdrv.upload_async(e.d_pos, pin, 4)
+                    hvdrv.upload_async(e.d_step, pin + 4, 4)
+                e._decode_one()
+                done[0] += 1
+        return decode
+
+    decode = decoder(eng)
+
+    def make_alt():
+        """The same model with dq weight tiles, prefilled like the first engine."""
+        e = make_engine("dq")
+        e._prefill(prompt)
+        hvdrv.synchronize()
+        e._check_status()
+        return e, decoder(e)
 
     decode(args.warmup)
     hvdrv.synchronize()
@@ -438,7 +472,7 @@ def run_ours(args, dist: Dist):
 
     ab = None
     if args.ab:
-        ab = run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv)
+        ab = run_ab(args, dist, eng, decode, pin, n_prompt, window, done, hvdrv, make_alt)
 
     # end to end through the public API: Engine.stream with host-fed tokens
     n_e2e = min(args.e2e_steps, window)
@@ -709,9 +743,17 @@ def main(argv=None):
                     help="sweep only the shapes with at most this many rows (0: all)")
     ap.add_argument("--gemv-rotate-mb", type=int, default=320)
     args = ap.parse_args(argv)
-    for opt in args.step_opt + [x for a in args.ab for x in a.split(",") if x.strip()]:
+    for opt in args.step_opt:
         if opt.partition("=")[0] not in STEP_OPTS or not opt.partition("=")[2].isdigit():
             ap.error(f"option {opt!r}: NAME=VALUE with NAME in {', '.join(STEP_OPTS)}")
+    ab_names = list(STEP_OPTS) + list(AB_ENGINE_OPTS)
+    for opt in [x for a in args.ab for x in a.split(",") if x.strip()]:
+        if opt.partition("=")[0] not in ab_names or not opt.partition("=")[2].isdigit():
+            ap.error(f"--ab option {opt!r}: NAME=VALUE with NAME in {', '.join(ab_names)}")
+    if any(parse_opts(a).get("layout_dq") for a in args.ab) and (
+            args.gemv_layout != "pp" or args.kv_dtype != "f32" or args.prefill != "steps"):
+        ap.error("--ab layout_dq=1 compares against a pp engine with --kv-dtype f32 and "
+                 "--prefill steps")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.gemv_layout == "dq" and (args.kv_dtype != "f32" or args.prefill != "steps"):

@@ -109,3 +109,39 @@ def test_ab_loop_times_every_set_and_restores_options(monkeypatch):
     assert calls.count(5) == 2 * 3                     # every set timed in every round
     # the options end as --step-opt left them: defaults plus evict_first=0
     assert drv.options == {1: 6, 2: 0, 3: 0, 4: 0}
+
+
+def test_ab_layout_set_runs_on_a_second_engine(monkeypatch):
+    """layout_dq=1 times a second engine (built once, freed at the end) with its own
+    decode loop; the step options are applied around it as for every set, and logits
+    identity is judged against the baseline engine's."""
+    drv = FakeDriver()
+    pin = (np.ctypeslib.ctypes.c_int32 * 4)()
+    addr = np.ctypeslib.ctypes.addressof(pin)
+    ns = types.SimpleNamespace(ab=["layout_dq=1"], ab_rounds=3, steps=4, step_opt=[])
+    base_calls, alt_calls, made, freed = [], [], [], []
+
+    class AltEngine(FakeEngine):
+        def free(self):
+            freed.append(1)
+
+    def make_alt():
+        made.append(1)
+        return AltEngine(drv), lambda k: alt_calls.append(k)
+
+    out = bench.run_ab(ns, FakeDist(), FakeEngine(drv), lambda k: base_calls.append(k), addr,
+                       4096, 256, [0], drv, make_alt)
+    assert [o["options"] for o in out] == ["baseline", {"layout_dq": 1}]
+    assert made == [1] and freed == [1]
+    assert base_calls.count(4) == 3 and alt_calls.count(4) == 3
+    assert all(o["logits_identical"] for o in out)
+    assert 5 not in drv.options                 # layout_dq is not passed as a step option
+
+
+def test_ab_option_names_are_checked():
+    with pytest.raises(SystemExit):
+        bench.main(["--ab", "layout_dq=1", "--kv-dtype", "f16"])
+    with pytest.raises(SystemExit):
+        bench.main(["--ab", "no_such_option=1"])
+    with pytest.raises(SystemExit):
+        bench.main(["--step-opt", "layout_dq=1"])
