@@ -751,13 +751,12 @@ def main(argv=None):
         if opt.partition("=")[0] not in ab_names or not opt.partition("=")[2].isdigit():
             ap.error(f"--ab option {opt!r}: NAME=VALUE with NAME in {', '.join(ab_names)}")
     if any(parse_opts(a).get("layout_dq") for a in args.ab) and (
-            args.gemv_layout != "pp" or args.kv_dtype != "f32" or args.prefill != "steps"):
-        ap.error("--ab layout_dq=1 compares against a pp engine with --kv-dtype f32 and "
-                 "--prefill steps")
+            args.gemv_layout != "pp" or args.kv_dtype != "f32"):
+        ap.error("--ab layout_dq=1 compares against a pp engine with --kv-dtype f32")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.gemv_layout == "dq" and (args.kv_dtype != "f32" or args.prefill != "steps"):
-        ap.error("--gemv-layout dq runs with --kv-dtype f32 and --prefill steps")
+    if args.gemv_layout == "dq" and args.kv_dtype != "f32":
+        ap.error("--gemv-layout dq runs with --kv-dtype f32")
     dist = Dist()
     try:
         if args.gemv_sweep:

@@ -43,6 +43,9 @@ HV_DEV float pf_term(float sw, float sa, int d, int bsum) {
   return __fmul_rn(__fmul_rn(sw, sa), i2f_exact(d - 8 * bsum));
 }
 
+// kDq: the weights are in the dq arrangement (hv_w4_prepack_dq): lane (g, t) loads word t
+// of each block j of row g from where that arrangement keeps it, as single words.
+template <bool kDq>
 __global__ void __launch_bounds__(256) k_a4gemm_pp(const int8_t* __restrict__ a8,
                                                    const float* __restrict__ sa,
                                                    const uint32_t* __restrict__ pb4,
@@ -63,8 +66,8 @@ __global__ void __launch_bounds__(256) k_a4gemm_pp(const int8_t* __restrict__ a8
   const int8_t* act = a8 + (size_t)tok_col * k + 8 * t;
   const float* sa0 = sa + (size_t)min(n0, ntok - 1) * 2 * nb;
   const float* sa1 = sa + (size_t)min(n1, ntok - 1) * 2 * nb;
-  const uint32_t* wa = pb4 + (size_t)tile_a * niter * kPpNibWords + 4 * lane;
-  const uint32_t* wb = pb4 + (size_t)tile_b * niter * kPpNibWords + 4 * lane;
+  const uint32_t* wa = pb4 + (size_t)tile_a * niter * kPpNibWords + (kDq ? 16 * g + t : 4 * lane);
+  const uint32_t* wb = pb4 + (size_t)tile_b * niter * kPpNibWords + (kDq ? 16 * g + t : 4 * lane);
   const float* sca = psw + (size_t)tile_a * niter * kPpScales + 8 * g;
   const float* scb = psw + (size_t)tile_b * niter * kPpScales + 8 * g;
 
@@ -73,12 +76,24 @@ __global__ void __launch_bounds__(256) k_a4gemm_pp(const int8_t* __restrict__ a8
   int sp = 0, leaf = 0, leaf_begin = 0;
   for (int it = 0; it < niter; ++it) {
     const size_t wo = (size_t)it * kPpNibWords, so = (size_t)it * kPpScales;
-    const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + wo));
-    const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wa + wo + 128));
-    const uint4 b_lo = __ldg(reinterpret_cast<const uint4*>(wb + wo));
-    const uint4 b_hi = __ldg(reinterpret_cast<const uint4*>(wb + wo + 128));
-    const unsigned wA[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
-    const unsigned wB[8] = {b_lo.x, b_lo.y, b_lo.z, b_lo.w, b_hi.x, b_hi.y, b_hi.z, b_hi.w};
+    unsigned wA[8], wB[8];
+    if constexpr (kDq) {
+      // word t of block j at (j & 1) * 128 + 4 (4 g + j / 2) + t
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        wA[j] = __ldg(wa + wo + (j & 1) * 128 + 4 * (j >> 1));
+        wB[j] = __ldg(wb + wo + (j & 1) * 128 + 4 * (j >> 1));
+      }
+    } else {
+      const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + wo));
+      const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wa + wo + 128));
+      const uint4 b_lo = __ldg(reinterpret_cast<const uint4*>(wb + wo));
+      const uint4 b_hi = __ldg(reinterpret_cast<const uint4*>(wb + wo + 128));
+      wA[0] = a_lo.x; wA[1] = a_lo.y; wA[2] = a_lo.z; wA[3] = a_lo.w;
+      wA[4] = a_hi.x; wA[5] = a_hi.y; wA[6] = a_hi.z; wA[7] = a_hi.w;
+      wB[0] = b_lo.x; wB[1] = b_lo.y; wB[2] = b_lo.z; wB[3] = b_lo.w;
+      wB[4] = b_hi.x; wB[5] = b_hi.y; wB[6] = b_hi.z; wB[7] = b_hi.w;
+    }
     const float4 sA0 = __ldg(reinterpret_cast<const float4*>(sca + so));
     const float4 sA1 = __ldg(reinterpret_cast<const float4*>(sca + so + 4));
     const float4 sB0 = __ldg(reinterpret_cast<const float4*>(scb + so));
@@ -429,35 +444,50 @@ extern "C" int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void
   HV_LAUNCHED("k_silu_rows");
 }
 
-extern "C" int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4,
-                            const float* psw, float* dst, int k8, int rows, int pair_ffn,
-                            int ntok, void* stream) {
+template <bool kDq>
+int a4gemm_any(const char* name, const int8_t* a8, const float* sa, const uint32_t* pb4,
+               const float* psw, float* dst, int k8, int rows, int pair_ffn, int ntok,
+               void* stream) {
   HV_REQUIRE(a8 && sa && pb4 && psw && dst && k8 > 0 && rows > 0 && ntok > 0, HV_E_INVALID,
-             "hv_a4gemm_pp: bad arguments");
+             "%s: bad arguments", name);
   HV_REQUIRE(pair_ffn == 0 || rows == 2 * pair_ffn, HV_E_INVALID,
-             "hv_a4gemm_pp: a paired matrix has 2 * pair_ffn rows");
+             "%s: a paired matrix has 2 * pair_ffn rows", name);
   HV_REQUIRE(k8 % 32 == 0, HV_E_UNSUPPORTED,
-             "hv_a4gemm_pp: K = %d is not a multiple of 256 (whole 8-block iterations)", k8 * 8);
+             "%s: K = %d is not a multiple of 256 (whole 8-block iterations)", name, k8 * 8);
   const int nb = k8 / 4;
-  HV_REQUIRE(nb <= kPfMaxBlocks, HV_E_UNSUPPORTED, "hv_a4gemm_pp: K = %d exceeds %d", k8 * 8,
+  HV_REQUIRE(nb <= kPfMaxBlocks, HV_E_UNSUPPORTED, "%s: K = %d exceeds %d", name, k8 * 8,
              kPfMaxBlocks * kBlock);
   HV_REQUIRE(((uintptr_t)a8 & 15) == 0 && ((uintptr_t)sa & 15) == 0 &&
                  ((uintptr_t)pb4 & 15) == 0 && ((uintptr_t)psw & 15) == 0,
-             HV_E_INVALID, "hv_a4gemm_pp: unaligned pointer");
+             HV_E_INVALID, "%s: unaligned pointer", name);
   GvPlan plan;
   HV_REQUIRE(gv_make_plan(nb, &plan) && plan.ntail == 0, HV_E_UNSUPPORTED,
-             "hv_a4gemm_pp: no reduction plan for K");
+             "%s: no reduction plan for K", name);
   int depth = 0, maxd = 0;
   for (int l = 0; l < plan.nleaf; ++l) {
     ++depth;
     maxd = depth > maxd ? depth : maxd;
     depth -= plan.pops[l];
   }
-  HV_REQUIRE(maxd <= 8, HV_E_UNSUPPORTED, "hv_a4gemm_pp: reduction stack deeper than 8");
+  HV_REQUIRE(maxd <= 8, HV_E_UNSUPPORTED, "%s: reduction stack deeper than 8", name);
   const int ntile = pp_tiles(rows, pair_ffn);
   const dim3 grid((unsigned)((ntile + 3) / 4), (unsigned)((ntok + 31) / 32));
-  HV_REQUIRE(grid.y <= 65535u, HV_E_UNSUPPORTED, "hv_a4gemm_pp: %d tokens at once", ntok);
-  k_a4gemm_pp<<<grid, 256, 0, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, ntok, rows,
-                                                      pair_ffn, plan);
+  HV_REQUIRE(grid.y <= 65535u, HV_E_UNSUPPORTED, "%s: %d tokens at once", name, ntok);
+  k_a4gemm_pp<kDq><<<grid, 256, 0, (cudaStream_t)stream>>>(a8, sa, pb4, psw, dst, ntok, rows,
+                                                           pair_ffn, plan);
   HV_LAUNCHED("k_a4gemm_pp");
+}
+
+extern "C" int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4,
+                            const float* psw, float* dst, int k8, int rows, int pair_ffn,
+                            int ntok, void* stream) {
+  return a4gemm_any<false>("hv_a4gemm_pp", a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok,
+                           stream);
+}
+
+extern "C" int hv_a4gemm_dq(const int8_t* a8, const float* sa, const uint32_t* pb4,
+                            const float* psw, float* dst, int k8, int rows, int pair_ffn,
+                            int ntok, void* stream) {
+  return a4gemm_any<true>("hv_a4gemm_dq", a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok,
+                          stream);
 }

@@ -102,6 +102,7 @@ _SIGS = {
     "hv_a4gv_dq": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _VP],
     "hv_gemv_set_split": [_I],
     "hv_a4gemm_pp": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
+    "hv_a4gemm_dq": [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
     "hv_gather_rows": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_qa8s_rows": [_VP, _VP, _VP, _I, _I, _VP],
     "hv_qk_rows": [_VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP],
@@ -514,6 +515,12 @@ def wait_probe(word, mask, want, limit_ns, status, stream=0):
 def a4gemm_pp(a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok, stream=0):
     """a4gv_pp for ntok tokens at once (prompt prefill); rows of dst are tokens."""
     _call("hv_a4gemm_pp", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
+          ntok, _p(stream))
+
+
+def a4gemm_dq(a8, sa, pb4, psw, dst, k8, rows, pair_ffn, ntok, stream=0):
+    """a4gemm_pp over weights in the dq arrangement (same results)."""
+    _call("hv_a4gemm_dq", _p(a8), _p(sa), _p(pb4), _p(psw), _p(dst), k8, rows, pair_ffn,
           ntok, _p(stream))
 
 

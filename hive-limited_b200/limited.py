@@ -139,9 +139,9 @@ class Engine:
                            `cache_hit` tells which happened (None without a cache).
       gemv_layout       -- "pp" (default): weight tiles for tensor-pipe block dots
                            (hv_w4_prepack); "dq": the same tiles arranged for dp4a block
-                           dots (hv_w4_prepack_dq, hv_a4gv_dq). Results are bit-identical;
-                           only the speed differs. "dq" runs with the f32 cache and the
-                           token-by-token prefill.
+                           dots (hv_w4_prepack_dq, hv_a4gv_dq, hv_a4gemm_dq). Results are
+                           bit-identical; only the speed differs. "dq" runs with the f32
+                           cache.
       kv_dtype          -- "f32" (default): the reference's fp32 KV cache; "f16": the
                            compressed-KV lane, an IEEE binary16 cache (half the KV bytes
                            per step). Each k/v row is rounded to nearest-even binary16 when
@@ -176,8 +176,8 @@ class Engine:
         self.kv_f16 = kv_dtype == "f16"
         if gemv_layout not in ("pp", "dq"):
             raise ValueError(f"gemv_layout={gemv_layout!r}: 'pp' or 'dq'")
-        if gemv_layout == "dq" and (self.kv_f16 or prefill == "batched"):
-            raise ValueError("gemv_layout='dq' runs with the f32 cache and the step prefill")
+        if gemv_layout == "dq" and self.kv_f16:
+            raise ValueError("gemv_layout='dq' runs with the f32 cache")
         self.gemv_layout = gemv_layout
         self._pf = None
         self.shard = shard_plan(self.cfg, self.world, self.rank)
@@ -739,7 +739,8 @@ class Engine:
         pb4, psw, k, n, pair = w4
         s, pf = self._stream_cur, self._pf
         hvdrv.qa8s_rows(src, pf["a8"], pf["sa"], k // BLOCK, m, s)
-        hvdrv.a4gemm_pp(pf["a8"], pf["sa"], pb4, psw, dst, k // 8, n, pair, m, s)
+        gemm = hvdrv.a4gemm_dq if self.gemv_layout == "dq" else hvdrv.a4gemm_pp
+        gemm(pf["a8"], pf["sa"], pb4, psw, dst, k // 8, n, pair, m, s)
 
     def _prefill_batched(self, prompt_ids, argmax: bool):
         """The prompt through every layer PREFILL_BATCH tokens at a time: per token the

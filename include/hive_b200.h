@@ -186,6 +186,9 @@ int hv_attn_rows_f16(const float* q, const uint16_t* kc, const uint16_t* vc, flo
  * the same matrix. No counterpart in the reference (its k_a4gv reads the row-major form). */
 int hv_w4_prepack_dq(const uint32_t* b4, const float* sw, int rows, int k, int pair_ffn,
                      uint32_t* pb4, float* psw, void* stream);
+/* hv_a4gemm_pp over weights in the dq arrangement (same results). */
+int hv_a4gemm_dq(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
+                 float* dst, int k8, int rows, int pair_ffn, int ntok, void* stream);
 int hv_a4gv_dq(const int8_t* a8, const float* sa, const uint32_t* pb4, const float* psw,
                float* dst, int k8, int rows, int pair_ffn, void* stream);
 /* hv_a4gv_pp's choice of kernel: 1 (default) lets small matrices use the iteration-split

@@ -97,3 +97,46 @@ def test_engine_dq_tiles_8b_shape(hv):
         assert np.array_equal(bits(la), bits(b.logits(prompt)))
     finally:
         b.free()
+
+
+@pytest.mark.parametrize("rows,k,pair,ntok", [(24, 512, 0, 11), (2048, 6144, 0, 37),
+                                              (2 * 1536, 4096, 1536, 40)])
+def test_prefill_gemm_dq_equals_pp(hv, rows, k, pair, ntok):
+    """hv_a4gemm_dq over dq tiles gives hv_a4gemm_pp's rows bit for bit."""
+    g = np.random.default_rng(rows + k + ntok)
+    p, sc = O.quantize_w4((g.standard_normal((rows, k)) * 0.02).astype(F32))
+    nib, scb = hv.w4_prepacked_size(rows, k, pair)
+    b4, sw = Dev(p), Dev(sc)
+    pp = (Dev(nbytes=nib), Dev(nbytes=scb))
+    dq = (Dev(nbytes=nib), Dev(nbytes=scb))
+    hv.w4_prepack(b4, sw, rows, k, pair, *pp)
+    hv.w4_prepack_dq(b4, sw, rows, k, pair, *dq)
+    x = (g.standard_normal((ntok, k)) * 2).astype(F32)
+    nb = k // 32
+    xd = Dev(x)
+    a8, sa = Dev(nbytes=ntok * k), Dev(nbytes=ntok * nb * 8)
+    hv.qa8s_rows(xd, a8, sa, nb, ntok)
+    y_pp, y_dq = Dev(nbytes=ntok * rows * 4), Dev(nbytes=ntok * rows * 4)
+    hv.a4gemm_pp(a8, sa, *pp, y_pp, k // 8, rows, pair, ntok)
+    hv.a4gemm_dq(a8, sa, *dq, y_dq, k // 8, rows, pair, ntok)
+    assert np.array_equal(bits(y_dq.get(F32)), bits(y_pp.get(F32)))
+
+
+def test_engine_dq_batched_prefill_equals_pp(hv):
+    """A 300-token prompt through the batched prefill (two 256-token runs) on dq tiles
+    leaves the pp engine's KV cache and logits bit for bit."""
+    import synth
+    arch = synth.tiny_arch(n_layer=2, hidden=512, ffn=1024, n_head=8, n_kv=2, vocab=4096)
+    out = []
+    for layout in ("pp", "dq"):
+        e = _engine(arch, 11, 320, prefill="batched", gemv_layout=layout)
+        try:
+            prompt = synth.prompt_ids(e.cfg, 11, 300)
+            lg = e.logits(prompt)
+            kv = np.empty(e.kv_bytes // 4, F32)
+            hv.download(kv.ctypes.data, e.d_kv, kv.nbytes)
+            out.append((lg, kv))
+        finally:
+            e.free()
+    assert np.array_equal(bits(out[0][0]), bits(out[1][0]))
+    assert np.array_equal(bits(out[0][1]), bits(out[1][1]))

@@ -131,10 +131,9 @@ def test_engine_rejects_unknown_kv_dtype():
 
 def test_engine_rejects_bad_gemv_layout():
     """Checked before any device work: an unknown arrangement, and dq tiles with the
-    binary16 cache or the batched prefill (neither has a dq form)."""
+    binary16 cache (the step has no such instantiation)."""
     import limited
     with pytest.raises(ValueError, match="gemv_layout"):
         limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="rowmajor")
-    for kw in ({"kv_dtype": "f16"}, {"prefill": "batched"}):
-        with pytest.raises(ValueError, match="dq"):
-            limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="dq", **kw)
+    with pytest.raises(ValueError, match="dq"):
+        limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="dq", kv_dtype="f16")

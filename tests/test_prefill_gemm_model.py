@@ -90,8 +90,10 @@ def bytes_s8(words):
     return np.ascontiguousarray(words, np.uint32).view(np.int8).reshape(*np.shape(words), 4)
 
 
-def model_gemm(a8, sa, pb4, psw, rows, k, pair, ntok):
-    """What k_a4gemm_pp computes, lane by lane: y [ntok, rows]."""
+def model_gemm(a8, sa, pb4, psw, rows, k, pair, ntok, layout="pp"):
+    """What k_a4gemm_pp computes, lane by lane: y [ntok, rows]. layout "dq": the weights
+    are in the dq arrangement and each lane loads word t of block j of row g from
+    (j & 1) * 128 + 4 (4 g + j // 2) + t (k_a4gemm_pp<true>)."""
     nb, niter = k // 32, k // 256
     it_end, pops = plan_of(nb)
     ntile = (pair + 3) // 4 if pair else (rows + 7) // 8
@@ -112,8 +114,13 @@ def model_gemm(a8, sa, pb4, psw, rows, k, pair, ntok):
                 n0, n1 = tq * 8 + 2 * t, tq * 8 + 2 * t + 1
                 sa0 = np.minimum(n0, ntok - 1) * 2 * nb
                 sa1 = np.minimum(n1, ntok - 1) * 2 * nb
-                wa = tile_a * niter * NIB_WORDS + 4 * lanes
-                wb = tile_b * niter * NIB_WORDS + 4 * lanes
+                lane_off = 4 * lanes if layout == "pp" else 16 * g + t
+                wa = tile_a * niter * NIB_WORDS + lane_off
+                wb = tile_b * niter * NIB_WORDS + lane_off
+                if layout == "pp":
+                    woff = [j if j < 4 else 128 + j - 4 for j in range(8)]
+                else:
+                    woff = [(j & 1) * 128 + 4 * (j >> 1) for j in range(8)]
                 sca = tile_a * niter * SCALES + 8 * g
                 scb = tile_b * niter * SCALES + 8 * g
                 act = tok_col * k + 8 * t
@@ -121,8 +128,8 @@ def model_gemm(a8, sa, pb4, psw, rows, k, pair, ntok):
                 st, leaf, leaf_begin = [], 0, 0
                 for it in range(niter):
                     wo, so = it * NIB_WORDS, it * SCALES
-                    wA = np.stack([pb4[wa + wo + (j if j < 4 else 128 + j - 4)] for j in range(8)])
-                    wB = np.stack([pb4[wb + wo + (j if j < 4 else 128 + j - 4)] for j in range(8)])
+                    wA = np.stack([pb4[wa + wo + woff[j]] for j in range(8)])
+                    wB = np.stack([pb4[wb + wo + woff[j]] for j in range(8)])
                     swA = np.stack([psw[sca + so + j] for j in range(8)])
                     swB = np.stack([psw[scb + so + j] for j in range(8)])
                     s0 = np.stack([sa[sa0 + 8 * it + j] for j in range(8)])
@@ -177,19 +184,24 @@ def model_gemm(a8, sa, pb4, psw, rows, k, pair, ntok):
     return y
 
 
+@pytest.mark.parametrize("layout", ["pp", "dq"])
 @pytest.mark.parametrize("rows,k,pair,ntok", [(24, 512, 0, 11), (24, 256, 12, 8),
                                               (16, 6144, 0, 3), (40, 1024, 20, 33)])
-def test_model_of_prefill_gemm_matches_oracle_per_token(rows, k, pair, ntok):
+def test_model_of_prefill_gemm_matches_oracle_per_token(rows, k, pair, ntok, layout):
     g = np.random.default_rng(rows * 7 + k + ntok)
     packed, scale = O.quantize_w4((g.standard_normal((rows, k)) * 0.02).astype(F32))
-    pb4, psw = prepack(packed, scale, rows, k, pair)
+    if layout == "pp":
+        pb4, psw = prepack(packed, scale, rows, k, pair)
+    else:
+        from test_gemv_dq_model import prepack_dq
+        pb4, psw = (x.reshape(-1) for x in prepack_dq(packed, scale, rows, k, pair))
     x = (g.standard_normal((ntok, k)) * 2).astype(F32)
     a8 = np.zeros((ntok, k), np.int8)
     sa = np.zeros((ntok, 2 * (k // 32)), F32)
     for n in range(ntok):
         q, s, b = O.quantize_act(x[n])
         a8[n], sa[n, :k // 32], sa[n, k // 32:] = q, s, b.view(F32)
-    y = model_gemm(a8, sa.reshape(-1), pb4, psw, rows, k, pair, ntok)
+    y = model_gemm(a8, sa.reshape(-1), pb4, psw, rows, k, pair, ntok, layout)
     for n in range(ntok):
         q, s, _ = O.quantize_act(x[n])
         _, want = O.gemv_q(q, s, packed, scale, k)

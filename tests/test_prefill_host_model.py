@@ -118,7 +118,15 @@ class FakeDevice:
         self.calls.append("a4gemm_pp")
         self._gemm(a8, sa, pb4, psw, dst, k8, rows, pair, ntok)
 
+    def a4gemm_dq(self, a8, sa, pb4, psw, dst, k8, rows, pair, ntok, stream=0):
+        self.calls.append("a4gemm_dq")
+        self._gemm(a8, sa, pb4, psw, dst, k8, rows, pair, ntok)
+
     def a4gv_pp(self, a8, sa, pb4, psw, dst, k8, rows, pair=0, stream=0):
+        self._gemm(a8, sa, pb4, psw, dst, k8, rows, pair, 1)
+
+    def a4gv_dq(self, a8, sa, pb4, psw, dst, k8, rows, pair=0, stream=0):
+        self.calls.append("a4gv_dq")
         self._gemm(a8, sa, pb4, psw, dst, k8, rows, pair, 1)
 
     def qk_rows(self, qkv, qn, kn, cos_t, sin_t, pos0, q_out, kc, vc, nq, nkv, hd, cap, eps,
@@ -176,13 +184,13 @@ class FakeDevice:
         self.view(pos, np.int32, 1)[0] += 1
 
 
-def fake_engine(dev, cfg, w, cap, fused, kv_dtype="f32"):
+def fake_engine(dev, cfg, w, cap, fused, kv_dtype="f32", gemv_layout="pp"):
     """An Engine whose device state lives on the fake device (constructor bypassed)."""
     c = cfg
     eng = object.__new__(limited.Engine)
     eng.cfg, eng.fused, eng.prefill_mode = c, fused, "batched"
     eng.kv_dtype, eng.kv_f16 = kv_dtype, kv_dtype == "f16"
-    eng.gemv_layout = "pp"
+    eng.gemv_layout = gemv_layout
     eng.world, eng.rank, eng._pf, eng._buffers, eng._stream_cur = 1, 0, None, [], 0
     eng.quiet = True
 
@@ -224,10 +232,12 @@ def fake_engine(dev, cfg, w, cap, fused, kv_dtype="f32"):
     return eng
 
 
-@pytest.mark.parametrize("fused,kv_dtype", [(False, "f32"), (True, "f32"), (True, "f16")])
-def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused, kv_dtype):
+@pytest.mark.parametrize("fused,kv_dtype,layout", [(False, "f32", "pp"), (True, "f32", "pp"),
+                                                   (True, "f16", "pp"), (False, "f32", "dq")])
+def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused, kv_dtype, layout):
     """kv_dtype "f16": the compressed-KV lane's prefill against the oracle run with the
-    same binary16 cache rounding."""
+    same binary16 cache rounding. layout "dq": the GEMMs and the head GEMV go to the dq
+    entry points (the fake device computes them from the same weights)."""
     arch = synth.tiny_arch(n_layer=2, hidden=256, ffn=512, n_head=4, n_kv=2, vocab=1000)
     cfg = Config(arch)
     cap = 320
@@ -236,8 +246,11 @@ def test_batched_prefill_host_code_matches_oracle(monkeypatch, fused, kv_dtype):
     prompt = synth.prompt_ids(cfg, 5, 300)
     dev = FakeDevice()
     monkeypatch.setattr(limited, "hvdrv", dev)
-    eng = fake_engine(dev, cfg, w, cap, fused, kv_dtype)
+    eng = fake_engine(dev, cfg, w, cap, fused, kv_dtype, layout)
     eng._prefill_batched(prompt, argmax=True)
+    gemm = "a4gemm_dq" if layout == "dq" else "a4gemm_pp"
+    assert dev.calls.count(gemm) == 2 * cfg.n_layer * 4      # 2 batches x 4 matrices
+    assert ("a4gv_dq" in dev.calls) == (layout == "dq")      # the LM head GEMV
     assert dev.calls.count("gather_rows") == 2               # 256 + 44 tokens
     sfx = "_f16" if kv_dtype == "f16" else ""
     assert dev.calls.count("qk_rows" + sfx) == dev.calls.count("attn_rows" + sfx) == 4
