@@ -750,13 +750,10 @@ def main(argv=None):
     for opt in [x for a in args.ab for x in a.split(",") if x.strip()]:
         if opt.partition("=")[0] not in ab_names or not opt.partition("=")[2].isdigit():
             ap.error(f"--ab option {opt!r}: NAME=VALUE with NAME in {', '.join(ab_names)}")
-    if any(parse_opts(a).get("layout_dq") for a in args.ab) and (
-            args.gemv_layout != "pp" or args.kv_dtype != "f32"):
-        ap.error("--ab layout_dq=1 compares against a pp engine with --kv-dtype f32")
+    if any(parse_opts(a).get("layout_dq") for a in args.ab) and args.gemv_layout != "pp":
+        ap.error("--ab layout_dq=1 compares a dq engine against the pp engine")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.gemv_layout == "dq" and args.kv_dtype != "f32":
-        ap.error("--gemv-layout dq runs with --kv-dtype f32")
     dist = Dist()
     try:
         if args.gemv_sweep:

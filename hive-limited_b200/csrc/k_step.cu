@@ -1499,7 +1499,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
 }
 
 // The step kernel for group size gs: variant 0 = f32 cache, 1 = f32 cache with the split
-// merge, 2 = binary16 cache, 3 = f32 cache over dq weight tiles.
+// merge, 2 = binary16 cache, 3 = f32 cache over dq weight tiles, 4 = binary16 cache over
+// dq weight tiles.
 static void* step_fn(int gs, int variant) {
   if (variant == 1) {
     switch (gs) {
@@ -1523,6 +1524,14 @@ static void* step_fn(int gs, int variant) {
       case 2: return (void*)k_step<2, false, float, true>;
       case 4: return (void*)k_step<4, false, float, true>;
       default: return (void*)k_step<8, false, float, true>;
+    }
+  }
+  if (variant == 4) {
+    switch (gs) {
+      case 1: return (void*)k_step<1, false, __half, true>;
+      case 2: return (void*)k_step<2, false, __half, true>;
+      case 4: return (void*)k_step<4, false, __half, true>;
+      default: return (void*)k_step<8, false, __half, true>;
     }
   }
   switch (gs) {
@@ -1669,19 +1678,17 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
              "hv_step_launch: kv_dtype %d (HV_KV_F32 or HV_KV_F16)", h.kv_dtype);
   HV_REQUIRE(h.w4_layout == HV_W4_PP || h.w4_layout == HV_W4_DQ, HV_E_INVALID,
              "hv_step_launch: w4_layout %d (HV_W4_PP or HV_W4_DQ)", h.w4_layout);
-  HV_REQUIRE(h.w4_layout == HV_W4_PP || h.kv_dtype == HV_KV_F32, HV_E_UNSUPPORTED,
-             "hv_step_launch: dq weight tiles run with the f32 cache");
   // the split merge (one GPU, f32 cache): its per-warp chunk weights live in the work area
   const bool split_merge = g_opt_split_merge && world == 1 && h.kv_dtype == HV_KV_F32 &&
       h.w4_layout == HV_W4_PP &&
       (lay.ring - lay.work) / sizeof(float) >= (size_t)kConsWarps * h.attn_chunks;
-  const int variant = h.w4_layout == HV_W4_DQ ? 3
-                      : h.kv_dtype == HV_KV_F16 ? 2 : split_merge ? 1 : 0;
+  const bool f16 = h.kv_dtype == HV_KV_F16;
+  const int variant = h.w4_layout == HV_W4_DQ ? (f16 ? 4 : 3) : f16 ? 2 : split_merge ? 1 : 0;
   void* fn = step_fn(gs, variant);
   {
     // set the function's shared-memory limit once per (kernel, device, size)
     static std::mutex mu;
-    static size_t done[16][64];
+    static size_t done[20][64];
     int dev = 0;
     HV_CUDA(cudaGetDevice(&dev));
     const int gi = (gs == 1 ? 0 : gs == 2 ? 1 : gs == 4 ? 2 : 3) + 4 * variant;

@@ -140,8 +140,7 @@ class Engine:
       gemv_layout       -- "pp" (default): weight tiles for tensor-pipe block dots
                            (hv_w4_prepack); "dq": the same tiles arranged for dp4a block
                            dots (hv_w4_prepack_dq, hv_a4gv_dq, hv_a4gemm_dq). Results are
-                           bit-identical; only the speed differs. "dq" runs with the f32
-                           cache.
+                           bit-identical; only the speed differs.
       kv_dtype          -- "f32" (default): the reference's fp32 KV cache; "f16": the
                            compressed-KV lane, an IEEE binary16 cache (half the KV bytes
                            per step). Each k/v row is rounded to nearest-even binary16 when
@@ -176,8 +175,6 @@ class Engine:
         self.kv_f16 = kv_dtype == "f16"
         if gemv_layout not in ("pp", "dq"):
             raise ValueError(f"gemv_layout={gemv_layout!r}: 'pp' or 'dq'")
-        if gemv_layout == "dq" and self.kv_f16:
-            raise ValueError("gemv_layout='dq' runs with the f32 cache")
         self.gemv_layout = gemv_layout
         self._pf = None
         self.shard = shard_plan(self.cfg, self.world, self.rank)

@@ -366,8 +366,7 @@ typedef struct hv_step_desc {
    * the arithmetic of hv_kv_append_f16 followed by hv_attn_decode_f16). */
   int kv_dtype;
   /* Arrangement of every prepacked weight tile: HV_W4_PP (0, hv_w4_prepack, block dots
-   * on the tensor pipe) or HV_W4_DQ (hv_w4_prepack_dq, dp4a block dots; same results;
-   * with the f32 cache only). */
+   * on the tensor pipe) or HV_W4_DQ (hv_w4_prepack_dq, dp4a block dots; same results). */
   int w4_layout;
 } hv_step_desc;
 

@@ -140,7 +140,7 @@ def test_ab_layout_set_runs_on_a_second_engine(monkeypatch):
 
 def test_ab_option_names_are_checked():
     with pytest.raises(SystemExit):
-        bench.main(["--ab", "layout_dq=1", "--kv-dtype", "f16"])
+        bench.main(["--ab", "layout_dq=1", "--gemv-layout", "dq"])
     with pytest.raises(SystemExit):
         bench.main(["--ab", "no_such_option=1"])
     with pytest.raises(SystemExit):

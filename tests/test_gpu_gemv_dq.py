@@ -140,3 +140,18 @@ def test_engine_dq_batched_prefill_equals_pp(hv):
             e.free()
     assert np.array_equal(bits(out[0][0]), bits(out[1][0]))
     assert np.array_equal(bits(out[0][1]), bits(out[1][1]))
+
+
+def test_engine_dq_tiles_with_binary16_cache(hv):
+    """dq tiles with the binary16 KV cache (k_step<GS, false, __half, true>): the pp
+    engine's logits with that cache, bit for bit."""
+    import synth
+    arch = synth.tiny_arch(n_layer=2, hidden=512, ffn=1024, n_head=8, n_kv=2, vocab=4096)
+    a = _engine(arch, 23, 64, kv_dtype="f16")
+    b = _engine(arch, 23, 64, kv_dtype="f16", gemv_layout="dq")
+    try:
+        prompt = synth.prompt_ids(a.cfg, 23, 12)
+        assert np.array_equal(bits(a.logits(prompt)), bits(b.logits(prompt)))
+    finally:
+        a.free()
+        b.free()

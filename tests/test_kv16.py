@@ -130,10 +130,7 @@ def test_engine_rejects_unknown_kv_dtype():
 
 
 def test_engine_rejects_bad_gemv_layout():
-    """Checked before any device work: an unknown arrangement, and dq tiles with the
-    binary16 cache (the step has no such instantiation)."""
+    """Checked before any device work."""
     import limited
     with pytest.raises(ValueError, match="gemv_layout"):
         limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="rowmajor")
-    with pytest.raises(ValueError, match="dq"):
-        limited.Engine(config=synth.tiny_arch(), tensors={}, gemv_layout="dq", kv_dtype="f16")
