@@ -1,0 +1,102 @@
+"""bench.py's decode line, produced on the CPU against a fake driver and a fake engine:
+one JSON line on stdout carrying every key the measurement contract names (metric,
+value, unit, n_gpus, steps, warmup, ms_per_step, higher_is_better, scaling,
+vs_baseline, dtype, data, config, roofline, cpu_baseline, e2e, gpu_launches, clocks),
+with the numbers derived from the device timing as documented: value = steps / time,
+roofline achieved = algorithmic bytes / step time. Only the host logic is under test;
+the numbers come from the B200 runs."""
+import ctypes
+import json
+import sys
+import types
+
+import numpy as np
+import pytest
+
+import bench
+
+
+class FakeDriver(types.ModuleType):
+    def __init__(self, ms):
+        super().__init__("hvdrv")
+        self.ms = ms
+        self.bufs = []
+
+    def host_alloc(self, n):
+        b = ctypes.create_string_buffer(int(n))
+        self.bufs.append(b)
+        return ctypes.addressof(b)
+
+    def event_elapsed_ms(self, a, b):
+        return self.ms
+
+    def __getattr__(self, name):        # every other call: accepted, no effect
+        return lambda *a, **k: 1
+
+
+class FakeEngine:
+    launched = 0
+
+    def __init__(self, *a, **kw):
+        self.kw = kw
+        self.d_pos, self.d_step, self.d_tok = 8, 16, 24
+        self.n_head_rows = 151936
+        self.cache_hit = None
+
+    def _prefill(self, prompt):
+        assert len(prompt) == 4096
+
+    def _decode_one(self):
+        FakeEngine.launched += 1
+
+    def _check_status(self):
+        pass
+
+    def free(self):
+        pass
+
+
+@pytest.mark.parametrize("extra", [[], ["--kv-dtype", "f16"], ["--gemv-layout", "dq"]])
+def test_decode_line_carries_the_contract(monkeypatch, capsys, extra):
+    import limited
+    drv = FakeDriver(ms=320.0)                              # 100 steps in 320 ms
+    monkeypatch.setitem(sys.modules, "hvdrv", drv)
+    monkeypatch.setattr(limited, "Engine", FakeEngine)
+    monkeypatch.setattr(bench.synth, "iter_tensors", lambda cfg, seed: iter(()))
+    assert bench.main(["--steps", "100", "--warmup", "3", "--no-cpu", "--e2e-steps", "0",
+                       *extra]) == 0
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    ln = lines[0]
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks"):
+        assert key in ln, key
+    assert ln["n_gpus"] == 1 and ln["steps"] == 100 and ln["warmup"] == 3
+    assert ln["ms_per_step"] == pytest.approx(3.2)
+    assert ln["value"] == pytest.approx(100 / 0.32)
+    assert ln["higher_is_better"] is True and ln["scaling"] == "weak"
+    assert ln["config"]["workload"] == "qwen3-8b-p4096-g256"
+    rf = ln["roofline"]
+    for key in ("bound", "achieved", "peak", "unit", "frac", "traffic"):
+        assert key in rf, key
+    assert rf["bound"] == "hbm" and rf["unit"] == "GB/s"
+    assert rf["achieved"] == pytest.approx(rf["bytes_per_step"] / 3.2e-3 / 1e9)
+    assert rf["frac"] == pytest.approx(rf["achieved"] / rf["peak"])
+    kv = dict(zip(extra[::2], extra[1::2])).get("--kv-dtype", "f32")
+    assert ln["config"]["kv"] == kv
+    if kv == "f16":                      # half the KV bytes, and no f32 ncu traffic figure
+        assert rf["traffic"] is None
+    assert set(ln["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
+    assert ln["gpu_launches"] == 100
+    assert set(ln["clocks"]) >= {"sm_mhz", "sm_max_mhz", "reasons"}
+
+
+def test_step_bytes_counts_the_kv_element_size():
+    import w4format
+    cfg = w4format.Config(bench.synth.ARCH["qwen3-8b"])
+    b32 = bench.step_bytes(cfg, 151936, 4224)
+    b16 = bench.step_bytes(cfg, 151936, 4224, kv_elem=2)
+    kv32 = 2 * cfg.n_layer * cfg.n_kv * 128 * 4 * 4225
+    assert b32 - b16 == kv32 // 2
+    assert b32 == pytest.approx(5.976e9, rel=2e-3)          # weights + scales + fp32 KV
