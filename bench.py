@@ -249,13 +249,10 @@ def run_reference(args, dist: Dist):
         return 0
     arch, seed, n_prompt, n_new = synth.WORKLOADS[args.workload]
     cfg = w4format.Config(synth.ARCH[arch])
-    per_step = []
-    total_steps, total_s = 0, 0.0
     rate, done, dt, threads, setup = cpu_decode_sample(cfg, seed, n_prompt,
                                                        max(args.warmup + args.steps, 2),
                                                        budget_s=args.cpu_budget)
-    total_steps, total_s = done, dt
-    value = total_steps / total_s
+    value = done / dt
     sample = (f"{done} oracle decode steps of {arch} at positions {n_prompt}..; "
               f"KV rows of the prompt filled with seeded values; setup {setup:.0f} s")
     line = {
@@ -271,7 +268,6 @@ def run_reference(args, dist: Dist):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    del per_step
     return 0
 
 

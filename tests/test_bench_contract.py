@@ -100,3 +100,23 @@ def test_step_bytes_counts_the_kv_element_size():
     kv32 = 2 * cfg.n_layer * cfg.n_kv * 128 * 4 * 4225
     assert b32 - b16 == kv32 // 2
     assert b32 == pytest.approx(5.976e9, rel=2e-3)          # weights + scales + fp32 KV
+
+
+def test_reference_line_carries_the_contract(monkeypatch, capsys):
+    """--impl reference: the CPU restatement's timing on rank 0, with impl, cpu_baseline
+    and an e2e block of zero copies; the CPU sample itself is stubbed here."""
+    monkeypatch.setattr(bench, "cpu_decode_sample",
+                        lambda cfg, seed, n_prompt, n_steps, budget_s: (0.5, 8, 16.0, 32, 4.0))
+    assert bench.main(["--impl", "reference", "--steps", "5", "--warmup", "3"]) == 0
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    ln = lines[0]
+    assert ln["impl"] == "reference"
+    assert ln["value"] == pytest.approx(0.5) and ln["unit"] == bench.UNIT
+    assert ln["metric"] == bench.METRIC and ln["higher_is_better"] is True
+    cb = ln["cpu_baseline"]
+    assert cb["value"] == ln["value"] and cb["cores"] == 32 and cb["kind"] in ("port",
+                                                                              "reference")
+    assert ln["e2e"] == {"value": ln["value"], "unit": ln["unit"], "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}
+    assert ln["config"]["workload"] == "qwen3-8b-p4096-g256"
