@@ -7,6 +7,7 @@ roofline achieved = algorithmic bytes / step time. Only the host logic is under 
 the numbers come from the B200 runs."""
 import ctypes
 import json
+import os
 import sys
 import types
 
@@ -14,6 +15,9 @@ import numpy as np
 import pytest
 
 import bench
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TESTS = os.path.dirname(os.path.abspath(__file__))
 
 
 class FakeDriver(types.ModuleType):
@@ -31,6 +35,8 @@ class FakeDriver(types.ModuleType):
         return self.ms
 
     def __getattr__(self, name):        # every other call: accepted, no effect
+        if name.startswith("__"):       # module introspection (importers, torch) sees none
+            raise AttributeError(name)
         return lambda *a, **k: 1
 
 
@@ -120,3 +126,61 @@ def test_reference_line_carries_the_contract(monkeypatch, capsys):
     assert ln["e2e"] == {"value": ln["value"], "unit": ln["unit"], "h2d_bytes_per_step": 0,
                          "d2h_bytes_per_step": 0}
     assert ln["config"]["workload"] == "qwen3-8b-p4096-g256"
+
+
+def _rank_bench(rank, world, port, mode, result):
+    """One rank of `bench.py --gpus 2` on the CPU: gloo plumbing, fake driver and engine
+    (each rank's device time differs, so the max over ranks is visible)."""
+    import contextlib
+    import io
+    sys.path[:0] = [p for p in (os.path.join(REPO, "hive-limited_b200"),
+                                os.path.join(REPO, "oracle"), REPO, TESTS) if p not in sys.path]
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        import bench as b
+        import limited
+        sys.modules["hvdrv"] = FakeDriver(ms=300.0 + 20.0 * rank)
+        limited.Engine = FakeEngine
+        b.synth.iter_tensors = lambda cfg, seed: iter(())
+        out = io.StringIO()
+        with contextlib.redirect_stdout(out):
+            rc = b.main(["--gpus", str(world), "--steps", "100", "--warmup", "3", "--no-cpu",
+                         "--e2e-steps", "0", "--mode", mode])
+        result.put((rank, rc, out.getvalue()))
+    except BaseException as e:                  # report, do not hang the parent
+        result.put((rank, -1, repr(e)))
+    finally:
+        result.close()
+        result.join_thread()
+
+
+@pytest.mark.parametrize("mode", ["sharded", "replicas"])
+def test_two_rank_line(mode):
+    """Rank 0 alone prints; ms_per_step is the slower rank's; sharded: one stream's
+    tok/s (strong scaling, roofline peak x 2); replicas: the sum over streams (weak)."""
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_bench, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, (rc, out)) for r, rc, out in (q.get(timeout=240) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[0][0] == 0 and got[1][0] == 0, got
+    assert not [x for x in got[1][1].splitlines() if x.startswith("{")]
+    lines = [json.loads(x) for x in got[0][1].splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    ln = lines[0]
+    assert ln["n_gpus"] == 2 and ln["ms_per_step"] == pytest.approx(3.2)
+    if mode == "sharded":
+        assert ln["scaling"] == "strong" and ln["value"] == pytest.approx(100 / 0.32)
+        assert ln["roofline"]["frac"] == pytest.approx(ln["roofline"]["achieved"]
+                                                       / ln["roofline"]["peak"])
+    else:
+        assert ln["scaling"] == "weak" and ln["value"] == pytest.approx(2 * 100 / 0.32)
