@@ -1233,7 +1233,8 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
 // CTA of that head while every other CTA waits. Lane d of the warp does dim d of the
 // block; the arithmetic and its order are attn_merge's (M = max_c m_c, w_c = exp(m_c - M),
 // L = fma(w_c, l_c, L) and o = fma(w_c, acc_c, o) in chunk order, ctx = o * (1 / L), then
-// quant_a8s of the block), so the bits are the same. `area`: kConsWarps * nch floats.
+// quant_a8s of the block), so the bits are the same; only the loads are arranged for
+// fewer L2 round trips. `area`: kConsWarps * nch floats.
 template <int GS>
 __device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1252,22 +1253,32 @@ __device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
     for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(ph + c * kChunk));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-    for (int c = lane; c < nch; c += 32) wv[c] = expf(__ldcg(ph + c * kChunk) - M);
-    __syncwarp();
-    float inv = 0.f;
-    if (lane == 0) {
-      float L = 0.f;
-      for (int c = 0; c < nch; ++c) L = fmaf(wv[c], __ldcg(ph + c * kChunk + 1), L);
-      inv = 1.0f / L;
+    // w_c = exp(m_c - M) and l_c, loaded by lane c of each pass of 32 chunks together (one
+    // L2 round trip per pass); every lane then runs the chain L = fma(w_c, l_c, L) in chunk
+    // order from shuffles, so L is attn_merge's value in every lane
+    float L = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const int c = c0 + lane;
+      float w = 0.f, l = 0.f;
+      if (c < nch) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(ph + c * kChunk));
+        w = expf(ml.x - M);
+        l = ml.y;
+        wv[c] = w;
+      }
+      const int n = min(32, nch - c0);
+      for (int k = 0; k < n; ++k)
+        L = fmaf(__shfl_sync(0xFFFFFFFFu, w, k), __shfl_sync(0xFFFFFFFFu, l, k), L);
     }
-    inv = __shfl_sync(0xFFFFFFFFu, inv, 0);
+    const float inv = 1.0f / L;
+    __syncwarp();                                   // wv[] of every lane
     float o = 0.f;
-    for (int c0 = 0; c0 < nch; c0 += 8) {
-      float a[8];
+    for (int c0 = 0; c0 < nch; c0 += 16) {
+      float a[16];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a[k] = (c0 + k < nch) ? __ldcg(ph + (c0 + k) * kChunk + 4 + d) : 0.f;
+      for (int k = 0; k < 16; ++k) a[k] = (c0 + k < nch) ? __ldcg(ph + (c0 + k) * kChunk + 4 + d) : 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
+      for (int k = 0; k < 16; ++k)
         if (c0 + k < nch) o = fmaf(wv[c0 + k], a[k], o);
     }
     int8_t q8;
