@@ -114,7 +114,7 @@ def test_ab_loop_times_every_set_and_restores_options(monkeypatch):
 def test_ab_layout_set_runs_on_a_second_engine(monkeypatch):
     """layout_dq=1 times a second engine (built once, freed at the end) with its own
     decode loop; the step options are applied around it as for every set, and logits
-    identity is judged against the baseline engine's."""
+    identity is checked against the baseline engine's."""
     drv = FakeDriver()
     pin = (np.ctypeslib.ctypes.c_int32 * 4)()
     addr = np.ctypeslib.ctypes.addressof(pin)
