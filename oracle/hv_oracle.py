@@ -2,10 +2,11 @@
 
 A CPU restatement, in numpy, of the numeric contract of HIVE Limited's batch-1 decode
 step (engine/reference.py and the weight format of engine/limited.py). Only tests/,
-__graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as the checker.
+__graft_entry__.smoke() and bench.py's CPU-baseline leg use it, to check and time
+the product against.
 
 Pinning: every function below is checked against golden vectors produced by running
-the reference's own engine/reference.py in the build container
+the reference's own engine/reference.py where its checkout is present
 (tests/golden/make_golden.py writes them, tests/test_oracle.py checks them):
 
 * bit-exact: quantize_w4, quantize_act, the int32 block dots, gemv_w4's fp32 output

@@ -1,6 +1,6 @@
 """Generate golden vectors by running HIVE Limited's own numpy reference.
 
-Runs ONLY where the reference checkout exists (the build container); the resulting
+Runs ONLY where the reference checkout exists; the resulting
 .npz files are committed and the tests read those, never the reference itself.
 
     python tests/golden/make_golden.py ops         # op-level vectors (seconds)

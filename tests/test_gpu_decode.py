@@ -6,7 +6,7 @@
 * the tiny model after 300- and 2000-token prompts, where decode attention runs over
   every sequence chunk (several position blocks per chunk at 2000);
 * the 1.7B-shaped workload (32-token prompt, 64 greedy tokens) against the tokens and
-  logits the reference produced in the build container;
+  logits the reference produced where its checkout is present;
 * 8B- and 32B-shaped models against the C oracle at short prompts.
 """
 import os
@@ -134,7 +134,7 @@ def test_context_guard(hv):
 
 
 def test_qwen3_1p7b_shape_matches_reference(hv, golden):
-    """32-token random prompt, 64 greedy tokens; the reference ran in the build container
+    """32-token random prompt, 64 greedy tokens; the reference ran where its checkout is
     (tests/golden/make_golden.py c1). The reference's own acceptance rule applies
     (verify.py:57-81): tokens agree, or the first divergence is a near-tie fork whose
     top-2 logit margin is below ln 2. Logits stay within the model's sensitivity floor."""
