@@ -8,6 +8,7 @@ Runs ONLY where the reference checkout exists; the resulting
     python tests/golden/make_golden.py tiny        # tiny-model greedy decode (seconds)
     python tests/golden/make_golden.py long        # tiny model, 300- and 2000-token prompts
     python tests/golden/make_golden.py c1          # 1.7B-shape 32+64 decode (~1 hour)
+    python tests/golden/make_golden.py c3          # 8B-shape 4+2 decode (~40 GB RAM)
 
 The reference's engine/limited.py dlopens libcuda at import; a stub `cudrv` module is
 placed in sys.modules first so that its pure-numpy parts (quantize_w4, Config) and all of
@@ -216,6 +217,11 @@ def main(argv):
         make_decode(HERE / "decode_tiny_long.npz", synth.tiny_arch(), 9, 300, 8, True)
         # over 20 positions per chunk on a 148-SM part: several position blocks per chunk
         make_decode(HERE / "decode_tiny_2k.npz", synth.tiny_arch(), 10, 2000, 4, True)
+    elif what == "c3":
+        # the 8B geometry (weights of the 8B workload's seed), the 4-token prompt the GPU
+        # test of the large shapes uses, 2 greedy tokens
+        arch, seed = synth.WORKLOADS["qwen3-8b-p4096-g256"][:2]
+        make_decode(HERE / "decode_qwen3_8b_p4.npz", synth.ARCH[arch], seed, 4, 2, False)
     elif what == "c1":
         arch, seed, n_prompt, n_new = synth.WORKLOADS["qwen3-1.7b-p32-g64"]
         make_decode(HERE / "decode_qwen3_1p7b.npz", synth.ARCH[arch], seed, n_prompt,

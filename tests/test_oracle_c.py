@@ -74,3 +74,33 @@ def test_quantize_model_c_matches_numpy():
                 assert all(np.array_equal(x, y) for x, y in zip(a[key], b[key])), key
             else:
                 assert np.array_equal(a[key], b[key]), key
+
+
+@pytest.mark.skipif(not __import__("os").environ.get("HV_SLOW_TESTS"),
+                    reason="set HV_SLOW_TESTS=1 (the 1.7B and 8B models drawn and quantised)")
+@pytest.mark.parametrize("name,workload,n_new", [
+    ("decode_qwen3_1p7b.npz", "qwen3-1.7b-p32-g64", 3),
+    ("decode_qwen3_8b_p4.npz", "qwen3-8b-p4096-g256", 2)])
+def test_fast_oracle_matches_reference_at_real_shapes(golden, name, workload, n_new):
+    """The oracle at the 1.7B and 8B geometries against the reference's own decode of the
+    same seeded model (tests/golden, make_golden.py c1 / c3): the greedy tokens, and every
+    step's logits bit for bit (sha256), on the host that made the fixtures."""
+    import hashlib
+
+    import synth
+    import w4format
+    try:
+        g = golden(name)
+    except FileNotFoundError:
+        pytest.skip(f"{name} not generated")
+    arch, seed = synth.WORKLOADS[workload][:2]
+    cfg = w4format.Config(synth.ARCH[arch])
+    prompt = g["prompt"].tolist()
+    assert prompt == synth.prompt_ids(cfg, seed, len(prompt))
+    w = O.quantize_model_c(cfg, synth.iter_tensors(cfg, seed))
+    m = O.FastOracleModel(cfg, w, len(prompt) + n_new + 2)
+    toks, logits = m.generate(prompt, n_new)
+    assert toks == g["tokens"].tolist()[:n_new]
+    for i, lg in enumerate(logits):
+        assert hashlib.sha256(np.ascontiguousarray(lg).tobytes()).hexdigest() == \
+            str(g["logits_sha"][i]), i
