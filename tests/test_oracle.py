@@ -108,6 +108,7 @@ def test_attention_matches_reference(golden, i):
     ("decode_tiny_tied.npz", synth.tiny_arch(n_layer=3, hidden=512, ffn=1024, n_head=8,
                                              n_kv=2, vocab=2048, tied=True), 8, 9),
     ("decode_tiny_long.npz", synth.tiny_arch(), 9, 300),
+    ("decode_tiny_2k.npz", synth.tiny_arch(), 10, 2000),
 ])
 def test_oracle_model_matches_reference_decode(golden, name, arch, seed, n_prompt):
     g = golden(name)
