@@ -35,6 +35,25 @@ def test_binding_covers_header():
     assert set(header_symbols()) == set(hvdrv.exported_symbols())
 
 
+def header_arities() -> dict:
+    """Parameter count of every hv_* declaration in the header ((void) counts 0)."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\bint\s+(hv_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_binding_arities_match_header():
+    """Every ctypes signature in hvdrv has the header's parameter count."""
+    import hvdrv
+    ar = header_arities()
+    assert set(ar) == set(hvdrv._SIGS)
+    bad = {n: (len(hvdrv._SIGS[n]), ar[n]) for n in ar if len(hvdrv._SIGS[n]) != ar[n]}
+    assert not bad, bad
+
+
 def test_library_version_and_kernels(lib):
     import hvdrv
     hvdrv.load()
