@@ -370,7 +370,7 @@ def run_ours(args, dist: Dist):
     def make_engine(gemv_layout):
         return limited.Engine(
             config=cfg, tensors=synth.iter_tensors(cfg, seed), quiet=True, max_context=cap,
-            device=dist.local, fused=True, world=dist.world if sharded else 1,
+            device=dist.local, fused=not args.eager, world=dist.world if sharded else 1,
             rank=dist.rank if sharded else 0,
             exchange=dist.allgather_bytes if sharded else None,
             weight_cache=args.weight_cache, prefill=args.prefill,
@@ -448,7 +448,7 @@ def run_ours(args, dist: Dist):
     peak, peak_kind = measured_peak()
     achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
     # the committed ncu capture is of the f32-cache step
-    traffic = (None if sharded or args.kv_dtype != "f32"
+    traffic = (None if sharded or args.kv_dtype != "f32" or args.eager
                else profiled_traffic("k_step_qwen3-8b_decode.md"))
 
     if args.profile and dist.rank == 0:
@@ -497,6 +497,7 @@ def run_ours(args, dist: Dist):
                        "prompt": n_prompt, "generated": n_new, "kv": args.kv_dtype,
                        "weights": "int4 + f32 scale per 32 (5.00 bits/weight)",
                        "gemv_layout": args.gemv_layout,
+                       "step": "eager kernel sequence" if args.eager else "fused (one launch)",
                        "parallelism": (f"column-sharded x{dist.world} (NVLink peer stores "
                                        "inside the fused step)" if sharded else
                                        "replicas" if dist.world > 1 else "single"),
@@ -504,12 +505,15 @@ def run_ours(args, dist: Dist):
                        "positions": f"{min(positions)}..{max(positions)}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * n_peak,
                          "unit": "GB/s", "frac": achieved / (peak * n_peak), "traffic": traffic,
-                         "peak_kind": peak_kind, "kernel": "k_step",
+                         "peak_kind": peak_kind,
+                         "kernel": "eager sequence" if args.eager else "k_step",
                          "bytes_per_step": bytes_mean},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_all, "unit": UNIT, "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
-            "gpu_launches": args.steps,
+            # the fused step is one launch; the eager sequence is the reference's 19 per
+            # layer plus the embedding gather, final norm, head (2) and argmax (2)
+            "gpu_launches": args.steps * (19 * cfg.n_layer + 6 if args.eager else 1),
             "clocks": clk,
             "load_s": round(t_load, 1), "prefill_s": round(t_prefill, 2),
             "prefill": args.prefill, "step_options": args.step_opt,
@@ -721,6 +725,9 @@ def main(argv=None):
     ap.add_argument("--kv-dtype", default="f32", choices=["f32", "f16"],
                     help="KV cache element type: f32 (the reference's cache) or f16 (the "
                          "compressed-KV lane)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the reference's kernel-by-kernel sequence (19 launches per "
+                         "layer) instead of the fused step, e.g. for a per-kernel ncu list")
     ap.add_argument("--gemv-layout", default="pp", choices=["pp", "dq"],
                     help="weight tiles for tensor-pipe block dots (pp) or dp4a block dots "
                          "(dq); results are bit-identical")
@@ -750,6 +757,9 @@ def main(argv=None):
         ap.error("--ab layout_dq=1 compares a dq engine against the pp engine")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.eager and (args.ab or (int(os.environ.get("WORLD_SIZE", "1")) > 1
+                                   and args.mode == "sharded")):
+        ap.error("--eager runs one GPU per stream (no --ab, no sharded mode)")
     dist = Dist()
     try:
         if args.gemv_sweep:

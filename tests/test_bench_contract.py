@@ -43,8 +43,11 @@ class FakeDriver(types.ModuleType):
 class FakeEngine:
     launched = 0
 
+    last_kw = {}
+
     def __init__(self, *a, **kw):
         self.kw = kw
+        FakeEngine.last_kw = kw
         self.d_pos, self.d_step, self.d_tok = 8, 16, 24
         self.n_head_rows = 151936
         self.cache_hit = None
@@ -62,7 +65,8 @@ class FakeEngine:
         pass
 
 
-@pytest.mark.parametrize("extra", [[], ["--kv-dtype", "f16"], ["--gemv-layout", "dq"]])
+@pytest.mark.parametrize("extra", [[], ["--kv-dtype", "f16"], ["--gemv-layout", "dq"],
+                                   ["--eager"]])
 def test_decode_line_carries_the_contract(monkeypatch, capsys, extra):
     import limited
     drv = FakeDriver(ms=320.0)                              # 100 steps in 320 ms
@@ -89,12 +93,16 @@ def test_decode_line_carries_the_contract(monkeypatch, capsys, extra):
     assert rf["bound"] == "hbm" and rf["unit"] == "GB/s"
     assert rf["achieved"] == pytest.approx(rf["bytes_per_step"] / 3.2e-3 / 1e9)
     assert rf["frac"] == pytest.approx(rf["achieved"] / rf["peak"])
-    kv = dict(zip(extra[::2], extra[1::2])).get("--kv-dtype", "f32")
+    kv = dict(zip(extra[::2], extra[1::2])).get("--kv-dtype", "f32") if len(extra) != 1 \
+        else "f32"
     assert ln["config"]["kv"] == kv
     if kv == "f16":                      # half the KV bytes, and no f32 ncu traffic figure
         assert rf["traffic"] is None
     assert set(ln["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
-    assert ln["gpu_launches"] == 100
+    eager = "--eager" in extra
+    assert ln["gpu_launches"] == 100 * (19 * 36 + 6 if eager else 1)
+    assert (ln["roofline"]["kernel"] == "eager sequence") == eager
+    assert FakeEngine.last_kw["fused"] is (not eager)
     assert set(ln["clocks"]) >= {"sm_mhz", "sm_max_mhz", "reasons"}
 
 
