@@ -201,19 +201,24 @@ class Engine:
         self._graph_ok = None
         self._stream = 0
         self._stream_cur = 0
-        entry = wcache.open_entry(weight_cache, key) if weight_cache is not None else None
-        if entry is not None:
-            self._upload_cached(entry)
-            self.cache_hit = True
-        else:
-            src = _TensorSource(tensors if tensors is not None
-                                else load_model_tensors(model_dir))
-            self._upload_weights(src, quantize_on)
-            del src
-            if weight_cache is not None:
-                self._save_cache(weight_cache, key, ident)
-                self.cache_hit = False
-        self._alloc_state()
+        try:
+            entry = wcache.open_entry(weight_cache, key) if weight_cache is not None else None
+            if entry is not None:
+                self._upload_cached(entry)
+                self.cache_hit = True
+            else:
+                src = _TensorSource(tensors if tensors is not None
+                                    else load_model_tensors(model_dir))
+                self._upload_weights(src, quantize_on)
+                del src
+                if weight_cache is not None:
+                    self._save_cache(weight_cache, key, ident)
+                    self.cache_hit = False
+            self._alloc_state()
+        except BaseException:
+            # the caller gets no engine to free(): release what was allocated so far
+            self.free()
+            raise
 
     # -- setup ----------------------------------------------------------------------
 
@@ -238,29 +243,36 @@ class Engine:
         and up rows). -> (pb4, psw, K, N, pair_ffn)"""
         k = parts[0].shape[1]
         n = sum(p.shape[0] for p in parts)
-        if self._quantize_on == "host":
-            w = np.concatenate([p.astype(F32, copy=False) for p in parts], 0)
-            packed, scale = quantize_w4(w)
-            b4 = hvdrv.alloc(packed.nbytes)
-            sw = hvdrv.alloc(scale.nbytes)
-            hvdrv.upload(b4, packed.ctypes.data, packed.nbytes)
-            hvdrv.upload(sw, scale.ctypes.data, scale.nbytes)
-        else:
-            b4 = hvdrv.alloc(n * k // 2)
-            sw = hvdrv.alloc(n * k // BLOCK * 4)
-            off = 0
-            for p in parts:
-                p = np.ascontiguousarray(p, dtype=F32)
-                hvdrv.upload(self._stage + off, p.ctypes.data, p.nbytes)
-                off += p.nbytes
-            hvdrv.quantize_w4(self._stage, b4, sw, n, k)
-        nib_bytes, sc_bytes = hvdrv.w4_prepacked_size(n, k, pair_ffn)
-        pb4, psw = self._alloc(nib_bytes), self._alloc(sc_bytes)
-        prepack = hvdrv.w4_prepack_dq if self.gemv_layout == "dq" else hvdrv.w4_prepack
-        prepack(b4, sw, n, k, pair_ffn, pb4, psw)
-        hvdrv.synchronize()
-        hvdrv.free(b4)
-        hvdrv.free(sw)
+        tmp = []                          # the reference-layout copy, freed below
+        try:
+            if self._quantize_on == "host":
+                w = np.concatenate([p.astype(F32, copy=False) for p in parts], 0)
+                packed, scale = quantize_w4(w)
+                b4 = hvdrv.alloc(packed.nbytes)
+                tmp.append(b4)
+                sw = hvdrv.alloc(scale.nbytes)
+                tmp.append(sw)
+                hvdrv.upload(b4, packed.ctypes.data, packed.nbytes)
+                hvdrv.upload(sw, scale.ctypes.data, scale.nbytes)
+            else:
+                b4 = hvdrv.alloc(n * k // 2)
+                tmp.append(b4)
+                sw = hvdrv.alloc(n * k // BLOCK * 4)
+                tmp.append(sw)
+                off = 0
+                for p in parts:
+                    p = np.ascontiguousarray(p, dtype=F32)
+                    hvdrv.upload(self._stage + off, p.ctypes.data, p.nbytes)
+                    off += p.nbytes
+                hvdrv.quantize_w4(self._stage, b4, sw, n, k)
+            nib_bytes, sc_bytes = hvdrv.w4_prepacked_size(n, k, pair_ffn)
+            pb4, psw = self._alloc(nib_bytes), self._alloc(sc_bytes)
+            prepack = hvdrv.w4_prepack_dq if self.gemv_layout == "dq" else hvdrv.w4_prepack
+            prepack(b4, sw, n, k, pair_ffn, pb4, psw)
+            hvdrv.synchronize()
+        finally:
+            for q in tmp:
+                hvdrv.free(q)
         return pb4, psw, k, n, pair_ffn
 
     def _upload_weights(self, src: _TensorSource, quantize_on: str):
