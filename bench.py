@@ -637,6 +637,109 @@ def run_gemv_sweep(args, dist: Dist):
     return 0
 
 
+def run_head_argmax(args, dist: Dist):
+    """The LM-head GEMV + greedy argmax workload (151936 x 5120 int4 weights from seed 4,
+    N(0,1) hidden states quantised per 32), vocabulary-sharded over the ranks: rank r holds
+    rows [r V/N, (r+1) V/N) in the engine's tile layout and, for every hidden state, runs
+    the GEMV of its shard and folds its logits into that state's 64-bit argmax key
+    (hv_a4gv_pp + hv_argmax_key). Device time over `--head-states` states (CUDA events, max
+    over ranks); weight copies rotate so the shard is read from HBM, not L2. After the
+    timed region the keys are all-gathered on the host (8 bytes per state and rank) and
+    the tokens formed. Their parity with np.argmax is tests/test_gpu_head_argmax.py's."""
+    import hvdrv
+    hvdrv.init()
+    hvdrv.retain_primary_context(hvdrv.device(dist.local))
+    n_all, k = synth.HEAD_SHAPE
+    world, rank = dist.world, dist.rank
+    if n_all % world:
+        raise SystemExit(f"{n_all} vocabulary rows do not split over {world} ranks")
+    rows = n_all // world
+    r0 = rank * rows
+    ns = args.head_states
+    w, h = synth.head_case(ns)
+    nb = k // 32
+    bufs = []
+
+    def dev(nbytes):
+        p = hvdrv.alloc(nbytes)
+        bufs.append(p)
+        return p
+
+    ws = np.ascontiguousarray(w[r0:r0 + rows])
+    wd = hvdrv.alloc(ws.nbytes)
+    hvdrv.upload(wd, ws.ctypes.data, ws.nbytes)
+    b4, sw = dev(rows * k // 2), dev(rows * nb * 4)
+    hvdrv.quantize_w4(wd, b4, sw, rows, k)
+    hvdrv.synchronize()
+    hvdrv.free(wd)
+    nib, scb = hvdrv.w4_prepacked_size(rows, k, 0)
+    alg = rows * k * 5 // 8
+    copies = max(1, -(-(args.gemv_rotate_mb << 20) // alg)) if args.gemv_rotate_mb else 1
+    rot = []
+    for _ in range(copies):
+        p, q = dev(nib), dev(scb)
+        hvdrv.w4_prepack(b4, sw, rows, k, 0, p, q)
+        rot.append((p, q))
+    hd = dev(ns * k * 4)
+    hvdrv.upload(hd, np.ascontiguousarray(h).ctypes.data, ns * k * 4)
+    a8, sa = dev(ns * k), dev(ns * nb * 8)
+    hvdrv.qa8s_rows(hd, a8, sa, nb, ns)
+    logits, keys = dev(rows * 4), dev(ns * 8)
+
+    def run(i0, i1):
+        for i in range(i0, i1):
+            pb, ps = rot[i % copies]
+            hvdrv.a4gv_pp(a8 + i * k, sa + i * nb * 8, pb, ps, logits, k // 8, rows, 0)
+            hvdrv.argmax_key(logits, rows, r0, keys + 8 * i)
+
+    warm = min(args.warmup, ns)
+    hvdrv.memset8(keys, 0, ns * 8)
+    run(0, warm)
+    hvdrv.synchronize()
+    hvdrv.memset8(keys, 0, ns * 8)
+    e0, e1 = hvdrv.event_create(), hvdrv.event_create()
+    dist.barrier()
+    hvdrv.synchronize()
+    hvdrv.event_record(e0, 0)
+    run(0, ns)
+    hvdrv.event_record(e1, 0)
+    hvdrv.synchronize()
+    ms = dist.max(hvdrv.event_elapsed_ms(e0, e1))
+    mine = np.zeros(ns, np.uint64)
+    hvdrv.download(mine.ctypes.data, keys, ns * 8)
+    blobs = dist.allgather_bytes(mine.tobytes())
+    best = np.max(np.stack([np.frombuffer(b, np.uint64) for b in blobs]), axis=0)
+    toks = [hvdrv.token_of_key(int(x)) for x in best]
+    line = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        per_state_s = ms / 1e3 / ns
+        achieved = alg / per_state_s / 1e9              # GB/s on each GPU
+        line = {
+            "metric": "LM-head GEMV + greedy argmax (151936x5120 W4A8, vocabulary-sharded)",
+            "value": ns / (ms / 1e3), "unit": "hidden states/s", "n_gpus": world,
+            "steps": ns, "warmup": warm, "ms_per_step": ms / ns, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seed 4 head weights, N(0,1) hidden states)",
+            "config": {"workload": "lm-head-argmax", "shape": [n_all, k], "shards": world,
+                       "rows_per_shard": rows, "states": ns,
+                       "l2": f"{copies} rotating weight copies per rank",
+                       "exchange": "8-byte key per state and rank, all-gathered on the "
+                                   "host after the timed region"},
+            "roofline": {"bound": "hbm", "achieved": achieved * world,
+                         "peak": peak * world, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "k_a4gv_pp + k_argmax_key",
+                         "bytes_per_state_per_gpu": alg},
+            "tokens": {"first": toks[:8], "all_valid": all(0 <= t < n_all for t in toks)},
+            "gpu_launches": 2 * ns,
+        }
+        print(json.dumps(line), flush=True)
+    for p in bufs:
+        hvdrv.free(p)
+    return 0 if line is None or line["tokens"]["all_valid"] else 1
+
+
 def run_prefill_sweep(args, dist: Dist):
     """The prefill GEMM (hv_a4gemm_pp) on the 8B layer shapes for a run of
     `--prefill-tokens` tokens: device time per GEMM (CUDA events over `--gemv-reps`
@@ -741,6 +844,10 @@ def main(argv=None):
                     help="instead of the decode step: the prefill GEMM on the 8B layer "
                          "shapes, one JSON line per matrix")
     ap.add_argument("--prefill-tokens", type=int, default=256)
+    ap.add_argument("--head-argmax", action="store_true",
+                    help="instead of the decode step: the vocabulary-sharded LM head + "
+                         "greedy argmax workload (151936 x 5120), one JSON line")
+    ap.add_argument("--head-states", type=int, default=2000)
     ap.add_argument("--gemv-reps", type=int, default=300)
     ap.add_argument("--gemv-max-rows", type=int, default=0,
                     help="sweep only the shapes with at most this many rows (0: all)")
@@ -766,6 +873,8 @@ def main(argv=None):
             return run_gemv_sweep(args, dist)
         if args.prefill_sweep:
             return run_prefill_sweep(args, dist)
+        if args.head_argmax:
+            return run_head_argmax(args, dist)
         if args.impl == "reference":
             return run_reference(args, dist)
         return run_ours(args, dist)

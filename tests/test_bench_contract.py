@@ -34,6 +34,9 @@ class FakeDriver(types.ModuleType):
     def event_elapsed_ms(self, a, b):
         return self.ms
 
+    def w4_prepacked_size(self, n, k, pair=0):
+        return n * k // 2, n * k // 32 * 4
+
     def __getattr__(self, name):        # every other call: accepted, no effect
         if name.startswith("__"):       # module introspection (importers, torch) sees none
             raise AttributeError(name)
@@ -192,3 +195,33 @@ def test_two_rank_line(mode):
                                                        / ln["roofline"]["peak"])
     else:
         assert ln["scaling"] == "weak" and ln["value"] == pytest.approx(2 * 100 / 0.32)
+
+
+def test_head_argmax_line(monkeypatch, capsys):
+    """--head-argmax: one line in hidden states/s with its roofline, on a shrunken head
+    (the fake driver's keys all carry token 5)."""
+    n_all, k = 64, 256
+    monkeypatch.setattr(bench.synth, "HEAD_SHAPE", (n_all, k))
+    monkeypatch.setattr(bench.synth, "head_case", lambda ns: (
+        np.zeros((n_all, k), np.float32), np.zeros((ns, k), np.float32)))
+    drv = FakeDriver(ms=10.0)
+    key = np.uint64((1 << 32) | ((~5) & 0xFFFFFFFF))
+
+    def download(host_ptr, src, n):
+        arr = np.full(n // 8, key, np.uint64)
+        ctypes.memmove(host_ptr, arr.ctypes.data, n)
+    drv.download = download
+    import hvdrv
+    drv.token_of_key = hvdrv.token_of_key        # the real key -> token rule (pure)
+    monkeypatch.setitem(sys.modules, "hvdrv", drv)
+    assert bench.main(["--head-argmax", "--head-states", "100", "--warmup", "3"]) == 0
+    lines = [json.loads(x) for x in capsys.readouterr().out.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    ln = lines[0]
+    assert ln["unit"] == "hidden states/s" and ln["value"] == pytest.approx(100 / 0.01)
+    assert ln["config"]["shards"] == 1 and ln["config"]["rows_per_shard"] == n_all
+    rf = ln["roofline"]
+    assert rf["achieved"] == pytest.approx(n_all * k * 5 // 8 / 1e-4 / 1e9)
+    assert rf["frac"] == pytest.approx(rf["achieved"] / rf["peak"])
+    assert ln["tokens"] == {"first": [5] * 8, "all_valid": True}
+    assert ln["gpu_launches"] == 200
