@@ -21,7 +21,7 @@ def _paths():
             sys.path.insert(0, p)
 
 
-def _run(world, rank, inbox, outbox, result):
+def _run(world, rank, inbox, outbox, result, kw):
     """One rank: build the (sharded) engine, decode, report tokens and the logits shard
     of the prompt's last position."""
     try:
@@ -39,7 +39,7 @@ def _run(world, rank, inbox, outbox, result):
         cfg = Config(synth.tiny_arch(**ARCH))
         eng = limited.Engine(config=cfg, tensors=synth.iter_tensors(cfg, SEED), quiet=True,
                              max_context=CAP, device=rank, world=world, rank=rank,
-                             exchange=exchange if world > 1 else None)
+                             exchange=exchange if world > 1 else None, **kw)
         toks, _, _ = eng.generate(PROMPT, NEW, stop_on_eos=False)
         lg = eng.logits(PROMPT)
         result.put((rank, toks, lg.tobytes()))
@@ -48,11 +48,11 @@ def _run(world, rank, inbox, outbox, result):
         result.put((rank, "error", repr(e)))
 
 
-def _launch(world):
+def _launch(world, kw=None):
     ctx = mp.get_context("spawn")
     inboxes = [ctx.Queue() for _ in range(world)]
     outbox, result = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_run, args=(world, r, inboxes[r], outbox, result))
+    procs = [ctx.Process(target=_run, args=(world, r, inboxes[r], outbox, result, kw or {}))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -80,6 +80,25 @@ def test_two_gpu_sharded_step_matches_one_gpu(hv):
         pytest.skip("needs 2 GPUs")
     one = _launch(1)[0]
     two = _launch(2)
+    assert two[0][0] == one[0] and two[1][0] == one[0], (two[0][0], two[1][0], one[0])
+    full = one[1]
+    n = full.size // 2
+    assert np.array_equal(two[0][1].view(np.uint32), full[:n].view(np.uint32))
+    assert np.array_equal(two[1][1].view(np.uint32), full[n:].view(np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not os.environ.get("HV_NEW_GPU_TESTS"),
+                    reason="kernels not yet run on a B200: set HV_NEW_GPU_TESTS=1")
+@pytest.mark.parametrize("kw", [{"kv_dtype": "f16"}, {"gemv_layout": "dq"},
+                                {"kv_dtype": "f16", "gemv_layout": "dq"}])
+def test_two_gpu_sharded_variants_match_one_gpu(hv, kw):
+    """The binary16 cache and the dq weight tiles sharded over 2 GPUs: the same tokens
+    and logits shards, bit for bit, as the same variant on one GPU."""
+    if hv.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    one = _launch(1, kw)[0]
+    two = _launch(2, kw)
     assert two[0][0] == one[0] and two[1][0] == one[0], (two[0][0], two[1][0], one[0])
     full = one[1]
     n = full.size // 2
