@@ -23,7 +23,7 @@ def build(force: bool = False) -> Path:
         return LIB
     OUT.mkdir(exist_ok=True)
     cmd = ["gcc", "-O3", "-fopenmp", "-ffp-contract=off", "-fno-fast-math", "-fPIC",
-           "-shared", "-o", str(LIB), str(SRC)]
+           "-shared", "-o", str(LIB), str(SRC), "-lm"]
     subprocess.run(cmd, check=True)
     return LIB
 

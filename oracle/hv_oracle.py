@@ -12,8 +12,14 @@ the reference's own engine/reference.py where its checkout is present
 * bit-exact: quantize_w4, quantize_act, the int32 block dots, gemv_w4's fp32 output
   (numpy's pairwise summation order restated in `pairwise_sum`), rmsnorm, rope, the
   residual add, the embedding gather and argmax;
-* exp-based ops (silu_mul, attention) call np.exp and a BLAS dot like the reference, so
-  they match it bit for bit on the same host; the GPU is held to a tolerance there.
+* exp-based ops (silu_mul, attention): the reference calls np.exp and OpenBLAS's gemv
+  (`keys @ q`), whose results depend on how numpy and OpenBLAS were built and on the
+  host's thread count. The oracle restates both (`np_exp`: numpy's float32 SIMD exp;
+  `blas_rowdots`: the order OpenBLAS forms each row dot, BLAS_THREADS runs for long
+  row counts) in oracle/hv_oracle_c.c, pinned bit for bit against np.exp and `keys @ q`
+  of the host that made the golden vectors (tests/test_oracle_c.py). The rest of the
+  attention (max, the pairwise w.sum(), the division, the sequential axis-0 sum of
+  w * v) is numpy's own, which does not depend on the host.
 
 The compressed-KV lane (kv_round, OracleModel(kv_dtype="f16")) has no counterpart in the
 reference: it is the reference's step with each appended k/v row rounded to binary16.
@@ -33,6 +39,10 @@ F32 = np.float32
 BLOCK = 32
 RMS_EPS = F32(1e-5)          # engine/reference.py:34 (the shipped kernel's epsilon)
 PW_BLOCK = 128               # numpy's pairwise-summation leaf size
+# OpenBLAS threads on the host that produced the golden vectors (8 cores): gemv calls of
+# 128 * rows >= 460800 are split into this many runs of rows, which changes the order of
+# the row dots near each run's end (hvo_blas_row_kind).
+BLAS_THREADS = 8
 
 
 # ---------------------------------------------------------------------------
@@ -205,7 +215,7 @@ def silu_mul(gate, up) -> np.ndarray:
     """engine/reference.py:96-101: g * sigma(g) * u, sigma by the sign-split exp form."""
     g = np.asarray(gate, F32)
     sgn = np.where(g < 0, F32(-1.0), F32(1.0)).astype(F32)
-    e = np.exp(-(sgn * g)).astype(F32)
+    e = np_exp(-(sgn * g))
     sig = (F32(0.5) * (F32(1.0) + sgn * ((F32(1.0) - e) / (F32(1.0) + e)))).astype(F32)
     return (g * sig * np.asarray(up, F32)).astype(F32)
 
@@ -219,11 +229,31 @@ def attention(q, kc, vc, pos: int, group: int, scale: float) -> np.ndarray:
         kvh = h // group
         keys = kc[kvh, : pos + 1].astype(F32)
         vals = vc[kvh, : pos + 1].astype(F32)
-        logits = (keys @ q[h].astype(F32)) * F32(scale)
+        logits = blas_rowdots(keys, q[h]) * F32(scale)
         logits -= logits.max()
-        w = np.exp(logits).astype(F32)
+        w = np_exp(logits)
         w /= w.sum()
         out[h] = (w[:, None] * vals).sum(0)
+    return out
+
+
+def np_exp(x) -> np.ndarray:
+    """np.exp on float32 as numpy's x86-64 SIMD kernel computes it (hvo_np_expf)."""
+    x = np.ascontiguousarray(x, F32)
+    y = np.empty_like(x)
+    _clib().hvo_np_exp_arr(x.ctypes.data, y.ctypes.data, x.size)
+    return y
+
+
+def blas_rowdots(keys, x, threads: int = None) -> np.ndarray:
+    """`keys @ x` for keys [T, 128] as OpenBLAS's gemv forms each row dot
+    (hvo_blas_rowdots); `threads`: the reference host's OpenBLAS thread count."""
+    keys = np.ascontiguousarray(keys, F32)
+    x = np.ascontiguousarray(x, F32)
+    assert keys.ndim == 2 and keys.shape[1] == 128 and x.shape == (128,)
+    out = np.empty(keys.shape[0], F32)
+    _clib().hvo_blas_rowdots(keys.ctypes.data, 128, x.ctypes.data, out.ctypes.data,
+                             keys.shape[0], BLAS_THREADS if threads is None else threads)
     return out
 
 
@@ -369,6 +399,14 @@ def _clib():
         lib.hvo_pairwise_sum.restype = ctypes.c_float
         lib.hvo_quantize_w4.argtypes = [vp, lg, lg, vp, vp]
         lib.hvo_quantize_w4.restype = None
+        lib.hvo_np_exp_arr.argtypes = [vp, vp, lg]
+        lib.hvo_np_exp_arr.restype = None
+        lib.hvo_np_expf.argtypes = [ctypes.c_float]
+        lib.hvo_np_expf.restype = ctypes.c_float
+        lib.hvo_blas_rowdots.argtypes = [vp, lg, vp, vp, ctypes.c_int, ctypes.c_int]
+        lib.hvo_blas_rowdots.restype = None
+        lib.hvo_blas_row_kind.argtypes = [ctypes.c_int] * 3
+        lib.hvo_blas_row_kind.restype = ctypes.c_int
         _CLIB = lib
     return _CLIB
 

@@ -9,6 +9,7 @@ Runs ONLY where the reference checkout exists; the resulting
     python tests/golden/make_golden.py long        # tiny model, 300- and 2000-token prompts
     python tests/golden/make_golden.py c1          # 1.7B-shape 32+64 decode (~1 hour)
     python tests/golden/make_golden.py c3          # 8B-shape 4+2 decode (~40 GB RAM)
+    python tests/golden/make_golden.py numerics    # np.exp and `keys @ q` samples (seconds)
 
 The reference's engine/limited.py dlopens libcuda at import; a stub `cudrv` module is
 placed in sys.modules first so that its pure-numpy parts (quantize_w4, Config) and all of
@@ -200,6 +201,38 @@ def make_decode(out: Path, arch: dict, seed: int, n_prompt: int, n_new: int,
     print(f"  done in {time.time() - t0:.0f} s", flush=True)
 
 
+# Row counts of the `keys @ q` samples: every remainder mod 4 of short and long runs,
+# the single-run limit of the host's OpenBLAS (128 rows x T < 460800) and the split runs
+# above it (up to the 8B workload's 4352 positions).
+NUMERICS_T = list(range(2, 70)) + [127, 128, 129, 130, 255, 256, 257, 299, 300, 301, 302,
+                                   1999, 2000, 2001, 2002, 3598, 3599, 3600, 3601, 3602,
+                                   4095, 4096, 4097, 4098, 4349, 4350, 4351, 4352, 4353]
+
+
+def numerics_inputs():
+    """The inputs of numerics.npz, regenerated by the tests from these seeds."""
+    # float32 bit patterns spread over [-104, 0] and [0, 89] (exp's finite range)
+    xneg = np.linspace(0x80000000, 0xC2D00000, 262144).astype(np.uint32).view(F32)
+    xpos = np.linspace(0x00000000, 0x42B20000, 65536).astype(np.uint32).view(F32)
+    rng = np.random.default_rng(12)
+    q = rng.standard_normal(128, dtype=F32)
+    keys = (rng.standard_normal((max(NUMERICS_T), 128), dtype=F32) * F32(0.5)).astype(F32)
+    return np.concatenate([xneg, xpos]), q, keys
+
+
+def make_numerics(out: Path):
+    """np.exp over float32 samples and `keys @ q` (OpenBLAS gemv through numpy) for the
+    row counts NUMERICS_T: the two library calls of the reference's attention and SiLU
+    (engine/reference.py:99, 112-114) whose results depend on the host."""
+    x, q, keys = numerics_inputs()
+    arrs = {"exp_x": x, "exp_y": np.exp(x).astype(F32), "dot_T": np.array(NUMERICS_T)}
+    for T in NUMERICS_T:
+        arrs[f"dot_{T}"] = (np.ascontiguousarray(keys[:T]) @ q).astype(F32)
+    arrs["host_cpus"] = np.array(os.cpu_count())
+    np.savez_compressed(out, **arrs)
+    print(f"wrote {out}", flush=True)
+
+
 def main(argv):
     what = argv[1] if len(argv) > 1 else "ops"
     import synth
@@ -226,6 +259,8 @@ def main(argv):
         arch, seed, n_prompt, n_new = synth.WORKLOADS["qwen3-1.7b-p32-g64"]
         make_decode(HERE / "decode_qwen3_1p7b.npz", synth.ARCH[arch], seed, n_prompt,
                     n_new, False)
+    elif what == "numerics":
+        make_numerics(HERE / "numerics.npz")
     else:
         raise SystemExit(f"unknown target {what}")
 

@@ -105,3 +105,60 @@ def test_fast_oracle_matches_reference_at_real_shapes(golden, name, workload, n_
     for i, lg in enumerate(logits):
         assert hashlib.sha256(np.ascontiguousarray(lg).tobytes()).hexdigest() == \
             str(g["logits_sha"][i]), i
+
+
+def _numerics_inputs():
+    import importlib.util
+    from conftest import GOLDEN
+    spec = importlib.util.spec_from_file_location("make_golden", GOLDEN / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    return mg.numerics_inputs()
+
+
+def test_np_exp_restatement_matches_reference_host(golden):
+    """hvo_np_expf == the reference host's np.exp on 327,680 float32 samples of exp's
+    whole finite range (tests/golden/numerics.npz)."""
+    g = golden("numerics.npz")
+    got = O.np_exp(g["exp_x"])
+    assert np.array_equal(got.view(np.uint32), g["exp_y"].view(np.uint32))
+
+
+def test_blas_rowdots_restatement_matches_reference_host(golden):
+    """hvo_blas_rowdots == the reference host's `keys @ q` (OpenBLAS gemv) for every row
+    of 97 row counts: every remainder mod 4, the single-run limit and the split runs
+    above it (tests/golden/numerics.npz)."""
+    g = golden("numerics.npz")
+    _, q, keys = _numerics_inputs()
+    assert int(g["host_cpus"]) == O.BLAS_THREADS
+    for T in g["dot_T"].tolist():
+        got = O.blas_rowdots(keys[:T], q)
+        assert np.array_equal(got.view(np.uint32), g[f"dot_{T}"].view(np.uint32)), T
+
+
+def _host_like_reference():
+    try:
+        from numpy._core._multiarray_umath import __cpu_features__ as f
+    except ImportError:
+        return False
+    return bool(f.get("AVX512F")) and bool(f.get("FMA3"))
+
+
+@pytest.mark.skipif(not _host_like_reference(), reason="numpy without its AVX-512 exp kernel")
+def test_np_exp_restatement_matches_live_numpy():
+    """On a host whose numpy runs the same SIMD kernel: every 61st float32 of [-104, 0]."""
+    b = np.arange(0x80000000, 0xC2D00001, 61, dtype=np.uint32)
+    x = b.view(F32)
+    assert np.array_equal(O.np_exp(x).view(np.uint32), np.exp(x).view(np.uint32))
+
+
+@pytest.mark.skipif(not _host_like_reference(), reason="numpy without its AVX-512 kernels")
+def test_blas_row_kinds_match_live_numpy_below_the_split():
+    """Row counts below OpenBLAS's single-run limit do not depend on the host's thread
+    count: there the restatement must equal this host's `keys @ q` too."""
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal(128, dtype=F32)
+    for T in list(range(2, 90)) + [513, 1022, 2047, 3599]:
+        keys = rng.standard_normal((T, 128), dtype=F32)
+        got = O.blas_rowdots(keys, q)
+        assert np.array_equal(got.view(np.uint32), (keys @ q).view(np.uint32)), T
