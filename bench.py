@@ -271,8 +271,8 @@ def run_reference(args, dist: Dist):
     return 0
 
 
-STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3, "split_merge": 4}
-STEP_OPT_DEFAULTS = {"inflight": 6, "evict_first": 1, "local_qkv_barrier": 0, "split_merge": 0}
+STEP_OPTS = {"inflight": 1, "evict_first": 2, "local_qkv_barrier": 3}
+STEP_OPT_DEFAULTS = {"inflight": 6, "evict_first": 1, "local_qkv_barrier": 0}
 # A/B-only names that are not step options: layout_dq=1 times a second engine of the same
 # model whose weight tiles are in the dq arrangement (gemv_layout="dq")
 AB_ENGINE_OPTS = ("layout_dq",)

@@ -289,12 +289,43 @@ HV_DEV unsigned quant_block_8lanes(float4 v, float* s_out, int* bsum_out) {
 }
 
 // ---------------------------------------------------------------------------
-// SiLU * up (engine/reference.py:96-101): sigma by the sign-split exp form.
-// exp is CUDA's expf (numpy's exp differs from it by an ulp now and then).
+// numpy's float32 exp (numpy/_core/src/umath/loops_exponent_log.dispatch.c.src,
+// simd_exp_f32, the AVX512F / AVX2+FMA3 kernel numpy runs on x86-64 hosts that have
+// them): n = rint(x log2 e) by the 1.5 * 2^23 add and subtract, a Cody-Waite reduction
+// r = x - n ln2 in fused multiply-adds, exp(r) ~ P5(r) / Q2(r) (Horner, fused
+// multiply-adds, one IEEE division), then the quotient times 2^n rounded once.
+// x >= 88.72283935546875 gives +inf, x <= -103.97208404541015625 gives +0, NaN stays NaN.
+// ---------------------------------------------------------------------------
+HV_DEV float np_expf(float x) {
+  if (x != x) return x;
+  if (x >= 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x <= -103.97208404541015625f) return 0.0f;
+  float n = __fmul_rn(x, 1.442695040888963407359924681001892137f);
+  n = __fadd_rn(n, 0x1.8p23f);
+  n = __fsub_rn(n, 0x1.8p23f);
+  float r = __fmaf_rn(n, -6.93145752e-1f, x);
+  r = __fmaf_rn(n, -1.42860677e-6f, r);
+  r = __fmaf_rn(n, 0.0f, r);
+  float p = __fmaf_rn(5.082762527590693718096e-04f, r, 6.757896990527504603057e-03f);
+  p = __fmaf_rn(p, r, 5.114512081637298353406e-02f);
+  p = __fmaf_rn(p, r, 2.473615434895520810817e-01f);
+  p = __fmaf_rn(p, r, 7.257664613233124478488e-01f);
+  p = __fmaf_rn(p, r, 9.999999999980870924916e-01f);
+  float q = __fmaf_rn(2.159509375685829852307e-02f, r, -2.742335390411667452936e-01f);
+  q = __fmaf_rn(q, r, 1.0f);
+  const float quot = __fdiv_rn(p, q);
+  // quot * 2^n: exact in double (n in [-150, 128]), then one rounding to float
+  const double two_n = __longlong_as_double((long long)((int)n + 1023) << 52);
+  return __double2float_rn(__dmul_rn((double)quot, two_n));
+}
+
+// ---------------------------------------------------------------------------
+// SiLU * up (engine/reference.py:96-101): sigma by the sign-split exp form, exp being
+// numpy's (np_expf), every operation rounded as numpy rounds it.
 // ---------------------------------------------------------------------------
 HV_DEV float silu_mul1(float g, float u) {
   const float sgn = (g < 0.0f) ? -1.0f : 1.0f;
-  const float e = expf(-__fmul_rn(sgn, g));
+  const float e = np_expf(-__fmul_rn(sgn, g));
   const float r = __fdiv_rn(__fsub_rn(1.0f, e), __fadd_rn(1.0f, e));
   const float sig = __fmul_rn(0.5f, __fadd_rn(1.0f, __fmul_rn(sgn, r)));
   return __fmul_rn(__fmul_rn(g, sig), u);

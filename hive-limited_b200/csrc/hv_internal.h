@@ -15,6 +15,17 @@ void set_error(const char* fmt, ...);
 int cuda_fail(const char* what, cudaError_t e);
 int sm_count(int* out);
 
+// The reference-order decode attention (attn_exact.cuh, kernels in k_ops.cu), shared by
+// hv_attn_decode, the batched prefill rows and the allocation-free entry point.
+int ref_blas_runs();
+int set_ref_blas_runs(int v);
+int attn_exact_chunks(int nkv, int cap, int* out);
+size_t attn_exact_scratch_floats(int nq, int cap, int nch);
+int attn_exact_launch(int group, bool kv_half, const float* q, size_t q_tok, const void* kc,
+                      const void* vc, float* ctx, size_t ctx_tok, const float* scale,
+                      const int32_t* pos_p, int pos0, int nq, int cap, int nch, int ntok,
+                      float* scr, size_t scr_tok, cudaStream_t st);
+
 }  // namespace hv
 
 #define HV_CUDA(call)                                         \

@@ -6,7 +6,7 @@
 
 #include <cuda_fp16.h>
 
-#include "attn_decode.cuh"
+#include "attn_exact.cuh"
 #include "gemv_mma.cuh"
 #include "hv_internal.h"
 #include "hv_wait.cuh"
@@ -557,118 +557,111 @@ __global__ void k_quantize_w4(const float* __restrict__ w, uint32_t* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// split-sequence attention (standalone): one CTA per (kv head, chunk)
+// decode attention in the reference's order (attn_exact.cuh): a scores kernel over
+// (kv head, chunk) items, then a context kernel over (kv head, 32-dim slice) items
 // ---------------------------------------------------------------------------
-constexpr int kAttnThreads = 256;
 
-template <int GS, class KT>
-__global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q,
-                                                       const KT* __restrict__ kc,
-                                                       const KT* __restrict__ vc,
-                                                       float* __restrict__ ctx,
-                                                       const float* __restrict__ scale_p,
-                                                       const int32_t* __restrict__ pos_p,
-                                                       int cap, int nch,
-                                                       float* __restrict__ part,
-                                                       int* __restrict__ ticket) {
-  extern __shared__ __align__(16) float fsm[];
-  const int nw = blockDim.x >> 5;
-  float* q_s = fsm;
-  float* lg_s = q_s + GS * kHd;
-  float* red_s = lg_s + kAttnChunkMax * GS;
-  float* stat_s = red_s + nw * GS * kHd;
-  __shared__ int last;
-  const int g = blockIdx.x / nch, c = blockIdx.x % nch;
-  const int pos = *pos_p;
-  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) q_s[e] = q[(size_t)g * GS * kHd + e];
-  __syncthreads();
-  int t0, t1;
-  chunk_bounds(pos + 1, nch, c, &t0, &t1);
-  float* mypart = part + ((size_t)g * nch + c) * GS * kPartStride;
-  attn_chunk<GS>(q_s, kc + (size_t)g * cap * kHd, vc + (size_t)g * cap * kHd, t0, t1,
-                 *scale_p, pos, nullptr, nullptr, lg_s, red_s, stat_s, mypart);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(ticket + g, 1) == nch - 1);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  attn_merge<GS>(part + (size_t)g * nch * GS * kPartStride, nch, ctx + (size_t)g * GS * kHd,
-                 red_s);
-  if (threadIdx.x == 0) ticket[g] = 0;
+// OpenBLAS threads of the host whose reference results the attention reproduces (the
+// row kinds of `keys @ q` depend on it); hv_step_set_option(HV_OPT_REF_BLAS_RUNS).
+static int g_ref_runs = kRefRuns;
+int ref_blas_runs() { return g_ref_runs; }
+int set_ref_blas_runs(int v) {
+  HV_REQUIRE(v >= 1 && v <= 1024, HV_E_INVALID, "reference BLAS runs %d outside [1, 1024]", v);
+  g_ref_runs = v;
+  return HV_OK;
 }
 
-// per-device attention scratch, grown on demand
-struct AttnScratch {
-  float* part = nullptr;
-  int* ticket = nullptr;
-  size_t part_floats = 0;
-  int tickets = 0;
-};
-static std::mutex g_attn_mu;
-static AttnScratch g_attn[64];
-
-static int attn_nch(int nkv, int cap, int* out) {
+int attn_exact_chunks(int nkv, int cap, int* out) {
   int sms = 0;
   int rc = sm_count(&sms);
   if (rc) return rc;
   int nch = (sms + nkv - 1) / nkv;
   const int need = (cap + kAttnChunkMax - 1) / kAttnChunkMax;
   *out = nch > need ? nch : need;
-  HV_REQUIRE(*out <= kAttnMaxChunks, HV_E_UNSUPPORTED,
-             "hv_attn_decode: %d chunks per kv head (at most %d; the cache is too long)", *out,
-             kAttnMaxChunks);
   return HV_OK;
 }
 
-static int attn_scratch(int nkv, int group, int cap, void* stream, AttnScratch** out) {
+size_t attn_exact_scratch_floats(int nq, int cap, int nch) {
+  return (size_t)nq * ((size_t)cap + (size_t)nch);
+}
+
+template <int GS, class KT>
+static int launch_exact(const float* q, size_t q_tok, const KT* kc, const KT* vc, float* ctx,
+                        size_t ctx_tok, const float* scale, const int32_t* pos_p, int pos0,
+                        int nq, int cap, int nch, int ntok, float* scr, size_t scr_tok,
+                        cudaStream_t st) {
+  const int nkv = nq / GS;
+  const size_t sm1 = sizeof(float) * ((size_t)GS * kHd + (size_t)((cap + nch - 1) / nch) * GS);
+  int rc = smem_attr((const void*)k_attn_sc<GS, KT>, sm1);
+  if (rc) return rc;
+  const size_t sm2 = attn_cx_smem<GS>();
+  rc = smem_attr((const void*)k_attn_cx<GS, KT>, sm2);
+  if (rc) return rc;
+  k_attn_sc<GS, KT><<<dim3(nkv * nch, ntok), kAttnExThreads, sm1, st>>>(
+      q, q_tok, kc, scale, pos_p, pos0, cap, nch, g_ref_runs, nq, scr, scr_tok);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail("k_attn_sc", e);
+  k_attn_cx<GS, KT><<<dim3(nkv * kSlices, ntok), kAttnExThreads, sm2, st>>>(
+      vc, ctx, ctx_tok, pos_p, pos0, cap, nch, nq, scr, scr_tok);
+  HV_LAUNCHED("k_attn_cx");
+}
+
+int attn_exact_launch(int group, bool kv_half, const float* q, size_t q_tok, const void* kc,
+                      const void* vc, float* ctx, size_t ctx_tok, const float* scale,
+                      const int32_t* pos_p, int pos0, int nq, int cap, int nch, int ntok,
+                      float* scr, size_t scr_tok, cudaStream_t st) {
+  HV_REQUIRE(cap <= kExactMaxCap, HV_E_UNSUPPORTED,
+             "attention: cache of %d positions (at most %d)", cap, kExactMaxCap);
+#define HV_EXACT(G)                                                                          \
+  return kv_half ? launch_exact<G>(q, q_tok, static_cast<const __half*>(kc),                 \
+                                   static_cast<const __half*>(vc), ctx, ctx_tok, scale,      \
+                                   pos_p, pos0, nq, cap, nch, ntok, scr, scr_tok, st)        \
+                 : launch_exact<G>(q, q_tok, static_cast<const float*>(kc),                  \
+                                   static_cast<const float*>(vc), ctx, ctx_tok, scale,       \
+                                   pos_p, pos0, nq, cap, nch, ntok, scr, scr_tok, st)
+  switch (group) {
+    case 1: HV_EXACT(1);
+    case 2: HV_EXACT(2);
+    case 4: HV_EXACT(4);
+    default: HV_EXACT(8);
+  }
+#undef HV_EXACT
+}
+
+// per-device attention scratch, grown on demand
+struct AttnScratch {
+  float* buf = nullptr;
+  size_t floats = 0;
+};
+static std::mutex g_attn_mu;
+static AttnScratch g_attn[64];
+
+static int attn_scratch(int nq, int cap, int nch, void* stream, AttnScratch** out) {
   int dev = 0;
   HV_CUDA(cudaGetDevice(&dev));
   HV_REQUIRE(dev >= 0 && dev < 64, HV_E_UNSUPPORTED, "device index %d out of range", dev);
-  int nch = 0;
-  int rc = attn_nch(nkv, cap, &nch);
-  if (rc) return rc;
-  const size_t need = (size_t)nkv * nch * group * kPartStride;
+  const size_t need = attn_exact_scratch_floats(nq, cap, nch);
   std::lock_guard<std::mutex> lk(g_attn_mu);
   AttnScratch& s = g_attn[dev];
-  if (s.part_floats < need || s.tickets < nkv) {
+  if (s.floats < need) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (stream) HV_CUDA(cudaStreamIsCapturing((cudaStream_t)stream, &cs));
     HV_REQUIRE(cs == cudaStreamCaptureStatusNone, HV_E_CAPTURE,
                "attention scratch must grow during stream capture; call hv_attn_reserve first");
-    if (s.part) cudaFree(s.part);
-    if (s.ticket) cudaFree(s.ticket);
-    s.part = nullptr;
-    s.ticket = nullptr;
-    const size_t nf = need > s.part_floats ? need : s.part_floats;
-    const int nt = nkv > s.tickets ? nkv : s.tickets;
-    HV_CUDA(cudaMalloc(&s.part, nf * sizeof(float)));
-    HV_CUDA(cudaMalloc(&s.ticket, (size_t)nt * sizeof(int)));
-    HV_CUDA(cudaMemset(s.ticket, 0, (size_t)nt * sizeof(int)));
-    s.part_floats = nf;
-    s.tickets = nt;
+    if (s.buf) cudaFree(s.buf);
+    s.buf = nullptr;
+    s.floats = 0;
+    HV_CUDA(cudaMalloc(&s.buf, need * sizeof(float)));
+    s.floats = need;
   }
   *out = &s;
   return HV_OK;
 }
 
-template <int GS, class KT>
-static int launch_attn(const float* q, const KT* kc, const KT* vc, float* ctx,
-                       const float* scale, const int32_t* pos, int nkv, int cap, int nch,
-                       AttnScratch* s, cudaStream_t st) {
-  const size_t smem = attn_smem_bytes<GS>(kAttnThreads / 32);
-  const int rc = smem_attr((const void*)k_attn<GS, KT>, smem);
-  if (rc) return rc;
-  k_attn<GS, KT><<<nkv * nch, kAttnThreads, smem, st>>>(q, kc, vc, ctx, scale, pos, cap, nch,
-                                                        s->part, s->ticket);
-  HV_LAUNCHED("k_attn");
-}
-
 // hv_attn_decode and hv_attn_decode_f16: checks, scratch, chunk count, launch.
-template <class KT>
-static int attn_decode_any(const char* name, const float* q, const KT* kc, const KT* vc,
-                           float* ctx, const float* scale, const int32_t* pos, int nq, int hd,
-                           int group, int kvstride, void* stream) {
+static int attn_decode_any(const char* name, bool kv_half, const float* q, const void* kc,
+                           const void* vc, float* ctx, const float* scale, const int32_t* pos,
+                           int nq, int hd, int group, int kvstride, void* stream) {
   HV_REQUIRE(q && kc && vc && ctx && scale && pos && nq > 0 && group > 0, HV_E_INVALID,
              "%s: bad arguments", name);
   HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, hd);
@@ -677,19 +670,14 @@ static int attn_decode_any(const char* name, const float* q, const KT* kc, const
   HV_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, HV_E_UNSUPPORTED,
              "%s: group size %d (1, 2, 4 or 8)", name, group);
   const int nkv = nq / group, cap = kvstride / hd;
-  AttnScratch* s = nullptr;
-  int rc = attn_scratch(nkv, group, cap, stream, &s);
-  if (rc) return rc;
   int nch = 0;
-  rc = attn_nch(nkv, cap, &nch);
+  int rc = attn_exact_chunks(nkv, cap, &nch);
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (group) {
-    case 1: return launch_attn<1>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    case 2: return launch_attn<2>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    case 4: return launch_attn<4>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-    default: return launch_attn<8>(q, kc, vc, ctx, scale, pos, nkv, cap, nch, s, st);
-  }
+  AttnScratch* s = nullptr;
+  rc = attn_scratch(nq, cap, nch, stream, &s);
+  if (rc) return rc;
+  return attn_exact_launch(group, kv_half, q, 0, kc, vc, ctx, 0, scale, pos, 0, nq, cap, nch,
+                           1, s->buf, 0, (cudaStream_t)stream);
 }
 
 }  // namespace hv
@@ -700,8 +688,8 @@ extern "C" {
 
 int hv_kernel_list(char* buf, size_t len) {
   static const char* names =
-      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_a4gv_dq,k_w4_prepack,k_w4_prepack_dq,k_rmsnorm,k_rope,k_kvapp,k_kvapp16,k_attn,k_silu,k_vadd,k_gather,"
-      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_attn_na,k_wait_probe,k_a4gemm_pp,k_gather_rows,k_qa8s_rows,k_qk_rows,k_attn_rows,k_silu_rows";
+      "k_qa8s,k_a4gv,k_a4gv_mma,k_a4gv_pp,k_a4gv_pps,k_a4gv_dq,k_w4_prepack,k_w4_prepack_dq,k_rmsnorm,k_rope,k_kvapp,k_kvapp16,k_attn_sc,k_attn_cx,k_silu,k_vadd,k_gather,"
+      "k_argmax_p,k_argmax_f,k_argmax_key,k_argmax_keyf,k_quantize_w4,k_step,k_wait_probe,k_a4gemm_pp,k_gather_rows,k_qa8s_rows,k_qk_rows,k_silu_rows";
   HV_REQUIRE(buf && len > 0, HV_E_INVALID, "hv_kernel_list: bad buffer");
   strncpy(buf, names, len - 1);
   buf[len - 1] = 0;
@@ -912,23 +900,25 @@ int hv_kv_append_f16(const float* k, const float* v, uint16_t* kc, uint16_t* vc,
 
 int hv_attn_reserve(int nkv, int group, int cap) {
   HV_REQUIRE(nkv > 0 && group > 0 && cap > 0, HV_E_INVALID, "hv_attn_reserve: bad arguments");
+  int nch = 0;
+  int rc = attn_exact_chunks(nkv, cap, &nch);
+  if (rc) return rc;
   AttnScratch* s = nullptr;
-  return attn_scratch(nkv, group, cap, nullptr, &s);
+  return attn_scratch(nkv * group, cap, nch, nullptr, &s);
 }
 
 int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
                    const float* scale, const int32_t* pos, int nq, int hd, int group,
                    int kvstride, void* stream) {
-  return attn_decode_any("hv_attn_decode", q, kc, vc, ctx, scale, pos, nq, hd, group,
+  return attn_decode_any("hv_attn_decode", false, q, kc, vc, ctx, scale, pos, nq, hd, group,
                          kvstride, stream);
 }
 
 int hv_attn_decode_f16(const float* q, const uint16_t* kc, const uint16_t* vc, float* ctx,
                        const float* scale, const int32_t* pos, int nq, int hd, int group,
                        int kvstride, void* stream) {
-  return attn_decode_any("hv_attn_decode_f16", q, reinterpret_cast<const __half*>(kc),
-                         reinterpret_cast<const __half*>(vc), ctx, scale, pos, nq, hd, group,
-                         kvstride, stream);
+  return attn_decode_any("hv_attn_decode_f16", true, q, kc, vc, ctx, scale, pos, nq, hd,
+                         group, kvstride, stream);
 }
 
 int hv_silu_mul(const float* gate, const float* up, float* act, int n, void* stream) {

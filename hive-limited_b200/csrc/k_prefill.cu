@@ -236,51 +236,6 @@ __global__ void __launch_bounds__(256) k_qk_rows(const float* __restrict__ qkv,
   }
 }
 
-// The eager step's split-sequence attention (k_attn) for a run of query tokens: token t
-// attends positions 0 .. pos0 + t with the same chunking (nch) and merge, so its ctx row
-// is what hv_attn_decode gives at that position. Grid (nkv * nch, ntok); per-token
-// partials and tickets in caller scratch (tickets zero; each merge re-zeroes its own).
-template <int GS, class KT>
-__global__ void __launch_bounds__(256) k_attn_rows(const float* __restrict__ q,
-                                                   const KT* __restrict__ kc,
-                                                   const KT* __restrict__ vc,
-                                                   float* __restrict__ ctx,
-                                                   const float* __restrict__ scale_p, int pos0,
-                                                   int cap, int nch, int nq,
-                                                   float* __restrict__ part,
-                                                   int* __restrict__ ticket) {
-  extern __shared__ __align__(16) float fsm[];
-  const int nw = blockDim.x >> 5;
-  float* q_s = fsm;
-  float* lg_s = q_s + GS * kHd;
-  float* red_s = lg_s + kAttnChunkMax * GS;
-  float* stat_s = red_s + nw * GS * kHd;
-  __shared__ int last;
-  const int nkv = nq / GS;
-  const int t = blockIdx.y;
-  const int g = blockIdx.x / nch, c = blockIdx.x % nch;
-  const int pos = pos0 + t;
-  const float* qt = q + (size_t)t * nq * kHd + (size_t)g * GS * kHd;
-  for (int e = threadIdx.x; e < GS * kHd; e += blockDim.x) q_s[e] = qt[e];
-  __syncthreads();
-  int t0, t1;
-  chunk_bounds(pos + 1, nch, c, &t0, &t1);
-  float* part_t = part + (size_t)t * nkv * nch * GS * kPartStride;
-  attn_chunk<GS>(q_s, kc + (size_t)g * cap * kHd, vc + (size_t)g * cap * kHd, t0, t1,
-                 *scale_p, pos, nullptr, nullptr, lg_s, red_s, stat_s,
-                 part_t + ((size_t)g * nch + c) * GS * kPartStride);
-  __threadfence();
-  __syncthreads();
-  int* tk = ticket + (size_t)t * nkv + g;
-  if (threadIdx.x == 0) last = (atomicAdd(tk, 1) == nch - 1);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  attn_merge<GS>(part_t + (size_t)g * nch * GS * kPartStride, nch,
-                 ctx + (size_t)t * nq * kHd + (size_t)g * GS * kHd, red_s);
-  if (threadIdx.x == 0) *tk = 0;
-}
-
 // act[t] = silu(gate[t]) * up[t] for rows [gate | up] of 2 ffn values (gpu_silu_mul).
 __global__ void k_silu_rows(const float* __restrict__ gu, float* __restrict__ act, int ffn) {
   const int t = blockIdx.y;
@@ -288,30 +243,6 @@ __global__ void k_silu_rows(const float* __restrict__ gu, float* __restrict__ ac
   if (i < ffn)
     act[(size_t)t * ffn + i] = silu_mul1(gu[(size_t)t * 2 * ffn + i],
                                          gu[(size_t)t * 2 * ffn + ffn + i]);
-}
-
-// The chunk count hv_attn_decode uses for (nkv, cap), so both split alike.
-int rows_attn_chunks(int nkv, int cap, int* out) {
-  int sms = 0;
-  const int rc = sm_count(&sms);
-  if (rc) return rc;
-  const int nch = (sms + nkv - 1) / nkv;
-  const int need = (cap + kAttnChunkMax - 1) / kAttnChunkMax;
-  *out = nch > need ? nch : need;
-  return HV_OK;
-}
-
-template <int GS, class KT>
-int launch_attn_rows(const float* q, const KT* kc, const KT* vc, float* ctx,
-                     const float* scale, int pos0, int cap, int nch, int nq, int ntok,
-                     float* part, int* ticket, cudaStream_t st) {
-  const size_t smem = attn_smem_bytes<GS>(8);
-  HV_CUDA(cudaFuncSetAttribute((const void*)k_attn_rows<GS, KT>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const dim3 grid((unsigned)(nq / GS * nch), (unsigned)ntok);
-  k_attn_rows<GS, KT><<<grid, 256, smem, st>>>(q, kc, vc, ctx, scale, pos0, cap, nch, nq,
-                                               part, ticket);
-  HV_LAUNCHED("k_attn_rows");
 }
 
 // hv_qk_rows and hv_qk_rows_f16.
@@ -334,13 +265,13 @@ int qk_rows_any(const char* name, const float* qkv, const float* qn, const float
   HV_LAUNCHED("k_qk_rows");
 }
 
-// hv_attn_rows and hv_attn_rows_f16.
-template <class KT>
-int attn_rows_any(const char* name, const float* q, const KT* kc, const KT* vc, float* ctx,
-                  const float* scale, int pos0, int nq, int hd, int group, int kvstride,
-                  int ntok, float* part, int32_t* ticket, void* stream) {
-  HV_REQUIRE(q && kc && vc && ctx && scale && part && ticket && nq > 0 && group > 0 &&
-                 ntok > 0 && ntok <= 65535 && pos0 >= 0,
+// hv_attn_rows and hv_attn_rows_f16: the reference-order attention of hv_attn_decode,
+// one query token per grid row, each at its own position pos0 + t.
+int attn_rows_any(const char* name, bool kv_half, const float* q, const void* kc,
+                  const void* vc, float* ctx, const float* scale, int pos0, int nq, int hd,
+                  int group, int kvstride, int ntok, float* part, void* stream) {
+  HV_REQUIRE(q && kc && vc && ctx && scale && part && nq > 0 && group > 0 && ntok > 0 &&
+                 ntok <= 65535 && pos0 >= 0,
              HV_E_INVALID, "%s: bad arguments", name);
   HV_REQUIRE(hd == kHd, HV_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, hd);
   HV_REQUIRE(nq % group == 0 && kvstride % hd == 0, HV_E_INVALID,
@@ -351,18 +282,11 @@ int attn_rows_any(const char* name, const float* q, const KT* kc, const KT* vc, 
   HV_REQUIRE((long long)pos0 + ntok <= cap, HV_E_INVALID,
              "%s: positions %d .. %d outside the cache of %d", name, pos0, pos0 + ntok - 1, cap);
   int nch = 0;
-  const int rc = rows_attn_chunks(nq / group, cap, &nch);
+  const int rc = attn_exact_chunks(nq / group, cap, &nch);
   if (rc) return rc;
-  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
-             "%s: %d chunks per kv head (at most %d)", name, nch, kAttnMaxChunks);
-  cudaStream_t st = (cudaStream_t)stream;
-  int* tk = reinterpret_cast<int*>(ticket);
-  switch (group) {
-    case 1: return launch_attn_rows<1>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    case 2: return launch_attn_rows<2>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    case 4: return launch_attn_rows<4>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-    default: return launch_attn_rows<8>(q, kc, vc, ctx, scale, pos0, cap, nch, nq, ntok, part, tk, st);
-  }
+  return attn_exact_launch(group, kv_half, q, (size_t)nq * kHd, kc, vc, ctx, (size_t)nq * kHd,
+                           scale, nullptr, pos0, nq, cap, nch, ntok, part,
+                           attn_exact_scratch_floats(nq, cap, nch), (cudaStream_t)stream);
 }
 
 }  // namespace
@@ -412,10 +336,10 @@ extern "C" int hv_attn_rows_scratch(int nq, int group, int cap, int ntok, size_t
                  ticket_bytes,
              HV_E_INVALID, "hv_attn_rows_scratch: bad arguments");
   int nch = 0;
-  const int rc = rows_attn_chunks(nq / group, cap, &nch);
+  const int rc = attn_exact_chunks(nq / group, cap, &nch);
   if (rc) return rc;
-  *part_bytes = (size_t)ntok * nq * nch * kPartStride * sizeof(float);
-  *ticket_bytes = (size_t)ntok * (nq / group) * sizeof(int);
+  *part_bytes = (size_t)ntok * attn_exact_scratch_floats(nq, cap, nch) * sizeof(float);
+  *ticket_bytes = sizeof(int);   // not used any more; kept for the entry point's signature
   return HV_OK;
 }
 
@@ -423,17 +347,18 @@ extern "C" int hv_attn_rows(const float* q, const float* kc, const float* vc, fl
                             const float* scale, int pos0, int nq, int hd, int group,
                             int kvstride, int ntok, float* part, int32_t* ticket,
                             void* stream) {
-  return attn_rows_any("hv_attn_rows", q, kc, vc, ctx, scale, pos0, nq, hd, group, kvstride,
-                       ntok, part, ticket, stream);
+  (void)ticket;
+  return attn_rows_any("hv_attn_rows", false, q, kc, vc, ctx, scale, pos0, nq, hd, group,
+                       kvstride, ntok, part, stream);
 }
 
 extern "C" int hv_attn_rows_f16(const float* q, const uint16_t* kc, const uint16_t* vc,
                                 float* ctx, const float* scale, int pos0, int nq, int hd,
                                 int group, int kvstride, int ntok, float* part,
                                 int32_t* ticket, void* stream) {
-  return attn_rows_any("hv_attn_rows_f16", q, reinterpret_cast<const __half*>(kc),
-                       reinterpret_cast<const __half*>(vc), ctx, scale, pos0, nq, hd, group,
-                       kvstride, ntok, part, ticket, stream);
+  (void)ticket;
+  return attn_rows_any("hv_attn_rows_f16", true, q, kc, vc, ctx, scale, pos0, nq, hd, group,
+                       kvstride, ntok, part, stream);
 }
 
 extern "C" int hv_silu_rows(const float* gu, float* act, int ffn, int ntok, void* stream) {

@@ -35,9 +35,10 @@
 // (ld.global.cg) after a grid barrier: L1 is not coherent across SMs.
 #include <mutex>
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 
-#include "attn_decode.cuh"
+#include "attn_exact.cuh"
 #include "gemv_mma.cuh"
 #include "hv_internal.h"
 #include "hv_wait.cuh"
@@ -68,7 +69,6 @@ static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention 
 static int g_opt_inflight = 6;
 static int g_opt_evict_first = 1;
 static int g_opt_local_qkv_barrier = 0;
-static int g_opt_split_merge = 0;
 // Launch flag set by the library (not by callers): the barrier after the qkv projection
 // of a sharded step stays among the rank's own CTAs.
 constexpr int kFlagLocalQkvBarrier = 1 << 8;
@@ -92,6 +92,7 @@ struct StepShared {
   int flag;
   int ok;
   int abort;                     // set by any warp of this CTA whose wait gave up
+  int tree_ok;                   // the pairwise tree of the softmax sum was built
   unsigned phase;                // top bit of the grid barrier counter to wait for next
   unsigned xphase;               // sharded: top bit of the cross-rank counter (CTA 0)
   unsigned gen;                  // sharded: generation of the local release word
@@ -101,16 +102,21 @@ struct StepShared {
 
 // Byte offsets of the dynamic shared memory regions (host and device agree).
 struct StepLayout {
-  size_t layers, bars, act_q, act_sb, work, ring, total;
+  size_t layers, bars, act_q, act_sb, tree, work, ring, total;
 };
 
 HV_HD size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Floats of the attention work area: phase A (q rows, this step's k and v rows, the
+// norm scratch, the chunk's scores) or phase B (node values of the pairwise tree per
+// head, two blocks of weights per head, the per-head maxima), whichever is larger.
 HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
   const size_t chunk_max = ((size_t)cap + nch - 1) / nch;
-  const size_t lg = ((size_t)chunk_max * gs + 3) & ~size_t(3);
-  return (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 4 * (size_t)gs + lg +
-         (size_t)kConsWarps * gs * kHd;
+  const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd +
+                   (((size_t)chunk_max * gs + 3) & ~size_t(3));
+  const size_t nvl = ((size_t)pw_tree_nodes_max(cap) + 3) & ~size_t(3);
+  const size_t b = (size_t)gs * nvl + (size_t)gs * 2 * (kSlotBytes / (32 * 2)) + 8;
+  return a > b ? a : b;
 }
 
 HV_HD StepLayout step_layout(int gs, int hid, int qdim, int ffn, int cap, int nch, int nslots,
@@ -121,7 +127,8 @@ HV_HD StepLayout step_layout(int gs, int hid, int qdim, int ffn, int cap, int nc
   L.bars = L.layers + align_up((size_t)n_layer * sizeof(hv_layer_w), 16);
   L.act_q = L.bars + 2 * kMaxSlots * sizeof(uint64_t);
   L.act_sb = L.act_q + align_up((size_t)kmax, 16);
-  L.work = L.act_sb + align_up((size_t)(kmax / kBlock) * 8, 16);
+  L.tree = L.act_sb + align_up((size_t)(kmax / kBlock) * 8, 16);
+  L.work = L.tree + align_up(sizeof(PwTree), 16);
   const size_t attn = attn_area_floats(gs, cap, nch) * 4;
   const size_t norm = (size_t)hid * 4;
   L.ring = align_up(L.work + (attn > norm ? attn : norm), 128);
@@ -379,6 +386,16 @@ HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
   }
 }
 
+// Rows of a phase-B V slot: 32-dim slices of BR consecutive positions.
+template <class KT>
+constexpr int kVRows = kSlotBytes / (32 * (int)sizeof(KT));
+
+// The phase-B item of CTA b (kv head * 4 + slice), or -1: items spread over the grid.
+HV_DEV int ctx_item(int b, int grid, int nitems) {
+  const int k = (int)(((long long)b * nitems + grid - 1) / grid);
+  return (k < nitems && (int)(((long long)k * grid) / nitems) == b) ? k : -1;
+}
+
 // ---- the producer ----------------------------------------------------------------------
 
 struct Producer {
@@ -399,16 +416,15 @@ struct Producer {
     policy = hint ? policy_evict_first() : 0ull;
   }
 
-  // Claims the next slot (waiting until its previous contents were released and until
-  // fewer than `inflight` earlier copies are still in flight) and starts up to two
-  // copies into it.
-  HV_DEV void issue(const void* a, unsigned na, const void* b, unsigned nb_, unsigned b_off) {
-    if (!live) return;
+  // Waits until the next slot's previous contents were released and until fewer than
+  // `inflight` earlier copies are still in flight; false if the wait gave up.
+  HV_DEV bool claim() {
+    if (!live) return false;
     if (q >= (unsigned)R.ns && !mbar_probe(R.empty_of(q), R.parity(q) ^ 1u)) {
       const unsigned long long t0 = global_ns();
       if (!mbar_wait(R.empty_of(q), R.parity(q) ^ 1u, S, status, kProducerWaitNs)) {
         live = false;
-        return;
+        return false;
       }
       t_empty += global_ns() - t0;
     }
@@ -418,11 +434,17 @@ struct Producer {
         const unsigned long long t0 = global_ns();
         if (!mbar_wait(R.full_of(p), R.parity(p), S, status, kProducerWaitNs)) {
           live = false;
-          return;
+          return false;
         }
         t_flight += global_ns() - t0;
       }
     }
+    return true;
+  }
+
+  // Claims the next slot and starts up to two bulk copies into it.
+  HV_DEV void issue(const void* a, unsigned na, const void* b, unsigned nb_, unsigned b_off) {
+    if (!claim()) return;
     unsigned char* dst = R.slot(q);
     uint64_t* full = R.full_of(q);
     mbar_arrive_tx(full, na + nb_);
@@ -461,16 +483,38 @@ struct Producer {
     }
   }
 
-  // K rows then V rows [t0, te) of kv head g for one attention work item (KT: the
-  // cache's element type, float or __half).
+  // K rows [t0, te) of kv head g for one attention work item (KT: the cache's element
+  // type, float or __half), kSlotRows rows per slot.
   template <class KT>
-  HV_DEV void kv(const KT* kc, const KT* vc, int g, int cap, int t0, int te) {
-    for (int pass = 0; pass < 2; ++pass) {
-      const KT* base = (pass == 0 ? kc : vc) + (size_t)g * cap * kHd;
-      for (int r = t0; r < te && live; r += kSlotRows) {
-        const unsigned n = (unsigned)min(kSlotRows, te - r);
-        issue(base + (size_t)r * kHd, n * kHd * (unsigned)sizeof(KT), nullptr, 0, 0);
-      }
+  HV_DEV void krows(const KT* kc, int g, int cap, int t0, int te) {
+    const KT* base = kc + (size_t)g * cap * kHd;
+    for (int r = t0; r < te && live; r += kSlotRows) {
+      const unsigned n = (unsigned)min(kSlotRows, te - r);
+      issue(base + (size_t)r * kHd, n * kHd * (unsigned)sizeof(KT), nullptr, 0, 0);
+    }
+  }
+
+  // The 32-dim slice x0 .. x0 + 31 of V rows [0, nrows) starting at row y0 of the cache's
+  // 2-D view `vmap`, kVRows rows per slot (tensor copies; rows past the view read zeros).
+  template <class KT>
+  HV_DEV void vslices(const CUtensorMap* vmap, int x0, int y0, int nrows) {
+    constexpr int BR = kVRows<KT>;
+    for (int r = 0; r < nrows && live; r += BR) {
+      if (!claim()) return;
+      unsigned char* dst = R.slot(q);
+      uint64_t* full = R.full_of(q);
+      mbar_arrive_tx(full, (unsigned)kSlotBytes);
+      if (hint)
+        asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+                     " [%0], [%1, {%2, %3}], [%4], %5;"
+                     :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0 + r), "r"(sm_addr(full)),
+                        "l"(policy) : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                     " [%0], [%1, {%2, %3}], [%4];"
+                     :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0 + r), "r"(sm_addr(full))
+                     : "memory");
+      ++q;
     }
   }
 };
@@ -488,7 +532,8 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
 
 template <class KT>
 HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int pos,
-                    const Ring& R, StepShared& S, int inflight, int evict_first) {
+                    const Ring& R, StepShared& S, int inflight, int evict_first,
+                    const CUtensorMap* vmap) {
   Producer P(R, S, D.status, inflight, evict_first);
   const int world = D.world > 1 ? D.world : 1;
   const int hid = D.hidden, ffn = D.ffn, qdim = D.n_head * kHd * world, hrows = hid / world;
@@ -496,6 +541,8 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
   const int nch = D.attn_chunks;
   const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
             it_ffn = pp_iters(ffn * world / kBlock);
+  const int citem = ctx_item(blockIdx.x, gridDim.x, D.n_kv * kSlices);
+  const long long rowb = (long long)kHd * sizeof(KT);
   int off = 0, t0, t1;
   for (int l = 0; l < D.n_layer && P.live; ++l) {
     const hv_layer_w* L = Ls + l;
@@ -504,8 +551,12 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
     for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
       int a0, a1, ae;
       attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
-      P.kv(reinterpret_cast<const KT*>(L->kc), reinterpret_cast<const KT*>(L->vc), wi / nch,
-           D.cap, a0, ae);
+      P.krows(reinterpret_cast<const KT*>(L->kc), wi / nch, D.cap, a0, ae);
+    }
+    if (citem >= 0) {
+      const long long vrow = ((const char*)L->vc - (const char*)D.kv_base) / rowb +
+                             (long long)(citem / kSlices) * D.cap;
+      P.vslices<KT>(vmap, 32 * (citem % kSlices), (int)vrow, pos);
     }
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
@@ -938,145 +989,63 @@ __device__ __noinline__ void gemv_ring(const Ring R, unsigned q0, const GvPlan& 
   }
 }
 
-// ---- attention -------------------------------------------------------------------------
+// ---- attention: the reference's order, bit for bit (attn_exact.cuh) ---------------------
+//
+// Phase A, per (kv head, chunk) work item: q/k RMSNorm + RoPE of the item's heads, the KV
+// append (by the chunk holding pos), then every position's dot with the GS query heads in
+// OpenBLAS's row-dot order, K rows from the ring. Scores go to D.part [head][cap], the
+// chunk's maximum per head to D.part [n_head][cap ..][chunk]; then the item adds one to
+// its kv head's ticket.
+// Phase B, per (kv head, 32-dim slice) on its own CTA, as soon as all nch chunks of the
+// kv head have arrived (ticket; no grid barrier): the maximum, numpy's pairwise sum of
+// the exps, then one warp per query head runs the sequential weighted V sum over V rows
+// that the producer brings into the ring as 32-dim slices (tensor copies), row pos from
+// this step's qkv; the warp quantises its 32 outputs (one quant_a8s block) into ctx.
 
-// Rows per score group: enough that one butterfly reduces 32 values (4 rows for GS = 8).
-// Each score is the lane-partial dot (x*x, then three fma) summed over the 32 lanes with
-// the xor-16, 8, 4, 2, 1 tree whatever the group size, so the grouping changes no bit.
-template <int GS>
-constexpr int kScoreRows = GS >= 8 ? 4 : 8;
-
-// Rows tb .. tb + RW - 1 of a block whose cached rows [r0, te) sit in `slot` (null for a
-// block that holds only pos): one shared-memory load per cached row (index clamped inside
-// the slot, so no branch precedes it), the pos row loaded once if this group holds it,
-// rows from `tend` on (not this block's) and stale slot rows selected to zero.
-// Dims 4 lane .. 4 lane + 3 of row r of a ring slot of cache rows, as floats (half ->
-// float is exact).
-HV_DEV float4 slot_row4(const float*, unsigned slot, int r, int lane) {
-  return lds_f4(slot + (unsigned)(r * kHd + 4 * lane) * 4);
-}
-HV_DEV float4 slot_row4(const __half*, unsigned slot, int r, int lane) {
-  const uint2 w = lds_u2(slot + (unsigned)(r * kHd + 4 * lane) * 2);
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-
-template <int RW, class KT>
-HV_DEV void block_rows(float4 (&kv)[RW], int tb, int tend, int te, int pos, unsigned slot,
-                       int r0, unsigned pos_s, int lane) {
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int p = 0; p < RW; ++p) {
-    const int r = min(tb + p - r0, kSlotRows - 1);
-    kv[p] = slot ? slot_row4(static_cast<const KT*>(nullptr), slot, r, lane) : zero;
-  }
-  const bool has_pos = pos >= tb && pos < tb + RW && pos < tend && pos >= te;
-  const float4 pv = has_pos ? lds_f4(pos_s + 16 * lane) : zero;
-#pragma unroll
-  for (int p = 0; p < RW; ++p) {
-    const int t = tb + p;
-    kv[p] = (t < te && t < tend) ? kv[p] : ((has_pos && t == pos) ? pv : zero);
-  }
-}
-
-// Scores of positions tb .. tb + kScoreRows - 1 (those below tend) for the GS heads, the
-// arithmetic of attn_chunk in attn_decode.cuh. slot (0: none), kpos_s and lg_s are shared
-// addresses.
-template <int GS, class KT>
-HV_DEV void group_scores(const float4 (&qv)[GS], int tb, int tend, int t0, int te, int pos,
-                         unsigned slot, int r0, unsigned kpos_s, float scale, unsigned lg_s) {
-  constexpr int RW = kScoreRows<GS>;
-  const int lane = threadIdx.x & 31;
-  float4 kv[RW];
-  block_rows<RW, KT>(kv, tb, tend, te, pos, slot, r0, kpos_s, lane);
-  float v[RW * GS];
-#pragma unroll
-  for (int p = 0; p < RW; ++p)
-#pragma unroll
-    for (int i = 0; i < GS; ++i) {
-      float s = qv[i].x * kv[p].x;
-      s = fmaf(qv[i].y, kv[p].y, s);
-      s = fmaf(qv[i].z, kv[p].z, s);
-      s = fmaf(qv[i].w, kv[p].w, s);
-      v[p * GS + i] = s;
-    }
-  int idx;
-  const float tot = halving_reduce<RW * GS>(v, lane, &idx);
-  constexpr int dup = 32 / (RW * GS) > 0 ? 32 / (RW * GS) : 1;
-  if ((lane & (dup - 1)) == 0) {
-    const int p = idx / GS, i = idx % GS;
-    const int t = tb + p;
-    if (t < tend) {
-      const float val = tot * scale;
-      asm volatile("st.shared.f32 [%0], %1;" :: "r"(lg_s + (unsigned)((t - t0) * GS + i) * 4),
-                   "f"(val) : "memory");
-    }
-  }
-}
-
-// Probability-weighted V rows [tb, tb + 8) (those below tend) into acc, rows in order
-// (the order of attn_chunk); all loads are issued before the first multiply-add.
-template <int GS, class KT>
-HV_DEV void group_values(float4 (&acc)[GS], int tb, int tend, int t0, int te, int pos,
-                         unsigned slot, int r0, unsigned vpos_s, unsigned lg_s) {
-  constexpr int RW = 8;
-  const int lane = threadIdx.x & 31;
-  float4 vv[RW];
-  float w[RW][GS];
-  block_rows<RW, KT>(vv, tb, tend, te, pos, slot, r0, vpos_s, lane);
-#pragma unroll
-  for (int p = 0; p < RW; ++p)
-#pragma unroll
-    for (int i = 0; i < GS; ++i)
-      w[p][i] = (tb + p < tend) ? lds_f1(lg_s + (unsigned)((tb + p - t0) * GS + i) * 4) : 0.f;
-#pragma unroll
-  for (int p = 0; p < RW; ++p) {
-    if (tb + p < tend) {
-#pragma unroll
-      for (int i = 0; i < GS; ++i) {
-        acc[i].x = fmaf(w[p][i], vv[p].x, acc[i].x);
-        acc[i].y = fmaf(w[p][i], vv[p].y, acc[i].y);
-        acc[i].z = fmaf(w[p][i], vv[p].z, acc[i].z);
-        acc[i].w = fmaf(w[p][i], vv[p].w, acc[i].w);
+// Element e of a cache row held in shared memory (a ring slot row of KT, or a float row).
+template <class KT>
+struct SlotRow {
+  unsigned addr;
+  bool f32row;                                     // this step's row, kept as floats
+  HV_DEV float operator()(int e) const {
+    if constexpr (kKvHalf<KT>) {
+      if (!f32row) {
+        unsigned short h;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr + 2u * e));
+        return __half2float(__ushort_as_half(h));
       }
     }
+    return lds_f1(addr + 4u * e);
   }
-}
+};
 
-// The attention phase: this CTA's (kv head, chunk) work items, K and V rows streamed
-// through the ring (sequence numbers from *q). Same arithmetic, in the same order, as
-// attn_chunk with eight warps (k_attn): blocks of 20 positions go to warp (block % 8)
-// for the scores and the weighted V sum; warp i takes head i for the max and exp.
-// KT = __half: the compressed-KV lane. This step's k and v rows are rounded to binary16
-// before use, so row pos enters the scores and the V sum exactly as the appended cache
-// row does (hv_kv_append_f16 then hv_attn_decode_f16).
-template <int GS, bool kSplitMerge, class KT>
-__device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* L, int pos,
-                                       const Ring R, unsigned* qp, StepShared& S,
-                                       float* area, int tb) {
+// Phase A of this CTA's (kv head, chunk) items.
+template <int GS, class KT>
+__device__ __noinline__ void attn_scores_ring(const hv_step_desc& D, const hv_layer_w* L,
+                                              int pos, int runs, const Ring R, unsigned* qp,
+                                              StepShared& S, float* area, int tb) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
-  const int chunk_max = (cap + nch - 1) / nch;
-  const int lg_floats = (chunk_max * GS + 3) & ~3;   // keeps red_s 16-byte aligned
   float* q_s = area;
   float* kpos_s = q_s + GS * kHd;
   float* vpos_s = kpos_s + kHd;
   float* tmp_s = vpos_s + kHd;                       // (GS + 1) x 128
-  float* stat_s = tmp_s + (GS + 1) * kHd;            // 2 GS (+pad)
-  float* lg_s = stat_s + 4 * GS;
-  float* red_s = lg_s + lg_floats;                   // accessed as float4
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* lg_s = tmp_s + (GS + 1) * kHd;              // [chunk_max][GS]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, rr = lane >> 3;
   const float* cs = D.cos_t + (size_t)pos * (kHd / 2);
   const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
   const float scale = D.attn_scale;
+  const int T = pos + 1;
+  float* lg_g = D.part;
+  float* cm_g = D.part + (size_t)nq * cap;
+  constexpr int HP = GS < 4 ? GS : 4;
   for (int wi = blockIdx.x; wi < nkv * nch; wi += gridDim.x) {
     const int g = wi / nch, c = wi % nch;
     int t0, t1, te;
     attn_rows(pos, nch, c, &t0, &t1, &te);
     const int n = t1 - t0;
     const int nk = (te - t0 + kSlotRows - 1) / kSlotRows;
-    const unsigned qk = *qp, qv0 = *qp + (unsigned)nk;
-    *qp += 2u * (unsigned)nk;
+    const unsigned qk = *qp;
+    *qp += (unsigned)nk;
     // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
     for (int h = warp; h < GS + 2; h += kConsWarps) {
       if (h < GS) {
@@ -1106,14 +1075,12 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
       vc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(vpos_s[threadIdx.x]);
     }
 
-    // ---- scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows, row
-    // pos from kpos_s) to warp m % 8, so each slot has a single consumer warp; the block
-    // after the last slot holds only pos when pos starts a block
-    float4 qv[GS];
-#pragma unroll
-    for (int i = 0; i < GS; ++i) qv[i] = reinterpret_cast<const float4*>(q_s + i * kHd)[lane];
+    // scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows; row pos from
+    // kpos_s) to warp m % 8, four positions per pass (8 lanes each)
     bool ok = true;
     const int nblk = (n + kSlotRows - 1) / kSlotRows;
+    float qr[HP][16];
+    if constexpr (GS <= 4) load_qregs<HP>(q_s, j, qr);
     for (int m = warp; m < nblk && ok; m += kConsWarps) {
       const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
       unsigned slot = 0;
@@ -1123,11 +1090,27 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
         if (!ok) break;
         slot = sh_addr(R.slot(q));
       }
-      const long long c0 = clock64();
-      for (int tg = r0; tg < r1; tg += kScoreRows<GS>)
-        group_scores<GS, KT>(qv, tg, r1, t0, te, pos, slot, r0, sh_addr(kpos_s), scale,
-                             sh_addr(lg_s));
-      if (lane == 0) S.busy[warp] += clock64() - c0;
+#pragma unroll 1
+      for (int p0 = 0; p0 < GS; p0 += HP) {
+        if constexpr (GS > 4) load_qregs<HP>(q_s + p0 * kHd, j, qr);
+#pragma unroll 1
+        for (int tg = r0; tg < r1; tg += 4) {
+          const int t = tg + rr;
+          const bool valid = t < r1;
+          const bool cached = t < te;
+          const int kind = valid ? blas_row_kind(T, t, runs) : 0;
+          SlotRow<KT> row;
+          row.f32row = !cached;
+          row.addr = cached ? slot + (unsigned)((t - r0) * kHd * (int)sizeof(KT))
+                            : sh_addr(kpos_s);
+          float d[HP];
+          rowdots_blas<HP>(row, kind, qr, q_s + p0 * kHd, j, d);
+          float v = d[0];
+#pragma unroll
+          for (int h = 1; h < HP; ++h) v = (j == h) ? d[h] : v;
+          if (valid && j < HP) lg_s[(t - t0) * GS + p0 + j] = __fmul_rn(v, scale);
+        }
+      }
       if (m < nk) {
         __syncwarp();
         if (lane == 0) mbar_arrive_n(R.empty_of(qk + (unsigned)m), kConsWarps);
@@ -1136,167 +1119,207 @@ __device__ __noinline__ void attn_ring(const hv_step_desc& D, const hv_layer_w* 
     csync();
     trace_mark(D, tb + 15);
     trace_wait(D, S, tb + 21);
-    if (threadIdx.x == 0 && D.trace != nullptr) {
-      D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + tb + 25] = S.busy[0];
-      S.busy[0] = 0;
-    }
-
-    // ---- per-head max and exp: warp i handles head i
+    // the chunk's scores and per-head maximum to global memory, then its ticket
     for (int i = warp; i < GS; i += kConsWarps) {
+      const int h = g * GS + i;
       float mx = -INFINITY;
-      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, lg_s[t * GS + i]);
+      for (int t = lane; t < n; t += 32) {
+        const float sc = lg_s[t * GS + i];
+        mx = fmaxf(mx, sc);
+        lg_g[(size_t)h * cap + t0 + t] = sc;
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-      float l = 0.f;
-      for (int t = lane; t < n; t += 32) {
-        const float e = (n > 0) ? expf(lg_s[t * GS + i] - mx) : 0.f;
-        lg_s[t * GS + i] = e;
-        l += e;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-      if (lane == 0) { stat_s[2 * i] = mx; stat_s[2 * i + 1] = l; }
+      if (lane == 0) cm_g[(size_t)h * nch + c] = mx;
     }
     csync();
-    trace_mark(D, tb + 16);
-    trace_wait(D, S, tb + 20);
-
-    // ---- probability-weighted V sum: V rows from the ring, the same block -> warp map,
-    // positions in order within a block
-    float4 acc[GS];
-#pragma unroll
-    for (int i = 0; i < GS; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int m = warp; m < nblk && ok; m += kConsWarps) {
-      const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
-      unsigned slot = 0;
-      if (m < nk) {
-        const unsigned q = qv0 + (unsigned)m;
-        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
-        if (!ok) break;
-        slot = sh_addr(R.slot(q));
-      }
-      for (int tg = r0; tg < r1; tg += 8)
-        group_values<GS, KT>(acc, tg, r1, t0, te, pos, slot, r0, sh_addr(vpos_s),
-                             sh_addr(lg_s));
-      if (m < nk) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)m), kConsWarps);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < GS; ++i)
-      reinterpret_cast<float4*>(red_s + ((size_t)warp * GS + i) * kHd)[lane] = acc[i];
-    csync();
-    float* part = D.part + ((size_t)g * nch + c) * GS * kPartStride;
-    for (int e = threadIdx.x; e < GS * kHd; e += kConsThreads) {
-      float s = 0.f;
-      for (int w = 0; w < kConsWarps; ++w) s += red_s[(size_t)w * GS * kHd + e];
-      const int i = e / kHd, d = e % kHd;
-      part[i * kPartStride + 4 + d] = s;
-    }
-    if (threadIdx.x < GS) {
-      part[threadIdx.x * kPartStride + 0] = (n > 0) ? stat_s[2 * threadIdx.x] : -INFINITY;
-      part[threadIdx.x * kPartStride + 1] = (n > 0) ? stat_s[2 * threadIdx.x + 1] : 0.f;
-    }
-    if constexpr (!kSplitMerge) __threadfence();
-    csync();
-    trace_mark(D, tb + 17);
-    trace_wait(D, S, tb + 22);
-    if constexpr (kSplitMerge) continue;             // merged after the grid barrier
-    if (threadIdx.x == 0) S.flag = (atomicAdd(D.ticket + g, 1) == nch - 1);
-    csync();
-    trace_mark(D, tb + 18);
-    if (S.flag) {
+    if (threadIdx.x == 0) {
       __threadfence();
-      // the o projection's input, quantised here: int8 [qdim] then (scale, sum) pairs;
-      // this rank's heads start at head rank * n_head of the whole vector
-      const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
-      const int qall = nq * kHd * world, first = (rank * nq + g * GS) * kHd;
-      int8_t* cq = reinterpret_cast<int8_t*>(D.ctx);
-      int2* csb = reinterpret_cast<int2*>(cq + qall);
-      attn_merge<GS, CSync, true>(D.part + (size_t)g * nch * GS * kPartStride, nch, nullptr,
-                                  red_s, cq + first, csb + first / kBlock);
-      if (threadIdx.x == 0) D.ticket[g] = 0;
-      if (world > 1) {
-        csync();
-        share_bytes(D.peers->ctx, rank, world, cq, first, GS * kHd, qall);
-      }
+      atomicAdd(D.ticket + g, 1);
     }
-    csync();
-    trace_mark(D, tb + 19);
+    trace_mark(D, tb + 16);
   }
 }
 
-// The attention merge as its own phase (HV_STEP_OPT_SPLIT_MERGE, one GPU): after the
-// barrier that ends attention, each 32-value quantisation block of ctx is merged by one
-// warp (blocks spread over the CTAs), instead of each kv head's whole merge by the last
-// CTA of that head while every other CTA waits. Lane d of the warp does dim d of the
-// block; the arithmetic and its order are attn_merge's (M = max_c m_c, w_c = exp(m_c - M),
-// L = fma(w_c, l_c, L) and o = fma(w_c, acc_c, o) in chunk order, ctx = o * (1 / L), then
-// quant_a8s of the block), so the bits are the same; only the loads are arranged for
-// fewer L2 round trips. `area`: kConsWarps * nch floats.
-template <int GS>
-__device__ __noinline__ void merge_blocks(const hv_step_desc& D, float* area) {
+// Phase B of this CTA's (kv head, slice) item, if it has one: waits (bounded) until the
+// kv head's ticket reaches (layer + 1) * nch. `tree`: numpy's pairwise tree for pos + 1
+// values, built here in layer 0 (warp 1, while thread 0 waits) and kept for the launch.
+template <int GS, class KT>
+__device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int layer,
+                                           const Ring R, unsigned* qp, StepShared& S,
+                                           PwTree* tree, float* area, int tb) {
+  const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
+  const int item = ctx_item(blockIdx.x, gridDim.x, nkv * kSlices);
+  if (item < 0) return true;
+  constexpr int BR = kVRows<KT>;
+  const int g = item / kSlices, jsl = item % kSlices;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = D.n_head, nch = D.attn_chunks;
-  constexpr int kPerHead = kHd / kBlock;
-  const int nblk = nq * kPerHead;
-  int8_t* cq = reinterpret_cast<int8_t*>(D.ctx);
-  int2* csb = reinterpret_cast<int2*>(cq + (size_t)nq * kHd);
-  float* wv = area + (size_t)warp * nch;
-  for (int qb = blockIdx.x + warp * gridDim.x; qb < nblk; qb += gridDim.x * kConsWarps) {
-    const int h = qb / kPerHead, d = (qb % kPerHead) * kBlock + lane;
-    const int g = h / GS, i = h % GS;
-    const float* ph = D.part + (size_t)g * nch * GS * kPartStride + (size_t)i * kPartStride;
-    constexpr size_t kChunk = (size_t)GS * kPartStride;
-    float M = -INFINITY;
-    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(ph + c * kChunk));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-    // w_c = exp(m_c - M) and l_c, loaded by lane c of each pass of 32 chunks together (one
-    // L2 round trip per pass); every lane then runs the chain L = fma(w_c, l_c, L) in chunk
-    // order from shuffles, so L is attn_merge's value in every lane
-    float L = 0.f;
-    for (int c0 = 0; c0 < nch; c0 += 32) {
-      const int c = c0 + lane;
-      float w = 0.f, l = 0.f;
-      if (c < nch) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(ph + c * kChunk));
-        w = expf(ml.x - M);
-        l = ml.y;
-        wv[c] = w;
-      }
-      const int n = min(32, nch - c0);
-      for (int k = 0; k < n; ++k)
-        L = fmaf(__shfl_sync(0xFFFFFFFFu, w, k), __shfl_sync(0xFFFFFFFFu, l, k), L);
-    }
-    const float inv = 1.0f / L;
-    __syncwarp();                                   // wv[] of every lane
-    float o = 0.f;
-    for (int c0 = 0; c0 < nch; c0 += 16) {
-      float a[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) a[k] = (c0 + k < nch) ? __ldcg(ph + (c0 + k) * kChunk + 4 + d) : 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (c0 + k < nch) o = fmaf(wv[c0 + k], a[k], o);
-    }
-    int8_t q8;
-    float sc;
-    int bs;
-    quant_block_warp(o * inv, lane, &q8, &sc, &bs);
-    cq[(size_t)h * kHd + d] = q8;
-    if (lane == 0) csb[qb] = make_int2(__float_as_int(sc), bs);
-    __syncwarp();                                   // wv is reused by the next block
+  const int T = pos + 1;
+  const int nvs = (pos + BR - 1) / BR;               // V slots: cached rows [0, pos)
+  const unsigned qv0 = *qp;
+  *qp += (unsigned)nvs;
+  const int nvl = (pw_tree_nodes_max(cap) + 3) & ~3;
+  float* vals = area;                                // [GS][nvl]: node values
+  float* wbuf = vals + (size_t)GS * nvl;             // [GS][2][BR]
+  float* ms = wbuf + (size_t)GS * 2 * BR;            // M per head
+  const float* lg_g = D.part;
+  const float* cm_g = D.part + (size_t)nq * cap;
+  if (layer == 0 && warp == 1) {
+    const bool built = pw_tree_build_warp(T, tree);
+    if (lane == 0) S.tree_ok = built;
   }
+  // the kv head's chunks (bounded wait on its ticket)
+  if (threadIdx.x == 0) {
+    const unsigned want = (unsigned)((layer + 1) * nch);
+    const unsigned* tk = reinterpret_cast<const unsigned*>(D.ticket + g);
+    bool ok = true;
+    if (ld_acquire(tk) < want) {
+      const unsigned long long t0 = global_ns();
+      while (ld_acquire(tk) < want) {
+        if (*(volatile int*)D.status != 0) { ok = false; break; }
+        if (global_ns() - t0 > kWaitNs) {
+          atomicCAS(D.status, 0, HV_E_TIMEOUT);
+          ok = false;
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+    if (!ok) *(volatile int*)&S.abort = 1;
+    S.ok = ok;
+  }
+  csync();
+  if (!S.ok) return false;
+  if (!S.tree_ok) {
+    if (threadIdx.x == 0) {
+      atomicCAS(D.status, 0, HV_E_INVALID);
+      *(volatile int*)&S.abort = 1;
+    }
+    return false;
+  }
+  trace_mark(D, tb + 17);
+  for (int i = warp; i < GS; i += kConsWarps) {
+    float m = -INFINITY;
+    for (int c = lane; c < nch; c += 32) m = fmaxf(m, __ldcg(cm_g + (size_t)(g * GS + i) * nch + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (lane == 0) ms[i] = m;
+  }
+  csync();
+  {
+    // numpy's pairwise leaves of the exps: head i's 8-lane groups are those of the warps
+    // w = i (mod GS)
+    const int i = warp % GS;
+    const int gi = (warp / GS) * 4 + (lane >> 3), ng = (kConsWarps / GS) * 4;
+    const float* lgh = lg_g + (size_t)(g * GS + i) * cap;
+    const float M = ms[i];
+    const auto e = [lgh, M](int t) { return np_expf(__fsub_rn(__ldcg(lgh + t), M)); };
+    for (int l0 = 0; l0 < tree->nleaf; l0 += ng) {
+      const int l = l0 + gi;
+      const bool live = l < tree->nleaf;
+      const int id = live ? (int)tree->leaf[l] : 0;
+      const float v = pw_leaf_f(e, live ? (int)tree->start[id] : 0, live ? (int)tree->size[id] : 1,
+                                lane & 7);
+      if (live && (lane & 7) == 0) vals[(size_t)i * nvl + id] = v;
+    }
+  }
+  csync();
+  trace_mark(D, tb + 18);
+  bool ok = true;
+  if (warp < GS) {
+    const int i = warp;
+    const float S_ = pw_tree_fold(tree, vals + (size_t)i * nvl);
+    const float M = ms[i];
+    const float* lgh = lg_g + (size_t)(g * GS + i) * cap;
+    float* wb[2] = {wbuf + (size_t)i * 2 * BR, wbuf + (size_t)i * 2 * BR + BR};
+    // weights of block k (positions [k BR, min((k + 1) BR, T))), 32 at a time
+    const auto wgroup = [&](int k, int u, float* dst) {
+      const int t = k * BR + 32 * u + lane;
+      if (32 * u + lane < BR && t < T)
+        dst[32 * u + lane] = __fdiv_rn(np_expf(__fsub_rn(__ldcg(lgh + t), M)), S_);
+    };
+    constexpr int kU = (BR + 31) / 32;
+    const int nblkv = (T + BR - 1) / BR;
+#pragma unroll 1
+    for (int u = 0; u < kU; ++u) wgroup(0, u, wb[0]);
+    __syncwarp();
+    // this step's v row (slice), rounded like the appended row
+    float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
+    if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
+    const unsigned rel = (unsigned)(kConsWarps / GS);
+    float acc = 0.0f;
+#pragma unroll 1
+    for (int k = 0; k < nblkv && ok; ++k) {
+      float* wc = wb[k & 1];
+      float* wn = wb[(k + 1) & 1];
+      const bool nxt = k + 1 < nblkv;
+      int done = 0;
+      const int base = k * BR;
+      const int ncache = max(0, min(BR, pos - base));   // rows of this block from the slot
+      if (ncache > 0) {
+        const unsigned q = qv0 + (unsigned)k;
+        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+        if (!ok) break;
+        const unsigned sl = sh_addr(R.slot(q)) + (unsigned)(lane * (int)sizeof(KT));
+        const unsigned wsh = sh_addr(wc);
+#pragma unroll 1
+        for (int r = 0; r < ncache; r += 8) {
+          if ((r & 31) == 0 && nxt && done < kU) wgroup(k + 1, done++, wn);
+          float v[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            const unsigned a = sl + (unsigned)((r + x) * 32 * (int)sizeof(KT));
+            if constexpr (kKvHalf<KT>) {
+              unsigned short h;
+              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+              v[x] = __half2float(__ushort_as_half(h));
+            } else {
+              v[x] = lds_f1(a);
+            }
+          }
+          const float4 w0 = lds_f4(wsh + 4u * r), w1 = lds_f4(wsh + 4u * r + 16u);
+          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int x = 0; x < 8; ++x)
+            if (r + x < ncache) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
+      }
+      if (pos >= base && pos < base + BR)            // the last row: this step's v
+        acc = __fadd_rn(acc, __fmul_rn(wc[pos - base], vpos));
+      if (nxt)
+        for (; done < kU; ++done) wgroup(k + 1, done, wn);
+      __syncwarp();
+    }
+    if (ok) {
+      // ctx element (head g GS + i, dim 32 jsl + lane) -> int8 + (scale, sum) of its block
+      const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
+      const int qall = nq * kHd * world;
+      const int idx = (rank * nq + g * GS + i) * kHd + 32 * jsl + lane;
+      int8_t q8;
+      float sc;
+      int bs;
+      quant_block_warp(acc, lane, &q8, &sc, &bs);
+      const int2 sbv = make_int2(__float_as_int(sc), bs);
+      for (int k = 0; k < world; ++k) {
+        int8_t* cq = reinterpret_cast<int8_t*>(world > 1 ? D.peers->ctx[k] : (void*)D.ctx);
+        cq[idx] = q8;
+        if (lane == 0) reinterpret_cast<int2*>(cq + qall)[idx / kBlock] = sbv;
+      }
+    }
+  }
+  csync();
+  trace_mark(D, tb + 19);
+  return *(volatile int*)&S.abort == 0;
 }
 
 // ---- the kernel ------------------------------------------------------------------------
 
-template <int GS, bool kSplitMerge, class KT, bool kDq>
-__global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, int flags,
-                                                          int nslots, int inflight,
-                                                          int evict_first) {
+template <int GS, class KT, bool kDq>
+__global__ void __launch_bounds__(kStepThreads, 1)
+k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_first, int runs,
+       const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(128) unsigned char smem[];
   // sharded: n_head, n_kv, ffn and head_rows are this rank's; hidden, the o projection's
   // input (qdim) and the down projection's input (ffn_all) are whole
@@ -1312,6 +1335,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   float* work = reinterpret_cast<float*>(smem + Lo.work);
   const Ring R{smem + Lo.ring, bars, bars + kMaxSlots, nslots};
   hv_layer_w* Ls = reinterpret_cast<hv_layer_w*>(smem + Lo.layers);
+  PwTree* tree = reinterpret_cast<PwTree*>(smem + Lo.tree);
   const ActView act{q_s, sb_s};
 
   trace_mark(D, 0);
@@ -1351,7 +1375,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   }
   if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
     if (threadIdx.x == kConsThreads)
-      produce<KT>(D, Ls, flags, pos, R, S, inflight, evict_first);
+      produce<KT>(D, Ls, flags, pos, R, S, inflight, evict_first, &vmap);
     return;
   }
 
@@ -1390,14 +1414,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_wait(D, S, tb + 23);
     if (!grid_sync(D, S, (flags & kFlagLocalQkvBarrier) == 0)) return;
     trace_mark(D, tb + 2);
-    // P2: attention
-    attn_ring<GS, kSplitMerge, KT>(D, L, pos, R, &q, S, work, tb);
+    // P2: attention -- scores per (kv head, chunk), then the context per (kv head, slice)
+    attn_scores_ring<GS, KT>(D, L, pos, runs, R, &q, S, work, tb);
+    if (!attn_ctx_ring<GS, KT>(D, pos, l, R, &q, S, tree, work, tb)) return;
     trace_mark(D, tb + 3);
     if (!grid_sync(D, S)) return;
-    if constexpr (kSplitMerge) {
-      merge_blocks<GS>(D, work);
-      if (!grid_sync(D, S)) return;
-    }
     trace_mark(D, tb + 4);
     if (threadIdx.x == 0) prefetch_vectors(L, hid, false);
     // P3: o projection + residual
@@ -1453,6 +1474,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
     trace_mark(D, tb + 13);
   }
 
+  // every CTA has passed its last attention phase: the kv heads' tickets restart at zero
+  if (blockIdx.x == 0 && threadIdx.x < D.n_kv) D.ticket[threadIdx.x] = 0;
   if (!(flags & HV_STEP_HEAD)) return;
   const int th = 2 + 28 * D.n_layer;
   norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s, D, -1);
@@ -1509,48 +1532,71 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(const hv_step_desc D, 
   trace_mark(D, th + 2);
 }
 
-// The step kernel for group size gs: variant 0 = f32 cache, 1 = f32 cache with the split
-// merge, 2 = binary16 cache, 3 = f32 cache over dq weight tiles, 4 = binary16 cache over
-// dq weight tiles.
-static void* step_fn(int gs, int variant) {
-  if (variant == 1) {
-    switch (gs) {
-      case 1: return (void*)k_step<1, true, float, false>;
-      case 2: return (void*)k_step<2, true, float, false>;
-      case 4: return (void*)k_step<4, true, float, false>;
-      default: return (void*)k_step<8, true, float, false>;
-    }
-  }
-  if (variant == 2) {
-    switch (gs) {
-      case 1: return (void*)k_step<1, false, __half, false>;
-      case 2: return (void*)k_step<2, false, __half, false>;
-      case 4: return (void*)k_step<4, false, __half, false>;
-      default: return (void*)k_step<8, false, __half, false>;
-    }
-  }
-  if (variant == 3) {
-    switch (gs) {
-      case 1: return (void*)k_step<1, false, float, true>;
-      case 2: return (void*)k_step<2, false, float, true>;
-      case 4: return (void*)k_step<4, false, float, true>;
-      default: return (void*)k_step<8, false, float, true>;
-    }
-  }
-  if (variant == 4) {
-    switch (gs) {
-      case 1: return (void*)k_step<1, false, __half, true>;
-      case 2: return (void*)k_step<2, false, __half, true>;
-      case 4: return (void*)k_step<4, false, __half, true>;
-      default: return (void*)k_step<8, false, __half, true>;
-    }
-  }
+// The step kernel for group size gs: variant 0 = f32 cache, 2 = binary16 cache, 3 = f32
+// cache over dq weight tiles, 4 = binary16 cache over dq weight tiles.
+template <class KT, bool kDq>
+static void* step_fn_gs(int gs) {
   switch (gs) {
-    case 1: return (void*)k_step<1, false, float, false>;
-    case 2: return (void*)k_step<2, false, float, false>;
-    case 4: return (void*)k_step<4, false, float, false>;
-    default: return (void*)k_step<8, false, float, false>;
+    case 1: return (void*)k_step<1, KT, kDq>;
+    case 2: return (void*)k_step<2, KT, kDq>;
+    case 4: return (void*)k_step<4, KT, kDq>;
+    default: return (void*)k_step<8, KT, kDq>;
   }
+}
+static void* step_fn(int gs, int variant) {
+  switch (variant) {
+    case 2: return step_fn_gs<__half, false>(gs);
+    case 3: return step_fn_gs<float, true>(gs);
+    case 4: return step_fn_gs<__half, true>(gs);
+    default: return step_fn_gs<float, false>(gs);
+  }
+}
+
+// The V-slice tensor map of a cache view (rows of 128 elements of `esz` bytes), encoded
+// once per (base, rows, element size) through the driver's cuTensorMapEncodeTiled.
+typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static int vslice_map(const void* base, long long rows, int esz, CUtensorMap* out) {
+  static std::mutex mu;
+  static TmapEncodeFn enc = nullptr;
+  static const void* last_base = nullptr;
+  static long long last_rows = 0;
+  static int last_esz = 0;
+  static CUtensorMap last;
+  std::lock_guard<std::mutex> lk(mu);
+  if (base == last_base && rows == last_rows && esz == last_esz) {
+    *out = last;
+    return HV_OK;
+  }
+  if (!enc) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    HV_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr));
+    HV_REQUIRE(fn != nullptr && qr == cudaDriverEntryPointSuccess, HV_E_UNSUPPORTED,
+               "hv_step_launch: the driver has no cuTensorMapEncodeTiled");
+    enc = (TmapEncodeFn)fn;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)kHd, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHd * (cuuint64_t)esz};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)(kSlotBytes / (32 * esz))};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  const CUresult r = enc(&m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                         2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  HV_REQUIRE(r == CUDA_SUCCESS, HV_E_INVALID,
+             "hv_step_launch: cuTensorMapEncodeTiled failed (%d) for the KV view %p x %lld rows",
+             (int)r, base, rows);
+  last = m;
+  last_base = base;
+  last_rows = rows;
+  last_esz = esz;
+  *out = m;
+  return HV_OK;
 }
 
 // Ring slots that fit next to the fixed regions (0 if the fixed regions alone do not).
@@ -1582,11 +1628,13 @@ int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t
   if (nch < 1) nch = 1;
   const int need = (cap + 511) / 512;
   if (nch < need) nch = need;
+  HV_REQUIRE(cap <= kExactMaxCap, HV_E_UNSUPPORTED,
+             "hv_step_config: cache of %d positions (at most %d)", cap, kExactMaxCap);
   HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
              "hv_step_config: %d attention chunks per kv head (at most %d; cap %d is too long)",
              nch, kAttnMaxChunks, cap);
   *chunks = nch;
-  *part_floats = (size_t)n_kv * nch * group * kPartStride;
+  *part_floats = (size_t)n_kv * group * ((size_t)cap + (size_t)nch);
   if (smem) *smem = 0;
   return HV_OK;
 }
@@ -1623,9 +1671,8 @@ int hv_step_set_option(int option, int value) {
     case HV_STEP_OPT_LOCAL_QKV_BARRIER:
       g_opt_local_qkv_barrier = value != 0;
       return HV_OK;
-    case HV_STEP_OPT_SPLIT_MERGE:
-      g_opt_split_merge = value != 0;
-      return HV_OK;
+    case HV_STEP_OPT_REF_BLAS_RUNS:
+      return set_ref_blas_runs(value);
     default:
       HV_REQUIRE(false, HV_E_INVALID, "hv_step_set_option: unknown option %d", option);
   }
@@ -1689,12 +1736,19 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
              "hv_step_launch: kv_dtype %d (HV_KV_F32 or HV_KV_F16)", h.kv_dtype);
   HV_REQUIRE(h.w4_layout == HV_W4_PP || h.w4_layout == HV_W4_DQ, HV_E_INVALID,
              "hv_step_launch: w4_layout %d (HV_W4_PP or HV_W4_DQ)", h.w4_layout);
-  // the split merge (one GPU, f32 cache): its per-warp chunk weights live in the work area
-  const bool split_merge = g_opt_split_merge && world == 1 && h.kv_dtype == HV_KV_F32 &&
-      h.w4_layout == HV_W4_PP &&
-      (lay.ring - lay.work) / sizeof(float) >= (size_t)kConsWarps * h.attn_chunks;
   const bool f16 = h.kv_dtype == HV_KV_F16;
-  const int variant = h.w4_layout == HV_W4_DQ ? (f16 ? 4 : 3) : f16 ? 2 : split_merge ? 1 : 0;
+  const int variant = h.w4_layout == HV_W4_DQ ? (f16 ? 4 : 3) : f16 ? 2 : 0;
+  HV_REQUIRE(h.cap <= kExactMaxCap, HV_E_UNSUPPORTED, "hv_step_launch: cap %d > %d", h.cap,
+             kExactMaxCap);
+  HV_REQUIRE(h.n_kv * kSlices <= sms, HV_E_UNSUPPORTED,
+             "hv_step_launch: %d kv heads need %d CTAs for the attention context", h.n_kv,
+             h.n_kv * kSlices);
+  HV_REQUIRE(h.kv_base != nullptr && h.kv_rows >= (long long)2 * h.n_kv * h.cap &&
+                 ((uintptr_t)h.kv_base & 15) == 0,
+             HV_E_INVALID, "hv_step_launch: kv_base/kv_rows do not describe the KV cache");
+  CUtensorMap vmap;
+  rc = vslice_map(h.kv_base, h.kv_rows, f16 ? 2 : 4, &vmap);
+  if (rc) return rc;
   void* fn = step_fn(gs, variant);
   {
     // set the function's shared-memory limit once per (kernel, device, size)
@@ -1713,9 +1767,9 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
              "hv_step_launch: unknown flags 0x%x", flags);
   if (g_opt_local_qkv_barrier && world > 1) flags |= kFlagLocalQkvBarrier;
 
-  int inflight = g_opt_inflight, evict_first = g_opt_evict_first;
+  int inflight = g_opt_inflight, evict_first = g_opt_evict_first, runs = ref_blas_runs();
   void* args[] = {(void*)&h, (void*)&flags, (void*)&nslots, (void*)&inflight,
-                  (void*)&evict_first};
+                  (void*)&evict_first, (void*)&runs, (void*)&vmap};
   HV_CUDA(cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kStepThreads), args, smem,
                                       (cudaStream_t)stream));
   return HV_OK;

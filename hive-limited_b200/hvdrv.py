@@ -425,7 +425,7 @@ def ipc_close(ptr):
 STEP_OPT_INFLIGHT = 1
 STEP_OPT_EVICT_FIRST = 2
 STEP_OPT_LOCAL_QKV_BARRIER = 3
-STEP_OPT_SPLIT_MERGE = 4
+STEP_OPT_REF_BLAS_RUNS = 5
 
 
 def step_set_option(option, value):

@@ -48,7 +48,8 @@ class _StepDesc(C.Structure):
                     "part", "ticket", "amax_v", "amax_i", "barrier", "status", "trace",
                     "plans")]
                 + [("world", C.c_int), ("rank", C.c_int), ("peers", C.c_void_p),
-                   ("kv_dtype", C.c_int), ("w4_layout", C.c_int)])
+                   ("kv_dtype", C.c_int), ("w4_layout", C.c_int),
+                   ("kv_base", C.c_void_p), ("kv_rows", C.c_longlong)])
 
 
 MAX_WORLD = 8
@@ -483,7 +484,8 @@ class Engine:
             self.d_ctx, self.d_act, self.d_logits, self.d_part, self.d_ticket,
             self.d_amax_v, self.d_amax_i, self.d_barrier, self.d_status, None, self.d_plans,
             self.world, self.rank, self.d_peers, 1 if self.kv_f16 else 0,
-            1 if self.gemv_layout == "dq" else 0)
+            1 if self.gemv_layout == "dq" else 0,
+            self.d_kv, 2 * c.n_layer * sh["n_kv"] * c.max_context)
 
     def _connect_peers(self):
         """Swap CUDA IPC handles of the buffers every rank's step writes into (residual,
@@ -577,8 +579,8 @@ class Engine:
                     "down_prologue", "down_gemv", "barrier5")
     TRACE_WAITS = ("wait_attn_scores", "wait_attn_values", "wait_qkv_gemv", "wait_gu_gemv",
                    "attn_scores_busy_kcycles")
-    TRACE_ATTN = ("attn_heads", "attn_scores", "attn_softmax", "attn_values", "attn_ticket",
-                  "attn_merge")
+    TRACE_ATTN = ("attn_heads", "attn_scores", "attn_scores_out", "attn_ctx_wait",
+                  "attn_ctx_sum", "attn_ctx_chain")
 
     def profile_step(self, flags: int = STEP_HEAD | STEP_ARGMAX) -> dict:
         """Run one fused step at the current tok/pos with the per-phase trace on.
@@ -616,9 +618,9 @@ class Engine:
             out[name] = {"median_us": float(np.median(d, axis=0).sum() / 1e3),
                          "max_us": float(d.max(axis=0).sum() / 1e3)}
         # inside the attention, CTAs that had a work item (the marks stay 0 otherwise)
-        busy = raw[:, 2 + 14] != 0
         prev = 2
         for k, name in zip(range(14, 20), self.TRACE_ATTN):
+            busy = raw[:, 2 + k] != 0       # phase B marks: only the CTAs of a ctx item
             idx = np.array([2 + 28 * l + k for l in range(c.n_layer)])
             d = (t[:, idx] - t[:, idx - k + prev])[busy]
             prev = k

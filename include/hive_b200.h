@@ -153,10 +153,10 @@ int hv_a4gemm_pp(const int8_t* a8, const float* sa, const uint32_t* pb4, const f
  *                   [ntok][(nq + 2 nkv) hd]; q heads to q_out [ntok][nq][hd], k and v
  *                   rows appended at pos0 + t of the f32 cache [nkv][cap][hd]
  *                                                     (rmsnorm_bp, rope_pos, kvapp_pos)
- *   hv_attn_rows    attention of query row t over positions 0 .. pos0 + t, with the
- *                   chunking and merge of hv_attn_decode at that position; part/ticket
- *                   are caller scratch of hv_attn_rows_scratch's sizes (tickets zeroed
- *                   once; every call leaves them zero)                (fda_warp_pos)
+ *   hv_attn_rows    attention of query row t over positions 0 .. pos0 + t, the
+ *                   arithmetic of hv_attn_decode at that position; part is caller
+ *                   scratch of hv_attn_rows_scratch's part_bytes (ticket is not used
+ *                   and may be any pointer)                             (fda_warp_pos)
  *   hv_silu_rows    act[t] = silu(gate[t]) * up[t] from [gate | up] rows (gpu_silu_mul) */
 int hv_gather_rows(const uint16_t* emb16, const int32_t* tok, float* h, int hid, int ntok,
                    void* stream);
@@ -213,9 +213,14 @@ int hv_kv_append(const float* k, const float* v, float* kc, float* vc, const int
 
 /* fda_warp_pos (k_devgen.ptx; engine/limited.py:401-404): causal decode attention of
  * nq query heads over cache positions 0..*pos, kv head = h / group, logits scaled by
- * *scale. Split-sequence: the library keeps a per-device scratch buffer for the partial
- * softmax state (allocated on first use; grow it with hv_attn_reserve before a stream
- * capture). hd must be 128. */
+ * *scale, in engine/reference.py:104-118's own order of operations, so ctx is bit for bit
+ * the reference's: row dots in OpenBLAS's order (HV_STEP_OPT_REF_BLAS_RUNS), numpy's
+ * exp, numpy's pairwise sum, one division per weight, and the weighted V rows summed
+ * position by position. Two launches (scores per (kv head, chunk), then the context per
+ * (kv head, 32-dim slice)); the library keeps a per-device scratch buffer for the scores
+ * (allocated on first use; grow it with hv_attn_reserve before a stream capture). hd must
+ * be 128, the cache at most 16384 positions. A *pos outside [0, cap) reads no cache row
+ * and leaves NaN in ctx. */
 int hv_attn_decode(const float* q, const float* kc, const float* vc, float* ctx,
                    const float* scale, const int32_t* pos, int nq, int hd, int group,
                    int kvstride, void* stream);
@@ -238,11 +243,11 @@ int hv_attn_reserve(int nkv, int group, int cap);
  * library allocate (a process that gives all of HBM to its own pool, or a loop that
  * cannot take the device-wide synchronisation of cudaMalloc/cudaFree): same arguments
  * and results, but its scratch is a fixed 2 MiB static device array, so it calls no
- * cudaMalloc or cudaFree. Limits: at most 64 kv heads and nkv x chunks x group x 528
- * bytes of partial state (chunks = max(ceil(SMs / nkv), ceil(cap / 1024))) within
- * 2 MiB - 256 B; larger problems return HV_E_INVALID. The first call on a device does
- * a one-time set-up (symbol address, kernel attributes): make it before any stream
- * capture. All calls on a device share the array; calls that overlap on the GPU race. */
+ * cudaMalloc or cudaFree. Limit: nq x (cap + chunks) x 4 bytes of scores within 2 MiB
+ * (chunks = max(ceil(SMs / nkv), ceil(cap / 1024))); larger problems return
+ * HV_E_INVALID. The first call on a device does a one-time set-up (the array's symbol
+ * address): make it before any stream capture. All calls on a device share the array;
+ * calls that overlap on the GPU race. */
 int hv_attn_decode_noalloc(const float* q, const float* kc, const float* vc, float* ctx,
                            const float* scale, const int32_t* pos, int nq, int hd, int group,
                            int kvstride, void* stream);
@@ -343,8 +348,10 @@ typedef struct hv_step_desc {
   float* act;                   /* room for [ffn] floats (whole); holds the SiLU output
                                    quantised the same way                           */
   float* logits;                /* [head_rows]                                     */
-  float* part;                  /* attention partials (hv_step_config)             */
-  int32_t* ticket;              /* [n_kv + 1] zeroed once                          */
+  float* part;                  /* attention scratch (hv_step_config): scores
+                                   [n_head][cap], then chunk maxima [n_head][chunks] */
+  int32_t* ticket;              /* [n_kv + 1] zeroed once; every launch leaves them
+                                   zero (after a failed launch the caller re-zeroes) */
   float* amax_v; int32_t* amax_i;                  /* [grid] argmax partials       */
   uint32_t* barrier;            /* four words, zeroed once                         */
   int32_t* status;              /* 0 = ok; nonzero after a bounded wait ran out    */
@@ -368,6 +375,11 @@ typedef struct hv_step_desc {
   /* Arrangement of every prepacked weight tile: HV_W4_PP (0, hv_w4_prepack, block dots
    * on the tensor pipe) or HV_W4_DQ (hv_w4_prepack_dq, dp4a block dots; same results). */
   int w4_layout;
+  /* The KV cache seen as one array of rows of head_dim elements (of kv_dtype): every
+   * layer's kc and vc lie within kv_rows rows from kv_base (16-byte aligned). The step
+   * copies 32-dim slices of V rows out of it with the tensor-copy engine. */
+  const void* kv_base;
+  long long kv_rows;
 } hv_step_desc;
 
 #define HV_KV_F32 0
@@ -429,10 +441,12 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream);
 #define HV_STEP_OPT_INFLIGHT 1
 #define HV_STEP_OPT_EVICT_FIRST 2
 #define HV_STEP_OPT_LOCAL_QKV_BARRIER 3
-/* HV_STEP_OPT_SPLIT_MERGE: on one GPU with the f32 cache, merge the attention partials as
- * a phase of their own, one warp per 32-value block of ctx, after a grid barrier (0/1,
- * default 0; steps over a binary16 cache ignore it). */
-#define HV_STEP_OPT_SPLIT_MERGE 4
+/* HV_STEP_OPT_REF_BLAS_RUNS: the OpenBLAS thread count of the host whose reference results
+ * the attention reproduces bit for bit (default 8). The reference's `keys @ q` splits a
+ * gemv of T rows into that many runs when 128 T >= 460800, and the row dot of each run's
+ * last rows takes another order; every attention entry point (decode, rows, no-alloc and
+ * the fused step) follows the same setting. Process-wide. */
+#define HV_STEP_OPT_REF_BLAS_RUNS 5
 int hv_step_set_option(int option, int value);
 
 #ifdef __cplusplus

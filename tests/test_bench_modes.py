@@ -88,27 +88,27 @@ class FakeEngine:
         pass
 
     def download_logits(self):
-        # identical logits unless the split merge is on (to see the check work)
-        return np.full(16, 2.0 if self.drv.options.get(4) else 1.0, np.float32)
+        # identical logits unless inflight is 3 (to see the check work)
+        return np.full(16, 2.0 if self.drv.options.get(1) == 3 else 1.0, np.float32)
 
 
 def test_ab_loop_times_every_set_and_restores_options(monkeypatch):
     drv = FakeDriver()
     pin = (np.ctypeslib.ctypes.c_int32 * 4)()
     addr = np.ctypeslib.ctypes.addressof(pin)
-    ns = types.SimpleNamespace(ab=["split_merge=1", "local_qkv_barrier=1,inflight=8"],
+    ns = types.SimpleNamespace(ab=["inflight=3", "local_qkv_barrier=1,inflight=8"],
                                ab_rounds=2, steps=5, step_opt=["evict_first=0"])
     done = [0]
     calls = []
     out = bench.run_ab(ns, FakeDist(), FakeEngine(drv), lambda k: calls.append(k), addr, 4096,
                        256, done, drv)
-    assert [o["options"] for o in out] == ["baseline", {"split_merge": 1},
+    assert [o["options"] for o in out] == ["baseline", {"inflight": 3},
                                            {"local_qkv_barrier": 1, "inflight": 8}]
     assert all(o["ms_per_step"] == pytest.approx(0.2) and len(o["runs_ms"]) == 2 for o in out)
     assert [o["logits_identical"] for o in out] == [True, False, True]
     assert calls.count(5) == 2 * 3                     # every set timed in every round
     # the options end as --step-opt left them: defaults plus evict_first=0
-    assert drv.options == {1: 6, 2: 0, 3: 0, 4: 0}
+    assert drv.options == {1: 6, 2: 0, 3: 0}
 
 
 def test_ab_layout_set_runs_on_a_second_engine(monkeypatch):

@@ -59,7 +59,7 @@ def test_library_version_and_kernels(lib):
     hvdrv.load()
     assert hvdrv.load().hv_version() == hvdrv.ABI_VERSION
     ks = hvdrv.kernel_list()
-    for k in ("k_a4gv", "k_qa8s", "k_rmsnorm", "k_attn", "k_step", "k_argmax_p"):
+    for k in ("k_a4gv", "k_qa8s", "k_rmsnorm", "k_attn_sc", "k_attn_cx", "k_step", "k_argmax_p"):
         assert k in ks
 
 
@@ -93,13 +93,15 @@ def test_step_desc_layout_matches_header(tmp_path):
     import limited
     assert ctypes.sizeof(limited._LayerW) == 14 * 8
     # 8 ints + 2 floats + 2 ints = 48 bytes, then 24 pointers, world, rank, peers, kv_dtype,
-    # w4_layout
+    # w4_layout, kv_base, kv_rows
     assert limited._StepDesc.layers.offset == 48
     assert limited._StepDesc.world.offset == 48 + 24 * 8
     assert limited._StepDesc.peers.offset == 48 + 24 * 8 + 8
     assert limited._StepDesc.kv_dtype.offset == 48 + 24 * 8 + 16
     assert limited._StepDesc.w4_layout.offset == 48 + 24 * 8 + 20
-    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 24
+    assert limited._StepDesc.kv_base.offset == 48 + 24 * 8 + 24
+    assert limited._StepDesc.kv_rows.offset == 48 + 24 * 8 + 32
+    assert ctypes.sizeof(limited._StepDesc) == 48 + 24 * 8 + 40
     assert ctypes.sizeof(limited._StepPeers) == 5 * 8 * 8
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:

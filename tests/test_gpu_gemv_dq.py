@@ -5,17 +5,13 @@ vocabulary-sized shapes of the GEMV sweep; the dq arrays are a rearrangement of 
 tile-interleaved ones (the lane-level CPU model checks the arithmetic,
 tests/test_gemv_dq_model.py). An engine with dq tiles (fused step and eager sequence)
 gives the pp engine's logits bit for bit."""
-import os
-
 import numpy as np
 import pytest
 
 import hv_oracle as O
 from gpu_util import Dev, bits, quantize_on_device
 
-pytestmark = [pytest.mark.gpu, pytest.mark.skipif(
-    not os.environ.get("HV_NEW_GPU_TESTS"),
-    reason="kernels not yet run on a B200: set HV_NEW_GPU_TESTS=1")]
+pytestmark = pytest.mark.gpu
 F32 = np.float32
 
 

@@ -88,8 +88,6 @@ def test_two_gpu_sharded_step_matches_one_gpu(hv):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(not os.environ.get("HV_NEW_GPU_TESTS"),
-                    reason="kernels not yet run on a B200: set HV_NEW_GPU_TESTS=1")
 @pytest.mark.parametrize("kw", [{"kv_dtype": "f16"}, {"gemv_layout": "dq"},
                                 {"kv_dtype": "f16", "gemv_layout": "dq"}])
 def test_two_gpu_sharded_variants_match_one_gpu(hv, kw):

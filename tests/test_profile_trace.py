@@ -36,8 +36,11 @@ def synthetic_trace():
             mark(0, 40)                          # quantised: qkv prologue ends
             mark(1, 100 + l)                     # qkv GEMV
             mark(2, 10)                          # barrier 1
-            for k, dur in zip(range(14, 20), (5, 15, 7, 9, 3, 50 if b == 0 else 1)):
-                mark(k, dur)                     # attention's own parts
+            for k, dur in zip(range(14, 17), (5, 15, 7)):
+                mark(k, dur)                     # attention scores (every CTA has a chunk)
+            if b != 1:                           # the context items: CTAs 0 and 2 only
+                for k, dur in zip(range(17, 20), (9, 3, 50 if b == 0 else 1)):
+                    mark(k, dur)
             mark(3, 2)
             for k in range(4, 14):
                 mark(k, 10 * k + b)
@@ -88,12 +91,14 @@ def test_profile_step_phases(monkeypatch):
     assert ph["qkv_prologue"]["max_us"] == pytest.approx(us([[90 + b for b in ctas]] * NL, np.max))
     assert ph["qkv_gemv"]["median_us"] == pytest.approx((100 + 101) / 1e3)
     assert ph["barrier1"]["max_us"] == pytest.approx(2 * 10 / 1e3)
-    # attention = its parts + 2 ns; CTA 0 merges (50 ns), the others tick (1 ns)
-    att = [[5 + 15 + 7 + 9 + 3 + (50 if b == 0 else 1) + 2 for b in ctas]] * NL
+    # attention = its parts + 2 ns; the context chain takes 50 ns on CTA 0, 1 ns on CTA 2,
+    # CTA 1 has no context item
+    att = [[5 + 15 + 7 + (0 if b == 1 else 9 + 3 + (50 if b == 0 else 1)) + 2 for b in ctas]] * NL
     assert ph["attention"]["median_us"] == pytest.approx(us(att, np.median))
     assert ph["attention"]["max_us"] == pytest.approx(us(att, np.max))
-    assert ph["attn_merge"]["max_us"] == pytest.approx(2 * 50 / 1e3)
-    assert ph["attn_merge"]["median_us"] == pytest.approx(2 * 1 / 1e3)
+    assert ph["attn_ctx_chain"]["max_us"] == pytest.approx(2 * 50 / 1e3)
+    assert ph["attn_ctx_chain"]["median_us"] == pytest.approx(2 * 25.5 / 1e3)
+    assert ph["attn_scores"]["median_us"] == pytest.approx(2 * 15 / 1e3)
     assert ph["down_gemv"]["median_us"] == pytest.approx(2 * (120 + 1) / 1e3)
     assert ph["barrier5"]["max_us"] == pytest.approx(2 * (130 + 2) / 1e3)
     assert ph["qkv_pro_load"]["median_us"] == pytest.approx(2 * 31 / 1e3)
