@@ -544,6 +544,9 @@ def run_gemv_sweep(args, dist: Dist):
     cases = [(j, n, k) for j, (n, k) in enumerate(synth.GEMV_SHAPES)] + [(None, *synth.HEAD_SHAPE)]
     if args.gemv_max_rows:
         cases = [c for c in cases if c[1] <= args.gemv_max_rows]
+    if getattr(args, "gemv_shape", None):
+        want = {tuple(int(x) for x in sh.lower().split("x")) for sh in args.gemv_shape}
+        cases = [c for c in cases if (c[1], c[2]) in want]
     for j, n, k in cases:
         if j is None:
             w, h = synth.head_case(1)
@@ -852,6 +855,8 @@ def main(argv=None):
     ap.add_argument("--gemv-max-rows", type=int, default=0,
                     help="sweep only the shapes with at most this many rows (0: all)")
     ap.add_argument("--gemv-rotate-mb", type=int, default=320)
+    ap.add_argument("--gemv-shape", action="append", default=[], metavar="NxK",
+                    help="sweep only these shapes (repeatable), e.g. 151936x4096")
     args = ap.parse_args(argv)
     for opt in args.step_opt:
         if opt.partition("=")[0] not in STEP_OPTS or not opt.partition("=")[2].isdigit():

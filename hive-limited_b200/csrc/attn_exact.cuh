@@ -67,6 +67,63 @@ HV_HD int blas_row_kind(int T, int t, int runs) {
   return 0;
 }
 
+// The same split, worked out once for a gemv of T rows: the rows whose dots are not of
+// kind 0 are the last 1-3 of each run; at most kMaxRuns runs.
+constexpr int kMaxRuns = 32;
+struct BlasRuns {
+  int n;                       // runs
+  int odd0[kMaxRuns];          // first row of the run's leftover (not kind 0)
+  int end[kMaxRuns];           // one past the run's last row
+  int k1end[kMaxRuns];         // rows [odd0, k1end) are kind 1, [k1end, end) kind 2
+};
+
+HV_HD void blas_runs(int T, int runs, BlasRuns* b) {
+  int nrun = (128L * T >= 460800L && runs > 1) ? runs : 1;
+  if (nrun > kMaxRuns) nrun = kMaxRuns;
+  int r0 = 0, left = T, n = 0;
+  for (int k = 0; k < nrun && left > 0; ++k) {
+    int w = (left + (nrun - k) - 1) / (nrun - k);
+    if (w < 4) w = 4;
+    if (w > left) w = left;
+    const int full = w & ~3;
+    b->odd0[n] = r0 + full;
+    b->end[n] = r0 + w;
+    b->k1end[n] = r0 + full + ((w & 2) ? 2 : 0);
+    ++n;
+    r0 += w;
+    left -= w;
+  }
+  b->n = n;
+}
+
+HV_HD int blas_kind_of(const BlasRuns& b, int t) {
+  for (int k = 0; k < b.n; ++k)
+    if (t < b.end[k]) return t < b.odd0[k] ? 0 : (t < b.k1end[k] ? 1 : 2);
+  return 0;
+}
+
+// The row kinds of a block of rows starting at r0, looked up once per block: the run
+// holding r0 and the next one (a block of up to 20 rows never spans more than two runs:
+// when there are several runs each holds at least 112 rows).
+struct RunWin {
+  int enda, odd0a, k1a, odd0b, k1b;
+};
+HV_DEV RunWin run_window(const BlasRuns& b, int r0) {
+  int k = 0;
+  while (k + 1 < b.n && r0 >= b.end[k]) ++k;
+  RunWin w;
+  w.enda = b.end[k];
+  w.odd0a = b.odd0[k];
+  w.k1a = b.k1end[k];
+  w.odd0b = k + 1 < b.n ? b.odd0[k + 1] : 0x7FFFFFFF;
+  w.k1b = k + 1 < b.n ? b.k1end[k + 1] : 0x7FFFFFFF;
+  return w;
+}
+HV_DEV int kind_in(const RunWin& w, int t) {
+  if (t < w.enda) return t < w.odd0a ? 0 : (t < w.k1a ? 1 : 2);
+  return t < w.odd0b ? 0 : (t < w.k1b ? 1 : 2);
+}
+
 // Query elements an 8-lane group's lane j keeps for kind-0/2 dots: q[h][j + 8 i].
 template <int HP>
 HV_DEV void load_qregs(const float* q_s, int j, float (&qr)[HP][16]) {
@@ -87,12 +144,13 @@ HV_DEV void rowdots_blas(const Row& row, int kind, const float (&qr)[HP][16],
 #pragma unroll
   for (int h = 0; h < HP; ++h) d[h] = 0.0f;
   if (kind == 0) {
+    float k[16];                                   // every load before the first FMA
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float k = row(j + 8 * i);
+    for (int i = 0; i < 16; ++i) k[i] = row(j + 8 * i);
 #pragma unroll
-      for (int h = 0; h < HP; ++h) d[h] = __fmaf_rn(k, qr[h][i], d[h]);
-    }
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int h = 0; h < HP; ++h) d[h] = __fmaf_rn(k[i], qr[h][i], d[h]);
   } else if (kind == 2) {
 #pragma unroll 4
     for (int i = 0; i < 16; ++i) {
@@ -199,27 +257,189 @@ HV_DEV bool pw_tree_build_warp(int n, PwTree* t) {
   return true;
 }
 
-// Sum of leaf [s, s + len) of x_t = f(t) by the 8 lanes of an aligned group (sub =
-// lane & 7), numpy's leaf order: < 8 values sequentially from +0; else eight strided
-// accumulators, ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the len % 8 tail in order.
-// Every lane of the group returns it.
-template <class F>
-HV_DEV float pw_leaf_f(const F& f, int s, int len, int sub) {
+// ---------------------------------------------------------------------------
+// The top of numpy's recursion over T values, cut at depth `depth`: the nodes at that
+// depth (or leaves, <= 128 values, above it) in left-to-right order are the chunks of the
+// fused step's attention, so each chunk's pairwise sum is an exact subtree of the whole
+// sum and only the nodes above the chunks remain to be added. pops[c]: how many '+' of
+// the recursion close right after chunk c (postfix order).
+// ---------------------------------------------------------------------------
+constexpr int kMaxFront = 128;
+
+struct PwFront {
+  int n;                                   // chunks
+  int cb[kMaxFront + 1];                   // chunk c = values [cb[c], cb[c + 1])
+  unsigned char pops[kMaxFront];
+};
+
+HV_HD bool pw_front_build(int T, int depth, PwFront* f) {
+  int ss[64], sm[64], sk[64], sd[64];      // DFS stack: start, count, kind (0 node, 1 '+')
+  int sp = 0, nc = 0;
+  ss[0] = 0; sm[0] = T; sk[0] = 0; sd[0] = 0; sp = 1;
+  while (sp > 0) {
+    --sp;
+    const int s = ss[sp], m = sm[sp], k = sk[sp], d = sd[sp];
+    if (k == 1) {
+      if (nc == 0) return false;
+      f->pops[nc - 1]++;
+    } else if (m <= kPwLeaf || d >= depth) {
+      if (nc >= kMaxFront) return false;
+      f->cb[nc] = s;
+      f->pops[nc] = 0;
+      ++nc;
+    } else {
+      if (sp + 3 > 64) return false;
+      int m2 = m / 2;
+      m2 -= m2 % 8;
+      ss[sp] = 0; sm[sp] = 0; sk[sp] = 1; sd[sp] = d; ++sp;
+      ss[sp] = s + m2; sm[sp] = m - m2; sk[sp] = 0; sd[sp] = d + 1; ++sp;
+      ss[sp] = s; sm[sp] = m2; sk[sp] = 0; sd[sp] = d + 1; ++sp;
+    }
+  }
+  f->cb[nc] = T;
+  f->n = nc;
+  return true;
+}
+
+// (+0) + the recursion's '+' over the chunks' sums val[0 .. n) (one thread).
+HV_DEV float pw_front_fold(const PwFront& f, const float* val) {
+  float st[24];
+  int sp = 0;
+  for (int c = 0; c < f.n; ++c) {
+    st[sp++] = val[c];
+    for (int k = 0; k < f.pops[c]; ++k) {
+      const float b = st[--sp];
+      const float a = st[--sp];
+      st[sp++] = __fadd_rn(a, b);
+    }
+  }
+  return __fadd_rn(0.0f, st[0]);
+}
+
+// Largest chunk of the recursion cut at a depth with nch = 2^depth chunks: a split leaves
+// at most half + 8 values on either side, so after d splits a node holds fewer than
+// T / 2^d + 16; leaves above the cut hold at most 128.
+HV_HD int front_chunk_max(int cap, int nch) {
+  const int a = (cap + nch - 1) / nch + 16;
+  return a > kPwLeaf ? a : kPwLeaf;
+}
+
+// Depth of the fused step's chunking for n_kv kv heads on `grid` CTAs: every (kv head,
+// chunk) work item gets a CTA of its own (n_kv 2^depth <= grid), at most kMaxFront chunks.
+HV_HD int front_depth(int n_kv, int grid) {
+  int d = 0;
+  while (d < 7 && (n_kv << (d + 1)) <= grid) ++d;
+  return d;
+}
+
+// One leaf [s, s + len) of a head's softmax sum: e_t = np_expf(lg[t] - M) for its
+// positions (stored into e[t] when e is set), summed by the 8 lanes of an aligned group
+// (sub = lane & 7) in numpy's leaf order: < 8 values sequentially from +0; else eight
+// strided accumulators, ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the len % 8 tail in
+// order. Every lane of the group returns the sum. All of a lane's scores are loaded
+// before the first exp, so a leaf costs one load latency.
+struct LeafRaw {
+  float x[16], tl[7];
+};
+
+// The scores of the lane's share of leaf [s, s + len) (loads only, all issued at once).
+HV_DEV void leaf_load(const float* lg, int s, int len, int sub, LeafRaw& L) {
+  const int full = len >= 8 ? len - (len % 8) : 0;
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int i = sub + 8 * m;
+    L.x[m] = i < full ? __ldcg(lg + s + i) : 0.0f;
+  }
+#pragma unroll
+  for (int m = 0; m < 7; ++m) L.tl[m] = full + m < len ? __ldcg(lg + s + full + m) : 0.0f;
+}
+
+// The exps and the leaf's sum from leaf_load's scores.
+HV_DEV float leaf_finish(LeafRaw& L, float M, float* e, int s, int len, int sub) {
   const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+  const int full = len >= 8 ? len - (len % 8) : 0;
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int i = sub + 8 * m;
+    if (i < full) {
+      L.x[m] = np_expf(__fsub_rn(L.x[m], M));
+      if (e) e[s + i] = L.x[m];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 7; ++m) {
+    if (full + m < len) {
+      L.tl[m] = np_expf(__fsub_rn(L.tl[m], M));
+      if (e && sub == 0) e[s + full + m] = L.tl[m];
+    }
+  }
   float r;
   if (len >= 8) {
-    const int full = len - (len % 8);
-    r = f(s + sub);
-    for (int i = 8 + sub; i < full; i += 8) r = __fadd_rn(r, f(s + i));
+    r = L.x[0];
+#pragma unroll
+    for (int m = 1; m < 16; ++m)
+      if (sub + 8 * m < full) r = __fadd_rn(r, L.x[m]);
     r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 1, 8));
     r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 2, 8));
     r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 4, 8));
-    for (int i = full; i < len; ++i) r = __fadd_rn(r, f(s + i));
   } else {
     r = 0.0f;
-    for (int i = 0; i < len; ++i) r = __fadd_rn(r, f(s + i));
   }
+#pragma unroll
+  for (int m = 0; m < 7; ++m)
+    if (full + m < len) r = __fadd_rn(r, L.tl[m]);
   return r;
+}
+
+HV_DEV float leaf_exp_sum(const float* lg, float M, float* e, int s, int len, int sub) {
+  LeafRaw L;
+  leaf_load(lg, s, len, sub, L);
+  return leaf_finish(L, M, e, s, len, sub);
+}
+
+// Sum of leaf [s, s + len) of values x[t * stride] (shared memory) by the 8 lanes of an
+// aligned group, numpy's leaf order (as leaf_finish); every lane of the group returns it.
+HV_DEV float leaf_sum_strided(const float* x, int stride, int s, int len, int sub) {
+  const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+  const int full = len >= 8 ? len - (len % 8) : 0;
+  float v[16], tl[7];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int i = sub + 8 * m;
+    v[m] = i < full ? x[(size_t)(s + i) * stride] : 0.0f;
+  }
+#pragma unroll
+  for (int m = 0; m < 7; ++m) tl[m] = full + m < len ? x[(size_t)(s + full + m) * stride] : 0.0f;
+  float r;
+  if (len >= 8) {
+    r = v[0];
+#pragma unroll
+    for (int m = 1; m < 16; ++m)
+      if (sub + 8 * m < full) r = __fadd_rn(r, v[m]);
+    r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 1, 8));
+    r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 2, 8));
+    r = __fadd_rn(r, __shfl_xor_sync(gmask, r, 4, 8));
+  } else {
+    r = 0.0f;
+  }
+#pragma unroll
+  for (int m = 0; m < 7; ++m)
+    if (full + m < len) r = __fadd_rn(r, tl[m]);
+  return r;
+}
+
+// pw_tree_fold without the final (+0) +: the value of the tree's root (a subtree of a
+// larger sum).
+HV_DEV float pw_tree_fold_raw(const PwTree* t, float* vals) {
+  const int lane = threadIdx.x & 31;
+  for (int d = t->nlev - 1; d >= 0; --d) {
+    for (int i = t->lev[d] + lane; i < t->lev[d + 1]; i += 32) {
+      const int c = t->child[i];
+      if (c >= 0) vals[i] = __fadd_rn(vals[c], vals[c + 1]);
+    }
+    __syncwarp();
+  }
+  return vals[0];
 }
 
 // One warp: the internal nodes of `t` from the deepest level up, over vals[] (leaf sums
@@ -305,6 +525,9 @@ k_attn_sc(const float* __restrict__ q, size_t q_tok, const KT* __restrict__ kc,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, r = lane >> 3;
   const float scale = *scale_p;
   const KT* kh = kc + (size_t)g * cap * kHd;
+  __shared__ BlasRuns br;
+  if (threadIdx.x == 0) blas_runs(T, runs, &br);
+  __syncthreads();
   constexpr int HP = GS < 4 ? GS : 4;
 #pragma unroll 1
   for (int p0 = 0; p0 < GS; p0 += HP) {
@@ -313,7 +536,7 @@ k_attn_sc(const float* __restrict__ q, size_t q_tok, const KT* __restrict__ kc,
     for (int tb = t0 + 4 * warp; tb < t1; tb += 4 * (kAttnExThreads / 32)) {
       const int t = tb + r;
       const bool ok = t < t1;
-      const int kind = ok ? blas_row_kind(T, t, runs) : 0;
+      const int kind = ok ? blas_kind_of(br, t) : 0;
       float d[HP];
       rowdots_blas<HP>(GlobalRow<KT>{kh + (size_t)(ok ? t : t0) * kHd}, kind, qr, q_s + p0 * kHd,
                        j, d);
@@ -394,13 +617,12 @@ k_attn_cx(const KT* __restrict__ vc, float* __restrict__ ctx, size_t ctx_tok,
     const int gi = (warp / GS) * 4 + (lane >> 3), ng = (kAttnExThreads / 32 / GS) * 4;
     const float* lgh = lg + (size_t)(g * GS + i) * cap;
     const float M = ms[2 * i];
-    const auto e = [lgh, M](int t) { return np_expf(__fsub_rn(__ldcg(lgh + t), M)); };
     for (int l0 = 0; l0 < tree.nleaf; l0 += ng) {
       const int l = l0 + gi;
       const bool live = l < tree.nleaf;
       const int id = live ? (int)tree.leaf[l] : 0;
-      const float v = pw_leaf_f(e, live ? (int)tree.start[id] : 0, live ? (int)tree.size[id] : 1,
-                                lane & 7);
+      const float v = leaf_exp_sum(lgh, M, nullptr, live ? (int)tree.start[id] : 0,
+                                   live ? (int)tree.size[id] : 1, lane & 7);
       if (live && (lane & 7) == 0) vals[(size_t)i * kTreeMaxNode + id] = v;
     }
   }

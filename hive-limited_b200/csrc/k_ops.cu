@@ -566,7 +566,8 @@ __global__ void k_quantize_w4(const float* __restrict__ w, uint32_t* __restrict_
 static int g_ref_runs = kRefRuns;
 int ref_blas_runs() { return g_ref_runs; }
 int set_ref_blas_runs(int v) {
-  HV_REQUIRE(v >= 1 && v <= 1024, HV_E_INVALID, "reference BLAS runs %d outside [1, 1024]", v);
+  HV_REQUIRE(v >= 1 && v <= kMaxRuns, HV_E_INVALID, "reference BLAS runs %d outside [1, %d]",
+             v, kMaxRuns);
   g_ref_runs = v;
   return HV_OK;
 }

@@ -93,11 +93,15 @@ struct StepShared {
   int ok;
   int abort;                     // set by any warp of this CTA whose wait gave up
   int tree_ok;                   // the pairwise tree of the softmax sum was built
+  BlasRuns runs;                 // the reference host's gemv runs over pos + 1 rows
+  PwFront front;                 // the attention chunks: numpy's recursion cut at a depth
   unsigned phase;                // top bit of the grid barrier counter to wait for next
   unsigned xphase;               // sharded: top bit of the cross-rank counter (CTA 0)
   unsigned gen;                  // sharded: generation of the local release word
   unsigned long long wait[kConsWarps];   // ns each consumer warp waited for ring slots
   long long busy[kConsWarps];            // cycles spent computing attention scores
+  unsigned long long ctx_wait_ns;        // phase B, whole launch: ns warp 0 waited for V slots
+  unsigned long long ctx_sum_ns;         // phase B, whole launch: ns of the exps + leaf sums
 };
 
 // Byte offsets of the dynamic shared memory regions (host and device agree).
@@ -109,13 +113,14 @@ HV_HD size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Floats of the attention work area: phase A (q rows, this step's k and v rows, the
 // norm scratch, the chunk's scores) or phase B (node values of the pairwise tree per
-// head, two blocks of weights per head, the per-head maxima), whichever is larger.
+// head, a 4-block ring of weights per head, the per-head maxima and sums), whichever is
+// larger.
 HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
-  const size_t chunk_max = ((size_t)cap + nch - 1) / nch;
-  const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd +
-                   (((size_t)chunk_max * gs + 3) & ~size_t(3));
-  const size_t nvl = ((size_t)pw_tree_nodes_max(cap) + 3) & ~size_t(3);
-  const size_t b = (size_t)gs * nvl + (size_t)gs * 2 * (kSlotBytes / (32 * 2)) + 8;
+  const size_t cm = (size_t)front_chunk_max(cap, nch);
+  const size_t nvl = ((size_t)pw_tree_nodes_max((int)cm) + 3) & ~size_t(3);
+  const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 8 +
+                   ((cm * gs + 3) & ~size_t(3)) + (size_t)gs * nvl;
+  const size_t b = (((size_t)gs * nch + 3) & ~size_t(3)) + 8 + (size_t)gs * 2 * 128;
   return a > b ? a : b;
 }
 
@@ -386,14 +391,68 @@ HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
   }
 }
 
-// Rows of a phase-B V slot: 32-dim slices of BR consecutive positions.
-template <class KT>
-constexpr int kVRows = kSlotBytes / (32 * (int)sizeof(KT));
-
 // The phase-B item of CTA b (kv head * 4 + slice), or -1: items spread over the grid.
 HV_DEV int ctx_item(int b, int grid, int nitems) {
   const int k = (int)(((long long)b * nitems + grid - 1) / grid);
   return (k < nitems && (int)(((long long)k * grid) / nitems) == b) ? k : -1;
+}
+
+// Rows of a phase-B slot: the V slice of BR positions (32 dims of KT) plus the GS heads'
+// exps of the same positions fill at most one slot; BR is a multiple of 32.
+template <class KT, int GS>
+constexpr int vrows_fit() {
+  int br = 32;
+  while ((br + 32) * (32 * (int)sizeof(KT) + 4 * GS) <= kSlotBytes) br += 32;
+  return br;
+}
+template <class KT, int GS>
+constexpr int kVRowsG = vrows_fit<KT, GS>();
+
+// Rows [t0, t1) of chunk c of the launch's frontier (empty past its last chunk), and te:
+// rows [t0, te) come from the cache, row pos (if in the chunk) from this step's qkv.
+HV_DEV void front_rows(const PwFront& F, int pos, int c, int* t0, int* t1, int* te) {
+  if (c < F.n) {
+    *t0 = F.cb[c];
+    *t1 = F.cb[c + 1];
+  } else {
+    *t0 = *t1 = pos + 1;
+  }
+  *te = max(*t0, min(*t1, pos));
+}
+
+// The attention scratch of the fused step (hv_step_desc.part): per query head the
+// chunks' maxima and pairwise sums [n_head][chunks], then the exps [n_head][ew] (ew = cap
+// rounded up to 4, rows 16-byte aligned) and room for one block past the last row.
+struct StepScratch {
+  float* cmax;
+  float* nsum;
+  float* exps;
+  int ew;
+};
+HV_HD size_t step_part_floats(int nq, int cap, int nch) {
+  const size_t a = ((size_t)nq * nch + 3) & ~size_t(3);
+  return 2 * a + (size_t)nq * (((size_t)cap + 3) & ~size_t(3)) + 256;
+}
+HV_DEV StepScratch step_scratch(const hv_step_desc& D) {
+  const size_t a = ((size_t)D.n_head * D.attn_chunks + 3) & ~size_t(3);
+  return StepScratch{D.part, D.part + a, D.part + 2 * a, (D.cap + 3) & ~3};
+}
+
+// One thread: bounded wait until *w >= want (acquire); false (and HV_E_TIMEOUT, unless a
+// failure is already recorded) when it gives up.
+HV_DEV bool wait_count(const int32_t* w, unsigned want, int* status) {
+  const unsigned* p = reinterpret_cast<const unsigned*>(w);
+  if (ld_acquire(p) >= want) return true;
+  const unsigned long long t0 = global_ns();
+  while (ld_acquire(p) < want) {
+    if (*(volatile int*)status != 0) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      atomicCAS(status, 0, HV_E_TIMEOUT);
+      return false;
+    }
+    __nanosleep(100);
+  }
+  return true;
 }
 
 // ---- the producer ----------------------------------------------------------------------
@@ -494,26 +553,68 @@ struct Producer {
     }
   }
 
-  // The 32-dim slice x0 .. x0 + 31 of V rows [0, nrows) starting at row y0 of the cache's
-  // 2-D view `vmap`, kVRows rows per slot (tensor copies; rows past the view read zeros).
-  template <class KT>
-  HV_DEV void vslices(const CUtensorMap* vmap, int x0, int y0, int nrows) {
-    constexpr int BR = kVRows<KT>;
-    for (int r = 0; r < nrows && live; r += BR) {
+  // The slot's V part: the 32-dim slice x0 .. x0 + 31 of BR rows from row y0 of the
+  // cache's 2-D view `vmap` (a tensor copy; rows past the view read zeros). Completes on
+  // the slot's full barrier, which expects `total` bytes (the exps come later).
+  HV_DEV void vpart(const CUtensorMap* vmap, int x0, int y0, unsigned total) {
+    unsigned char* dst = R.slot(q);
+    uint64_t* full = R.full_of(q);
+    mbar_arrive_tx(full, total);
+    if (hint)
+      asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+                   " [%0], [%1, {%2, %3}], [%4], %5;"
+                   :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0), "r"(sm_addr(full)),
+                      "l"(policy) : "memory");
+    else
+      asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                   " [%0], [%1, {%2, %3}], [%4];"
+                   :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0), "r"(sm_addr(full))
+                   : "memory");
+  }
+
+  // The slot of sequence number qs gets its exps part: GS rows of BR floats.
+  HV_DEV void epart(unsigned qs, const float* e0, int ew, int gs, int br, unsigned voff) {
+    unsigned char* dst = R.slot(qs) + voff;
+    uint64_t* full = R.full_of(qs);
+    for (int i = 0; i < gs; ++i) {
+      if (hint) bulk_load_hint(dst + i * br * 4, e0 + (size_t)i * ew, (unsigned)br * 4, full, policy);
+      else bulk_load(dst + i * br * 4, e0 + (size_t)i * ew, (unsigned)br * 4, full);
+    }
+  }
+
+  // Non-blocking claim: true if the next slot is free and the in-flight limit allows a
+  // copy now.
+  HV_DEV bool try_claim() {
+    if (!live) return false;
+    if (q >= (unsigned)R.ns && !mbar_probe(R.empty_of(q), R.parity(q) ^ 1u)) return false;
+    if (q >= inflight && !mbar_probe(R.full_of(q - inflight), R.parity(q - inflight)))
+      return false;
+    return true;
+  }
+
+  // The phase-B slots of kv head g, slice x0 / 32: V rows y0 + k BR ... and the GS heads'
+  // exps e0 + k BR ..., for blocks k < nblk. V parts of the first blocks go out while
+  // slots are free without waiting; the exps only once every chunk of the kv head has
+  // written them (the second ticket `tk` reaches `want`).
+  template <class KT, int GS>
+  HV_DEV void ctx_slots(const CUtensorMap* vmap, int x0, int y0, const float* e0, int ew,
+                        int nblk, const int32_t* tk, unsigned want) {
+    constexpr int BR = kVRowsG<KT, GS>;
+    constexpr unsigned kVB = BR * 32 * sizeof(KT), kTot = kVB + GS * BR * 4;
+    const unsigned qb = q;
+    int k = 0;
+    for (; k < nblk && try_claim(); ++k, ++q) vpart(vmap, x0, y0 + k * BR, kTot);
+    if (!live) return;
+    if (!wait_count(tk, want, status)) {
+      live = false;
+      return;
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");   // exps written by other SMs
+    for (int kk = 0; kk < k; ++kk) epart(qb + kk, e0 + (size_t)kk * BR, ew, GS, BR, kVB);
+    for (; k < nblk && live; ++k) {
       if (!claim()) return;
-      unsigned char* dst = R.slot(q);
-      uint64_t* full = R.full_of(q);
-      mbar_arrive_tx(full, (unsigned)kSlotBytes);
-      if (hint)
-        asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-                     " [%0], [%1, {%2, %3}], [%4], %5;"
-                     :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0 + r), "r"(sm_addr(full)),
-                        "l"(policy) : "memory");
-      else
-        asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                     " [%0], [%1, {%2, %3}], [%4];"
-                     :: "r"(sm_addr(dst)), "l"(vmap), "r"(x0), "r"(y0 + r), "r"(sm_addr(full))
-                     : "memory");
+      vpart(vmap, x0, y0 + k * BR, kTot);
+      epart(q, e0 + (size_t)k * BR, ew, GS, BR, kVB);
       ++q;
     }
   }
@@ -530,7 +631,7 @@ HV_DEV void producer_drain(const Ring& R, unsigned q, StepShared& S) {
     }
 }
 
-template <class KT>
+template <int GS, class KT>
 HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int pos,
                     const Ring& R, StepShared& S, int inflight, int evict_first,
                     const CUtensorMap* vmap) {
@@ -548,15 +649,20 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
     const hv_layer_w* L = Ls + l;
     phase_tiles(pp_tiles(nqkv, 0), &off, &t0, &t1);
     P.gemv(L->qkv_b4, L->qkv_sw, it_hid, t0, t1, S.P.gv_hid.nleaf);
-    for (int wi = blockIdx.x; wi < D.n_kv * nch; wi += gridDim.x) {
+    if ((int)blockIdx.x < D.n_kv * nch) {            // this CTA's chunk: K rows
       int a0, a1, ae;
-      attn_rows(pos, nch, wi % nch, &a0, &a1, &ae);
-      P.krows(reinterpret_cast<const KT*>(L->kc), wi / nch, D.cap, a0, ae);
+      front_rows(S.front, pos, blockIdx.x % nch, &a0, &a1, &ae);
+      P.krows(reinterpret_cast<const KT*>(L->kc), blockIdx.x / nch, D.cap, a0, ae);
     }
-    if (citem >= 0) {
+    if (citem >= 0) {                                // this CTA's context item
+      const int g = citem / kSlices;
       const long long vrow = ((const char*)L->vc - (const char*)D.kv_base) / rowb +
-                             (long long)(citem / kSlices) * D.cap;
-      P.vslices<KT>(vmap, 32 * (citem % kSlices), (int)vrow, pos);
+                             (long long)g * D.cap;
+      const StepScratch X = step_scratch(D);
+      constexpr int BR = kVRowsG<KT, GS>;
+      P.ctx_slots<KT, GS>(vmap, 32 * (citem % kSlices), (int)vrow,
+                          X.exps + (size_t)g * GS * X.ew, X.ew, (pos + BR) / BR,
+                          D.ticket + D.n_kv + g, (unsigned)((l + 1) * nch));
     }
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
@@ -576,6 +682,8 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
     tr[3] = P.t_empty;
     tr[4] = P.t_flight;
     tr[5] = P.q;
+    tr[6] = S.ctx_wait_ns;      // the consumers' phase-B totals (they finished before the
+    tr[7] = S.ctx_sum_ns;       // producer's drain returned: every slot was released)
   }
 }
 
@@ -1002,6 +1110,18 @@ __device__ __noinline__ void gemv_ring(const Ring R, unsigned q0, const GvPlan& 
 // that the producer brings into the ring as 32-dim slices (tensor copies), row pos from
 // this step's qkv; the warp quantises its 32 outputs (one quant_a8s block) into ctx.
 
+// One cache element at shared address a, as a float (binary16 widens exactly).
+template <class KT>
+HV_DEV float slot_elem(unsigned a) {
+  if constexpr (kKvHalf<KT>) {
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+    return __half2float(__ushort_as_half(h));
+  } else {
+    return lds_f1(a);
+  }
+}
+
 // Element e of a cache row held in shared memory (a ring slot row of KT, or a float row).
 template <class KT>
 struct SlotRow {
@@ -1019,177 +1139,127 @@ struct SlotRow {
   }
 };
 
-// Phase A of this CTA's (kv head, chunk) items.
+// Phase A of this CTA's (kv head, chunk) item -- at most one per CTA (the host checks
+// n_kv * attn_chunks <= grid), because an item waits for the other chunks of its kv head.
+// Chunk c is node c of numpy's recursion over the T = pos + 1 positions cut at the
+// launch's depth (S.front), so its pairwise sum is an exact subtree of the softmax sum.
+// Steps: q/k norm + RoPE, the KV append (the last chunk holds pos), the scores (OpenBLAS's
+// row-dot order, K rows from the ring), the chunk's maximum per head to global memory and
+// one count on the kv head's first ticket; once every chunk of the kv head has counted,
+// M = their maximum, e_t = np_expf(s_t - M) for the chunk's rows (to D.part's exp rows)
+// and the chunk's pairwise sum per head (to D.part's node sums); one count on the second
+// ticket.
 template <int GS, class KT>
-__device__ __noinline__ void attn_scores_ring(const hv_step_desc& D, const hv_layer_w* L,
-                                              int pos, int runs, const Ring R, unsigned* qp,
-                                              StepShared& S, float* area, int tb) {
+__device__ __noinline__ bool attn_scores_ring(const hv_step_desc& D, const hv_layer_w* L,
+                                              int pos, int layer, const Ring R, unsigned* qp,
+                                              StepShared& S, PwTree* tree, float* area,
+                                              int tb) {
   const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
+  const int wi = blockIdx.x;
+  if (wi >= nkv * nch) return true;
+  const StepScratch X = step_scratch(D);
   float* q_s = area;
   float* kpos_s = q_s + GS * kHd;
   float* vpos_s = kpos_s + kHd;
   float* tmp_s = vpos_s + kHd;                       // (GS + 1) x 128
-  float* lg_s = tmp_s + (GS + 1) * kHd;              // [chunk_max][GS]
+  float* m_s = tmp_s + (GS + 1) * kHd;               // GS maxima (+ pad)
+  float* lg_s = m_s + 8;                             // [chunk_max][GS]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, rr = lane >> 3;
   const float* cs = D.cos_t + (size_t)pos * (kHd / 2);
   const float* sn = D.sin_t + (size_t)pos * (kHd / 2);
   const float scale = D.attn_scale;
-  const int T = pos + 1;
-  float* lg_g = D.part;
-  float* cm_g = D.part + (size_t)nq * cap;
   constexpr int HP = GS < 4 ? GS : 4;
-  for (int wi = blockIdx.x; wi < nkv * nch; wi += gridDim.x) {
-    const int g = wi / nch, c = wi % nch;
-    int t0, t1, te;
-    attn_rows(pos, nch, c, &t0, &t1, &te);
-    const int n = t1 - t0;
-    const int nk = (te - t0 + kSlotRows - 1) / kSlotRows;
-    const unsigned qk = *qp;
-    *qp += (unsigned)nk;
-    // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
-    for (int h = warp; h < GS + 2; h += kConsWarps) {
-      if (h < GS) {
-        warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, L->qn, cs, sn, D.eps,
-                       tmp_s + h * kHd, q_s + h * kHd);
-      } else if (h == GS) {
-        warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, L->kn, cs, sn, D.eps,
-                       tmp_s + GS * kHd, kpos_s);
-        if constexpr (kKvHalf<KT>) {
-          float4* k4 = reinterpret_cast<float4*>(kpos_s) + lane;
-          *k4 = round_half4(*k4);
-        }
-      } else {
-        float4 v4 =
-            __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
-        if constexpr (kKvHalf<KT>) v4 = round_half4(v4);
-        reinterpret_cast<float4*>(vpos_s)[lane] = v4;
-      }
-    }
-    csync();
-    trace_mark(D, tb + 14);
-    trace_wait(D, S, tb + 20);
-    if (c == nch - 1 && threadIdx.x < kHd) {         // the chunk holding pos appends
-      KT* kc = reinterpret_cast<KT*>(L->kc) + (size_t)g * cap * kHd;
-      KT* vc = reinterpret_cast<KT*>(L->vc) + (size_t)g * cap * kHd;
-      kc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(kpos_s[threadIdx.x]);
-      vc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(vpos_s[threadIdx.x]);
-    }
-
-    // scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows; row pos from
-    // kpos_s) to warp m % 8, four positions per pass (8 lanes each)
-    bool ok = true;
-    const int nblk = (n + kSlotRows - 1) / kSlotRows;
-    float qr[HP][16];
-    if constexpr (GS <= 4) load_qregs<HP>(q_s, j, qr);
-    for (int m = warp; m < nblk && ok; m += kConsWarps) {
-      const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
-      unsigned slot = 0;
-      if (m < nk) {
-        const unsigned q = qk + (unsigned)m;
-        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
-        if (!ok) break;
-        slot = sh_addr(R.slot(q));
-      }
-#pragma unroll 1
-      for (int p0 = 0; p0 < GS; p0 += HP) {
-        if constexpr (GS > 4) load_qregs<HP>(q_s + p0 * kHd, j, qr);
-#pragma unroll 1
-        for (int tg = r0; tg < r1; tg += 4) {
-          const int t = tg + rr;
-          const bool valid = t < r1;
-          const bool cached = t < te;
-          const int kind = valid ? blas_row_kind(T, t, runs) : 0;
-          SlotRow<KT> row;
-          row.f32row = !cached;
-          row.addr = cached ? slot + (unsigned)((t - r0) * kHd * (int)sizeof(KT))
-                            : sh_addr(kpos_s);
-          float d[HP];
-          rowdots_blas<HP>(row, kind, qr, q_s + p0 * kHd, j, d);
-          float v = d[0];
-#pragma unroll
-          for (int h = 1; h < HP; ++h) v = (j == h) ? d[h] : v;
-          if (valid && j < HP) lg_s[(t - t0) * GS + p0 + j] = __fmul_rn(v, scale);
-        }
-      }
-      if (m < nk) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(qk + (unsigned)m), kConsWarps);
-      }
-    }
-    csync();
-    trace_mark(D, tb + 15);
-    trace_wait(D, S, tb + 21);
-    // the chunk's scores and per-head maximum to global memory, then its ticket
-    for (int i = warp; i < GS; i += kConsWarps) {
-      const int h = g * GS + i;
-      float mx = -INFINITY;
-      for (int t = lane; t < n; t += 32) {
-        const float sc = lg_s[t * GS + i];
-        mx = fmaxf(mx, sc);
-        lg_g[(size_t)h * cap + t0 + t] = sc;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-      if (lane == 0) cm_g[(size_t)h * nch + c] = mx;
-    }
-    csync();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      atomicAdd(D.ticket + g, 1);
-    }
-    trace_mark(D, tb + 16);
-  }
-}
-
-// Phase B of this CTA's (kv head, slice) item, if it has one: waits (bounded) until the
-// kv head's ticket reaches (layer + 1) * nch. `tree`: numpy's pairwise tree for pos + 1
-// values, built here in layer 0 (warp 1, while thread 0 waits) and kept for the launch.
-template <int GS, class KT>
-__device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int layer,
-                                           const Ring R, unsigned* qp, StepShared& S,
-                                           PwTree* tree, float* area, int tb) {
-  const int nkv = D.n_kv, nch = D.attn_chunks, cap = D.cap, nq = D.n_head;
-  const int item = ctx_item(blockIdx.x, gridDim.x, nkv * kSlices);
-  if (item < 0) return true;
-  constexpr int BR = kVRows<KT>;
-  const int g = item / kSlices, jsl = item % kSlices;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = wi / nch, c = wi % nch;
   const int T = pos + 1;
-  const int nvs = (pos + BR - 1) / BR;               // V slots: cached rows [0, pos)
-  const unsigned qv0 = *qp;
-  *qp += (unsigned)nvs;
-  const int nvl = (pw_tree_nodes_max(cap) + 3) & ~3;
-  float* vals = area;                                // [GS][nvl]: node values
-  float* wbuf = vals + (size_t)GS * nvl;             // [GS][2][BR]
-  float* ms = wbuf + (size_t)GS * 2 * BR;            // M per head
-  const float* lg_g = D.part;
-  const float* cm_g = D.part + (size_t)nq * cap;
-  if (layer == 0 && warp == 1) {
-    const bool built = pw_tree_build_warp(T, tree);
+  int t0, t1, te;
+  front_rows(S.front, pos, c, &t0, &t1, &te);
+  const int n = t1 - t0;
+  const int nk = (te - t0 + kSlotRows - 1) / kSlotRows;
+  const unsigned qk = *qp;
+  *qp += (unsigned)nk;
+  // GS query heads, the kv head's k (normed + rotated) and its raw v, a warp each
+  for (int h = warp; h < GS + 2; h += kConsWarps) {
+    if (h < GS) {
+      warp_norm_rope(D.qkv + (size_t)(g * GS + h) * kHd, L->qn, cs, sn, D.eps,
+                     tmp_s + h * kHd, q_s + h * kHd);
+    } else if (h == GS) {
+      warp_norm_rope(D.qkv + (size_t)(nq + g) * kHd, L->kn, cs, sn, D.eps,
+                     tmp_s + GS * kHd, kpos_s);
+      if constexpr (kKvHalf<KT>) {
+        float4* k4 = reinterpret_cast<float4*>(kpos_s) + lane;
+        *k4 = round_half4(*k4);
+      }
+    } else {
+      float4 v4 =
+          __ldcg(reinterpret_cast<const float4*>(D.qkv + (size_t)(nq + nkv + g) * kHd) + lane);
+      if constexpr (kKvHalf<KT>) v4 = round_half4(v4);
+      reinterpret_cast<float4*>(vpos_s)[lane] = v4;
+    }
+  }
+  if (layer == 0 && warp == kConsWarps - 1) {        // this chunk's subtree, for the launch
+    const bool built = n == 0 || pw_tree_build_warp(n, tree);
     if (lane == 0) S.tree_ok = built;
   }
-  // the kv head's chunks (bounded wait on its ticket)
-  if (threadIdx.x == 0) {
-    const unsigned want = (unsigned)((layer + 1) * nch);
-    const unsigned* tk = reinterpret_cast<const unsigned*>(D.ticket + g);
-    bool ok = true;
-    if (ld_acquire(tk) < want) {
-      const unsigned long long t0 = global_ns();
-      while (ld_acquire(tk) < want) {
-        if (*(volatile int*)D.status != 0) { ok = false; break; }
-        if (global_ns() - t0 > kWaitNs) {
-          atomicCAS(D.status, 0, HV_E_TIMEOUT);
-          ok = false;
-          break;
-        }
-        __nanosleep(200);
+  csync();
+  trace_mark(D, tb + 14);
+  trace_wait(D, S, tb + 20);
+  if (n > 0 && t1 == T && threadIdx.x < kHd) {       // the chunk holding pos appends
+    KT* kc = reinterpret_cast<KT*>(L->kc) + (size_t)g * cap * kHd;
+    KT* vc = reinterpret_cast<KT*>(L->vc) + (size_t)g * cap * kHd;
+    kc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(kpos_s[threadIdx.x]);
+    vc[(size_t)pos * kHd + threadIdx.x] = to_kv<KT>(vpos_s[threadIdx.x]);
+  }
+
+  // scores: block m = positions [t0 + 20 m, +20) (one ring slot of K rows; row pos from
+  // kpos_s) to warp m % 8, four positions per pass (8 lanes each)
+  bool ok = true;
+  const int nblk = (n + kSlotRows - 1) / kSlotRows;
+  float qr[HP][16];
+  if constexpr (GS <= 4) load_qregs<HP>(q_s, j, qr);
+  for (int m = warp; m < nblk && ok; m += kConsWarps) {
+    const int r0 = t0 + m * kSlotRows, r1 = min(r0 + kSlotRows, t1);
+    unsigned slot = 0;
+    if (m < nk) {
+      const unsigned q = qk + (unsigned)m;
+      ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+      if (!ok) break;
+      slot = sh_addr(R.slot(q));
+    }
+    const long long c0 = clock64();
+    const RunWin rw = run_window(S.runs, r0);
+#pragma unroll 1
+    for (int p0 = 0; p0 < GS; p0 += HP) {
+      if constexpr (GS > 4) load_qregs<HP>(q_s + p0 * kHd, j, qr);
+#pragma unroll 1
+      for (int tg = r0; tg < r1; tg += 4) {
+        const int t = tg + rr;
+        const bool valid = t < r1;
+        const bool cached = t < te;
+        const int kind = valid ? kind_in(rw, t) : 0;
+        SlotRow<KT> row;
+        row.f32row = !cached;
+        row.addr = cached ? slot + (unsigned)((t - r0) * kHd * (int)sizeof(KT)) : sh_addr(kpos_s);
+        float d[HP];
+        rowdots_blas<HP>(row, kind, qr, q_s + p0 * kHd, j, d);
+        float v = d[0];
+#pragma unroll
+        for (int h = 1; h < HP; ++h) v = (j == h) ? d[h] : v;
+        if (valid && j < HP) lg_s[(t - t0) * GS + p0 + j] = __fmul_rn(v, scale);
       }
     }
-    if (!ok) *(volatile int*)&S.abort = 1;
-    S.ok = ok;
+    if (lane == 0) S.busy[warp] += clock64() - c0;
+    if (m < nk) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive_n(R.empty_of(qk + (unsigned)m), kConsWarps);
+    }
   }
   csync();
-  if (!S.ok) return false;
+  trace_mark(D, tb + 15);
+  trace_wait(D, S, tb + 21);
+  if (threadIdx.x == 0 && D.trace != nullptr) {
+    D.trace[(size_t)blockIdx.x * HV_STEP_TRACE_STRIDE(D.n_layer) + tb + 25] = S.busy[0];
+    S.busy[0] = 0;
+  }
   if (!S.tree_ok) {
     if (threadIdx.x == 0) {
       atomicCAS(D.status, 0, HV_E_INVALID);
@@ -1197,100 +1267,211 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
     }
     return false;
   }
-  trace_mark(D, tb + 17);
+  // the chunk's maximum per head, then the first ticket
   for (int i = warp; i < GS; i += kConsWarps) {
-    float m = -INFINITY;
-    for (int c = lane; c < nch; c += 32) m = fmaxf(m, __ldcg(cm_g + (size_t)(g * GS + i) * nch + c));
+    float mx = -INFINITY;
+    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, lg_s[t * GS + i]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    if (lane == 0) ms[i] = m;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) X.cmax[(size_t)(g * GS + i) * nch + c] = mx;
   }
   csync();
-  {
-    // numpy's pairwise leaves of the exps: head i's 8-lane groups are those of the warps
-    // w = i (mod GS)
-    const int i = warp % GS;
-    const int gi = (warp / GS) * 4 + (lane >> 3), ng = (kConsWarps / GS) * 4;
-    const float* lgh = lg_g + (size_t)(g * GS + i) * cap;
-    const float M = ms[i];
-    const auto e = [lgh, M](int t) { return np_expf(__fsub_rn(__ldcg(lgh + t), M)); };
-    for (int l0 = 0; l0 < tree->nleaf; l0 += ng) {
-      const int l = l0 + gi;
-      const bool live = l < tree->nleaf;
-      const int id = live ? (int)tree->leaf[l] : 0;
-      const float v = pw_leaf_f(e, live ? (int)tree->start[id] : 0, live ? (int)tree->size[id] : 1,
-                                lane & 7);
-      if (live && (lane & 7) == 0) vals[(size_t)i * nvl + id] = v;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(D.ticket + g, 1);
+    S.ok = wait_count(D.ticket + g, (unsigned)((layer + 1) * nch), D.status);
+    if (!S.ok) *(volatile int*)&S.abort = 1;
+  }
+  csync();
+  if (!S.ok) return false;
+  trace_mark(D, tb + 16);
+  // M per head over every chunk of the kv head; the exps in place and to global memory
+  for (int i = warp; i < GS; i += kConsWarps) {
+    float mx = -INFINITY;
+    for (int k = lane; k < nch; k += 32) mx = fmaxf(mx, __ldcg(X.cmax + (size_t)(g * GS + i) * nch + k));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) m_s[i] = mx;
+  }
+  csync();
+  for (int i = 0; i < GS; ++i) {
+    const float M = m_s[i];
+    float* eg = X.exps + (size_t)(g * GS + i) * X.ew + t0;
+    for (int t = threadIdx.x; t < n; t += kConsThreads) {
+      const float e = np_expf(__fsub_rn(lg_s[t * GS + i], M));
+      lg_s[t * GS + i] = e;
+      eg[t] = e;
     }
   }
   csync();
+  // the chunk's pairwise sum per head: leaves by 8-lane groups, then one warp per head
+  if (n > 0) {
+    const int ngr = kConsWarps * 4, gi = warp * 4 + (lane >> 3);
+    const int nvl = (pw_tree_nodes_max(front_chunk_max(cap, nch)) + 3) & ~3;
+    float* vals = lg_s + (((size_t)n * GS + 3) & ~size_t(3));   // [GS][nvl]
+    for (int pl = gi; pl < ((tree->nleaf * GS + ngr - 1) / ngr) * ngr; pl += ngr) {
+      const bool live = pl < tree->nleaf * GS;
+      const int i = live ? pl % GS : 0, l = live ? pl / GS : 0;
+      const int id = tree->leaf[l];
+      const float v = leaf_sum_strided(lg_s + i, GS, live ? (int)tree->start[id] : 0,
+                                       live ? (int)tree->size[id] : 1, lane & 7);
+      if (live && (lane & 7) == 0) vals[(size_t)i * nvl + id] = v;
+    }
+    csync();
+    for (int i = warp; i < GS; i += kConsWarps) {
+      const float sum = pw_tree_fold_raw(tree, vals + (size_t)i * nvl);
+      if (lane == 0) X.nsum[(size_t)(g * GS + i) * nch + c] = sum;
+    }
+  }
+  csync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(D.ticket + nkv + g, 1);
+  }
+  trace_mark(D, tb + 17);
+  return true;
+}
+
+// Phase B of this CTA's (kv head, 32-dim slice) item, if it has one: once every chunk of
+// the kv head has its exps and subtree sums in (the second ticket), S = the top of the
+// recursion over the chunks' sums; then one warp per query head runs the sequential
+// weighted V sum. Block k's ring slot holds V rows [k BR, k BR + BR) (this slice) and the
+// GS heads' exps for the same rows; the warp turns its head's exps into w = e / S in the
+// slot, and takes row pos's v from this step's qkv.
+template <int GS, class KT>
+__device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int layer,
+                                           const Ring R, unsigned* qp, StepShared& S,
+                                           float* area, int tb) {
+  const int nkv = D.n_kv, nch = D.attn_chunks, nq = D.n_head;
+  const int item = ctx_item(blockIdx.x, gridDim.x, nkv * kSlices);
+  if (item < 0) return true;
+  constexpr int BR = kVRowsG<KT, GS>;
+  constexpr int kVB = BR * 32 * (int)sizeof(KT);     // bytes of the V part of a slot
+  const StepScratch X = step_scratch(D);
+  const int g = item / kSlices, jsl = item % kSlices;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = pos + 1;
+  const int nblkv = (T + BR - 1) / BR;
+  const unsigned qv0 = *qp;
+  *qp += (unsigned)nblkv;
+  float* vals = area;                                // [GS][nch] chunk sums
+  float* s_s = vals + (((size_t)GS * nch + 3) & ~size_t(3));   // S per head (+ pad)
+  float* wbuf = s_s + 8;                             // [GS][2][BR] weights per chain warp
+  if (threadIdx.x == 0) {
+    S.ok = wait_count(D.ticket + nkv + g, (unsigned)((layer + 1) * nch), D.status);
+    if (!S.ok) *(volatile int*)&S.abort = 1;
+  }
+  csync();
+  if (!S.ok) return false;
   trace_mark(D, tb + 18);
+  const int nf = S.front.n;
+  for (int e = threadIdx.x; e < GS * nf; e += kConsThreads)
+    vals[e] = __ldcg(X.nsum + (size_t)(g * GS + e / nf) * nch + e % nf);
+  csync();
+  if (threadIdx.x < GS) s_s[threadIdx.x] = pw_front_fold(S.front, vals + threadIdx.x * nf);
+  csync();
   bool ok = true;
   if (warp < GS) {
+    // the chain over the cached rows [0, pos) in 16-row chunks: chunk c+1's V loads and
+    // (at a block boundary) the next block's weights are issued before chunk c's adds
     const int i = warp;
-    const float S_ = pw_tree_fold(tree, vals + (size_t)i * nvl);
-    const float M = ms[i];
-    const float* lgh = lg_g + (size_t)(g * GS + i) * cap;
-    float* wb[2] = {wbuf + (size_t)i * 2 * BR, wbuf + (size_t)i * 2 * BR + BR};
-    // weights of block k (positions [k BR, min((k + 1) BR, T))), 32 at a time
-    const auto wgroup = [&](int k, int u, float* dst) {
-      const int t = k * BR + 32 * u + lane;
-      if (32 * u + lane < BR && t < T)
-        dst[32 * u + lane] = __fdiv_rn(np_expf(__fsub_rn(__ldcg(lgh + t), M)), S_);
-    };
-    constexpr int kU = (BR + 31) / 32;
-    const int nblkv = (T + BR - 1) / BR;
-#pragma unroll 1
-    for (int u = 0; u < kU; ++u) wgroup(0, u, wb[0]);
-    __syncwarp();
-    // this step's v row (slice), rounded like the appended row
+    const float S_ = s_s[i];
     float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
     if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
     const unsigned rel = (unsigned)(kConsWarps / GS);
+    constexpr int kRowB = 32 * (int)sizeof(KT);      // bytes of one 32-dim row slice
+    constexpr int CR = 16;                           // rows per chunk
+    constexpr int CPB = BR / CR;                     // chunks per block
+    const unsigned wb0 = sh_addr(wbuf + (size_t)i * 2 * BR);
+    if (lane == 0) S.wait[warp] = 0;
     float acc = 0.0f;
-#pragma unroll 1
-    for (int k = 0; k < nblkv && ok; ++k) {
-      float* wc = wb[k & 1];
-      float* wn = wb[(k + 1) & 1];
-      const bool nxt = k + 1 < nblkv;
-      int done = 0;
-      const int base = k * BR;
-      const int ncache = max(0, min(BR, pos - base));   // rows of this block from the slot
-      if (ncache > 0) {
-        const unsigned q = qv0 + (unsigned)k;
-        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
-        if (!ok) break;
-        const unsigned sl = sh_addr(R.slot(q)) + (unsigned)(lane * (int)sizeof(KT));
-        const unsigned wsh = sh_addr(wc);
-#pragma unroll 1
-        for (int r = 0; r < ncache; r += 8) {
-          if ((r & 31) == 0 && nxt && done < kU) wgroup(k + 1, done++, wn);
-          float v[8];
+    int prepared = -1;
+    // block k: wait for its slot, w = e / S into the warp's buffer k & 1
+    const auto prep = [&](int k) -> bool {
+      const unsigned q = qv0 + (unsigned)k;
+      if (!warp_wait(R.full_of(q), R.parity(q), S, D.status)) return false;
+      const unsigned esh = sh_addr(R.slot(q)) + (unsigned)(kVB + i * BR * 4);
+      const unsigned wsh = wb0 + 4u * (unsigned)((k & 1) * BR);
 #pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            const unsigned a = sl + (unsigned)((r + x) * 32 * (int)sizeof(KT));
-            if constexpr (kKvHalf<KT>) {
-              unsigned short h;
-              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
-              v[x] = __half2float(__ushort_as_half(h));
-            } else {
-              v[x] = lds_f1(a);
-            }
-          }
-          const float4 w0 = lds_f4(wsh + 4u * r), w1 = lds_f4(wsh + 4u * r + 16u);
-          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      for (int u = 0; u < BR / 32; ++u) {
+        const int o = 32 * u + lane;
+        const float e = lds_f1(esh + 4u * (unsigned)o);
+        const float w = (k * BR + o < T) ? __fdiv_rn(e, S_) : 0.0f;
+        asm volatile("st.shared.f32 [%0], %1;" :: "r"(wsh + 4u * (unsigned)o), "f"(w) : "memory");
+      }
+      prepared = k;
+      return true;
+    };
+    const auto loadv = [&](int c, float (&v)[CR]) {
+      const int k = c / CPB;
+      const unsigned sl = sh_addr(R.slot(qv0 + (unsigned)k)) + (unsigned)(lane * (int)sizeof(KT));
+      const int r0 = CR * c - k * BR;
 #pragma unroll
-          for (int x = 0; x < 8; ++x)
-            if (r + x < ncache) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
+      for (int x = 0; x < CR; ++x) v[x] = slot_elem<KT>(sl + (unsigned)(min(r0 + x, BR - 1) * kRowB));
+    };
+    const int nchunk = (pos + CR - 1) / CR;
+    float va[CR], vb[CR];
+    if (nchunk > 0) {
+      ok = prep(0);
+      if (ok) loadv(0, va);
+    }
+#pragma unroll 1
+    for (int c = 0; c < nchunk && ok; c += 2) {
+      // two chunks per iteration so the V registers alternate statically (va, vb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int cc = c + h;
+        if (cc >= nchunk || !ok) break;
+        float (&vcur)[CR] = h == 0 ? va : vb;
+        float (&vnxt)[CR] = h == 0 ? vb : va;
+        const int k = cc / CPB;
+        if (cc + 1 < nchunk) {
+          const int k2 = (cc + 1) / CPB;
+          if (k2 != k) ok = prep(k2);
+          if (ok) loadv(cc + 1, vnxt);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
+        const unsigned wsh = wb0 + 4u * (unsigned)((k & 1) * BR + (CR * cc - k * BR));
+        const int nv = min(CR, pos - CR * cc);       // cached rows in this chunk
+        const long long cc0 = clock64();
+        if (nv == CR) {
+#pragma unroll
+          for (int x = 0; x < CR; x += 4) {
+            const float4 w4 = lds_f4(wsh + 4u * (unsigned)x);
+            acc = __fadd_rn(acc, __fmul_rn(w4.x, vcur[x]));
+            acc = __fadd_rn(acc, __fmul_rn(w4.y, vcur[x + 1]));
+            acc = __fadd_rn(acc, __fmul_rn(w4.z, vcur[x + 2]));
+            acc = __fadd_rn(acc, __fmul_rn(w4.w, vcur[x + 3]));
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < CR; x += 4) {
+            const float4 w4 = lds_f4(wsh + 4u * (unsigned)x);
+            if (x < nv) acc = __fadd_rn(acc, __fmul_rn(w4.x, vcur[x]));
+            if (x + 1 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.y, vcur[x + 1]));
+            if (x + 2 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.z, vcur[x + 2]));
+            if (x + 3 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.w, vcur[x + 3]));
+          }
+        }
+        if (warp == 0 && lane == 0) S.ctx_wait_ns += (unsigned long long)(clock64() - cc0);
+        const bool blk_end = (cc % CPB == CPB - 1) || cc + 1 == nchunk;
+        if (blk_end && k != pos / BR) {              // the block holding pos stays for its w
+          __syncwarp();
+          if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)k), rel);
+        }
       }
-      if (pos >= base && pos < base + BR)            // the last row: this step's v
-        acc = __fadd_rn(acc, __fmul_rn(wc[pos - base], vpos));
-      if (nxt)
-        for (; done < kU; ++done) wgroup(k + 1, done, wn);
-      __syncwarp();
+    }
+    if (ok) {
+      // the last row: this step's v, its weight in the block holding pos
+      const int kp = pos / BR;
+      if (prepared != kp) ok = prep(kp);
+      if (ok) {
+        __syncwarp();
+        acc = __fadd_rn(acc, __fmul_rn(lds_f1(wb0 + 4u * (unsigned)((kp & 1) * BR + pos - kp * BR)),
+                                       vpos));
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)kp), rel);
+      }
     }
     if (ok) {
       // ctx element (head g GS + i, dim 32 jsl + lane) -> int8 + (scale, sum) of its block
@@ -1354,6 +1535,8 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
     S.xphase = D.world > 1 ? ld_acquire_sys(D.barrier + 1) & 0x80000000u : 0u;
     S.gen = D.world > 1 ? ld_acquire(D.barrier + 2) : 0u;
     for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0, S.busy[w] = 0;
+    S.ctx_wait_ns = 0;
+    S.ctx_sum_ns = 0;
   }
   {
     const int* src = reinterpret_cast<const int*>(D.plans);
@@ -1367,19 +1550,26 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
   }
   const int pos = *D.pos;
   const int tok = *D.tok;
+  if (threadIdx.x == 0) {
+    // the attention chunks: numpy's recursion over pos + 1 positions cut at depth
+    // log2(attn_chunks) (every CTA builds the same list)
+    const int depth = 31 - __clz(D.attn_chunks);
+    S.tree_ok = pos >= 0 && pos < D.cap && pw_front_build(pos + 1, depth, &S.front);
+  }
   __syncthreads();
-  if (pos < 0 || pos >= D.cap || tok < 0 || tok >= D.vocab) {
+  if (pos < 0 || pos >= D.cap || tok < 0 || tok >= D.vocab || !S.tree_ok) {
     // every CTA reads the same values, so all leave here, before any copy or barrier
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(D.status, HV_E_INVALID);
     return;
   }
   if (threadIdx.x >= kConsThreads) {               // the producer warp: one lane copies
     if (threadIdx.x == kConsThreads)
-      produce<KT>(D, Ls, flags, pos, R, S, inflight, evict_first, &vmap);
+      produce<GS, KT>(D, Ls, flags, pos, R, S, inflight, evict_first, &vmap);
     return;
   }
 
   // ---- consumers
+  if (threadIdx.x == 0) blas_runs(pos + 1, runs, &S.runs);   // read after the first csync
   const int nqkv = (D.n_head + 2 * D.n_kv) * kHd;
   const __half* emb_row = reinterpret_cast<const __half*>(D.emb16) + (size_t)tok * hid;
   {
@@ -1415,8 +1605,8 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
     if (!grid_sync(D, S, (flags & kFlagLocalQkvBarrier) == 0)) return;
     trace_mark(D, tb + 2);
     // P2: attention -- scores per (kv head, chunk), then the context per (kv head, slice)
-    attn_scores_ring<GS, KT>(D, L, pos, runs, R, &q, S, work, tb);
-    if (!attn_ctx_ring<GS, KT>(D, pos, l, R, &q, S, tree, work, tb)) return;
+    if (!attn_scores_ring<GS, KT>(D, L, pos, l, R, &q, S, tree, work, tb)) return;
+    if (!attn_ctx_ring<GS, KT>(D, pos, l, R, &q, S, work, tb)) return;
     trace_mark(D, tb + 3);
     if (!grid_sync(D, S)) return;
     trace_mark(D, tb + 4);
@@ -1475,7 +1665,7 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
   }
 
   // every CTA has passed its last attention phase: the kv heads' tickets restart at zero
-  if (blockIdx.x == 0 && threadIdx.x < D.n_kv) D.ticket[threadIdx.x] = 0;
+  if (blockIdx.x == 0 && threadIdx.x < 2 * D.n_kv) D.ticket[threadIdx.x] = 0;
   if (!(flags & HV_STEP_HEAD)) return;
   const int th = 2 + 28 * D.n_layer;
   norm_quant(D.h, nullptr, D.onorm, hid, D.eps, S, work, q_s, sb_s, D, -1);
@@ -1508,7 +1698,7 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
       D.amax_v[blockIdx.x] = S.sv[0];
       D.amax_i[blockIdx.x] = S.si[0];
       __threadfence();
-      S.flag = (atomicAdd(D.ticket + D.n_kv, 1) == (int)gridDim.x - 1);
+      S.flag = (atomicAdd(D.ticket + 2 * D.n_kv, 1) == (int)gridDim.x - 1);
     }
     csync();
     if (S.flag && threadIdx.x == 0) {
@@ -1526,7 +1716,7 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
       if (s >= 0 && s <= D.cap) D.gen[s] = idx;      // gen holds cap + 1 entries
       *D.step = s + 1;
       *D.pos = pos + 1;
-      D.ticket[D.n_kv] = 0;
+      D.ticket[2 * D.n_kv] = 0;
     }
   }
   trace_mark(D, th + 2);
@@ -1559,15 +1749,25 @@ typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static int vslice_map(const void* base, long long rows, int esz, CUtensorMap* out) {
+// Rows per phase-B slot for a cache of esz-byte elements and group size gs (kVRowsG).
+static int vslice_rows(int esz, int gs) {
+  if (esz == 2)
+    return gs == 1 ? kVRowsG<__half, 1> : gs == 2 ? kVRowsG<__half, 2>
+         : gs == 4 ? kVRowsG<__half, 4> : kVRowsG<__half, 8>;
+  return gs == 1 ? kVRowsG<float, 1> : gs == 2 ? kVRowsG<float, 2>
+       : gs == 4 ? kVRowsG<float, 4> : kVRowsG<float, 8>;
+}
+
+static int vslice_map(const void* base, long long rows, int esz, int box_rows,
+                      CUtensorMap* out) {
   static std::mutex mu;
   static TmapEncodeFn enc = nullptr;
   static const void* last_base = nullptr;
   static long long last_rows = 0;
-  static int last_esz = 0;
+  static int last_esz = 0, last_box = 0;
   static CUtensorMap last;
   std::lock_guard<std::mutex> lk(mu);
-  if (base == last_base && rows == last_rows && esz == last_esz) {
+  if (base == last_base && rows == last_rows && esz == last_esz && box_rows == last_box) {
     *out = last;
     return HV_OK;
   }
@@ -1581,7 +1781,7 @@ static int vslice_map(const void* base, long long rows, int esz, CUtensorMap* ou
   }
   const cuuint64_t dims[2] = {(cuuint64_t)kHd, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)kHd * (cuuint64_t)esz};
-  const cuuint32_t box[2] = {32u, (cuuint32_t)(kSlotBytes / (32 * esz))};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1u, 1u};
   CUtensorMap m;
   const CUresult r = enc(&m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
@@ -1595,6 +1795,7 @@ static int vslice_map(const void* base, long long rows, int esz, CUtensorMap* ou
   last_base = base;
   last_rows = rows;
   last_esz = esz;
+  last_box = box_rows;
   *out = m;
   return HV_OK;
 }
@@ -1624,17 +1825,14 @@ int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t
   if (rc) return rc;
   *grid = sms;
   *threads = kStepThreads;
-  int nch = sms / n_kv;
-  if (nch < 1) nch = 1;
-  const int need = (cap + 511) / 512;
-  if (nch < need) nch = need;
   HV_REQUIRE(cap <= kExactMaxCap, HV_E_UNSUPPORTED,
              "hv_step_config: cache of %d positions (at most %d)", cap, kExactMaxCap);
-  HV_REQUIRE(nch <= kAttnMaxChunks, HV_E_UNSUPPORTED,
-             "hv_step_config: %d attention chunks per kv head (at most %d; cap %d is too long)",
-             nch, kAttnMaxChunks, cap);
+  HV_REQUIRE(n_kv * kSlices <= sms, HV_E_UNSUPPORTED,
+             "hv_step_config: %d kv heads need %d CTAs for the attention context", n_kv,
+             n_kv * kSlices);
+  const int nch = 1 << front_depth(n_kv, sms);
   *chunks = nch;
-  *part_floats = (size_t)n_kv * group * ((size_t)cap + (size_t)nch);
+  *part_floats = step_part_floats(n_kv * group, cap, nch);
   if (smem) *smem = 0;
   return HV_OK;
 }
@@ -1689,9 +1887,10 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   HV_REQUIRE(h.plans != nullptr, HV_E_INVALID, "hv_step_launch: plans not set (hv_step_plans)");
   HV_REQUIRE(h.n_layer > 0 && h.layers != nullptr, HV_E_INVALID,
              "hv_step_launch: no layer table");
-  HV_REQUIRE(h.attn_chunks > 0 && 2 * h.attn_chunks + 1 <= kConsWarps * kHd, HV_E_INVALID,
-             "hv_step_launch: attn_chunks %d outside [1, %d]", h.attn_chunks,
-             (kConsWarps * kHd - 1) / 2);
+  HV_REQUIRE(h.attn_chunks > 0 && h.attn_chunks <= kMaxFront &&
+                 (h.attn_chunks & (h.attn_chunks - 1)) == 0,
+             HV_E_INVALID, "hv_step_launch: attn_chunks %d (a power of two, at most %d)",
+             h.attn_chunks, kMaxFront);
   const int gs = h.n_head / h.n_kv;
   HV_REQUIRE(gs == 1 || gs == 2 || gs == 4 || gs == 8, HV_E_UNSUPPORTED,
              "hv_step_launch: group size %d", gs);
@@ -1740,14 +1939,14 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const int variant = h.w4_layout == HV_W4_DQ ? (f16 ? 4 : 3) : f16 ? 2 : 0;
   HV_REQUIRE(h.cap <= kExactMaxCap, HV_E_UNSUPPORTED, "hv_step_launch: cap %d > %d", h.cap,
              kExactMaxCap);
-  HV_REQUIRE(h.n_kv * kSlices <= sms, HV_E_UNSUPPORTED,
-             "hv_step_launch: %d kv heads need %d CTAs for the attention context", h.n_kv,
-             h.n_kv * kSlices);
+  HV_REQUIRE(h.n_kv * kSlices <= sms && h.n_kv * h.attn_chunks <= sms, HV_E_UNSUPPORTED,
+             "hv_step_launch: %d kv heads x %d chunks need one CTA per attention item (%d)",
+             h.n_kv, h.attn_chunks, sms);
   HV_REQUIRE(h.kv_base != nullptr && h.kv_rows >= (long long)2 * h.n_kv * h.cap &&
                  ((uintptr_t)h.kv_base & 15) == 0,
              HV_E_INVALID, "hv_step_launch: kv_base/kv_rows do not describe the KV cache");
   CUtensorMap vmap;
-  rc = vslice_map(h.kv_base, h.kv_rows, f16 ? 2 : 4, &vmap);
+  rc = vslice_map(h.kv_base, h.kv_rows, f16 ? 2 : 4, vslice_rows(f16 ? 2 : 4, gs), &vmap);
   if (rc) return rc;
   void* fn = step_fn(gs, variant);
   {

@@ -457,8 +457,8 @@ class Engine:
         self.d_layers = self._alloc(C.sizeof(lw))
         hvdrv.upload(self.d_layers, C.addressof(lw), C.sizeof(lw))
         self.d_part = self._alloc(part.value * 4)
-        self.d_ticket = self._alloc((sh["n_kv"] + 1) * 4)
-        hvdrv.memset8(self.d_ticket, 0, (sh["n_kv"] + 1) * 4)
+        self.d_ticket = self._alloc((2 * sh["n_kv"] + 1) * 4)
+        hvdrv.memset8(self.d_ticket, 0, (2 * sh["n_kv"] + 1) * 4)
         self.d_amax_v = self._alloc(grid.value * 4)
         self.d_amax_i = self._alloc(grid.value * 4)
         self.d_barrier = self._alloc(16)
@@ -589,7 +589,7 @@ class Engine:
         [grid, stride]} where each phase's duration is taken per CTA and summed over the
         layers (median and max over CTAs)."""
         c = self.cfg
-        stride = 8 + 28 * c.n_layer
+        stride = 10 + 28 * c.n_layer
         n = self.step_grid * stride
         buf = hvdrv.alloc(n * 8)
         try:
@@ -646,9 +646,10 @@ class Engine:
             out[name] = {"median_us": float(np.median(d) / 1e3), "max_us": float(d.max() / 1e3)}
         out["setup"] = {"median_us": float(np.median(t[:, 1]) / 1e3),
                         "max_us": float(t[:, 1].max() / 1e3)}
-        for k, name in zip(range(3, 6), ("producer_wait_slot_us", "producer_wait_flight_us",
-                                          "producer_slots")):
-            v = raw[:, th + k].astype(np.float64) / (1e3 if k < 5 else 1.0)
+        for k, name in zip(range(3, 8), ("producer_wait_slot_us", "producer_wait_flight_us",
+                                          "producer_slots", "ctx_wait_slots_us",
+                                          "ctx_sum_us")):
+            v = raw[:, th + k].astype(np.float64) / (1.0 if k == 5 else 1e3)
             out[name] = {"median_us": float(np.median(v)), "max_us": float(v.max())}
         last = flags & STEP_ARGMAX and th + 2 or (flags & STEP_HEAD and th + 1 or th - 1)
         return {"total_us": float(t[:, last].max() / 1e3), "phases": out, "raw": raw}
@@ -662,7 +663,7 @@ class Engine:
         hvdrv.synchronize()
         hvdrv.memset8(self.d_barrier, 0, 16)
         hvdrv.memset8(self.d_status, 0, 4)
-        hvdrv.memset8(self.d_ticket, 0, (self.shard["n_kv"] + 1) * 4)
+        hvdrv.memset8(self.d_ticket, 0, (2 * self.shard["n_kv"] + 1) * 4)
 
     def _check_status(self):
         st = self.step_status()

@@ -350,7 +350,7 @@ typedef struct hv_step_desc {
   float* logits;                /* [head_rows]                                     */
   float* part;                  /* attention scratch (hv_step_config): scores
                                    [n_head][cap], then chunk maxima [n_head][chunks] */
-  int32_t* ticket;              /* [n_kv + 1] zeroed once; every launch leaves them
+  int32_t* ticket;              /* [2 n_kv + 1] zeroed once; every launch leaves them
                                    zero (after a failed launch the caller re-zeroes) */
   float* amax_v; int32_t* amax_i;                  /* [grid] argmax partials       */
   uint32_t* barrier;            /* four words, zeroed once                         */
@@ -402,16 +402,18 @@ typedef struct hv_step_peers {
  * +0 qkv prologue, +1 qkv GEMV, +2 barrier, +3 attention, +4 barrier, +5 o prologue,
  * +6 o GEMV, +7 barrier, +8 gate/up prologue, +9 gate/up GEMV, +10 barrier,
  * +11 down prologue, +12 down GEMV, +13 barrier; inside the attention (last work item
- * of the CTA): +14 q/k norms and RoPE, +15 scores, +16 softmax, +17 weighted V sum and
- * partials, +18 ticket, +19 merge (all %globaltimer ns). Durations (ns) that consumer
- * warp 0 spent waiting for its shared-memory ring slots: +21 attention scores, +22
- * attention V sum, +23 qkv GEMV, +24 gate/up GEMV (+20 is scratch); +25 = SM cycles
- * warp 0 spent computing attention scores; +26 / +27: inside the qkv prologue, vector
- * loaded and squared / sum of squares done. Then
+ * of the CTA): +14 q/k norms and RoPE, +15 scores, +16 scores stored and ticket taken;
+ * on the CTAs of a context item: +17 its kv head's scores all in, +18 exps and pairwise
+ * leaves done, +19 weighted V chain and quantisation done (all %globaltimer ns).
+ * Durations (ns) that consumer warp 0 spent waiting for its shared-memory ring slots:
+ * +21 attention scores, +23 qkv GEMV, +24 gate/up GEMV (+20 is scratch); +25 = SM
+ * cycles warp 0 spent computing attention scores; +26 / +27: inside the qkv prologue,
+ * vector loaded and squared / sum of squares done. Then
  * the head prologue, head GEMV and argmax at 2 + 28 n_layer + {0, 1, 2}; then, for the
  * producer warp: ns blocked on a ring slot still in use (+3), ns blocked on the copies in
- * flight (+4), slots copied (+5). */
-#define HV_STEP_TRACE_STRIDE(n_layer) (8 + 28 * (n_layer))
+ * flight (+4), slots copied (+5); for a context item's CTA, over the whole launch: ns its
+ * warp 0 waited for V slots (+6), ns of its exps and leaf sums (+7). */
+#define HV_STEP_TRACE_STRIDE(n_layer) (10 + 28 * (n_layer))
 
 #define HV_STEP_HEAD 1     /* compute the LM head into logits                          */
 #define HV_STEP_ARGMAX 2   /* then greedy argmax: tok = argmax, gen[step] = tok,

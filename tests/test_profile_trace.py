@@ -18,7 +18,7 @@ TL = 28                                          # trace entries per layer
 
 def synthetic_trace():
     th = 2 + TL * NL
-    raw = np.zeros((GRID, 8 + TL * NL), np.uint64)
+    raw = np.zeros((GRID, 10 + TL * NL), np.uint64)
     for b in range(GRID):
         clock = 1000 * b
         raw[b, 0] = clock
