@@ -120,7 +120,7 @@ HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
   const size_t nvl = ((size_t)pw_tree_nodes_max((int)cm) + 3) & ~size_t(3);
   const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 8 +
                    ((cm * gs + 3) & ~size_t(3)) + (size_t)gs * nvl;
-  const size_t b = (((size_t)gs * nch + 3) & ~size_t(3)) + 8 + (size_t)gs * 2 * 128;
+  const size_t b = (((size_t)gs * nch + 3) & ~size_t(3)) + 8;
   return a > b ? a : b;
 }
 
@@ -390,6 +390,7 @@ HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
     prefetch_l2(L->fn, (size_t)hid * 4);
   }
 }
+
 
 // The phase-B item of CTA b (kv head * 4 + slice), or -1: items spread over the grid.
 HV_DEV int ctx_item(int b, int grid, int nitems) {
@@ -941,6 +942,9 @@ HV_DEV float lds_f1(unsigned a) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
+HV_DEV void sts_f1(unsigned a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" :: "r"(a), "f"(v) : "memory");
+}
 
 // Block terms of iteration u of a ring slot for the lane's row g: blocks 2t (x) and
 // 2t+1 (y) of logical iteration `it` (the combine of gemv_tile8 in gemv_mma.cuh).
@@ -1355,8 +1359,7 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
   const unsigned qv0 = *qp;
   *qp += (unsigned)nblkv;
   float* vals = area;                                // [GS][nch] chunk sums
-  float* s_s = vals + (((size_t)GS * nch + 3) & ~size_t(3));   // S per head (+ pad)
-  float* wbuf = s_s + 8;                             // [GS][2][BR] weights per chain warp
+  float* s_s = vals + (size_t)GS * nch;              // S per head
   if (threadIdx.x == 0) {
     S.ok = wait_count(D.ticket + nkv + g, (unsigned)((layer + 1) * nch), D.status);
     if (!S.ok) *(volatile int*)&S.abort = 1;
@@ -1372,107 +1375,72 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
   csync();
   bool ok = true;
   if (warp < GS) {
-    // the chain over the cached rows [0, pos) in 16-row chunks: chunk c+1's V loads and
-    // (at a block boundary) the next block's weights are issued before chunk c's adds
     const int i = warp;
     const float S_ = s_s[i];
     float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
     if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
     const unsigned rel = (unsigned)(kConsWarps / GS);
     constexpr int kRowB = 32 * (int)sizeof(KT);      // bytes of one 32-dim row slice
-    constexpr int CR = 16;                           // rows per chunk
-    constexpr int CPB = BR / CR;                     // chunks per block
-    const unsigned wb0 = sh_addr(wbuf + (size_t)i * 2 * BR);
     if (lane == 0) S.wait[warp] = 0;
     float acc = 0.0f;
-    int prepared = -1;
-    // block k: wait for its slot, w = e / S into the warp's buffer k & 1
-    const auto prep = [&](int k) -> bool {
-      const unsigned q = qv0 + (unsigned)k;
-      if (!warp_wait(R.full_of(q), R.parity(q), S, D.status)) return false;
-      const unsigned esh = sh_addr(R.slot(q)) + (unsigned)(kVB + i * BR * 4);
-      const unsigned wsh = wb0 + 4u * (unsigned)((k & 1) * BR);
-#pragma unroll
-      for (int u = 0; u < BR / 32; ++u) {
-        const int o = 32 * u + lane;
-        const float e = lds_f1(esh + 4u * (unsigned)o);
-        const float w = (k * BR + o < T) ? __fdiv_rn(e, S_) : 0.0f;
-        asm volatile("st.shared.f32 [%0], %1;" :: "r"(wsh + 4u * (unsigned)o), "f"(w) : "memory");
-      }
-      prepared = k;
-      return true;
-    };
-    const auto loadv = [&](int c, float (&v)[CR]) {
-      const int k = c / CPB;
-      const unsigned sl = sh_addr(R.slot(qv0 + (unsigned)k)) + (unsigned)(lane * (int)sizeof(KT));
-      const int r0 = CR * c - k * BR;
-#pragma unroll
-      for (int x = 0; x < CR; ++x) v[x] = slot_elem<KT>(sl + (unsigned)(min(r0 + x, BR - 1) * kRowB));
-    };
-    const int nchunk = (pos + CR - 1) / CR;
-    float va[CR], vb[CR];
-    if (nchunk > 0) {
-      ok = prep(0);
-      if (ok) loadv(0, va);
-    }
 #pragma unroll 1
-    for (int c = 0; c < nchunk && ok; c += 2) {
-      // two chunks per iteration so the V registers alternate statically (va, vb)
+    for (int k = 0; k < nblkv && ok; ++k) {
+      const unsigned q = qv0 + (unsigned)k;
+      ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+      if (!ok) break;
+      const unsigned sl = sh_addr(R.slot(q));
+      const unsigned wsh = sl + (unsigned)(kVB + i * BR * 4);
+      const int base = k * BR;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int cc = c + h;
-        if (cc >= nchunk || !ok) break;
-        float (&vcur)[CR] = h == 0 ? va : vb;
-        float (&vnxt)[CR] = h == 0 ? vb : va;
-        const int k = cc / CPB;
-        if (cc + 1 < nchunk) {
-          const int k2 = (cc + 1) / CPB;
-          if (k2 != k) ok = prep(k2);
-          if (ok) loadv(cc + 1, vnxt);
-        }
-        __syncwarp();
-        const unsigned wsh = wb0 + 4u * (unsigned)((k & 1) * BR + (CR * cc - k * BR));
-        const int nv = min(CR, pos - CR * cc);       // cached rows in this chunk
-        const long long cc0 = clock64();
-        if (nv == CR) {
-#pragma unroll
-          for (int x = 0; x < CR; x += 4) {
-            const float4 w4 = lds_f4(wsh + 4u * (unsigned)x);
-            acc = __fadd_rn(acc, __fmul_rn(w4.x, vcur[x]));
-            acc = __fadd_rn(acc, __fmul_rn(w4.y, vcur[x + 1]));
-            acc = __fadd_rn(acc, __fmul_rn(w4.z, vcur[x + 2]));
-            acc = __fadd_rn(acc, __fmul_rn(w4.w, vcur[x + 3]));
-          }
-        } else {
-#pragma unroll
-          for (int x = 0; x < CR; x += 4) {
-            const float4 w4 = lds_f4(wsh + 4u * (unsigned)x);
-            if (x < nv) acc = __fadd_rn(acc, __fmul_rn(w4.x, vcur[x]));
-            if (x + 1 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.y, vcur[x + 1]));
-            if (x + 2 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.z, vcur[x + 2]));
-            if (x + 3 < nv) acc = __fadd_rn(acc, __fmul_rn(w4.w, vcur[x + 3]));
-          }
-        }
-        if (warp == 0 && lane == 0) S.ctx_wait_ns += (unsigned long long)(clock64() - cc0);
-        const bool blk_end = (cc % CPB == CPB - 1) || cc + 1 == nchunk;
-        if (blk_end && k != pos / BR) {              // the block holding pos stays for its w
-          __syncwarp();
-          if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)k), rel);
+      for (int u = 0; u < BR / 32; ++u) {            // w = e / S for the block's rows
+        const int o = 32 * u + lane;
+        if (base + o < T) {
+          const unsigned a = wsh + 4u * (unsigned)o;
+          asm volatile("st.shared.f32 [%0], %1;" :: "r"(a), "f"(__fdiv_rn(lds_f1(a), S_))
+                       : "memory");
         }
       }
-    }
-    if (ok) {
-      // the last row: this step's v, its weight in the block holding pos
-      const int kp = pos / BR;
-      if (prepared != kp) ok = prep(kp);
-      if (ok) {
-        __syncwarp();
-        acc = __fadd_rn(acc, __fmul_rn(lds_f1(wb0 + 4u * (unsigned)((kp & 1) * BR + pos - kp * BR)),
-                                       vpos));
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(qv0 + (unsigned)kp), rel);
+      __syncwarp();
+      const int ncache = max(0, min(BR, pos - base));   // rows of this block from the cache
+      const unsigned vsl = sl + (unsigned)(lane * (int)sizeof(KT));
+      int r = 0;
+#pragma unroll 1
+      for (; r + 32 <= ncache; r += 32) {            // whole 32-row chunks
+        const unsigned vb = vsl + (unsigned)(r * kRowB), wb4 = wsh + 4u * (unsigned)r;
+        float v[32], w[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) v[x] = slot_elem<KT>(vb + (unsigned)(x * kRowB));
+#pragma unroll
+        for (int x = 0; x < 32; x += 4) {
+          const float4 w4 = lds_f4(wb4 + 4u * (unsigned)x);
+          w[x] = w4.x; w[x + 1] = w4.y; w[x + 2] = w4.z; w[x + 3] = w4.w;
+        }
+#pragma unroll
+        for (int x = 0; x < 32; ++x) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
       }
+      if (r < ncache) {                              // the block's last cached rows
+        float v[32], w[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x)
+          v[x] = slot_elem<KT>(vsl + (unsigned)(min(r + x, BR - 1) * kRowB));
+#pragma unroll
+        for (int x = 0; x < 32; x += 4) {
+          const float4 w4 = lds_f4(wsh + 4u * min(r + x, BR - 4));
+          w[x] = w4.x; w[x + 1] = w4.y; w[x + 2] = w4.z; w[x + 3] = w4.w;
+        }
+#pragma unroll
+        for (int x = 0; x < 32; ++x)
+          if (r + x < ncache) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
+      }
+      if (pos >= base && pos < base + BR)            // the last row: this step's v
+        acc = __fadd_rn(acc, __fmul_rn(lds_f1(wsh + 4u * (pos - base)), vpos));
+      // the slot was written (w) by the generic proxy: order that before the producer's
+      // next bulk copy into it
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
     }
+    if (warp == 0 && lane == 0) S.ctx_wait_ns += S.wait[0];
     if (ok) {
       // ctx element (head g GS + i, dim 32 jsl + lane) -> int8 + (scale, sum) of its block
       const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;

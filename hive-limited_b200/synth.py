@@ -44,6 +44,12 @@ ARCH = {
                       num_attention_heads=64, num_key_value_heads=8, head_dim=128,
                       vocab_size=151936, rope_theta=1000000.0, rms_norm_eps=1e-6,
                       tie_word_embeddings=False, eos_token_id=None),
+    # the 8B layer shapes with 2 layers: a small case of the same kernels for profiler
+    # captures (every launch holds well under the device's memory)
+    "qwen3-8b-2l": dict(num_hidden_layers=2, hidden_size=4096, intermediate_size=12288,
+                        num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                        vocab_size=151936, rope_theta=1000000.0, rms_norm_eps=1e-6,
+                        tie_word_embeddings=False, eos_token_id=None),
 }
 
 # Named workloads: architecture, weight seed, prompt length, tokens generated.
@@ -51,6 +57,7 @@ WORKLOADS = {
     "qwen3-1.7b-p32-g64": ("qwen3-1.7b", 0, 32, 64),
     "qwen3-8b-p4096-g256": ("qwen3-8b", 2, 4096, 256),
     "qwen3-32b-p2048-g256": ("qwen3-32b", 3, 2048, 256),
+    "qwen3-8b-2l-p4096-g16": ("qwen3-8b-2l", 2, 4096, 16),
 }
 
 # The isolated GEMV sweep (N x K), weights from seed 1.
