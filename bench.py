@@ -181,18 +181,16 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(name: str):
-    """dram bytes per launch of the fused step, from the committed ncu summary."""
-    p = REPO / "profiles" / name
-    if not p.exists():
+def profiled_traffic(bytes_per_step: float):
+    """DRAM bytes per launch of the fused step: the ratio of ncu's DRAM bytes to the
+    algorithmic bytes, measured on a small case of the same kernel
+    (profiles/k_step_traffic.json), applied to this workload's algorithmic bytes."""
+    p = REPO / "profiles" / "k_step_traffic.json"
+    try:
+        ratio = float(json.loads(p.read_text())["traffic_over_algorithmic"])
+    except (OSError, ValueError, KeyError):
         return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_step_full_workload:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+    return ratio * bytes_per_step
 
 
 def step_bytes(cfg, head_rows: int, pos: int, kv_elem: int = 4) -> int:
@@ -447,9 +445,9 @@ def run_ours(args, dist: Dist):
     bytes_mean = float(np.mean([step_bytes(cfg, head_rows, p, kv_elem) for p in positions]))
     peak, peak_kind = measured_peak()
     achieved = bytes_mean / (ms_per_step / 1e3) / 1e9
-    # the committed ncu capture is of the f32-cache step
-    traffic = (None if sharded or args.kv_dtype != "f32" or args.eager
-               else profiled_traffic("k_step_qwen3-8b_decode.md"))
+    # the committed ncu capture is of the one-GPU f32-cache step over pp tiles
+    traffic = (None if sharded or args.kv_dtype != "f32" or args.eager or args.gemv_layout != "pp"
+               else profiled_traffic(bytes_mean))
 
     if args.profile and dist.rank == 0:
         # one extra step with the per-phase device trace, at the next decode position

@@ -70,55 +70,80 @@ def unpack_w4(packed: np.ndarray, k: int) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------
-# safetensors (engine/limited.py:79-131): a minimal reader, no torch
+# safetensors reader (the public file format: an 8-byte little-endian header size, a
+# JSON header mapping each tensor name to {dtype, shape, data_offsets}, then the raw
+# tensor bytes). The module keeps the reference engine's names (SafeTensors with keys()
+# and get(), load_model_tensors) because limited.Engine and its callers import them.
 # ---------------------------------------------------------------------------
 
-_ST_DTYPES = {
-    "F32": np.float32, "F16": np.float16, "BF16": np.uint16,
-    "I8": np.int8, "U8": np.uint8, "I32": np.int32, "I64": np.int64,
-}
+# numpy element type of each safetensors dtype tag; BF16 is read as its 16 raw bits and
+# widened to float32 (bf16 is the top half of an f32)
+_NP_OF_TAG = {"F64": np.float64, "F32": np.float32, "F16": np.float16, "BF16": np.uint16,
+              "I64": np.int64, "I32": np.int32, "I16": np.int16, "I8": np.int8,
+              "U8": np.uint8, "BOOL": np.bool_}
+
+
+def _read_index(path: Path) -> tuple[dict, int]:
+    """The header's tensor entries and the file offset where tensor data begins; every
+    entry's byte range is checked against its dtype and shape and against the file."""
+    size = path.stat().st_size
+    with open(path, "rb") as fh:
+        prefix = fh.read(8)
+        if len(prefix) != 8:
+            raise ValueError(f"{path}: not a safetensors file (no header size)")
+        hlen = int.from_bytes(prefix, "little")
+        if hlen <= 0 or 8 + hlen > size:
+            raise ValueError(f"{path}: header size {hlen} does not fit the file")
+        header = json.loads(fh.read(hlen))
+    base = 8 + hlen
+    index = {}
+    for name, entry in header.items():
+        if name == "__metadata__":
+            continue
+        tag, shape, (lo, hi) = entry["dtype"], list(entry["shape"]), entry["data_offsets"]
+        if tag not in _NP_OF_TAG:
+            raise ValueError(f"{name}: unsupported dtype {tag}")
+        count = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        if hi - lo != count * np.dtype(_NP_OF_TAG[tag]).itemsize or base + hi > size:
+            raise ValueError(f"{name}: data range {lo}..{hi} does not match {tag}{shape}")
+        index[name] = (tag, tuple(shape), lo)
+    return index, base
 
 
 class SafeTensors:
-    """Read-only view over a .safetensors file. Header is JSON; tensors are raw bytes."""
+    """Tensors of one .safetensors file, mapped read-only (no copy until a tensor is
+    widened or written to)."""
 
     def __init__(self, path):
         self.path = Path(path)
-        with open(self.path, "rb") as fh:
-            (header_len,) = struct.unpack("<Q", fh.read(8))
-            self.header = json.loads(fh.read(header_len).decode("utf-8"))
-        self._data_start = 8 + header_len
+        self._index, self._base = _read_index(self.path)
+        self._map = np.memmap(self.path, dtype=np.uint8, mode="r")
 
     def keys(self) -> list[str]:
-        return [k for k in self.header if k != "__metadata__"]
+        return list(self._index)
 
     def get(self, name: str) -> np.ndarray:
-        meta = self.header[name]
-        dtype_name = meta["dtype"]
-        if dtype_name not in _ST_DTYPES:
-            raise ValueError(f"{name}: unsupported dtype {dtype_name}")
-        begin, end = meta["data_offsets"]
-        with open(self.path, "rb") as fh:
-            fh.seek(self._data_start + begin)
-            raw = fh.read(end - begin)
-        arr = np.frombuffer(raw, dtype=_ST_DTYPES[dtype_name]).reshape(meta["shape"])
-        if dtype_name == "BF16":
-            arr = (arr.astype(np.uint32) << 16).view(np.float32)
+        tag, shape, lo = self._index[name]
+        dt = np.dtype(_NP_OF_TAG[tag])
+        count = int(np.prod(shape, dtype=np.int64)) if shape else 1
+        start = self._base + lo
+        arr = self._map[start:start + count * dt.itemsize].view(dt).reshape(shape)
+        if tag == "BF16":
+            return (arr.astype(np.uint32) << 16).view(np.float32)
         return arr
 
 
 def load_model_tensors(model_dir) -> dict[str, np.ndarray]:
-    """Load every tensor from a directory of .safetensors shards."""
-    model_dir = Path(model_dir)
-    shards = sorted(model_dir.glob("*.safetensors"))
-    if not shards:
+    """Every tensor of every .safetensors file in a model directory (files in name
+    order; a name that appears twice keeps its last file's tensor)."""
+    files = sorted(Path(model_dir).glob("*.safetensors"))
+    if not files:
         raise FileNotFoundError(f"no .safetensors files in {model_dir}")
-    tensors: dict[str, np.ndarray] = {}
-    for shard in shards:
-        st = SafeTensors(shard)
-        for key in st.keys():
-            tensors[key] = st.get(key)
-    return tensors
+    out: dict[str, np.ndarray] = {}
+    for f in files:
+        st = SafeTensors(f)
+        out.update((name, st.get(name)) for name in st.keys())
+    return out
 
 
 def save_safetensors(path, tensors: dict[str, np.ndarray]) -> None:
