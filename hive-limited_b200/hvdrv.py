@@ -63,6 +63,12 @@ _SIGS = {
     "hv_upload_async": [_VP, _VP, _SZ, _VP],
     "hv_download_async": [_VP, _VP, _SZ, _VP],
     "hv_copy_async": [_VP, _VP, _SZ, _VP],
+    "hv_comm_init": [_I, C.POINTER(_I), C.POINTER(_VP)],
+    "hv_comm_unique_id": [_VP],
+    "hv_comm_init_rank": [_I, _I, _VP, _I, C.POINTER(_VP)],
+    "hv_allgather": [_VP, C.POINTER(_VP), C.POINTER(_VP), _SZ, C.POINTER(_VP)],
+    "hv_comm_size": [_VP, C.POINTER(_I), C.POINTER(_I)],
+    "hv_comm_destroy": [_VP],
     "hv_stream_create": [C.POINTER(_VP)],
     "hv_stream_destroy": [_VP],
     "hv_stream_synchronize": [_VP],
@@ -406,6 +412,51 @@ def ipc_handle(ptr) -> bytes:
     """64-byte CUDA IPC handle of a device allocation made by this process."""
     buf = C.create_string_buffer(IPC_HANDLE_BYTES)
     _call("hv_ipc_handle", _p(ptr), buf)
+    return buf.raw
+
+
+COMM_ID_BYTES = 128
+
+
+class Comm:
+    """The C ABI's all-gather communicator (hv_comm_*): Comm(devs=[0, 1]) drives several
+    GPUs from this process; Comm(nranks=, rank=, uid=, dev=) is one rank of a
+    one-process-per-GPU job (uid from comm_unique_id() on one rank, passed to all)."""
+
+    def __init__(self, devs=None, nranks=None, rank=None, uid=None, dev=None):
+        self.ptr = _VP()
+        if devs is not None:
+            arr = (_I * len(devs))(*devs)
+            _call("hv_comm_init", len(devs), arr, C.byref(self.ptr))
+            self.ndev = len(devs)
+        else:
+            _call("hv_comm_init_rank", nranks, rank,
+                  C.create_string_buffer(uid, COMM_ID_BYTES), dev, C.byref(self.ptr))
+            self.ndev = 1
+
+    def size(self):
+        n, d = _I(), _I()
+        _call("hv_comm_size", self.ptr, C.byref(n), C.byref(d))
+        return n.value, d.value
+
+    def allgather(self, send, recv, nbytes, streams=None):
+        """recv[i] <- every rank's nbytes of send, rank after rank (device i of this
+        process); asynchronous on streams[i] (default stream when None)."""
+        n = self.ndev
+        s = (_VP * n)(*[int(x) for x in send])
+        r = (_VP * n)(*[int(x) for x in recv])
+        st = (_VP * n)(*[int(x) for x in streams]) if streams else None
+        _call("hv_allgather", self.ptr, s, r, nbytes, st)
+
+    def destroy(self):
+        if self.ptr:
+            _call("hv_comm_destroy", self.ptr)
+            self.ptr = _VP()
+
+
+def comm_unique_id() -> bytes:
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    _call("hv_comm_unique_id", buf)
     return buf.raw
 
 

@@ -86,6 +86,28 @@ int hv_ipc_handle(const void* dev_ptr, void* handle_out);
 int hv_ipc_open(const void* handle, void** dev_ptr);
 int hv_ipc_close(void* dev_ptr);
 
+/* The column-parallel layout's all-gather as a collective (NCCL over NVLink/NVSwitch),
+ * for callers outside the fused step (which exchanges its slices itself): every rank
+ * contributes `bytes` and every rank receives all contributions, rank after rank. No
+ * counterpart in the reference (it has no multi-GPU path); the collective that a sharded
+ * deployment of its GEMV (engine/limited.py:364-372) needs between layers.
+ *   hv_comm_init       one process driving ndev GPUs (devs[i], rank i)
+ *   hv_comm_unique_id  an id (HV_COMM_ID_BYTES) made on one rank, handed to every rank
+ *   hv_comm_init_rank  one process per GPU: rank `rank` of `nranks` on device `dev`
+ *   hv_allgather       send[i] / recv[i] / streams[i] for each device the process drives
+ *                      (recv[i] holds nranks * bytes); asynchronous on the streams
+ *   hv_comm_size       ranks of the communicator, devices this process drives
+ *   hv_comm_destroy    frees the communicator (NULL is a no-op) */
+#define HV_COMM_ID_BYTES 128
+typedef struct hv_comm hv_comm;
+int hv_comm_init(int ndev, const int* devs, hv_comm** out);
+int hv_comm_unique_id(void* id_out);
+int hv_comm_init_rank(int nranks, int rank, const void* id, int dev, hv_comm** out);
+int hv_allgather(hv_comm* comm, const void* const* send, void* const* recv, size_t bytes,
+                 void* const* streams);
+int hv_comm_size(const hv_comm* comm, int* nranks, int* ndev);
+int hv_comm_destroy(hv_comm* comm);
+
 /* ---- streams, graphs, events (engine/cudrv.py:226-266) --------------------------- */
 
 int hv_stream_create(void** stream);                          /* cudrv.stream_create :226-230 */
