@@ -35,6 +35,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import struct
 import subprocess
 import sys
 import threading
@@ -56,55 +57,120 @@ UNIT = "tok/s"
 
 
 # ---------------------------------------------------------------------------
-# distributed plumbing (torch.distributed over gloo for host-side barrier and max)
+# distributed plumbing (host-side barrier, max and all-gather over TCP, stdlib only)
 # ---------------------------------------------------------------------------
 
+def _recv_exact(sock, n: int) -> bytes:
+    buf = bytearray()
+    while len(buf) < n:
+        chunk = sock.recv(n - len(buf))
+        if not chunk:
+            raise ConnectionError("a rank closed its connection")
+        buf += chunk
+    return bytes(buf)
+
+
+def _send_msg(sock, payload: bytes):
+    sock.sendall(struct.pack("<Q", len(payload)) + payload)
+
+
+def _recv_msg(sock) -> bytes:
+    return _recv_exact(sock, struct.unpack("<Q", _recv_exact(sock, 8))[0])
+
+
 class Dist:
+    """The ranks of one `torchrun` job on one node, with the standard library only: rank 0
+    serves a TCP socket on MASTER_ADDR, port HV_BENCH_PORT or else MASTER_PORT + 1
+    (torchrun's own store holds MASTER_PORT), and every collective is an all-gather of one
+    bytes object per rank through it. A rank that leaves closes its socket, so the others'
+    next collective raises instead of waiting; so does a silent rank after `timeout_s`."""
+
     def __init__(self, timeout_s: float = 600.0):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = None
+        self.timeout = timeout_s
+        self.peers = []           # rank 0: the sockets of ranks 1 .. world - 1, in order
+        self.sock = None          # other ranks: the socket to rank 0
         if self.world > 1:
-            import datetime
+            self._connect()
 
-            import torch.distributed as dist
-            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=timeout_s))
-            self.pg = dist
-
-    def barrier(self):
-        if self.pg:
-            self.pg.barrier()
-
-    def max(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
+    def _connect(self):
+        import socket
+        addr = os.environ.get("MASTER_ADDR", "127.0.0.1")
+        port = int(os.environ.get("HV_BENCH_PORT")
+                   or int(os.environ.get("MASTER_PORT", "29500")) + 1)
+        deadline = time.monotonic() + self.timeout
+        if self.rank == 0:
+            srv = socket.create_server((addr, port))
+            srv.settimeout(self.timeout)
+            got = {}
+            try:
+                while len(got) < self.world - 1:
+                    c, _ = srv.accept()
+                    c.settimeout(self.timeout)
+                    got[struct.unpack("<i", _recv_exact(c, 4))[0]] = c
+            except BaseException:
+                for c in got.values():
+                    c.close()
+                raise
+            finally:
+                srv.close()
+            self.peers = [got[r] for r in range(1, self.world)]
+            return
+        while True:
+            try:
+                s = socket.create_connection((addr, port), timeout=5.0)
+                break
+            except OSError:
+                if time.monotonic() > deadline:
+                    raise TimeoutError(f"rank {self.rank}: no rank 0 at {addr}:{port}")
+                time.sleep(0.2)
+        s.settimeout(self.timeout)
+        s.sendall(struct.pack("<i", self.rank))
+        self.sock = s
 
     def allgather_bytes(self, blob: bytes) -> list[bytes]:
-        """All-gather of one bytes object per rank (host plumbing: the sharded engine's
-        one swap of CUDA IPC handles)."""
-        if not self.pg:
+        """One bytes object per rank, in rank order, on every rank (also the sharded
+        engine's one swap of CUDA IPC handles)."""
+        if self.world == 1:
             return [blob]
-        out = [None] * self.world
-        self.pg.all_gather_object(out, blob)
-        return out
+        try:
+            if self.rank == 0:
+                parts = [blob] + [_recv_msg(c) for c in self.peers]
+                out = struct.pack("<i", len(parts)) + b"".join(
+                    struct.pack("<Q", len(p)) + p for p in parts)
+                for c in self.peers:
+                    _send_msg(c, out)
+                return parts
+            _send_msg(self.sock, blob)
+            out = _recv_msg(self.sock)
+        except BaseException:
+            self.close()              # the other ranks' next collective fails too
+            raise
+        n, off, parts = struct.unpack_from("<i", out)[0], 4, []
+        for _ in range(n):
+            ln = struct.unpack_from("<Q", out, off)[0]
+            parts.append(out[off + 8:off + 8 + ln])
+            off += 8 + ln
+        return parts
+
+    def barrier(self):
+        self.allgather_bytes(b"")
+
+    def max(self, x: float) -> float:
+        return max(struct.unpack("<d", b)[0] for b in self.allgather_bytes(struct.pack("<d", x)))
+
+    def sum(self, x: float) -> float:
+        return sum(struct.unpack("<d", b)[0] for b in self.allgather_bytes(struct.pack("<d", x)))
 
     def close(self):
-        if self.pg:
-            self.pg.destroy_process_group()
+        for c in self.peers + ([self.sock] if self.sock else []):
+            try:
+                c.close()
+            except OSError:
+                pass
+        self.peers, self.sock = [], None
 
 
 # ---------------------------------------------------------------------------

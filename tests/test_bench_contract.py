@@ -140,14 +140,14 @@ def test_reference_line_carries_the_contract(monkeypatch, capsys):
 
 
 def _rank_bench(rank, world, port, mode, result):
-    """One rank of `bench.py --gpus 2` on the CPU: gloo plumbing, fake driver and engine
+    """One rank of `bench.py --gpus 2` on the CPU: TCP plumbing, fake driver and engine
     (each rank's device time differs, so the max over ranks is visible)."""
     import contextlib
     import io
     sys.path[:0] = [p for p in (os.path.join(REPO, "hive-limited_b200"),
                                 os.path.join(REPO, "oracle"), REPO, TESTS) if p not in sys.path]
     os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world),
-                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), HV_BENCH_PORT=str(port))
     try:
         import bench as b
         import limited

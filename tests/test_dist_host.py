@@ -1,5 +1,5 @@
-"""The multi-rank host path on CPU: two ranks (spawned processes) over torch.distributed
-gloo, as bench.py --gpus 2 runs them (barrier, max over ranks, sum, the all-gather of
+"""The multi-rank host path on CPU: two ranks (spawned processes) over bench.Dist's TCP
+plumbing, as bench.py --gpus 2 runs them (barrier, max over ranks, sum, the all-gather of
 bytes that carries the sharded engine's one swap of CUDA IPC handles), and the
 cross-rank half of the vocabulary-sharded greedy argmax: each rank folds its shard of
 the logits into a 64-bit key, the keys are all-gathered, and every rank picks the same
@@ -32,7 +32,7 @@ def _paths():
 
 def _env(rank, world, port):
     os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world),
-                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), HV_BENCH_PORT=str(port))
 
 
 def _rank_main(rank, world, port, result):
@@ -41,6 +41,7 @@ def _rank_main(rank, world, port, result):
         _env(rank, world, port)
         import bench
         import hvdrv
+        assert "torch" not in sys.modules          # the bench's plumbing is stdlib only
         from test_argmax_key import keys_of
         d = bench.Dist(timeout_s=60)
         out = {}
@@ -107,7 +108,7 @@ def _spawn(target, world=2, timeout=120):
                 p.kill()
 
 
-def test_two_gloo_ranks_plumbing_and_sharded_argmax():
+def test_two_ranks_plumbing_and_sharded_argmax():
     out = _spawn(_rank_main)
     for rank in (0, 1):
         o = out[rank]
