@@ -63,6 +63,23 @@ static_assert(sizeof(hv_layer_w) % 8 == 0, "layer table copied as 8-byte words")
 static_assert(kSlotRows % 4 == 0, "attention groups of 4 rows never straddle slots");
 static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention block");
 
+// Phase B (the context) runs one item per (query head, 32-dim slice): a chain warp adds
+// the products w_t v_t[d] of its 32 dims position after position, while helper warps of
+// the same CTA form those products from the ring's V rows and the head's exps and hand
+// them over transposed, so that the chain reads four positions per 16-byte load.
+constexpr int kCtxRows = 64;                           // V rows per phase-B slot
+constexpr int kCtxHelpers = 4;                         // helper warps: 1, 2, 3 and 5
+constexpr int kCtxHelperRows = kCtxRows / kCtxHelpers; // rows of a slot per helper
+constexpr int kCtxPStride = kCtxRows + 4;              // floats per dim in a products buffer
+constexpr int kCtxPBufs = 2;                           // products buffers (double-buffered)
+constexpr int kCtxPFloats = 32 * kCtxPStride;          // one products buffer
+static_assert(kCtxPBufs == 2, "StepShared holds two products-buffer barrier pairs");
+static_assert(kCtxRows * (32 * 4 + 4) <= kSlotBytes, "a phase-B slot: V rows + exps");
+static_assert(kCtxHelperRows % 4 == 0 && kConsWarps / kCtxHelpers * kCtxHelpers == kConsWarps,
+              "helpers split a slot into 4-row groups and share the slot's release");
+static_assert((kCtxPStride / 4) % 2 == 1, "products buffer: conflict-free 16-byte loads");
+
+
 // Run-time tunables (hv_step_set_option): bulk copies a producer keeps in flight, and
 // whether streamed bytes are marked evict-first in L2. Copies beyond what saturates HBM
 // only queue in front of the consumers' own (latency-critical) loads.
@@ -100,8 +117,11 @@ struct StepShared {
   unsigned gen;                  // sharded: generation of the local release word
   unsigned long long wait[kConsWarps];   // ns each consumer warp waited for ring slots
   long long busy[kConsWarps];            // cycles spent computing attention scores
-  unsigned long long ctx_wait_ns;        // phase B, whole launch: ns warp 0 waited for V slots
-  unsigned long long ctx_sum_ns;         // phase B, whole launch: ns of the exps + leaf sums
+  unsigned long long ctx_wait_ns;        // phase B, whole launch: ns the chain waited for products
+  unsigned long long ctx_sum_ns;         // phase B, whole launch: ns helper 0 waited for V slots
+  uint64_t pfull[2];             // phase B: products buffer b written (one arrive per helper)
+  uint64_t pfree[2];             // phase B: products buffer b read by the chain (one arrive)
+  unsigned pseq;                 // phase B: products buffers used so far in this launch
 };
 
 // Byte offsets of the dynamic shared memory regions (host and device agree).
@@ -112,15 +132,15 @@ struct StepLayout {
 HV_HD size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Floats of the attention work area: phase A (q rows, this step's k and v rows, the
-// norm scratch, the chunk's scores) or phase B (node values of the pairwise tree per
-// head, a 4-block ring of weights per head, the per-head maxima and sums), whichever is
-// larger.
+// norm scratch, the chunk's scores, the chunk's pairwise tree per head) or phase B (the
+// chunks' sums, S, two products buffers, the helpers' weights), whichever is larger.
 HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
   const size_t cm = (size_t)front_chunk_max(cap, nch);
   const size_t nvl = ((size_t)pw_tree_nodes_max((int)cm) + 3) & ~size_t(3);
   const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 8 +
                    ((cm * gs + 3) & ~size_t(3)) + (size_t)gs * nvl;
-  const size_t b = (((size_t)gs * nch + 3) & ~size_t(3)) + 8;
+  const size_t b = (((size_t)nch + 3) & ~size_t(3)) + 4 + (size_t)kCtxPBufs * kCtxPFloats +
+                   (size_t)kCtxHelpers * kCtxHelperRows;
   return a > b ? a : b;
 }
 
@@ -392,22 +412,21 @@ HV_DEV void prefetch_vectors(const hv_layer_w* L, int hid, bool attn) {
 }
 
 
-// The phase-B item of CTA b (kv head * 4 + slice), or -1: items spread over the grid.
-HV_DEV int ctx_item(int b, int grid, int nitems) {
+// Helper index of consumer warp w (warps 1, 2, 3, 5: SM sub-partitions 1-3, none beside
+// the chain warp 0), or -1.
+HV_DEV int ctx_helper(int w) { return w >= 1 && w <= 3 ? w - 1 : w == 5 ? 3 : -1; }
+
+// The j-th phase-B item of CTA b, or -1. Up to one item per CTA the items spread over the
+// grid; past that CTA b takes items b, b + grid, b + 2 grid, ...
+HV_DEV int ctx_item(int b, int grid, int nitems, int j) {
+  if (nitems > grid) {
+    const long long k = (long long)j * grid + b;
+    return k < nitems ? (int)k : -1;
+  }
+  if (j > 0) return -1;
   const int k = (int)(((long long)b * nitems + grid - 1) / grid);
   return (k < nitems && (int)(((long long)k * grid) / nitems) == b) ? k : -1;
 }
-
-// Rows of a phase-B slot: the V slice of BR positions (32 dims of KT) plus the GS heads'
-// exps of the same positions fill at most one slot; BR is a multiple of 32.
-template <class KT, int GS>
-constexpr int vrows_fit() {
-  int br = 32;
-  while ((br + 32) * (32 * (int)sizeof(KT) + 4 * GS) <= kSlotBytes) br += 32;
-  return br;
-}
-template <class KT, int GS>
-constexpr int kVRowsG = vrows_fit<KT, GS>();
 
 // Rows [t0, t1) of chunk c of the launch's frontier (empty past its last chunk), and te:
 // rows [t0, te) come from the cache, row pos (if in the chunk) from this step's qkv.
@@ -476,9 +495,9 @@ struct Producer {
     policy = hint ? policy_evict_first() : 0ull;
   }
 
-  // Waits until the next slot's previous contents were released and until fewer than
-  // `inflight` earlier copies are still in flight; false if the wait gave up.
-  HV_DEV bool claim() {
+  // Waits until the next slot's previous contents were released and (cap) until fewer
+  // than `inflight` earlier copies are still in flight; false if the wait gave up.
+  HV_DEV bool claim(bool cap = true) {
     if (!live) return false;
     if (q >= (unsigned)R.ns && !mbar_probe(R.empty_of(q), R.parity(q) ^ 1u)) {
       const unsigned long long t0 = global_ns();
@@ -488,7 +507,7 @@ struct Producer {
       }
       t_empty += global_ns() - t0;
     }
-    if (q >= inflight) {
+    if (cap && q >= inflight) {
       const unsigned p = q - inflight;
       if (!mbar_probe(R.full_of(p), R.parity(p))) {
         const unsigned long long t0 = global_ns();
@@ -573,49 +592,48 @@ struct Producer {
                    : "memory");
   }
 
-  // The slot of sequence number qs gets its exps part: GS rows of BR floats.
-  HV_DEV void epart(unsigned qs, const float* e0, int ew, int gs, int br, unsigned voff) {
+  // The slot of sequence number qs gets its exps part: `bytes` from e0, at byte voff.
+  HV_DEV void epart(unsigned qs, const float* e0, unsigned bytes, unsigned voff) {
     unsigned char* dst = R.slot(qs) + voff;
     uint64_t* full = R.full_of(qs);
-    for (int i = 0; i < gs; ++i) {
-      if (hint) bulk_load_hint(dst + i * br * 4, e0 + (size_t)i * ew, (unsigned)br * 4, full, policy);
-      else bulk_load(dst + i * br * 4, e0 + (size_t)i * ew, (unsigned)br * 4, full);
-    }
+    if (hint) bulk_load_hint(dst, e0, bytes, full, policy);
+    else bulk_load(dst, e0, bytes, full);
   }
 
-  // Non-blocking claim: true if the next slot is free and the in-flight limit allows a
-  // copy now.
-  HV_DEV bool try_claim() {
+  // Non-blocking claim: true if the next slot is free (and, cap, the in-flight limit
+  // allows a copy now).
+  HV_DEV bool try_claim(bool cap = true) {
     if (!live) return false;
     if (q >= (unsigned)R.ns && !mbar_probe(R.empty_of(q), R.parity(q) ^ 1u)) return false;
-    if (q >= inflight && !mbar_probe(R.full_of(q - inflight), R.parity(q - inflight)))
+    if (cap && q >= inflight && !mbar_probe(R.full_of(q - inflight), R.parity(q - inflight)))
       return false;
     return true;
   }
 
-  // The phase-B slots of kv head g, slice x0 / 32: V rows y0 + k BR ... and the GS heads'
-  // exps e0 + k BR ..., for blocks k < nblk. V parts of the first blocks go out while
-  // slots are free without waiting; the exps only once every chunk of the kv head has
-  // written them (the second ticket `tk` reaches `want`).
-  template <class KT, int GS>
-  HV_DEV void ctx_slots(const CUtensorMap* vmap, int x0, int y0, const float* e0, int ew,
-                        int nblk, const int32_t* tk, unsigned want) {
-    constexpr int BR = kVRowsG<KT, GS>;
-    constexpr unsigned kVB = BR * 32 * sizeof(KT), kTot = kVB + GS * BR * 4;
+  // The phase-B slots of one item (a query head and a 32-dim slice x0 .. x0 + 31 of its kv
+  // head's V rows from row y0): per block k < nblk, kCtxRows V rows and the head's exps
+  // e0 + k kCtxRows .... V parts of the first blocks go out while slots are free without
+  // waiting; the exps only once every chunk of the kv head has written them (the second
+  // ticket `tk` reaches `want`). The chain consumes a slot in a few hundred cycles, far
+  // less than a copy's latency, so these copies take the whole ring (no in-flight cap).
+  template <class KT>
+  HV_DEV void ctx_slots(const CUtensorMap* vmap, int x0, int y0, const float* e0, int nblk,
+                        const int32_t* tk, unsigned want) {
+    constexpr unsigned kVB = kCtxRows * 32 * sizeof(KT), kEB = kCtxRows * 4;
     const unsigned qb = q;
     int k = 0;
-    for (; k < nblk && try_claim(); ++k, ++q) vpart(vmap, x0, y0 + k * BR, kTot);
+    for (; k < nblk && try_claim(false); ++k, ++q) vpart(vmap, x0, y0 + k * kCtxRows, kVB + kEB);
     if (!live) return;
     if (!wait_count(tk, want, status)) {
       live = false;
       return;
     }
     asm volatile("fence.proxy.async.global;" ::: "memory");   // exps written by other SMs
-    for (int kk = 0; kk < k; ++kk) epart(qb + kk, e0 + (size_t)kk * BR, ew, GS, BR, kVB);
+    for (int kk = 0; kk < k; ++kk) epart(qb + kk, e0 + (size_t)kk * kCtxRows, kEB, kVB);
     for (; k < nblk && live; ++k) {
-      if (!claim()) return;
-      vpart(vmap, x0, y0 + k * BR, kTot);
-      epart(q, e0 + (size_t)k * BR, ew, GS, BR, kVB);
+      if (!claim(false)) return;
+      vpart(vmap, x0, y0 + k * kCtxRows, kVB + kEB);
+      epart(q, e0 + (size_t)k * kCtxRows, kEB, kVB);
       ++q;
     }
   }
@@ -643,7 +661,7 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
   const int nch = D.attn_chunks;
   const int it_hid = pp_iters(hid / kBlock), it_q = pp_iters(qdim / kBlock),
             it_ffn = pp_iters(ffn * world / kBlock);
-  const int citem = ctx_item(blockIdx.x, gridDim.x, D.n_kv * kSlices);
+  const int nitems = D.n_head * kSlices;
   const long long rowb = (long long)kHd * sizeof(KT);
   int off = 0, t0, t1;
   for (int l = 0; l < D.n_layer && P.live; ++l) {
@@ -655,15 +673,16 @@ HV_DEV void produce(const hv_step_desc& D, const hv_layer_w* Ls, int flags, int 
       front_rows(S.front, pos, blockIdx.x % nch, &a0, &a1, &ae);
       P.krows(reinterpret_cast<const KT*>(L->kc), blockIdx.x / nch, D.cap, a0, ae);
     }
-    if (citem >= 0) {                                // this CTA's context item
-      const int g = citem / kSlices;
+    for (int j = 0; P.live; ++j) {                   // this CTA's context items
+      const int item = ctx_item(blockIdx.x, gridDim.x, nitems, j);
+      if (item < 0) break;
+      const int h = item / kSlices, g = h / GS;
       const long long vrow = ((const char*)L->vc - (const char*)D.kv_base) / rowb +
                              (long long)g * D.cap;
       const StepScratch X = step_scratch(D);
-      constexpr int BR = kVRowsG<KT, GS>;
-      P.ctx_slots<KT, GS>(vmap, 32 * (citem % kSlices), (int)vrow,
-                          X.exps + (size_t)g * GS * X.ew, X.ew, (pos + BR) / BR,
-                          D.ticket + D.n_kv + g, (unsigned)((l + 1) * nch));
+      P.ctx_slots<KT>(vmap, 32 * (item % kSlices), (int)vrow, X.exps + (size_t)h * X.ew,
+                      (pos + kCtxRows) / kCtxRows, D.ticket + D.n_kv + g,
+                      (unsigned)((l + 1) * nch));
     }
     phase_tiles(pp_tiles(hrows, 0), &off, &t0, &t1);
     P.gemv(L->o_b4, L->o_sw, it_q, t0, t1, S.P.gv_o.nleaf);
@@ -944,6 +963,10 @@ HV_DEV float lds_f1(unsigned a) {
 }
 HV_DEV void sts_f1(unsigned a, float v) {
   asm volatile("st.shared.f32 [%0], %1;" :: "r"(a), "f"(v) : "memory");
+}
+HV_DEV void sts_f4(unsigned a, float x, float y, float z, float w) {
+  asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" :: "r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
 }
 
 // Block terms of iteration u of a ring slot for the lane's row g: blocks 2t (x) and
@@ -1336,129 +1359,167 @@ __device__ __noinline__ bool attn_scores_ring(const hv_step_desc& D, const hv_la
   return true;
 }
 
-// Phase B of this CTA's (kv head, 32-dim slice) item, if it has one: once every chunk of
-// the kv head has its exps and subtree sums in (the second ticket), S = the top of the
-// recursion over the chunks' sums; then one warp per query head runs the sequential
-// weighted V sum. Block k's ring slot holds V rows [k BR, k BR + BR) (this slice) and the
-// GS heads' exps for the same rows; the warp turns its head's exps into w = e / S in the
-// slot, and takes row pos's v from this step's qkv.
+// Phase B of this CTA's items (query head h, 32-dim slice): once every chunk of h's kv
+// head has its exps and subtree sums in (the second ticket), S = the top of the
+// recursion over the chunks' sums; then the sequential weighted V sum
+// acc_d = (((+0 + w_0 v_0[d]) + w_1 v_1[d]) + ...), w_t = e_t / S, one chain of T adds per
+// output element. Block k's ring slot holds V rows [64 k, 64 k + 64) of the slice and h's
+// exps for the same rows. Helper warps 1, 2, 3, 5 take 16 rows each: they divide the
+// exps by S, form the products (row pos's v from this step's qkv, +0 past it: the chain
+// never holds -0, so +0 terms leave it unchanged), and store them transposed into a
+// products buffer, dim-major, four rows per 16 bytes; warp 0 (the chain) then needs one
+// 16-byte load per four adds. Two products buffers let the helpers fill the next block
+// while the chain adds the current one.
 template <int GS, class KT>
 __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int layer,
                                            const Ring R, unsigned* qp, StepShared& S,
                                            float* area, int tb) {
   const int nkv = D.n_kv, nch = D.attn_chunks, nq = D.n_head;
-  const int item = ctx_item(blockIdx.x, gridDim.x, nkv * kSlices);
-  if (item < 0) return true;
-  constexpr int BR = kVRowsG<KT, GS>;
+  const int nitems = nq * kSlices;
+  constexpr int BR = kCtxRows;
   constexpr int kVB = BR * 32 * (int)sizeof(KT);     // bytes of the V part of a slot
+  constexpr int kRowB = 32 * (int)sizeof(KT);        // bytes of one 32-dim row slice
   const StepScratch X = step_scratch(D);
-  const int g = item / kSlices, jsl = item % kSlices;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hw = ctx_helper(warp);
   const int T = pos + 1;
-  const int nblkv = (T + BR - 1) / BR;
-  const unsigned qv0 = *qp;
-  *qp += (unsigned)nblkv;
-  float* vals = area;                                // [GS][nch] chunk sums
-  float* s_s = vals + (size_t)GS * nch;              // S per head
-  if (threadIdx.x == 0) {
-    S.ok = wait_count(D.ticket + nkv + g, (unsigned)((layer + 1) * nch), D.status);
-    if (!S.ok) *(volatile int*)&S.abort = 1;
-  }
-  csync();
-  if (!S.ok) return false;
-  trace_mark(D, tb + 18);
-  const int nf = S.front.n;
-  for (int e = threadIdx.x; e < GS * nf; e += kConsThreads)
-    vals[e] = __ldcg(X.nsum + (size_t)(g * GS + e / nf) * nch + e % nf);
-  csync();
-  if (threadIdx.x < GS) s_s[threadIdx.x] = pw_front_fold(S.front, vals + threadIdx.x * nf);
-  csync();
+  const int nblk = (T + BR - 1) / BR;
+  const int nch4 = (nch + 3) & ~3;
+  float* vals = area;                                // [nch] the chunks' sums
+  float* s_s = vals + nch4;                          // S
+  float* pbuf = s_s + 4;                             // [kCtxPBufs][32][kCtxPStride]
+  float* wsc = pbuf + kCtxPBufs * kCtxPFloats;       // [kCtxHelpers][16] weights
+  if (ctx_item(blockIdx.x, gridDim.x, nitems, 0) < 0) return true;
   bool ok = true;
-  if (warp < GS) {
-    const int i = warp;
-    const float S_ = s_s[i];
-    float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
-    if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
-    const unsigned rel = (unsigned)(kConsWarps / GS);
-    constexpr int kRowB = 32 * (int)sizeof(KT);      // bytes of one 32-dim row slice
-    if (lane == 0) S.wait[warp] = 0;
-    float acc = 0.0f;
+  for (int j = 0;; ++j) {
+    const int item = ctx_item(blockIdx.x, gridDim.x, nitems, j);
+    if (item < 0) break;
+    const int h = item / kSlices, jsl = item % kSlices, g = h / GS;
+    const unsigned qv0 = *qp;
+    *qp += (unsigned)nblk;
+    if (threadIdx.x == 0) {
+      S.ok = wait_count(D.ticket + nkv + g, (unsigned)((layer + 1) * nch), D.status);
+      if (!S.ok) *(volatile int*)&S.abort = 1;
+    }
+    csync();
+    if (!S.ok) return false;
+    if (j == 0) trace_mark(D, tb + 18);
+    const unsigned u0 = S.pseq;                      // products buffers used before this item
+    const int nf = S.front.n;
+    for (int e = threadIdx.x; e < nf; e += kConsThreads)
+      vals[e] = __ldcg(X.nsum + (size_t)h * nch + e);
+    csync();
+    if (threadIdx.x == 0) {
+      s_s[0] = pw_front_fold(S.front, vals);
+      S.pseq = u0 + (unsigned)nblk;
+    }
+    csync();
+    const float S_ = s_s[0];
+    const unsigned pb = sh_addr(pbuf);
+    if (warp == 0) {
+      // the chain: lane = dim 32 jsl + lane of head h
+      float acc = 0.0f;
+      const unsigned pl = pb + (unsigned)(lane * kCtxPStride * 4);
+      if (lane == 0) S.wait[0] = 0;
 #pragma unroll 1
-    for (int k = 0; k < nblkv && ok; ++k) {
-      const unsigned q = qv0 + (unsigned)k;
-      ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
-      if (!ok) break;
-      const unsigned sl = sh_addr(R.slot(q));
-      const unsigned wsh = sl + (unsigned)(kVB + i * BR * 4);
-      const int base = k * BR;
+      for (int k = 0; k < nblk && ok; ++k) {
+        const unsigned u = u0 + (unsigned)k, b = u % kCtxPBufs;
+        ok = warp_wait(S.pfull + b, (u / kCtxPBufs) & 1u, S, D.status);
+        if (!ok) break;
+        const unsigned a = pl + b * (unsigned)(kCtxPFloats * 4);
+        float4 p[BR / 4];
 #pragma unroll
-      for (int u = 0; u < BR / 32; ++u) {            // w = e / S for the block's rows
-        const int o = 32 * u + lane;
-        if (base + o < T) {
-          const unsigned a = wsh + 4u * (unsigned)o;
-          asm volatile("st.shared.f32 [%0], %1;" :: "r"(a), "f"(__fdiv_rn(lds_f1(a), S_))
-                       : "memory");
+        for (int x = 0; x < BR / 4; ++x) p[x] = lds_f4(a + 16u * (unsigned)x);
+        // the loads above are ordered before this release: the helpers may refill the
+        // buffer while the adds run
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(S.pfree + b, 1);
+#pragma unroll
+        for (int x = 0; x < BR / 4; ++x) {
+          acc = __fadd_rn(acc, p[x].x);
+          acc = __fadd_rn(acc, p[x].y);
+          acc = __fadd_rn(acc, p[x].z);
+          acc = __fadd_rn(acc, p[x].w);
         }
       }
-      __syncwarp();
-      const int ncache = max(0, min(BR, pos - base));   // rows of this block from the cache
-      const unsigned vsl = sl + (unsigned)(lane * (int)sizeof(KT));
-      int r = 0;
+      if (lane == 0) S.ctx_wait_ns += S.wait[0];
+      if (ok) {
+        // ctx element (head h, dim 32 jsl + lane) -> int8 + (scale, sum) of its block
+        const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
+        const int qall = nq * kHd * world;
+        const int idx = (rank * nq + h) * kHd + 32 * jsl + lane;
+        int8_t q8;
+        float sc;
+        int bs;
+        quant_block_warp(acc, lane, &q8, &sc, &bs);
+        const int2 sbv = make_int2(__float_as_int(sc), bs);
+        for (int k = 0; k < world; ++k) {
+          int8_t* cq = reinterpret_cast<int8_t*>(world > 1 ? D.peers->ctx[k] : (void*)D.ctx);
+          cq[idx] = q8;
+          if (lane == 0) reinterpret_cast<int2*>(cq + qall)[idx / kBlock] = sbv;
+        }
+      }
+    } else if (hw >= 0) {
+      // a helper: rows r0 .. r0 + 15 of every block; lane = dim
+      float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
+      if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
+      const int r0 = hw * kCtxHelperRows;
+      const unsigned wl = sh_addr(wsc + hw * kCtxHelperRows);
+      const unsigned pl = pb + (unsigned)((lane * kCtxPStride + r0) * 4);
+      const unsigned rel = (unsigned)(kConsWarps / kCtxHelpers);
+      if (lane == 0) S.wait[warp] = 0;
 #pragma unroll 1
-      for (; r + 32 <= ncache; r += 32) {            // whole 32-row chunks
-        const unsigned vb = vsl + (unsigned)(r * kRowB), wb4 = wsh + 4u * (unsigned)r;
-        float v[32], w[32];
+      for (int k = 0; k < nblk && ok; ++k) {
+        const unsigned q = qv0 + (unsigned)k;
+        const unsigned u = u0 + (unsigned)k, b = u % kCtxPBufs;
+        ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
+        if (!ok) break;
+        const unsigned sl = sh_addr(R.slot(q));
+        const int t0 = k * BR + r0;                  // position of the helper's first row
+        if (lane < kCtxHelperRows) {
+          const float e = lds_f1(sl + (unsigned)(kVB + 4 * (r0 + lane)));
+          sts_f1(wl + 4u * (unsigned)lane, t0 + lane < T ? __fdiv_rn(e, S_) : 0.0f);
+        }
+        __syncwarp();
+        float w[kCtxHelperRows], v[kCtxHelperRows];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = slot_elem<KT>(vb + (unsigned)(x * kRowB));
-#pragma unroll
-        for (int x = 0; x < 32; x += 4) {
-          const float4 w4 = lds_f4(wb4 + 4u * (unsigned)x);
+        for (int x = 0; x < kCtxHelperRows; x += 4) {
+          const float4 w4 = lds_f4(wl + 4u * (unsigned)x);
           w[x] = w4.x; w[x + 1] = w4.y; w[x + 2] = w4.z; w[x + 3] = w4.w;
         }
+        const unsigned vl = sl + (unsigned)(r0 * kRowB + lane * (int)sizeof(KT));
 #pragma unroll
-        for (int x = 0; x < 32; ++x) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
-      }
-      if (r < ncache) {                              // the block's last cached rows
-        float v[32], w[32];
+        for (int x = 0; x < kCtxHelperRows; ++x) v[x] = slot_elem<KT>(vl + (unsigned)(x * kRowB));
+        float p[kCtxHelperRows];
+        if (t0 + kCtxHelperRows <= pos) {            // every row from the cache
 #pragma unroll
-        for (int x = 0; x < 32; ++x)
-          v[x] = slot_elem<KT>(vsl + (unsigned)(min(r + x, BR - 1) * kRowB));
+          for (int x = 0; x < kCtxHelperRows; ++x) p[x] = __fmul_rn(w[x], v[x]);
+        } else {
 #pragma unroll
-        for (int x = 0; x < 32; x += 4) {
-          const float4 w4 = lds_f4(wsh + 4u * min(r + x, BR - 4));
-          w[x] = w4.x; w[x + 1] = w4.y; w[x + 2] = w4.z; w[x + 3] = w4.w;
+          for (int x = 0; x < kCtxHelperRows; ++x) {
+            const int t = t0 + x;
+            p[x] = t < pos ? __fmul_rn(w[x], v[x]) : t == pos ? __fmul_rn(w[x], vpos) : 0.0f;
+          }
         }
+        // the slot is read (the products depend on every load): release it
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
+        if (u >= (unsigned)kCtxPBufs) {
+          ok = warp_wait(S.pfree + b, ((u / kCtxPBufs) & 1u) ^ 1u, S, D.status);
+          if (!ok) break;
+        }
+        const unsigned a = pl + b * (unsigned)(kCtxPFloats * 4);
 #pragma unroll
-        for (int x = 0; x < 32; ++x)
-          if (r + x < ncache) acc = __fadd_rn(acc, __fmul_rn(w[x], v[x]));
+        for (int x = 0; x < kCtxHelperRows; x += 4)
+          sts_f4(a + 4u * (unsigned)x, p[x], p[x + 1], p[x + 2], p[x + 3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(S.pfull + b, 1);
       }
-      if (pos >= base && pos < base + BR)            // the last row: this step's v
-        acc = __fadd_rn(acc, __fmul_rn(lds_f1(wsh + 4u * (pos - base)), vpos));
-      // the slot was written (w) by the generic proxy: order that before the producer's
-      // next bulk copy into it
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
+      if (hw == 0 && lane == 0) S.ctx_sum_ns += S.wait[warp];
     }
-    if (warp == 0 && lane == 0) S.ctx_wait_ns += S.wait[0];
-    if (ok) {
-      // ctx element (head g GS + i, dim 32 jsl + lane) -> int8 + (scale, sum) of its block
-      const int world = D.world > 1 ? D.world : 1, rank = world > 1 ? D.rank : 0;
-      const int qall = nq * kHd * world;
-      const int idx = (rank * nq + g * GS + i) * kHd + 32 * jsl + lane;
-      int8_t q8;
-      float sc;
-      int bs;
-      quant_block_warp(acc, lane, &q8, &sc, &bs);
-      const int2 sbv = make_int2(__float_as_int(sc), bs);
-      for (int k = 0; k < world; ++k) {
-        int8_t* cq = reinterpret_cast<int8_t*>(world > 1 ? D.peers->ctx[k] : (void*)D.ctx);
-        cq[idx] = q8;
-        if (lane == 0) reinterpret_cast<int2*>(cq + qall)[idx / kBlock] = sbv;
-      }
-    }
+    csync();
+    if (!ok || *(volatile int*)&S.abort) return false;
   }
-  csync();
   trace_mark(D, tb + 19);
   return *(volatile int*)&S.abort == 0;
 }
@@ -1505,6 +1566,11 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
     for (int w = 0; w < kConsWarps; ++w) S.wait[w] = 0, S.busy[w] = 0;
     S.ctx_wait_ns = 0;
     S.ctx_sum_ns = 0;
+    for (int b = 0; b < kCtxPBufs; ++b) {
+      mbar_init(S.pfull + b, kCtxHelpers);
+      mbar_init(S.pfree + b, 1);
+    }
+    S.pseq = 0;
   }
   {
     const int* src = reinterpret_cast<const int*>(D.plans);
@@ -1717,15 +1783,6 @@ typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// Rows per phase-B slot for a cache of esz-byte elements and group size gs (kVRowsG).
-static int vslice_rows(int esz, int gs) {
-  if (esz == 2)
-    return gs == 1 ? kVRowsG<__half, 1> : gs == 2 ? kVRowsG<__half, 2>
-         : gs == 4 ? kVRowsG<__half, 4> : kVRowsG<__half, 8>;
-  return gs == 1 ? kVRowsG<float, 1> : gs == 2 ? kVRowsG<float, 2>
-       : gs == 4 ? kVRowsG<float, 4> : kVRowsG<float, 8>;
-}
-
 static int vslice_map(const void* base, long long rows, int esz, int box_rows,
                       CUtensorMap* out) {
   static std::mutex mu;
@@ -1795,9 +1852,6 @@ int hv_step_config(int n_kv, int group, int cap, int* grid, int* threads, size_t
   *threads = kStepThreads;
   HV_REQUIRE(cap <= kExactMaxCap, HV_E_UNSUPPORTED,
              "hv_step_config: cache of %d positions (at most %d)", cap, kExactMaxCap);
-  HV_REQUIRE(n_kv * kSlices <= sms, HV_E_UNSUPPORTED,
-             "hv_step_config: %d kv heads need %d CTAs for the attention context", n_kv,
-             n_kv * kSlices);
   const int nch = 1 << front_depth(n_kv, sms);
   *chunks = nch;
   *part_floats = step_part_floats(n_kv * group, cap, nch);
@@ -1907,14 +1961,14 @@ int hv_step_launch(const hv_step_desc* desc, int flags, void* stream) {
   const int variant = h.w4_layout == HV_W4_DQ ? (f16 ? 4 : 3) : f16 ? 2 : 0;
   HV_REQUIRE(h.cap <= kExactMaxCap, HV_E_UNSUPPORTED, "hv_step_launch: cap %d > %d", h.cap,
              kExactMaxCap);
-  HV_REQUIRE(h.n_kv * kSlices <= sms && h.n_kv * h.attn_chunks <= sms, HV_E_UNSUPPORTED,
+  HV_REQUIRE(h.n_kv * h.attn_chunks <= sms, HV_E_UNSUPPORTED,
              "hv_step_launch: %d kv heads x %d chunks need one CTA per attention item (%d)",
              h.n_kv, h.attn_chunks, sms);
   HV_REQUIRE(h.kv_base != nullptr && h.kv_rows >= (long long)2 * h.n_kv * h.cap &&
                  ((uintptr_t)h.kv_base & 15) == 0,
              HV_E_INVALID, "hv_step_launch: kv_base/kv_rows do not describe the KV cache");
   CUtensorMap vmap;
-  rc = vslice_map(h.kv_base, h.kv_rows, f16 ? 2 : 4, vslice_rows(f16 ? 2 : 4, gs), &vmap);
+  rc = vslice_map(h.kv_base, h.kv_rows, f16 ? 2 : 4, kCtxRows, &vmap);
   if (rc) return rc;
   void* fn = step_fn(gs, variant);
   {
