@@ -66,18 +66,17 @@ static_assert(kSlotRows == kAttnBlock, "a ring slot of KV rows is one attention 
 // Phase B (the context) runs one item per (query head, 32-dim slice): a chain warp adds
 // the products w_t v_t[d] of its 32 dims position after position, while helper warps of
 // the same CTA form those products from the ring's V rows and the head's exps and hand
-// them over transposed, so that the chain reads four positions per 16-byte load.
-constexpr int kCtxRows = 64;                           // V rows per phase-B slot
+// them over transposed, so that the chain reads four positions per 16-byte load. Block u
+// (counted over the launch) goes to helper u % 4 and its products buffer.
+constexpr int kCtxRows = 64;                           // V rows per phase-B slot (a block)
 constexpr int kCtxHelpers = 4;                         // helper warps: 1, 2, 3 and 5
-constexpr int kCtxHelperRows = kCtxRows / kCtxHelpers; // rows of a slot per helper
 constexpr int kCtxPStride = kCtxRows + 4;              // floats per dim in a products buffer
-constexpr int kCtxPBufs = 2;                           // products buffers (double-buffered)
+constexpr int kCtxPBufs = kCtxHelpers;                 // one products buffer per helper
 constexpr int kCtxPFloats = 32 * kCtxPStride;          // one products buffer
-static_assert(kCtxPBufs == 2, "StepShared holds two products-buffer barrier pairs");
+static_assert(kCtxPBufs == 4, "StepShared holds four products-buffer barrier pairs");
 static_assert(kCtxRows * (32 * 4 + 4) <= kSlotBytes, "a phase-B slot: V rows + exps");
-static_assert(kCtxHelperRows % 4 == 0 && kConsWarps / kCtxHelpers * kCtxHelpers == kConsWarps,
-              "helpers split a slot into 4-row groups and share the slot's release");
-static_assert((kCtxPStride / 4) % 2 == 1, "products buffer: conflict-free 16-byte loads");
+static_assert(kCtxRows == 64, "a helper divides two rows per lane");
+static_assert((kCtxPStride / 4) % 2 == 1, "products buffer: conflict-free 16-byte accesses");
 
 
 // Run-time tunables (hv_step_set_option): bulk copies a producer keeps in flight, and
@@ -119,8 +118,8 @@ struct StepShared {
   long long busy[kConsWarps];            // cycles spent computing attention scores
   unsigned long long ctx_wait_ns;        // phase B, whole launch: ns the chain waited for products
   unsigned long long ctx_sum_ns;         // phase B, whole launch: ns helper 0 waited for V slots
-  uint64_t pfull[2];             // phase B: products buffer b written (one arrive per helper)
-  uint64_t pfree[2];             // phase B: products buffer b read by the chain (one arrive)
+  uint64_t pfull[4];             // phase B: products buffer b written (its helper arrives)
+  uint64_t pfree[4];             // phase B: products buffer b read by the chain (one arrive)
   unsigned pseq;                 // phase B: products buffers used so far in this launch
 };
 
@@ -140,7 +139,7 @@ HV_HD size_t attn_area_floats(int gs, int cap, int nch) {
   const size_t a = (size_t)gs * kHd + 2 * kHd + (size_t)(gs + 1) * kHd + 8 +
                    ((cm * gs + 3) & ~size_t(3)) + (size_t)gs * nvl;
   const size_t b = (((size_t)nch + 3) & ~size_t(3)) + 4 + (size_t)kCtxPBufs * kCtxPFloats +
-                   (size_t)kCtxHelpers * kCtxHelperRows;
+                   (size_t)kCtxHelpers * kCtxRows;
   return a > b ? a : b;
 }
 
@@ -375,13 +374,6 @@ HV_DEV void gu_tiles(int ffn, int* off, int* t0, int* t1) {
   phase_tiles((ntiles + 7) / 8, off, &u0, &u1);
   *t0 = min(u0 * 8, ntiles);
   *t1 = min(u1 * 8, ntiles);
-}
-
-// Positions [t0, t1) of attention chunk c, and te: rows [t0, te) come from the cache,
-// row pos (if in the chunk) from this step's qkv.
-HV_DEV void attn_rows(int pos, int nch, int c, int* t0, int* t1, int* te) {
-  chunk_bounds(pos + 1, nch, c, t0, t1);
-  *te = max(*t0, min(*t1, pos));
 }
 
 HV_DEV int slots_per_tile(int niter) { return (niter + kSlotIters - 1) / kSlotIters; }
@@ -1364,12 +1356,13 @@ __device__ __noinline__ bool attn_scores_ring(const hv_step_desc& D, const hv_la
 // recursion over the chunks' sums; then the sequential weighted V sum
 // acc_d = (((+0 + w_0 v_0[d]) + w_1 v_1[d]) + ...), w_t = e_t / S, one chain of T adds per
 // output element. Block k's ring slot holds V rows [64 k, 64 k + 64) of the slice and h's
-// exps for the same rows. Helper warps 1, 2, 3, 5 take 16 rows each: they divide the
-// exps by S, form the products (row pos's v from this step's qkv, +0 past it: the chain
-// never holds -0, so +0 terms leave it unchanged), and store them transposed into a
-// products buffer, dim-major, four rows per 16 bytes; warp 0 (the chain) then needs one
-// 16-byte load per four adds. Two products buffers let the helpers fill the next block
-// while the chain adds the current one.
+// exps for the same rows. Block u (counted over the launch) goes to helper u % 4: it
+// divides the block's exps by S, forms the products (row pos's v from this step's qkv,
+// +0 past it: the chain never holds -0, so +0 terms leave it unchanged) and stores them
+// transposed into its own products buffer, dim-major, four rows per 16 bytes. Warp 0
+// (the chain) loads each half of block k + 1 as soon as the adds of the same half of
+// block k are issued: 16 loads and 64 dependent adds per block, nothing else on its
+// sub-partition.
 template <int GS, class KT>
 __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int layer,
                                            const Ring R, unsigned* qp, StepShared& S,
@@ -1379,6 +1372,7 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
   constexpr int BR = kCtxRows;
   constexpr int kVB = BR * 32 * (int)sizeof(KT);     // bytes of the V part of a slot
   constexpr int kRowB = 32 * (int)sizeof(KT);        // bytes of one 32-dim row slice
+  constexpr unsigned kPB = kCtxPFloats * 4;          // bytes of one products buffer
   const StepScratch X = step_scratch(D);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hw = ctx_helper(warp);
@@ -1388,7 +1382,7 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
   float* vals = area;                                // [nch] the chunks' sums
   float* s_s = vals + nch4;                          // S
   float* pbuf = s_s + 4;                             // [kCtxPBufs][32][kCtxPStride]
-  float* wsc = pbuf + kCtxPBufs * kCtxPFloats;       // [kCtxHelpers][16] weights
+  float* wsc = pbuf + kCtxPBufs * kCtxPFloats;       // [kCtxHelpers][64] weights
   if (ctx_item(blockIdx.x, gridDim.x, nitems, 0) < 0) return true;
   bool ok = true;
   for (int j = 0;; ++j) {
@@ -1404,7 +1398,7 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
     csync();
     if (!S.ok) return false;
     if (j == 0) trace_mark(D, tb + 18);
-    const unsigned u0 = S.pseq;                      // products buffers used before this item
+    const unsigned u0 = S.pseq;                      // blocks of earlier items this launch
     const int nf = S.front.n;
     for (int e = threadIdx.x; e < nf; e += kConsThreads)
       vals[e] = __ldcg(X.nsum + (size_t)h * nch + e);
@@ -1421,26 +1415,48 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
       float acc = 0.0f;
       const unsigned pl = pb + (unsigned)(lane * kCtxPStride * 4);
       if (lane == 0) S.wait[0] = 0;
-#pragma unroll 1
-      for (int k = 0; k < nblk && ok; ++k) {
+      // rows 0-31 (r0) and 32-63 (r1) of the block being added; the next block's halves
+      // are loaded into each as soon as its adds are issued
+      constexpr int H = BR / 8;                      // float4 per half block
+      float4 r0[H], r1[H];
+      auto wait_blk = [&](int k) -> unsigned {      // shared address of block k's products
         const unsigned u = u0 + (unsigned)k, b = u % kCtxPBufs;
         ok = warp_wait(S.pfull + b, (u / kCtxPBufs) & 1u, S, D.status);
-        if (!ok) break;
-        const unsigned a = pl + b * (unsigned)(kCtxPFloats * 4);
-        float4 p[BR / 4];
+        return pl + b * kPB;
+      };
+      auto load = [&](unsigned a, float4* r) {
 #pragma unroll
-        for (int x = 0; x < BR / 4; ++x) p[x] = lds_f4(a + 16u * (unsigned)x);
-        // the loads above are ordered before this release: the helpers may refill the
-        // buffer while the adds run
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(S.pfree + b, 1);
+        for (int x = 0; x < H; ++x) r[x] = lds_f4(a + 16u * (unsigned)x);
+      };
+      auto adds = [&](const float4* r) {
 #pragma unroll
-        for (int x = 0; x < BR / 4; ++x) {
-          acc = __fadd_rn(acc, p[x].x);
-          acc = __fadd_rn(acc, p[x].y);
-          acc = __fadd_rn(acc, p[x].z);
-          acc = __fadd_rn(acc, p[x].w);
+        for (int x = 0; x < H; ++x) {
+          acc = __fadd_rn(acc, r[x].x);
+          acc = __fadd_rn(acc, r[x].y);
+          acc = __fadd_rn(acc, r[x].z);
+          acc = __fadd_rn(acc, r[x].w);
         }
+      };
+      const unsigned a0 = wait_blk(0);
+      if (ok) {
+        load(a0, r0);
+        load(a0 + 16u * H, r1);
+      }
+#pragma unroll 1
+      for (int k = 0; k < nblk && ok; ++k) {
+        adds(r0);
+        const bool more = k + 1 < nblk;
+        unsigned an = 0;
+        if (more) {
+          an = wait_blk(k + 1);
+          if (!ok) break;
+          load(an, r0);
+        }
+        adds(r1);
+        if (more) load(an + 16u * H, r1);
+        // block k's loads completed long ago: its buffer goes back to its helper
+        __syncwarp();
+        if (lane == 0) mbar_arrive_n(S.pfree + (u0 + (unsigned)k) % kCtxPBufs, 1);
       }
       if (lane == 0) S.ctx_wait_ns += S.wait[0];
       if (ok) {
@@ -1460,60 +1476,56 @@ __device__ __noinline__ bool attn_ctx_ring(const hv_step_desc& D, int pos, int l
         }
       }
     } else if (hw >= 0) {
-      // a helper: rows r0 .. r0 + 15 of every block; lane = dim
+      // a helper: every fourth block, all 64 rows; lane = dim
       float vpos = __ldcg(D.qkv + (size_t)(nq + nkv + g) * kHd + 32 * jsl + lane);
       if constexpr (kKvHalf<KT>) vpos = __half2float(__float2half_rn(vpos));
-      const int r0 = hw * kCtxHelperRows;
-      const unsigned wl = sh_addr(wsc + hw * kCtxHelperRows);
-      const unsigned pl = pb + (unsigned)((lane * kCtxPStride + r0) * 4);
-      const unsigned rel = (unsigned)(kConsWarps / kCtxHelpers);
+      const unsigned wl = sh_addr(wsc + hw * BR);
+      const unsigned pl = pb + (unsigned)(hw * kCtxPFloats + lane * kCtxPStride) * 4u;
       if (lane == 0) S.wait[warp] = 0;
+      const int kfirst = (int)(((unsigned)hw + kCtxHelpers - u0 % kCtxHelpers) % kCtxHelpers);
 #pragma unroll 1
-      for (int k = 0; k < nblk && ok; ++k) {
+      for (int k = kfirst; k < nblk && ok; k += kCtxHelpers) {
         const unsigned q = qv0 + (unsigned)k;
-        const unsigned u = u0 + (unsigned)k, b = u % kCtxPBufs;
+        const unsigned c = (u0 + (unsigned)k) / kCtxPBufs;   // this buffer's use number
         ok = warp_wait(R.full_of(q), R.parity(q), S, D.status);
         if (!ok) break;
         const unsigned sl = sh_addr(R.slot(q));
-        const int t0 = k * BR + r0;                  // position of the helper's first row
-        if (lane < kCtxHelperRows) {
-          const float e = lds_f1(sl + (unsigned)(kVB + 4 * (r0 + lane)));
-          sts_f1(wl + 4u * (unsigned)lane, t0 + lane < T ? __fdiv_rn(e, S_) : 0.0f);
+        const int t0 = k * BR;                       // position of the block's first row
+        {
+          const float e0 = lds_f1(sl + (unsigned)(kVB + 4 * lane));
+          const float e1 = lds_f1(sl + (unsigned)(kVB + 4 * (32 + lane)));
+          sts_f1(wl + 4u * (unsigned)lane, t0 + lane < T ? __fdiv_rn(e0, S_) : 0.0f);
+          sts_f1(wl + 4u * (unsigned)(32 + lane), t0 + 32 + lane < T ? __fdiv_rn(e1, S_) : 0.0f);
         }
         __syncwarp();
-        float w[kCtxHelperRows], v[kCtxHelperRows];
+        float p[BR];
+        const unsigned vl = sl + (unsigned)(lane * (int)sizeof(KT));
 #pragma unroll
-        for (int x = 0; x < kCtxHelperRows; x += 4) {
+        for (int x = 0; x < BR; ++x) p[x] = slot_elem<KT>(vl + (unsigned)(x * kRowB));
+        const bool tail = t0 + BR > pos;             // the block holds row pos (or rows past it)
+#pragma unroll
+        for (int x = 0; x < BR; x += 4) {
           const float4 w4 = lds_f4(wl + 4u * (unsigned)x);
-          w[x] = w4.x; w[x + 1] = w4.y; w[x + 2] = w4.z; w[x + 3] = w4.w;
-        }
-        const unsigned vl = sl + (unsigned)(r0 * kRowB + lane * (int)sizeof(KT));
+          const float w[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int x = 0; x < kCtxHelperRows; ++x) v[x] = slot_elem<KT>(vl + (unsigned)(x * kRowB));
-        float p[kCtxHelperRows];
-        if (t0 + kCtxHelperRows <= pos) {            // every row from the cache
-#pragma unroll
-          for (int x = 0; x < kCtxHelperRows; ++x) p[x] = __fmul_rn(w[x], v[x]);
-        } else {
-#pragma unroll
-          for (int x = 0; x < kCtxHelperRows; ++x) {
-            const int t = t0 + x;
-            p[x] = t < pos ? __fmul_rn(w[x], v[x]) : t == pos ? __fmul_rn(w[x], vpos) : 0.0f;
+          for (int y = 0; y < 4; ++y) {
+            const int t = t0 + x + y;
+            p[x + y] = !tail || t < pos ? __fmul_rn(w[y], p[x + y])
+                     : t == pos          ? __fmul_rn(w[y], vpos)
+                                         : 0.0f;
           }
         }
         // the slot is read (the products depend on every load): release it
         __syncwarp();
-        if (lane == 0) mbar_arrive_n(R.empty_of(q), rel);
-        if (u >= (unsigned)kCtxPBufs) {
-          ok = warp_wait(S.pfree + b, ((u / kCtxPBufs) & 1u) ^ 1u, S, D.status);
+        if (lane == 0) mbar_arrive_n(R.empty_of(q), (unsigned)kConsWarps);
+        if (c > 0) {
+          ok = warp_wait(S.pfree + hw, (c - 1) & 1u, S, D.status);
           if (!ok) break;
         }
-        const unsigned a = pl + b * (unsigned)(kCtxPFloats * 4);
 #pragma unroll
-        for (int x = 0; x < kCtxHelperRows; x += 4)
-          sts_f4(a + 4u * (unsigned)x, p[x], p[x + 1], p[x + 2], p[x + 3]);
+        for (int x = 0; x < BR; x += 4) sts_f4(pl + 4u * (unsigned)x, p[x], p[x + 1], p[x + 2], p[x + 3]);
         __syncwarp();
-        if (lane == 0) mbar_arrive_n(S.pfull + b, 1);
+        if (lane == 0) mbar_arrive_n(S.pfull + hw, 1);
       }
       if (hw == 0 && lane == 0) S.ctx_sum_ns += S.wait[warp];
     }
@@ -1567,7 +1579,7 @@ k_step(const hv_step_desc D, int flags, int nslots, int inflight, int evict_firs
     S.ctx_wait_ns = 0;
     S.ctx_sum_ns = 0;
     for (int b = 0; b < kCtxPBufs; ++b) {
-      mbar_init(S.pfull + b, kCtxHelpers);
+      mbar_init(S.pfull + b, 1);
       mbar_init(S.pfree + b, 1);
     }
     S.pseq = 0;
