@@ -46,6 +46,12 @@ ARCH = {
                       tie_word_embeddings=False, eos_token_id=None),
     # the 8B layer shapes with 2 layers: a small case of the same kernels for profiler
     # captures (every launch holds well under the device's memory)
+    # the 32B layer shapes (64 q heads over 8 kv heads, ffn 25600) with 2 layers: the
+    # fused step's group-8 path at full width, for parity runs of seconds
+    "qwen3-32b-2l": dict(num_hidden_layers=2, hidden_size=5120, intermediate_size=25600,
+                         num_attention_heads=64, num_key_value_heads=8, head_dim=128,
+                         vocab_size=151936, rope_theta=1000000.0, rms_norm_eps=1e-6,
+                         tie_word_embeddings=False, eos_token_id=None),
     "qwen3-8b-2l": dict(num_hidden_layers=2, hidden_size=4096, intermediate_size=12288,
                         num_attention_heads=32, num_key_value_heads=8, head_dim=128,
                         vocab_size=151936, rope_theta=1000000.0, rms_norm_eps=1e-6,

@@ -197,6 +197,34 @@ def test_large_shapes_match_oracle(hv, arch_name, seed):
         eng.free()
 
 
+def test_32b_layer_shapes_match_oracle(hv):
+    """Two layers of the 32B shapes (hidden 5120, ffn 25600, 64 q heads over 8 kv heads)
+    and the 151936 x 5120 head: a 70-token prompt and 3 greedy tokens through the fused
+    step give the C oracle's tokens and logits bit for bit, and the eager sequence the
+    same bits. 64 heads x 4 slices are 256 context items on 148 CTAs, so CTAs take two
+    items each, and at 70+ positions every item spans two 64-row blocks."""
+    import hvdrv
+    arch = synth.ARCH["qwen3-32b-2l"]
+    eng = make_engine(arch, 3, 80)
+    cfg = eng.cfg
+    try:
+        w = download_weights(eng, hvdrv)
+        prompt = synth.prompt_ids(cfg, 3, 70)
+        want_toks, want_logits = O.FastOracleModel(cfg, w, 80).generate(prompt, 3)
+        toks, _, _ = eng.generate(prompt, 3)
+        lg = eng.logits(prompt)
+        print(f"32B shapes: tokens {toks} vs {want_toks}; "
+              f"step-0 logits rel err {rel_err(lg, want_logits[0]):.2e}")
+        assert toks == want_toks
+        assert np.array_equal(bits(lg), bits(want_logits[0]))
+        eng.fused = False
+        lg_eager = eng.logits(prompt)
+        eng.fused = True
+        assert np.array_equal(bits(lg), bits(lg_eager))
+    finally:
+        eng.free()
+
+
 def test_layer_ops_bit_exact_at_8b_shape(hv):
     """One decoder layer of the 8B-shape model (layers 0, 17 and 35) at position 77, with
     a seeded KV history. Each op is fed the oracle's input, so every op that the
