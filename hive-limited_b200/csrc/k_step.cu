@@ -10,7 +10,8 @@
 // Why warp-specialised: the step reads ~6 GB (8B shape at a 4k context) and computes
 // little, so its speed is how continuously HBM is kept busy. Each CTA (one per SM) has a
 // PRODUCER warp that walks the CTA's share of every byte the step streams -- its weight
-// tiles of every GEMV, the K and V rows of its attention chunks, its rows of the LM head
+// tiles of every GEMV, the K rows of its attention chunk and the V rows and exps of its
+// context items, its rows of the LM head
 // -- in the order they are consumed, and copies them with the bulk-copy engine
 // (cp.async.bulk, completion on an mbarrier) into a ring of 10 KB shared-memory slots.
 // Eight CONSUMER warps wait for slots, compute, and release them. Only the consumers
@@ -22,8 +23,10 @@
 //
 // Per layer, five phases separated by grid barriers:
 //   P1 qkv  : act <- quant(rmsnorm(h, an)); rows of W_qkv        -> qkv
-//   P2 attn : per (kv head, chunk): q/k norm + RoPE, KV append at pos, split softmax;
-//             last CTA of each kv head merges                     -> ctx
+//   P2 attn : A, per (kv head, chunk of numpy's pairwise recursion): q/k norm + RoPE,
+//             KV append at pos, scores in OpenBLAS's order, exps and the chunk's
+//             subtree sum; B, per (query head, 32-dim slice), once its kv head's chunks
+//             are in: the sequential weighted V sum               -> ctx
 //   P3 o    : act <- quant(ctx);   rows of W_o, h[row] += y        -> h
 //   P4 gu   : act <- quant(rmsnorm(h, fn)); gate/up row pairs, SiLU -> act
 //   P5 down : act <- quant(act);   rows of W_down, h[row] += y     -> h
